@@ -1,0 +1,96 @@
+"""ctypes binding of libabkv.so (the C ABI declared in include/abkv.h).
+
+The shared library is the product: there is no CPU or PyTorch fallback.  If
+the library is missing, every entry point raises at import of the op.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import threading
+from pathlib import Path
+
+_LIB_PATH = Path(__file__).resolve().parent / "libabkv.so"
+_lock = threading.Lock()
+_lib: C.CDLL | None = None
+
+c_int = C.c_int
+c_i32p = C.POINTER(C.c_int32)
+c_i64p = C.POINTER(C.c_int64)
+c_vp = C.c_void_p
+c_vpp = C.POINTER(C.c_void_p)
+c_size = C.c_size_t
+
+# name -> (restype, argtypes); must mirror include/abkv.h exactly.
+SIGNATURES: dict[str, tuple] = {
+    "abkv_status_string": (C.c_char_p, [c_int]),
+    "abkv_version": (C.c_char_p, []),
+    "abkv_workspace_error": (c_int, [c_vp, c_vp, c_i32p]),
+    "abkv_decode_workspace_size": (c_size, [c_int, c_int, c_int, c_int, c_int, c_int, c_int]),
+    "abkv_decode": (
+        c_int,
+        [c_vpp, c_vpp, c_vpp, c_i64p, c_vpp, c_i64p, c_vpp, c_int, c_int, c_int, c_int, c_int,
+         c_int, c_int, C.c_float, c_int, c_vp, c_size, c_vp],
+    ),
+}
+
+
+class AbkvError(RuntimeError):
+    """A libabkv entry point returned a non-zero status."""
+
+    def __init__(self, fn: str, status: int, detail: str = ""):
+        self.status = status
+        msg = f"{fn} failed: {status_string(status)} (status {status})"
+        if detail:
+            msg += f": {detail}"
+        super().__init__(msg)
+
+
+def lib() -> C.CDLL:
+    """Load libabkv.so once (raises if it was not built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not _LIB_PATH.exists():
+                raise RuntimeError(
+                    f"{_LIB_PATH} is missing: build it with `python -m abridgekv_b200.build` "
+                    "(the sm_100a kernels have no fallback)"
+                )
+            handle = C.CDLL(str(_LIB_PATH))
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(handle, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = handle
+    return _lib
+
+
+def status_string(status: int) -> str:
+    return lib().abkv_status_string(status).decode()
+
+
+def check(fn: str, status: int, detail: str = "") -> None:
+    if status != 0:
+        raise AbkvError(fn, status, detail)
+
+
+def ptr_array(values) -> C.Array:
+    arr = (C.c_void_p * len(values))()
+    for i, v in enumerate(values):
+        arr[i] = int(v)
+    return arr
+
+
+def i64_array(values) -> C.Array:
+    arr = (C.c_int64 * len(values))()
+    for i, v in enumerate(values):
+        arr[i] = int(v)
+    return arr
+
+
+def i32_array(values) -> C.Array:
+    arr = (C.c_int32 * len(values))()
+    for i, v in enumerate(values):
+        arr[i] = int(v)
+    return arr

@@ -1,0 +1,380 @@
+#!/usr/bin/env python
+"""Benchmark: compressed-KV decode attention on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one decode step of the whole batch through all 36 layers'
+attention: a single abkv_decode launch over the Qwen3-4B-shaped compressed
+cache (per-layer quotas 6x256 / 18x128 / 12x64, B=64 sequences of 256-token
+prompt + 31 compressed blocks + a live tail ~U[0,511], page size 16; ~42 GB
+of K/V read per step, far larger than L2, so no flush is needed).
+
+Multi-GPU (torchrun, one rank per GPU): sequences shard across ranks with no
+collective on the data path; every rank runs its own B=64 batch (weak
+scaling).  Device time is the max over ranks.
+
+Prints ONE JSON line on rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "compressed-KV decode attn tokens/s/GPU + % HBM roofline at 1/2/4/8 B200"
+FALLBACK_HBM_GBS = 6650.0
+
+
+# ---------------------------------------------------------------------------
+def measured_hbm_peak() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def profiled_traffic(kernel: str) -> float | None:
+    """Per-launch DRAM bytes of `kernel` from the committed ncu summary, if any."""
+    p = ROOT / "profiles" / f"{kernel}.md"
+    if not p.exists():
+        return None
+    m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", p.read_text())
+    return float(m.group(1)) if m else None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self._t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except FileNotFoundError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self._t.join(timeout=2)
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+def dist_setup(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n_gpus:
+        raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}; launch N>1 with torchrun")
+    torch.cuda.set_device(local)
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return rank, world, local
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+# ---------------------------------------------------------------------------
+def cpu_baseline_decode(wl_rows: dict, budget_s: float = 20.0) -> dict:
+    """Reference CPU path (oracle port of PackedKVSidecar._attend_decode_batched)
+    on the host cores, over a bounded sample of config-2 sequences."""
+    from abridgekv_b200.workloads import SCHEDULE_PERLAYER_MEAN128, build_decode_workload
+    from oracle.decode_ref import sidecar_decode_torch
+
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    samples = []
+    for b in range(min(4, len(next(iter(wl_rows.values()))))):
+        rows = {q: r[b:b + 1] for q, r in wl_rows.items()}
+        samples.append(build_decode_workload("cpu-sample", SCHEDULE_PERLAYER_MEAN128, rows, num_q_heads=32,
+                                             num_kv_heads=8, head_dim=128, device="cpu", seed=100 + b))
+    scale = 1.0 / np.sqrt(128)
+    seqs_done, t_total = 0, 0.0
+    while t_total < budget_s or seqs_done < len(samples):
+        wl = samples[seqs_done % len(samples)]
+        t0 = time.perf_counter()
+        for l in range(wl.num_layers):
+            sidecar_decode_torch(wl.queries[l], wl.kv_caches[l], wl.seq_lens[l], wl.block_tables[l],
+                                 8, 4, scale, wl.page)
+        t_total += time.perf_counter() - t0
+        seqs_done += 1
+    return {"value": seqs_done / t_total, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"{seqs_done} decode steps of single config-2 sequences (4 distinct, cycled) x 36 "
+                      f"layers, torch CPU (oracle/decode_ref.sidecar_decode_torch), {t_total:.1f} s"}
+
+
+def run_reference(args, rank: int, world: int) -> None:
+    """Reference arm: the reference's own CPU implementation of the path
+    (PackedKVSidecar._attend_decode_batched restated as oracle/decode_ref.py's
+    torch port; the reference itself is Python and is not installable here),
+    timed on this box's host cores."""
+    if rank != 0:
+        return
+    from abridgekv_b200.workloads import SCHEDULE_PERLAYER_MEAN128, build_decode_workload, config2_rows
+    from oracle.decode_ref import sidecar_decode_torch
+
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    rows_all = config2_rows(64, seed=0)
+    # one sampled sequence per step (bounded), cycling through the batch
+    wls = []
+    for b in range(min(4, args.steps + args.warmup)):
+        rows = {q: r[b:b + 1] for q, r in rows_all.items()}
+        wls.append(build_decode_workload("ref-sample", SCHEDULE_PERLAYER_MEAN128, rows, num_q_heads=32,
+                                         num_kv_heads=8, head_dim=128, device="cpu", seed=100 + b))
+    scale = 1.0 / np.sqrt(128)
+
+    def step(i):
+        wl = wls[i % len(wls)]
+        for l in range(wl.num_layers):
+            sidecar_decode_torch(wl.queries[l], wl.kv_caches[l], wl.seq_lens[l], wl.block_tables[l],
+                                 8, 4, scale, wl.page)
+
+    for i in range(args.warmup):
+        step(i)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        step(i)
+    dt = time.perf_counter() - t0
+    value = args.steps / dt  # one sequence per step
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic", "config": config_block(world),
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": "1 config-2 sequence x 36 layers per step (torch CPU port of "
+                                   "compresslm_packed_kv.py:564-616)"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def config_block(world: int, chunk_tokens: int = 0) -> dict:
+    return {
+        "workload": "config2: Qwen3-4B decode attention over the compressed paged cache; 36 layers, "
+                    "32 q / 8 kv heads, head_dim 128, per-layer quotas 6x256/18x128/12x64 "
+                    "(sched_trunc_perlayer_mean128), B=64 per GPU, 256-token prompt + 31 compressed "
+                    "blocks + tail U[0,511], page 16, K/V/Q ~ N(0,1) bf16",
+        "global_batch": 64 * world,
+        "seq_len": "2496..8959 cache rows per layer",
+        "parallelism": f"sequence-sharded x{world}, no collective",
+        "l2": "inputs larger than L2 (~42.3 GB of K/V per step per GPU); no flush",
+        "chunk_tokens": chunk_tokens or "auto",
+    }
+
+
+def run_ours(args, rank: int, world: int, local: int) -> None:
+    from abridgekv_b200 import decode, _lib
+    from abridgekv_b200.workloads import qwen3_decode_workload
+    from abridgekv_b200.workspace import Workspace
+
+    dev = torch.device("cuda", local)
+    wl = qwen3_decode_workload(2, device=dev, seed=rank)
+    B, L = wl.num_seqs, wl.num_layers
+    outs = [torch.empty_like(q) for q in wl.queries]
+    ws = Workspace(dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        decode.paged_decode(wl.queries, wl.kv_caches, wl.block_tables, wl.seq_lens, outputs=outs,
+                            max_pages_per_seq=wl.max_pages, chunk_tokens=args.chunk_tokens,
+                            workspace=ws)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    assert ws.read_error() == 0, "device error word set during warm-up"
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    barrier(world)
+    torch.cuda.synchronize()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    for e0, e1 in evs:
+        e0.record(stream)
+        step()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    launch_ms = [e0.elapsed_time(e1) for e0, e1 in evs]
+    total_ms = evs[0][0].elapsed_time(evs[-1][1])
+    clocks = sampler.stop()
+    total_ms_max = max_over_ranks(total_ms, world)
+    mean_launch_ms = statistics.mean(launch_ms)
+    tokens = B * args.steps * world
+    value = tokens / (total_ms_max / 1e3)
+
+    # ---- end to end through the public API with pinned host buffers --------
+    q_host = [q.cpu().pin_memory() for q in wl.queries]
+    bt_host = {id(t): t.cpu().pin_memory() for t in wl.block_tables}
+    sl_host = {id(t): t.cpu().pin_memory() for t in wl.seq_lens}
+    out_host = [torch.empty(o.shape, dtype=o.dtype).pin_memory() for o in outs]
+    q_dev = [torch.empty_like(q) for q in wl.queries]
+    bt_dev = {k: torch.empty_like(v, device=dev) for k, v in bt_host.items()}
+    sl_dev = {k: torch.empty_like(v, device=dev) for k, v in sl_host.items()}
+    h2d = sum(q.numel() * 2 for q in q_host) + sum(t.numel() * 4 for t in bt_host.values()) + \
+        sum(t.numel() * 4 for t in sl_host.values())
+    d2h = sum(o.numel() * 2 for o in out_host)
+
+    def e2e_step():
+        for qd, qh in zip(q_dev, q_host):
+            qd.copy_(qh, non_blocking=True)
+        for k in bt_host:
+            bt_dev[k].copy_(bt_host[k], non_blocking=True)
+        for k in sl_host:
+            sl_dev[k].copy_(sl_host[k], non_blocking=True)
+        decode.paged_decode(q_dev, wl.kv_caches, [bt_dev[id(t)] for t in wl.block_tables],
+                            [sl_dev[id(t)] for t in wl.seq_lens], outputs=outs,
+                            max_pages_per_seq=wl.max_pages, chunk_tokens=args.chunk_tokens, workspace=ws)
+        for oh, od in zip(out_host, outs):
+            oh.copy_(od, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2e_steps = max(1, min(args.steps, 50))
+    e_start.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e_end.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_ms = max_over_ranks(e_start.elapsed_time(e_end), world)
+    e2e_value = B * e2e_steps * world / (e2e_ms / 1e3)
+    # the e2e outputs equal the device-resident run's outputs
+    assert all(torch.equal(oh, od.cpu()) for oh, od in zip(out_host, outs))
+    assert ws.read_error() == 0
+
+    if rank != 0:
+        return
+    peak, peak_kind = measured_hbm_peak()
+    alg_bytes = wl.kv_bytes + wl.qo_bytes
+    achieved = alg_bytes / (mean_launch_ms / 1e3) / 1e9
+    traffic = profiled_traffic("decode_split_kernel")
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline_decode(_config2_rows_for_cpu(), budget_s=args.cpu_budget)
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": total_ms_max / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": config_block(world, args.chunk_tokens),
+        "roofline": {"bound": "hbm", "kernel": "decode_split_kernel", "achieved": achieved, "peak": peak,
+                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                     else "fallback 6.65 TB/s", "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": traffic, "algorithmic_bytes_per_launch": alg_bytes,
+                     "mean_launch_ms": mean_launch_ms},
+        "cpu_baseline": cpu,
+        "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "steps": e2e_steps},
+        "gpu_launches": args.steps * ((L + 55) // 56),
+        "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def _config2_rows_for_cpu():
+    from abridgekv_b200.workloads import config2_rows
+    return config2_rows(64, seed=0)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--chunk-tokens", type=int, default=0)
+    ap.add_argument("--cpu-budget", type=float, default=15.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        rank = int(os.environ.get("RANK", "0"))
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        run_reference(args, rank, world)
+        return
+    rank, world, local = dist_setup(args.gpus)
+    try:
+        run_ours(args, rank, world, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

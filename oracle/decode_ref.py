@@ -1,0 +1,106 @@
+"""Decode-attention oracle (test infrastructure).
+
+Restates PackedKVSidecar._attend_decode_batched
+(third_party/vllm_overlay/vllm/v1/worker/compresslm_packed_kv.py:564-616) for
+the physical per-quota cache (no sidecar pages):
+
+  * rows 0..seq_len-1 of a request are gathered through its block-table row
+    (page = table[r // P], offset = r % P; _batched_main_index :501-524);
+  * scores = (q . K) * scale, computed in bf16 (two roundings: the einsum's
+    bf16 result, then the scaled bf16 product) (:610);
+  * rows >= seq_len are masked to -inf (:611);
+  * softmax in fp32, weights rounded to bf16 (:612);
+  * out = sum_t w_t V_t with fp32 accumulation, rounded to bf16 (:613-616).
+
+Two numpy forms: ``decode_reference`` reproduces those roundings,
+``decode_exact`` is float64 ground truth on the same bf16 inputs.
+``sidecar_decode_torch`` is the same computation as torch CPU ops (used to
+time the reference's CPU path in bench.py).
+"""
+from __future__ import annotations
+
+import numpy as np
+
+from .bf16 import round_bf16
+
+
+def _gather(kv: np.ndarray, bt_row: np.ndarray, seq_len: int, page: int) -> tuple[np.ndarray, np.ndarray]:
+    r = np.arange(seq_len)
+    pages = bt_row[r // page]
+    offs = r % page
+    k = kv[pages, 0, offs]  # [T, Hkv, D]
+    v = kv[pages, 1, offs]
+    return k, v
+
+
+def decode_reference(q, kv, block_table, seq_lens, scale, page) -> np.ndarray:
+    """Reference-rounding decode. q [B,Hq,D] (bf16 values in float32) -> [B,Hq,D] float32 (bf16 values)."""
+    B, Hq, D = q.shape
+    Hkv = kv.shape[3]
+    G = Hq // Hkv
+    out = np.zeros((B, Hq, D), dtype=np.float32)
+    for b in range(B):
+        s_len = int(seq_lens[b])
+        if s_len == 0:
+            continue
+        k, v = _gather(kv, block_table[b], s_len, page)
+        for h in range(Hq):
+            kh = k[:, h // G, :].astype(np.float32)
+            vh = v[:, h // G, :].astype(np.float32)
+            s = round_bf16(kh @ q[b, h].astype(np.float32))
+            s = round_bf16(s * np.float32(scale))
+            m = s.max()
+            e = np.exp((s - m).astype(np.float32))
+            w = round_bf16((e / e.sum()).astype(np.float32))
+            out[b, h] = round_bf16((w.astype(np.float64) @ vh.astype(np.float64)).astype(np.float32))
+    return out
+
+
+def decode_exact(q, kv, block_table, seq_lens, scale, page) -> np.ndarray:
+    """float64 ground truth on the same inputs (no intermediate rounding)."""
+    B, Hq, D = q.shape
+    Hkv = kv.shape[3]
+    G = Hq // Hkv
+    out = np.zeros((B, Hq, D), dtype=np.float64)
+    for b in range(B):
+        s_len = int(seq_lens[b])
+        if s_len == 0:
+            continue
+        k, v = _gather(kv, block_table[b], s_len, page)
+        for h in range(Hq):
+            kh = k[:, h // G, :].astype(np.float64)
+            vh = v[:, h // G, :].astype(np.float64)
+            s = (kh @ q[b, h].astype(np.float64)) * scale
+            e = np.exp(s - s.max())
+            out[b, h] = (e / e.sum()) @ vh
+    return out
+
+
+def sidecar_decode_torch(query, kv_cache, seq_lens, block_table, num_kv_heads: int, groups: int,
+                         scale: float, page: int):
+    """torch (CPU) form of the reference's batched decode for one layer.
+
+    query [n, Hq, D] bf16, kv_cache [nb, 2, P, Hkv, D] bf16, seq_lens [n] int,
+    block_table [n, maxp] int -> [n, Hq, D] bf16.  Same op sequence as
+    compresslm_packed_kv.py:579-616 (gather, bf16 einsum, -inf mask, fp32
+    softmax, bf16 weights, bf16 einsum)."""
+    import torch
+
+    n = query.shape[0]
+    lens = seq_lens[:n].to(torch.long)
+    s_max = int(lens.max())
+    pos = torch.arange(s_max)
+    hidden = pos.unsqueeze(0) >= lens.unsqueeze(1)
+    bidx = torch.clamp(pos // page, max=block_table.shape[1] - 1)
+    blocks = block_table[:n].to(torch.long)[:, bidx].masked_fill(hidden, 0)
+    offs = (pos % page).unsqueeze(0).expand(n, -1).masked_fill(hidden, 0)
+    rows = kv_cache[blocks, :, offs]                  # [n, S, 2, Hkv, D]
+    key = rows[:, :, 0].permute(0, 2, 1, 3)           # [n, Hkv, S, D]
+    value = rows[:, :, 1].permute(0, 2, 1, 3)
+    D = query.shape[-1]
+    q = query[:n].reshape(n, num_kv_heads, groups, D)
+    scores = torch.einsum("rhgd,rhtd->rhgt", q, key) * scale
+    scores.masked_fill_(hidden.view(n, 1, 1, s_max), -torch.inf)
+    weights = torch.softmax(scores, dim=-1, dtype=torch.float32).to(q.dtype)
+    att = torch.einsum("rhgt,rhtd->rhgd", weights, value)
+    return att.reshape(n, num_kv_heads * groups, D)

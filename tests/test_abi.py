@@ -1,0 +1,68 @@
+"""libabkv.so loads, exports every entry point declared in include/*.h, and its
+host-side validation rejects bad arguments before any launch (CPU-only test)."""
+import ctypes as C
+import re
+from pathlib import Path
+
+import pytest
+
+from abridgekv_b200 import _lib
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def declared_functions() -> list[str]:
+    names = []
+    for h in sorted((ROOT / "include").glob("*.h")):
+        text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        names += re.findall(r"^\s*(?:[\w\s\*]+?)\b(abkv_\w+)\s*\(", text, flags=re.M)
+    return sorted(set(names))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.lib()
+    names = declared_functions()
+    assert len(names) >= 4
+    for n in names:
+        assert hasattr(lib, n), f"{n} declared in include/ but not exported"
+    # and the ctypes binding covers exactly what the header declares
+    assert sorted(_lib.SIGNATURES) == names
+
+
+def test_status_strings_and_version():
+    assert _lib.status_string(0) == "ok"
+    assert "workspace" in _lib.status_string(2)
+    assert _lib.lib().abkv_version().decode().startswith("abkv")
+
+
+def test_decode_workspace_size():
+    lib = _lib.lib()
+    n = lib.abkv_decode_workspace_size(36, 64, 32, 128, 16, 544, 0)
+    assert n > 0 and n % 256 == 0
+    assert lib.abkv_decode_workspace_size(36, 64, 32, 96, 16, 544, 0) == 0   # head_dim 96 unsupported
+    assert lib.abkv_decode_workspace_size(36, 64, 32, 128, 8, 544, 0) == 0   # page 8 unsupported
+    assert lib.abkv_decode_workspace_size(1, 1, 8, 128, 16, 1, 0) == 256     # single chunk: header only
+
+
+@pytest.mark.parametrize("bad", ["null_q", "kv_heads", "group", "scale", "workspace", "chunk"])
+def test_decode_validation_rejects_before_launch(bad):
+    lib = _lib.lib()
+    fake = 1 << 20  # never dereferenced: validation fails first
+    q = _lib.ptr_array([0 if bad == "null_q" else fake])
+    kv = _lib.ptr_array([fake])
+    bt = _lib.ptr_array([fake])
+    sl = _lib.ptr_array([fake])
+    out = _lib.ptr_array([fake])
+    strides = _lib.i64_array([4])
+    nblk = _lib.i64_array([16])
+    hq, hkv = 8, 2
+    if bad == "kv_heads":
+        hq, hkv = 6, 3
+    if bad == "group":
+        hq, hkv = 32, 2
+    scale = -1.0 if bad == "scale" else 0.088
+    ws, ws_bytes = (0, 0) if bad == "workspace" else (fake, 1 << 30)
+    chunk = 24 if bad == "chunk" else 0
+    st = lib.abkv_decode(q, kv, bt, strides, sl, nblk, out, 1, 2, hq, hkv, 128, 16, 4, scale, chunk,
+                         ws, ws_bytes, None)
+    assert st in (1, 2, 3), st
