@@ -75,8 +75,8 @@ def paged_decode(
             raise ValueError("every query must be a contiguous [B, Hq, D] tensor")
         if tuple(kv.shape[1:]) != (2, page, Hkv, D) or not kv.is_contiguous():
             raise ValueError("every kv cache must be a contiguous [num_blocks, 2, page, Hkv, D] tensor")
-        if bt.dim() != 2 or bt.shape[0] < B or bt.stride(1) != 1:
-            raise ValueError("block_table must be [>=B, max_pages] with unit column stride")
+        if bt.dim() != 2 or bt.shape[0] < B or not bt.is_contiguous():
+            raise ValueError("block_table must be a contiguous [>=B, max_pages] tensor")
         if sl.dim() != 1 or sl.shape[0] < B or not sl.is_contiguous():
             raise ValueError("seq_lens must be a contiguous [>=B] tensor")
         if outputs is not None:
@@ -143,8 +143,8 @@ def attend_decode_batched(
         sl = sl.to(kv_cache.device, non_blocking=True)
     sl = sl.to(torch.int32).contiguous()
     bt = block_table[:n]
-    if bt.dtype != torch.int32:
-        bt = bt.to(torch.int32)
+    if bt.dtype != torch.int32 or not bt.is_contiguous():
+        bt = bt.to(torch.int32).contiguous()
     out_view = output[:n].reshape(n, Hq, D)
     direct = out_view.is_contiguous() and out_view.dtype == torch.bfloat16
     o = out_view if direct else torch.empty((n, Hq, D), dtype=torch.bfloat16, device=kv_cache.device)
