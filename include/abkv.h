@@ -102,6 +102,90 @@ int abkv_decode(const void* const* q, const void* const* kv,
                 int chunk_tokens, void* workspace, size_t workspace_bytes,
                 void* stream);
 
+
+/* ========================================================================
+ * 2. Compaction planner (host C++): page tables, free-block queue, span
+ *    index and span -> copy-op planning, bit-exact with the reference.
+ *
+ * One planner = one vLLM KV-cache manager with `num_groups` KV-cache groups
+ * (one per distinct code quota under physical per-layer quotas) sharing one
+ * block pool of `num_blocks` pages of `block_size` rows.  Block 0 is the null
+ * block and is never handed out.  Request ids are caller-chosen int64 keys.
+ *
+ * Replaces (file:line in the reference's vLLM overlay, vllm/v1/...):
+ *   abkv_planner_create          BlockPool.__init__ (core/block_pool.py:148-175)
+ *   abkv_planner_allocate_slots  KVCacheManager.allocate_slots' per-group
+ *                                compacted-token deduction + allocate_new_blocks
+ *                                (core/kv_cache_manager.py:281-299,
+ *                                 core/single_type_kv_cache_manager.py:122-145)
+ *   abkv_planner_free_request    SingleTypeKVCacheManager.free (:176-187)
+ *   abkv_planner_mask_token_span Scheduler.mask_token_span
+ *                                (core/sched/scheduler.py:2060-2204) ->
+ *                                compact_kv_cache_span_group -> compact_kv_cache_span
+ *                                (single_type_kv_cache_manager.py:358-420) ->
+ *                                BlockPool.copy_kv_slots (block_pool.py:488-550)
+ *   abkv_planner_finish_block    CompressLMProcessor._compact_response_content,
+ *                                physical-quota branch (core/compresslm/processor.py:467-557)
+ *   abkv_planner_span_map        CompactedSpanIndex.logical_to_physical /
+ *                                physical_to_logical (compacted_spans.py:54-68)
+ * Like the reference, mask_token_span reports a rejected span in the result
+ * (success = 0, error_message set) and returns ABKV_OK; it never partially
+ * applies a rejected span.  Copy ops (src_block, src_off, dst_block, dst_off)
+ * are queued per request and per group as ORDERED batches, one per removal,
+ * exactly as Scheduler.pending_kv_copy_operations; read them with the
+ * abkv_planner_pending_* functions and drop them with abkv_planner_clear_pending.
+ * A planner is not thread-safe; use one per scheduler thread.
+ * ====================================================================== */
+typedef struct abkv_planner abkv_planner_t;
+
+typedef struct abkv_span_result {
+  int32_t success;          /* 1 = span removed from every target group       */
+  int32_t tokens_removed;   /* end - start on success                         */
+  int32_t blocks_freed;     /* pages returned to the free queue               */
+  char error_message[160];  /* reference wording when success == 0            */
+} abkv_span_result_t;
+
+abkv_planner_t* abkv_planner_create(int num_blocks, int block_size, int num_groups);
+void abkv_planner_destroy(abkv_planner_t* planner);
+int abkv_planner_add_request(abkv_planner_t* planner, int64_t request);
+int abkv_planner_set_num_computed(abkv_planner_t* planner, int64_t request,
+                                  int64_t num_computed_tokens);
+int abkv_planner_allocate_slots(abkv_planner_t* planner, int64_t request,
+                                int64_t num_tokens);
+int abkv_planner_free_request(abkv_planner_t* planner, int64_t request);
+/* groups == NULL removes the span from every group. */
+int abkv_planner_mask_token_span(abkv_planner_t* planner, int64_t request,
+                                 int64_t start, int64_t end,
+                                 const int32_t* groups, int num_groups,
+                                 abkv_span_result_t* result);
+/* resp_end == resp_start: no response content to remove. */
+int abkv_planner_finish_block(abkv_planner_t* planner, int64_t request,
+                              int64_t resp_start, int64_t resp_end,
+                              int64_t code_start, int64_t code_end,
+                              const int32_t* group_quotas, int num_groups,
+                              int num_code_tokens, abkv_span_result_t* result);
+int abkv_planner_block_table(const abkv_planner_t* planner, int64_t request,
+                             int group, int32_t* out, int cap, int* n);
+int abkv_planner_free_queue(const abkv_planner_t* planner, int32_t* out,
+                            int cap, int* n);
+int abkv_planner_num_free(const abkv_planner_t* planner);
+int abkv_planner_span_map(const abkv_planner_t* planner, int64_t request,
+                          int group, int64_t position, int to_physical,
+                          int64_t* out);
+int abkv_planner_compacted_spans(const abkv_planner_t* planner, int64_t request,
+                                 int group, int64_t* out, int cap, int* n);
+int abkv_planner_pending_requests(const abkv_planner_t* planner, int64_t* out,
+                                  int cap, int* n);
+int abkv_planner_pending_num_batches(const abkv_planner_t* planner,
+                                     int64_t request, int group);
+int abkv_planner_pending_batch(const abkv_planner_t* planner, int64_t request,
+                               int group, int batch, int32_t* ops, int cap_ops,
+                               int* n_ops);
+int abkv_planner_pending_truncation(const abkv_planner_t* planner,
+                                    int64_t request, int32_t* out, int cap,
+                                    int* n);
+int abkv_planner_clear_pending(abkv_planner_t* planner);
+
 #ifdef __cplusplus
 }
 #endif
