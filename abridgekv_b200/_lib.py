@@ -31,6 +31,30 @@ SIGNATURES: dict[str, tuple] = {
         [c_vpp, c_vpp, c_vpp, c_i64p, c_vpp, c_i64p, c_vpp, c_int, c_int, c_int, c_int, c_int,
          c_int, c_int, C.c_float, c_int, c_vp, c_size, c_vp],
     ),
+    "abkv_planner_create": (c_vp, [c_int, c_int, c_int]),
+    "abkv_planner_destroy": (None, [c_vp]),
+    "abkv_planner_add_request": (c_int, [c_vp, C.c_int64]),
+    "abkv_planner_set_num_computed": (c_int, [c_vp, C.c_int64, C.c_int64]),
+    "abkv_planner_allocate_slots": (c_int, [c_vp, C.c_int64, C.c_int64]),
+    "abkv_planner_free_request": (c_int, [c_vp, C.c_int64]),
+    "abkv_planner_mask_token_span": (c_int, [c_vp, C.c_int64, C.c_int64, C.c_int64, c_i32p, c_int, c_vp]),
+    "abkv_planner_finish_block": (
+        c_int, [c_vp, C.c_int64, C.c_int64, C.c_int64, C.c_int64, C.c_int64, c_i32p, c_int, c_int, c_vp]),
+    "abkv_planner_block_table": (c_int, [c_vp, C.c_int64, c_int, c_i32p, c_int, C.POINTER(c_int)]),
+    "abkv_planner_free_queue": (c_int, [c_vp, c_i32p, c_int, C.POINTER(c_int)]),
+    "abkv_planner_num_free": (c_int, [c_vp]),
+    "abkv_planner_span_map": (c_int, [c_vp, C.c_int64, c_int, C.c_int64, c_int, c_i64p]),
+    "abkv_planner_compacted_spans": (c_int, [c_vp, C.c_int64, c_int, c_i64p, c_int, C.POINTER(c_int)]),
+    "abkv_planner_pending_requests": (c_int, [c_vp, c_i64p, c_int, C.POINTER(c_int)]),
+    "abkv_planner_pending_num_batches": (c_int, [c_vp, C.c_int64, c_int]),
+    "abkv_planner_pending_batch": (c_int, [c_vp, C.c_int64, c_int, c_int, c_i32p, c_int, C.POINTER(c_int)]),
+    "abkv_planner_pending_truncation": (c_int, [c_vp, C.c_int64, c_i32p, c_int, C.POINTER(c_int)]),
+    "abkv_planner_clear_pending": (c_int, [c_vp]),
+    "abkv_compact_workspace_size": (c_size, [c_int, c_int, c_int, c_int, C.c_int64]),
+    "abkv_compact": (c_int, [c_vpp, c_int, c_int, C.c_int64, c_int, c_int, c_int, c_i32p, c_i64p, c_int,
+                             c_vp, c_size, c_vp]),
+    "abkv_gather_rows": (c_int, [c_vpp, c_vpp, c_int, C.c_int64, C.c_int64, C.c_int64, C.c_int64, c_vp,
+                                 c_vp, c_size, c_vp]),
 }
 
 

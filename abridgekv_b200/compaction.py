@@ -1,0 +1,124 @@
+"""KV compaction executor (host side) over libabkv's sm_100a copy kernels.
+
+* ``execute_kv_copy_operations(kv_copy_operations, kv_caches_by_group)``
+  mirrors ``GPUModelRunner._execute_kv_copy_operations``
+  (third_party/vllm_overlay/vllm/v1/worker/gpu_model_runner.py:1147-1176): for
+  each KV-cache group, the b-th batch of every request is merged and the
+  batches are applied in order, each with gather-all-then-scatter semantics,
+  to every layer tensor of the group.  One ``abkv_compact`` call per group.
+* ``execute_kv_copy_group(all_ops, layer_caches)`` mirrors
+  ``_execute_kv_copy_group`` (:1194-1220): one batch.
+* ``evict_columns(K, V, keep_cols)`` mirrors ``KVStore.evict``
+  (abridgekv/gen_compress.py:72-77) for all layers in one launch.
+
+Both paged layouts are accepted, detected like the reference: a leading dim of
+2 is the FlashAttention layout ``[2, num_blocks, page, Hkv, D]``, otherwise
+FlashInfer ``[num_blocks, 2, page, Hkv, D]``.  The copy is byte-exact for any
+2-byte or wider element type.
+"""
+from __future__ import annotations
+
+from typing import Hashable, Sequence
+
+import torch
+
+from . import _lib
+from .workspace import Workspace, default_workspace
+
+
+def _layout_of(kv: torch.Tensor) -> tuple[int, int, int, int, int]:
+    if kv.dim() != 5:
+        raise ValueError(f"unsupported KV cache shape {tuple(kv.shape)}")
+    if kv.shape[0] == 2:
+        _, nb, page, hkv, d = kv.shape
+        return 1, nb, page, hkv, d
+    nb, two, page, hkv, d = kv.shape
+    if two != 2:
+        raise ValueError(f"unsupported KV cache shape {tuple(kv.shape)}")
+    return 0, nb, page, hkv, d
+
+
+def _compact(layer_caches: Sequence[torch.Tensor], batches: Sequence[Sequence[Sequence[int]]],
+             workspace: Workspace | None, stream: torch.cuda.Stream | None) -> None:
+    if not layer_caches:
+        return
+    kv0 = layer_caches[0]
+    layout, nb, page, hkv, d = _layout_of(kv0)
+    for kv in layer_caches:
+        if not kv.is_cuda or not kv.is_contiguous():
+            raise TypeError("KV caches must be contiguous CUDA tensors (libabkv has no CPU path)")
+        if kv.shape != kv0.shape or kv.dtype != kv0.dtype:
+            raise ValueError("every layer tensor of a group must share shape and dtype")
+    elem = kv0.element_size()
+    # the kernel moves rows as bytes: express the row as 2-byte units
+    units = hkv * d * elem // 2
+    flat, offsets = [], [0]
+    for b in batches:
+        for op in b:
+            flat.extend(int(x) for x in op)
+        offsets.append(len(flat) // 4)
+    n_batches = len(batches)
+    if offsets[-1] == 0:
+        return
+    max_ops = max(offsets[i + 1] - offsets[i] for i in range(n_batches))
+    lib = _lib.lib()
+    need = lib.abkv_compact_workspace_size(len(layer_caches), page, 1, units, max_ops)
+    ws = (workspace or default_workspace(kv0.device)).ensure(need)
+    s = torch.cuda.current_stream(kv0.device) if stream is None else stream
+    ops_arr = _lib.i32_array(flat)
+    off_arr = _lib.i64_array(offsets)
+    st = lib.abkv_compact(_lib.ptr_array([kv.data_ptr() for kv in layer_caches]), len(layer_caches), layout,
+                          nb, page, 1, units, ops_arr, off_arr, n_batches, ws.ptr(), ws.nbytes, s.cuda_stream)
+    _lib.check("abkv_compact", st)
+
+
+def execute_kv_copy_group(all_ops: Sequence[Sequence[int]], layer_caches: Sequence[torch.Tensor],
+                          workspace: Workspace | None = None, stream=None) -> None:
+    """One batch of (src_block, src_off, dst_block, dst_off) over every layer tensor."""
+    _compact(layer_caches, [list(all_ops)], workspace, stream)
+
+
+def execute_kv_copy_operations(kv_copy_operations: dict[Hashable, list[list[list[tuple[int, int, int, int]]]]],
+                               kv_caches_by_group: Sequence[Sequence[torch.Tensor]],
+                               workspace: Workspace | None = None, stream=None) -> None:
+    """request -> per group -> ordered batches, applied group by group."""
+    for g, layer_caches in enumerate(kv_caches_by_group):
+        per_req = [ops[g] for ops in kv_copy_operations.values() if g < len(ops)]
+        nb = max((len(b) for b in per_req), default=0)
+        batches = []
+        for b in range(nb):
+            merged = []
+            for req_batches in per_req:
+                if b < len(req_batches):
+                    merged.extend(req_batches[b])
+            if merged:
+                batches.append(merged)
+        if batches:
+            _compact(layer_caches, batches, workspace, stream)
+
+
+def evict_columns(K: Sequence[torch.Tensor], V: Sequence[torch.Tensor], keep_cols: torch.Tensor,
+                  workspace: Workspace | None = None, stream=None) -> tuple[list[torch.Tensor], list[torch.Tensor]]:
+    """KVStore.evict: K[l][:, :, keep_cols, :] and V[l][...] for every layer, one launch.
+
+    K[l], V[l]: contiguous CUDA [B, Hkv, T, D]; keep_cols: 1-D integer tensor.
+    Returns new contiguous tensors [B, Hkv, len(keep_cols), D]."""
+    tensors = list(K) + list(V)
+    if not tensors:
+        return [], []
+    t0 = tensors[0]
+    for t in tensors:
+        if not t.is_cuda or not t.is_contiguous() or t.shape != t0.shape or t.dtype != t0.dtype:
+            raise ValueError("evict_columns needs contiguous CUDA tensors of one shape and dtype")
+    b, h, T, d = t0.shape
+    keep = keep_cols.to(device=t0.device, dtype=torch.int64).contiguous()
+    n = keep.numel()
+    outs = [torch.empty((b, h, n, d), dtype=t0.dtype, device=t0.device) for _ in tensors]
+    ws = workspace or default_workspace(t0.device)
+    s = torch.cuda.current_stream(t0.device) if stream is None else stream
+    st = _lib.lib().abkv_gather_rows(
+        _lib.ptr_array([t.data_ptr() for t in tensors]), _lib.ptr_array([o.data_ptr() for o in outs]),
+        len(tensors), b * h, T, n, d * t0.element_size(), keep.data_ptr(), ws.ptr(), ws.nbytes, s.cuda_stream)
+    _lib.check("abkv_gather_rows", st)
+    L = len(K)
+    return outs[:L], outs[L:]

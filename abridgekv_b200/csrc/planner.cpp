@@ -415,7 +415,7 @@ int abkv_planner_mask_token_span(abkv_planner_t* p, int64_t req, int64_t start, 
                                  const int32_t* groups, int num_groups_given,
                                  abkv_span_result_t* result) {
   if (!p || !result) return ABKV_ERR_INVALID_ARG;
-  if (groups && num_groups_given <= 0) return ABKV_ERR_INVALID_ARG;
+  if (groups && num_groups_given < 0) return ABKV_ERR_INVALID_ARG;
   return p->mask_token_span(req, start, end, groups, num_groups_given, result);
 }
 

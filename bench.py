@@ -217,13 +217,13 @@ def run_reference(args, rank: int, world: int) -> None:
     print(json.dumps(line), flush=True)
 
 
-def config_block(world: int, chunk_tokens: int = 0) -> dict:
+def config_block(world: int, chunk_tokens: int = 0, num_seqs: int = 64) -> dict:
     return {
         "workload": "config2: Qwen3-4B decode attention over the compressed paged cache; 36 layers, "
                     "32 q / 8 kv heads, head_dim 128, per-layer quotas 6x256/18x128/12x64 "
-                    "(sched_trunc_perlayer_mean128), B=64 per GPU, 256-token prompt + 31 compressed "
+                    f"(sched_trunc_perlayer_mean128), B={num_seqs} per GPU, 256-token prompt + 31 compressed "
                     "blocks + tail U[0,511], page 16, K/V/Q ~ N(0,1) bf16",
-        "global_batch": 64 * world,
+        "global_batch": num_seqs * world,
         "seq_len": "2496..8959 cache rows per layer",
         "parallelism": f"sequence-sharded x{world}, no collective",
         "l2": "inputs larger than L2 (~42.3 GB of K/V per step per GPU); no flush",
@@ -237,7 +237,7 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     from abridgekv_b200.workspace import Workspace
 
     dev = torch.device("cuda", local)
-    wl = qwen3_decode_workload(2, device=dev, seed=rank)
+    wl = qwen3_decode_workload(2, num_seqs=args.num_seqs, device=dev, seed=rank)
     B, L = wl.num_seqs, wl.num_layers
     outs = [torch.empty_like(q) for q in wl.queries]
     ws = Workspace(dev)
@@ -330,7 +330,7 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": total_ms_max / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": config_block(world, args.chunk_tokens),
+        "config": config_block(world, args.chunk_tokens, args.num_seqs),
         "roofline": {"bound": "hbm", "kernel": "decode_split_kernel", "achieved": achieved, "peak": peak,
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                      else "fallback 6.65 TB/s", "unit": "GB/s", "frac": achieved / peak,
@@ -357,6 +357,7 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--chunk-tokens", type=int, default=0)
+    ap.add_argument("--num-seqs", type=int, default=64, help="sequences per GPU (config 2 uses 64)")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()

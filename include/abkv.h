@@ -153,7 +153,8 @@ int abkv_planner_set_num_computed(abkv_planner_t* planner, int64_t request,
 int abkv_planner_allocate_slots(abkv_planner_t* planner, int64_t request,
                                 int64_t num_tokens);
 int abkv_planner_free_request(abkv_planner_t* planner, int64_t request);
-/* groups == NULL removes the span from every group. */
+/* groups == NULL removes the span from every group; a non-NULL list of
+ * num_groups entries (possibly zero) names the target groups. */
 int abkv_planner_mask_token_span(abkv_planner_t* planner, int64_t request,
                                  int64_t start, int64_t end,
                                  const int32_t* groups, int num_groups,
@@ -185,6 +186,45 @@ int abkv_planner_pending_truncation(const abkv_planner_t* planner,
                                     int64_t request, int32_t* out, int cap,
                                     int* n);
 int abkv_planner_clear_pending(abkv_planner_t* planner);
+
+/* ========================================================================
+ * 3. Compaction executor (device): ordered batches of KV slot copies.
+ *
+ * Replaces GPUModelRunner._execute_kv_copy_operations /
+ * _execute_kv_copy_group (third_party/vllm_overlay/vllm/v1/worker/
+ * gpu_model_runner.py:1147-1220) for ONE KV-cache group: `num_batches`
+ * ordered batches, batch b = ops[batch_offsets[b] .. batch_offsets[b+1]),
+ * each op = (src_block, src_off, dst_block, dst_off) (host int32 [n][4]).
+ * Every batch is applied to every layer tensor of the group with
+ * gather-all-then-scatter semantics; batches are applied in order.
+ *   layout 0: FlashInfer      [num_blocks][2][page][Hkv][D]
+ *   layout 1: FlashAttention  [2][num_blocks][page][Hkv][D]
+ * Element type is opaque (rows are copied as bytes; Hkv*D*2 must be a
+ * multiple of 16, i.e. 2-byte elements).  Every op is validated on the host
+ * (blocks in [0, num_blocks), offsets in [0, page)) before anything runs.
+ * Up to 96 layer tensors per call.  The call may wait for the stream while
+ * it uploads each batch's plan from host memory.
+ * ====================================================================== */
+size_t abkv_compact_workspace_size(int num_layers, int page_size, int num_kv_heads,
+                                   int head_dim, int64_t max_ops_per_batch);
+
+int abkv_compact(void* const* layer_caches, int num_layers, int layout,
+                 int64_t num_blocks, int page_size, int num_kv_heads,
+                 int head_dim, const int32_t* ops, const int64_t* batch_offsets,
+                 int num_batches, void* workspace, size_t workspace_bytes,
+                 void* stream);
+
+/* Row gather over many tensors in one launch: each tensor t is viewed as
+ * [outer][rows][row_bytes]; dst[t][o][j] = src[t][o][keep[j]] for
+ * j < dst_rows.  keep is a DEVICE int64 array; an index outside
+ * [0, src_rows) sets ABKV_DEVERR_ROW_OOB and zero-fills that row.
+ * Replaces KVStore.evict(keep_cols) (abridgekv/gen_compress.py:72-77), which
+ * gathers the kept columns of every layer's K and V ([1, Hkv, T, D]).
+ * row_bytes must be a multiple of 16. */
+int abkv_gather_rows(const void* const* src, void* const* dst, int num_tensors,
+                     int64_t outer, int64_t src_rows, int64_t dst_rows,
+                     int64_t row_bytes, const int64_t* keep, void* workspace,
+                     size_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }
