@@ -80,13 +80,32 @@ __device__ __forceinline__ int clamp_seq_len(const DecodeParams& p, const LayerA
   return s;
 }
 
-__global__ void __launch_bounds__(kThreads, 2)
+// Dynamic shared memory layout of decode_split_kernel:
+//   [kStages][kStageBytes]  K/V tile groups (a group = nsub tiles, one per
+//                           warp slot; tile = 16 cache rows, K then V, all
+//                           KV heads) -- 64 KiB per stage for head_dim 128
+//   s_pages[kMaxChunkPages + 4]
+//   mbarriers: full[kStages], page-list barrier
+// After the main loop the stage buffers are reused for the epilogue arrays.
+constexpr int kStages = 3;
+constexpr int kStageBytes = kWarps * 2 * kTile * kD * 2;  // nsub * Hkv == kWarps
+constexpr size_t kSmemBytes =
+    (size_t)kStages * kStageBytes + (kMaxChunkPages + 4) * sizeof(int32_t) + (kStages + 1) * 8;
+
+__device__ __forceinline__ uint4 lds128(const void* p) {
+  uint4 r;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "r"(smem_u32(p)));
+  return r;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
     decode_split_kernel(const __grid_constant__ DecodeParams p) {
-  __shared__ __align__(16) int32_t s_pages[kMaxChunkPages + 4];
-  __shared__ __align__(8) uint64_t s_bar;
-  __shared__ float s_o[kWarps][kMaxG][kD];
-  __shared__ float s_m[kWarps][kMaxG];
-  __shared__ float s_l[kWarps][kMaxG];
+  extern __shared__ __align__(1024) uint8_t smem[];
+  int32_t* s_pages = reinterpret_cast<int32_t*>(smem + (size_t)kStages * kStageBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(s_pages + kMaxChunkPages + 4);
+  uint64_t* pg_bar = full + kStages;
 
   const int chunk = blockIdx.x, b = blockIdx.y, li = blockIdx.z;
   const LayerArgs& L = p.layer[li];
@@ -115,25 +134,66 @@ __global__ void __launch_bounds__(kThreads, 2)
   if (head > npages) head = npages;
   const int body = ((npages - head) >> 2) << 2;
   const int shift = (4 - head) & 3;  // makes s_pages + shift + head 16-byte aligned
-  if (threadIdx.x == 0 && body > 0) mbar_init(&s_bar, 1);
+  if (threadIdx.x == 0) {
+    for (int s2 = 0; s2 < kStages; ++s2) mbar_init(&full[s2], 1);
+    if (body > 0) mbar_init(pg_bar, 1);
+  }
   __syncthreads();
   if (threadIdx.x == 0 && body > 0) {
-    mbar_expect_tx(&s_bar, (uint32_t)body * 4u);
-    bulk_g2s(s_pages + shift + head, src + head, (uint32_t)body * 4u, &s_bar);
+    mbar_expect_tx(pg_bar, (uint32_t)body * 4u);
+    bulk_g2s(s_pages + shift + head, src + head, (uint32_t)body * 4u, pg_bar);
   }
   for (int i = threadIdx.x; i < head; i += kThreads) s_pages[shift + i] = __ldg(src + i);
   for (int i = head + body + threadIdx.x; i < npages; i += kThreads)
     s_pages[shift + i] = __ldg(src + i);
-  if (body > 0 && !mbar_wait(&s_bar, 0)) {
-    set_error(p.err, ABKV_DEVERR_TIMEOUT);
-  }
+  if (body > 0 && !mbar_wait(pg_bar, 0)) set_error(p.err, ABKV_DEVERR_TIMEOUT);
   __syncthreads();
 
-  // ---- per-warp streaming over the chunk's tiles -------------------------
+  // ---- bulk-copy pipeline over tile groups --------------------------------
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int Hkv = p.Hkv, G = p.G, P = p.P;
   const int h = warp % Hkv, sub = warp / Hkv, nsub = kWarps / Hkv;
   const int g = lane >> 2, c = lane & 3;
+  const int row_bytes = Hkv * kD * 2;      // one cache row, all KV heads
+  const int tile_half = kTile * row_bytes;  // 16 rows of K (or of V)
+  const int64_t row_elems = (int64_t)Hkv * kD;
+  const int64_t half_elems = (int64_t)P * row_elems;
+  const int64_t page_elems = 2 * half_elems;
+  const int64_t nblk = L.num_blocks;
+  const int ngroups = (tile1 - tile0 + nsub - 1) / nsub;
+
+  auto tile_page = [&](int t, bool& ok) -> int64_t {
+    const int pg = s_pages[shift + t * kTile / P - page0];
+    ok = pg >= 0 && (int64_t)pg < nblk;
+    return pg;
+  };
+  // thread 0: copy tile group gi (K rows then V rows of each tile) into its stage
+  auto issue = [&](int gi) {
+    const int st = gi % kStages;
+    uint8_t* dst = smem + (size_t)st * kStageBytes;
+    uint32_t bytes = 0;
+    for (int j = 0; j < nsub; ++j) {
+      const int t = tile0 + gi * nsub + j;
+      bool ok = false;
+      if (t < tile1) tile_page(t, ok);
+      if (ok) bytes += 2u * (uint32_t)tile_half;
+    }
+    mbar_expect_tx(&full[st], bytes);
+    for (int j = 0; j < nsub; ++j) {
+      const int t = tile0 + gi * nsub + j;
+      if (t >= tile1) break;
+      bool ok;
+      const int64_t pg = tile_page(t, ok);
+      if (!ok) {
+        set_error(p.err, ABKV_DEVERR_PAGE_OOB);
+        continue;
+      }
+      const __nv_bfloat16* ksrc = L.kv + pg * page_elems + (int64_t)((t * kTile) % P) * row_elems;
+      bulk_g2s(dst + (size_t)j * 2 * tile_half, ksrc, (uint32_t)tile_half, &full[st]);
+      bulk_g2s(dst + (size_t)j * 2 * tile_half + tile_half, ksrc + half_elems, (uint32_t)tile_half,
+               &full[st]);
+    }
+  };
 
   uint32_t qr[4][4];
   {
@@ -146,53 +206,9 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
   }
 
-  const int row_elems = Hkv * kD;
-  const int64_t half_elems = (int64_t)P * row_elems;
-  const int64_t page_elems = 2 * half_elems;
-  const __nv_bfloat16* kvh = L.kv + h * kD;
-  const int64_t nblk = L.num_blocks;
-
-  auto tile_base = [&](int t, bool& ok) -> const __nv_bfloat16* {
-    const int tok0 = t * kTile;
-    const int pg = s_pages[shift + tok0 / P - page0];
-    ok = pg >= 0 && (int64_t)pg < nblk;
-    if (!ok) set_error(p.err, ABKV_DEVERR_PAGE_OOB);
-    return kvh + (ok ? (int64_t)pg : 0) * page_elems + (int64_t)(tok0 % P) * row_elems;
-  };
-
-  uint32_t kr[2][4][4];  // [n-tile][m][4 regs]
-  uint32_t vr[4][2][4];  // [token: 2c,2c+1,2c+8,2c+9][dim half][4 regs]
-
-  auto load_k = [&](int t, const __nv_bfloat16* base, bool ok) {
-    const int tok0 = t * kTile;
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
-      const int T = 8 * nt + g;
-      const bool valid = ok && (tok0 + T < seq_len);
-      const __nv_bfloat16* rp = base + (int64_t)T * row_elems + 8 * c;
-#pragma unroll
-      for (int m = 0; m < 4; ++m) {
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (valid) v = ld_stream_v4(rp + 32 * m);
-        kr[nt][m][0] = v.x; kr[nt][m][1] = v.y; kr[nt][m][2] = v.z; kr[nt][m][3] = v.w;
-      }
-    }
-  };
-  auto load_v = [&](int t, const __nv_bfloat16* base, bool ok) {
-    const int tok0 = t * kTile;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int T = 2 * c + (i & 1) + 8 * (i >> 1);
-      const bool valid = ok && (tok0 + T < seq_len);
-      const __nv_bfloat16* rp = base + half_elems + (int64_t)T * row_elems + 8 * g;
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (valid) v = ld_stream_v4(rp + 64 * hh);
-        vr[i][hh][0] = v.x; vr[i][hh][1] = v.y; vr[i][hh][2] = v.z; vr[i][hh][3] = v.w;
-      }
-    }
-  };
+  if (threadIdx.x == 0) {
+    for (int gi = 0; gi < kStages && gi < ngroups; ++gi) issue(gi);
+  }
 
   float o[8][4];
 #pragma unroll
@@ -200,78 +216,99 @@ __global__ void __launch_bounds__(kThreads, 2)
   float m_run = -INFINITY, l_run = 0.f;
   const float sl2 = p.scale_log2;
 
-  int t = tile0 + sub;
-  bool ok_cur = false;
-  if (t < tile1) {
-    const __nv_bfloat16* base = tile_base(t, ok_cur);
-    load_k(t, base, ok_cur);
-    load_v(t, base, ok_cur);
-  }
-  for (; t < tile1; t += nsub) {
-    // S = Q.K^T : rows = query heads (g < G real), cols = tokens 8nt + 2c + {0,1}
-    float s[2][4];
+  for (int gi = 0; gi < ngroups; ++gi) {
+    const int st = gi % kStages;
+    if (!mbar_wait(&full[st], (uint32_t)((gi / kStages) & 1))) set_error(p.err, ABKV_DEVERR_TIMEOUT);
+    const int t = tile0 + gi * nsub + sub;
+    if (t < tile1) {
+      bool ok;
+      tile_page(t, ok);
+      const int tok0 = t * kTile;
+      const uint8_t* kb = smem + (size_t)st * kStageBytes + (size_t)sub * 2 * tile_half + h * kD * 2;
+      const uint8_t* vb = kb + tile_half;
+
+      // S = Q.K^T : rows = query heads (g < G real), cols = tokens 8nt + 2c + {0,1}
+      float s[2][4];
 #pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
-      s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
+      for (int nt = 0; nt < 2; ++nt) {
+        const int T = 8 * nt + g;
+        const bool valid = ok && (tok0 + T < seq_len);
+        uint32_t kr[4][4];
 #pragma unroll
-      for (int m = 0; m < 4; ++m) {
-        mma_bf16_16816(s[nt], qr[m][0], 0u, qr[m][1], 0u, kr[nt][m][0], kr[nt][m][1]);
-        mma_bf16_16816(s[nt], qr[m][2], 0u, qr[m][3], 0u, kr[nt][m][2], kr[nt][m][3]);
+        for (int m = 0; m < 4; ++m) {
+          uint4 v = make_uint4(0, 0, 0, 0);
+          if (valid) v = lds128(kb + T * row_bytes + (32 * m + 8 * c) * 2);
+          kr[m][0] = v.x; kr[m][1] = v.y; kr[m][2] = v.z; kr[m][3] = v.w;
+        }
+        s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+          mma_bf16_16816(s[nt], qr[m][0], 0u, qr[m][1], 0u, kr[m][0], kr[m][1]);
+          mma_bf16_16816(s[nt], qr[m][2], 0u, qr[m][3], 0u, kr[m][2], kr[m][3]);
+        }
+      }
+
+      // online softmax (base-2, scale folded in)
+      float x[2][2];
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const bool valid = ok && (tok0 + 8 * nt + 2 * c + j < seq_len);
+          x[nt][j] = valid ? s[nt][j] * sl2 : -INFINITY;
+        }
+      float tmax = fmaxf(fmaxf(x[0][0], x[0][1]), fmaxf(x[1][0], x[1][1]));
+      tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 1));
+      tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 2));
+      const float m_new = fmaxf(m_run, tmax);
+      const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+      const float alpha = exp2f(m_run - m_use);
+      float pr[2][2];
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int j = 0; j < 2; ++j) pr[nt][j] = exp2f(x[nt][j] - m_use);
+      l_run = l_run * alpha + ((pr[0][0] + pr[0][1]) + (pr[1][0] + pr[1][1]));
+      m_run = m_new;
+
+      // O^T columns held by this lane are heads 2c and 2c+1
+      const float a0 = __shfl_sync(0xffffffffu, alpha, 8 * c);
+      const float a1 = __shfl_sync(0xffffffffu, alpha, 8 * c + 4);
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) {
+        o[mt][0] *= a0; o[mt][1] *= a1; o[mt][2] *= a0; o[mt][3] *= a1;
+      }
+      const uint32_t pb0 = pack_bf16x2(pr[0][0], pr[0][1]);
+      const uint32_t pb1 = pack_bf16x2(pr[1][0], pr[1][1]);
+
+      // V rows 2c, 2c+1, 2c+8, 2c+9 (zero when masked: 0 * NaN would poison O)
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        uint32_t vr[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int T = 2 * c + (i & 1) + 8 * (i >> 1);
+          uint4 v = make_uint4(0, 0, 0, 0);
+          if (ok && (tok0 + T < seq_len)) v = lds128(vb + T * row_bytes + (64 * hh + 8 * g) * 2);
+          vr[i][0] = v.x; vr[i][1] = v.y; vr[i][2] = v.z; vr[i][3] = v.w;
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int mt = 4 * hh + i;
+          const uint32_t v0 = vr[0][i], v1 = vr[1][i], v2 = vr[2][i], v3 = vr[3][i];
+          mma_bf16_16816(o[mt], prmt(v0, v1, 0x5410u), prmt(v0, v1, 0x7632u), prmt(v2, v3, 0x5410u),
+                         prmt(v2, v3, 0x7632u), pb0, pb1);
+        }
       }
     }
-    const int tok0 = t * kTile;
-    const bool ok_this = ok_cur;
-    const int tn = t + nsub;
-    const __nv_bfloat16* base_n = nullptr;
-    bool ok_next = false;
-    if (tn < tile1) {
-      base_n = tile_base(tn, ok_next);
-      load_k(tn, base_n, ok_next);
-    }
-
-    // online softmax (base-2, scale folded in)
-    float x[2][2];
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const bool valid = ok_this && (tok0 + 8 * nt + 2 * c + j < seq_len);
-        x[nt][j] = valid ? s[nt][j] * sl2 : -INFINITY;
-      }
-    float tmax = fmaxf(fmaxf(x[0][0], x[0][1]), fmaxf(x[1][0], x[1][1]));
-    tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 1));
-    tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 2));
-    const float m_new = fmaxf(m_run, tmax);
-    const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-    const float alpha = exp2f(m_run - m_use);
-    float pr[2][2];
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-      for (int j = 0; j < 2; ++j) pr[nt][j] = exp2f(x[nt][j] - m_use);
-    l_run = l_run * alpha + ((pr[0][0] + pr[0][1]) + (pr[1][0] + pr[1][1]));
-    m_run = m_new;
-
-    // O^T columns held by this lane are heads 2c and 2c+1
-    const float a0 = __shfl_sync(0xffffffffu, alpha, 8 * c);
-    const float a1 = __shfl_sync(0xffffffffu, alpha, 8 * c + 4);
-#pragma unroll
-    for (int mt = 0; mt < 8; ++mt) {
-      o[mt][0] *= a0; o[mt][1] *= a1; o[mt][2] *= a0; o[mt][3] *= a1;
-    }
-    const uint32_t pb0 = pack_bf16x2(pr[0][0], pr[0][1]);
-    const uint32_t pb1 = pack_bf16x2(pr[1][0], pr[1][1]);
-#pragma unroll
-    for (int mt = 0; mt < 8; ++mt) {
-      const int hh = mt >> 2, i = mt & 3;
-      const uint32_t v0 = vr[0][hh][i], v1 = vr[1][hh][i];
-      const uint32_t v2 = vr[2][hh][i], v3 = vr[3][hh][i];
-      mma_bf16_16816(o[mt], prmt(v0, v1, 0x5410u), prmt(v0, v1, 0x7632u), prmt(v2, v3, 0x5410u),
-                     prmt(v2, v3, 0x7632u), pb0, pb1);
-    }
-    if (tn < tile1) load_v(tn, base_n, ok_next);
-    ok_cur = ok_next;
+    __syncthreads();  // every warp is done with this stage
+    if (threadIdx.x == 0 && gi + kStages < ngroups) issue(gi + kStages);
   }
+
+  // epilogue arrays alias the (now idle) stage buffers
+  float (*s_o)[kMaxG][kD] = reinterpret_cast<float (*)[kMaxG][kD]>(smem);
+  float (*s_m)[kMaxG] = reinterpret_cast<float (*)[kMaxG]>(smem + sizeof(float) * kWarps * kMaxG * kD);
+  float (*s_l)[kMaxG] = s_m + kWarps;
 
   // ---- epilogue: per-warp partials -> shared memory -> merged output -----
   l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
@@ -445,6 +482,10 @@ extern "C" int abkv_decode(const void* const* q, const void* const* kv,
   }
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   char* ws = static_cast<char*>(workspace);
+  // opt in to > 48 KiB of dynamic shared memory (idempotent, per device)
+  if (cudaFuncSetAttribute(decode_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)kSmemBytes) != cudaSuccess)
+    return ABKV_ERR_CUDA;
 
   DecodeParams prm;
   memset(&prm, 0, sizeof(prm));
@@ -479,7 +520,7 @@ extern "C" int abkv_decode(const void* const* q, const void* const* kv,
     }
     prm.layer_base = l0;
     dim3 grid(plan.max_chunks, num_seqs, nl);
-    decode_split_kernel<<<grid, kThreads, 0, s>>>(prm);
+    decode_split_kernel<<<grid, kThreads, kSmemBytes, s>>>(prm);
   }
   if (cudaGetLastError() != cudaSuccess) return ABKV_ERR_CUDA;
   return ABKV_OK;
