@@ -62,7 +62,11 @@ def build(verbose: bool = False, ptxas_info: bool = False, force: bool = False) 
 
     def compile_one(src: Path) -> tuple[Path, str]:
         obj = BUILD / (src.stem + src.suffix.replace(".", "_") + ".o")
-        cmd = [nvcc] + (flags if src.suffix == ".cu" else COMMON + ["-x", "c++"]) + ["-c", str(src), "-o", str(obj)]
+        if src.suffix == ".cu":
+            cmd = [nvcc] + flags + ["-c", str(src), "-o", str(obj)]
+        else:  # host-only C++ (the planner): plain g++
+            cmd = [shutil.which("g++") or "g++", "-O3", "-std=c++17", "-fPIC", "-Wall", f"-I{INCLUDE}",
+                   f"-I{CSRC}", "-c", str(src), "-o", str(obj)]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"nvcc failed on {src.name}:\n{' '.join(cmd)}\n{r.stdout}\n{r.stderr}")

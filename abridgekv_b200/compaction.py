@@ -67,8 +67,10 @@ def _compact(layer_caches: Sequence[torch.Tensor], batches: Sequence[Sequence[Se
     s = torch.cuda.current_stream(kv0.device) if stream is None else stream
     ops_arr = _lib.i32_array(flat)
     off_arr = _lib.i64_array(offsets)
-    st = lib.abkv_compact(_lib.ptr_array([kv.data_ptr() for kv in layer_caches]), len(layer_caches), layout,
-                          nb, page, 1, units, ops_arr, off_arr, n_batches, ws.ptr(), ws.nbytes, s.cuda_stream)
+    with torch.cuda.device(kv0.device):
+        st = lib.abkv_compact(_lib.ptr_array([kv.data_ptr() for kv in layer_caches]), len(layer_caches),
+                              layout, nb, page, 1, units, ops_arr, off_arr, n_batches, ws.ptr(), ws.nbytes,
+                              s.cuda_stream)
     _lib.check("abkv_compact", st)
 
 
@@ -116,9 +118,11 @@ def evict_columns(K: Sequence[torch.Tensor], V: Sequence[torch.Tensor], keep_col
     outs = [torch.empty((b, h, n, d), dtype=t0.dtype, device=t0.device) for _ in tensors]
     ws = workspace or default_workspace(t0.device)
     s = torch.cuda.current_stream(t0.device) if stream is None else stream
-    st = _lib.lib().abkv_gather_rows(
-        _lib.ptr_array([t.data_ptr() for t in tensors]), _lib.ptr_array([o.data_ptr() for o in outs]),
-        len(tensors), b * h, T, n, d * t0.element_size(), keep.data_ptr(), ws.ptr(), ws.nbytes, s.cuda_stream)
+    with torch.cuda.device(t0.device):
+        st = _lib.lib().abkv_gather_rows(
+            _lib.ptr_array([t.data_ptr() for t in tensors]), _lib.ptr_array([o.data_ptr() for o in outs]),
+            len(tensors), b * h, T, n, d * t0.element_size(), keep.data_ptr(), ws.ptr(), ws.nbytes,
+            s.cuda_stream)
     _lib.check("abkv_gather_rows", st)
     L = len(K)
     return outs[:L], outs[L:]

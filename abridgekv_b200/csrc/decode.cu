@@ -7,30 +7,32 @@
 // is the PyTorch image of the FlashInfer decode the vLLM overlay runs per KV
 // cache group (gpu_model_runner.py:1672-1681, 2184-2204).
 //
-// Work decomposition.  One CTA = (split-KV chunk, sequence, layer); its eight
-// warps cover the KV heads of that chunk (warp w -> head w % Hkv; with fewer
-// than eight KV heads the remaining warps take interleaved tiles of the same
-// head and are merged through shared memory).  A "tile" is 16 consecutive
-// cache rows.  Per tile a warp:
-//   * loads K rows g and g+8 (g = lane/4) as four 16-byte vectors each and V
-//     rows 2c,2c+1,2c+8,2c+9 (c = lane%4) as two 16-byte vectors each, straight
-//     from HBM into registers in mma fragment order (dims are permuted
-//     consistently between Q and K, and between V and the output, so no shared
-//     memory or ldmatrix is needed; every warp load covers whole 32-byte
-//     sectors);
+// Structure: a persistent kernel, one CTA per SM (8 consumer warps + 1
+// producer warp).  Work items are (split-KV chunk, layer, sequence); the
+// producer takes them from a global atomic counter (chunk-major order, empty
+// chunks skipped), stages each item's page ids in shared memory and streams
+// "tile groups" into a 3-stage shared-memory ring with bulk copies
+// (cp.async.bulk on the TMA engine, no multicast) completed on full/empty
+// mbarriers, running ahead across item boundaries.  A tile is 16 cache rows;
+// a group holds one tile per consumer-warp slot (K rows then V rows, all KV
+// heads: 64 KiB for head_dim 128).  Consumer warp w handles KV head w % Hkv
+// (with fewer than 8 KV heads, warps of one head take different tiles of a
+// group and are merged at the end of the item).  Per tile a warp
+//   * reads K rows g and g+8 (g = lane/4) and V rows 2c,2c+1,2c+8,2c+9
+//     (c = lane%4) from shared memory in mma fragment order (dims permuted
+//     consistently between Q and K, and between V and the output);
 //   * S = Q.K^T with mma.m16n8k16 (rows = the G query heads of the KV head);
 //   * online softmax in fp32 (quad shuffles), P rounded to bf16 as the
 //     reference does before its P.V product;
 //   * O^T += V^T.P^T with mma.m16n8k16: the S accumulator fragment is exactly
 //     the B fragment of this product, so P never leaves registers.
-// The block-table slice of the chunk is staged into shared memory by one bulk
-// copy (cp.async.bulk on the TMA engine, no multicast) completed on an
-// mbarrier with a bounded wait.
-// Chunks of one (layer, sequence) are merged inside the same launch: each
-// chunk CTA stores its normalised partial and log-sum-exp, and the last one
-// to finish (a per-(layer, sequence) counter in the workspace, reset by that
-// CTA) combines them.  Single-chunk rows are written directly.  Concurrent
-// calls must not share a workspace.
+// At the end of an item the consumers merge warp partials in shared memory
+// (named barrier 1, consumers only); single-chunk rows are written directly,
+// otherwise each chunk stores a normalised partial + log-sum-exp and the last
+// chunk to finish for its (layer, sequence) (a counter in the workspace,
+// reset by that chunk) combines them.  The last CTA to run out of work resets
+// the work counters, so a workspace is ready for the next call; concurrent
+// calls must not share a workspace.  Every mbarrier wait is bounded.
 #include <cstring>
 
 #include "common.cuh"
@@ -40,11 +42,14 @@ namespace {
 
 constexpr int kD = 128;
 constexpr int kTile = 16;
-constexpr int kWarps = 8;
-constexpr int kThreads = kWarps * 32;
+constexpr int kWarps = 8;                  // consumer warps
+constexpr int kThreads = (kWarps + 1) * 32;  // + producer warp
+constexpr int kConsumerThreads = kWarps * 32;
 constexpr int kMaxLayers = 56;       // layers per launch: keeps params < 4 KB
-constexpr int kMaxChunkPages = 256;  // page ids staged per CTA
+constexpr int kMaxChunkPages = 256;  // page ids staged per work item
 constexpr int kMaxG = 8;             // query heads per KV head
+constexpr int kStages = 3;
+constexpr int kStageBytes = kWarps * 2 * kTile * kD * 2;  // nsub * Hkv == kWarps -> 64 KiB
 
 struct LayerArgs {
   const __nv_bfloat16* q;
@@ -58,15 +63,33 @@ struct LayerArgs {
 
 struct DecodeParams {
   LayerArgs layer[kMaxLayers];
-  float* part_o;    // [layers][B][max_chunks][Hq][D]
-  float* part_lse;  // [layers][B][max_chunks][Hq]
+  float* part_o;      // [layers][B][max_chunks][Hq][D]
+  float* part_lse;    // [layers][B][max_chunks][Hq]
   int32_t* counters;  // [layers][B] chunks finished; zero between calls
+  int32_t* work;      // [2]: next item, CTAs done; zero between calls
   int32_t* err;
   float scale_log2;
   int B, Hq, Hkv, G, P;
   int chunk_tiles, max_chunks, max_rows;
-  int layer_base;
+  int layer_base, nl;
+  int num_items;
 };
+
+struct StageMeta {
+  int li, b, chunk, n_chunks, seq_len, t0, ntiles, bits;  // bits: ok mask | kFirst | kLast
+};
+constexpr int kFirst = 1 << 8;
+constexpr int kLast = 1 << 9;
+
+// Dynamic shared memory layout.
+constexpr size_t kOffStage = 0;
+constexpr size_t kOffO = kOffStage + (size_t)kStages * kStageBytes;        // float[8][8][128]
+constexpr size_t kOffML = kOffO + sizeof(float) * kWarps * kMaxG * kD;     // float[2][8][8]
+constexpr size_t kOffMeta = kOffML + sizeof(float) * 2 * kWarps * kMaxG;   // StageMeta[kStages]
+constexpr size_t kOffPages = kOffMeta + sizeof(StageMeta) * kStages;       // int32[kMaxChunkPages]
+constexpr size_t kOffBar = kOffPages + sizeof(int32_t) * kMaxChunkPages;   // u64 full[3], empty[3]
+constexpr size_t kOffFlag = kOffBar + sizeof(uint64_t) * 2 * kStages;
+constexpr size_t kSmemBytes = kOffFlag + 16;
 
 __device__ __forceinline__ int clamp_seq_len(const DecodeParams& p, const LayerArgs& L, int b,
                                              bool report) {
@@ -80,151 +103,181 @@ __device__ __forceinline__ int clamp_seq_len(const DecodeParams& p, const LayerA
   return s;
 }
 
-// Dynamic shared memory layout of decode_split_kernel:
-//   [kStages][kStageBytes]  K/V tile groups (a group = nsub tiles, one per
-//                           warp slot; tile = 16 cache rows, K then V, all
-//                           KV heads) -- 64 KiB per stage for head_dim 128
-//   s_pages[kMaxChunkPages + 4]
-//   mbarriers: full[kStages], page-list barrier
-// After the main loop the stage buffers are reused for the epilogue arrays.
-constexpr int kStages = 3;
-constexpr int kStageBytes = kWarps * 2 * kTile * kD * 2;  // nsub * Hkv == kWarps
-constexpr size_t kSmemBytes =
-    (size_t)kStages * kStageBytes + (kMaxChunkPages + 4) * sizeof(int32_t) + (kStages + 1) * 8;
-
-__device__ __forceinline__ uint4 lds128(const void* p) {
+__device__ __forceinline__ uint4 lds128(const void* ptr) {
   uint4 r;
   asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];\n"
                : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-               : "r"(smem_u32(p)));
+               : "r"(smem_u32(ptr)));
   return r;
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
-    decode_split_kernel(const __grid_constant__ DecodeParams p) {
-  extern __shared__ __align__(1024) uint8_t smem[];
-  int32_t* s_pages = reinterpret_cast<int32_t*>(smem + (size_t)kStages * kStageBytes);
-  uint64_t* full = reinterpret_cast<uint64_t*>(s_pages + kMaxChunkPages + 4);
-  uint64_t* pg_bar = full + kStages;
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(bar)) : "memory");
+}
 
-  const int chunk = blockIdx.x, b = blockIdx.y, li = blockIdx.z;
-  const LayerArgs& L = p.layer[li];
-  const int seq_len = clamp_seq_len(p, L, b, chunk == 0 && threadIdx.x == 0);
-  const int n_tiles = (seq_len + kTile - 1) / kTile;
-  const int n_chunks = (n_tiles + p.chunk_tiles - 1) / p.chunk_tiles;
+__device__ __forceinline__ void consumer_sync() {
+  asm volatile("bar.sync 1, %0;\n" ::"n"(kConsumerThreads) : "memory");
+}
 
-  if (n_chunks == 0) {  // empty sequence: defined as an all-zero row
-    if (chunk == 0) {
-      __nv_bfloat16* o = L.out + (int64_t)b * p.Hq * kD;
-      for (int i = threadIdx.x; i < p.Hq * kD; i += kThreads) o[i] = __float2bfloat16(0.f);
-    }
-    return;
-  }
-  if (chunk >= n_chunks) return;
-
-  const int tile0 = chunk * p.chunk_tiles;
-  const int tile1 = min(tile0 + p.chunk_tiles, n_tiles);
-  const int page0 = tile0 * kTile / p.P;
-  const int page1 = (tile1 * kTile + p.P - 1) / p.P;
-  const int npages = page1 - page0;
-
-  // ---- stage this chunk's page ids in shared memory --------------------
-  const int32_t* src = L.bt + (int64_t)b * L.bt_stride + page0;
-  int head = (int)(((16 - (reinterpret_cast<uintptr_t>(src) & 15)) & 15) >> 2);
-  if (head > npages) head = npages;
-  const int body = ((npages - head) >> 2) << 2;
-  const int shift = (4 - head) & 3;  // makes s_pages + shift + head 16-byte aligned
-  if (threadIdx.x == 0) {
-    for (int s2 = 0; s2 < kStages; ++s2) mbar_init(&full[s2], 1);
-    if (body > 0) mbar_init(pg_bar, 1);
-  }
-  __syncthreads();
-  if (threadIdx.x == 0 && body > 0) {
-    mbar_expect_tx(pg_bar, (uint32_t)body * 4u);
-    bulk_g2s(s_pages + shift + head, src + head, (uint32_t)body * 4u, pg_bar);
-  }
-  for (int i = threadIdx.x; i < head; i += kThreads) s_pages[shift + i] = __ldg(src + i);
-  for (int i = head + body + threadIdx.x; i < npages; i += kThreads)
-    s_pages[shift + i] = __ldg(src + i);
-  if (body > 0 && !mbar_wait(pg_bar, 0)) set_error(p.err, ABKV_DEVERR_TIMEOUT);
-  __syncthreads();
-
-  // ---- bulk-copy pipeline over tile groups --------------------------------
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int Hkv = p.Hkv, G = p.G, P = p.P;
-  const int h = warp % Hkv, sub = warp / Hkv, nsub = kWarps / Hkv;
-  const int g = lane >> 2, c = lane & 3;
-  const int row_bytes = Hkv * kD * 2;      // one cache row, all KV heads
-  const int tile_half = kTile * row_bytes;  // 16 rows of K (or of V)
+// ---------------------------------------------------------------------------
+__device__ void producer(const DecodeParams& p, uint8_t* smem) {
+  StageMeta* meta = reinterpret_cast<StageMeta*>(smem + kOffMeta);
+  int32_t* s_pages = reinterpret_cast<int32_t*>(smem + kOffPages);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  uint64_t* empty = full + kStages;
+  const int lane = threadIdx.x & 31;
+  const int Hkv = p.Hkv, P = p.P, nsub = kWarps / Hkv;
+  const int tile_half = kTile * Hkv * kD * 2;
   const int64_t row_elems = (int64_t)Hkv * kD;
   const int64_t half_elems = (int64_t)P * row_elems;
   const int64_t page_elems = 2 * half_elems;
-  const int64_t nblk = L.num_blocks;
-  const int ngroups = (tile1 - tile0 + nsub - 1) / nsub;
+  const int lb_items = p.nl * p.B;
+  int gq = 0;  // groups issued by this CTA
+  bool alive = true;
 
-  auto tile_page = [&](int t, bool& ok) -> int64_t {
-    const int pg = s_pages[shift + t * kTile / P - page0];
-    ok = pg >= 0 && (int64_t)pg < nblk;
-    return pg;
-  };
-  // thread 0: copy tile group gi (K rows then V rows of each tile) into its stage
-  auto issue = [&](int gi) {
-    const int st = gi % kStages;
-    uint8_t* dst = smem + (size_t)st * kStageBytes;
-    uint32_t bytes = 0;
-    for (int j = 0; j < nsub; ++j) {
-      const int t = tile0 + gi * nsub + j;
-      bool ok = false;
-      if (t < tile1) tile_page(t, ok);
-      if (ok) bytes += 2u * (uint32_t)tile_half;
-    }
-    mbar_expect_tx(&full[st], bytes);
-    for (int j = 0; j < nsub; ++j) {
-      const int t = tile0 + gi * nsub + j;
-      if (t >= tile1) break;
-      bool ok;
-      const int64_t pg = tile_page(t, ok);
-      if (!ok) {
-        set_error(p.err, ABKV_DEVERR_PAGE_OOB);
-        continue;
+  while (alive) {
+    int li = -1, b = 0, chunk = 0, nch = 0, slen = 0;
+    if (lane == 0) {
+      for (;;) {
+        const int i = atomicAdd(p.work, 1);
+        if (i >= p.num_items) break;
+        chunk = i / lb_items;
+        const int rem = i - chunk * lb_items;
+        li = rem / p.B;
+        b = rem - li * p.B;
+        slen = clamp_seq_len(p, p.layer[li], b, chunk == 0);
+        const int ntl = (slen + kTile - 1) / kTile;
+        nch = max(1, (ntl + p.chunk_tiles - 1) / p.chunk_tiles);
+        if (chunk < nch) break;
+        li = -1;
       }
-      const __nv_bfloat16* ksrc = L.kv + pg * page_elems + (int64_t)((t * kTile) % P) * row_elems;
-      bulk_g2s(dst + (size_t)j * 2 * tile_half, ksrc, (uint32_t)tile_half, &full[st]);
-      bulk_g2s(dst + (size_t)j * 2 * tile_half + tile_half, ksrc + half_elems, (uint32_t)tile_half,
-               &full[st]);
     }
-  };
-
-  uint32_t qr[4][4];
-  {
-    const __nv_bfloat16* qrow = L.q + ((int64_t)b * p.Hq + h * G + g) * kD + 8 * c;
-#pragma unroll
-    for (int m = 0; m < 4; ++m) {
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (g < G) v = __ldg(reinterpret_cast<const uint4*>(qrow + 32 * m));
-      qr[m][0] = v.x; qr[m][1] = v.y; qr[m][2] = v.z; qr[m][3] = v.w;
+    li = __shfl_sync(0xffffffffu, li, 0);
+    if (li < 0) break;
+    b = __shfl_sync(0xffffffffu, b, 0);
+    chunk = __shfl_sync(0xffffffffu, chunk, 0);
+    nch = __shfl_sync(0xffffffffu, nch, 0);
+    slen = __shfl_sync(0xffffffffu, slen, 0);
+    const LayerArgs& L = p.layer[li];
+    const int ntl = (slen + kTile - 1) / kTile;
+    const int tile0 = chunk * p.chunk_tiles;
+    const int tile1 = min(tile0 + p.chunk_tiles, ntl);
+    const int ntiles = max(0, tile1 - tile0);
+    const int page0 = tile0 * kTile / P;
+    const int npages = ntiles ? (tile1 * kTile + P - 1) / P - page0 : 0;
+    const int32_t* bt = L.bt + (int64_t)b * L.bt_stride + page0;
+    for (int i = lane; i < npages; i += 32) s_pages[i] = __ldg(bt + i);
+    __syncwarp();
+    const int ngroups = max(1, (ntiles + nsub - 1) / nsub);
+    for (int grp = 0; grp < ngroups; ++grp, ++gq) {
+      if (lane == 0) {
+        const int st = gq % kStages;
+        const uint32_t k = (uint32_t)(gq / kStages);
+        if (!mbar_wait(&empty[st], (k & 1u) ^ 1u)) {
+          set_error(p.err, ABKV_DEVERR_TIMEOUT);
+          alive = false;
+        }
+        int okmask = 0;
+        uint32_t bytes = 0;
+        const int tg0 = tile0 + grp * nsub;
+        const int nt = min(nsub, tile1 - tg0) > 0 ? min(nsub, tile1 - tg0) : 0;
+        for (int j = 0; j < nt; ++j) {
+          const int pg = s_pages[(tg0 + j) * kTile / P - page0];
+          if (pg >= 0 && (int64_t)pg < L.num_blocks) {
+            okmask |= 1 << j;
+            bytes += 2u * (uint32_t)tile_half;
+          } else {
+            set_error(p.err, ABKV_DEVERR_PAGE_OOB);
+          }
+        }
+        StageMeta m;
+        m.li = li; m.b = b; m.chunk = chunk; m.n_chunks = nch; m.seq_len = slen;
+        m.t0 = tg0; m.ntiles = nt;
+        m.bits = okmask | (grp == 0 ? kFirst : 0) | (grp == ngroups - 1 ? kLast : 0);
+        meta[st] = m;
+        mbar_expect_tx(&full[st], bytes);  // release: meta is visible once the phase completes
+        uint8_t* dst = smem + kOffStage + (size_t)st * kStageBytes;
+        for (int j = 0; j < nt; ++j) {
+          if (!((okmask >> j) & 1)) continue;
+          const int t = tg0 + j;
+          const int64_t pg = s_pages[t * kTile / P - page0];
+          const __nv_bfloat16* ksrc = L.kv + pg * page_elems + (int64_t)((t * kTile) % P) * row_elems;
+          bulk_g2s(dst + (size_t)j * 2 * tile_half, ksrc, (uint32_t)tile_half, &full[st]);
+          bulk_g2s(dst + (size_t)j * 2 * tile_half + tile_half, ksrc + half_elems, (uint32_t)tile_half,
+                   &full[st]);
+        }
+      }
+      alive = __shfl_sync(0xffffffffu, alive ? 1 : 0, 0) != 0;
+      if (!alive) break;
+    }
+    __syncwarp();  // s_pages is rewritten for the next item only after this one is issued
+  }
+  if (lane == 0) {
+    // end-of-work marker for the consumers
+    const int st = gq % kStages;
+    const uint32_t k = (uint32_t)(gq / kStages);
+    if (!mbar_wait(&empty[st], (k & 1u) ^ 1u)) set_error(p.err, ABKV_DEVERR_TIMEOUT);
+    meta[st].li = -1;
+    mbar_expect_tx(&full[st], 0u);
+    // the last CTA to run out of work resets the work counters for the next call
+    __threadfence();
+    const int prev = atomicAdd(p.work + 1, 1);
+    if (prev == (int)gridDim.x - 1) {
+      p.work[0] = 0;
+      p.work[1] = 0;
     }
   }
+}
 
-  if (threadIdx.x == 0) {
-    for (int gi = 0; gi < kStages && gi < ngroups; ++gi) issue(gi);
-  }
+// ---------------------------------------------------------------------------
+__device__ void consumer(const DecodeParams& p, uint8_t* smem) {
+  const StageMeta* meta = reinterpret_cast<const StageMeta*>(smem + kOffMeta);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  uint64_t* empty = full + kStages;
+  float (*s_o)[kMaxG][kD] = reinterpret_cast<float (*)[kMaxG][kD]>(smem + kOffO);
+  float (*s_m)[kMaxG] = reinterpret_cast<float (*)[kMaxG]>(smem + kOffML);
+  float (*s_l)[kMaxG] = s_m + kWarps;
+  int* s_flag = reinterpret_cast<int*>(smem + kOffFlag);
 
-  float o[8][4];
-#pragma unroll
-  for (int mt = 0; mt < 8; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
-  float m_run = -INFINITY, l_run = 0.f;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int Hkv = p.Hkv, G = p.G;
+  const int h = warp % Hkv, sub = warp / Hkv, nsub = kWarps / Hkv;
+  const int g = lane >> 2, c = lane & 3;
+  const int row_bytes = Hkv * kD * 2;
+  const int tile_half = kTile * row_bytes;
   const float sl2 = p.scale_log2;
 
-  for (int gi = 0; gi < ngroups; ++gi) {
-    const int st = gi % kStages;
-    if (!mbar_wait(&full[st], (uint32_t)((gi / kStages) & 1))) set_error(p.err, ABKV_DEVERR_TIMEOUT);
-    const int t = tile0 + gi * nsub + sub;
-    if (t < tile1) {
-      bool ok;
-      tile_page(t, ok);
-      const int tok0 = t * kTile;
-      const uint8_t* kb = smem + (size_t)st * kStageBytes + (size_t)sub * 2 * tile_half + h * kD * 2;
+  float o[8][4];
+  float m_run = -INFINITY, l_run = 0.f;
+  uint32_t qr[4][4];
+
+  for (int gq = 0;; ++gq) {
+    const int st = gq % kStages;
+    if (!mbar_wait(&full[st], (uint32_t)((gq / kStages) & 1))) {
+      set_error(p.err, ABKV_DEVERR_TIMEOUT);
+      break;
+    }
+    const StageMeta M = meta[st];
+    if (M.li < 0) break;
+    const LayerArgs& L = p.layer[M.li];
+    if (M.bits & kFirst) {
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+      m_run = -INFINITY;
+      l_run = 0.f;
+      const __nv_bfloat16* qrow = L.q + ((int64_t)M.b * p.Hq + h * G + g) * kD + 8 * c;
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (g < G) v = __ldg(reinterpret_cast<const uint4*>(qrow + 32 * m));
+        qr[m][0] = v.x; qr[m][1] = v.y; qr[m][2] = v.z; qr[m][3] = v.w;
+      }
+    }
+    if (sub < M.ntiles) {
+      const bool ok = (M.bits >> sub) & 1;
+      const int tok0 = (M.t0 + sub) * kTile;
+      const int seq_len = M.seq_len;
+      const uint8_t* kb = smem + kOffStage + (size_t)st * kStageBytes + (size_t)sub * 2 * tile_half + h * kD * 2;
       const uint8_t* vb = kb + tile_half;
 
       // S = Q.K^T : rows = query heads (g < G real), cols = tokens 8nt + 2c + {0,1}
@@ -301,98 +354,115 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-    __syncthreads();  // every warp is done with this stage
-    if (threadIdx.x == 0 && gi + kStages < ngroups) issue(gi + kStages);
-  }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[st]);  // this warp is done with the stage
+    if (!(M.bits & kLast)) continue;
 
-  // epilogue arrays alias the (now idle) stage buffers
-  float (*s_o)[kMaxG][kD] = reinterpret_cast<float (*)[kMaxG][kD]>(smem);
-  float (*s_m)[kMaxG] = reinterpret_cast<float (*)[kMaxG]>(smem + sizeof(float) * kWarps * kMaxG * kD);
-  float (*s_l)[kMaxG] = s_m + kWarps;
-
-  // ---- epilogue: per-warp partials -> shared memory -> merged output -----
-  l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
-  l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+    // ---- end of item: merge warp partials, write output or chunk partial ----
+    float lq = l_run;
+    lq += __shfl_xor_sync(0xffffffffu, lq, 1);
+    lq += __shfl_xor_sync(0xffffffffu, lq, 2);
 #pragma unroll
-  for (int jh = 0; jh < 2; ++jh) {
-    const int head = 2 * c + jh;
-    if (head < G) {
+    for (int jh = 0; jh < 2; ++jh) {
+      const int head = 2 * c + jh;
+      if (head < G) {
 #pragma unroll
-      for (int mt = 0; mt < 8; ++mt) {
-        const int hh = mt >> 2, i = mt & 3;
-        const int d = 8 * g + 64 * hh + 2 * i;
-        s_o[warp][head][d] = o[mt][jh];
-        s_o[warp][head][d + 1] = o[mt][2 + jh];
+        for (int mt = 0; mt < 8; ++mt) {
+          const int hh = mt >> 2, i = mt & 3;
+          const int d = 8 * g + 64 * hh + 2 * i;
+          s_o[warp][head][d] = o[mt][jh];
+          s_o[warp][head][d + 1] = o[mt][2 + jh];
+        }
       }
     }
-  }
-  if (c == 0 && g < G) {
-    s_m[warp][g] = m_run;
-    s_l[warp][g] = l_run;
-  }
-  __syncthreads();
-
-  const int items = p.Hq * kD;
-  const int64_t lb = (int64_t)(p.layer_base + li) * p.B + b;  // (layer, sequence) slot
-  const int64_t prow = (lb * p.max_chunks + chunk) * p.Hq;
-  for (int it = threadIdx.x; it < items; it += kThreads) {
-    const int d = it % kD, hr = it / kD;
-    const int kh = hr / G, r = hr % G;
-    float M = -INFINITY;
-    for (int s2 = 0; s2 < nsub; ++s2) M = fmaxf(M, s_m[s2 * Hkv + kh][r]);
-    const float Mu = (M == -INFINITY) ? 0.f : M;
-    float Ls = 0.f, Os = 0.f;
-    for (int s2 = 0; s2 < nsub; ++s2) {
-      const int w = s2 * Hkv + kh;
-      const float f = exp2f(s_m[w][r] - Mu);
-      Ls += s_l[w][r] * f;
-      Os += s_o[w][r][d] * f;
+    if (c == 0 && g < G) {
+      s_m[warp][g] = m_run;
+      s_l[warp][g] = lq;
     }
-    const float val = Ls > 0.f ? Os / Ls : 0.f;
-    if (n_chunks == 1) {
-      L.out[((int64_t)b * p.Hq + hr) * kD + d] = __float2bfloat16(val);
-    } else {
-      p.part_o[(prow + hr) * kD + d] = val;
-      if (d == 0) p.part_lse[prow + hr] = Ls > 0.f ? Mu + log2f(Ls) : -INFINITY;
+    consumer_sync();
+    const int items = p.Hq * kD;
+    const int n_chunks = M.n_chunks;
+    const int64_t lb = (int64_t)(p.layer_base + M.li) * p.B + M.b;  // (layer, sequence) slot
+    const int64_t prow = (lb * p.max_chunks + M.chunk) * p.Hq;
+    for (int it = threadIdx.x; it < items; it += kConsumerThreads) {
+      const int d = it % kD, hr = it / kD;
+      const int kh = hr / G, r = hr % G;
+      float Mx = -INFINITY;
+      for (int s2 = 0; s2 < nsub; ++s2) Mx = fmaxf(Mx, s_m[s2 * Hkv + kh][r]);
+      const float Mu = (Mx == -INFINITY) ? 0.f : Mx;
+      float Ls = 0.f, Os = 0.f;
+      for (int s2 = 0; s2 < nsub; ++s2) {
+        const int w = s2 * Hkv + kh;
+        const float f = exp2f(s_m[w][r] - Mu);
+        Ls += s_l[w][r] * f;
+        Os += s_o[w][r][d] * f;
+      }
+      const float val = Ls > 0.f ? Os / Ls : 0.f;
+      if (n_chunks == 1) {
+        L.out[((int64_t)M.b * p.Hq + hr) * kD + d] = __float2bfloat16(val);
+      } else {
+        p.part_o[(prow + hr) * kD + d] = val;
+        if (d == 0) p.part_lse[prow + hr] = Ls > 0.f ? Mu + log2f(Ls) : -INFINITY;
+      }
     }
+    if (n_chunks > 1) {
+      // the last chunk of this (layer, sequence) combines all chunk partials
+      __threadfence();
+      consumer_sync();
+      if (threadIdx.x == 0) {
+        const int prev = atomicAdd(p.counters + lb, 1);
+        *s_flag = (prev == n_chunks - 1);
+      }
+      consumer_sync();
+      if (*s_flag) {
+        __threadfence();
+        const int64_t row0 = lb * p.max_chunks * p.Hq;
+        for (int it = threadIdx.x; it < items; it += kConsumerThreads) {
+          const int d = it % kD, hr = it / kD;
+          float Mx = -INFINITY;
+          for (int ch = 0; ch < n_chunks; ++ch)
+            Mx = fmaxf(Mx, __ldcg(p.part_lse + row0 + (int64_t)ch * p.Hq + hr));
+          const float Mu = (Mx == -INFINITY) ? 0.f : Mx;
+          float Ls = 0.f, Os = 0.f;
+          for (int ch = 0; ch < n_chunks; ++ch) {
+            const int64_t rr = row0 + (int64_t)ch * p.Hq + hr;
+            const float f = exp2f(__ldcg(p.part_lse + rr) - Mu);
+            Ls += f;
+            Os += f * __ldcg(p.part_o + rr * kD + d);
+          }
+          L.out[((int64_t)M.b * p.Hq + hr) * kD + d] = __float2bfloat16(Ls > 0.f ? Os / Ls : 0.f);
+        }
+        if (threadIdx.x == 0) p.counters[lb] = 0;  // ready for the next call on this workspace
+      }
+    }
+    consumer_sync();  // s_o / s_m / s_l / s_flag may be rewritten by the next item
   }
-  if (n_chunks == 1) return;
+}
 
-  // ---- split-KV merge: the last chunk CTA of this (layer, sequence) combines
-  // every chunk's partial with log-sum-exp weights and resets the counter.
-  __shared__ int s_last;
-  __threadfence();
-  __syncthreads();
+__global__ void __launch_bounds__(kThreads, 1) decode_split_kernel(const __grid_constant__ DecodeParams p) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  uint64_t* empty = full + kStages;
   if (threadIdx.x == 0) {
-    const int prev = atomicAdd(p.counters + lb, 1);
-    s_last = (prev == n_chunks - 1);
+    for (int st = 0; st < kStages; ++st) {
+      mbar_init(&full[st], 1);
+      mbar_init(&empty[st], kWarps);
+    }
   }
   __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  const int64_t row0 = lb * p.max_chunks * p.Hq;
-  for (int it = threadIdx.x; it < items; it += kThreads) {
-    const int d = it % kD, hr = it / kD;
-    float M = -INFINITY;
-    for (int ch = 0; ch < n_chunks; ++ch) M = fmaxf(M, __ldcg(p.part_lse + row0 + (int64_t)ch * p.Hq + hr));
-    const float Mu = (M == -INFINITY) ? 0.f : M;
-    float Ls = 0.f, Os = 0.f;
-    for (int ch = 0; ch < n_chunks; ++ch) {
-      const int64_t rr = row0 + (int64_t)ch * p.Hq + hr;
-      const float f = exp2f(__ldcg(p.part_lse + rr) - Mu);
-      Ls += f;
-      Os += f * __ldcg(p.part_o + rr * kD + d);
-    }
-    L.out[((int64_t)b * p.Hq + hr) * kD + d] = __float2bfloat16(Ls > 0.f ? Os / Ls : 0.f);
+  if ((threadIdx.x >> 5) == kWarps) {
+    producer(p, smem);
+  } else {
+    consumer(p, smem);
   }
-  if (threadIdx.x == 0) p.counters[lb] = 0;  // ready for the next call on this workspace
 }
 
 int auto_chunk_tiles(int num_layers, int num_seqs, int max_tiles, int page_tiles) {
-  // Aim for >= ~8 waves of two CTAs on 148 SMs, with chunks of 32..128 tiles.
+  // Persistent CTAs take items dynamically: aim for >= ~8 items per SM, with
+  // chunks of 16..128 tiles (256..2048 cache rows).
   const int64_t total = (int64_t)num_layers * num_seqs * max_tiles;
   int ct = 128;
-  while (ct > 32 && total / ct < 148 * 2 * 8) ct >>= 1;
+  while (ct > 16 && total / ct < 148 * 8) ct >>= 1;
   if (ct < page_tiles) ct = page_tiles;
   ct = (ct / page_tiles) * page_tiles;
   return ct;
@@ -486,10 +556,15 @@ extern "C" int abkv_decode(const void* const* q, const void* const* kv,
   if (cudaFuncSetAttribute(decode_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)kSmemBytes) != cudaSuccess)
     return ABKV_ERR_CUDA;
+  int dev = 0, num_sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || num_sms <= 0)
+    return ABKV_ERR_CUDA;
 
   DecodeParams prm;
   memset(&prm, 0, sizeof(prm));
   prm.err = reinterpret_cast<int32_t*>(ws);
+  prm.work = reinterpret_cast<int32_t*>(ws + 64);  // [next item, CTAs done], inside the header
   const bool split = plan.max_chunks > 1;
   prm.counters = split ? reinterpret_cast<int32_t*>(ws + kWsHeader) : nullptr;
   prm.part_lse = split ? reinterpret_cast<float*>(ws + kWsHeader + plan.counter_bytes) : nullptr;
@@ -519,7 +594,9 @@ extern "C" int abkv_decode(const void* const* q, const void* const* kv,
       a.num_blocks = num_blocks[l0 + i];
     }
     prm.layer_base = l0;
-    dim3 grid(plan.max_chunks, num_seqs, nl);
+    prm.nl = nl;
+    prm.num_items = plan.max_chunks * nl * num_seqs;
+    const int grid = prm.num_items < num_sms ? prm.num_items : num_sms;
     decode_split_kernel<<<grid, kThreads, kSmemBytes, s>>>(prm);
   }
   if (cudaGetLastError() != cudaSuccess) return ABKV_ERR_CUDA;

@@ -98,7 +98,16 @@ def paged_decode(
                              f"unsupported shape (B={B}, Hq={Hq}, D={D}, page={page})")
     ws = (workspace or default_workspace(device)).ensure(need)
     s = torch.cuda.current_stream(device) if stream is None else stream
-    st = lib.abkv_decode(
+    with torch.cuda.device(device):
+        st = _call_decode(lib, queries, kv_caches, block_tables, seq_lens, outs, L, B, Hq, Hkv, D, page,
+                          max_pages_per_seq, scale, chunk_tokens, ws, s)
+    _lib.check("abkv_decode", st)
+    return outs
+
+
+def _call_decode(lib, queries, kv_caches, block_tables, seq_lens, outs, L, B, Hq, Hkv, D, page,
+                 max_pages_per_seq, scale, chunk_tokens, ws, s):
+    return lib.abkv_decode(
         _lib.ptr_array([q.data_ptr() for q in queries]),
         _lib.ptr_array([kv.data_ptr() for kv in kv_caches]),
         _lib.ptr_array([bt.data_ptr() for bt in block_tables]),
@@ -109,8 +118,6 @@ def paged_decode(
         L, B, Hq, Hkv, D, page, max_pages_per_seq, float(scale), chunk_tokens,
         ws.ptr(), ws.nbytes, s.cuda_stream,
     )
-    _lib.check("abkv_decode", st)
-    return outs
 
 
 def attend_decode_batched(
