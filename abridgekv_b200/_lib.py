@@ -31,6 +31,11 @@ SIGNATURES: dict[str, tuple] = {
         [c_vpp, c_vpp, c_vpp, c_i64p, c_vpp, c_i64p, c_vpp, c_int, c_int, c_int, c_int, c_int,
          c_int, c_int, C.c_float, c_int, c_vp, c_size, c_vp],
     ),
+    "abkv_decode_noalloc": (
+        c_int,
+        [c_vpp, c_vpp, c_vpp, c_i64p, c_vpp, c_i64p, c_vpp, c_int, c_int, c_int, c_int, c_int,
+         c_int, c_int, C.c_float, c_int, c_vp, c_vp],
+    ),
     "abkv_planner_create": (c_vp, [c_int, c_int, c_int]),
     "abkv_planner_destroy": (None, [c_vp]),
     "abkv_planner_add_request": (c_int, [c_vp, C.c_int64]),

@@ -15,6 +15,7 @@ extern "C" const char* abkv_status_string(int status) {
     case ABKV_ERR_SPAN: return "span rejected by the compaction planner";
     case ABKV_ERR_NO_BLOCKS: return "free block queue exhausted";
     case ABKV_ERR_TIMEOUT: return "bounded device wait gave up";
+    case ABKV_ERR_SCRATCH_LIMIT: return "request exceeds the 32 MiB scratch of abkv_decode_noalloc";
     default: return "unknown status";
   }
 }

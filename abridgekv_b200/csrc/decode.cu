@@ -34,6 +34,7 @@
 // the work counters, so a workspace is ready for the next call; concurrent
 // calls must not share a workspace.  Every mbarrier wait is bounded.
 #include <cstring>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -600,5 +601,68 @@ extern "C" int abkv_decode(const void* const* q, const void* const* kv,
     decode_split_kernel<<<grid, kThreads, kSmemBytes, s>>>(prm);
   }
   if (cudaGetLastError() != cudaSuccess) return ABKV_ERR_CUDA;
+  return ABKV_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Decode without any allocation by the caller or by the library.
+//
+// Some callers cannot allocate device memory at the point where they decode:
+// an inference engine that reserves all of HBM for its KV cache up front and
+// forbids later cudaMalloc calls, a host loop whose allocator is not
+// thread-safe, or code that must not touch the CUDA caching allocator at all.
+// For them the split-KV scratch (partials, counters, error word) lives in one
+// file-scope device array of kNoAllocScratchBytes that every GPU loading this
+// library holds until process exit.  The caller passes only inputs and outputs.
+namespace {
+constexpr size_t kNoAllocScratchBytes = size_t(32) << 20;  // 32 MiB per device
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mutex;
+void* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+
+// Device address of g_noalloc_scratch on the current device.  In host code the
+// symbol name is only a host-side stand-in, so its address is looked up once
+// per device (with that device current) and cached.
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices) return ABKV_ERR_CUDA;
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) return ABKV_ERR_CUDA;
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return ABKV_OK;
+}
+}  // namespace
+
+extern "C" int abkv_decode_noalloc(const void* const* q, const void* const* kv,
+                                   const int32_t* const* block_tables, const int64_t* bt_strides,
+                                   const int32_t* const* seq_lens, const int64_t* num_blocks,
+                                   void* const* out, int num_layers, int num_seqs, int num_q_heads,
+                                   int num_kv_heads, int head_dim, int page_size, int max_pages_per_seq,
+                                   float scale, int chunk_tokens, int32_t* device_error, void* stream) {
+  DecodePlan plan;
+  const int st = plan_decode(num_layers, num_seqs, num_q_heads, head_dim, page_size, max_pages_per_seq,
+                             chunk_tokens, &plan);
+  if (st != ABKV_OK) return st;
+  if (plan.total > kNoAllocScratchBytes) return ABKV_ERR_SCRATCH_LIMIT;
+  void* scratch = nullptr;
+  const int se = noalloc_scratch(&scratch);
+  if (se != ABKV_OK) return se;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  // The array keeps the previous call's contents: clear the error word, the
+  // work counters and the per-(layer, sequence) chunk counters.
+  if (cudaMemsetAsync(scratch, 0, kWsHeader + plan.counter_bytes, s) != cudaSuccess) return ABKV_ERR_CUDA;
+  const int rc = abkv_decode(q, kv, block_tables, bt_strides, seq_lens, num_blocks, out, num_layers,
+                             num_seqs, num_q_heads, num_kv_heads, head_dim, page_size, max_pages_per_seq,
+                             scale, chunk_tokens, scratch, kNoAllocScratchBytes, stream);
+  if (rc != ABKV_OK) return rc;
+  if (device_error &&
+      cudaMemcpyAsync(device_error, scratch, sizeof(int32_t), cudaMemcpyDeviceToDevice, s) != cudaSuccess)
+    return ABKV_ERR_CUDA;
   return ABKV_OK;
 }

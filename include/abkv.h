@@ -40,6 +40,8 @@ extern "C" {
 #define ABKV_ERR_SPAN 7          /* host planner: span rejected                */
 #define ABKV_ERR_NO_BLOCKS 8     /* host planner: free queue exhausted         */
 #define ABKV_ERR_TIMEOUT 9       /* device: a bounded wait gave up             */
+#define ABKV_ERR_SCRATCH_LIMIT 10 /* request needs more than the fixed scratch of
+                                     abkv_decode_noalloc (32 MiB)               */
 
 /* Device error-word bits (OR-ed by kernels into workspace bytes 0..3). */
 #define ABKV_DEVERR_PAGE_OOB 0x1
@@ -101,6 +103,35 @@ int abkv_decode(const void* const* q, const void* const* kv,
                 int page_size, int max_pages_per_seq, float scale,
                 int chunk_tokens, void* workspace, size_t workspace_bytes,
                 void* stream);
+
+/* Decode that allocates nothing and takes no workspace.  No counterpart in the
+ * reference: it exists for callers that cannot allocate device memory when
+ * they decode (an engine that has reserved all of HBM for its KV cache, an
+ * allocator that must not be touched from this thread).  Arguments and
+ * results are those of abkv_decode; the split-KV scratch instead lives in a
+ * 32 MiB device array inside this library that every GPU loading the library
+ * keeps until the process exits.
+ *   - The first call on a device looks up that array's device address (with
+ *     the device current) and caches it; make that first call before any
+ *     stream capture.
+ *   - A request whose scratch would exceed 32 MiB is rejected with
+ *     ABKV_ERR_SCRATCH_LIMIT before anything runs (the scratch grows with
+ *     num_layers x num_seqs x split-KV chunks x num_q_heads x head_dim x 4 B;
+ *     per-layer calls or a larger chunk_tokens keep it small).
+ *   - Every call shares the array and it keeps the last call's contents: each
+ *     call clears its counters first, and calls that overlap on the GPU (two
+ *     streams, or two host threads) race on it and must be serialised.
+ *   - device_error: optional DEVICE int32 that receives the call's device
+ *     error bits (ABKV_DEVERR_*); NULL to ignore them. */
+int abkv_decode_noalloc(const void* const* q, const void* const* kv,
+                        const int32_t* const* block_tables,
+                        const int64_t* bt_strides,
+                        const int32_t* const* seq_lens,
+                        const int64_t* num_blocks, void* const* out,
+                        int num_layers, int num_seqs, int num_q_heads,
+                        int num_kv_heads, int head_dim, int page_size,
+                        int max_pages_per_seq, float scale, int chunk_tokens,
+                        int32_t* device_error, void* stream);
 
 
 /* ========================================================================
