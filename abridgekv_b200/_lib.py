@@ -60,6 +60,9 @@ SIGNATURES: dict[str, tuple] = {
                              c_vp, c_size, c_vp]),
     "abkv_gather_rows": (c_int, [c_vpp, c_vpp, c_int, C.c_int64, C.c_int64, C.c_int64, C.c_int64, c_vp,
                                  c_vp, c_size, c_vp]),
+    "abkv_prefill_masked": (c_int, [c_vp, c_i64p, c_vp, c_i64p, c_vp, c_i64p, c_vp, c_i64p, c_vp, c_i32p, c_vp,
+                                    c_int, c_int, c_int, c_int, c_int, c_int, c_int, C.c_float, c_vp, c_size,
+                                    c_vp]),
 }
 
 

@@ -80,7 +80,7 @@ def build(verbose: bool = False, ptxas_info: bool = False, force: bool = False) 
                 print(f"--- {src.name}\n{log}", file=sys.stderr)
     objs = [str(o) for o, _ in results]
     tmp = LIB.with_suffix(".so.tmp")
-    cmd = [nvcc] + ARCH + ["-shared", "-Xcompiler", "-fPIC", "-o", str(tmp)] + objs + ["-lcuda"]
+    cmd = [nvcc] + ARCH + ["-shared", "-Xcompiler", "-fPIC", "-o", str(tmp)] + objs
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"link failed:\n{' '.join(cmd)}\n{r.stdout}\n{r.stderr}")

@@ -1,0 +1,505 @@
+// Pause-token prefill attention with the in-block-position causal/pause mask,
+// on 5th-generation tensor cores (tcgen05 + TMEM) for sm_100a.
+//
+// Mask: CompressLM._arith_mask_mod (abridgekv/compress_forward.py:695-727),
+// equal to _mask_mod / _mask_rawprompt_mod for the simple config (L=1, no
+// tails, pause_xattn="full"; :678-688).  With per = C + K, qb = q / per,
+// kb = kv / per, qw = q % per, kw = kv % per, k_content = kw < C:
+//   vis = (k_content & kb == qb) | (!k_content & kb < qb)
+//   vis |= k_content & (kb*C + kw < prompt_len[b])           (raw prompt)
+//   vis &= kv <= q                                            (causal)
+//   vis |= (qw >= C) & !k_content & kb == qb                  (codes <-> codes)
+//   vis &= k_content | (kw - C < quota[h])                    (per-head quota)
+// out = softmax(q.k^T * scale + mask) v, fp32 softmax.  The attention math is
+// that of torch FlexAttention, which the reference runs for this mask
+// (compress_forward.py:248,1229).
+//
+// Tiling: 128 x 128 tiles.  C and K are multiples of 128, so no tile straddles
+// a block or the content/code boundary, and every tile is FULL, PARTIAL or
+// EMPTY by the analytic classification below (the same block structure as
+// _fast_layer_blockmasks, :760-789).  EMPTY tiles are never loaded; only
+// PARTIAL tiles evaluate the mask per element.
+//
+// CTA = one 128-row query tile of one (sequence, query head); 6 warps:
+//   warp 0      TMA producer: Q once, then K/V tiles into a 2-stage ring
+//               (cp.async.bulk.tensor, 128B swizzle, no multicast)
+//   warp 1      TMEM owner; lane 0 issues tcgen05.mma:
+//                 S  = Q K^T   (A = Q, B = K, both K-major, fp32 in TMEM)
+//                 O += P V     (A = P from shared memory, K-major; B = V, MN-major)
+//   warps 2..5  softmax: thread = one TMEM lane = one query row; S read with
+//               tcgen05.ld, masked online softmax in fp32, P written to shared
+//               memory (bf16, 128B-swizzled K-major), O rescaled in TMEM when
+//               the row maximum grows; epilogue divides by the row sum.
+// Every mbarrier wait is bounded and records ABKV_DEVERR_TIMEOUT on expiry.
+#include <cuda.h>
+
+#include <cstring>
+
+#include "common.cuh"
+
+namespace abkv {
+namespace {
+
+constexpr int kBM = 128, kBN = 128, kD = 128;
+constexpr int kThreads = 192;
+constexpr int kMaxHeads = 128;
+constexpr uint32_t kTmemCols = 256;  // S: cols [0,128), O: cols [128,256)
+
+// dynamic shared memory layout (1024-byte aligned pieces for 128B swizzle)
+constexpr int kOffQ = 0;                    // 2 x [128 rows][128 B]
+constexpr int kOffKV = 32768;               // 2 stages x (K 32 KiB + V 32 KiB)
+constexpr int kStageBytes = 65536;
+constexpr int kOffP = kOffKV + 2 * kStageBytes;  // 2 x [128 rows][128 B]
+constexpr int kOffBar = kOffP + 32768;
+constexpr int kSmemBytes = kOffBar + 128 + 1024;  // + slack for 1024-byte alignment
+
+struct alignas(64) PrefillParams {
+  CUtensorMap tm_q, tm_k, tm_v;
+  __nv_bfloat16* out;
+  int64_t o_sb, o_sh, o_ss;
+  float* lse;  // [B][H][S] or null
+  const int32_t* prompt_len;  // [B] or null
+  int32_t* err;
+  int quota[kMaxHeads];
+  int B, H, Hkv, S, C, KL, per, n_qtiles;
+  float scale_log2;
+};
+
+// 0 = empty, 1 = full, 2 = partial, for query tile qt / key tile kt of head h.
+__device__ __forceinline__ int tile_class(const PrefillParams& p, int h, int qt, int kt, int pl) {
+  const int q0 = qt * kBM, q1 = q0 + kBM - 1;
+  const int k0 = kt * kBN, k1 = k0 + kBN - 1;
+  const int qb = q0 / p.per, kb = k0 / p.per;
+  if (kb > qb) return 0;
+  const int qw0 = q0 - qb * p.per;
+  const int kw0 = k0 - kb * p.per, kw1 = k1 - kb * p.per;
+  const bool q_code = qw0 >= p.C;
+  if (kw0 < p.C) {  // content keys
+    if (kb == qb) {  // own block: causal (the raw-prompt term adds nothing here)
+      if (q_code || k1 <= q0) return 1;
+      if (k0 > q1) return 0;
+      return 2;
+    }
+    // earlier block: visible only as raw prompt (kb*C + kw < prompt_len)
+    const int a0 = kb * p.C + kw0, a1 = kb * p.C + kw1;
+    if (a1 < pl) return 1;
+    if (a0 >= pl) return 0;
+    return 2;
+  }
+  // code keys: quota on the slot; own block only for code queries
+  const int s0 = kw0 - p.C, s1 = kw1 - p.C;
+  const int qq = p.quota[h];
+  const int qc = (s1 < qq) ? 1 : (s0 >= qq ? 0 : 2);
+  if (kb < qb) return qc;
+  return q_code ? qc : 0;
+}
+
+__device__ __forceinline__ bool elem_vis(const PrefillParams& p, int h, int q, int kv, int pl) {
+  const int qb = q / p.per, qw = q - qb * p.per;
+  const int kb = kv / p.per, kw = kv - kb * p.per;
+  const bool kc = kw < p.C;
+  const bool same = kb == qb;
+  bool vis = (kc && same) || (!kc && kb < qb);
+  vis = vis || (kc && (kb * p.C + kw < pl));
+  vis = vis && (kv <= q);
+  vis = vis || (qw >= p.C && !kc && same);
+  vis = vis && (kc || (kw - p.C < p.quota[h]));
+  return vis;
+}
+
+// ---- tcgen05 / TMA helpers --------------------------------------------------
+__device__ __forceinline__ uint64_t desc_kmajor_sw128(uint32_t saddr) {
+  // K-major, 128B swizzle: rows of 128 B, 8-row atoms 1024 B apart (SBO),
+  // LBO unused (1), descriptor version 1, layout type 2 (SWIZZLE_128B).
+  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+__device__ __forceinline__ uint64_t desc_mnmajor_sw128(uint32_t saddr) {
+  // MN-major, 128B swizzle: a K row = 64 MN elements (128 B); 8 K rows form a
+  // 1024 B atom (SBO = 1024); the next 64 MN elements are 16 KiB away (LBO).
+  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)(16384 >> 4) << 16) |
+         ((uint64_t)(1024 >> 4) << 32) | ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+// kind::f16 instruction descriptor: D f32, A/B bf16, M=128, N=128.
+constexpr uint32_t kIdescQK = (1u << 4) | (1u << 7) | (1u << 10) | ((128u >> 3) << 17) | ((128u >> 4) << 24);
+constexpr uint32_t kIdescPV = kIdescQK | (1u << 16);  // B (V) is MN-major
+
+__device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                     uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+        "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
+        "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
+        "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};\n" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+      "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+      "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+      "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+      "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+      "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+      "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+      "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+      "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+      "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
+
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+      "[%6];\n" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
+      : "memory");
+}
+// Bounded wait; after the first expiry a thread stops waiting altogether (its
+// remaining work is skipped and the error word says why), so a fault in one
+// role cannot stall the CTA for long.
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, bool& dead, int32_t* err) {
+  if (dead) return false;
+  const uint32_t addr = smem_u32(bar);
+  for (uint32_t i = 0; i < (1u << 20); ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    if (done) return true;
+  }
+  set_error(err, ABKV_DEVERR_TIMEOUT);
+  dead = true;
+  return false;
+}
+
+__device__ __forceinline__ void mbar_arrive_one(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_constant__ PrefillParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  uint64_t* q_full = bar + 0;
+  uint64_t* kv_full = bar + 1;   // [2]
+  uint64_t* kv_empty = bar + 3;  // [2]
+  uint64_t* s_full = bar + 5;
+  uint64_t* p_full = bar + 6;
+  uint64_t* o_full = bar + 7;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bar + 8);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qt = p.n_qtiles - 1 - (int)blockIdx.x;  // heaviest query tiles first
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int hk = h / (p.H / p.Hkv);
+  const int pl = p.prompt_len ? __ldg(p.prompt_len + b) : 0;
+  const int qb = qt * kBM / p.per;
+  const int kt_end = (qb + 1) * p.per / kBN;  // key tiles beyond the query's block are never visible
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    mbar_init(&kv_full[0], 1);
+    mbar_init(&kv_full[1], 1);
+    mbar_init(&kv_empty[0], 1);
+    mbar_init(&kv_empty[1], 1);
+    mbar_init(s_full, 1);
+    mbar_init(p_full, 128);
+    mbar_init(o_full, 1);
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(s_tmem)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *s_tmem;
+  const uint32_t tmem_s = tmem, tmem_o = tmem + 128;
+  bool dead = false;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      mbar_expect_tx(q_full, 2 * 16384);
+      tma_load_4d(smem + kOffQ, &p.tm_q, 0, qt * kBM, h, b, q_full);
+      tma_load_4d(smem + kOffQ + 16384, &p.tm_q, 64, qt * kBM, h, b, q_full);
+      int j = 0;
+      for (int kt = 0; kt < kt_end; ++kt) {
+        if (tile_class(p, h, qt, kt, pl) == 0) continue;
+        const int st = j & 1;
+        if (!wait_or_abort(&kv_empty[st], (uint32_t)(((j >> 1) & 1) ^ 1), dead, p.err)) break;
+        uint8_t* kbuf = smem + kOffKV + st * kStageBytes;
+        mbar_expect_tx(&kv_full[st], 4 * 16384);
+        tma_load_4d(kbuf, &p.tm_k, 0, kt * kBN, hk, b, &kv_full[st]);
+        tma_load_4d(kbuf + 16384, &p.tm_k, 64, kt * kBN, hk, b, &kv_full[st]);
+        tma_load_4d(kbuf + 32768, &p.tm_v, 0, kt * kBN, hk, b, &kv_full[st]);
+        tma_load_4d(kbuf + 49152, &p.tm_v, 64, kt * kBN, hk, b, &kv_full[st]);
+        ++j;
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      wait_or_abort(q_full, 0, dead, p.err);
+      const uint32_t q_addr = smem_u32(smem + kOffQ);
+      const uint32_t p_addr = smem_u32(smem + kOffP);
+      int j = 0;
+      for (int kt = 0; kt < kt_end; ++kt) {
+        if (tile_class(p, h, qt, kt, pl) == 0) continue;
+        const int st = j & 1;
+        if (!wait_or_abort(&kv_full[st], (uint32_t)((j >> 1) & 1), dead, p.err)) break;
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(smem + kOffKV + st * kStageBytes);
+        const uint32_t v_addr = k_addr + 32768;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {  // S = Q K^T over head_dim in steps of 16
+          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+          umma(tmem_s, desc_kmajor_sw128(q_addr + off), desc_kmajor_sw128(k_addr + off), kIdescQK,
+               kk > 0 ? 1u : 0u);
+        }
+        umma_commit(s_full);
+        if (!wait_or_abort(p_full, (uint32_t)(j & 1), dead, p.err)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {  // O += P V over the 128 keys in steps of 16
+          const uint32_t poff = (kk >> 2) * 16384 + (kk & 3) * 32;
+          umma(tmem_o, desc_kmajor_sw128(p_addr + poff), desc_mnmajor_sw128(v_addr + kk * 2048), kIdescPV,
+               (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(&kv_empty[st]);
+        ++j;
+      }
+      umma_commit(o_full);
+    }
+  } else {
+    // ---------------- softmax / correction / epilogue (warps 2..5) ----------------
+    const int quarter = warp & 3;                 // TMEM lane quarter this warp may access
+    const int row = quarter * 32 + lane;          // query row within the tile
+    const int q = qt * kBM + row;
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    const float sl2 = p.scale_log2;
+    uint8_t* pbuf = smem + kOffP;
+    float m_run = -INFINITY, l_run = 0.f;
+    int j = 0;
+    for (int kt = 0; kt < kt_end; ++kt) {
+      const int cls = tile_class(p, h, qt, kt, pl);
+      if (cls == 0) continue;
+      // warp-uniform decision: the tcgen05.ld below is a warp-collective
+      const bool ok = __all_sync(0xffffffffu, wait_or_abort(s_full, (uint32_t)(j & 1), dead, p.err));
+      if (!ok) {
+        dead = true;
+        break;
+      }
+      tc_fence_after();
+      float x[128];
+#pragma unroll
+      for (int c4 = 0; c4 < 4; ++c4) {
+        float t[32];
+        tmem_ld32(tmem_s + lane_base + c4 * 32, t);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) x[c4 * 32 + i] = t[i];
+      }
+      tmem_wait_ld();
+      float mx = -INFINITY;
+      const int kv0 = kt * kBN;
+#pragma unroll
+      for (int c = 0; c < 128; ++c) {
+        float v = x[c] * sl2;
+        if (cls == 2 && !elem_vis(p, h, q, kv0 + c, pl)) v = -INFINITY;
+        x[c] = v;
+        mx = fmaxf(mx, v);
+      }
+      const float m_new = fmaxf(m_run, mx);
+      const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+      const float alpha = exp2f(m_run - m_use);
+      float rs = 0.f;
+      // P row -> shared memory, bf16, 128B-swizzled K-major (chunk ^= row % 8)
+#pragma unroll
+      for (int ch = 0; ch < 16; ++ch) {
+        uint32_t w[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float p0 = exp2f(x[ch * 8 + 2 * e] - m_use);
+          const float p1 = exp2f(x[ch * 8 + 2 * e + 1] - m_use);
+          rs += p0 + p1;
+          w[e] = pack_bf16x2(p0, p1);
+        }
+        const int atom = ch >> 3, chunk = ch & 7;
+        uint8_t* dst = pbuf + atom * 16384 + row * 128 + ((chunk ^ (row & 7)) << 4);
+        *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      l_run = l_run * alpha + rs;
+      m_run = m_new;
+      // rescale the O accumulator when this row's maximum grew (PV(j-1) has
+      // completed: s_full(j) was committed after it)
+      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) {
+          float t[32];
+          tmem_ld32(tmem_o + lane_base + c4 * 32, t);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) t[i] *= alpha;
+          tmem_st32(tmem_o + lane_base + c4 * 32, t);
+        }
+        tmem_wait_st();
+      }
+      asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // P visible to the tensor core
+      tc_fence_before();
+      mbar_arrive_one(p_full);
+      ++j;
+    }
+    // epilogue
+    const bool o_ok = __all_sync(0xffffffffu, wait_or_abort(o_full, 0, dead, p.err));
+    tc_fence_after();
+    if (o_ok) {
+    const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+    __nv_bfloat16* orow = p.out + (int64_t)b * p.o_sb + (int64_t)h * p.o_sh + (int64_t)q * p.o_ss;
+#pragma unroll
+    for (int c4 = 0; c4 < 4; ++c4) {
+      float t[32];
+      tmem_ld32(tmem_o + lane_base + c4 * 32, t);
+      tmem_wait_ld();
+#pragma unroll
+      for (int v8 = 0; v8 < 4; ++v8) {
+        uint4 pk;
+        pk.x = pack_bf16x2(t[v8 * 8 + 0] * inv, t[v8 * 8 + 1] * inv);
+        pk.y = pack_bf16x2(t[v8 * 8 + 2] * inv, t[v8 * 8 + 3] * inv);
+        pk.z = pack_bf16x2(t[v8 * 8 + 4] * inv, t[v8 * 8 + 5] * inv);
+        pk.w = pack_bf16x2(t[v8 * 8 + 6] * inv, t[v8 * 8 + 7] * inv);
+        *reinterpret_cast<uint4*>(orow + c4 * 32 + v8 * 8) = pk;
+      }
+    }
+    if (p.lse) {
+      const float lse2 = l_run > 0.f ? m_run + log2f(l_run) : -INFINITY;
+      p.lse[((int64_t)b * p.H + h) * p.S + q] = lse2 * 0.6931471805599453f;  // natural log
+    }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(kTmemCols));
+  }
+}
+
+// ---------------------------------------------------------------------------
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// [B][heads][S][128] bf16 with element strides (sb, sh, ss) -> 4D tensor map,
+// box = 64 dims x 128 rows, 128B swizzle.
+int make_map(CUtensorMap* m, const void* base, int B, int heads, int S, const int64_t* strides) {
+  cuuint64_t dims[4] = {(cuuint64_t)kD, (cuuint64_t)S, (cuuint64_t)heads, (cuuint64_t)B};
+  cuuint64_t gstr[3] = {(cuuint64_t)strides[2] * 2, (cuuint64_t)strides[1] * 2, (cuuint64_t)strides[0] * 2};
+  for (int i = 0; i < 3; ++i)
+    if (gstr[i] % 16 != 0 || gstr[i] == 0) return ABKV_ERR_INVALID_ARG;
+  cuuint32_t box[4] = {64, (cuuint32_t)kBN, 1, 1};
+  cuuint32_t es[4] = {1, 1, 1, 1};
+  // the driver entry point is resolved through the runtime, so the library
+  // does not link libcuda and still loads on hosts without a GPU driver
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult qres;
+  if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &qres) != cudaSuccess ||
+      qres != cudaDriverEntryPointSuccess || !fn)
+    return ABKV_ERR_CUDA;
+  CUresult r = reinterpret_cast<EncodeTiled>(fn)(
+      m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, gstr, box, es,
+      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? ABKV_OK : ABKV_ERR_INVALID_ARG;
+}
+
+}  // namespace
+}  // namespace abkv
+
+using namespace abkv;
+
+extern "C" int abkv_prefill_masked(const void* q, const int64_t* q_strides, const void* k,
+                                   const int64_t* k_strides, const void* v, const int64_t* v_strides,
+                                   void* out, const int64_t* out_strides, float* lse,
+                                   const int32_t* quota_per_head, const int32_t* prompt_len, int B, int H,
+                                   int Hkv, int S, int head_dim, int C, int K_layout, float scale,
+                                   void* workspace, size_t workspace_bytes, void* stream) {
+  if (!q || !k || !v || !out || !q_strides || !k_strides || !v_strides || !out_strides) return ABKV_ERR_INVALID_ARG;
+  if (B <= 0 || H <= 0 || Hkv <= 0 || S <= 0 || H % Hkv != 0 || !(scale > 0.f)) return ABKV_ERR_INVALID_ARG;
+  if (head_dim != kD || H > kMaxHeads || B > 65535) return ABKV_ERR_UNSUPPORTED;
+  if (C <= 0 || K_layout <= 0 || C % kBN || K_layout % kBN || S % (C + K_layout)) return ABKV_ERR_UNSUPPORTED;
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) |
+       reinterpret_cast<uintptr_t>(out)) & 15)
+    return ABKV_ERR_INVALID_ARG;
+  if (out_strides[0] % 8 || out_strides[1] % 8 || out_strides[2] % 8) return ABKV_ERR_INVALID_ARG;
+  if (!workspace || workspace_bytes < 256 || (reinterpret_cast<uintptr_t>(workspace) & 255))
+    return ABKV_ERR_WORKSPACE;
+  PrefillParams prm;
+  std::memset(&prm, 0, sizeof(prm));
+  int st = make_map(&prm.tm_q, q, B, H, S, q_strides);
+  if (st == ABKV_OK) st = make_map(&prm.tm_k, k, B, Hkv, S, k_strides);
+  if (st == ABKV_OK) st = make_map(&prm.tm_v, v, B, Hkv, S, v_strides);
+  if (st != ABKV_OK) return st;
+  prm.out = static_cast<__nv_bfloat16*>(out);
+  prm.o_sb = out_strides[0];
+  prm.o_sh = out_strides[1];
+  prm.o_ss = out_strides[2];
+  prm.lse = lse;
+  prm.prompt_len = prompt_len;
+  prm.err = static_cast<int32_t*>(workspace);
+  for (int h = 0; h < H; ++h) {
+    const int qq = quota_per_head ? quota_per_head[h] : K_layout;
+    if (qq < 0) return ABKV_ERR_INVALID_ARG;
+    prm.quota[h] = qq;
+  }
+  prm.B = B;
+  prm.H = H;
+  prm.Hkv = Hkv;
+  prm.S = S;
+  prm.C = C;
+  prm.KL = K_layout;
+  prm.per = C + K_layout;
+  prm.n_qtiles = S / kBM;
+  prm.scale_log2 = scale * 1.4426950408889634f;
+  if (cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) !=
+      cudaSuccess)
+    return ABKV_ERR_CUDA;
+  dim3 grid(prm.n_qtiles, H, B);
+  prefill_kernel<<<grid, kThreads, kSmemBytes, reinterpret_cast<cudaStream_t>(stream)>>>(prm);
+  if (cudaGetLastError() != cudaSuccess) return ABKV_ERR_CUDA;
+  return ABKV_OK;
+}

@@ -257,6 +257,31 @@ int abkv_gather_rows(const void* const* src, void* const* dst, int num_tensors,
                      int64_t row_bytes, const int64_t* keep, void* workspace,
                      size_t workspace_bytes, void* stream);
 
+/* ========================================================================
+ * 4. Pause-token prefill attention with the compressed-cache mask (tcgen05).
+ *
+ * Replaces the FlexAttention call CompressLM makes through transformers
+ * (abridgekv/compress_forward.py:248,1229) with the per-layer BlockMasks of
+ * _arith_mask_mod / _fast_layer_blockmasks (:695-727, :760-789): the mask is
+ * evaluated arithmetically from the block layout instead of a BlockMask.
+ * q: [B][H][S][head_dim], k, v: [B][Hkv][S][head_dim] bf16, element strides
+ * (batch, head, seq) given in *_strides[3], last dim contiguous; out likewise
+ * [B][H][S][head_dim] (strides multiples of 8 elements); lse: optional
+ * contiguous [B][H][S] f32, natural log.  Sequence layout: blocks of
+ * [C content | K_layout code rows]; quota_per_head: HOST [H] code quota of each
+ * query head (NULL = K_layout); prompt_len: DEVICE [B] raw prompt lengths
+ * (NULL = none).  Supported: head_dim 128, C and K_layout multiples of 128,
+ * S a multiple of C + K_layout, H <= 128, H % Hkv == 0.
+ * ====================================================================== */
+int abkv_prefill_masked(const void* q, const int64_t* q_strides, const void* k,
+                        const int64_t* k_strides, const void* v,
+                        const int64_t* v_strides, void* out,
+                        const int64_t* out_strides, float* lse,
+                        const int32_t* quota_per_head, const int32_t* prompt_len,
+                        int B, int H, int Hkv, int S, int head_dim, int C,
+                        int K_layout, float scale, void* workspace,
+                        size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -21,3 +21,21 @@ def load_decode(name: str):
                       num_kv_heads=int(z["num_kv_heads"]), head_dim=int(z["head_dim"]),
                       page=int(z["page"]))
     return case, from_bits(z["out_bits"])
+
+
+def prefill_cases():
+    return sorted(p.stem[len("prefill_"):] for p in GOLDEN.glob("prefill_*.npz"))
+
+
+def load_prefill(name: str):
+    """-> dict(case params, q, k, v, mask [B,H,S,S], rows, out_rows, lse) from the reference goldens."""
+    from tests.golden.make_golden import prefill_inputs
+
+    z = dict(np.load(GOLDEN / f"prefill_{name}.npz"))
+    B, H, Hkv = int(z["B"]), int(z["H"]), int(z["Hkv"])
+    S0 = int(z["N"]) * (int(z["C"]) + int(z["K"]))
+    q, k, v = prefill_inputs(int(z["seed"]), B, H, Hkv, S0)
+    mask = np.unpackbits(z["mask_bits"])[: B * H * S0 * S0].reshape(B, H, S0, S0).astype(bool)
+    pl = z["prompt_len"] if z["prompt_len"].size else None
+    return dict(B=B, H=H, Hkv=Hkv, S0=S0, C=int(z["C"]), K=int(z["K"]), quota=z["quota_per_head"], prompt_len=pl,
+                q=q, k=k, v=v, mask=mask, rows=z["rows"], out_rows=z["out_rows"], lse=z["lse"])
