@@ -1,0 +1,203 @@
+"""Secondary benchmarks (one JSON line each); the headline decode line is bench.py.
+
+    python -m abridgekv_b200.benchmarks prefill   [--layers 36] [--steps 3] [--flex]
+    python -m abridgekv_b200.benchmarks compaction [--steps 5]
+
+prefill    BASELINE config 4: B=16 sequences of 16 blocks x (512 content + 256 code rows)
+           = 12,288 rows, Qwen3-4B attention (32 q / 8 kv heads, head_dim 128), per-layer
+           quotas from sched_trunc_perlayer_mean128, prompt_len 0, bf16 N(0,1) Q/K/V.  One
+           step = all layers (one abkv_prefill_masked launch each).  Algorithmic FLOPs =
+           4 x head_dim per visible (query, key) pair per head.  With --flex the same step
+           is also timed with torch FlexAttention compiled on this GPU (the reference's
+           prefill kernel: compress_forward.py:1229 through transformers' flex path) using
+           the reference's mask formula.
+compaction BASELINE config 4's block compaction for all 16 sequences and 36 layers
+           (12 physical tensors shared by 3 quota groups): finish one block per sequence,
+           execute the planned copy ops; algorithmic bytes = 2 x rows moved x 4 KiB per layer.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import time
+
+import numpy as np
+import torch
+
+from .workloads import SCHEDULE_PERLAYER_MEAN128
+
+
+def visible_pairs(N: int, C: int, K: int, quota: int, prompt_len: int = 0) -> int:
+    """Visible (query, key) pairs of one (sequence, head) under _arith_mask_mod with prompt_len 0."""
+    assert prompt_len == 0
+    tot = 0
+    for qb in range(N):
+        tot += C * (C + 1) // 2 + C * qb * quota          # content rows: causal own block + earlier codes
+        tot += K * (C + quota + qb * quota)                # code rows: own content + own codes + earlier
+    return tot
+
+
+def _peaks() -> dict:
+    from pathlib import Path
+
+    p = Path(__file__).resolve().parents[1] / "MEASURED_PEAKS.json"
+    try:
+        return json.loads(p.read_text())
+    except Exception:
+        return {"bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "hbm_gbs": 6650.0, "fallback": True}
+
+
+def bench_prefill(args) -> dict:
+    from . import prefill
+
+    B, H, Hkv, D, C, K, N = 16, 32, 8, 128, 512, 256, 16
+    S0 = N * (C + K)
+    dev = torch.device("cuda")
+    gen = torch.Generator(device=dev).manual_seed(0)
+    q = torch.randn((B, S0, H, D), device=dev, generator=gen, dtype=torch.bfloat16).transpose(1, 2)
+    k = torch.randn((B, S0, Hkv, D), device=dev, generator=gen, dtype=torch.bfloat16).transpose(1, 2)
+    v = torch.randn((B, S0, Hkv, D), device=dev, generator=gen, dtype=torch.bfloat16).transpose(1, 2)
+    out = torch.empty((B, S0, H, D), device=dev, dtype=torch.bfloat16).transpose(1, 2)
+    quotas = SCHEDULE_PERLAYER_MEAN128[: args.layers]
+    flops = sum(4 * D * visible_pairs(N, C, K, qq) * B * H for qq in quotas)
+
+    def step():
+        for qq in quotas:
+            prefill.prefill_masked(q, k, v, C=C, K_layout=K, quota_per_head=[qq] * H, out=out)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    pk = _peaks()
+    tflops = flops / (ms / 1e3) / 1e12
+    line = {
+        "metric": "pause-token prefill attention TFLOP/s (config 4)", "value": tflops, "unit": "TFLOP/s",
+        "ms_per_step": ms, "layers": len(quotas), "algorithmic_tflop_per_step": flops / 1e12,
+        "roofline": {"bound": "tensor", "achieved": tflops, "peak": pk.get("bf16_tflops_sustained"),
+                     "peak_kind": "measured sustained cuBLAS bf16 (MEASURED_PEAKS.json)",
+                     "frac": tflops / pk.get("bf16_tflops_sustained", 1400.0)},
+        "config": {"B": B, "S0": S0, "heads": f"{H}/{Hkv}", "C": C, "K_layout": K, "quotas": "per layer",
+                   "prompt_len": 0},
+    }
+    if args.flex:
+        line["flex"] = bench_flex(q, k, v, quotas, C, K, N, args, flops)
+        line["speedup_vs_flex"] = line["flex"]["ms_per_step"] / ms
+        # parity on one layer: our kernel vs compiled FlexAttention on the same inputs
+        line["flex"]["max_abs_diff_layer0"] = line["flex"].pop("_diff")
+    return line
+
+
+def bench_flex(q, k, v, quotas, C, K, N, args, flops) -> dict:
+    from torch.nn.attention.flex_attention import create_block_mask, flex_attention
+
+    from . import prefill
+
+    B, H, S0, D = q.shape
+    per = C + K
+    masks = {}
+    for qq in sorted(set(quotas)):
+        def mm(b, h, qi, kv, qq=qq):
+            qb, qw = qi // per, qi % per
+            kb, kw = kv // per, kv % per
+            kc = kw < C
+            same = kb == qb
+            vis = (kc & same) | (~kc & (kb < qb))
+            vis = (kv <= qi) & vis
+            vis = vis | ((qw >= C) & ~kc & same)
+            return vis & (kc | ((kw - C) < qq))
+        masks[qq] = create_block_mask(mm, B=None, H=None, Q_LEN=S0, KV_LEN=S0, device="cuda", _compile=True)
+    fa = torch.compile(flex_attention, dynamic=False)
+    opts = {"BLOCK_M": 128, "BLOCK_N": 64, "num_warps": 8}  # the reference's launch/env.sh options
+    scale = 1.0 / math.sqrt(D)
+
+    def step():
+        for qq in quotas:
+            fa(q, k, v, block_mask=masks[qq], scale=scale, enable_gqa=True, kernel_options=opts)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    ref = fa(q, k, v, block_mask=masks[quotas[0]], scale=scale, enable_gqa=True, kernel_options=opts)
+    ours = prefill.prefill_masked(q, k, v, C=C, K_layout=K, quota_per_head=[quotas[0]] * H)
+    diff = (ref.float() - ours.float()).abs().max().item()
+    return {"ms_per_step": ms, "tflops": flops / (ms / 1e3) / 1e12, "kernel_options": opts, "_diff": diff}
+
+
+def bench_compaction(args) -> dict:
+    from . import compaction
+    from .planner import BlockPlanner
+    from .workspace import Workspace
+
+    C, K, page = 512, 256, 16
+    quotas = (256, 128, 64)
+    G = len(quotas)
+    B, L = 16, 36
+    per = C + K
+    blocks = args.blocks
+    n_tensors = L // G
+    nb = 1 + B * (blocks * per // page) * G + 64
+    dev = torch.device("cuda")
+    caches = [torch.zeros((nb, 2, page, 8, 128), device=dev, dtype=torch.bfloat16) for _ in range(n_tensors)]
+    planner = BlockPlanner(nb, page, G)
+    for b in range(B):
+        planner.add_request(b)
+    ws = Workspace(dev)
+    times, moved = [], []
+    for blk in range(blocks):
+        for b in range(B):
+            n = (blk + 1) * per
+            assert planner.allocate_slots(b, n)
+            planner.set_num_computed_tokens(b, n)
+            planner.finish_block(b, (blk * per, blk * per + C), (blk * per + C, (blk + 1) * per), quotas, K)
+        ops, _ = planner.take_pending()
+        rows = sum(len(x) for per_g in ops.values() for bl in per_g for x in bl)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        compaction.execute_kv_copy_operations(ops, [caches] * G, workspace=ws)
+        e1.record()
+        torch.cuda.synchronize()
+        times.append((e0.elapsed_time(e1), (time.perf_counter() - t0) * 1e3))
+        moved.append(rows * n_tensors * 2 * 2 * 8 * 128 * 2)  # rows x layers-of-group x (K,V) x R+W x bytes
+    dev_ms = float(np.mean([t[0] for t in times[1:]] or [times[0][0]]))
+    host_ms = float(np.mean([t[1] for t in times[1:]] or [times[0][1]]))
+    gbs = float(np.mean(moved)) / (dev_ms / 1e3) / 1e9
+    pk = _peaks()
+    return {"metric": "block compaction executor GB/s (config 4, 16 seqs x 36 layers)", "value": gbs,
+            "unit": "GB/s", "ms_per_block_finish_device": dev_ms, "ms_per_block_finish_wall": host_ms,
+            "bytes_per_block_finish": float(np.mean(moved)),
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": pk.get("hbm_gbs"),
+                         "frac": gbs / pk.get("hbm_gbs", 6650.0)}}
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("which", choices=["prefill", "compaction"])
+    ap.add_argument("--layers", type=int, default=36)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=2)
+    ap.add_argument("--flex", action="store_true")
+    ap.add_argument("--blocks", type=int, default=6)
+    args = ap.parse_args()
+    fn = {"prefill": bench_prefill, "compaction": bench_compaction}[args.which]
+    print(json.dumps(fn(args)), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -94,17 +94,31 @@ __device__ __forceinline__ int tile_class(const PrefillParams& p, int h, int qt,
   return q_code ? qc : 0;
 }
 
-__device__ __forceinline__ bool elem_vis(const PrefillParams& p, int h, int q, int kv, int pl) {
-  const int qb = q / p.per, qw = q - qb * p.per;
-  const int kb = kv / p.per, kw = kv - kb * p.per;
-  const bool kc = kw < p.C;
-  const bool same = kb == qb;
-  bool vis = (kc && same) || (!kc && kb < qb);
-  vis = vis || (kc && (kb * p.C + kw < pl));
-  vis = vis && (kv <= q);
-  vis = vis || (qw >= p.C && !kc && same);
-  vis = vis && (kc || (kw - p.C < p.quota[h]));
-  return vis;
+// Inside any tile the visible keys of one query row are a PREFIX of the tile's
+// 128 columns: the causal diagonal of the own block (kv <= q), the raw-prompt
+// boundary of an earlier block (kb*C + kw < prompt_len) or the quota boundary
+// of a code tile (kw - C < quota).  Returns that prefix length in [0, 128]
+// (128 for FULL tiles, 0 for EMPTY ones); the element-wise mask is c < limit.
+__device__ __forceinline__ int tile_limit(const PrefillParams& p, int h, int kt, int q, int pl) {
+  const int k0 = kt * kBN;
+  const int qb = q / p.per, kb = k0 / p.per;
+  if (kb > qb) return 0;
+  const int qw = q - qb * p.per, kw0 = k0 - kb * p.per;
+  int lim;
+  if (kw0 < p.C) {
+    if (kb == qb) lim = (qw >= p.C) ? kBN : q - k0 + 1;
+    else lim = pl - (kb * p.C + kw0);
+  } else {
+    if (kb == qb && qw < p.C) return 0;
+    lim = p.quota[h] - (kw0 - p.C);
+  }
+  return lim < 0 ? 0 : (lim > kBN ? kBN : lim);
+}
+
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
+  return y;
 }
 
 // ---- tcgen05 / TMA helpers --------------------------------------------------
@@ -326,49 +340,51 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         break;
       }
       tc_fence_after();
-      float x[128];
-#pragma unroll
+      const int lim = tile_limit(p, h, kt, q, pl);  // visible columns of this row: c < lim
+      // pass 1: row maximum over the visible columns (S read from TMEM in 32-column chunks)
+      float mx = -INFINITY;
+#pragma unroll 1
       for (int c4 = 0; c4 < 4; ++c4) {
         float t[32];
         tmem_ld32(tmem_s + lane_base + c4 * 32, t);
+        tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) x[c4 * 32 + i] = t[i];
+        for (int i = 0; i < 32; ++i) mx = fmaxf(mx, (c4 * 32 + i < lim) ? t[i] : -INFINITY);
       }
-      tmem_wait_ld();
-      float mx = -INFINITY;
-      const int kv0 = kt * kBN;
-#pragma unroll
-      for (int c = 0; c < 128; ++c) {
-        float v = x[c] * sl2;
-        if (cls == 2 && !elem_vis(p, h, q, kv0 + c, pl)) v = -INFINITY;
-        x[c] = v;
-        mx = fmaxf(mx, v);
-      }
+      mx *= sl2;
       const float m_new = fmaxf(m_run, mx);
       const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-      const float alpha = exp2f(m_run - m_use);
+      const float alpha = fast_exp2(m_run - m_use);
+      // pass 2: P = exp2(s * scale * log2e - m) -> shared memory, bf16, 128B-swizzled
+      // K-major (16-byte chunk index ^= row % 8), and the row sum
       float rs = 0.f;
-      // P row -> shared memory, bf16, 128B-swizzled K-major (chunk ^= row % 8)
+#pragma unroll 1
+      for (int c4 = 0; c4 < 4; ++c4) {
+        float t[32];
+        tmem_ld32(tmem_s + lane_base + c4 * 32, t);
+        tmem_wait_ld();
 #pragma unroll
-      for (int ch = 0; ch < 16; ++ch) {
-        uint32_t w[4];
+        for (int e8 = 0; e8 < 4; ++e8) {
+          uint32_t w[4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float p0 = exp2f(x[ch * 8 + 2 * e] - m_use);
-          const float p1 = exp2f(x[ch * 8 + 2 * e + 1] - m_use);
-          rs += p0 + p1;
-          w[e] = pack_bf16x2(p0, p1);
+          for (int e = 0; e < 4; ++e) {
+            const int c = c4 * 32 + e8 * 8 + 2 * e;
+            const float p0 = (c < lim) ? fast_exp2(fmaf(t[e8 * 8 + 2 * e], sl2, -m_use)) : 0.f;
+            const float p1 = (c + 1 < lim) ? fast_exp2(fmaf(t[e8 * 8 + 2 * e + 1], sl2, -m_use)) : 0.f;
+            rs += p0 + p1;
+            w[e] = pack_bf16x2(p0, p1);
+          }
+          const int ch = c4 * 4 + e8, atom = ch >> 3, chunk = ch & 7;
+          uint8_t* dst = pbuf + atom * 16384 + row * 128 + ((chunk ^ (row & 7)) << 4);
+          *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
         }
-        const int atom = ch >> 3, chunk = ch & 7;
-        uint8_t* dst = pbuf + atom * 16384 + row * 128 + ((chunk ^ (row & 7)) << 4);
-        *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
       }
       l_run = l_run * alpha + rs;
       m_run = m_new;
       // rescale the O accumulator when this row's maximum grew (PV(j-1) has
       // completed: s_full(j) was committed after it)
       if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
-#pragma unroll
+#pragma unroll 1
         for (int c4 = 0; c4 < 4; ++c4) {
           float t[32];
           tmem_ld32(tmem_o + lane_base + c4 * 32, t);
@@ -390,7 +406,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
     if (o_ok) {
     const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
     __nv_bfloat16* orow = p.out + (int64_t)b * p.o_sb + (int64_t)h * p.o_sh + (int64_t)q * p.o_ss;
-#pragma unroll
+#pragma unroll 1
     for (int c4 = 0; c4 < 4; ++c4) {
       float t[32];
       tmem_ld32(tmem_o + lane_base + c4 * 32, t);
