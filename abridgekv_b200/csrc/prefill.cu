@@ -14,22 +14,27 @@
 // that of torch FlexAttention, which the reference runs for this mask
 // (compress_forward.py:248,1229).
 //
-// Tiling: 128 x 128 tiles.  C and K are multiples of 128, so no tile straddles
-// a block or the content/code boundary, and every tile is FULL, PARTIAL or
-// EMPTY by the analytic classification below (the same block structure as
-// _fast_layer_blockmasks, :760-789).  EMPTY tiles are never loaded; only
-// PARTIAL tiles evaluate the mask per element.
+// Tiling: 128 query rows x 64 keys.  C and K are multiples of 128, so no tile
+// straddles a block or the content/code boundary, and every tile is FULL,
+// PARTIAL or EMPTY by the analytic classification below (the block structure
+// of _fast_layer_blockmasks, :760-789).  EMPTY tiles are never loaded; inside
+// a PARTIAL tile the visible keys of a row are a prefix of the tile.
 //
-// CTA = one 128-row query tile of one (sequence, query head); 6 warps:
-//   warp 0      TMA producer: Q once, then K/V tiles into a 2-stage ring
-//               (cp.async.bulk.tensor, 128B swizzle, no multicast)
-//   warp 1      TMEM owner; lane 0 issues tcgen05.mma:
+// CTA = one 128-row query tile of TWO query heads of the same KV head.  Their
+// masks are the same block structure, so both heads share every K/V tile
+// (loaded once); 10 warps:
+//   warp 0      TMA producer: Q of both heads, then K/V tiles into a 3-stage
+//               ring (cp.async.bulk.tensor, 128B swizzle, no multicast)
+//   warp 1      TMEM owner (512 columns); lane 0 issues tcgen05.mma in the order
+//               S_A(0) S_B(0) | PV_A(j) S_A(j+1) PV_B(j) S_B(j+1) | ...
 //                 S  = Q K^T   (A = Q, B = K, both K-major, fp32 in TMEM)
 //                 O += P V     (A = P from shared memory, K-major; B = V, MN-major)
-//   warps 2..5  softmax: thread = one TMEM lane = one query row; S read with
-//               tcgen05.ld, masked online softmax in fp32, P written to shared
-//               memory (bf16, 128B-swizzled K-major), O rescaled in TMEM when
-//               the row maximum grows; epilogue divides by the row sum.
+//               so each head's softmax overlaps the other head's MMAs
+//   warps 2..5  softmax of head A, warps 6..9 softmax of head B: thread = one
+//               TMEM lane = one query row; S read with tcgen05.ld, masked online
+//               softmax in fp32, P written to shared memory (bf16, 128B-swizzled
+//               K-major), O rescaled in TMEM when the row maximum grows;
+//               epilogue divides by the row sum.
 // Every mbarrier wait is bounded and records ABKV_DEVERR_TIMEOUT on expiry.
 #include <cuda.h>
 
@@ -40,17 +45,21 @@
 namespace abkv {
 namespace {
 
-constexpr int kBM = 128, kBN = 128, kD = 128;
-constexpr int kThreads = 192;
+constexpr int kBM = 128, kBN = 64, kD = 128;
+constexpr int kThreads = 320;
 constexpr int kMaxHeads = 128;
-constexpr uint32_t kTmemCols = 256;  // S: cols [0,128), O: cols [128,256)
+constexpr int kStages = 3;
+constexpr uint32_t kTmemCols = 512;  // head A: S [0,64) O [64,192); head B: S [256,320) O [320,448)
 
 // dynamic shared memory layout (1024-byte aligned pieces for 128B swizzle)
-constexpr int kOffQ = 0;                    // 2 x [128 rows][128 B]
-constexpr int kOffKV = 32768;               // 2 stages x (K 32 KiB + V 32 KiB)
-constexpr int kStageBytes = 65536;
-constexpr int kOffP = kOffKV + 2 * kStageBytes;  // 2 x [128 rows][128 B]
-constexpr int kOffBar = kOffP + 32768;
+constexpr int kQBytes = kBM * kD * 2;          // 32 KiB: 2 atoms of [128 rows][128 B]
+constexpr int kKVHalf = kBN * kD * 2;          // 16 KiB: 2 atoms of [64 rows][128 B]
+constexpr int kStageBytes = 2 * kKVHalf;       // K then V
+constexpr int kPBytes = kBM * kBN * 2;         // 16 KiB: 1 atom of [128 rows][128 B]
+constexpr int kOffQ = 0;                        // Q_A, Q_B
+constexpr int kOffKV = 2 * kQBytes;
+constexpr int kOffP = kOffKV + kStages * kStageBytes;  // P_A, P_B
+constexpr int kOffBar = kOffP + 2 * kPBytes;
 constexpr int kSmemBytes = kOffBar + 128 + 1024;  // + slack for 1024-byte alignment
 
 struct alignas(64) PrefillParams {
@@ -61,7 +70,7 @@ struct alignas(64) PrefillParams {
   const int32_t* prompt_len;  // [B] or null
   int32_t* err;
   int quota[kMaxHeads];
-  int B, H, Hkv, S, C, KL, per, n_qtiles;
+  int B, H, Hkv, G, npairs, S, C, KL, per, n_qtiles;
   float scale_log2;
 };
 
@@ -95,10 +104,9 @@ __device__ __forceinline__ int tile_class(const PrefillParams& p, int h, int qt,
 }
 
 // Inside any tile the visible keys of one query row are a PREFIX of the tile's
-// 128 columns: the causal diagonal of the own block (kv <= q), the raw-prompt
+// columns: the causal diagonal of the own block (kv <= q), the raw-prompt
 // boundary of an earlier block (kb*C + kw < prompt_len) or the quota boundary
-// of a code tile (kw - C < quota).  Returns that prefix length in [0, 128]
-// (128 for FULL tiles, 0 for EMPTY ones); the element-wise mask is c < limit.
+// of a code tile (kw - C < quota).  Returns that prefix length in [0, kBN].
 __device__ __forceinline__ int tile_limit(const PrefillParams& p, int h, int kt, int q, int pl) {
   const int k0 = kt * kBN;
   const int qb = q / p.per, kb = k0 / p.per;
@@ -128,15 +136,18 @@ __device__ __forceinline__ uint64_t desc_kmajor_sw128(uint32_t saddr) {
   return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
          ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
-__device__ __forceinline__ uint64_t desc_mnmajor_sw128(uint32_t saddr) {
+__device__ __forceinline__ uint64_t desc_mnmajor_sw128(uint32_t saddr, uint32_t lbo) {
   // MN-major, 128B swizzle: a K row = 64 MN elements (128 B); 8 K rows form a
-  // 1024 B atom (SBO = 1024); the next 64 MN elements are 16 KiB away (LBO).
-  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)(16384 >> 4) << 16) |
+  // 1024 B atom (SBO = 1024); the next 64 MN elements are `lbo` bytes away.
+  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
          ((uint64_t)(1024 >> 4) << 32) | ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
-// kind::f16 instruction descriptor: D f32, A/B bf16, M=128, N=128.
-constexpr uint32_t kIdescQK = (1u << 4) | (1u << 7) | (1u << 10) | ((128u >> 3) << 17) | ((128u >> 4) << 24);
-constexpr uint32_t kIdescPV = kIdescQK | (1u << 16);  // B (V) is MN-major
+// kind::f16 instruction descriptors: D f32, A/B bf16, M = 128.
+//   S = Q K^T : N = kBN keys, A and B K-major
+//   O += P V  : N = head_dim, A (P) K-major, B (V) MN-major
+constexpr uint32_t kIdescBase = (1u << 4) | (1u << 7) | (1u << 10) | ((128u >> 4) << 24);
+constexpr uint32_t kIdescQK = kIdescBase | ((uint32_t)(kBN >> 3) << 17);
+constexpr uint32_t kIdescPV = kIdescBase | ((uint32_t)(kD >> 3) << 17) | (1u << 16);
 
 __device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                      uint32_t accumulate) {
@@ -223,35 +234,117 @@ __device__ __forceinline__ void mbar_arrive_one(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(bar)) : "memory");
 }
 
+
 // ---------------------------------------------------------------------------
+// Softmax of one head: thread = query row `row` of the tile (TMEM lane).
+struct SoftmaxState {
+  float m_run, l_run;
+};
+
+__device__ __forceinline__ void softmax_tile(const PrefillParams& p, int h, int kt, int q, int pl, int row,
+                                             uint32_t tmem_s, uint32_t tmem_o, uint32_t lane_base, uint8_t* pbuf,
+                                             bool rescale_allowed, SoftmaxState& st) {
+  const float sl2 = p.scale_log2;
+  const int lim = tile_limit(p, h, kt, q, pl);  // visible columns of this row: c < lim
+  float t0[32], t1[32];
+  tmem_ld32(tmem_s + lane_base, t0);
+  tmem_ld32(tmem_s + lane_base + 32, t1);
+  tmem_wait_ld();
+  float mx = -INFINITY;
+  if (lim == kBN) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) mx = fmaxf(mx, fmaxf(t0[i], t1[i]));
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      mx = fmaxf(mx, i < lim ? t0[i] : -INFINITY);
+      mx = fmaxf(mx, i + 32 < lim ? t1[i] : -INFINITY);
+    }
+  }
+  mx *= sl2;
+  const float m_new = fmaxf(st.m_run, mx);
+  const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+  const float alpha = fast_exp2(st.m_run - m_use);
+  float rs = 0.f;
+  // P = exp2(s * scale * log2e - m) -> shared memory, bf16, 128B-swizzled K-major
+  // (16-byte chunk index ^= row % 8)
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    const float* t = half ? t1 : t0;
+#pragma unroll
+    for (int e8 = 0; e8 < 4; ++e8) {
+      uint32_t w[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int c = half * 32 + e8 * 8 + 2 * e;
+        float p0 = fast_exp2(fmaf(t[e8 * 8 + 2 * e], sl2, -m_use));
+        float p1 = fast_exp2(fmaf(t[e8 * 8 + 2 * e + 1], sl2, -m_use));
+        if (lim != kBN) {
+          p0 = c < lim ? p0 : 0.f;
+          p1 = c + 1 < lim ? p1 : 0.f;
+        }
+        rs += p0 + p1;
+        w[e] = pack_bf16x2(p0, p1);
+      }
+      const int ch = half * 4 + e8;
+      uint8_t* dst = pbuf + row * 128 + ((ch ^ (row & 7)) << 4);
+      *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  }
+  st.l_run = st.l_run * alpha + rs;
+  st.m_run = m_new;
+  // rescale the O accumulator when this row's maximum grew (the previous P.V
+  // of this head has completed: this tile's S was committed after it)
+  if (rescale_allowed && __any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll 1
+    for (int c4 = 0; c4 < 4; ++c4) {
+      float t[32];
+      tmem_ld32(tmem_o + lane_base + c4 * 32, t);
+      tmem_wait_ld();
+#pragma unroll
+      for (int i = 0; i < 32; ++i) t[i] *= alpha;
+      tmem_st32(tmem_o + lane_base + c4 * 32, t);
+    }
+    tmem_wait_st();
+  }
+}
+
+__device__ __forceinline__ bool visit_tile(const PrefillParams& p, int hA, int hB, int qt, int kt, int pl) {
+  return tile_class(p, hA, qt, kt, pl) != 0 || (hB >= 0 && tile_class(p, hB, qt, kt, pl) != 0);
+}
+
 __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_constant__ PrefillParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint64_t* q_full = bar + 0;
-  uint64_t* kv_full = bar + 1;   // [2]
-  uint64_t* kv_empty = bar + 3;  // [2]
-  uint64_t* s_full = bar + 5;
-  uint64_t* p_full = bar + 6;
-  uint64_t* o_full = bar + 7;
-  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bar + 8);
+  uint64_t* kv_full = bar + 1;   // [kStages]
+  uint64_t* kv_empty = bar + 4;  // [kStages]
+  uint64_t* s_full = bar + 7;    // [2] per head
+  uint64_t* p_full = bar + 9;    // [2] per head
+  uint64_t* o_full = bar + 11;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bar + 12);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qt = p.n_qtiles - 1 - (int)blockIdx.x;  // heaviest query tiles first
-  const int h = blockIdx.y, b = blockIdx.z;
-  const int hk = h / (p.H / p.Hkv);
+  const int hk = blockIdx.y / p.npairs, hp = blockIdx.y % p.npairs;
+  const int hA = hk * p.G + 2 * hp;
+  const int hB = (2 * hp + 1 < p.G) ? hA + 1 : -1;  // odd group size: the last pair has one head
+  const int b = blockIdx.z;
   const int pl = p.prompt_len ? __ldg(p.prompt_len + b) : 0;
   const int qb = qt * kBM / p.per;
   const int kt_end = (qb + 1) * p.per / kBN;  // key tiles beyond the query's block are never visible
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    mbar_init(&kv_full[0], 1);
-    mbar_init(&kv_full[1], 1);
-    mbar_init(&kv_empty[0], 1);
-    mbar_init(&kv_empty[1], 1);
-    mbar_init(s_full, 1);
-    mbar_init(p_full, 128);
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+    }
+    mbar_init(&s_full[0], 1);
+    mbar_init(&s_full[1], 1);
+    mbar_init(&p_full[0], 128);
+    mbar_init(&p_full[1], 128);
     mbar_init(o_full, 1);
   }
   if (warp == 1) {
@@ -263,168 +356,152 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *s_tmem;
-  const uint32_t tmem_s = tmem, tmem_o = tmem + 128;
   bool dead = false;
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
-      mbar_expect_tx(q_full, 2 * 16384);
-      tma_load_4d(smem + kOffQ, &p.tm_q, 0, qt * kBM, h, b, q_full);
-      tma_load_4d(smem + kOffQ + 16384, &p.tm_q, 64, qt * kBM, h, b, q_full);
+      mbar_expect_tx(q_full, (hB >= 0 ? 2 : 1) * kQBytes);
+      tma_load_4d(smem + kOffQ, &p.tm_q, 0, qt * kBM, hA, b, q_full);
+      tma_load_4d(smem + kOffQ + kQBytes / 2, &p.tm_q, 64, qt * kBM, hA, b, q_full);
+      if (hB >= 0) {
+        tma_load_4d(smem + kOffQ + kQBytes, &p.tm_q, 0, qt * kBM, hB, b, q_full);
+        tma_load_4d(smem + kOffQ + kQBytes + kQBytes / 2, &p.tm_q, 64, qt * kBM, hB, b, q_full);
+      }
       int j = 0;
       for (int kt = 0; kt < kt_end; ++kt) {
-        if (tile_class(p, h, qt, kt, pl) == 0) continue;
-        const int st = j & 1;
-        if (!wait_or_abort(&kv_empty[st], (uint32_t)(((j >> 1) & 1) ^ 1), dead, p.err)) break;
+        if (!visit_tile(p, hA, hB, qt, kt, pl)) continue;
+        const int st = j % kStages;
+        if (!wait_or_abort(&kv_empty[st], (uint32_t)(((j / kStages) & 1) ^ 1), dead, p.err)) break;
         uint8_t* kbuf = smem + kOffKV + st * kStageBytes;
-        mbar_expect_tx(&kv_full[st], 4 * 16384);
+        mbar_expect_tx(&kv_full[st], kStageBytes);
         tma_load_4d(kbuf, &p.tm_k, 0, kt * kBN, hk, b, &kv_full[st]);
-        tma_load_4d(kbuf + 16384, &p.tm_k, 64, kt * kBN, hk, b, &kv_full[st]);
-        tma_load_4d(kbuf + 32768, &p.tm_v, 0, kt * kBN, hk, b, &kv_full[st]);
-        tma_load_4d(kbuf + 49152, &p.tm_v, 64, kt * kBN, hk, b, &kv_full[st]);
+        tma_load_4d(kbuf + kKVHalf / 2, &p.tm_k, 64, kt * kBN, hk, b, &kv_full[st]);
+        tma_load_4d(kbuf + kKVHalf, &p.tm_v, 0, kt * kBN, hk, b, &kv_full[st]);
+        tma_load_4d(kbuf + kKVHalf + kKVHalf / 2, &p.tm_v, 64, kt * kBN, hk, b, &kv_full[st]);
         ++j;
       }
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
+      const bool two = hB >= 0;
       wait_or_abort(q_full, 0, dead, p.err);
-      const uint32_t q_addr = smem_u32(smem + kOffQ);
-      const uint32_t p_addr = smem_u32(smem + kOffP);
-      int j = 0;
-      for (int kt = 0; kt < kt_end; ++kt) {
-        if (tile_class(p, h, qt, kt, pl) == 0) continue;
-        const int st = j & 1;
-        if (!wait_or_abort(&kv_full[st], (uint32_t)((j >> 1) & 1), dead, p.err)) break;
-        tc_fence_after();
-        const uint32_t k_addr = smem_u32(smem + kOffKV + st * kStageBytes);
-        const uint32_t v_addr = k_addr + 32768;
+      const uint32_t qa = smem_u32(smem + kOffQ), qbv = qa + kQBytes;
+      const uint32_t pa = smem_u32(smem + kOffP), pbv = pa + kPBytes;
+      const uint32_t sA = tmem, oA = tmem + 64, sB = tmem + 256, oB = tmem + 320;
+      auto issue_s = [&](uint32_t qaddr, uint32_t sd, int st) {
+        const uint32_t kaddr = smem_u32(smem + kOffKV + st * kStageBytes);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {  // S = Q K^T over head_dim in steps of 16
-          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-          umma(tmem_s, desc_kmajor_sw128(q_addr + off), desc_kmajor_sw128(k_addr + off), kIdescQK,
-               kk > 0 ? 1u : 0u);
+        for (int kk = 0; kk < 8; ++kk) {  // over head_dim in steps of 16
+          umma(sd, desc_kmajor_sw128(qaddr + (kk >> 2) * (kQBytes / 2) + (kk & 3) * 32),
+               desc_kmajor_sw128(kaddr + (kk >> 2) * (kKVHalf / 2) + (kk & 3) * 32), kIdescQK, kk > 0 ? 1u : 0u);
         }
-        umma_commit(s_full);
-        if (!wait_or_abort(p_full, (uint32_t)(j & 1), dead, p.err)) break;
-        tc_fence_after();
+      };
+      auto issue_pv = [&](uint32_t paddr, uint32_t od, int st, bool first) {
+        const uint32_t vaddr = smem_u32(smem + kOffKV + st * kStageBytes + kKVHalf);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {  // O += P V over the 128 keys in steps of 16
-          const uint32_t poff = (kk >> 2) * 16384 + (kk & 3) * 32;
-          umma(tmem_o, desc_kmajor_sw128(p_addr + poff), desc_mnmajor_sw128(v_addr + kk * 2048), kIdescPV,
-               (j > 0 || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < kBN / 16; ++kk) {  // over the tile's keys in steps of 16
+          umma(od, desc_kmajor_sw128(paddr + kk * 32), desc_mnmajor_sw128(vaddr + kk * 2048, kKVHalf / 2),
+               kIdescPV, (!first || kk > 0) ? 1u : 0u);
         }
-        umma_commit(&kv_empty[st]);
-        ++j;
+      };
+      // tile sequence
+      int n = 0;
+      for (int kt = 0; kt < kt_end; ++kt) n += visit_tile(p, hA, hB, qt, kt, pl) ? 1 : 0;
+      if (n > 0 && !dead) {
+        if (wait_or_abort(&kv_full[0], 0, dead, p.err)) {
+          tc_fence_after();
+          issue_s(qa, sA, 0);
+          umma_commit(&s_full[0]);
+          if (two) {
+            issue_s(qbv, sB, 0);
+            umma_commit(&s_full[1]);
+          }
+        }
+      }
+      for (int j = 0; j < n && !dead; ++j) {
+        const int st = j % kStages, stn = (j + 1) % kStages;
+        const bool more = j + 1 < n;
+        // head A: P_A(j) V_j, then S_A(j+1)
+        if (!wait_or_abort(&p_full[0], (uint32_t)(j & 1), dead, p.err)) break;
+        tc_fence_after();
+        issue_pv(pa, oA, st, j == 0);
+        if (!two) umma_commit(&kv_empty[st]);
+        if (more) {
+          if (!wait_or_abort(&kv_full[stn], (uint32_t)(((j + 1) / kStages) & 1), dead, p.err)) break;
+          tc_fence_after();
+          issue_s(qa, sA, stn);
+          umma_commit(&s_full[0]);
+        }
+        if (two) {
+          // head B: P_B(j) V_j (last use of this K/V stage), then S_B(j+1)
+          if (!wait_or_abort(&p_full[1], (uint32_t)(j & 1), dead, p.err)) break;
+          tc_fence_after();
+          issue_pv(pbv, oB, st, j == 0);
+          umma_commit(&kv_empty[st]);
+          if (more) {
+            issue_s(qbv, sB, stn);
+            umma_commit(&s_full[1]);
+          }
+        }
       }
       umma_commit(o_full);
     }
   } else {
-    // ---------------- softmax / correction / epilogue (warps 2..5) ----------------
-    const int quarter = warp & 3;                 // TMEM lane quarter this warp may access
-    const int row = quarter * 32 + lane;          // query row within the tile
+    // ---------------- softmax / correction / epilogue ----------------
+    const int head_slot = (warp - 2) >> 2;          // 0: head A (warps 2..5), 1: head B (warps 6..9)
+    const int h = head_slot ? hB : hA;
+    const int quarter = warp & 3;                    // TMEM lane quarter this warp may access
+    const int row = quarter * 32 + lane;             // query row within the tile
     const int q = qt * kBM + row;
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
-    const float sl2 = p.scale_log2;
-    uint8_t* pbuf = smem + kOffP;
-    float m_run = -INFINITY, l_run = 0.f;
-    int j = 0;
-    for (int kt = 0; kt < kt_end; ++kt) {
-      const int cls = tile_class(p, h, qt, kt, pl);
-      if (cls == 0) continue;
-      // warp-uniform decision: the tcgen05.ld below is a warp-collective
-      const bool ok = __all_sync(0xffffffffu, wait_or_abort(s_full, (uint32_t)(j & 1), dead, p.err));
-      if (!ok) {
-        dead = true;
-        break;
-      }
-      tc_fence_after();
-      const int lim = tile_limit(p, h, kt, q, pl);  // visible columns of this row: c < lim
-      // pass 1: row maximum over the visible columns (S read from TMEM in 32-column chunks)
-      float mx = -INFINITY;
-#pragma unroll 1
-      for (int c4 = 0; c4 < 4; ++c4) {
-        float t[32];
-        tmem_ld32(tmem_s + lane_base + c4 * 32, t);
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) mx = fmaxf(mx, (c4 * 32 + i < lim) ? t[i] : -INFINITY);
-      }
-      mx *= sl2;
-      const float m_new = fmaxf(m_run, mx);
-      const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-      const float alpha = fast_exp2(m_run - m_use);
-      // pass 2: P = exp2(s * scale * log2e - m) -> shared memory, bf16, 128B-swizzled
-      // K-major (16-byte chunk index ^= row % 8), and the row sum
-      float rs = 0.f;
-#pragma unroll 1
-      for (int c4 = 0; c4 < 4; ++c4) {
-        float t[32];
-        tmem_ld32(tmem_s + lane_base + c4 * 32, t);
-        tmem_wait_ld();
-#pragma unroll
-        for (int e8 = 0; e8 < 4; ++e8) {
-          uint32_t w[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int c = c4 * 32 + e8 * 8 + 2 * e;
-            const float p0 = (c < lim) ? fast_exp2(fmaf(t[e8 * 8 + 2 * e], sl2, -m_use)) : 0.f;
-            const float p1 = (c + 1 < lim) ? fast_exp2(fmaf(t[e8 * 8 + 2 * e + 1], sl2, -m_use)) : 0.f;
-            rs += p0 + p1;
-            w[e] = pack_bf16x2(p0, p1);
-          }
-          const int ch = c4 * 4 + e8, atom = ch >> 3, chunk = ch & 7;
-          uint8_t* dst = pbuf + atom * 16384 + row * 128 + ((chunk ^ (row & 7)) << 4);
-          *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+    const uint32_t tmem_s = tmem + (head_slot ? 256 : 0), tmem_o = tmem_s + 64;
+    uint8_t* pbuf = smem + kOffP + head_slot * kPBytes;
+    if (h >= 0) {
+      SoftmaxState st{-INFINITY, 0.f};
+      int j = 0;
+      for (int kt = 0; kt < kt_end; ++kt) {
+        if (!visit_tile(p, hA, hB, qt, kt, pl)) continue;
+        // warp-uniform decision: tcgen05.ld is a warp-collective
+        const bool ok = __all_sync(0xffffffffu, wait_or_abort(&s_full[head_slot], (uint32_t)(j & 1), dead, p.err));
+        if (!ok) {
+          dead = true;
+          break;
         }
+        tc_fence_after();
+        softmax_tile(p, h, kt, q, pl, row, tmem_s, tmem_o, lane_base, pbuf, j > 0, st);
+        asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // P visible to the tensor core
+        tc_fence_before();
+        mbar_arrive_one(&p_full[head_slot]);
+        ++j;
       }
-      l_run = l_run * alpha + rs;
-      m_run = m_new;
-      // rescale the O accumulator when this row's maximum grew (PV(j-1) has
-      // completed: s_full(j) was committed after it)
-      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+      // epilogue
+      const bool o_ok = __all_sync(0xffffffffu, wait_or_abort(o_full, 0, dead, p.err));
+      tc_fence_after();
+      if (o_ok) {
+        const float inv = st.l_run > 0.f ? 1.f / st.l_run : 0.f;
+        __nv_bfloat16* orow = p.out + (int64_t)b * p.o_sb + (int64_t)h * p.o_sh + (int64_t)q * p.o_ss;
 #pragma unroll 1
         for (int c4 = 0; c4 < 4; ++c4) {
           float t[32];
           tmem_ld32(tmem_o + lane_base + c4 * 32, t);
           tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) t[i] *= alpha;
-          tmem_st32(tmem_o + lane_base + c4 * 32, t);
+          for (int v8 = 0; v8 < 4; ++v8) {
+            uint4 pk;
+            pk.x = pack_bf16x2(t[v8 * 8 + 0] * inv, t[v8 * 8 + 1] * inv);
+            pk.y = pack_bf16x2(t[v8 * 8 + 2] * inv, t[v8 * 8 + 3] * inv);
+            pk.z = pack_bf16x2(t[v8 * 8 + 4] * inv, t[v8 * 8 + 5] * inv);
+            pk.w = pack_bf16x2(t[v8 * 8 + 6] * inv, t[v8 * 8 + 7] * inv);
+            *reinterpret_cast<uint4*>(orow + c4 * 32 + v8 * 8) = pk;
+          }
         }
-        tmem_wait_st();
+        if (p.lse) {
+          const float lse2 = st.l_run > 0.f ? st.m_run + log2f(st.l_run) : -INFINITY;
+          p.lse[((int64_t)b * p.H + h) * p.S + q] = lse2 * 0.6931471805599453f;  // natural log
+        }
       }
-      asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // P visible to the tensor core
-      tc_fence_before();
-      mbar_arrive_one(p_full);
-      ++j;
-    }
-    // epilogue
-    const bool o_ok = __all_sync(0xffffffffu, wait_or_abort(o_full, 0, dead, p.err));
-    tc_fence_after();
-    if (o_ok) {
-    const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-    __nv_bfloat16* orow = p.out + (int64_t)b * p.o_sb + (int64_t)h * p.o_sh + (int64_t)q * p.o_ss;
-#pragma unroll 1
-    for (int c4 = 0; c4 < 4; ++c4) {
-      float t[32];
-      tmem_ld32(tmem_o + lane_base + c4 * 32, t);
-      tmem_wait_ld();
-#pragma unroll
-      for (int v8 = 0; v8 < 4; ++v8) {
-        uint4 pk;
-        pk.x = pack_bf16x2(t[v8 * 8 + 0] * inv, t[v8 * 8 + 1] * inv);
-        pk.y = pack_bf16x2(t[v8 * 8 + 2] * inv, t[v8 * 8 + 3] * inv);
-        pk.z = pack_bf16x2(t[v8 * 8 + 4] * inv, t[v8 * 8 + 5] * inv);
-        pk.w = pack_bf16x2(t[v8 * 8 + 6] * inv, t[v8 * 8 + 7] * inv);
-        *reinterpret_cast<uint4*>(orow + c4 * 32 + v8 * 8) = pk;
-      }
-    }
-    if (p.lse) {
-      const float lse2 = l_run > 0.f ? m_run + log2f(l_run) : -INFINITY;
-      p.lse[((int64_t)b * p.H + h) * p.S + q] = lse2 * 0.6931471805599453f;  // natural log
-    }
     }
   }
   tc_fence_before();
@@ -441,13 +518,13 @@ using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, 
                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
 // [B][heads][S][128] bf16 with element strides (sb, sh, ss) -> 4D tensor map,
-// box = 64 dims x 128 rows, 128B swizzle.
-int make_map(CUtensorMap* m, const void* base, int B, int heads, int S, const int64_t* strides) {
+// box = 64 dims x box_rows rows, 128B swizzle.
+int make_map(CUtensorMap* m, const void* base, int B, int heads, int S, const int64_t* strides, int box_rows) {
   cuuint64_t dims[4] = {(cuuint64_t)kD, (cuuint64_t)S, (cuuint64_t)heads, (cuuint64_t)B};
   cuuint64_t gstr[3] = {(cuuint64_t)strides[2] * 2, (cuuint64_t)strides[1] * 2, (cuuint64_t)strides[0] * 2};
   for (int i = 0; i < 3; ++i)
     if (gstr[i] % 16 != 0 || gstr[i] == 0) return ABKV_ERR_INVALID_ARG;
-  cuuint32_t box[4] = {64, (cuuint32_t)kBN, 1, 1};
+  cuuint32_t box[4] = {64, (cuuint32_t)box_rows, 1, 1};
   cuuint32_t es[4] = {1, 1, 1, 1};
   // the driver entry point is resolved through the runtime, so the library
   // does not link libcuda and still loads on hosts without a GPU driver
@@ -477,7 +554,7 @@ extern "C" int abkv_prefill_masked(const void* q, const int64_t* q_strides, cons
   if (!q || !k || !v || !out || !q_strides || !k_strides || !v_strides || !out_strides) return ABKV_ERR_INVALID_ARG;
   if (B <= 0 || H <= 0 || Hkv <= 0 || S <= 0 || H % Hkv != 0 || !(scale > 0.f)) return ABKV_ERR_INVALID_ARG;
   if (head_dim != kD || H > kMaxHeads || B > 65535) return ABKV_ERR_UNSUPPORTED;
-  if (C <= 0 || K_layout <= 0 || C % kBN || K_layout % kBN || S % (C + K_layout)) return ABKV_ERR_UNSUPPORTED;
+  if (C <= 0 || K_layout <= 0 || C % kBM || K_layout % kBM || S % (C + K_layout)) return ABKV_ERR_UNSUPPORTED;
   if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) |
        reinterpret_cast<uintptr_t>(out)) & 15)
     return ABKV_ERR_INVALID_ARG;
@@ -486,9 +563,9 @@ extern "C" int abkv_prefill_masked(const void* q, const int64_t* q_strides, cons
     return ABKV_ERR_WORKSPACE;
   PrefillParams prm;
   std::memset(&prm, 0, sizeof(prm));
-  int st = make_map(&prm.tm_q, q, B, H, S, q_strides);
-  if (st == ABKV_OK) st = make_map(&prm.tm_k, k, B, Hkv, S, k_strides);
-  if (st == ABKV_OK) st = make_map(&prm.tm_v, v, B, Hkv, S, v_strides);
+  int st = make_map(&prm.tm_q, q, B, H, S, q_strides, kBM);
+  if (st == ABKV_OK) st = make_map(&prm.tm_k, k, B, Hkv, S, k_strides, kBN);
+  if (st == ABKV_OK) st = make_map(&prm.tm_v, v, B, Hkv, S, v_strides, kBN);
   if (st != ABKV_OK) return st;
   prm.out = static_cast<__nv_bfloat16*>(out);
   prm.o_sb = out_strides[0];
@@ -505,6 +582,8 @@ extern "C" int abkv_prefill_masked(const void* q, const int64_t* q_strides, cons
   prm.B = B;
   prm.H = H;
   prm.Hkv = Hkv;
+  prm.G = H / Hkv;
+  prm.npairs = (prm.G + 1) / 2;
   prm.S = S;
   prm.C = C;
   prm.KL = K_layout;
@@ -514,7 +593,8 @@ extern "C" int abkv_prefill_masked(const void* q, const int64_t* q_strides, cons
   if (cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) !=
       cudaSuccess)
     return ABKV_ERR_CUDA;
-  dim3 grid(prm.n_qtiles, H, B);
+  if (Hkv * prm.npairs > 65535) return ABKV_ERR_UNSUPPORTED;
+  dim3 grid(prm.n_qtiles, Hkv * prm.npairs, B);
   prefill_kernel<<<grid, kThreads, kSmemBytes, reinterpret_cast<cudaStream_t>(stream)>>>(prm);
   if (cudaGetLastError() != cudaSuccess) return ABKV_ERR_CUDA;
   return ABKV_OK;
