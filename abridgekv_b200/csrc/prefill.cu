@@ -25,8 +25,9 @@
 // (loaded once); 10 warps:
 //   warp 0      TMA producer: Q of both heads, then K/V tiles into a 3-stage
 //               ring (cp.async.bulk.tensor, 128B swizzle, no multicast)
-//   warp 1      TMEM owner (512 columns); lane 0 issues tcgen05.mma in the order
-//               S_A(0) S_B(0) | PV_A(j) S_A(j+1) PV_B(j) S_B(j+1) | ...
+//   warp 1      TMEM owner (512 columns: per head two S buffers + O); lane 0
+//               issues tcgen05.mma in the order
+//               S_A(0) S_B(0) S_A(1) S_B(1) | PV_A(j) S_A(j+2) PV_B(j) S_B(j+2) | ...
 //                 S  = Q K^T   (A = Q, B = K, both K-major, fp32 in TMEM)
 //                 O += P V     (A = P from shared memory, K-major; B = V, MN-major)
 //               so each head's softmax overlaps the other head's MMAs
@@ -49,7 +50,7 @@ constexpr int kBM = 128, kBN = 64, kD = 128;
 constexpr int kThreads = 320;
 constexpr int kMaxHeads = 128;
 constexpr int kStages = 3;
-constexpr uint32_t kTmemCols = 512;  // head A: S [0,64) O [64,192); head B: S [256,320) O [320,448)
+constexpr uint32_t kTmemCols = 512;  // per head (A at 0, B at 256): S buffers [0,64) [64,128), O [128,256)
 
 // dynamic shared memory layout (1024-byte aligned pieces for 128B swizzle)
 constexpr int kQBytes = kBM * kD * 2;          // 32 KiB: 2 atoms of [128 rows][128 B]
@@ -60,7 +61,11 @@ constexpr int kOffQ = 0;                        // Q_A, Q_B
 constexpr int kOffKV = 2 * kQBytes;
 constexpr int kOffP = kOffKV + kStages * kStageBytes;  // P_A, P_B
 constexpr int kOffBar = kOffP + 2 * kPBytes;
-constexpr int kSmemBytes = kOffBar + 128 + 1024;  // + slack for 1024-byte alignment
+constexpr int kSmemBytes = kOffBar + 256 + 1024;  // + slack for 1024-byte alignment
+// Lazy rescaling: a row keeps its reference maximum until a tile's maximum
+// exceeds it by more than this (log2 units), so P <= 2^8 and O is rescaled
+// only on large jumps (O and the row sum always share the reference).
+constexpr float kRescaleThreshold = 8.f;
 
 struct alignas(64) PrefillParams {
   CUtensorMap tm_q, tm_k, tm_v;
@@ -241,9 +246,13 @@ struct SoftmaxState {
   float m_run, l_run;
 };
 
+// Softmax of one (head, key tile) for query row `row` (= TMEM lane):
+// reads S, updates the reference maximum / row sum, waits until the previous
+// P.V of this head has completed (o_done), rescales O when needed and writes
+// P (bf16, 128B-swizzled K-major: 16-byte chunk index ^= row % 8).
 __device__ __forceinline__ void softmax_tile(const PrefillParams& p, int h, int kt, int q, int pl, int row,
                                              uint32_t tmem_s, uint32_t tmem_o, uint32_t lane_base, uint8_t* pbuf,
-                                             bool rescale_allowed, SoftmaxState& st) {
+                                             int j, uint64_t* o_done, bool& dead, SoftmaxState& st) {
   const float sl2 = p.scale_log2;
   const int lim = tile_limit(p, h, kt, q, pl);  // visible columns of this row: c < lim
   float t0[32], t1[32];
@@ -262,18 +271,17 @@ __device__ __forceinline__ void softmax_tile(const PrefillParams& p, int h, int 
     }
   }
   mx *= sl2;
-  const float m_new = fmaxf(st.m_run, mx);
+  const bool need = mx > st.m_run + kRescaleThreshold || (st.m_run == -INFINITY && mx > -INFINITY);
+  const float m_new = need ? mx : st.m_run;
   const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-  const float alpha = fast_exp2(st.m_run - m_use);
+  const float alpha = need ? fast_exp2(st.m_run - m_use) : 1.f;
   float rs = 0.f;
-  // P = exp2(s * scale * log2e - m) -> shared memory, bf16, 128B-swizzled K-major
-  // (16-byte chunk index ^= row % 8)
+  uint32_t w[8][4];
 #pragma unroll
   for (int half = 0; half < 2; ++half) {
     const float* t = half ? t1 : t0;
 #pragma unroll
     for (int e8 = 0; e8 < 4; ++e8) {
-      uint32_t w[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int c = half * 32 + e8 * 8 + 2 * e;
@@ -284,28 +292,33 @@ __device__ __forceinline__ void softmax_tile(const PrefillParams& p, int h, int 
           p1 = c + 1 < lim ? p1 : 0.f;
         }
         rs += p0 + p1;
-        w[e] = pack_bf16x2(p0, p1);
+        w[half * 4 + e8][e] = pack_bf16x2(p0, p1);
       }
-      const int ch = half * 4 + e8;
-      uint8_t* dst = pbuf + row * 128 + ((ch ^ (row & 7)) << 4);
-      *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
     }
   }
   st.l_run = st.l_run * alpha + rs;
   st.m_run = m_new;
-  // rescale the O accumulator when this row's maximum grew (the previous P.V
-  // of this head has completed: this tile's S was committed after it)
-  if (rescale_allowed && __any_sync(0xffffffffu, alpha != 1.f)) {
+  if (j > 0) {
+    // the previous P.V of this head must be done before P and O are touched
+    const bool ok = __all_sync(0xffffffffu, wait_or_abort(o_done, (uint32_t)((j - 1) & 1), dead, p.err));
+    tc_fence_after();
+    if (ok && __any_sync(0xffffffffu, need)) {
 #pragma unroll 1
-    for (int c4 = 0; c4 < 4; ++c4) {
-      float t[32];
-      tmem_ld32(tmem_o + lane_base + c4 * 32, t);
-      tmem_wait_ld();
+      for (int c4 = 0; c4 < 4; ++c4) {
+        float t[32];
+        tmem_ld32(tmem_o + lane_base + c4 * 32, t);
+        tmem_wait_ld();
 #pragma unroll
-      for (int i = 0; i < 32; ++i) t[i] *= alpha;
-      tmem_st32(tmem_o + lane_base + c4 * 32, t);
+        for (int i = 0; i < 32; ++i) t[i] *= alpha;
+        tmem_st32(tmem_o + lane_base + c4 * 32, t);
+      }
+      tmem_wait_st();
     }
-    tmem_wait_st();
+  }
+#pragma unroll
+  for (int ch = 0; ch < 8; ++ch) {
+    uint8_t* dst = pbuf + row * 128 + ((ch ^ (row & 7)) << 4);
+    *reinterpret_cast<uint4*>(dst) = make_uint4(w[ch][0], w[ch][1], w[ch][2], w[ch][3]);
   }
 }
 
@@ -320,10 +333,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
   uint64_t* q_full = bar + 0;
   uint64_t* kv_full = bar + 1;   // [kStages]
   uint64_t* kv_empty = bar + 4;  // [kStages]
-  uint64_t* s_full = bar + 7;    // [2] per head
-  uint64_t* p_full = bar + 9;    // [2] per head
-  uint64_t* o_full = bar + 11;
-  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bar + 12);
+  uint64_t* s_full = bar + 7;    // [head][S buffer]
+  uint64_t* p_full = bar + 11;   // [head]
+  uint64_t* o_done = bar + 13;   // [head]: one phase per P.V
+  uint64_t* o_full = bar + 15;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bar + 16);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qt = p.n_qtiles - 1 - (int)blockIdx.x;  // heaviest query tiles first
@@ -341,10 +355,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
     }
-    mbar_init(&s_full[0], 1);
-    mbar_init(&s_full[1], 1);
+    for (int i = 0; i < 4; ++i) mbar_init(&s_full[i], 1);
     mbar_init(&p_full[0], 128);
     mbar_init(&p_full[1], 128);
+    mbar_init(&o_done[0], 1);
+    mbar_init(&o_done[1], 1);
     mbar_init(o_full, 1);
   }
   if (warp == 1) {
@@ -389,7 +404,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
       wait_or_abort(q_full, 0, dead, p.err);
       const uint32_t qa = smem_u32(smem + kOffQ), qbv = qa + kQBytes;
       const uint32_t pa = smem_u32(smem + kOffP), pbv = pa + kPBytes;
-      const uint32_t sA = tmem, oA = tmem + 64, sB = tmem + 256, oB = tmem + 320;
+      const uint32_t sA = tmem, oA = tmem + 128, sB = tmem + 256, oB = tmem + 384;
       auto issue_s = [&](uint32_t qaddr, uint32_t sd, int st) {
         const uint32_t kaddr = smem_u32(smem + kOffKV + st * kStageBytes);
 #pragma unroll
@@ -406,43 +421,44 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                kIdescPV, (!first || kk > 0) ? 1u : 0u);
         }
       };
-      // tile sequence
+      // tile sequence; S of tile j goes to S buffer j % 2 of each head
       int n = 0;
       for (int kt = 0; kt < kt_end; ++kt) n += visit_tile(p, hA, hB, qt, kt, pl) ? 1 : 0;
-      if (n > 0 && !dead) {
-        if (wait_or_abort(&kv_full[0], 0, dead, p.err)) {
-          tc_fence_after();
-          issue_s(qa, sA, 0);
-          umma_commit(&s_full[0]);
-          if (two) {
-            issue_s(qbv, sB, 0);
-            umma_commit(&s_full[1]);
-          }
+      for (int t = 0; t < 2 && t < n && !dead; ++t) {
+        if (!wait_or_abort(&kv_full[t], 0, dead, p.err)) break;
+        tc_fence_after();
+        issue_s(qa, sA + 64 * t, t);
+        umma_commit(&s_full[t]);
+        if (two) {
+          issue_s(qbv, sB + 64 * t, t);
+          umma_commit(&s_full[2 + t]);
         }
       }
       for (int j = 0; j < n && !dead; ++j) {
-        const int st = j % kStages, stn = (j + 1) % kStages;
-        const bool more = j + 1 < n;
-        // head A: P_A(j) V_j, then S_A(j+1)
+        const int st = j % kStages, st2 = (j + 2) % kStages;
+        const bool more = j + 2 < n;
+        // head A: P_A(j) V_j; S_A(j+2) into the S buffer softmax A(j) has released
         if (!wait_or_abort(&p_full[0], (uint32_t)(j & 1), dead, p.err)) break;
         tc_fence_after();
         issue_pv(pa, oA, st, j == 0);
+        umma_commit(&o_done[0]);
         if (!two) umma_commit(&kv_empty[st]);
         if (more) {
-          if (!wait_or_abort(&kv_full[stn], (uint32_t)(((j + 1) / kStages) & 1), dead, p.err)) break;
+          if (!wait_or_abort(&kv_full[st2], (uint32_t)(((j + 2) / kStages) & 1), dead, p.err)) break;
           tc_fence_after();
-          issue_s(qa, sA, stn);
-          umma_commit(&s_full[0]);
+          issue_s(qa, sA + 64 * (j & 1), st2);
+          umma_commit(&s_full[j & 1]);
         }
         if (two) {
-          // head B: P_B(j) V_j (last use of this K/V stage), then S_B(j+1)
+          // head B: P_B(j) V_j (last use of this K/V stage), then S_B(j+2)
           if (!wait_or_abort(&p_full[1], (uint32_t)(j & 1), dead, p.err)) break;
           tc_fence_after();
           issue_pv(pbv, oB, st, j == 0);
+          umma_commit(&o_done[1]);
           umma_commit(&kv_empty[st]);
           if (more) {
-            issue_s(qbv, sB, stn);
-            umma_commit(&s_full[1]);
+            issue_s(qbv, sB + 64 * (j & 1), st2);
+            umma_commit(&s_full[2 + (j & 1)]);
           }
         }
       }
@@ -456,7 +472,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
     const int row = quarter * 32 + lane;             // query row within the tile
     const int q = qt * kBM + row;
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
-    const uint32_t tmem_s = tmem + (head_slot ? 256 : 0), tmem_o = tmem_s + 64;
+    const uint32_t tmem_h = tmem + (head_slot ? 256 : 0), tmem_o = tmem_h + 128;
     uint8_t* pbuf = smem + kOffP + head_slot * kPBytes;
     if (h >= 0) {
       SoftmaxState st{-INFINITY, 0.f};
@@ -464,13 +480,15 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
       for (int kt = 0; kt < kt_end; ++kt) {
         if (!visit_tile(p, hA, hB, qt, kt, pl)) continue;
         // warp-uniform decision: tcgen05.ld is a warp-collective
-        const bool ok = __all_sync(0xffffffffu, wait_or_abort(&s_full[head_slot], (uint32_t)(j & 1), dead, p.err));
+        const bool ok = __all_sync(
+            0xffffffffu, wait_or_abort(&s_full[2 * head_slot + (j & 1)], (uint32_t)((j >> 1) & 1), dead, p.err));
         if (!ok) {
           dead = true;
           break;
         }
         tc_fence_after();
-        softmax_tile(p, h, kt, q, pl, row, tmem_s, tmem_o, lane_base, pbuf, j > 0, st);
+        softmax_tile(p, h, kt, q, pl, row, tmem_h + 64 * (j & 1), tmem_o, lane_base, pbuf, j,
+                     &o_done[head_slot], dead, st);
         asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // P visible to the tensor core
         tc_fence_before();
         mbar_arrive_one(&p_full[head_slot]);
