@@ -61,7 +61,9 @@ constexpr int kOffQ = 0;                        // Q_A, Q_B
 constexpr int kOffKV = 2 * kQBytes;
 constexpr int kOffP = kOffKV + kStages * kStageBytes;  // P_A, P_B
 constexpr int kOffBar = kOffP + 2 * kPBytes;
-constexpr int kSmemBytes = kOffBar + 256 + 1024;  // + slack for 1024-byte alignment
+constexpr int kOffList = kOffBar + 256;         // visited key tiles: (kb << 16) | kw0, per 64-key tile
+constexpr int kMaxKeyTiles = 512;               // S up to 512 x 64 = 32K rows
+constexpr int kSmemBytes = kOffList + 4 * kMaxKeyTiles + 16 + 1024;  // + slack for 1024-byte alignment
 // Lazy rescaling: a row keeps its reference maximum until a tile's maximum
 // exceeds it by more than this (log2 units), so P <= 2^8 and O is rescaled
 // only on large jumps (O and the row sum always share the reference).
@@ -124,6 +126,21 @@ __device__ __forceinline__ int tile_limit(const PrefillParams& p, int h, int kt,
   } else {
     if (kb == qb && qw < p.C) return 0;
     lim = p.quota[h] - (kw0 - p.C);
+  }
+  return lim < 0 ? 0 : (lim > kBN ? kBN : lim);
+}
+
+// Same limit from precomputed coordinates: the row's block qb and in-block
+// offset qw, the tile's block kb and in-block offset kw0 (k0 = key tile start).
+__device__ __forceinline__ int tile_limit_fast(const PrefillParams& p, int quota, int q, int qb, int qw, int kb,
+                                               int kw0, int k0, int pl) {
+  int lim;
+  if (kw0 < p.C) {
+    if (kb == qb) lim = (qw >= p.C) ? kBN : q - k0 + 1;
+    else lim = pl - (kb * p.C + kw0);
+  } else {
+    if (kb == qb && qw < p.C) return 0;
+    lim = quota - (kw0 - p.C);
   }
   return lim < 0 ? 0 : (lim > kBN ? kBN : lim);
 }
@@ -250,32 +267,31 @@ struct SoftmaxState {
 // reads S, updates the reference maximum / row sum, waits until the previous
 // P.V of this head has completed (o_done), rescales O when needed and writes
 // P (bf16, 128B-swizzled K-major: 16-byte chunk index ^= row % 8).
-__device__ __forceinline__ void softmax_tile(const PrefillParams& p, int h, int kt, int q, int pl, int row,
-                                             uint32_t tmem_s, uint32_t tmem_o, uint32_t lane_base, uint8_t* pbuf,
-                                             int j, uint64_t* o_done, bool& dead, SoftmaxState& st) {
-  const float sl2 = p.scale_log2;
-  const int lim = tile_limit(p, h, kt, q, pl);  // visible columns of this row: c < lim
+__device__ __forceinline__ void softmax_tile(const PrefillParams& p, int lim, int row, uint32_t tmem_s,
+                                             uint32_t tmem_o, uint32_t lane_base, uint8_t* pbuf, int j,
+                                             uint64_t* o_done, bool& dead, SoftmaxState& st) {
+  const float sl2 = p.scale_log2;  // lim: visible columns of this row are c < lim
   float t0[32], t1[32];
   tmem_ld32(tmem_s + lane_base, t0);
   tmem_ld32(tmem_s + lane_base + 32, t1);
   tmem_wait_ld();
-  float mx = -INFINITY;
+  float mxa[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // independent chains
   if (lim == kBN) {
 #pragma unroll
-    for (int i = 0; i < 32; ++i) mx = fmaxf(mx, fmaxf(t0[i], t1[i]));
+    for (int i = 0; i < 32; ++i) mxa[i & 3] = fmaxf(mxa[i & 3], fmaxf(t0[i], t1[i]));
   } else {
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
-      mx = fmaxf(mx, i < lim ? t0[i] : -INFINITY);
-      mx = fmaxf(mx, i + 32 < lim ? t1[i] : -INFINITY);
+      mxa[i & 3] = fmaxf(mxa[i & 3], i < lim ? t0[i] : -INFINITY);
+      mxa[i & 3] = fmaxf(mxa[i & 3], i + 32 < lim ? t1[i] : -INFINITY);
     }
   }
-  mx *= sl2;
+  const float mx = fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3])) * sl2;
   const bool need = mx > st.m_run + kRescaleThreshold || (st.m_run == -INFINITY && mx > -INFINITY);
   const float m_new = need ? mx : st.m_run;
   const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
   const float alpha = need ? fast_exp2(st.m_run - m_use) : 1.f;
-  float rs = 0.f;
+  float rsa[4] = {0.f, 0.f, 0.f, 0.f};
   uint32_t w[8][4];
 #pragma unroll
   for (int half = 0; half < 2; ++half) {
@@ -291,12 +307,12 @@ __device__ __forceinline__ void softmax_tile(const PrefillParams& p, int h, int 
           p0 = c < lim ? p0 : 0.f;
           p1 = c + 1 < lim ? p1 : 0.f;
         }
-        rs += p0 + p1;
+        rsa[e] += p0 + p1;
         w[half * 4 + e8][e] = pack_bf16x2(p0, p1);
       }
     }
   }
-  st.l_run = st.l_run * alpha + rs;
+  st.l_run = st.l_run * alpha + ((rsa[0] + rsa[1]) + (rsa[2] + rsa[3]));
   st.m_run = m_new;
   if (j > 0) {
     // the previous P.V of this head must be done before P and O are touched
@@ -367,10 +383,28 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                  "r"(kTmemCols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n");
   }
+  // the visited key tiles, in order, built once by warp 2 (ballot compaction)
+  int32_t* s_list = reinterpret_cast<int32_t*>(smem + kOffList);
+  int32_t* s_nlist = s_list + kMaxKeyTiles;
+  if (warp == 2) {
+    int n = 0;
+    for (int base = 0; base < kt_end; base += 32) {
+      const int kt = base + lane;
+      const bool vis = kt < kt_end && visit_tile(p, hA, hB, qt, kt, pl);
+      const uint32_t m = __ballot_sync(0xffffffffu, vis);
+      if (vis) {
+        const int k0 = kt * kBN, kb = k0 / p.per;
+        s_list[n + __popc(m & ((1u << lane) - 1u))] = (kb << 16) | (k0 - kb * p.per);
+      }
+      n += __popc(m);
+    }
+    if (lane == 0) *s_nlist = n;
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *s_tmem;
+  const int n_tiles = *s_nlist;
   bool dead = false;
 
   if (warp == 0) {
@@ -383,9 +417,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         tma_load_4d(smem + kOffQ + kQBytes, &p.tm_q, 0, qt * kBM, hB, b, q_full);
         tma_load_4d(smem + kOffQ + kQBytes + kQBytes / 2, &p.tm_q, 64, qt * kBM, hB, b, q_full);
       }
-      int j = 0;
-      for (int kt = 0; kt < kt_end; ++kt) {
-        if (!visit_tile(p, hA, hB, qt, kt, pl)) continue;
+      for (int j = 0; j < n_tiles; ++j) {
+        const int e = s_list[j];
+        const int kt = ((e >> 16) * p.per + (e & 0xFFFF)) / kBN;
         const int st = j % kStages;
         if (!wait_or_abort(&kv_empty[st], (uint32_t)(((j / kStages) & 1) ^ 1), dead, p.err)) break;
         uint8_t* kbuf = smem + kOffKV + st * kStageBytes;
@@ -394,7 +428,6 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         tma_load_4d(kbuf + kKVHalf / 2, &p.tm_k, 64, kt * kBN, hk, b, &kv_full[st]);
         tma_load_4d(kbuf + kKVHalf, &p.tm_v, 0, kt * kBN, hk, b, &kv_full[st]);
         tma_load_4d(kbuf + kKVHalf + kKVHalf / 2, &p.tm_v, 64, kt * kBN, hk, b, &kv_full[st]);
-        ++j;
       }
     }
   } else if (warp == 1) {
@@ -422,8 +455,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         }
       };
       // tile sequence; S of tile j goes to S buffer j % 2 of each head
-      int n = 0;
-      for (int kt = 0; kt < kt_end; ++kt) n += visit_tile(p, hA, hB, qt, kt, pl) ? 1 : 0;
+      const int n = n_tiles;
       for (int t = 0; t < 2 && t < n && !dead; ++t) {
         if (!wait_or_abort(&kv_full[t], 0, dead, p.err)) break;
         tc_fence_after();
@@ -476,9 +508,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
     uint8_t* pbuf = smem + kOffP + head_slot * kPBytes;
     if (h >= 0) {
       SoftmaxState st{-INFINITY, 0.f};
-      int j = 0;
-      for (int kt = 0; kt < kt_end; ++kt) {
-        if (!visit_tile(p, hA, hB, qt, kt, pl)) continue;
+      const int qbr = q / p.per, qwr = q - qbr * p.per, quota = p.quota[h];
+      for (int j = 0; j < n_tiles; ++j) {
+        const int e = s_list[j];
+        const int kb = e >> 16, kw0 = e & 0xFFFF;
+        const int lim = tile_limit_fast(p, quota, q, qbr, qwr, kb, kw0, kb * p.per + kw0, pl);
         // warp-uniform decision: tcgen05.ld is a warp-collective
         const bool ok = __all_sync(
             0xffffffffu, wait_or_abort(&s_full[2 * head_slot + (j & 1)], (uint32_t)((j >> 1) & 1), dead, p.err));
@@ -487,12 +521,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
           break;
         }
         tc_fence_after();
-        softmax_tile(p, h, kt, q, pl, row, tmem_h + 64 * (j & 1), tmem_o, lane_base, pbuf, j,
-                     &o_done[head_slot], dead, st);
+        softmax_tile(p, lim, row, tmem_h + 64 * (j & 1), tmem_o, lane_base, pbuf, j, &o_done[head_slot], dead,
+                     st);
         asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // P visible to the tensor core
         tc_fence_before();
         mbar_arrive_one(&p_full[head_slot]);
-        ++j;
       }
       // epilogue
       const bool o_ok = __all_sync(0xffffffffu, wait_or_abort(o_full, 0, dead, p.err));
@@ -573,6 +606,7 @@ extern "C" int abkv_prefill_masked(const void* q, const int64_t* q_strides, cons
   if (B <= 0 || H <= 0 || Hkv <= 0 || S <= 0 || H % Hkv != 0 || !(scale > 0.f)) return ABKV_ERR_INVALID_ARG;
   if (head_dim != kD || H > kMaxHeads || B > 65535) return ABKV_ERR_UNSUPPORTED;
   if (C <= 0 || K_layout <= 0 || C % kBM || K_layout % kBM || S % (C + K_layout)) return ABKV_ERR_UNSUPPORTED;
+  if (S / kBN > kMaxKeyTiles || C + K_layout > 65535) return ABKV_ERR_UNSUPPORTED;
   if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) |
        reinterpret_cast<uintptr_t>(out)) & 15)
     return ABKV_ERR_INVALID_ARG;
