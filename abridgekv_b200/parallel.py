@@ -1,0 +1,43 @@
+"""Multi-GPU layouts of the compressed-cache decode (one process per GPU).
+
+* Sequence sharding (default): decode and compaction are independent per
+  sequence, so each rank owns whole sequences -- their pages, block tables and
+  compaction plans -- and runs the same kernels with no collective on the data
+  path.  ``shard_sequences`` gives a rank's contiguous share.
+* KV-head sharding (optional): each rank holds KV heads
+  [r*Hkv/W, (r+1)*Hkv/W) of every sequence and computes the matching query
+  heads; after each layer's attention one all-gather (NCCL over NVLink /
+  NVSwitch on GPUs, gloo on CPU) assembles the [B, Hq, D] head outputs.
+  Compaction is per rank with identical page tables everywhere.
+
+The reference serves on one GPU; its vLLM TP groups are compatible by design
+because every head of a layer has the same quota
+(scripts/compresslm_schedules.py:17-25).
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+
+def shard_sequences(num_seqs: int, world: int, rank: int) -> slice:
+    """Contiguous, balanced share of `num_seqs` sequences for `rank`."""
+    base, extra = divmod(num_seqs, world)
+    start = rank * base + min(rank, extra)
+    return slice(start, start + base + (1 if rank < extra else 0))
+
+
+def kv_head_shard(num_kv_heads: int, world: int, rank: int) -> slice:
+    if num_kv_heads % world:
+        raise ValueError(f"{num_kv_heads} KV heads do not split over {world} ranks")
+    per = num_kv_heads // world
+    return slice(rank * per, (rank + 1) * per)
+
+
+def gather_head_outputs(local: torch.Tensor, group=None) -> torch.Tensor:
+    """[B, Hq/W, D] per rank -> [B, Hq, D] on every rank (heads in rank order)."""
+    world = dist.get_world_size(group)
+    B, hl, D = local.shape
+    out = torch.empty((world * B, hl, D), dtype=local.dtype, device=local.device)
+    dist.all_gather_into_tensor(out, local.contiguous(), group=group)
+    return out.view(world, B, hl, D).permute(1, 0, 2, 3).reshape(B, world * hl, D)

@@ -64,8 +64,8 @@ class ClockSampler:
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
+    def __init__(self, gpu: int | str):
+        self.gpu = gpu  # nvidia-smi --id accepts an index or a GPU-<uuid>
         self.proc = None
         self.lines: list[str] = []
         self._t = None
@@ -253,7 +253,8 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     torch.cuda.synchronize()
     assert ws.read_error() == 0, "device error word set during warm-up"
 
-    sampler = ClockSampler(local)
+    uuid = str(getattr(torch.cuda.get_device_properties(dev), "uuid", "") or "")
+    sampler = ClockSampler(("GPU-" + uuid) if uuid and not uuid.startswith("GPU-") else (uuid or local))
     sampler.start()
     time.sleep(0.3)
     barrier(world)
