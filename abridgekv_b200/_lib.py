@@ -16,6 +16,7 @@ _lib: C.CDLL | None = None
 c_int = C.c_int
 c_i32p = C.POINTER(C.c_int32)
 c_i64p = C.POINTER(C.c_int64)
+c_i64 = C.c_int64
 c_vp = C.c_void_p
 c_vpp = C.POINTER(C.c_void_p)
 c_size = C.c_size_t
@@ -63,6 +64,9 @@ SIGNATURES: dict[str, tuple] = {
     "abkv_prefill_masked": (c_int, [c_vp, c_i64p, c_vp, c_i64p, c_vp, c_i64p, c_vp, c_i64p, c_vp, c_i32p, c_vp,
                                     c_int, c_int, c_int, c_int, c_int, c_int, c_int, C.c_float, c_vp, c_size,
                                     c_vp]),
+    "abkv_code_step_attention": (c_int, [c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_vp, c_int, c_i64, c_int,
+                                         c_vp, c_i64, c_vp, c_vp, c_i32p, c_int, c_int, c_int, c_int, c_int,
+                                         c_int, C.c_float, c_vp, c_size, c_vp]),
 }
 
 

@@ -2,6 +2,7 @@
 
     python -m abridgekv_b200.benchmarks prefill   [--layers 36] [--steps 3] [--flex]
     python -m abridgekv_b200.benchmarks compaction [--steps 5]
+    python -m abridgekv_b200.benchmarks codestep   [--layers 36] [--steps 3]
 
 prefill    BASELINE config 4: B=16 sequences of 16 blocks x (512 content + 256 code rows)
            = 12,288 rows, Qwen3-4B attention (32 q / 8 kv heads, head_dim 128), per-layer
@@ -14,6 +15,11 @@ prefill    BASELINE config 4: B=16 sequences of 16 blocks x (512 content + 256 c
 compaction BASELINE config 4's block compaction for all 16 sequences and 36 layers
            (12 physical tensors shared by 3 quota groups): finish one block per sequence,
            execute the planned copy ops; algorithmic bytes = 2 x rows moved x 4 KiB per layer.
+codestep   the code step at a block boundary on BASELINE config 2's caches: 64 requests,
+           36 layers with per-layer quotas, each request's cache = its config-2 rows + the
+           K=256 freshly written code rows; 256 code queries per request (32 q / 8 kv heads,
+           head_dim 128).  One step = all layers (one abkv_code_step_attention launch each).
+           Algorithmic FLOPs = 4 x head_dim x visible keys per query per head.
 """
 from __future__ import annotations
 
@@ -186,16 +192,61 @@ def bench_compaction(args) -> dict:
                          "frac": gbs / pk.get("hbm_gbs", 6650.0)}}
 
 
+def bench_codestep(args) -> dict:
+    from . import codestep
+    from .workloads import QWEN3_4B, build_decode_workload, config2_rows
+
+    K = 256
+    rows = {q: r + K for q, r in config2_rows(64, 0).items()}
+    quotas = SCHEDULE_PERLAYER_MEAN128[: args.layers]
+    wl = build_decode_workload("codestep", quotas, rows, num_q_heads=QWEN3_4B["num_q_heads"],
+                               num_kv_heads=QWEN3_4B["num_kv_heads"], head_dim=QWEN3_4B["head_dim"])
+    R, Hq, Hkv, D = wl.num_seqs, wl.num_q_heads, wl.num_kv_heads, wl.head_dim
+    dev = torch.device("cuda")
+    gen = torch.Generator(device=dev).manual_seed(1)
+    q = torch.randn((R * K, Hq, D), device=dev, generator=gen, dtype=torch.bfloat16)
+    out = torch.empty_like(q)
+    qs = (torch.arange(R + 1, device=dev) * K).to(torch.int32)
+    flops = sum(4.0 * D * K * Hq * float((wl.rows[l] - K + qq).sum()) for l, qq in enumerate(quotas))
+    kv_bytes = float(wl.rows.sum()) * Hkv * D * 2 * 2
+
+    def step():
+        for l, qq in enumerate(quotas):
+            codestep.code_step_attention(q, wl.kv_caches[l], wl.block_tables[l], wl.seq_lens[l], qs,
+                                         quota_per_kv_head=[qq] * Hkv, k_max=K, out=out)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    pk = _peaks()
+    tflops = flops / (ms / 1e3) / 1e12
+    return {"metric": "code-step attention TFLOP/s (config 2 caches + 256 code rows)", "value": tflops,
+            "unit": "TFLOP/s", "ms_per_step": ms, "layers": len(quotas), "algorithmic_tflop_per_step": flops / 1e12,
+            "kv_gb_per_step": kv_bytes / 1e9,
+            "roofline": {"bound": "tensor", "achieved": tflops, "peak": pk.get("bf16_tflops_sustained"),
+                         "peak_kind": "measured sustained cuBLAS bf16 (MEASURED_PEAKS.json)",
+                         "frac": tflops / pk.get("bf16_tflops_sustained", 1400.0)},
+            "config": {"requests": R, "K": K, "heads": f"{Hq}/{Hkv}", "page": wl.page,
+                       "mean_seq_len": float(wl.rows.mean())}}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("which", choices=["prefill", "compaction"])
+    ap.add_argument("which", choices=["prefill", "compaction", "codestep"])
     ap.add_argument("--layers", type=int, default=36)
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=2)
     ap.add_argument("--flex", action="store_true")
     ap.add_argument("--blocks", type=int, default=6)
     args = ap.parse_args()
-    fn = {"prefill": bench_prefill, "compaction": bench_compaction}[args.which]
+    fn = {"prefill": bench_prefill, "compaction": bench_compaction, "codestep": bench_codestep}[args.which]
     print(json.dumps(fn(args)), flush=True)
 
 

@@ -1,0 +1,108 @@
+"""Code step over the paged cache (host side).
+
+The code step runs the K code queries of every active request in one forward
+pass: they attend, non-causally, to the request's rows [0, seq_len) in the
+paged KV cache, where a KV head with quota q sees only the first q of the
+request's own K code slots (the last K rows), and an optional per-request
+"tail exclusion" range of rows is hidden as well.  This is the noncausal branch
+of PackedKVSidecar._attend_request_vectorized
+(third_party/vllm_overlay/vllm/v1/worker/compresslm_packed_kv.py:648-741),
+driven per request from override_attention (:329-420) with
+query_start_loc / seq_lens / block_table from the common attention metadata
+and ranges from set_code_excluded_ranges (:244-260).
+
+``code_step_attention`` runs all requests, all heads in one launch of
+``abkv_code_step_attention`` (tcgen05 tensor cores; libabkv.so).  There is no
+CPU path: a missing library or a non-CUDA tensor raises.
+"""
+from __future__ import annotations
+
+import math
+from typing import Mapping, Sequence
+
+import torch
+
+from . import _lib
+from .workspace import Workspace, default_workspace
+
+
+def _layout_of(kv: torch.Tensor, num_kv_heads: int) -> tuple[int, int, int]:
+    """-> (kv_layout, num_blocks, page) for a contiguous paged cache."""
+    if kv.dim() != 5 or not kv.is_contiguous():
+        raise ValueError("kv_cache must be a contiguous 5-D paged cache")
+    if kv.shape[1] == 2 and kv.shape[3] == num_kv_heads:
+        return 0, kv.shape[0], kv.shape[2]           # FlashInfer [nb, 2, page, Hkv, D]
+    if kv.shape[0] == 2 and kv.shape[3] == num_kv_heads:
+        return 1, kv.shape[1], kv.shape[2]           # FlashAttention [2, nb, page, Hkv, D]
+    raise ValueError(f"unrecognised paged KV layout {tuple(kv.shape)}")
+
+
+def code_step_attention(query: torch.Tensor, kv_cache: torch.Tensor, block_table: torch.Tensor,
+                        seq_lens: torch.Tensor, query_start_loc: torch.Tensor, *,
+                        quota_per_kv_head: Sequence[int], k_max: int, scale: float | None = None,
+                        excluded: torch.Tensor | None = None, num_requests: int | None = None,
+                        out: torch.Tensor | None = None, workspace: Workspace | None = None,
+                        stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """query [T, Hq, D] bf16 (last dim contiguous); kv_cache paged bf16 (either layout);
+    block_table [R, max_pages] int32; seq_lens [R] int32 (each >= k_max); query_start_loc
+    [>= R] int32 (request r's code queries are rows query_start_loc[r] .. + k_max - 1);
+    quota_per_kv_head: this layer's quotas (each in [0, k_max]); excluded: optional [R, 2]
+    int32 hidden row ranges (start == end = none).  Writes and returns out [T, Hq, D]."""
+    for name, t in (("query", query), ("kv_cache", kv_cache)):
+        if not isinstance(t, torch.Tensor) or not t.is_cuda or t.dtype != torch.bfloat16:
+            raise TypeError(f"{name} must be a bf16 CUDA tensor (libabkv has no CPU path)")
+    if query.dim() != 3 or query.stride(2) != 1:
+        raise ValueError("query must be [T, Hq, D] with a contiguous last dimension")
+    T, Hq, D = query.shape
+    Hkv = len(quota_per_kv_head)
+    if Hkv == 0 or Hq % Hkv:
+        raise ValueError("quota_per_kv_head must hold one quota per KV head dividing the query heads")
+    layout, nb, page = _layout_of(kv_cache, Hkv)
+    R = block_table.shape[0] if num_requests is None else int(num_requests)
+    dev = query.device
+
+    def i32(name, t, shape_ok):
+        if not isinstance(t, torch.Tensor) or not t.is_cuda or t.dtype != torch.int32:
+            raise TypeError(f"{name} must be an int32 CUDA tensor")
+        if not shape_ok(t):
+            raise ValueError(f"{name} has shape {tuple(t.shape)}")
+        return t.contiguous()
+
+    bt = i32("block_table", block_table, lambda t: t.dim() == 2 and t.shape[0] >= R)
+    if bt.stride(1) != 1:
+        raise ValueError("block_table rows must be contiguous")
+    sl = i32("seq_lens", seq_lens, lambda t: t.dim() == 1 and t.shape[0] >= R)
+    qs = i32("query_start_loc", query_start_loc, lambda t: t.dim() == 1 and t.shape[0] >= R)
+    ex = None
+    if excluded is not None:
+        ex = i32("excluded", excluded, lambda t: t.dim() == 2 and t.shape[0] >= R and t.shape[1] == 2)
+    if out is None:
+        out = torch.empty((T, Hq, D), dtype=torch.bfloat16, device=dev)
+    if tuple(out.shape) != (T, Hq, D) or out.dtype != torch.bfloat16 or out.stride(2) != 1:
+        raise ValueError("out must be a bf16 [T, Hq, D] tensor with a contiguous last dimension")
+    scale = 1.0 / math.sqrt(D) if scale is None else float(scale)
+    ws = workspace or default_workspace(dev)
+    s = torch.cuda.current_stream(dev) if stream is None else stream
+    with torch.cuda.device(dev):
+        st = _lib.lib().abkv_code_step_attention(
+            query.data_ptr(), query.stride(0), query.stride(1), out.data_ptr(), out.stride(0), out.stride(1),
+            qs.data_ptr(), kv_cache.data_ptr(), layout, nb, page, bt.data_ptr(), bt.stride(0), sl.data_ptr(),
+            ex.data_ptr() if ex is not None else None, _lib.i32_array(quota_per_kv_head), R, Hq, Hkv, D,
+            int(k_max), T, scale, ws.ptr(), ws.nbytes, s.cuda_stream)
+    _lib.check("abkv_code_step_attention", st)
+    return out
+
+
+def excluded_tensor(request_ids: Sequence[str], ranges: Mapping[str, tuple[int, int]] | None,
+                    device: torch.device | str) -> torch.Tensor | None:
+    """[R, 2] int32 exclusion ranges in active-request order from the mapping the reference's
+    set_code_excluded_ranges takes (compresslm_packed_kv.py:244-260): None when there is none.
+    A request missing from a non-empty mapping raises, as _code_excluded_range does."""
+    if not ranges:
+        return None
+    rows = []
+    for rid in request_ids:
+        if rid not in ranges:
+            raise RuntimeError(f"packed KV code step: request {rid} has no tail exclusion range")
+        rows.append(tuple(int(x) for x in ranges[rid]))
+    return torch.tensor(rows, dtype=torch.int32, device=device).reshape(len(rows), 2)

@@ -62,7 +62,7 @@ constexpr int kOffKV = 2 * kQBytes;
 constexpr int kOffP = kOffKV + kStages * kStageBytes;  // P_A, P_B
 constexpr int kOffBar = kOffP + 2 * kPBytes;
 constexpr int kOffList = kOffBar + 256;         // visited key tiles: (kb << 16) | kw0, per 64-key tile
-constexpr int kMaxKeyTiles = 512;               // S up to 512 x 64 = 32K rows
+constexpr int kMaxKeyTiles = 2048;              // keys up to 2048 x 64 = 128K rows
 constexpr int kSmemBytes = kOffList + 4 * kMaxKeyTiles + 16 + 1024;  // + slack for 1024-byte alignment
 // Lazy rescaling: a row keeps its reference maximum until a tile's maximum
 // exceeds it by more than this (log2 units), so P <= 2^8 and O is rescaled
@@ -79,6 +79,15 @@ struct alignas(64) PrefillParams {
   int quota[kMaxHeads];
   int B, H, Hkv, G, npairs, S, C, KL, per, n_qtiles;
   float scale_log2;
+  // code step (paged K/V): request r's K code queries are rows q_start[r] ..
+  // q_start[r] + Kc - 1 of q [T][H][D]; its keys are the first seq_lens[r]
+  // rows of the paged cache through block-table row r.
+  const int32_t* bt;
+  const int32_t* seq_lens;
+  const int32_t* q_start;
+  const int32_t* excl;  // optional [R][2]: rows [start, end) hidden from the code queries
+  int64_t bt_stride, num_blocks;
+  int page, Kc, T, fa_layout;
 };
 
 // 0 = empty, 1 = full, 2 = partial, for query tile qt / key tile kt of head h.
@@ -113,24 +122,8 @@ __device__ __forceinline__ int tile_class(const PrefillParams& p, int h, int qt,
 // Inside any tile the visible keys of one query row are a PREFIX of the tile's
 // columns: the causal diagonal of the own block (kv <= q), the raw-prompt
 // boundary of an earlier block (kb*C + kw < prompt_len) or the quota boundary
-// of a code tile (kw - C < quota).  Returns that prefix length in [0, kBN].
-__device__ __forceinline__ int tile_limit(const PrefillParams& p, int h, int kt, int q, int pl) {
-  const int k0 = kt * kBN;
-  const int qb = q / p.per, kb = k0 / p.per;
-  if (kb > qb) return 0;
-  const int qw = q - qb * p.per, kw0 = k0 - kb * p.per;
-  int lim;
-  if (kw0 < p.C) {
-    if (kb == qb) lim = (qw >= p.C) ? kBN : q - k0 + 1;
-    else lim = pl - (kb * p.C + kw0);
-  } else {
-    if (kb == qb && qw < p.C) return 0;
-    lim = p.quota[h] - (kw0 - p.C);
-  }
-  return lim < 0 ? 0 : (lim > kBN ? kBN : lim);
-}
-
-// Same limit from precomputed coordinates: the row's block qb and in-block
+// of a code tile (kw - C < quota).  tile_limit_fast returns that prefix length
+// in [0, kBN] from precomputed coordinates: the row's block qb and in-block
 // offset qw, the tile's block kb and in-block offset kw0 (k0 = key tile start).
 __device__ __forceinline__ int tile_limit_fast(const PrefillParams& p, int quota, int q, int qb, int qw, int kb,
                                                int kw0, int k0, int pl) {
@@ -267,23 +260,27 @@ struct SoftmaxState {
 // reads S, updates the reference maximum / row sum, waits until the previous
 // P.V of this head has completed (o_done), rescales O when needed and writes
 // P (bf16, 128B-swizzled K-major: 16-byte chunk index ^= row % 8).
-__device__ __forceinline__ void softmax_tile(const PrefillParams& p, int lim, int row, uint32_t tmem_s,
-                                             uint32_t tmem_o, uint32_t lane_base, uint8_t* pbuf, int j,
-                                             uint64_t* o_done, bool& dead, SoftmaxState& st) {
+// kHole: columns [hs, he) are hidden as well (the code step's tail exclusion).
+template <bool kHole>
+__device__ __forceinline__ void softmax_tile(const PrefillParams& p, int lim, int hs, int he, int row,
+                                             uint32_t tmem_s, uint32_t tmem_o, uint32_t lane_base, uint8_t* pbuf,
+                                             int j, uint64_t* o_done, bool& dead, SoftmaxState& st) {
   const float sl2 = p.scale_log2;  // lim: visible columns of this row are c < lim
   float t0[32], t1[32];
   tmem_ld32(tmem_s + lane_base, t0);
   tmem_ld32(tmem_s + lane_base + 32, t1);
   tmem_wait_ld();
+  auto vis = [&](int c) { return c < lim && (!kHole || c < hs || c >= he); };
+  const bool full = lim == kBN && (!kHole || he <= 0 || hs >= kBN);
   float mxa[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // independent chains
-  if (lim == kBN) {
+  if (full) {
 #pragma unroll
     for (int i = 0; i < 32; ++i) mxa[i & 3] = fmaxf(mxa[i & 3], fmaxf(t0[i], t1[i]));
   } else {
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
-      mxa[i & 3] = fmaxf(mxa[i & 3], i < lim ? t0[i] : -INFINITY);
-      mxa[i & 3] = fmaxf(mxa[i & 3], i + 32 < lim ? t1[i] : -INFINITY);
+      mxa[i & 3] = fmaxf(mxa[i & 3], vis(i) ? t0[i] : -INFINITY);
+      mxa[i & 3] = fmaxf(mxa[i & 3], vis(i + 32) ? t1[i] : -INFINITY);
     }
   }
   const float mx = fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3])) * sl2;
@@ -303,9 +300,9 @@ __device__ __forceinline__ void softmax_tile(const PrefillParams& p, int lim, in
         const int c = half * 32 + e8 * 8 + 2 * e;
         float p0 = fast_exp2(fmaf(t[e8 * 8 + 2 * e], sl2, -m_use));
         float p1 = fast_exp2(fmaf(t[e8 * 8 + 2 * e + 1], sl2, -m_use));
-        if (lim != kBN) {
-          p0 = c < lim ? p0 : 0.f;
-          p1 = c + 1 < lim ? p1 : 0.f;
+        if (!full) {
+          p0 = vis(c) ? p0 : 0.f;
+          p1 = vis(c + 1) ? p1 : 0.f;
         }
         rsa[e] += p0 + p1;
         w[half * 4 + e8][e] = pack_bf16x2(p0, p1);
@@ -342,7 +339,8 @@ __device__ __forceinline__ bool visit_tile(const PrefillParams& p, int hA, int h
   return tile_class(p, hA, qt, kt, pl) != 0 || (hB >= 0 && tile_class(p, hB, qt, kt, pl) != 0);
 }
 
-__global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_constant__ PrefillParams p) {
+template <bool kPaged>
+__device__ __forceinline__ void attn_body(const PrefillParams& p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kOffBar);
@@ -356,14 +354,48 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bar + 16);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qt = p.n_qtiles - 1 - (int)blockIdx.x;  // heaviest query tiles first
+  // dense: heaviest query tiles first; paged: query tile of the request's code rows
+  const int qt = kPaged ? (int)blockIdx.x : p.n_qtiles - 1 - (int)blockIdx.x;
   const int hk = blockIdx.y / p.npairs, hp = blockIdx.y % p.npairs;
   const int hA = hk * p.G + 2 * hp;
   const int hB = (2 * hp + 1 < p.G) ? hA + 1 : -1;  // odd group size: the last pair has one head
-  const int b = blockIdx.z;
-  const int pl = p.prompt_len ? __ldg(p.prompt_len + b) : 0;
-  const int qb = qt * kBM / p.per;
-  const int kt_end = (qb + 1) * p.per / kBN;  // key tiles beyond the query's block are never visible
+  const int b = blockIdx.z;                         // sequence (dense) or request (paged)
+  int pl = 0, kt_end = 0, seq_len = 0, leffA = 0, leffB = 0, hole_s = 0, hole_e = 0;
+  if constexpr (kPaged) {
+    // every thread reads the same values, so an early return is CTA-uniform and
+    // happens before any barrier, TMEM allocation or copy
+    const int q0 = __ldg(p.q_start + b);
+    if (q0 < 0 || (int64_t)q0 + p.Kc > p.T) {
+      if (threadIdx.x == 0) set_error(p.err, ABKV_DEVERR_RANGE);
+      return;
+    }
+    // trim identity: a head with quota q sees rows [0, seq_len - (Kc - q)) --
+    // its own code slots >= q are the last Kc - q rows of the request
+    int sl = __ldg(p.seq_lens + b);
+    const int64_t cap = min(p.bt_stride * (int64_t)p.page, (int64_t)kMaxKeyTiles * kBN);
+    if (sl < p.Kc || (int64_t)sl > cap) {
+      if (threadIdx.x == 0) set_error(p.err, ABKV_DEVERR_SEQ_OOB);
+      sl = sl < p.Kc ? p.Kc : (int)cap;
+    }
+    seq_len = sl;
+    if (p.excl) {
+      hole_s = __ldg(p.excl + 2 * b);
+      hole_e = __ldg(p.excl + 2 * b + 1);
+      if (hole_s == hole_e) {
+        hole_s = hole_e = 0;  // no exclusion for this request
+      } else if (!(0 <= hole_s && hole_s < hole_e && hole_e <= seq_len - p.Kc)) {
+        if (threadIdx.x == 0) set_error(p.err, ABKV_DEVERR_RANGE);
+        hole_s = hole_e = 0;
+      }
+    }
+    leffA = min(max(seq_len - (p.Kc - p.quota[hA]), 0), seq_len);
+    leffB = hB >= 0 ? min(max(seq_len - (p.Kc - p.quota[hB]), 0), seq_len) : 0;
+    kt_end = (max(leffA, leffB) + kBN - 1) / kBN;
+  } else {
+    pl = p.prompt_len ? __ldg(p.prompt_len + b) : 0;
+    const int qb = qt * kBM / p.per;
+    kt_end = (qb + 1) * p.per / kBN;  // key tiles beyond the query's block are never visible
+  }
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -390,11 +422,13 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
     int n = 0;
     for (int base = 0; base < kt_end; base += 32) {
       const int kt = base + lane;
-      const bool vis = kt < kt_end && visit_tile(p, hA, hB, qt, kt, pl);
+      bool vis;
+      if constexpr (kPaged) vis = kt < kt_end && !(kt * kBN >= hole_s && kt * kBN + kBN <= hole_e);
+      else vis = kt < kt_end && visit_tile(p, hA, hB, qt, kt, pl);
       const uint32_t m = __ballot_sync(0xffffffffu, vis);
       if (vis) {
-        const int k0 = kt * kBN, kb = k0 / p.per;
-        s_list[n + __popc(m & ((1u << lane) - 1u))] = (kb << 16) | (k0 - kb * p.per);
+        const int k0 = kt * kBN, kb = kPaged ? 0 : k0 / p.per;
+        s_list[n + __popc(m & ((1u << lane) - 1u))] = kPaged ? kt : (kb << 16) | (k0 - kb * p.per);
       }
       n += __popc(m);
     }
@@ -411,12 +445,73 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
     // ---------------- TMA producer ----------------
     if (lane == 0) {
       mbar_expect_tx(q_full, (hB >= 0 ? 2 : 1) * kQBytes);
-      tma_load_4d(smem + kOffQ, &p.tm_q, 0, qt * kBM, hA, b, q_full);
-      tma_load_4d(smem + kOffQ + kQBytes / 2, &p.tm_q, 64, qt * kBM, hA, b, q_full);
-      if (hB >= 0) {
-        tma_load_4d(smem + kOffQ + kQBytes, &p.tm_q, 0, qt * kBM, hB, b, q_full);
-        tma_load_4d(smem + kOffQ + kQBytes + kQBytes / 2, &p.tm_q, 64, qt * kBM, hB, b, q_full);
+      if constexpr (kPaged) {
+        const int qrow = __ldg(p.q_start + b) + qt * kBM;
+        tma_load_4d(smem + kOffQ, &p.tm_q, 0, hA, qrow, 0, q_full);
+        tma_load_4d(smem + kOffQ + kQBytes / 2, &p.tm_q, 64, hA, qrow, 0, q_full);
+        if (hB >= 0) {
+          tma_load_4d(smem + kOffQ + kQBytes, &p.tm_q, 0, hB, qrow, 0, q_full);
+          tma_load_4d(smem + kOffQ + kQBytes + kQBytes / 2, &p.tm_q, 64, hB, qrow, 0, q_full);
+        }
+      } else {
+        tma_load_4d(smem + kOffQ, &p.tm_q, 0, qt * kBM, hA, b, q_full);
+        tma_load_4d(smem + kOffQ + kQBytes / 2, &p.tm_q, 64, qt * kBM, hA, b, q_full);
+        if (hB >= 0) {
+          tma_load_4d(smem + kOffQ + kQBytes, &p.tm_q, 0, qt * kBM, hB, b, q_full);
+          tma_load_4d(smem + kOffQ + kQBytes + kQBytes / 2, &p.tm_q, 64, qt * kBM, hB, b, q_full);
+        }
       }
+    }
+    if constexpr (kPaged) {
+      // The whole warp: lane i holds the page id of 16-row slice i % 4 of tile
+      // j0 + i / 4, so one coalesced block-table read covers 8 tiles and the
+      // next batch's read is in flight while this batch's copies are issued.
+      // Slices past seq_len (or with an invalid page id) are not loaded; their
+      // V rows are zero-filled by the softmax warps.
+      auto slice_page = [&](int j0) -> int {
+        const int j = j0 + (lane >> 2);
+        if (j >= n_tiles) return -1;
+        const int row0 = s_list[j] * kBN + 16 * (lane & 3);
+        if (row0 >= seq_len) return -1;
+        const int v = __ldg(p.bt + (int64_t)b * p.bt_stride + row0 / p.page);
+        if (v < 0 || (int64_t)v >= p.num_blocks) {
+          set_error(p.err, ABKV_DEVERR_PAGE_OOB);
+          return -1;
+        }
+        return v;
+      };
+      int cur = slice_page(0);
+      bool stop = false;
+      for (int j0 = 0; j0 < n_tiles && !stop; j0 += 8) {
+        const int nxt = slice_page(j0 + 8);
+        for (int jj = 0; jj < 8 && j0 + jj < n_tiles; ++jj) {
+          const int j = j0 + jj, st = j % kStages;
+          const int kt = s_list[j];
+          const int pg = __shfl_sync(0xffffffffu, cur, 4 * jj + (lane & 3));  // lanes 0..3: slices 0..3
+          const uint32_t valid = __ballot_sync(0xffffffffu, pg >= 0) & 0xFu;
+          bool ok = true;
+          if (lane == 0) {
+            ok = wait_or_abort(&kv_empty[st], (uint32_t)(((j / kStages) & 1) ^ 1), dead, p.err);
+            if (ok) mbar_expect_tx(&kv_full[st], (uint32_t)__popc(valid) * 4u * 2048u);
+          }
+          if (!__shfl_sync(0xffffffffu, ok, 0)) {
+            stop = true;
+            break;
+          }
+          if (lane < 4 && pg >= 0) {
+            uint8_t* kbuf = smem + kOffKV + st * kStageBytes + lane * 2048;
+            const int off = (kt * kBN + 16 * lane) % p.page;
+            const int pk = p.fa_layout ? pg : 2 * pg;
+            const int pv = p.fa_layout ? pg + (int)p.num_blocks : 2 * pg + 1;
+            tma_load_4d(kbuf, &p.tm_k, 0, hk, off, pk, &kv_full[st]);
+            tma_load_4d(kbuf + kKVHalf / 2, &p.tm_k, 64, hk, off, pk, &kv_full[st]);
+            tma_load_4d(kbuf + kKVHalf, &p.tm_k, 0, hk, off, pv, &kv_full[st]);
+            tma_load_4d(kbuf + kKVHalf + kKVHalf / 2, &p.tm_k, 64, hk, off, pv, &kv_full[st]);
+          }
+        }
+        cur = nxt;
+      }
+    } else if (lane == 0) {
       for (int j = 0; j < n_tiles; ++j) {
         const int e = s_list[j];
         const int kt = ((e >> 16) * p.per + (e & 0xFFFF)) / kBN;
@@ -508,11 +603,17 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
     uint8_t* pbuf = smem + kOffP + head_slot * kPBytes;
     if (h >= 0) {
       SoftmaxState st{-INFINITY, 0.f};
-      const int qbr = q / p.per, qwr = q - qbr * p.per, quota = p.quota[h];
+      const int qbr = kPaged ? 0 : q / p.per, qwr = kPaged ? 0 : q - qbr * p.per, quota = p.quota[h];
+      const int leff = head_slot ? leffB : leffA;
       for (int j = 0; j < n_tiles; ++j) {
         const int e = s_list[j];
-        const int kb = e >> 16, kw0 = e & 0xFFFF;
-        const int lim = tile_limit_fast(p, quota, q, qbr, qwr, kb, kw0, kb * p.per + kw0, pl);
+        int lim;
+        if constexpr (kPaged) {
+          lim = min(max(leff - e * kBN, 0), kBN);
+        } else {
+          const int kb = e >> 16, kw0 = e & 0xFFFF;
+          lim = tile_limit_fast(p, quota, q, qbr, qwr, kb, kw0, kb * p.per + kw0, pl);
+        }
         // warp-uniform decision: tcgen05.ld is a warp-collective
         const bool ok = __all_sync(
             0xffffffffu, wait_or_abort(&s_full[2 * head_slot + (j & 1)], (uint32_t)((j >> 1) & 1), dead, p.err));
@@ -521,8 +622,28 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
           break;
         }
         tc_fence_after();
-        softmax_tile(p, lim, row, tmem_h + 64 * (j & 1), tmem_o, lane_base, pbuf, j, &o_done[head_slot], dead,
-                     st);
+        if (kPaged && head_slot == 0 && e * kBN + kBN > seq_len) {
+          // V rows at or past seq_len (stale page slots or unloaded slices) become
+          // zeros before either head's P.V reads them (P is 0 there, but 0 * NaN
+          // would not be)
+          const int first = max(seq_len - e * kBN, 0);
+          uint8_t* vb = smem + kOffKV + (j % kStages) * kStageBytes + kKVHalf;
+          const int wt = (warp - 2) * 32 + lane;
+          for (int idx = wt; idx < 2 * (kBN - first) * 8; idx += 128) {
+            const int dh = idx / ((kBN - first) * 8), rem = idx - dh * (kBN - first) * 8;
+            *reinterpret_cast<uint4*>(vb + dh * (kKVHalf / 2) + (first + rem / 8) * 128 + (rem & 7) * 16) =
+                make_uint4(0, 0, 0, 0);
+          }
+          // each thread's zeros precede its own P writes, proxy fence and p_full
+          // arrival, and both heads' P.V wait for head A's p_full
+        }
+        if constexpr (kPaged) {
+          softmax_tile<true>(p, lim, hole_s - e * kBN, hole_e - e * kBN, row, tmem_h + 64 * (j & 1), tmem_o,
+                             lane_base, pbuf, j, &o_done[head_slot], dead, st);
+        } else {
+          softmax_tile<false>(p, lim, 0, 0, row, tmem_h + 64 * (j & 1), tmem_o, lane_base, pbuf, j,
+                              &o_done[head_slot], dead, st);
+        }
         asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // P visible to the tensor core
         tc_fence_before();
         mbar_arrive_one(&p_full[head_slot]);
@@ -531,13 +652,22 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
       const bool o_ok = __all_sync(0xffffffffu, wait_or_abort(o_full, 0, dead, p.err));
       tc_fence_after();
       if (o_ok) {
-        const float inv = st.l_run > 0.f ? 1.f / st.l_run : 0.f;
-        __nv_bfloat16* orow = p.out + (int64_t)b * p.o_sb + (int64_t)h * p.o_sh + (int64_t)q * p.o_ss;
+        // a row that saw no visible key (possible in the code step when the
+        // quota and the exclusion hide everything) is written as zeros
+        const bool none = !(st.l_run > 0.f);
+        const float inv = none ? 0.f : 1.f / st.l_run;
+        __nv_bfloat16* orow =
+            kPaged ? p.out + (int64_t)(__ldg(p.q_start + b) + q) * p.o_ss + (int64_t)h * p.o_sh
+                   : p.out + (int64_t)b * p.o_sb + (int64_t)h * p.o_sh + (int64_t)q * p.o_ss;
 #pragma unroll 1
         for (int c4 = 0; c4 < 4; ++c4) {
           float t[32];
           tmem_ld32(tmem_o + lane_base + c4 * 32, t);
           tmem_wait_ld();
+          if (none) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) t[i] = 0.f;
+          }
 #pragma unroll
           for (int v8 = 0; v8 < 4; ++v8) {
             uint4 pk;
@@ -548,7 +678,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
             *reinterpret_cast<uint4*>(orow + c4 * 32 + v8 * 8) = pk;
           }
         }
-        if (p.lse) {
+        if (!kPaged && p.lse) {
           const float lse2 = st.l_run > 0.f ? st.m_run + log2f(st.l_run) : -INFINITY;
           p.lse[((int64_t)b * p.H + h) * p.S + q] = lse2 * 0.6931471805599453f;  // natural log
         }
@@ -561,6 +691,14 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
   if (warp == 1) {
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(kTmemCols));
   }
+}
+
+__global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_constant__ PrefillParams p) {
+  attn_body<false>(p);
+}
+
+__global__ void __launch_bounds__(kThreads, 1) codestep_kernel(const __grid_constant__ PrefillParams p) {
+  attn_body<true>(p);
 }
 
 // ---------------------------------------------------------------------------
@@ -648,6 +786,109 @@ extern "C" int abkv_prefill_masked(const void* q, const int64_t* q_strides, cons
   if (Hkv * prm.npairs > 65535) return ABKV_ERR_UNSUPPORTED;
   dim3 grid(prm.n_qtiles, Hkv * prm.npairs, B);
   prefill_kernel<<<grid, kThreads, kSmemBytes, reinterpret_cast<cudaStream_t>(stream)>>>(prm);
+  if (cudaGetLastError() != cudaSuccess) return ABKV_ERR_CUDA;
+  return ABKV_OK;
+}
+
+namespace abkv {
+namespace {
+// 4D tensor map over bf16 with byte strides gstr (dims 1..3), 128B swizzle.
+int make_map_raw(CUtensorMap* m, const void* base, const cuuint64_t (&dims)[4], const cuuint64_t (&gstr)[3],
+                 const cuuint32_t (&box)[4]) {
+  for (int i = 0; i < 3; ++i)
+    if (gstr[i] % 16 != 0 || gstr[i] == 0) return ABKV_ERR_INVALID_ARG;
+  const cuuint32_t es[4] = {1, 1, 1, 1};
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult qres;
+  if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &qres) != cudaSuccess ||
+      qres != cudaDriverEntryPointSuccess || !fn)
+    return ABKV_ERR_CUDA;
+  CUresult r = reinterpret_cast<EncodeTiled>(fn)(
+      m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, gstr, box, es,
+      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? ABKV_OK : ABKV_ERR_INVALID_ARG;
+}
+}  // namespace
+}  // namespace abkv
+
+extern "C" int abkv_code_step_attention(const void* q, int64_t q_row_stride, int64_t q_head_stride, void* out,
+                                        int64_t out_row_stride, int64_t out_head_stride, const int32_t* q_start,
+                                        const void* kv_cache, int kv_layout, int64_t num_blocks, int page_size,
+                                        const int32_t* block_table, int64_t bt_stride, const int32_t* seq_lens,
+                                        const int32_t* excluded, const int32_t* quota_per_kv_head, int R, int Hq,
+                                        int Hkv, int head_dim, int K_code, int T, float scale, void* workspace,
+                                        size_t workspace_bytes, void* stream) {
+  if (!q || !out || !q_start || !kv_cache || !block_table || !seq_lens || !quota_per_kv_head)
+    return ABKV_ERR_INVALID_ARG;
+  if (R <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv != 0 || T <= 0 || num_blocks <= 0 || bt_stride <= 0 ||
+      !(scale > 0.f) || (kv_layout != 0 && kv_layout != 1))
+    return ABKV_ERR_INVALID_ARG;
+  if (head_dim != kD || Hq > kMaxHeads || R > 65535 || K_code <= 0 || K_code % kBM || page_size <= 0 ||
+      page_size % 16 || 2 * num_blocks > INT32_MAX || K_code > T)
+    return ABKV_ERR_UNSUPPORTED;
+  if (q_row_stride <= 0 || q_head_stride <= 0 || out_row_stride % 8 || out_head_stride % 8 ||
+      out_row_stride <= 0 || out_head_stride <= 0)
+    return ABKV_ERR_INVALID_ARG;
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(kv_cache)) &
+      15)
+    return ABKV_ERR_INVALID_ARG;
+  if (!workspace || workspace_bytes < 256 || (reinterpret_cast<uintptr_t>(workspace) & 255))
+    return ABKV_ERR_WORKSPACE;
+  PrefillParams prm;
+  std::memset(&prm, 0, sizeof(prm));
+  {
+    const cuuint64_t dims[4] = {(cuuint64_t)kD, (cuuint64_t)Hq, (cuuint64_t)T, 1};
+    const cuuint64_t gstr[3] = {(cuuint64_t)q_head_stride * 2, (cuuint64_t)q_row_stride * 2,
+                                (cuuint64_t)q_row_stride * 2 * (cuuint64_t)T};
+    const cuuint32_t box[4] = {64, 1, (cuuint32_t)kBM, 1};
+    const int st = make_map_raw(&prm.tm_q, q, dims, gstr, box);
+    if (st != ABKV_OK) return st;
+  }
+  {
+    // K and V planes of the paged cache as one 4D tensor: (dim, kv head, page
+    // row, plane) with plane = 2 * block + {0, 1} (FlashInfer) or
+    // {0, num_blocks} + block (FlashAttention); both have the same strides
+    const cuuint64_t row = (cuuint64_t)Hkv * kD * 2;
+    const cuuint64_t dims[4] = {(cuuint64_t)kD, (cuuint64_t)Hkv, (cuuint64_t)page_size, (cuuint64_t)(2 * num_blocks)};
+    const cuuint64_t gstr[3] = {(cuuint64_t)kD * 2, row, row * (cuuint64_t)page_size};
+    const cuuint32_t box[4] = {64, 1, 16, 1};
+    const int st = make_map_raw(&prm.tm_k, kv_cache, dims, gstr, box);
+    if (st != ABKV_OK) return st;
+  }
+  prm.out = static_cast<__nv_bfloat16*>(out);
+  prm.o_sh = out_head_stride;
+  prm.o_ss = out_row_stride;
+  prm.err = static_cast<int32_t*>(workspace);
+  const int G = Hq / Hkv;
+  for (int h = 0; h < Hq; ++h) {
+    const int qq = quota_per_kv_head[h / G];
+    if (qq < 0 || qq > K_code) return ABKV_ERR_INVALID_ARG;
+    prm.quota[h] = qq;
+  }
+  prm.B = R;
+  prm.H = Hq;
+  prm.Hkv = Hkv;
+  prm.G = G;
+  prm.npairs = (G + 1) / 2;
+  prm.n_qtiles = K_code / kBM;
+  prm.scale_log2 = scale * 1.4426950408889634f;
+  prm.bt = block_table;
+  prm.seq_lens = seq_lens;
+  prm.q_start = q_start;
+  prm.excl = excluded;
+  prm.bt_stride = bt_stride;
+  prm.num_blocks = num_blocks;
+  prm.page = page_size;
+  prm.Kc = K_code;
+  prm.T = T;
+  prm.fa_layout = kv_layout;
+  if (Hkv * prm.npairs > 65535) return ABKV_ERR_UNSUPPORTED;
+  if (cudaFuncSetAttribute(codestep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) !=
+      cudaSuccess)
+    return ABKV_ERR_CUDA;
+  dim3 grid(prm.n_qtiles, Hkv * prm.npairs, R);
+  codestep_kernel<<<grid, kThreads, kSmemBytes, reinterpret_cast<cudaStream_t>(stream)>>>(prm);
   if (cudaGetLastError() != cudaSuccess) return ABKV_ERR_CUDA;
   return ABKV_OK;
 }

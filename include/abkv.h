@@ -48,6 +48,7 @@ extern "C" {
 #define ABKV_DEVERR_SEQ_OOB 0x2
 #define ABKV_DEVERR_TIMEOUT 0x4
 #define ABKV_DEVERR_ROW_OOB 0x8
+#define ABKV_DEVERR_RANGE 0x10   /* code step: query rows or exclusion range invalid */
 
 /* Human-readable name of a status code (static string, never NULL). */
 const char* abkv_status_string(int status);
@@ -281,6 +282,43 @@ int abkv_prefill_masked(const void* q, const int64_t* q_strides, const void* k,
                         int B, int H, int Hkv, int S, int head_dim, int C,
                         int K_layout, float scale, void* workspace,
                         size_t workspace_bytes, void* stream);
+
+/* ========================================================================
+ * 5. Code step: K_code code queries per request over the paged cache (tcgen05).
+ *
+ * Replaces the noncausal branch of PackedKVSidecar._attend_request_vectorized
+ * (third_party/vllm_overlay/vllm/v1/worker/compresslm_packed_kv.py:648-741),
+ * reached from override_attention (:329-420) when the step holds the K_code
+ * code rows of each active request: request r's queries are rows
+ * q_start[r] .. q_start[r] + K_code - 1 of q (query_start_loc); its keys are
+ * rows [0, seq_lens[r]) gathered through block-table row r; a KV head with
+ * quota q sees rows [0, seq_lens[r] - K_code + q) (:711-720), minus the
+ * optional per-request exclusion range [excluded[2r], excluded[2r+1])
+ * (:721-726; start == end = none).  Scores, softmax and P.V run on the
+ * tensor cores with fp32 accumulation and an online softmax.
+ *
+ * q: [T][Hq][head_dim] bf16 with element strides (q_row_stride,
+ * q_head_stride), last dim contiguous; out likewise.  kv_cache: FlashInfer
+ * (kv_layout 0, [num_blocks][2][page][Hkv][D]) or FlashAttention (1,
+ * [2][num_blocks][page][Hkv][D]).  block_table: DEVICE [R][bt_stride] int32;
+ * q_start, seq_lens: DEVICE [R] int32; excluded: DEVICE [R][2] int32 or NULL;
+ * quota_per_kv_head: HOST [Hkv] in [0, K_code].  Supported: head_dim 128,
+ * K_code a multiple of 128, page a multiple of 16, seq_lens[r] in
+ * [K_code, min(bt_stride * page, 131072)].  Invalid device-side values set
+ * ABKV_DEVERR_SEQ_OOB / PAGE_OOB / RANGE in the workspace error word (a request
+ * whose query rows fall outside [0, T) is skipped).
+ * ====================================================================== */
+int abkv_code_step_attention(const void* q, int64_t q_row_stride,
+                             int64_t q_head_stride, void* out,
+                             int64_t out_row_stride, int64_t out_head_stride,
+                             const int32_t* q_start, const void* kv_cache,
+                             int kv_layout, int64_t num_blocks, int page_size,
+                             const int32_t* block_table, int64_t bt_stride,
+                             const int32_t* seq_lens, const int32_t* excluded,
+                             const int32_t* quota_per_kv_head, int R, int Hq,
+                             int Hkv, int head_dim, int K_code, int T,
+                             float scale, void* workspace,
+                             size_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }

@@ -104,3 +104,31 @@ def sidecar_decode_torch(query, kv_cache, seq_lens, block_table, num_kv_heads: i
     weights = torch.softmax(scores, dim=-1, dtype=torch.float32).to(q.dtype)
     att = torch.einsum("rhgt,rhtd->rhgd", weights, value)
     return att.reshape(n, num_kv_heads * groups, D)
+
+
+def codestep_exact(qrows, kv, block_table, seq_lens, K, quota_per_kv_head, scale, page, excluded=None):
+    """Code-step attention in float64 (compresslm_packed_kv.py:708-733 noncausal branch, no
+    sidecar pages): the K code queries of request r (rows r*K .. r*K+K-1 of qrows, [T, Hq, D])
+    attend to physical rows [0, seq_len) of its block-table row, own code slots >= the head's
+    quota hidden (rows >= seq_len - K + quota), and rows [excluded[r][0], excluded[r][1])
+    hidden when ``excluded`` is given (:721-726, _code_excluded_range :249-260).
+    Returns [T, Hq, D]."""
+    T, Hq, D = qrows.shape
+    Hkv = kv.shape[3]
+    G = Hq // Hkv
+    out = np.zeros((T, Hq, D))
+    for r, s_len in enumerate(seq_lens):
+        s_len = int(s_len)
+        k, v = _gather(kv, block_table[r], s_len, page)
+        prefix = s_len - K
+        for h in range(Hq):
+            limit = prefix + int(quota_per_kv_head[h // G])
+            keep = np.arange(limit)
+            if excluded is not None and excluded[r][1] > excluded[r][0]:
+                keep = keep[(keep < excluded[r][0]) | (keep >= excluded[r][1])]
+            kh = k[keep, h // G, :].astype(np.float64)
+            vh = v[keep, h // G, :].astype(np.float64)
+            s = (qrows[r * K:(r + 1) * K, h].astype(np.float64) @ kh.T) * scale
+            e = np.exp(s - s.max(axis=1, keepdims=True))
+            out[r * K:(r + 1) * K, h] = (e / e.sum(axis=1, keepdims=True)) @ vh
+    return out

@@ -39,3 +39,22 @@ def load_prefill(name: str):
     pl = z["prompt_len"] if z["prompt_len"].size else None
     return dict(B=B, H=H, Hkv=Hkv, S0=S0, C=int(z["C"]), K=int(z["K"]), quota=z["quota_per_head"], prompt_len=pl,
                 q=q, k=k, v=v, mask=mask, rows=z["rows"], out_rows=z["out_rows"], lse=z["lse"])
+
+
+def codestep_cases():
+    return sorted(p.stem[len("codestep_"):] for p in GOLDEN.glob("codestep_*.npz"))
+
+
+def load_codestep(name: str):
+    """-> (case, qrows [T,Hq,D], K, quotas per kv head, reference output [T,Hq,D],
+    exclusion ranges [R,2] or None)."""
+    from oracle.bf16 import round_bf16
+
+    z = np.load(GOLDEN / f"codestep_{name}.npz")
+    K = int(z["K"])
+    case = paged_case(int(z["seed"]), z["seq_lens"], num_q_heads=int(z["num_q_heads"]),
+                      num_kv_heads=int(z["num_kv_heads"]), head_dim=128, page=int(z["page"]))
+    rng = np.random.default_rng(int(z["seed"]) + 1000)
+    qrows = round_bf16(rng.standard_normal((len(z["seq_lens"]) * K, int(z["num_q_heads"]), 128)).astype(np.float32))
+    excl = z["excluded"] if "excluded" in z.files and len(z["excluded"]) else None
+    return case, qrows, K, z["quotas"], from_bits(z["out_bits"]), excl

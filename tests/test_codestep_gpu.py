@@ -1,0 +1,183 @@
+"""Code-step attention (tcgen05, paged K/V) through the C ABI on a B200.
+
+Tolerances (bf16 outputs; scores in fp32, P rounded to bf16 for the P.V MMA):
+|gpu - float64 oracle| <= 2.5e-2 max and 2e-3 mean; |gpu - reference| <= 3e-2
+(the reference rounds scores and weights to bf16).
+"""
+import numpy as np
+import pytest
+import torch
+
+from abridgekv_b200 import codestep
+from abridgekv_b200._lib import AbkvError
+from abridgekv_b200.workspace import Workspace
+from oracle.decode_ref import codestep_exact
+from tests.goldens import codestep_cases, load_codestep
+
+pytestmark = pytest.mark.gpu
+ATOL_EXACT, MEAN_EXACT, ATOL_REF = 2.5e-2, 2e-3, 3e-2
+
+
+def _inputs(name):
+    case, qrows, K, quotas, ref, excl = load_codestep(name)
+    R = len(case.seq_lens)
+    dev = dict(device="cuda")
+    q = torch.from_numpy(qrows).to(torch.bfloat16).cuda()
+    kv = torch.from_numpy(case.kv).to(torch.bfloat16).cuda()
+    bt = torch.from_numpy(case.block_table).cuda()
+    sl = torch.from_numpy(case.seq_lens).cuda()
+    qs = torch.arange(R + 1, dtype=torch.int32, **dev) * K
+    ex = torch.from_numpy(excl).cuda() if excl is not None else None
+    return case, qrows, K, quotas, ref, excl, q, kv, bt, sl, qs, ex
+
+
+@pytest.mark.parametrize("name", codestep_cases())
+def test_codestep_matches_reference_golden(name):
+    case, qrows, K, quotas, ref, excl, q, kv, bt, sl, qs, ex = _inputs(name)
+    ws = Workspace()
+    out = codestep.code_step_attention(q, kv, bt, sl, qs, quota_per_kv_head=[int(x) for x in quotas], k_max=K,
+                                       scale=case.scale, excluded=ex, workspace=ws)
+    torch.cuda.synchronize()
+    assert ws.read_error() == 0
+    got = out.float().cpu().numpy()
+    assert np.isfinite(got).all()
+    exact = codestep_exact(qrows, case.kv, case.block_table, case.seq_lens, K, quotas, case.scale, case.page, excl)
+    e = np.abs(got - exact)
+    print(f"{name}: max|gpu-f64|={e.max():.3e} mean={e.mean():.3e} max|gpu-ref|={np.abs(got - ref).max():.3e}")
+    assert e.max() <= ATOL_EXACT and e.mean() <= MEAN_EXACT
+    assert np.abs(got - ref).max() <= ATOL_REF
+
+
+def test_codestep_flashattention_layout_and_strided_query_equal():
+    """[2, nb, page, Hkv, D] caches and query views with a padded row stride give the same bits."""
+    case, qrows, K, quotas, ref, excl, q, kv, bt, sl, qs, ex = _inputs("k128_excl_g3")
+    quot = [int(x) for x in quotas]
+    a = codestep.code_step_attention(q, kv, bt, sl, qs, quota_per_kv_head=quot, k_max=K, scale=case.scale,
+                                     excluded=ex)
+    kv_fa = kv.transpose(0, 1).contiguous()
+    T, Hq, D = q.shape
+    wide = torch.zeros((T, Hq + 3, D), dtype=torch.bfloat16, device="cuda")
+    wide[:, 1:Hq + 1] = q
+    out_wide = torch.full((T, Hq + 2, D), 7.0, dtype=torch.bfloat16, device="cuda")
+    b = codestep.code_step_attention(wide[:, 1:Hq + 1], kv_fa, bt, sl, qs, quota_per_kv_head=quot, k_max=K,
+                                     scale=case.scale, excluded=ex, out=out_wide[:, :Hq])
+    assert torch.equal(a, b)
+    assert torch.all(out_wide[:, Hq:] == 7.0)
+
+
+def test_codestep_query_start_loc_permuted_and_padded():
+    """Requests' code rows at arbitrary starts (out of order, with gaps): each lands at its rows,
+    rows of no request are left untouched."""
+    case, qrows, K, quotas, ref, excl, q, kv, bt, sl, qs, ex = _inputs("k128_q64")
+    R = len(case.seq_lens)
+    starts = [2 * K + 5, 0, K + 3][:R]
+    T = 3 * K + 9
+    qp = torch.zeros((T, q.shape[1], q.shape[2]), dtype=torch.bfloat16, device="cuda")
+    for r, s0 in enumerate(starts):
+        qp[s0:s0 + K] = q[r * K:(r + 1) * K]
+    out = torch.full_like(qp, -3.0)
+    quot = [int(x) for x in quotas]
+    codestep.code_step_attention(qp, kv, bt, sl, torch.tensor(starts, dtype=torch.int32, device="cuda"),
+                                 quota_per_kv_head=quot, k_max=K, scale=case.scale, out=out, num_requests=R)
+    base = codestep.code_step_attention(q, kv, bt, sl, qs, quota_per_kv_head=quot, k_max=K, scale=case.scale)
+    covered = torch.zeros(T, dtype=torch.bool, device="cuda")
+    for r, s0 in enumerate(starts):
+        assert torch.equal(out[s0:s0 + K], base[r * K:(r + 1) * K])
+        covered[s0:s0 + K] = True
+    assert torch.all(out[~covered] == -3.0)
+
+
+def test_codestep_device_errors_are_reported():
+    """seq_len below k_max, a page id outside the cache and an invalid exclusion range set the
+    workspace error bits (the kernel clamps / skips instead of reading out of bounds)."""
+    case, qrows, K, quotas, ref, excl, q, kv, bt, sl, qs, ex = _inputs("k128_q64")
+    quot = [int(x) for x in quotas]
+    ws = Workspace()
+    bad = sl.clone()
+    bad[0] = K - 1
+    codestep.code_step_attention(q, kv, bt, bad, qs, quota_per_kv_head=quot, k_max=K, workspace=ws)
+    assert ws.read_error() & 0x2
+    bt2 = bt.clone()
+    bt2[1, 0] = kv.shape[0] + 5
+    codestep.code_step_attention(q, kv, bt2, sl, qs, quota_per_kv_head=quot, k_max=K, workspace=ws)
+    assert ws.read_error() & 0x1
+    exb = torch.tensor([[0, 0], [10, 5], [0, 0]], dtype=torch.int32, device="cuda")
+    codestep.code_step_attention(q, kv, bt, sl, qs, quota_per_kv_head=quot, k_max=K, excluded=exb, workspace=ws)
+    assert ws.read_error() & 0x10
+    qs_bad = qs.clone()
+    qs_bad[2] = q.shape[0] - K + 1
+    codestep.code_step_attention(q, kv, bt, sl, qs_bad, quota_per_kv_head=quot, k_max=K, workspace=ws)
+    assert ws.read_error() & 0x10
+    torch.cuda.synchronize()
+
+
+def test_codestep_host_validation():
+    case, qrows, K, quotas, ref, excl, q, kv, bt, sl, qs, ex = _inputs("k128_q64")
+    with pytest.raises(AbkvError):
+        codestep.code_step_attention(q[:, :, :64].contiguous(), kv[..., :64].contiguous(), bt, sl, qs,
+                                     quota_per_kv_head=[64, 64], k_max=K)
+    with pytest.raises(AbkvError):
+        codestep.code_step_attention(q, kv, bt, sl, qs, quota_per_kv_head=[K + 1, 0], k_max=K)
+    with pytest.raises(AbkvError):
+        codestep.code_step_attention(q, kv, bt, sl, qs, quota_per_kv_head=[64, 64], k_max=96)
+
+
+def test_codestep_qwen_scale_sampled_requests():
+    """Qwen3-4B code step at serving scale (64 requests, seq 3-5K, K=256, 32/8 heads, quotas
+    256/128/64): sampled requests against a PyTorch fp32 reference on the GPU."""
+    torch.manual_seed(3)
+    R, K, Hq, Hkv, D, page = 64, 256, 32, 8, 128, 16
+    quotas = [256, 128, 64, 128, 256, 64, 128, 128]
+    lens = torch.randint(3000, 5000, (R,)) + K
+    pages = (lens + page - 1) // page
+    nb = int(pages.sum()) + 1
+    kv = torch.randn((nb, 2, page, Hkv, D), device="cuda", dtype=torch.bfloat16)
+    perm = torch.randperm(nb - 1) + 1
+    maxp = int(pages.max())
+    bt = torch.zeros((R, maxp), dtype=torch.int32)
+    off = 0
+    for r in range(R):
+        bt[r, :pages[r]] = perm[off:off + pages[r]]
+        off += int(pages[r])
+    bt, sl = bt.cuda(), lens.to(torch.int32).cuda()
+    q = torch.randn((R * K, Hq, D), device="cuda", dtype=torch.bfloat16)
+    qs = (torch.arange(R + 1) * K).to(torch.int32).cuda()
+    ws = Workspace()
+    out = codestep.code_step_attention(q, kv, bt, sl, qs, quota_per_kv_head=quotas, k_max=K, workspace=ws)
+    torch.cuda.synchronize()
+    assert ws.read_error() == 0
+    G = Hq // Hkv
+    for r in (0, 17, 63):
+        L = int(lens[r])
+        rows = torch.arange(L, device="cuda")
+        blk = bt[r].long()[rows // page]
+        k = kv[blk, 0, rows % page].float()     # [L, Hkv, D]
+        v = kv[blk, 1, rows % page].float()
+        qq = q[r * K:(r + 1) * K].float()
+        for h in range(Hq):
+            lim = L - K + quotas[h // G]
+            s = (qq[:, h] @ k[:lim, h // G].T) / D ** 0.5
+            ref = torch.softmax(s, dim=-1) @ v[:lim, h // G]
+            err = (out[r * K:(r + 1) * K, h].float() - ref).abs()
+            assert err.max().item() <= ATOL_EXACT and err.mean().item() <= MEAN_EXACT
+
+
+def test_codestep_rows_with_no_visible_key_are_zero():
+    """quota 0 with the whole prefix excluded leaves a head nothing to attend to: zeros, no error
+    (the reference's softmax over an all -inf row would give NaN)."""
+    K, Hq, Hkv, D, page = 128, 4, 2, 128, 16
+    L = K + 64
+    kv = torch.randn((L // page + 1, 2, page, Hkv, D), device="cuda", dtype=torch.bfloat16)
+    bt = torch.arange(1, L // page + 1, dtype=torch.int32, device="cuda").view(1, -1)
+    sl = torch.tensor([L], dtype=torch.int32, device="cuda")
+    q = torch.randn((K, Hq, D), device="cuda", dtype=torch.bfloat16)
+    qs = torch.tensor([0, K], dtype=torch.int32, device="cuda")
+    ex = torch.tensor([[0, 64]], dtype=torch.int32, device="cuda")
+    ws = Workspace()
+    out = codestep.code_step_attention(q, kv, bt, sl, qs, quota_per_kv_head=[0, 1], k_max=K, excluded=ex,
+                                       workspace=ws)
+    torch.cuda.synchronize()
+    assert ws.read_error() == 0
+    assert torch.all(out[:, :2] == 0)
+    ref = kv[bt[0].long()[64 // page], 1, 0, 1].float()   # heads 2, 3: only code slot 0 (row 64) visible
+    assert torch.allclose(out[:, 2:].float(), ref.expand(K, 2, D), atol=1e-2)

@@ -27,3 +27,17 @@ def test_reference_rounding_error_is_small(name):
     case, ref = load_decode(name)
     exact = decode_exact(case.q, case.kv, case.block_table, case.seq_lens, case.scale, case.page)
     assert np.abs(ref - exact).max() < 3e-2
+
+
+from oracle.decode_ref import codestep_exact  # noqa: E402
+from tests.goldens import codestep_cases, load_codestep  # noqa: E402
+
+
+@pytest.mark.parametrize("name", codestep_cases())
+def test_codestep_oracle_matches_reference(name):
+    case, qrows, K, quotas, ref, excl = load_codestep(name)
+    ex = codestep_exact(qrows, case.kv, case.block_table, case.seq_lens, K, quotas, case.scale, case.page, excl)
+    assert np.isfinite(ref).all()
+    # the reference rounds scores and weights to bf16; float64 stays within its error budget
+    assert np.abs(ex - ref).max() < 3e-2
+    assert np.abs(ex - ref).mean() < 2e-3
