@@ -47,7 +47,7 @@ constexpr int kWarps = 8;                  // consumer warps
 constexpr int kThreads = (kWarps + 1) * 32;  // + producer warp
 constexpr int kConsumerThreads = kWarps * 32;
 constexpr int kMaxLayers = 56;       // layers per launch: keeps params < 4 KB
-constexpr int kMaxChunkPages = 256;  // page ids staged per work item
+constexpr int kMaxChunkPages = 512;  // page ids staged per work item
 constexpr int kMaxG = 8;             // query heads per KV head
 constexpr int kStages = 3;
 constexpr int kStageBytes = kWarps * 2 * kTile * kD * 2;  // nsub * Hkv == kWarps -> 64 KiB
@@ -171,45 +171,47 @@ __device__ void producer(const DecodeParams& p, uint8_t* smem) {
     __syncwarp();
     const int ngroups = max(1, (ntiles + nsub - 1) / nsub);
     for (int grp = 0; grp < ngroups; ++grp, ++gq) {
+      // lane j < nt owns tile j of the group: its page lookup, bounds check and
+      // copies run in parallel across the lanes (one tile's latency per group)
+      const int st = gq % kStages;
+      const int tg0 = tile0 + grp * nsub;
+      const int nt = max(0, min(nsub, tile1 - tg0));
+      int64_t pg = -1;
+      if (lane < nt) {
+        const int t = tg0 + lane;
+        pg = s_pages[(P == kTile ? t : t * kTile / P) - page0];
+        if (pg < 0 || pg >= L.num_blocks) {
+          set_error(p.err, ABKV_DEVERR_PAGE_OOB);
+          pg = -1;
+        }
+      }
+      const uint32_t okmask = __ballot_sync(0xffffffffu, pg >= 0) & ((1u << nt) - 1u);
       if (lane == 0) {
-        const int st = gq % kStages;
         const uint32_t k = (uint32_t)(gq / kStages);
         if (!mbar_wait(&empty[st], (k & 1u) ^ 1u)) {
           set_error(p.err, ABKV_DEVERR_TIMEOUT);
           alive = false;
         }
-        int okmask = 0;
-        uint32_t bytes = 0;
-        const int tg0 = tile0 + grp * nsub;
-        const int nt = min(nsub, tile1 - tg0) > 0 ? min(nsub, tile1 - tg0) : 0;
-        for (int j = 0; j < nt; ++j) {
-          const int pg = s_pages[(tg0 + j) * kTile / P - page0];
-          if (pg >= 0 && (int64_t)pg < L.num_blocks) {
-            okmask |= 1 << j;
-            bytes += 2u * (uint32_t)tile_half;
-          } else {
-            set_error(p.err, ABKV_DEVERR_PAGE_OOB);
-          }
-        }
-        StageMeta m;
-        m.li = li; m.b = b; m.chunk = chunk; m.n_chunks = nch; m.seq_len = slen;
-        m.t0 = tg0; m.ntiles = nt;
-        m.bits = okmask | (grp == 0 ? kFirst : 0) | (grp == ngroups - 1 ? kLast : 0);
-        meta[st] = m;
-        mbar_expect_tx(&full[st], bytes);  // release: meta is visible once the phase completes
-        uint8_t* dst = smem + kOffStage + (size_t)st * kStageBytes;
-        for (int j = 0; j < nt; ++j) {
-          if (!((okmask >> j) & 1)) continue;
-          const int t = tg0 + j;
-          const int64_t pg = s_pages[t * kTile / P - page0];
-          const __nv_bfloat16* ksrc = L.kv + pg * page_elems + (int64_t)((t * kTile) % P) * row_elems;
-          bulk_g2s(dst + (size_t)j * 2 * tile_half, ksrc, (uint32_t)tile_half, &full[st]);
-          bulk_g2s(dst + (size_t)j * 2 * tile_half + tile_half, ksrc + half_elems, (uint32_t)tile_half,
-                   &full[st]);
-        }
       }
       alive = __shfl_sync(0xffffffffu, alive ? 1 : 0, 0) != 0;
       if (!alive) break;
+      if (lane == 0) {
+        StageMeta m;
+        m.li = li; m.b = b; m.chunk = chunk; m.n_chunks = nch; m.seq_len = slen;
+        m.t0 = tg0; m.ntiles = nt;
+        m.bits = (int)okmask | (grp == 0 ? kFirst : 0) | (grp == ngroups - 1 ? kLast : 0);
+        meta[st] = m;
+        // release: meta is visible once the phase completes
+        mbar_expect_tx(&full[st], (uint32_t)__popc(okmask) * 2u * (uint32_t)tile_half);
+      }
+      __syncwarp();  // the expected byte count is posted before any copy can complete
+      if (pg >= 0) {
+        const int t = tg0 + lane;
+        uint8_t* dst = smem + kOffStage + (size_t)st * kStageBytes + (size_t)lane * 2 * tile_half;
+        const __nv_bfloat16* ksrc = L.kv + pg * page_elems + (int64_t)((t * kTile) % P) * row_elems;
+        bulk_g2s(dst, ksrc, (uint32_t)tile_half, &full[st]);
+        bulk_g2s(dst + tile_half, ksrc + half_elems, (uint32_t)tile_half, &full[st]);
+      }
     }
     __syncwarp();  // s_pages is rewritten for the next item only after this one is issued
   }

@@ -346,6 +346,126 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_scaling(args, rank: int, world: int, local: int) -> None:
+    """BASELINE configs 3 and 5 (strong scaling: the global batch is fixed).
+
+    config 3: 512 sequences with generated lengths log-uniform in [2K, 32K]
+      (247.8 GB of K/V), sequence-sharded; a rank whose share exceeds
+      --mem-budget-gb decodes it in waves (each wave's caches are built, timed
+      and freed in turn) and one step = one decode step of every wave.
+    config 5: 256 sequences, quota 128 in every layer, 63 compressed blocks +
+      tail (323.7 GB).  --shard seq: whole sequences per rank, one 36-layer
+      launch per step.  --shard kv: every rank holds KV heads
+      [r*8/W, (r+1)*8/W) of all sequences; per layer one decode launch of its
+      heads, then an NCCL all-gather of the [B, 32/W, 128] head outputs."""
+    from abridgekv_b200 import decode, parallel
+    from abridgekv_b200.workloads import QWEN3_4B, config3_rows, config5_rows, qwen3_decode_workload
+    from abridgekv_b200.workspace import Workspace
+
+    dev = torch.device("cuda", local)
+    cfg = args.config
+    n_global = args.num_seqs if args.num_seqs != 64 else (512 if cfg == 3 else 256)
+    rows_all = (config3_rows if cfg == 3 else config5_rows)(n_global, 0)
+    hkv, hd = QWEN3_4B["num_kv_heads"], QWEN3_4B["head_dim"]
+    kv_mode = cfg == 5 and args.shard == "kv"
+    heads = parallel.kv_head_shard(hkv, world, rank) if kv_mode else None
+    seqs = slice(0, n_global) if kv_mode else parallel.shard_sequences(n_global, world, rank)
+    sched = (128,) * 36 if cfg == 5 else None
+    from abridgekv_b200.workloads import SCHEDULE_PERLAYER_MEAN128
+    quotas = sched or SCHEDULE_PERLAYER_MEAN128
+    h_local = hkv // world if kv_mode else hkv
+    per_seq = np.zeros(n_global)
+    for q in quotas:
+        per_seq += rows_all[q] * h_local * hd * 4
+    mine = np.arange(n_global)[seqs]
+    budget = args.mem_budget_gb * 1e9
+    waves, cur, acc = [], [], 0.0
+    for i in mine:
+        if cur and acc + per_seq[i] > budget:
+            waves.append(cur)
+            cur, acc = [], 0.0
+        cur.append(int(i))
+        acc += per_seq[i]
+    if cur:
+        waves.append(cur)
+    if kv_mode and len(waves) > 1:
+        raise SystemExit(f"config 5 KV-head sharding needs {per_seq.sum() / 1e9:.1f} GB per rank "
+                         f"(> --mem-budget-gb {args.mem_budget_gb}); use more GPUs")
+    ws = Workspace(dev)
+    stream = torch.cuda.current_stream(dev)
+    wave_ms, alg_bytes, launches, waves_info = [], 0, 0, []
+    for wi, idx in enumerate(waves):
+        sl = slice(idx[0], idx[-1] + 1)
+        assert idx == list(range(sl.start, sl.stop))
+        wl = qwen3_decode_workload(cfg, num_seqs=n_global, device=dev, seed=0, seq_slice=sl, kv_heads=heads)
+        outs = [torch.empty_like(q) for q in wl.queries]
+        gathered = [None] * wl.num_layers
+
+        if kv_mode:
+            def step():
+                for l in range(wl.num_layers):
+                    decode.paged_decode([wl.queries[l]], [wl.kv_caches[l]], [wl.block_tables[l]],
+                                        [wl.seq_lens[l]], outputs=[outs[l]], max_pages_per_seq=wl.max_pages,
+                                        chunk_tokens=args.chunk_tokens, workspace=ws)
+                    gathered[l] = parallel.gather_head_outputs(outs[l])
+            per_step = wl.num_layers
+        else:
+            def step():
+                decode.paged_decode(wl.queries, wl.kv_caches, wl.block_tables, wl.seq_lens, outputs=outs,
+                                    max_pages_per_seq=wl.max_pages, chunk_tokens=args.chunk_tokens,
+                                    workspace=ws)
+            per_step = (wl.num_layers + 55) // 56
+        for _ in range(max(args.warmup, 3)):
+            step()
+        torch.cuda.synchronize()
+        assert ws.read_error() == 0, "device error word set during warm-up"
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+        wave_ms.append(e0.elapsed_time(e1) / args.steps)
+        alg_bytes += wl.kv_bytes + wl.qo_bytes
+        launches += per_step * args.steps
+        waves_info.append({"seqs": len(idx), "kv_gb": wl.kv_bytes / 1e9, "ms_per_step": wave_ms[-1]})
+        del wl, outs, gathered
+        torch.cuda.empty_cache()
+    ms_step = sum(wave_ms)
+    ms_max = max_over_ranks(ms_step, world)
+    bytes_total = alg_bytes
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([float(alg_bytes)], dtype=torch.float64, device=dev)
+        dist.all_reduce(t)
+        bytes_total = float(t.item())
+    if rank != 0:
+        return
+    peak, peak_kind = measured_hbm_peak()
+    value = n_global / (ms_max / 1e3)
+    achieved = bytes_total / world / (ms_max / 1e3) / 1e9
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"config{cfg}: Qwen3-4B decode attention, {n_global} sequences, "
+                               + ("per-layer quotas 6x256/18x128/12x64, generated length log-uniform [2K,32K]"
+                                  if cfg == 3 else "quota 128 in all 36 layers, 63 compressed blocks + tail"),
+                   "global_batch": n_global,
+                   "parallelism": (f"KV-head-sharded x{world} + NCCL all-gather per layer" if kv_mode
+                                   else f"sequence-sharded x{world}, no collective"),
+                   "waves_rank0": waves_info, "mem_budget_gb": args.mem_budget_gb,
+                   "l2": "inputs larger than L2; no flush"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "note": "per-GPU mean: all ranks' algorithmic bytes / W / max time",
+                     "peak_source": peak_kind},
+        "gpu_launches": launches,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def _config2_rows_for_cpu():
     from abridgekv_b200.workloads import config2_rows
     return config2_rows(64, seed=0)
@@ -361,6 +481,11 @@ def main() -> None:
     ap.add_argument("--num-seqs", type=int, default=64, help="sequences per GPU (config 2 uses 64)")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--config", type=int, choices=[2, 3, 5], default=2,
+                    help="2 (default, headline): weak scaling; 3 / 5: strong-scaling saturation runs")
+    ap.add_argument("--shard", choices=["seq", "kv"], default="seq", help="config 5: sequence or KV-head sharding")
+    ap.add_argument("--mem-budget-gb", type=float, default=130.0,
+                    help="configs 3/5: K/V bytes one wave may hold per GPU")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -371,7 +496,10 @@ def main() -> None:
         return
     rank, world, local = dist_setup(args.gpus)
     try:
-        run_ours(args, rank, world, local)
+        if args.config == 2:
+            run_ours(args, rank, world, local)
+        else:
+            run_scaling(args, rank, world, local)
     finally:
         if world > 1:
             import torch.distributed as dist
