@@ -21,6 +21,17 @@ c_vp = C.c_void_p
 c_vpp = C.POINTER(C.c_void_p)
 c_size = C.c_size_t
 
+GATHER_FLAG_BYTES = 256   # ABKV_GATHER_FLAG_BYTES
+MAX_PEERS = 8             # ABKV_MAX_PEERS
+PEER_HANDLE_BYTES = 64    # ABKV_PEER_HANDLE_BYTES
+
+
+class GatherT(C.Structure):
+    """abkv_gather_t."""
+    _fields_ = [("rank_buffers", C.c_void_p * MAX_PEERS), ("buffer_bytes", C.c_size_t), ("world", C.c_int),
+                ("rank", C.c_int), ("hq_total", C.c_int), ("epoch", C.c_uint32), ("timeout_us", C.c_uint32)]
+
+
 # name -> (restype, argtypes); must mirror include/abkv.h exactly.
 SIGNATURES: dict[str, tuple] = {
     "abkv_status_string": (C.c_char_p, [c_int]),
@@ -37,6 +48,15 @@ SIGNATURES: dict[str, tuple] = {
         [c_vpp, c_vpp, c_vpp, c_i64p, c_vpp, c_i64p, c_vpp, c_int, c_int, c_int, c_int, c_int,
          c_int, c_int, C.c_float, c_int, c_vp, c_vp],
     ),
+    "abkv_decode_gather": (
+        c_int,
+        [c_vpp, c_vpp, c_vpp, c_i64p, c_vpp, c_i64p, c_vpp, c_int, c_int, c_int, c_int, c_int,
+         c_int, c_int, C.c_float, c_int, c_vp, c_vp, c_size, c_vp],
+    ),
+    "abkv_peer_alloc": (c_int, [c_size, c_vpp, c_vp]),
+    "abkv_peer_open": (c_int, [c_vp, c_vpp]),
+    "abkv_peer_close": (c_int, [c_vp]),
+    "abkv_peer_free": (c_int, [c_vp]),
     "abkv_planner_create": (c_vp, [c_int, c_int, c_int]),
     "abkv_planner_destroy": (None, [c_vp]),
     "abkv_planner_add_request": (c_int, [c_vp, C.c_int64]),

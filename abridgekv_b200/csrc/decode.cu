@@ -62,8 +62,27 @@ struct LayerArgs {
   int64_t num_blocks;
 };
 
+// Output placement.  Row (b, h) of a layer goes to out + b * out_row + (head0 + h) * D
+// in every rank's copy of the output buffer: world == 1 is the plain decode
+// ([B][Hq][D], head0 0); world > 1 is the KV-head-sharded decode whose epilogue
+// is also the all-gather -- each rank stores its heads straight into all ranks'
+// buffers (peer memory over NVLink), then the last CTA raises this rank's flag
+// in every peer's flag array and waits (bounded) until all peers' flags for
+// this epoch are up in its own.
+constexpr int kMaxPeers = 8;
+struct GatherArgs {
+  int64_t peer_delta[kMaxPeers];  // element offset from this rank's buffer to rank r's
+  uint32_t* peer_flags[kMaxPeers];
+  uint32_t* my_flags;
+  int64_t out_row;
+  uint64_t timeout_ns;
+  int world, rank, head0;
+  uint32_t epoch;
+};
+
 struct DecodeParams {
   LayerArgs layer[kMaxLayers];
+  GatherArgs gather;
   float* part_o;      // [layers][B][max_chunks][Hq][D]
   float* part_lse;    // [layers][B][max_chunks][Hq]
   int32_t* counters;  // [layers][B] chunks finished; zero between calls
@@ -118,6 +137,56 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 
 __device__ __forceinline__ void consumer_sync() {
   asm volatile("bar.sync 1, %0;\n" ::"n"(kConsumerThreads) : "memory");
+}
+
+__device__ __forceinline__ void store_out(const DecodeParams& p, const LayerArgs& L, int b, int hr, int d,
+                                          float val) {
+  const GatherArgs& g = p.gather;
+  __nv_bfloat16* dst = L.out + (int64_t)b * g.out_row + (int64_t)(g.head0 + hr) * kD + d;
+  const __nv_bfloat16 v = __float2bfloat16(val);
+  for (int r = 0; r < g.world; ++r) dst[g.peer_delta[r]] = v;
+}
+
+__device__ __forceinline__ void st_release_sys(uint32_t* ptr, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;\n" ::"l"(ptr), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* ptr) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];\n" : "=r"(v) : "l"(ptr) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t));
+  return t;
+}
+
+// End of a gathering launch: every CTA's output stores are fenced system-wide
+// before it is counted; the last CTA publishes this rank's epoch to all ranks
+// and waits for theirs.  The wait gives up after timeout_ns (or kPeerSpinLimit
+// polls, whichever comes first) and records ABKV_DEVERR_TIMEOUT, so a missing
+// peer cannot hang the GPU.
+constexpr uint32_t kPeerSpinLimit = 1u << 26;
+__device__ void gather_barrier(const DecodeParams& p) {
+  const GatherArgs& g = p.gather;
+  __threadfence_system();
+  const int prev = atomicAdd(p.work + 2, 1);
+  if (prev != (int)gridDim.x - 1) return;
+  p.work[2] = 0;  // ready for the next launch on this workspace
+  __threadfence_system();
+  for (int r = 0; r < g.world; ++r) st_release_sys(g.peer_flags[r] + g.rank, g.epoch);
+  const uint64_t t0 = globaltimer_ns();
+  for (int r = 0; r < g.world; ++r) {
+    uint32_t i = 0;
+    while ((int32_t)(ld_acquire_sys(g.my_flags + r) - g.epoch) < 0) {
+      if (++i >= kPeerSpinLimit || globaltimer_ns() - t0 > g.timeout_ns) {
+        set_error(p.err, ABKV_DEVERR_TIMEOUT);
+        return;
+      }
+      __nanosleep(128);
+    }
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -402,7 +471,7 @@ __device__ void consumer(const DecodeParams& p, uint8_t* smem) {
       }
       const float val = Ls > 0.f ? Os / Ls : 0.f;
       if (n_chunks == 1) {
-        L.out[((int64_t)M.b * p.Hq + hr) * kD + d] = __float2bfloat16(val);
+        store_out(p, L, M.b, hr, d, val);
       } else {
         p.part_o[(prow + hr) * kD + d] = val;
         if (d == 0) p.part_lse[prow + hr] = Ls > 0.f ? Mu + log2f(Ls) : -INFINITY;
@@ -433,7 +502,7 @@ __device__ void consumer(const DecodeParams& p, uint8_t* smem) {
             Ls += f;
             Os += f * __ldcg(p.part_o + rr * kD + d);
           }
-          L.out[((int64_t)M.b * p.Hq + hr) * kD + d] = __float2bfloat16(Ls > 0.f ? Os / Ls : 0.f);
+          store_out(p, L, M.b, hr, d, Ls > 0.f ? Os / Ls : 0.f);
         }
         if (threadIdx.x == 0) p.counters[lb] = 0;  // ready for the next call on this workspace
       }
@@ -457,6 +526,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_split_kernel(const __grid_
     producer(p, smem);
   } else {
     consumer(p, smem);
+  }
+  if (p.gather.my_flags) {
+    __threadfence_system();  // this thread's output stores, to every rank
+    __syncthreads();
+    if (threadIdx.x == 0) gather_barrier(p);
   }
 }
 
@@ -524,13 +598,13 @@ extern "C" size_t abkv_decode_workspace_size(int num_layers, int num_seqs, int n
   return plan.total;
 }
 
-extern "C" int abkv_decode(const void* const* q, const void* const* kv,
-                           const int32_t* const* block_tables, const int64_t* bt_strides,
-                           const int32_t* const* seq_lens, const int64_t* num_blocks,
-                           void* const* out, int num_layers, int num_seqs, int num_q_heads,
-                           int num_kv_heads, int head_dim, int page_size, int max_pages_per_seq,
-                           float scale, int chunk_tokens, void* workspace, size_t workspace_bytes,
-                           void* stream) {
+namespace abkv {
+namespace {
+int launch_decode(const void* const* q, const void* const* kv, const int32_t* const* block_tables,
+                  const int64_t* bt_strides, const int32_t* const* seq_lens, const int64_t* num_blocks,
+                  void* const* out, int num_layers, int num_seqs, int num_q_heads, int num_kv_heads,
+                  int head_dim, int page_size, int max_pages_per_seq, float scale, int chunk_tokens,
+                  void* workspace, size_t workspace_bytes, void* stream, const GatherArgs& gather) {
   if (!q || !kv || !block_tables || !bt_strides || !seq_lens || !num_blocks || !out)
     return ABKV_ERR_INVALID_ARG;
   if (num_kv_heads <= 0 || num_q_heads % num_kv_heads != 0) return ABKV_ERR_INVALID_ARG;
@@ -583,6 +657,7 @@ extern "C" int abkv_decode(const void* const* q, const void* const* kv,
   prm.chunk_tiles = plan.chunk_tiles;
   prm.max_chunks = plan.max_chunks;
   prm.max_rows = plan.max_tiles * kTile;
+  prm.gather = gather;
 
   for (int l0 = 0; l0 < num_layers; l0 += kMaxLayers) {
     const int nl = (num_layers - l0) < kMaxLayers ? (num_layers - l0) : kMaxLayers;
@@ -604,6 +679,66 @@ extern "C" int abkv_decode(const void* const* q, const void* const* kv,
   }
   if (cudaGetLastError() != cudaSuccess) return ABKV_ERR_CUDA;
   return ABKV_OK;
+}
+}  // namespace
+}  // namespace abkv
+
+extern "C" int abkv_decode(const void* const* q, const void* const* kv,
+                           const int32_t* const* block_tables, const int64_t* bt_strides,
+                           const int32_t* const* seq_lens, const int64_t* num_blocks,
+                           void* const* out, int num_layers, int num_seqs, int num_q_heads,
+                           int num_kv_heads, int head_dim, int page_size, int max_pages_per_seq,
+                           float scale, int chunk_tokens, void* workspace, size_t workspace_bytes,
+                           void* stream) {
+  GatherArgs g;
+  memset(&g, 0, sizeof(g));
+  g.out_row = (int64_t)num_q_heads * kD;
+  g.world = 1;
+  return launch_decode(q, kv, block_tables, bt_strides, seq_lens, num_blocks, out, num_layers, num_seqs,
+                       num_q_heads, num_kv_heads, head_dim, page_size, max_pages_per_seq, scale, chunk_tokens,
+                       workspace, workspace_bytes, stream, g);
+}
+
+extern "C" int abkv_decode_gather(const void* const* q, const void* const* kv,
+                                  const int32_t* const* block_tables, const int64_t* bt_strides,
+                                  const int32_t* const* seq_lens, const int64_t* num_blocks,
+                                  void* const* out, int num_layers, int num_seqs, int num_q_heads,
+                                  int num_kv_heads, int head_dim, int page_size, int max_pages_per_seq,
+                                  float scale, int chunk_tokens, const abkv_gather_t* gather,
+                                  void* workspace, size_t workspace_bytes, void* stream) {
+  if (!gather || !out) return ABKV_ERR_INVALID_ARG;
+  const abkv_gather_t& a = *gather;
+  if (a.world < 1 || a.world > kMaxPeers || a.rank < 0 || a.rank >= a.world || a.epoch == 0)
+    return ABKV_ERR_INVALID_ARG;
+  if (a.hq_total != a.world * num_q_heads) return ABKV_ERR_INVALID_ARG;
+  for (int r = 0; r < a.world; ++r)
+    if (!a.rank_buffers[r] || (reinterpret_cast<uintptr_t>(a.rank_buffers[r]) & 255)) return ABKV_ERR_INVALID_ARG;
+  // every layer's output slot [num_seqs][hq_total][D] lies in this rank's buffer
+  // after the flag area (the same offsets are written in the peers' buffers)
+  const char* base = static_cast<const char*>(a.rank_buffers[a.rank]);
+  const size_t slot = (size_t)num_seqs * a.hq_total * kD * 2;
+  for (int l = 0; l < num_layers; ++l) {
+    const char* o = static_cast<const char*>(out[l]);
+    if (!o || o < base + ABKV_GATHER_FLAG_BYTES || o + slot > base + a.buffer_bytes ||
+        ((o - base) & 15))
+      return ABKV_ERR_INVALID_ARG;
+  }
+  GatherArgs g;
+  memset(&g, 0, sizeof(g));
+  for (int r = 0; r < a.world; ++r) {
+    g.peer_delta[r] = (static_cast<const char*>(a.rank_buffers[r]) - base) / 2;
+    g.peer_flags[r] = static_cast<uint32_t*>(a.rank_buffers[r]);
+  }
+  g.my_flags = static_cast<uint32_t*>(a.rank_buffers[a.rank]);
+  g.out_row = (int64_t)a.hq_total * kD;
+  g.world = a.world;
+  g.rank = a.rank;
+  g.head0 = a.rank * num_q_heads;
+  g.epoch = a.epoch;
+  g.timeout_ns = (a.timeout_us ? (uint64_t)a.timeout_us : 5000000ull) * 1000ull;
+  return launch_decode(q, kv, block_tables, bt_strides, seq_lens, num_blocks, out, num_layers, num_seqs,
+                       num_q_heads, num_kv_heads, head_dim, page_size, max_pages_per_seq, scale, chunk_tokens,
+                       workspace, workspace_bytes, stream, g);
 }
 
 // ---------------------------------------------------------------------------

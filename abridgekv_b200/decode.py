@@ -36,6 +36,47 @@ def _check_cuda(name: str, t: torch.Tensor, dtype: torch.dtype | None = None) ->
         raise TypeError(f"{name} must be {dtype}, got {t.dtype}")
 
 
+def _validate(queries, kv_caches, block_tables, seq_lens, outputs, out_shape=None, alloc=True):
+    """Check the per-layer arguments; -> (B, Hq, Hkv, D, page, outputs) (no outputs
+    are allocated when `outputs` is None and `alloc` is False)."""
+    L = len(queries)
+    if not (L == len(kv_caches) == len(block_tables) == len(seq_lens)) or L == 0:
+        raise ValueError("per-layer argument lists must be non-empty and of equal length")
+    q0, kv0 = queries[0], kv_caches[0]
+    B, Hq, D = q0.shape
+    _, two, page, Hkv, D2 = kv0.shape
+    if two != 2 or D2 != D:
+        raise ValueError(f"kv cache must be [num_blocks, 2, page, Hkv, {D}], got {tuple(kv0.shape)}")
+    device = q0.device
+    out_shape = (B, Hq, D) if out_shape is None else tuple(out_shape)
+    outs = []
+    for l in range(L):
+        q, kv, bt, sl = queries[l], kv_caches[l], block_tables[l], seq_lens[l]
+        _check_cuda("query", q, torch.bfloat16)
+        _check_cuda("kv_cache", kv, torch.bfloat16)
+        _check_cuda("block_table", bt, torch.int32)
+        _check_cuda("seq_lens", sl, torch.int32)
+        if tuple(q.shape) != (B, Hq, D) or not q.is_contiguous():
+            raise ValueError("every query must be a contiguous [B, Hq, D] tensor")
+        if tuple(kv.shape[1:]) != (2, page, Hkv, D) or not kv.is_contiguous():
+            raise ValueError("every kv cache must be a contiguous [num_blocks, 2, page, Hkv, D] tensor")
+        if bt.dim() != 2 or bt.shape[0] < B or not bt.is_contiguous():
+            raise ValueError("block_table must be a contiguous [>=B, max_pages] tensor")
+        if sl.dim() != 1 or sl.shape[0] < B or not sl.is_contiguous():
+            raise ValueError("seq_lens must be a contiguous [>=B] tensor")
+        if outputs is not None:
+            o = outputs[l]
+            _check_cuda("output", o, torch.bfloat16)
+            if tuple(o.shape) != out_shape or not o.is_contiguous():
+                raise ValueError(f"every output must be a contiguous {list(out_shape)} tensor")
+        elif alloc:
+            o = torch.empty(out_shape, dtype=torch.bfloat16, device=device)
+        else:
+            continue
+        outs.append(o)
+    return B, Hq, Hkv, D, page, outs
+
+
 def paged_decode(
     queries: Sequence[torch.Tensor],
     kv_caches: Sequence[torch.Tensor],
@@ -56,37 +97,8 @@ def paged_decode(
     Returns outputs[l]: [B, Hq, D] bf16.
     """
     L = len(queries)
-    if not (L == len(kv_caches) == len(block_tables) == len(seq_lens)) or L == 0:
-        raise ValueError("per-layer argument lists must be non-empty and of equal length")
-    q0, kv0 = queries[0], kv_caches[0]
-    B, Hq, D = q0.shape
-    _, two, page, Hkv, D2 = kv0.shape
-    if two != 2 or D2 != D:
-        raise ValueError(f"kv cache must be [num_blocks, 2, page, Hkv, {D}], got {tuple(kv0.shape)}")
-    device = q0.device
-    outs = []
-    for l in range(L):
-        q, kv, bt, sl = queries[l], kv_caches[l], block_tables[l], seq_lens[l]
-        _check_cuda("query", q, torch.bfloat16)
-        _check_cuda("kv_cache", kv, torch.bfloat16)
-        _check_cuda("block_table", bt, torch.int32)
-        _check_cuda("seq_lens", sl, torch.int32)
-        if tuple(q.shape) != (B, Hq, D) or not q.is_contiguous():
-            raise ValueError("every query must be a contiguous [B, Hq, D] tensor")
-        if tuple(kv.shape[1:]) != (2, page, Hkv, D) or not kv.is_contiguous():
-            raise ValueError("every kv cache must be a contiguous [num_blocks, 2, page, Hkv, D] tensor")
-        if bt.dim() != 2 or bt.shape[0] < B or not bt.is_contiguous():
-            raise ValueError("block_table must be a contiguous [>=B, max_pages] tensor")
-        if sl.dim() != 1 or sl.shape[0] < B or not sl.is_contiguous():
-            raise ValueError("seq_lens must be a contiguous [>=B] tensor")
-        if outputs is not None:
-            o = outputs[l]
-            _check_cuda("output", o, torch.bfloat16)
-            if tuple(o.shape) != (B, Hq, D) or not o.is_contiguous():
-                raise ValueError("every output must be a contiguous [B, Hq, D] tensor")
-        else:
-            o = torch.empty((B, Hq, D), dtype=torch.bfloat16, device=device)
-        outs.append(o)
+    B, Hq, Hkv, D, page, outs = _validate(queries, kv_caches, block_tables, seq_lens, outputs)
+    device = queries[0].device
     if max_pages_per_seq is None:
         max_pages_per_seq = max(int(bt.shape[1]) for bt in block_tables)
     if scale is None:

@@ -357,7 +357,9 @@ def run_scaling(args, rank: int, world: int, local: int) -> None:
       tail (323.7 GB).  --shard seq: whole sequences per rank, one 36-layer
       launch per step.  --shard kv: every rank holds KV heads
       [r*8/W, (r+1)*8/W) of all sequences; per layer one decode launch of its
-      heads, then an NCCL all-gather of the [B, 32/W, 128] head outputs."""
+      heads whose epilogue all-gathers the [B, 32, 128] outputs into every
+      rank's buffer over NVLink (--gather fused, abkv_decode_gather), or the
+      plain decode followed by an NCCL all-gather (--gather nccl)."""
     from abridgekv_b200 import decode, parallel
     from abridgekv_b200.workloads import QWEN3_4B, config3_rows, config5_rows, qwen3_decode_workload
     from abridgekv_b200.workspace import Workspace
@@ -394,6 +396,7 @@ def run_scaling(args, rank: int, world: int, local: int) -> None:
     ws = Workspace(dev)
     stream = torch.cuda.current_stream(dev)
     wave_ms, alg_bytes, launches, waves_info = [], 0, 0, []
+    head_gather = None
     for wi, idx in enumerate(waves):
         sl = slice(idx[0], idx[-1] + 1)
         assert idx == list(range(sl.start, sl.stop))
@@ -401,7 +404,17 @@ def run_scaling(args, rank: int, world: int, local: int) -> None:
         outs = [torch.empty_like(q) for q in wl.queries]
         gathered = [None] * wl.num_layers
 
-        if kv_mode:
+        if kv_mode and args.gather == "fused":
+            from abridgekv_b200.gather import HeadGather
+            head_gather = HeadGather(wl.num_layers, wl.num_seqs, wl.num_q_heads * world, device=dev)
+
+            def step():
+                for l in range(wl.num_layers):
+                    head_gather.decode([l], [wl.queries[l]], [wl.kv_caches[l]], [wl.block_tables[l]],
+                                       [wl.seq_lens[l]], max_pages_per_seq=wl.max_pages,
+                                       chunk_tokens=args.chunk_tokens, workspace=ws)
+            per_step = wl.num_layers
+        elif kv_mode:
             def step():
                 for l in range(wl.num_layers):
                     decode.paged_decode([wl.queries[l]], [wl.kv_caches[l]], [wl.block_tables[l]],
@@ -431,6 +444,10 @@ def run_scaling(args, rank: int, world: int, local: int) -> None:
         alg_bytes += wl.kv_bytes + wl.qo_bytes
         launches += per_step * args.steps
         waves_info.append({"seqs": len(idx), "kv_gb": wl.kv_bytes / 1e9, "ms_per_step": wave_ms[-1]})
+        if head_gather is not None:
+            assert ws.read_error() == 0, "device error word set during the timed region"
+            head_gather.close()
+            head_gather = None
         del wl, outs, gathered
         torch.cuda.empty_cache()
     ms_step = sum(wave_ms)
@@ -454,7 +471,9 @@ def run_scaling(args, rank: int, world: int, local: int) -> None:
                                + ("per-layer quotas 6x256/18x128/12x64, generated length log-uniform [2K,32K]"
                                   if cfg == 3 else "quota 128 in all 36 layers, 63 compressed blocks + tail"),
                    "global_batch": n_global,
-                   "parallelism": (f"KV-head-sharded x{world} + NCCL all-gather per layer" if kv_mode
+                   "parallelism": ((f"KV-head-sharded x{world}, all-gather fused into the decode epilogue "
+                                    "(peer stores over NVLink)" if args.gather == "fused"
+                                    else f"KV-head-sharded x{world} + NCCL all-gather per layer") if kv_mode
                                    else f"sequence-sharded x{world}, no collective"),
                    "waves_rank0": waves_info, "mem_budget_gb": args.mem_budget_gb,
                    "l2": "inputs larger than L2; no flush"},
@@ -484,6 +503,8 @@ def main() -> None:
     ap.add_argument("--config", type=int, choices=[2, 3, 5], default=2,
                     help="2 (default, headline): weak scaling; 3 / 5: strong-scaling saturation runs")
     ap.add_argument("--shard", choices=["seq", "kv"], default="seq", help="config 5: sequence or KV-head sharding")
+    ap.add_argument("--gather", choices=["fused", "nccl"], default="fused",
+                    help="config 5 --shard kv: all-gather fused into the decode kernel, or NCCL after it")
     ap.add_argument("--mem-budget-gb", type=float, default=130.0,
                     help="configs 3/5: K/V bytes one wave may hold per GPU")
     args = ap.parse_args()

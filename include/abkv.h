@@ -134,6 +134,61 @@ int abkv_decode_noalloc(const void* const* q, const void* const* kv,
                         int max_pages_per_seq, float scale, int chunk_tokens,
                         int32_t* device_error, void* stream);
 
+/* KV-head-sharded decode with the all-gather fused into the epilogue.
+ *
+ * BASELINE config 5's optional mode (one process per GPU, rank r holding KV
+ * heads [r*Hkv, (r+1)*Hkv) of every sequence; num_q_heads / num_kv_heads are
+ * this rank's share).  Where the reference's layout would follow the
+ * attention with an all-gather of the [B, world*Hq, D] head outputs, this
+ * call's epilogue stores each output row straight into every rank's gather
+ * buffer (peer memory mapped with abkv_peer_open), then its last CTA raises
+ * this rank's flag (= epoch) in every rank's flag area and waits until all
+ * ranks' flags have reached epoch, so when the launch completes the full
+ * [B][world*Hq][D] output of every layer is in this rank's buffer.
+ *
+ * Every rank calls it with the same layers, shapes and epoch, in the same
+ * order (like a collective); epochs start at 1 and increase by one per call.
+ * Gather buffer layout (identical on all ranks): ABKV_GATHER_FLAG_BYTES of
+ * flags (zero at allocation), then the output slots; out[l] must point into
+ * this rank's buffer past the flags, at the same offset on every rank, each
+ * slot [num_seqs][hq_total][head_dim] contiguous.  A peer that does not arrive
+ * within timeout_us sets ABKV_DEVERR_TIMEOUT in the workspace error word; the
+ * kernel still returns.  Other arguments as abkv_decode. */
+#define ABKV_GATHER_FLAG_BYTES 256
+#define ABKV_MAX_PEERS 8
+typedef struct abkv_gather {
+  void* rank_buffers[ABKV_MAX_PEERS]; /* every rank's gather buffer, as mapped in
+                                         this process (index = rank)           */
+  size_t buffer_bytes;                /* size of each gather buffer            */
+  int world;                          /* ranks, 1..ABKV_MAX_PEERS              */
+  int rank;                           /* this rank                             */
+  int hq_total;                       /* world * num_q_heads                   */
+  uint32_t epoch;                     /* this call's barrier epoch (>= 1)      */
+  uint32_t timeout_us;                /* barrier wait limit; 0 = 5 s           */
+} abkv_gather_t;
+
+int abkv_decode_gather(const void* const* q, const void* const* kv,
+                       const int32_t* const* block_tables,
+                       const int64_t* bt_strides,
+                       const int32_t* const* seq_lens,
+                       const int64_t* num_blocks, void* const* out,
+                       int num_layers, int num_seqs, int num_q_heads,
+                       int num_kv_heads, int head_dim, int page_size,
+                       int max_pages_per_seq, float scale, int chunk_tokens,
+                       const abkv_gather_t* gather, void* workspace,
+                       size_t workspace_bytes, void* stream);
+
+/* Peer-visible buffers (CUDA IPC; no multicast object).  abkv_peer_alloc
+ * allocates `bytes` (>= ABKV_GATHER_FLAG_BYTES) of zeroed device memory on the
+ * current device and writes its ABKV_PEER_HANDLE_BYTES-byte handle;
+ * abkv_peer_open maps another process's buffer from its handle;
+ * abkv_peer_close unmaps it; abkv_peer_free releases an allocation. */
+#define ABKV_PEER_HANDLE_BYTES 64
+int abkv_peer_alloc(size_t bytes, void** ptr, unsigned char* handle);
+int abkv_peer_open(const unsigned char* handle, void** ptr);
+int abkv_peer_close(void* ptr);
+int abkv_peer_free(void* ptr);
+
 
 /* ========================================================================
  * 2. Compaction planner (host C++): page tables, free-block queue, span

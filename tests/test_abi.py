@@ -66,3 +66,46 @@ def test_decode_validation_rejects_before_launch(bad):
     st = lib.abkv_decode(q, kv, bt, strides, sl, nblk, out, 1, 2, hq, hkv, 128, 16, 4, scale, chunk,
                          ws, ws_bytes, None)
     assert st in (1, 2, 3), st
+
+
+@pytest.mark.parametrize("bad", ["no_gather", "epoch", "world", "rank", "hq_total", "unaligned", "out_in_flags",
+                                 "out_past_end"])
+def test_decode_gather_validation_rejects_before_launch(bad):
+    """abkv_decode_gather checks its gather descriptor (and that every output slot lies in
+    this rank's buffer past the flag area) before touching the GPU."""
+    lib = _lib.lib()
+    fake = 1 << 20
+    base = 1 << 30
+    B, hq, hkv, D = 2, 4, 1, 128
+    world = 2
+    slot = B * hq * world * D * 2
+    g = _lib.GatherT()
+    g.rank_buffers[0], g.rank_buffers[1] = base, base + (1 << 28)
+    g.buffer_bytes = _lib.GATHER_FLAG_BYTES + slot
+    g.world, g.rank, g.hq_total, g.epoch = world, 0, hq * world, 1
+    out_ptr = base + _lib.GATHER_FLAG_BYTES
+    if bad == "epoch":
+        g.epoch = 0
+    if bad == "world":
+        g.world = 9
+    if bad == "rank":
+        g.rank = 2
+    if bad == "hq_total":
+        g.hq_total = hq
+    if bad == "unaligned":
+        g.rank_buffers[1] = base + 64
+    if bad == "out_in_flags":
+        out_ptr = base + 16
+    if bad == "out_past_end":
+        out_ptr = base + _lib.GATHER_FLAG_BYTES + 256
+    st = lib.abkv_decode_gather(
+        _lib.ptr_array([fake]), _lib.ptr_array([fake]), _lib.ptr_array([fake]), _lib.i64_array([4]),
+        _lib.ptr_array([fake]), _lib.i64_array([16]), _lib.ptr_array([out_ptr]), 1, B, hq, hkv, D, 16, 4,
+        0.088, 0, None if bad == "no_gather" else C.byref(g), fake, 1 << 30, None)
+    assert st == 1, st
+
+
+def test_gather_struct_layout():
+    # abkv_gather_t: 8 pointers, size_t, 3 ints, 2 uint32 (natural alignment, no packing)
+    assert C.sizeof(_lib.GatherT) == 8 * 8 + 8 + 4 * 5 + 4
+    assert _lib.GatherT.epoch.offset == 84
