@@ -18,8 +18,10 @@ FlashInfer ``[num_blocks, 2, page, Hkv, D]``.  The copy is byte-exact for any
 """
 from __future__ import annotations
 
+import itertools
 from typing import Hashable, Sequence
 
+import numpy as np
 import torch
 
 from . import _lib
@@ -52,21 +54,21 @@ def _compact(layer_caches: Sequence[torch.Tensor], batches: Sequence[Sequence[Se
     elem = kv0.element_size()
     # the kernel moves rows as bytes: express the row as 2-byte units
     units = hkv * d * elem // 2
-    flat, offsets = [], [0]
-    for b in batches:
-        for op in b:
-            flat.extend(int(x) for x in op)
-        offsets.append(len(flat) // 4)
+    counts = [len(b) for b in batches]
     n_batches = len(batches)
-    if offsets[-1] == 0:
+    if sum(counts) == 0:
         return
-    max_ops = max(offsets[i + 1] - offsets[i] for i in range(n_batches))
+    flat = np.fromiter(itertools.chain.from_iterable(itertools.chain.from_iterable(batches)), dtype=np.int32,
+                       count=4 * sum(counts))
+    offsets = np.zeros(n_batches + 1, dtype=np.int64)
+    np.cumsum(counts, out=offsets[1:])
+    max_ops = max(counts)
     lib = _lib.lib()
     need = lib.abkv_compact_workspace_size(len(layer_caches), page, 1, units, max_ops)
     ws = (workspace or default_workspace(kv0.device)).ensure(need)
     s = torch.cuda.current_stream(kv0.device) if stream is None else stream
-    ops_arr = _lib.i32_array(flat)
-    off_arr = _lib.i64_array(offsets)
+    ops_arr = flat.ctypes.data_as(_lib.c_i32p)
+    off_arr = offsets.ctypes.data_as(_lib.c_i64p)
     with torch.cuda.device(kv0.device):
         st = lib.abkv_compact(_lib.ptr_array([kv.data_ptr() for kv in layer_caches]), len(layer_caches),
                               layout, nb, page, 1, units, ops_arr, off_arr, n_batches, ws.ptr(), ws.nbytes,

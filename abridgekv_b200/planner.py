@@ -26,6 +26,8 @@ import ctypes as C
 from dataclasses import dataclass
 from typing import Hashable, Iterable, Sequence
 
+import numpy as np
+
 from . import _lib
 
 
@@ -207,7 +209,8 @@ class BlockPlanner:
                     _lib.check("abkv_planner_pending_batch",
                                self._lib.abkv_planner_pending_batch(self._h, k, g, b, buf, cnt.value,
                                                                     C.byref(cnt)))
-                    batches.append([tuple(buf[4 * i:4 * i + 4]) for i in range(cnt.value)])
+                    rows = np.frombuffer(buf, dtype=np.int32, count=4 * cnt.value).reshape(-1, 4)
+                    batches.append(list(zip(*rows.T.tolist())))
                 per_group.append(batches)
             ops[self._names.get(k, k)] = per_group
         trunc = {}
