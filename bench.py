@@ -485,6 +485,133 @@ def run_scaling(args, rank: int, world: int, local: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------------------
+# Secondary paths (--path prefill | codestep | compaction): one GPU, one JSON line
+# with the GPU measurement of abridgekv_b200.benchmarks and the reference's CPU
+# path timed on this box's host cores over a bounded sample.
+def cpu_baseline_prefill(budget_s: float) -> dict:
+    """Eager dense-mask attention (the reference's _dense_mask + matmul/softmax path) in fp32
+    torch on the host cores, reduced shape; credited with the algorithmic FLOPs of its
+    visible pairs, like the GPU number."""
+    from oracle.mask_ref import arith_mask
+
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    C, K, N, D = 512, 256, 4, 128
+    quota = [256, 128, 64, 128]
+    S0 = N * (C + K)
+    g = torch.Generator().manual_seed(0)
+    q = torch.randn((len(quota), S0, D), generator=g)
+    k = torch.randn((1, S0, D), generator=g)
+    v = torch.randn((1, S0, D), generator=g)
+    mask = torch.from_numpy(arith_mask(S0, C, K, quota_per_head=quota)[0])
+    flops = 4.0 * D * float(mask.sum())
+    scale = 1.0 / np.sqrt(D)
+    n, t = 0, 0.0
+    while t < budget_s or n == 0:
+        t0 = time.perf_counter()
+        s_ = (q @ k.transpose(1, 2)) * scale
+        s_ = s_.masked_fill(~mask, float("-inf"))
+        _ = torch.softmax(s_, dim=-1) @ v
+        t += time.perf_counter() - t0
+        n += 1
+    return {"value": flops * n / t / 1e12, "unit": "TFLOP/s", "cores": cores, "kind": "port",
+            "sample": f"{n} x (1 sequence of {N} blocks x (512 + 256), 4 query heads with quotas {quota}, "
+                      f"fp32 dense-mask attention), {t:.1f} s"}
+
+
+def cpu_baseline_codestep(budget_s: float) -> dict:
+    """The reference's noncausal code step (_attend_request_vectorized, torch CPU port) on one
+    config-2 request's caches + 256 code rows, layer after layer."""
+    from abridgekv_b200.workloads import SCHEDULE_PERLAYER_MEAN128, build_decode_workload, config2_rows
+    from oracle.decode_ref import sidecar_codestep_torch
+
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    K = 256
+    rows = {q: r[:1] + K for q, r in config2_rows(64, 0).items()}
+    wl = build_decode_workload("cpu-codestep", SCHEDULE_PERLAYER_MEAN128, rows, num_q_heads=32, num_kv_heads=8,
+                               head_dim=128, device="cpu", seed=7)
+    q = torch.randn((K, 32, 128), generator=torch.Generator().manual_seed(1)).to(torch.bfloat16)
+    scale = 1.0 / np.sqrt(128)
+    n, t, flops = 0, 0.0, 0.0
+    while t < budget_s or n == 0:
+        l = n % wl.num_layers
+        quota = wl.quotas[l]
+        L = int(wl.seq_lens[l][0])
+        t0 = time.perf_counter()
+        sidecar_codestep_torch(q, wl.kv_caches[l], L, wl.block_tables[l][0], [quota] * 8, K, 8, 4, scale, wl.page)
+        t += time.perf_counter() - t0
+        flops += 4.0 * 128 * K * 32 * (L - K + quota)
+        n += 1
+    return {"value": flops / t / 1e12, "unit": "TFLOP/s", "cores": cores, "kind": "port",
+            "sample": f"{n} layer code steps of one config-2 request (+256 code rows), torch CPU port of "
+                      f"compresslm_packed_kv.py:648-741, {t:.1f} s"}
+
+
+def cpu_baseline_compaction(budget_s: float) -> dict:
+    """The reference's compaction on the host: the planner restatement (mask_token_span ->
+    copy ops) and the gather-then-scatter executor on numpy caches, 2 sequences x 12 tensors."""
+    from oracle.compaction_ref import Planner, execute_kv_copy_operations
+
+    cores = 1
+    C, K, page, quotas, B, T = 512, 256, 16, (256, 128, 64), 2, 12
+    per = C + K
+    n, t, moved = 0, 0.0, 0
+    while t < budget_s or n == 0:
+        blocks = 3
+        nb = 1 + B * (blocks * per // page) * 3 + 8
+        caches = [np.zeros((nb, 2, page, 8, 128), dtype=np.uint16) for _ in range(T)]
+        pl = Planner(nb, page, 3)
+        for b in range(B):
+            pl.add_request(b)
+        for blk in range(blocks):
+            t0 = time.perf_counter()
+            for b in range(B):
+                m = (blk + 1) * per
+                pl.allocate_slots(b, m)
+                pl.computed[b] = m
+                pl.finish_block(b, (blk * per, blk * per + C), (blk * per + C, (blk + 1) * per), quotas, K)
+            ops = pl.take_pending()[0]
+            execute_kv_copy_operations(ops, [caches] * 3)
+            t += time.perf_counter() - t0
+            rows = sum(len(x) for g_ in ops.values() for bl in g_ for x in bl)
+            moved += rows * T * 2 * 2 * 8 * 128 * 2
+        n += 1
+    return {"value": moved / t / 1e9, "unit": "GB/s", "cores": cores, "kind": "port",
+            "sample": f"{n} x (2 sequences x 3 block finishes x 12 layer tensors: planner restatement + numpy "
+                      f"gather/scatter executor), {t:.1f} s"}
+
+
+def run_path(args) -> None:
+    from abridgekv_b200 import benchmarks
+
+    torch.cuda.set_device(0)
+    ns = argparse.Namespace(layers=36, steps=args.steps, warmup=args.warmup, flex=args.flex, blocks=6)
+    uuid = str(getattr(torch.cuda.get_device_properties(0), "uuid", "") or "")
+    sampler = ClockSampler(("GPU-" + uuid) if uuid and not uuid.startswith("GPU-") else (uuid or 0))
+    sampler.start()
+    if args.path == "prefill":
+        line = benchmarks.bench_prefill(ns)
+        launches = 36 * args.steps
+    elif args.path == "codestep":
+        line = benchmarks.bench_codestep(ns)
+        launches = 36 * args.steps
+    else:
+        line = benchmarks.bench_compaction(ns)
+        launches = None
+    clocks = sampler.stop()
+    budget = 0.0 if args.no_cpu_baseline else args.cpu_budget
+    cpu = None if args.no_cpu_baseline else {"prefill": cpu_baseline_prefill, "codestep": cpu_baseline_codestep,
+                                             "compaction": cpu_baseline_compaction}[args.path](budget)
+    line.update({"n_gpus": 1, "steps": args.steps if args.path != "compaction" else ns.blocks,
+                 "warmup": args.warmup, "higher_is_better": True, "scaling": None, "vs_baseline": None,
+                 "dtype": "bf16", "data": "synthetic", "cpu_baseline": cpu, "gpu_launches": launches,
+                 "clocks": clocks, "path": args.path,
+                 "e2e": None, "e2e_note": "secondary path: inputs stay in HBM (the headline e2e is the decode line)"})
+    print(json.dumps(line), flush=True)
+
+
 def _config2_rows_for_cpu():
     from abridgekv_b200.workloads import config2_rows
     return config2_rows(64, seed=0)
@@ -503,6 +630,9 @@ def main() -> None:
     ap.add_argument("--config", type=int, choices=[2, 3, 5], default=2,
                     help="2 (default, headline): weak scaling; 3 / 5: strong-scaling saturation runs")
     ap.add_argument("--shard", choices=["seq", "kv"], default="seq", help="config 5: sequence or KV-head sharding")
+    ap.add_argument("--path", choices=["decode", "prefill", "codestep", "compaction"], default="decode",
+                    help="decode (default, the headline) or a secondary path's line with its CPU baseline")
+    ap.add_argument("--flex", action="store_true", help="--path prefill: also time compiled FlexAttention")
     ap.add_argument("--gather", choices=["fused", "nccl"], default="fused",
                     help="config 5 --shard kv: all-gather fused into the decode kernel, or NCCL after it")
     ap.add_argument("--mem-budget-gb", type=float, default=130.0,
@@ -510,6 +640,11 @@ def main() -> None:
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.path != "decode":
+        if args.gpus != 1 or args.impl != "ours":
+            raise SystemExit("--path prefill/codestep/compaction runs on one GPU with --impl ours")
+        run_path(args)
+        return
     if args.impl == "reference":
         rank = int(os.environ.get("RANK", "0"))
         world = int(os.environ.get("WORLD_SIZE", "1"))

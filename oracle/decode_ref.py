@@ -15,7 +15,9 @@ the physical per-quota cache (no sidecar pages):
 Two numpy forms: ``decode_reference`` reproduces those roundings,
 ``decode_exact`` is float64 ground truth on the same bf16 inputs.
 ``sidecar_decode_torch`` is the same computation as torch CPU ops (used to
-time the reference's CPU path in bench.py).
+time the reference's CPU path in bench.py).  ``codestep_exact`` (float64) and
+``sidecar_codestep_torch`` (torch CPU, the reference's op sequence) restate the
+noncausal code step of _attend_request_vectorized (:648-741).
 """
 from __future__ import annotations
 
@@ -132,3 +134,33 @@ def codestep_exact(qrows, kv, block_table, seq_lens, K, quota_per_kv_head, scale
             e = np.exp(s - s.max(axis=1, keepdims=True))
             out[r * K:(r + 1) * K, h] = (e / e.sum(axis=1, keepdims=True)) @ vh
     return out
+
+
+def sidecar_codestep_torch(query, kv_cache, seq_len: int, block_row, quotas_per_kv_head, k_max: int,
+                           num_kv_heads: int, groups: int, scale: float, page: int, excluded=None):
+    """torch (CPU) form of one request's noncausal code step,
+    PackedKVSidecar._attend_request_vectorized(causal=False) without sidecar pages
+    (compresslm_packed_kv.py:648-741): gather rows [0, seq_len) through the block-table row
+    (_gather_cache_span_indexed), bf16 score einsum, hide rows >= prefix + quota per KV head and
+    the optional exclusion range, fp32 softmax, bf16 weights, bf16 value einsum.
+    query [k_max, Hq, D] bf16 -> [k_max, Hq, D] bf16."""
+    import torch
+
+    pos = torch.arange(seq_len)
+    blocks = block_row.to(torch.long)[pos // page]
+    rows = kv_cache[blocks, :, pos % page]                    # [S, 2, Hkv, D]
+    key = rows[:, 0].permute(1, 0, 2)                         # [Hkv, S, D]
+    value = rows[:, 1].permute(1, 0, 2)
+    D = query.shape[-1]
+    q = query.reshape(k_max, num_kv_heads, groups, D)
+    scores = torch.einsum("qhgd,htd->qhgt", q, key) * scale
+    prefix = seq_len - k_max
+    quotas = torch.as_tensor(list(quotas_per_kv_head))
+    hidden = pos.unsqueeze(0) >= (prefix + quotas).unsqueeze(1)   # [Hkv, S]
+    hidden = hidden.unsqueeze(0).expand(k_max, -1, -1).clone()
+    if excluded is not None and excluded[1] > excluded[0]:
+        hidden[:, :, int(excluded[0]):int(excluded[1])] = True
+    scores.masked_fill_(hidden.unsqueeze(2), -torch.inf)
+    weights = torch.softmax(scores, dim=-1, dtype=torch.float32).to(q.dtype)
+    att = torch.einsum("qhgt,htd->qhgd", weights, value)
+    return att.reshape(k_max, num_kv_heads * groups, D)

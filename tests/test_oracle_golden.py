@@ -41,3 +41,24 @@ def test_codestep_oracle_matches_reference(name):
     # the reference rounds scores and weights to bf16; float64 stays within its error budget
     assert np.abs(ex - ref).max() < 3e-2
     assert np.abs(ex - ref).mean() < 2e-3
+
+
+@pytest.mark.parametrize("name", codestep_cases())
+def test_codestep_torch_port_matches_reference(name):
+    """The torch CPU port timed as the code step's CPU baseline reproduces the reference's
+    outputs (same op sequence and roundings) on the golden cases."""
+    import torch
+
+    from oracle.decode_ref import sidecar_codestep_torch
+
+    case, qrows, K, quotas, ref, excl = load_codestep(name)
+    kv = torch.from_numpy(case.kv).to(torch.bfloat16)
+    Hq, Hkv = qrows.shape[1], case.kv.shape[3]
+    outs = []
+    for r, s_len in enumerate(case.seq_lens):
+        q = torch.from_numpy(qrows[r * K:(r + 1) * K]).to(torch.bfloat16)
+        outs.append(sidecar_codestep_torch(q, kv, int(s_len), torch.from_numpy(case.block_table[r]), quotas, K,
+                                           Hkv, Hq // Hkv, case.scale, case.page,
+                                           None if excl is None else excl[r]).float().numpy())
+    got = np.concatenate(outs)
+    assert np.abs(got - ref).max() <= 1e-2
