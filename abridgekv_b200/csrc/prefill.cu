@@ -29,13 +29,16 @@
 //               issues tcgen05.mma in the order
 //               S_A(0) S_B(0) S_A(1) S_B(1) | PV_A(j) S_A(j+2) PV_B(j) S_B(j+2) | ...
 //                 S  = Q K^T   (A = Q, B = K, both K-major, fp32 in TMEM)
-//                 O += P V     (A = P from shared memory, K-major; B = V, MN-major)
+//                 O += P V     (A = P from TMEM, B = V, MN-major)
 //               so each head's softmax overlaps the other head's MMAs
 //   warps 2..5  softmax of head A, warps 6..9 softmax of head B: thread = one
 //               TMEM lane = one query row; S read with tcgen05.ld, masked online
-//               softmax in fp32, P written to shared memory (bf16, 128B-swizzled
-//               K-major), O rescaled in TMEM when the row maximum grows;
-//               epilogue divides by the row sum.
+//               softmax in fp32, P (bf16 pairs) stored back into the upper half
+//               of its own S buffer with tcgen05.st -- so P is double-buffered
+//               with S, and a head's softmax of tile j+1 never waits for its
+//               P.V of tile j unless O must be rescaled; epilogue divides by the
+//               row sum.  The S MMA of tile j+2 overwrites P(j) after P.V(j) read
+//               it: tcgen05.mma operations of one thread run in issue order.
 // Every mbarrier wait is bounded and records ABKV_DEVERR_TIMEOUT on expiry.
 #include <cuda.h>
 
@@ -49,18 +52,26 @@ namespace {
 constexpr int kBM = 128, kBN = 64, kD = 128;
 constexpr int kThreads = 320;
 constexpr int kMaxHeads = 128;
-constexpr int kStages = 3;
+constexpr int kStages = 4;
 constexpr uint32_t kTmemCols = 512;  // per head (A at 0, B at 256): S buffers [0,64) [64,128), O [128,256)
+constexpr uint32_t kPCol = 32;       // P (64 bf16 = 32 columns) lives in columns [32, 64) of its S buffer
 
 // dynamic shared memory layout (1024-byte aligned pieces for 128B swizzle)
 constexpr int kQBytes = kBM * kD * 2;          // 32 KiB: 2 atoms of [128 rows][128 B]
 constexpr int kKVHalf = kBN * kD * 2;          // 16 KiB: 2 atoms of [64 rows][128 B]
 constexpr int kStageBytes = 2 * kKVHalf;       // K then V
-constexpr int kPBytes = kBM * kBN * 2;         // 16 KiB: 1 atom of [128 rows][128 B]
 constexpr int kOffQ = 0;                        // Q_A, Q_B
 constexpr int kOffKV = 2 * kQBytes;
-constexpr int kOffP = kOffKV + kStages * kStageBytes;  // P_A, P_B
-constexpr int kOffBar = kOffP + 2 * kPBytes;
+constexpr int kOffBar = kOffKV + kStages * kStageBytes;
+// mbarriers (u64 slots from kOffBar): q_full, kv_full[kStages], kv_empty[kStages],
+// s_full[head][S buffer], p_full[head][S buffer], o_done[head], o_full, then the TMEM
+// address.  p_full is double-buffered like S: a head's softmax may finish tile j+1
+// before the MMA thread has taken tile j's P, and one barrier per buffer keeps the
+// two arrivals in different barriers (a parity wait cannot tell phases 2 apart).
+constexpr int kBarKvFull = 1, kBarKvEmpty = kBarKvFull + kStages, kBarSFull = kBarKvEmpty + kStages,
+              kBarPFull = kBarSFull + 4, kBarODone = kBarPFull + 4, kBarOFull = kBarODone + 2,
+              kBarTmem = kBarOFull + 1;
+static_assert((kBarTmem + 1) * 8 <= 256, "barrier area");
 constexpr int kOffList = kOffBar + 256;         // visited key tiles: (kb << 16) | kw0, per 64-key tile
 constexpr int kMaxKeyTiles = 2048;              // keys up to 2048 x 64 = 128K rows
 constexpr int kSmemBytes = kOffList + 4 * kMaxKeyTiles + 16 + 1024;  // + slack for 1024-byte alignment
@@ -172,6 +183,15 @@ __device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t adesc, uint64_t b
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// A operand from TMEM (128 lanes x 16 bf16 = 8 columns per K step of 16).
+__device__ __forceinline__ void umma_tmem_a(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(
                    smem_u32(bar))
@@ -263,8 +283,8 @@ struct SoftmaxState {
 // kHole: columns [hs, he) are hidden as well (the code step's tail exclusion).
 template <bool kHole>
 __device__ __forceinline__ void softmax_tile(const PrefillParams& p, int lim, int hs, int he, int row,
-                                             uint32_t tmem_s, uint32_t tmem_o, uint32_t lane_base, uint8_t* pbuf,
-                                             int j, uint64_t* o_done, bool& dead, SoftmaxState& st) {
+                                             uint32_t tmem_s, uint32_t tmem_o, uint32_t lane_base, int j,
+                                             uint64_t* o_done, bool& dead, SoftmaxState& st) {
   const float sl2 = p.scale_log2;  // lim: visible columns of this row are c < lim
   float t0[32], t1[32];
   tmem_ld32(tmem_s + lane_base, t0);
@@ -311,11 +331,15 @@ __device__ __forceinline__ void softmax_tile(const PrefillParams& p, int lim, in
   }
   st.l_run = st.l_run * alpha + ((rsa[0] + rsa[1]) + (rsa[2] + rsa[3]));
   st.m_run = m_new;
-  if (j > 0) {
-    // the previous P.V of this head must be done before P and O are touched
+  // P(j) into the upper half of this tile's S buffer (already read into registers);
+  // the buffer's previous P was consumed by P.V(j-2), which completed before S(j)
+  // was signalled
+  tmem_st32(tmem_s + lane_base + kPCol, reinterpret_cast<const float(&)[32]>(w));
+  if (j > 0 && __any_sync(0xffffffffu, need)) {
+    // O is touched only after the previous P.V of this head completed
     const bool ok = __all_sync(0xffffffffu, wait_or_abort(o_done, (uint32_t)((j - 1) & 1), dead, p.err));
     tc_fence_after();
-    if (ok && __any_sync(0xffffffffu, need)) {
+    if (ok) {
 #pragma unroll 1
       for (int c4 = 0; c4 < 4; ++c4) {
         float t[32];
@@ -325,14 +349,9 @@ __device__ __forceinline__ void softmax_tile(const PrefillParams& p, int lim, in
         for (int i = 0; i < 32; ++i) t[i] *= alpha;
         tmem_st32(tmem_o + lane_base + c4 * 32, t);
       }
-      tmem_wait_st();
     }
   }
-#pragma unroll
-  for (int ch = 0; ch < 8; ++ch) {
-    uint8_t* dst = pbuf + row * 128 + ((ch ^ (row & 7)) << 4);
-    *reinterpret_cast<uint4*>(dst) = make_uint4(w[ch][0], w[ch][1], w[ch][2], w[ch][3]);
-  }
+  tmem_wait_st();
 }
 
 __device__ __forceinline__ bool visit_tile(const PrefillParams& p, int hA, int hB, int qt, int kt, int pl) {
@@ -345,13 +364,13 @@ __device__ __forceinline__ void attn_body(const PrefillParams& p) {
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint64_t* q_full = bar + 0;
-  uint64_t* kv_full = bar + 1;   // [kStages]
-  uint64_t* kv_empty = bar + 4;  // [kStages]
-  uint64_t* s_full = bar + 7;    // [head][S buffer]
-  uint64_t* p_full = bar + 11;   // [head]
-  uint64_t* o_done = bar + 13;   // [head]: one phase per P.V
-  uint64_t* o_full = bar + 15;
-  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bar + 16);
+  uint64_t* kv_full = bar + kBarKvFull;    // [kStages]
+  uint64_t* kv_empty = bar + kBarKvEmpty;  // [kStages]
+  uint64_t* s_full = bar + kBarSFull;      // [head][S buffer]
+  uint64_t* p_full = bar + kBarPFull;      // [head][S buffer]
+  uint64_t* o_done = bar + kBarODone;      // [head]: one phase per P.V
+  uint64_t* o_full = bar + kBarOFull;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bar + kBarTmem);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // dense: heaviest query tiles first; paged: query tile of the request's code rows
@@ -404,8 +423,7 @@ __device__ __forceinline__ void attn_body(const PrefillParams& p) {
       mbar_init(&kv_empty[i], 1);
     }
     for (int i = 0; i < 4; ++i) mbar_init(&s_full[i], 1);
-    mbar_init(&p_full[0], 128);
-    mbar_init(&p_full[1], 128);
+    for (int i = 0; i < 4; ++i) mbar_init(&p_full[i], 128);
     mbar_init(&o_done[0], 1);
     mbar_init(&o_done[1], 1);
     mbar_init(o_full, 1);
@@ -531,7 +549,6 @@ __device__ __forceinline__ void attn_body(const PrefillParams& p) {
       const bool two = hB >= 0;
       wait_or_abort(q_full, 0, dead, p.err);
       const uint32_t qa = smem_u32(smem + kOffQ), qbv = qa + kQBytes;
-      const uint32_t pa = smem_u32(smem + kOffP), pbv = pa + kPBytes;
       const uint32_t sA = tmem, oA = tmem + 128, sB = tmem + 256, oB = tmem + 384;
       auto issue_s = [&](uint32_t qaddr, uint32_t sd, int st) {
         const uint32_t kaddr = smem_u32(smem + kOffKV + st * kStageBytes);
@@ -541,12 +558,12 @@ __device__ __forceinline__ void attn_body(const PrefillParams& p) {
                desc_kmajor_sw128(kaddr + (kk >> 2) * (kKVHalf / 2) + (kk & 3) * 32), kIdescQK, kk > 0 ? 1u : 0u);
         }
       };
-      auto issue_pv = [&](uint32_t paddr, uint32_t od, int st, bool first) {
+      auto issue_pv = [&](uint32_t ptmem, uint32_t od, int st, bool first) {
         const uint32_t vaddr = smem_u32(smem + kOffKV + st * kStageBytes + kKVHalf);
 #pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk) {  // over the tile's keys in steps of 16
-          umma(od, desc_kmajor_sw128(paddr + kk * 32), desc_mnmajor_sw128(vaddr + kk * 2048, kKVHalf / 2),
-               kIdescPV, (!first || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < kBN / 16; ++kk) {  // over the tile's keys in steps of 16 (8 TMEM columns)
+          umma_tmem_a(od, ptmem + kk * 8, desc_mnmajor_sw128(vaddr + kk * 2048, kKVHalf / 2), kIdescPV,
+                      (!first || kk > 0) ? 1u : 0u);
         }
       };
       // tile sequence; S of tile j goes to S buffer j % 2 of each head
@@ -565,9 +582,9 @@ __device__ __forceinline__ void attn_body(const PrefillParams& p) {
         const int st = j % kStages, st2 = (j + 2) % kStages;
         const bool more = j + 2 < n;
         // head A: P_A(j) V_j; S_A(j+2) into the S buffer softmax A(j) has released
-        if (!wait_or_abort(&p_full[0], (uint32_t)(j & 1), dead, p.err)) break;
+        if (!wait_or_abort(&p_full[j & 1], (uint32_t)((j >> 1) & 1), dead, p.err)) break;
         tc_fence_after();
-        issue_pv(pa, oA, st, j == 0);
+        issue_pv(sA + 64 * (j & 1) + kPCol, oA, st, j == 0);
         umma_commit(&o_done[0]);
         if (!two) umma_commit(&kv_empty[st]);
         if (more) {
@@ -578,9 +595,9 @@ __device__ __forceinline__ void attn_body(const PrefillParams& p) {
         }
         if (two) {
           // head B: P_B(j) V_j (last use of this K/V stage), then S_B(j+2)
-          if (!wait_or_abort(&p_full[1], (uint32_t)(j & 1), dead, p.err)) break;
+          if (!wait_or_abort(&p_full[2 + (j & 1)], (uint32_t)((j >> 1) & 1), dead, p.err)) break;
           tc_fence_after();
-          issue_pv(pbv, oB, st, j == 0);
+          issue_pv(sB + 64 * (j & 1) + kPCol, oB, st, j == 0);
           umma_commit(&o_done[1]);
           umma_commit(&kv_empty[st]);
           if (more) {
@@ -600,7 +617,6 @@ __device__ __forceinline__ void attn_body(const PrefillParams& p) {
     const int q = qt * kBM + row;
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
     const uint32_t tmem_h = tmem + (head_slot ? 256 : 0), tmem_o = tmem_h + 128;
-    uint8_t* pbuf = smem + kOffP + head_slot * kPBytes;
     if (h >= 0) {
       SoftmaxState st{-INFINITY, 0.f};
       const int qbr = kPaged ? 0 : q / p.per, qwr = kPaged ? 0 : q - qbr * p.per, quota = p.quota[h];
@@ -634,19 +650,19 @@ __device__ __forceinline__ void attn_body(const PrefillParams& p) {
             *reinterpret_cast<uint4*>(vb + dh * (kKVHalf / 2) + (first + rem / 8) * 128 + (rem & 7) * 16) =
                 make_uint4(0, 0, 0, 0);
           }
-          // each thread's zeros precede its own P writes, proxy fence and p_full
-          // arrival, and both heads' P.V wait for head A's p_full
+          // each thread's zeros are made visible to the tensor core before its
+          // p_full arrival, and both heads' P.V wait for head A's p_full
+          asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
         }
         if constexpr (kPaged) {
           softmax_tile<true>(p, lim, hole_s - e * kBN, hole_e - e * kBN, row, tmem_h + 64 * (j & 1), tmem_o,
-                             lane_base, pbuf, j, &o_done[head_slot], dead, st);
+                             lane_base, j, &o_done[head_slot], dead, st);
         } else {
-          softmax_tile<false>(p, lim, 0, 0, row, tmem_h + 64 * (j & 1), tmem_o, lane_base, pbuf, j,
+          softmax_tile<false>(p, lim, 0, 0, row, tmem_h + 64 * (j & 1), tmem_o, lane_base, j,
                               &o_done[head_slot], dead, st);
         }
-        asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // P visible to the tensor core
-        tc_fence_before();
-        mbar_arrive_one(&p_full[head_slot]);
+        tc_fence_before();  // P's tcgen05.st completed (wait::st) before the arrival
+        mbar_arrive_one(&p_full[2 * head_slot + (j & 1)]);
       }
       // epilogue
       const bool o_ok = __all_sync(0xffffffffu, wait_or_abort(o_full, 0, dead, p.err));
