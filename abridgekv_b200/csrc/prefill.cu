@@ -149,6 +149,26 @@ __device__ __forceinline__ int tile_limit_fast(const PrefillParams& p, int quota
   return lim < 0 ? 0 : (lim > kBN ? kBN : lim);
 }
 
+// Packed fp32 pairs (sm_100 f32x2 pipes) and a three-input max: fewer issue
+// slots per score in the softmax.
+__device__ __forceinline__ void ffma2(float& d0, float& d1, float a0, float a1, float b, float c) {
+  asm("{\n .reg .b64 x, y, z, r;\n mov.b64 x, {%2, %3};\n mov.b64 y, {%4, %4};\n mov.b64 z, {%5, %5};\n"
+      " fma.rn.f32x2 r, x, y, z;\n mov.b64 {%0, %1}, r;\n}\n"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b), "f"(c));
+}
+__device__ __forceinline__ void fadd2(float& d0, float& d1, float a0, float a1) {
+  asm("{\n .reg .b64 x, y, r;\n mov.b64 x, {%0, %1};\n mov.b64 y, {%2, %3};\n"
+      " add.rn.f32x2 r, x, y;\n mov.b64 {%0, %1}, r;\n}\n"
+      : "+f"(d0), "+f"(d1)
+      : "f"(a0), "f"(a1));
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;\n" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
@@ -295,20 +315,18 @@ __device__ __forceinline__ void softmax_tile(const PrefillParams& p, int lim, in
   float mxa[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // independent chains
   if (full) {
 #pragma unroll
-    for (int i = 0; i < 32; ++i) mxa[i & 3] = fmaxf(mxa[i & 3], fmaxf(t0[i], t1[i]));
+    for (int i = 0; i < 32; ++i) mxa[i & 3] = fmax3(mxa[i & 3], t0[i], t1[i]);
   } else {
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      mxa[i & 3] = fmaxf(mxa[i & 3], vis(i) ? t0[i] : -INFINITY);
-      mxa[i & 3] = fmaxf(mxa[i & 3], vis(i + 32) ? t1[i] : -INFINITY);
-    }
+    for (int i = 0; i < 32; ++i)
+      mxa[i & 3] = fmax3(mxa[i & 3], vis(i) ? t0[i] : -INFINITY, vis(i + 32) ? t1[i] : -INFINITY);
   }
   const float mx = fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3])) * sl2;
   const bool need = mx > st.m_run + kRescaleThreshold || (st.m_run == -INFINITY && mx > -INFINITY);
   const float m_new = need ? mx : st.m_run;
   const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
   const float alpha = need ? fast_exp2(st.m_run - m_use) : 1.f;
-  float rsa[4] = {0.f, 0.f, 0.f, 0.f};
+  float rsa[4][2] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};  // packed pair accumulators
   uint32_t w[8][4];
 #pragma unroll
   for (int half = 0; half < 2; ++half) {
@@ -318,18 +336,22 @@ __device__ __forceinline__ void softmax_tile(const PrefillParams& p, int lim, in
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int c = half * 32 + e8 * 8 + 2 * e;
-        float p0 = fast_exp2(fmaf(t[e8 * 8 + 2 * e], sl2, -m_use));
-        float p1 = fast_exp2(fmaf(t[e8 * 8 + 2 * e + 1], sl2, -m_use));
+        float x0, x1;
+        ffma2(x0, x1, t[e8 * 8 + 2 * e], t[e8 * 8 + 2 * e + 1], sl2, -m_use);
+        float p0 = fast_exp2(x0);
+        float p1 = fast_exp2(x1);
         if (!full) {
           p0 = vis(c) ? p0 : 0.f;
           p1 = vis(c + 1) ? p1 : 0.f;
         }
-        rsa[e] += p0 + p1;
+        fadd2(rsa[e][0], rsa[e][1], p0, p1);
         w[half * 4 + e8][e] = pack_bf16x2(p0, p1);
       }
     }
   }
-  st.l_run = st.l_run * alpha + ((rsa[0] + rsa[1]) + (rsa[2] + rsa[3]));
+  fadd2(rsa[0][0], rsa[0][1], rsa[1][0], rsa[1][1]);
+  fadd2(rsa[2][0], rsa[2][1], rsa[3][0], rsa[3][1]);
+  st.l_run = st.l_run * alpha + ((rsa[0][0] + rsa[0][1]) + (rsa[2][0] + rsa[2][1]));
   st.m_run = m_new;
   // P(j) into the upper half of this tile's S buffer (already read into registers);
   // the buffer's previous P was consumed by P.V(j-2), which completed before S(j)
