@@ -1,0 +1,554 @@
+// Code step: the K code queries of every active request over the paged KV
+// cache, on 5th-generation tensor cores (tcgen05 + TMEM) for sm_100a.
+//
+// Semantics: the noncausal branch of PackedKVSidecar._attend_request_vectorized
+// (third_party/vllm_overlay/vllm/v1/worker/compresslm_packed_kv.py:648-741):
+// request r's queries (rows q_start[r] .. q_start[r] + Kc - 1 of q) attend to
+// rows [0, seq_len) of its block-table row; a KV head with quota q hides its
+// own code slots >= q, i.e. sees rows [0, seq_len - (Kc - q)) (:711-720), and
+// an optional per-request range [start, end) is hidden as well (:721-726).
+// out = softmax(q.k^T * scale + mask) v with an fp32 online softmax.
+//
+// CTA = one 128-row query tile of TWO query heads of the same KV head (both
+// heads share every K/V tile); 64-key tiles; 10 warps:
+//   warp 0      TMA producer: Q of both heads, then the tile's four 16-row page
+//               slices of K and V into a 4-stage ring (cp.async.bulk.tensor,
+//               128B swizzle, no multicast); the block table is read 32 entries
+//               at a time, one lane per slice, the next read in flight
+//   warp 1      TMEM owner (512 columns: per head two S buffers + O); lane 0
+//               issues tcgen05.mma in the order
+//               S_A(0) S_B(0) S_A(1) S_B(1) | PV_A(j) S_A(j+2) PV_B(j) S_B(j+2) | ...
+//                 S  = Q K^T   (A = Q, B = K, both K-major, fp32 in TMEM)
+//                 O += P V     (A = P from TMEM, B = V, MN-major)
+//   warps 2..5  softmax of head A, warps 6..9 softmax of head B: thread = one
+//               TMEM lane = one query row; masked online softmax in fp32, P
+//               (bf16 pairs) stored into the upper half of its own S buffer with
+//               tcgen05.st -- P is double-buffered with S, so a head's softmax of
+//               tile j+1 waits for its P.V of tile j only to rescale O; epilogue
+//               divides by the row sum.  The S MMA of tile j+2 overwrites P(j)
+//               after P.V(j) read it: tcgen05.mma operations of one thread run
+//               in issue order.
+// With all tiles full (no causal diagonal), the double-buffered S keeps the
+// tensor core busier here than the 128-key single-buffer tiling of prefill.cu.
+// Every mbarrier wait is bounded and records ABKV_DEVERR_TIMEOUT on expiry.
+#include <cstring>
+
+#include "tcgen05.cuh"
+
+namespace abkv {
+namespace {
+using namespace tc;
+
+constexpr int kBM = 128, kBN = 64, kD = 128;
+constexpr int kThreads = 320;
+constexpr int kMaxHeads = 128;
+constexpr int kStages = 4;
+constexpr uint32_t kTmemCols = 512;  // per head (A at 0, B at 256): S buffers [0,64) [64,128), O [128,256)
+constexpr uint32_t kPCol = 32;       // P (64 bf16 = 32 columns) lives in columns [32, 64) of its S buffer
+constexpr uint32_t kIdescQK = idesc_bf16_m128(kBN, false);  // S = Q K^T: N = keys, A and B K-major
+constexpr uint32_t kIdescPV = idesc_bf16_m128(kD, true);    // O += P V: N = head_dim, B (V) MN-major
+
+// dynamic shared memory layout (1024-byte aligned pieces for 128B swizzle)
+constexpr int kQBytes = kBM * kD * 2;          // 32 KiB: 2 atoms of [128 rows][128 B]
+constexpr int kKVHalf = kBN * kD * 2;          // 16 KiB: 2 atoms of [64 rows][128 B]
+constexpr int kStageBytes = 2 * kKVHalf;       // K then V
+constexpr int kOffQ = 0;                        // Q_A, Q_B
+constexpr int kOffKV = 2 * kQBytes;
+constexpr int kOffBar = kOffKV + kStages * kStageBytes;
+// mbarriers (u64 slots from kOffBar): q_full, kv_full[kStages], kv_empty[kStages],
+// s_full[head][S buffer], p_full[head][S buffer], o_done[head], o_full, then the TMEM
+// address.  p_full is double-buffered like S: a head's softmax may finish tile j+1
+// before the MMA thread has taken tile j's P, and one barrier per buffer keeps the
+// two arrivals in different barriers (a parity wait cannot tell phases 2 apart).
+constexpr int kBarKvFull = 1, kBarKvEmpty = kBarKvFull + kStages, kBarSFull = kBarKvEmpty + kStages,
+              kBarPFull = kBarSFull + 4, kBarODone = kBarPFull + 4, kBarOFull = kBarODone + 2,
+              kBarTmem = kBarOFull + 1;
+static_assert((kBarTmem + 1) * 8 <= 256, "barrier area");
+constexpr int kOffList = kOffBar + 256;         // visited key tiles (tile indices)
+constexpr int kMaxKeyTiles = 2048;              // keys up to 2048 x 64 = 128K rows
+constexpr int kSmemBytes = kOffList + 4 * kMaxKeyTiles + 16 + 1024;  // + slack for 1024-byte alignment
+// Lazy rescaling: a row keeps its reference maximum until a tile's maximum
+// exceeds it by more than this (log2 units), so P <= 2^8 and O is rescaled
+// only on large jumps (O and the row sum always share the reference).
+constexpr float kRescaleThreshold = 8.f;
+
+struct alignas(64) CodeStepParams {
+  CUtensorMap tm_q, tm_k;  // q [T][H][D]; K/V planes of the paged cache
+  __nv_bfloat16* out;
+  int64_t o_sh, o_ss;
+  int32_t* err;
+  int quota[kMaxHeads];
+  int H, Hkv, G, npairs;
+  float scale_log2;
+  const int32_t* bt;
+  const int32_t* seq_lens;
+  const int32_t* q_start;
+  const int32_t* excl;  // optional [R][2]: rows [start, end) hidden from the code queries
+  int64_t bt_stride, num_blocks;
+  int page, Kc, T, fa_layout;
+};
+
+// Softmax of one (head, key tile) for query row `row` (= TMEM lane):
+// reads S, updates the reference maximum / row sum, waits until the previous
+// P.V of this head has completed (o_done), rescales O when needed and writes
+// P (bf16, 128B-swizzled K-major: 16-byte chunk index ^= row % 8).
+// kHole: columns [hs, he) are hidden as well (the code step's tail exclusion).
+template <bool kHole>
+__device__ __forceinline__ void softmax_tile(const CodeStepParams& p, int lim, int hs, int he, int row,
+                                             uint32_t tmem_s, uint32_t tmem_o, uint32_t lane_base, int j,
+                                             uint64_t* o_done, bool& dead, SoftmaxState& st) {
+  const float sl2 = p.scale_log2;  // lim: visible columns of this row are c < lim
+  float t0[32], t1[32];
+  tmem_ld32(tmem_s + lane_base, t0);
+  tmem_ld32(tmem_s + lane_base + 32, t1);
+  tmem_wait_ld();
+  auto vis = [&](int c) { return c < lim && (!kHole || c < hs || c >= he); };
+  const bool full = lim == kBN && (!kHole || he <= 0 || hs >= kBN);
+  float mxa[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // independent chains
+  if (full) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) mxa[i & 3] = fmax3(mxa[i & 3], t0[i], t1[i]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      mxa[i & 3] = fmax3(mxa[i & 3], vis(i) ? t0[i] : -INFINITY, vis(i + 32) ? t1[i] : -INFINITY);
+  }
+  const float mx = fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3])) * sl2;
+  const bool need = mx > st.m_run + kRescaleThreshold || (st.m_run == -INFINITY && mx > -INFINITY);
+  const float m_new = need ? mx : st.m_run;
+  const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+  const float alpha = need ? fast_exp2(st.m_run - m_use) : 1.f;
+  float rsa[4][2] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};  // packed pair accumulators
+  uint32_t w[8][4];
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    const float* t = half ? t1 : t0;
+#pragma unroll
+    for (int e8 = 0; e8 < 4; ++e8) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int c = half * 32 + e8 * 8 + 2 * e;
+        float x0, x1;
+        ffma2(x0, x1, t[e8 * 8 + 2 * e], t[e8 * 8 + 2 * e + 1], sl2, -m_use);
+        float p0 = fast_exp2(x0);
+        float p1 = fast_exp2(x1);
+        if (!full) {
+          p0 = vis(c) ? p0 : 0.f;
+          p1 = vis(c + 1) ? p1 : 0.f;
+        }
+        fadd2(rsa[e][0], rsa[e][1], p0, p1);
+        w[half * 4 + e8][e] = pack_bf16x2(p0, p1);
+      }
+    }
+  }
+  fadd2(rsa[0][0], rsa[0][1], rsa[1][0], rsa[1][1]);
+  fadd2(rsa[2][0], rsa[2][1], rsa[3][0], rsa[3][1]);
+  st.l_run = st.l_run * alpha + ((rsa[0][0] + rsa[0][1]) + (rsa[2][0] + rsa[2][1]));
+  st.m_run = m_new;
+  // P(j) into the upper half of this tile's S buffer (already read into registers);
+  // the buffer's previous P was consumed by P.V(j-2), which completed before S(j)
+  // was signalled
+  tmem_st32(tmem_s + lane_base + kPCol, reinterpret_cast<const float(&)[32]>(w));
+  if (j > 0 && __any_sync(0xffffffffu, need)) {
+    // O is touched only after the previous P.V of this head completed
+    const bool ok = __all_sync(0xffffffffu, wait_or_abort(o_done, (uint32_t)((j - 1) & 1), dead, p.err));
+    tc_fence_after();
+    if (ok) {
+#pragma unroll 1
+      for (int c4 = 0; c4 < 4; ++c4) {
+        float t[32];
+        tmem_ld32(tmem_o + lane_base + c4 * 32, t);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) t[i] *= alpha;
+        tmem_st32(tmem_o + lane_base + c4 * 32, t);
+      }
+    }
+  }
+  tmem_wait_st();
+}
+
+__global__ void __launch_bounds__(kThreads, 1) codestep_kernel(const __grid_constant__ CodeStepParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  uint64_t* q_full = bar + 0;
+  uint64_t* kv_full = bar + kBarKvFull;    // [kStages]
+  uint64_t* kv_empty = bar + kBarKvEmpty;  // [kStages]
+  uint64_t* s_full = bar + kBarSFull;      // [head][S buffer]
+  uint64_t* p_full = bar + kBarPFull;      // [head][S buffer]
+  uint64_t* o_done = bar + kBarODone;      // [head]: one phase per P.V
+  uint64_t* o_full = bar + kBarOFull;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bar + kBarTmem);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qt = blockIdx.x;  // query tile of the request's code rows
+  const int hk = blockIdx.y / p.npairs, hp = blockIdx.y % p.npairs;
+  const int hA = hk * p.G + 2 * hp;
+  const int hB = (2 * hp + 1 < p.G) ? hA + 1 : -1;  // odd group size: the last pair has one head
+  const int b = blockIdx.z;  // request
+  int kt_end = 0, seq_len = 0, leffA = 0, leffB = 0, hole_s = 0, hole_e = 0;
+  {
+    // every thread reads the same values, so an early return is CTA-uniform and
+    // happens before any barrier, TMEM allocation or copy
+    const int q0 = __ldg(p.q_start + b);
+    if (q0 < 0 || (int64_t)q0 + p.Kc > p.T) {
+      if (threadIdx.x == 0) set_error(p.err, ABKV_DEVERR_RANGE);
+      return;
+    }
+    // trim identity: a head with quota q sees rows [0, seq_len - (Kc - q)) --
+    // its own code slots >= q are the last Kc - q rows of the request
+    int sl = __ldg(p.seq_lens + b);
+    const int64_t cap = min(p.bt_stride * (int64_t)p.page, (int64_t)kMaxKeyTiles * kBN);
+    if (sl < p.Kc || (int64_t)sl > cap) {
+      if (threadIdx.x == 0) set_error(p.err, ABKV_DEVERR_SEQ_OOB);
+      sl = sl < p.Kc ? p.Kc : (int)cap;
+    }
+    seq_len = sl;
+    if (p.excl) {
+      hole_s = __ldg(p.excl + 2 * b);
+      hole_e = __ldg(p.excl + 2 * b + 1);
+      if (hole_s == hole_e) {
+        hole_s = hole_e = 0;  // no exclusion for this request
+      } else if (!(0 <= hole_s && hole_s < hole_e && hole_e <= seq_len - p.Kc)) {
+        if (threadIdx.x == 0) set_error(p.err, ABKV_DEVERR_RANGE);
+        hole_s = hole_e = 0;
+      }
+    }
+    leffA = min(max(seq_len - (p.Kc - p.quota[hA]), 0), seq_len);
+    leffB = hB >= 0 ? min(max(seq_len - (p.Kc - p.quota[hB]), 0), seq_len) : 0;
+    kt_end = (max(leffA, leffB) + kBN - 1) / kBN;
+  }
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+    }
+    for (int i = 0; i < 4; ++i) mbar_init(&s_full[i], 1);
+    for (int i = 0; i < 4; ++i) mbar_init(&p_full[i], 128);
+    mbar_init(&o_done[0], 1);
+    mbar_init(&o_done[1], 1);
+    mbar_init(o_full, 1);
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(s_tmem)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n");
+  }
+  // the visited key tiles, in order, built once by warp 2 (ballot compaction)
+  int32_t* s_list = reinterpret_cast<int32_t*>(smem + kOffList);
+  int32_t* s_nlist = s_list + kMaxKeyTiles;
+  if (warp == 2) {
+    int n = 0;
+    for (int base = 0; base < kt_end; base += 32) {
+      const int kt = base + lane;
+      // tiles entirely inside the exclusion range are skipped for both heads
+      const bool vis = kt < kt_end && !(kt * kBN >= hole_s && kt * kBN + kBN <= hole_e);
+      const uint32_t m = __ballot_sync(0xffffffffu, vis);
+      if (vis) s_list[n + __popc(m & ((1u << lane) - 1u))] = kt;
+      n += __popc(m);
+    }
+    if (lane == 0) *s_nlist = n;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *s_tmem;
+  const int n_tiles = *s_nlist;
+  bool dead = false;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      mbar_expect_tx(q_full, (hB >= 0 ? 2 : 1) * kQBytes);
+      const int qrow = __ldg(p.q_start + b) + qt * kBM;
+      tma_load_4d(smem + kOffQ, &p.tm_q, 0, hA, qrow, 0, q_full);
+      tma_load_4d(smem + kOffQ + kQBytes / 2, &p.tm_q, 64, hA, qrow, 0, q_full);
+      if (hB >= 0) {
+        tma_load_4d(smem + kOffQ + kQBytes, &p.tm_q, 0, hB, qrow, 0, q_full);
+        tma_load_4d(smem + kOffQ + kQBytes + kQBytes / 2, &p.tm_q, 64, hB, qrow, 0, q_full);
+      }
+    }
+    {
+      // The whole warp: lane i holds the page id of 16-row slice i % 4 of tile
+      // j0 + i / 4, so one coalesced block-table read covers 8 tiles and the
+      // next batch's read is in flight while this batch's copies are issued.
+      // Slices past seq_len (or with an invalid page id) are not loaded; their
+      // V rows are zero-filled by the softmax warps.
+      auto slice_page = [&](int j0) -> int {
+        const int j = j0 + (lane >> 2);
+        if (j >= n_tiles) return -1;
+        const int row0 = s_list[j] * kBN + 16 * (lane & 3);
+        if (row0 >= seq_len) return -1;
+        const int v = __ldg(p.bt + (int64_t)b * p.bt_stride + row0 / p.page);
+        if (v < 0 || (int64_t)v >= p.num_blocks) {
+          set_error(p.err, ABKV_DEVERR_PAGE_OOB);
+          return -1;
+        }
+        return v;
+      };
+      int cur = slice_page(0);
+      bool stop = false;
+      for (int j0 = 0; j0 < n_tiles && !stop; j0 += 8) {
+        const int nxt = slice_page(j0 + 8);
+        for (int jj = 0; jj < 8 && j0 + jj < n_tiles; ++jj) {
+          const int j = j0 + jj, st = j % kStages;
+          const int kt = s_list[j];
+          const int pg = __shfl_sync(0xffffffffu, cur, 4 * jj + (lane & 3));  // lanes 0..3: slices 0..3
+          const uint32_t valid = __ballot_sync(0xffffffffu, pg >= 0) & 0xFu;
+          bool ok = true;
+          if (lane == 0) {
+            ok = wait_or_abort(&kv_empty[st], (uint32_t)(((j / kStages) & 1) ^ 1), dead, p.err);
+            if (ok) mbar_expect_tx(&kv_full[st], (uint32_t)__popc(valid) * 4u * 2048u);
+          }
+          if (!__shfl_sync(0xffffffffu, ok, 0)) {
+            stop = true;
+            break;
+          }
+          if (lane < 4 && pg >= 0) {
+            uint8_t* kbuf = smem + kOffKV + st * kStageBytes + lane * 2048;
+            const int off = (kt * kBN + 16 * lane) % p.page;
+            const int pk = p.fa_layout ? pg : 2 * pg;
+            const int pv = p.fa_layout ? pg + (int)p.num_blocks : 2 * pg + 1;
+            tma_load_4d(kbuf, &p.tm_k, 0, hk, off, pk, &kv_full[st]);
+            tma_load_4d(kbuf + kKVHalf / 2, &p.tm_k, 64, hk, off, pk, &kv_full[st]);
+            tma_load_4d(kbuf + kKVHalf, &p.tm_k, 0, hk, off, pv, &kv_full[st]);
+            tma_load_4d(kbuf + kKVHalf + kKVHalf / 2, &p.tm_k, 64, hk, off, pv, &kv_full[st]);
+          }
+        }
+        cur = nxt;
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      const bool two = hB >= 0;
+      wait_or_abort(q_full, 0, dead, p.err);
+      const uint32_t qa = smem_u32(smem + kOffQ), qbv = qa + kQBytes;
+      const uint32_t sA = tmem, oA = tmem + 128, sB = tmem + 256, oB = tmem + 384;
+      auto issue_s = [&](uint32_t qaddr, uint32_t sd, int st) {
+        const uint32_t kaddr = smem_u32(smem + kOffKV + st * kStageBytes);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {  // over head_dim in steps of 16
+          umma(sd, desc_kmajor_sw128(qaddr + (kk >> 2) * (kQBytes / 2) + (kk & 3) * 32),
+               desc_kmajor_sw128(kaddr + (kk >> 2) * (kKVHalf / 2) + (kk & 3) * 32), kIdescQK, kk > 0 ? 1u : 0u);
+        }
+      };
+      auto issue_pv = [&](uint32_t ptmem, uint32_t od, int st, bool first) {
+        const uint32_t vaddr = smem_u32(smem + kOffKV + st * kStageBytes + kKVHalf);
+#pragma unroll
+        for (int kk = 0; kk < kBN / 16; ++kk) {  // over the tile's keys in steps of 16 (8 TMEM columns)
+          umma_tmem_a(od, ptmem + kk * 8, desc_mnmajor_sw128(vaddr + kk * 2048, kKVHalf / 2), kIdescPV,
+                      (!first || kk > 0) ? 1u : 0u);
+        }
+      };
+      // tile sequence; S of tile j goes to S buffer j % 2 of each head
+      const int n = n_tiles;
+      for (int t = 0; t < 2 && t < n && !dead; ++t) {
+        if (!wait_or_abort(&kv_full[t], 0, dead, p.err)) break;
+        tc_fence_after();
+        issue_s(qa, sA + 64 * t, t);
+        umma_commit(&s_full[t]);
+        if (two) {
+          issue_s(qbv, sB + 64 * t, t);
+          umma_commit(&s_full[2 + t]);
+        }
+      }
+      for (int j = 0; j < n && !dead; ++j) {
+        const int st = j % kStages, st2 = (j + 2) % kStages;
+        const bool more = j + 2 < n;
+        // head A: P_A(j) V_j; S_A(j+2) into the S buffer softmax A(j) has released
+        if (!wait_or_abort(&p_full[j & 1], (uint32_t)((j >> 1) & 1), dead, p.err)) break;
+        tc_fence_after();
+        issue_pv(sA + 64 * (j & 1) + kPCol, oA, st, j == 0);
+        umma_commit(&o_done[0]);
+        if (!two) umma_commit(&kv_empty[st]);
+        if (more) {
+          if (!wait_or_abort(&kv_full[st2], (uint32_t)(((j + 2) / kStages) & 1), dead, p.err)) break;
+          tc_fence_after();
+          issue_s(qa, sA + 64 * (j & 1), st2);
+          umma_commit(&s_full[j & 1]);
+        }
+        if (two) {
+          // head B: P_B(j) V_j (last use of this K/V stage), then S_B(j+2)
+          if (!wait_or_abort(&p_full[2 + (j & 1)], (uint32_t)((j >> 1) & 1), dead, p.err)) break;
+          tc_fence_after();
+          issue_pv(sB + 64 * (j & 1) + kPCol, oB, st, j == 0);
+          umma_commit(&o_done[1]);
+          umma_commit(&kv_empty[st]);
+          if (more) {
+            issue_s(qbv, sB + 64 * (j & 1), st2);
+            umma_commit(&s_full[2 + (j & 1)]);
+          }
+        }
+      }
+      umma_commit(o_full);
+    }
+  } else {
+    // ---------------- softmax / correction / epilogue ----------------
+    const int head_slot = (warp - 2) >> 2;          // 0: head A (warps 2..5), 1: head B (warps 6..9)
+    const int h = head_slot ? hB : hA;
+    const int quarter = warp & 3;                    // TMEM lane quarter this warp may access
+    const int row = quarter * 32 + lane;             // query row within the tile
+    const int q = qt * kBM + row;
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    const uint32_t tmem_h = tmem + (head_slot ? 256 : 0), tmem_o = tmem_h + 128;
+    if (h >= 0) {
+      SoftmaxState st{-INFINITY, 0.f};
+      const int leff = head_slot ? leffB : leffA;
+      for (int j = 0; j < n_tiles; ++j) {
+        const int e = s_list[j];
+        const int lim = min(max(leff - e * kBN, 0), kBN);
+        // warp-uniform decision: tcgen05.ld is a warp-collective
+        const bool ok = __all_sync(
+            0xffffffffu, wait_or_abort(&s_full[2 * head_slot + (j & 1)], (uint32_t)((j >> 1) & 1), dead, p.err));
+        if (!ok) {
+          dead = true;
+          break;
+        }
+        tc_fence_after();
+        if (head_slot == 0 && e * kBN + kBN > seq_len) {
+          // V rows at or past seq_len (stale page slots or unloaded slices) become
+          // zeros before either head's P.V reads them (P is 0 there, but 0 * NaN
+          // would not be)
+          const int first = max(seq_len - e * kBN, 0);
+          uint8_t* vb = smem + kOffKV + (j % kStages) * kStageBytes + kKVHalf;
+          const int wt = (warp - 2) * 32 + lane;
+          for (int idx = wt; idx < 2 * (kBN - first) * 8; idx += 128) {
+            const int dh = idx / ((kBN - first) * 8), rem = idx - dh * (kBN - first) * 8;
+            *reinterpret_cast<uint4*>(vb + dh * (kKVHalf / 2) + (first + rem / 8) * 128 + (rem & 7) * 16) =
+                make_uint4(0, 0, 0, 0);
+          }
+          // each thread's zeros are made visible to the tensor core before its
+          // p_full arrival, and both heads' P.V wait for head A's p_full
+          asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+        }
+        softmax_tile<true>(p, lim, hole_s - e * kBN, hole_e - e * kBN, row, tmem_h + 64 * (j & 1), tmem_o,
+                           lane_base, j, &o_done[head_slot], dead, st);
+        tc_fence_before();  // P's tcgen05.st completed (wait::st) before the arrival
+        mbar_arrive_one(&p_full[2 * head_slot + (j & 1)]);
+      }
+      // epilogue
+      const bool o_ok = __all_sync(0xffffffffu, wait_or_abort(o_full, 0, dead, p.err));
+      tc_fence_after();
+      if (o_ok) {
+        // a row that saw no visible key (possible in the code step when the
+        // quota and the exclusion hide everything) is written as zeros
+        const bool none = !(st.l_run > 0.f);
+        const float inv = none ? 0.f : 1.f / st.l_run;
+        __nv_bfloat16* orow = p.out + (int64_t)(__ldg(p.q_start + b) + q) * p.o_ss + (int64_t)h * p.o_sh;
+#pragma unroll 1
+        for (int c4 = 0; c4 < 4; ++c4) {
+          float t[32];
+          tmem_ld32(tmem_o + lane_base + c4 * 32, t);
+          tmem_wait_ld();
+          if (none) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) t[i] = 0.f;
+          }
+#pragma unroll
+          for (int v8 = 0; v8 < 4; ++v8) {
+            uint4 pk;
+            pk.x = pack_bf16x2(t[v8 * 8 + 0] * inv, t[v8 * 8 + 1] * inv);
+            pk.y = pack_bf16x2(t[v8 * 8 + 2] * inv, t[v8 * 8 + 3] * inv);
+            pk.z = pack_bf16x2(t[v8 * 8 + 4] * inv, t[v8 * 8 + 5] * inv);
+            pk.w = pack_bf16x2(t[v8 * 8 + 6] * inv, t[v8 * 8 + 7] * inv);
+            *reinterpret_cast<uint4*>(orow + c4 * 32 + v8 * 8) = pk;
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(kTmemCols));
+  }
+}
+
+}  // namespace
+}  // namespace abkv
+
+using namespace abkv;
+
+extern "C" int abkv_code_step_attention(const void* q, int64_t q_row_stride, int64_t q_head_stride, void* out,
+                                        int64_t out_row_stride, int64_t out_head_stride, const int32_t* q_start,
+                                        const void* kv_cache, int kv_layout, int64_t num_blocks, int page_size,
+                                        const int32_t* block_table, int64_t bt_stride, const int32_t* seq_lens,
+                                        const int32_t* excluded, const int32_t* quota_per_kv_head, int R, int Hq,
+                                        int Hkv, int head_dim, int K_code, int T, float scale, void* workspace,
+                                        size_t workspace_bytes, void* stream) {
+  if (!q || !out || !q_start || !kv_cache || !block_table || !seq_lens || !quota_per_kv_head)
+    return ABKV_ERR_INVALID_ARG;
+  if (R <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv != 0 || T <= 0 || num_blocks <= 0 || bt_stride <= 0 ||
+      !(scale > 0.f) || (kv_layout != 0 && kv_layout != 1))
+    return ABKV_ERR_INVALID_ARG;
+  if (head_dim != kD || Hq > kMaxHeads || R > 65535 || K_code <= 0 || K_code % kBM || page_size <= 0 ||
+      page_size % 16 || 2 * num_blocks > INT32_MAX || K_code > T)
+    return ABKV_ERR_UNSUPPORTED;
+  if (q_row_stride <= 0 || q_head_stride <= 0 || out_row_stride % 8 || out_head_stride % 8 ||
+      out_row_stride <= 0 || out_head_stride <= 0)
+    return ABKV_ERR_INVALID_ARG;
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(kv_cache)) &
+      15)
+    return ABKV_ERR_INVALID_ARG;
+  if (!workspace || workspace_bytes < 256 || (reinterpret_cast<uintptr_t>(workspace) & 255))
+    return ABKV_ERR_WORKSPACE;
+  CodeStepParams prm;
+  std::memset(&prm, 0, sizeof(prm));
+  {
+    const cuuint64_t dims[4] = {(cuuint64_t)kD, (cuuint64_t)Hq, (cuuint64_t)T, 1};
+    const cuuint64_t gstr[3] = {(cuuint64_t)q_head_stride * 2, (cuuint64_t)q_row_stride * 2,
+                                (cuuint64_t)q_row_stride * 2 * (cuuint64_t)T};
+    const cuuint32_t box[4] = {64, 1, (cuuint32_t)kBM, 1};
+    const int st = tc::encode_tiled_4d(&prm.tm_q, q, dims, gstr, box);
+    if (st != ABKV_OK) return st;
+  }
+  {
+    // K and V planes of the paged cache as one 4D tensor: (dim, kv head, page
+    // row, plane) with plane = 2 * block + {0, 1} (FlashInfer) or
+    // {0, num_blocks} + block (FlashAttention); both have the same strides
+    const cuuint64_t row = (cuuint64_t)Hkv * kD * 2;
+    const cuuint64_t dims[4] = {(cuuint64_t)kD, (cuuint64_t)Hkv, (cuuint64_t)page_size, (cuuint64_t)(2 * num_blocks)};
+    const cuuint64_t gstr[3] = {(cuuint64_t)kD * 2, row, row * (cuuint64_t)page_size};
+    const cuuint32_t box[4] = {64, 1, 16, 1};
+    const int st = tc::encode_tiled_4d(&prm.tm_k, kv_cache, dims, gstr, box);
+    if (st != ABKV_OK) return st;
+  }
+  prm.out = static_cast<__nv_bfloat16*>(out);
+  prm.o_sh = out_head_stride;
+  prm.o_ss = out_row_stride;
+  prm.err = static_cast<int32_t*>(workspace);
+  const int G = Hq / Hkv;
+  for (int h = 0; h < Hq; ++h) {
+    const int qq = quota_per_kv_head[h / G];
+    if (qq < 0 || qq > K_code) return ABKV_ERR_INVALID_ARG;
+    prm.quota[h] = qq;
+  }
+  prm.H = Hq;
+  prm.Hkv = Hkv;
+  prm.G = G;
+  prm.npairs = (G + 1) / 2;
+  prm.scale_log2 = scale * 1.4426950408889634f;
+  prm.bt = block_table;
+  prm.seq_lens = seq_lens;
+  prm.q_start = q_start;
+  prm.excl = excluded;
+  prm.bt_stride = bt_stride;
+  prm.num_blocks = num_blocks;
+  prm.page = page_size;
+  prm.Kc = K_code;
+  prm.T = T;
+  prm.fa_layout = kv_layout;
+  if (Hkv * prm.npairs > 65535) return ABKV_ERR_UNSUPPORTED;
+  if (cudaFuncSetAttribute(codestep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) !=
+      cudaSuccess)
+    return ABKV_ERR_CUDA;
+  dim3 grid(K_code / kBM, Hkv * prm.npairs, R);
+  codestep_kernel<<<grid, kThreads, kSmemBytes, reinterpret_cast<cudaStream_t>(stream)>>>(prm);
+  if (cudaGetLastError() != cudaSuccess) return ABKV_ERR_CUDA;
+  return ABKV_OK;
+}
