@@ -41,7 +41,7 @@
 namespace abkv {
 namespace {
 
-constexpr int kD = 128;
+constexpr int kD = 128;  // largest head_dim (64 and 128 are compiled); buffers are sized for it
 constexpr int kTile = 16;
 constexpr int kWarps = 8;                  // consumer warps
 constexpr int kThreads = (kWarps + 1) * 32;  // + producer warp
@@ -139,10 +139,11 @@ __device__ __forceinline__ void consumer_sync() {
   asm volatile("bar.sync 1, %0;\n" ::"n"(kConsumerThreads) : "memory");
 }
 
+template <int D>
 __device__ __forceinline__ void store_out(const DecodeParams& p, const LayerArgs& L, int b, int hr, int d,
                                           float val) {
   const GatherArgs& g = p.gather;
-  __nv_bfloat16* dst = L.out + (int64_t)b * g.out_row + (int64_t)(g.head0 + hr) * kD + d;
+  __nv_bfloat16* dst = L.out + (int64_t)b * g.out_row + (int64_t)(g.head0 + hr) * D + d;
   const __nv_bfloat16 v = __float2bfloat16(val);
   for (int r = 0; r < g.world; ++r) dst[g.peer_delta[r]] = v;
 }
@@ -190,6 +191,7 @@ __device__ void gather_barrier(const DecodeParams& p) {
 }
 
 // ---------------------------------------------------------------------------
+template <int D>
 __device__ void producer(const DecodeParams& p, uint8_t* smem) {
   StageMeta* meta = reinterpret_cast<StageMeta*>(smem + kOffMeta);
   int32_t* s_pages = reinterpret_cast<int32_t*>(smem + kOffPages);
@@ -197,8 +199,8 @@ __device__ void producer(const DecodeParams& p, uint8_t* smem) {
   uint64_t* empty = full + kStages;
   const int lane = threadIdx.x & 31;
   const int Hkv = p.Hkv, P = p.P, nsub = kWarps / Hkv;
-  const int tile_half = kTile * Hkv * kD * 2;
-  const int64_t row_elems = (int64_t)Hkv * kD;
+  const int tile_half = kTile * Hkv * D * 2;
+  const int64_t row_elems = (int64_t)Hkv * D;
   const int64_t half_elems = (int64_t)P * row_elems;
   const int64_t page_elems = 2 * half_elems;
   const int lb_items = p.nl * p.B;
@@ -302,6 +304,9 @@ __device__ void producer(const DecodeParams& p, uint8_t* smem) {
 }
 
 // ---------------------------------------------------------------------------
+// D = head_dim: the Q.K^T product runs over D / 32 chunks of 32 dims (8 per lane),
+// P.V over D / 64 halves of 64 dims, O^T in D / 16 accumulator tiles.
+template <int D>
 __device__ void consumer(const DecodeParams& p, uint8_t* smem) {
   const StageMeta* meta = reinterpret_cast<const StageMeta*>(smem + kOffMeta);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kOffBar);
@@ -315,13 +320,14 @@ __device__ void consumer(const DecodeParams& p, uint8_t* smem) {
   const int Hkv = p.Hkv, G = p.G;
   const int h = warp % Hkv, sub = warp / Hkv, nsub = kWarps / Hkv;
   const int g = lane >> 2, c = lane & 3;
-  const int row_bytes = Hkv * kD * 2;
+  const int row_bytes = Hkv * D * 2;
   const int tile_half = kTile * row_bytes;
   const float sl2 = p.scale_log2;
+  constexpr int kQC = D / 32, kVH = D / 64, kOT = D / 16;
 
-  float o[8][4];
+  float o[kOT][4];
   float m_run = -INFINITY, l_run = 0.f;
-  uint32_t qr[4][4];
+  uint32_t qr[kQC][4];
 
   for (int gq = 0;; ++gq) {
     const int st = gq % kStages;
@@ -334,12 +340,12 @@ __device__ void consumer(const DecodeParams& p, uint8_t* smem) {
     const LayerArgs& L = p.layer[M.li];
     if (M.bits & kFirst) {
 #pragma unroll
-      for (int mt = 0; mt < 8; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+      for (int mt = 0; mt < kOT; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
       m_run = -INFINITY;
       l_run = 0.f;
-      const __nv_bfloat16* qrow = L.q + ((int64_t)M.b * p.Hq + h * G + g) * kD + 8 * c;
+      const __nv_bfloat16* qrow = L.q + ((int64_t)M.b * p.Hq + h * G + g) * D + 8 * c;
 #pragma unroll
-      for (int m = 0; m < 4; ++m) {
+      for (int m = 0; m < kQC; ++m) {
         uint4 v = make_uint4(0, 0, 0, 0);
         if (g < G) v = __ldg(reinterpret_cast<const uint4*>(qrow + 32 * m));
         qr[m][0] = v.x; qr[m][1] = v.y; qr[m][2] = v.z; qr[m][3] = v.w;
@@ -349,7 +355,7 @@ __device__ void consumer(const DecodeParams& p, uint8_t* smem) {
       const bool ok = (M.bits >> sub) & 1;
       const int tok0 = (M.t0 + sub) * kTile;
       const int seq_len = M.seq_len;
-      const uint8_t* kb = smem + kOffStage + (size_t)st * kStageBytes + (size_t)sub * 2 * tile_half + h * kD * 2;
+      const uint8_t* kb = smem + kOffStage + (size_t)st * kStageBytes + (size_t)sub * 2 * tile_half + h * D * 2;
       const uint8_t* vb = kb + tile_half;
 
       // S = Q.K^T : rows = query heads (g < G real), cols = tokens 8nt + 2c + {0,1}
@@ -358,16 +364,16 @@ __device__ void consumer(const DecodeParams& p, uint8_t* smem) {
       for (int nt = 0; nt < 2; ++nt) {
         const int T = 8 * nt + g;
         const bool valid = ok && (tok0 + T < seq_len);
-        uint32_t kr[4][4];
+        uint32_t kr[kQC][4];
 #pragma unroll
-        for (int m = 0; m < 4; ++m) {
+        for (int m = 0; m < kQC; ++m) {
           uint4 v = make_uint4(0, 0, 0, 0);
           if (valid) v = lds128(kb + T * row_bytes + (32 * m + 8 * c) * 2);
           kr[m][0] = v.x; kr[m][1] = v.y; kr[m][2] = v.z; kr[m][3] = v.w;
         }
         s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
 #pragma unroll
-        for (int m = 0; m < 4; ++m) {
+        for (int m = 0; m < kQC; ++m) {
           mma_bf16_16816(s[nt], qr[m][0], 0u, qr[m][1], 0u, kr[m][0], kr[m][1]);
           mma_bf16_16816(s[nt], qr[m][2], 0u, qr[m][3], 0u, kr[m][2], kr[m][3]);
         }
@@ -400,7 +406,7 @@ __device__ void consumer(const DecodeParams& p, uint8_t* smem) {
       const float a0 = __shfl_sync(0xffffffffu, alpha, 8 * c);
       const float a1 = __shfl_sync(0xffffffffu, alpha, 8 * c + 4);
 #pragma unroll
-      for (int mt = 0; mt < 8; ++mt) {
+      for (int mt = 0; mt < kOT; ++mt) {
         o[mt][0] *= a0; o[mt][1] *= a1; o[mt][2] *= a0; o[mt][3] *= a1;
       }
       const uint32_t pb0 = pack_bf16x2(pr[0][0], pr[0][1]);
@@ -408,7 +414,7 @@ __device__ void consumer(const DecodeParams& p, uint8_t* smem) {
 
       // V rows 2c, 2c+1, 2c+8, 2c+9 (zero when masked: 0 * NaN would poison O)
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
+      for (int hh = 0; hh < kVH; ++hh) {
         uint32_t vr[4][4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -439,7 +445,7 @@ __device__ void consumer(const DecodeParams& p, uint8_t* smem) {
       const int head = 2 * c + jh;
       if (head < G) {
 #pragma unroll
-        for (int mt = 0; mt < 8; ++mt) {
+        for (int mt = 0; mt < kOT; ++mt) {
           const int hh = mt >> 2, i = mt & 3;
           const int d = 8 * g + 64 * hh + 2 * i;
           s_o[warp][head][d] = o[mt][jh];
@@ -452,12 +458,12 @@ __device__ void consumer(const DecodeParams& p, uint8_t* smem) {
       s_l[warp][g] = lq;
     }
     consumer_sync();
-    const int items = p.Hq * kD;
+    const int items = p.Hq * D;
     const int n_chunks = M.n_chunks;
     const int64_t lb = (int64_t)(p.layer_base + M.li) * p.B + M.b;  // (layer, sequence) slot
     const int64_t prow = (lb * p.max_chunks + M.chunk) * p.Hq;
     for (int it = threadIdx.x; it < items; it += kConsumerThreads) {
-      const int d = it % kD, hr = it / kD;
+      const int d = it % D, hr = it / D;
       const int kh = hr / G, r = hr % G;
       float Mx = -INFINITY;
       for (int s2 = 0; s2 < nsub; ++s2) Mx = fmaxf(Mx, s_m[s2 * Hkv + kh][r]);
@@ -471,9 +477,9 @@ __device__ void consumer(const DecodeParams& p, uint8_t* smem) {
       }
       const float val = Ls > 0.f ? Os / Ls : 0.f;
       if (n_chunks == 1) {
-        store_out(p, L, M.b, hr, d, val);
+        store_out<D>(p, L, M.b, hr, d, val);
       } else {
-        p.part_o[(prow + hr) * kD + d] = val;
+        p.part_o[(prow + hr) * D + d] = val;
         if (d == 0) p.part_lse[prow + hr] = Ls > 0.f ? Mu + log2f(Ls) : -INFINITY;
       }
     }
@@ -490,7 +496,7 @@ __device__ void consumer(const DecodeParams& p, uint8_t* smem) {
         __threadfence();
         const int64_t row0 = lb * p.max_chunks * p.Hq;
         for (int it = threadIdx.x; it < items; it += kConsumerThreads) {
-          const int d = it % kD, hr = it / kD;
+          const int d = it % D, hr = it / D;
           float Mx = -INFINITY;
           for (int ch = 0; ch < n_chunks; ++ch)
             Mx = fmaxf(Mx, __ldcg(p.part_lse + row0 + (int64_t)ch * p.Hq + hr));
@@ -500,9 +506,9 @@ __device__ void consumer(const DecodeParams& p, uint8_t* smem) {
             const int64_t rr = row0 + (int64_t)ch * p.Hq + hr;
             const float f = exp2f(__ldcg(p.part_lse + rr) - Mu);
             Ls += f;
-            Os += f * __ldcg(p.part_o + rr * kD + d);
+            Os += f * __ldcg(p.part_o + rr * D + d);
           }
-          store_out(p, L, M.b, hr, d, Ls > 0.f ? Os / Ls : 0.f);
+          store_out<D>(p, L, M.b, hr, d, Ls > 0.f ? Os / Ls : 0.f);
         }
         if (threadIdx.x == 0) p.counters[lb] = 0;  // ready for the next call on this workspace
       }
@@ -511,6 +517,7 @@ __device__ void consumer(const DecodeParams& p, uint8_t* smem) {
   }
 }
 
+template <int D>
 __global__ void __launch_bounds__(kThreads, 1) decode_split_kernel(const __grid_constant__ DecodeParams p) {
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kOffBar);
@@ -523,9 +530,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_split_kernel(const __grid_
   }
   __syncthreads();
   if ((threadIdx.x >> 5) == kWarps) {
-    producer(p, smem);
+    producer<D>(p, smem);
   } else {
-    consumer(p, smem);
+    consumer<D>(p, smem);
   }
   if (p.gather.my_flags) {
     __threadfence_system();  // this thread's output stores, to every rank
@@ -556,7 +563,7 @@ int plan_decode(int num_layers, int num_seqs, int num_q_heads, int head_dim, int
                 int max_pages, int chunk_tokens, DecodePlan* plan) {
   if (num_layers <= 0 || num_seqs <= 0 || num_q_heads <= 0 || page_size <= 0 || max_pages <= 0)
     return ABKV_ERR_INVALID_ARG;
-  if (head_dim != kD || page_size % kTile != 0) return ABKV_ERR_UNSUPPORTED;
+  if ((head_dim != 64 && head_dim != kD) || page_size % kTile != 0) return ABKV_ERR_UNSUPPORTED;
   const int page_tiles = page_size / kTile;
   const int64_t max_tiles = (int64_t)max_pages * page_tiles;
   if (max_tiles > (1 << 26)) return ABKV_ERR_UNSUPPORTED;
@@ -574,7 +581,7 @@ int plan_decode(int num_layers, int num_seqs, int num_q_heads, int head_dim, int
   if (plan->max_chunks > 1) {
     const size_t rows = (size_t)num_layers * num_seqs * plan->max_chunks * num_q_heads;
     plan->counter_bytes = ((size_t)num_layers * num_seqs * sizeof(int32_t) + 255) / 256 * 256;
-    plan->part_o_bytes = rows * kD * sizeof(float);
+    plan->part_o_bytes = rows * head_dim * sizeof(float);
     plan->part_lse_bytes = ((rows * sizeof(float)) + 255) / 256 * 256;
   } else {
     plan->counter_bytes = plan->part_o_bytes = plan->part_lse_bytes = 0;
@@ -630,7 +637,8 @@ int launch_decode(const void* const* q, const void* const* kv, const int32_t* co
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   char* ws = static_cast<char*>(workspace);
   // opt in to > 48 KiB of dynamic shared memory (idempotent, per device)
-  if (cudaFuncSetAttribute(decode_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  auto kernel = head_dim == 64 ? decode_split_kernel<64> : decode_split_kernel<kD>;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)kSmemBytes) != cudaSuccess)
     return ABKV_ERR_CUDA;
   int dev = 0, num_sms = 0;
@@ -675,7 +683,7 @@ int launch_decode(const void* const* q, const void* const* kv, const int32_t* co
     prm.nl = nl;
     prm.num_items = plan.max_chunks * nl * num_seqs;
     const int grid = prm.num_items < num_sms ? prm.num_items : num_sms;
-    decode_split_kernel<<<grid, kThreads, kSmemBytes, s>>>(prm);
+    kernel<<<grid, kThreads, kSmemBytes, s>>>(prm);
   }
   if (cudaGetLastError() != cudaSuccess) return ABKV_ERR_CUDA;
   return ABKV_OK;
@@ -692,7 +700,7 @@ extern "C" int abkv_decode(const void* const* q, const void* const* kv,
                            void* stream) {
   GatherArgs g;
   memset(&g, 0, sizeof(g));
-  g.out_row = (int64_t)num_q_heads * kD;
+  g.out_row = (int64_t)num_q_heads * head_dim;
   g.world = 1;
   return launch_decode(q, kv, block_tables, bt_strides, seq_lens, num_blocks, out, num_layers, num_seqs,
                        num_q_heads, num_kv_heads, head_dim, page_size, max_pages_per_seq, scale, chunk_tokens,
@@ -716,7 +724,7 @@ extern "C" int abkv_decode_gather(const void* const* q, const void* const* kv,
   // every layer's output slot [num_seqs][hq_total][D] lies in this rank's buffer
   // after the flag area (the same offsets are written in the peers' buffers)
   const char* base = static_cast<const char*>(a.rank_buffers[a.rank]);
-  const size_t slot = (size_t)num_seqs * a.hq_total * kD * 2;
+  const size_t slot = (size_t)num_seqs * a.hq_total * head_dim * 2;
   for (int l = 0; l < num_layers; ++l) {
     const char* o = static_cast<const char*>(out[l]);
     if (!o || o < base + ABKV_GATHER_FLAG_BYTES || o + slot > base + a.buffer_bytes ||
@@ -730,7 +738,7 @@ extern "C" int abkv_decode_gather(const void* const* q, const void* const* kv,
     g.peer_flags[r] = static_cast<uint32_t*>(a.rank_buffers[r]);
   }
   g.my_flags = static_cast<uint32_t*>(a.rank_buffers[a.rank]);
-  g.out_row = (int64_t)a.hq_total * kD;
+  g.out_row = (int64_t)a.hq_total * head_dim;
   g.world = a.world;
   g.rank = a.rank;
   g.head0 = a.rank * num_q_heads;

@@ -52,22 +52,28 @@ namespace abkv {
 namespace {
 using namespace tc;
 
-constexpr int kBM = 128, kBN = 128, kD = 128;
+constexpr int kBM = 128, kBN = 128;  // head_dim D is 64 or 128 (template parameter)
 constexpr int kThreads = 320;
 constexpr int kMaxHeads = 128;
 constexpr int kStages = 2;
-constexpr uint32_t kTmemCols = 512;  // per head (A at 0, B at 256): S/P [0,128), O [128,256)
+constexpr uint32_t kTmemCols = 512;  // per head (A at 0, B at 256): S/P [0,128), O [128,128+D)
 constexpr uint32_t kPCol = 64;       // P (128 bf16 = 64 columns) lives in columns [64, 128) of the S buffer
 constexpr uint32_t kIdescQK = idesc_bf16_m128(kBN, false);  // S = Q K^T: N = keys, A and B K-major
-constexpr uint32_t kIdescPV = idesc_bf16_m128(kD, true);    // O += P V: N = head_dim, B (V) MN-major
-
-// dynamic shared memory layout (1024-byte aligned pieces for 128B swizzle)
-constexpr int kQBytes = kBM * kD * 2;          // 32 KiB: 2 atoms of [128 rows][128 B]
-constexpr int kKVHalf = kBN * kD * 2;          // 32 KiB: 2 atoms of [128 rows][128 B]
-constexpr int kStageBytes = 2 * kKVHalf;       // K then V
 constexpr int kOffQ = 0;                        // Q_A, Q_B
-constexpr int kOffKV = 2 * kQBytes;
-constexpr int kOffBar = kOffKV + kStages * kStageBytes;
+
+// Dynamic shared memory layout for head_dim D (1024-byte aligned pieces for
+// 128B swizzle): a [rows][D] bf16 tile is D / 64 atom columns of [rows][128 B].
+template <int D>
+struct Layout {
+  static constexpr int kAtoms = D / 64;
+  static constexpr int kQBytes = kBM * D * 2;        // per head
+  static constexpr int kKVHalf = kBN * D * 2;        // K or V tile
+  static constexpr int kStageBytes = 2 * kKVHalf;    // K then V
+  static constexpr int kOffKV = 2 * kQBytes;
+  static constexpr int kOffBar = kOffKV + kStages * kStageBytes;
+  static constexpr int kOffList = kOffBar + 256;     // visited key tiles: (kb << 16) | kw0, per key tile
+  static constexpr uint32_t kIdescPV = idesc_bf16_m128(D, true);  // O += P V: N = D, B (V) MN-major
+};
 // mbarriers (u64 slots from kOffBar): q_full, kv_full[kStages], kv_empty[kStages],
 // s_full[head], p_full[head], o_full, then the TMEM address.  A head's softmax of
 // tile j+1 needs S(j+1), which is issued only after the MMA thread took P(j), so
@@ -75,9 +81,9 @@ constexpr int kOffBar = kOffKV + kStages * kStageBytes;
 constexpr int kBarKvFull = 1, kBarKvEmpty = kBarKvFull + kStages, kBarSFull = kBarKvEmpty + kStages,
               kBarPFull = kBarSFull + 2, kBarOFull = kBarPFull + 2, kBarTmem = kBarOFull + 1;
 static_assert((kBarTmem + 1) * 8 <= 256, "barrier area");
-constexpr int kOffList = kOffBar + 256;         // visited key tiles: (kb << 16) | kw0, per key tile
 constexpr int kMaxKeyTiles = 1024;              // keys up to 1024 x 128 = 128K rows
-constexpr int kSmemBytes = kOffList + 4 * kMaxKeyTiles + 16 + 1024;  // + slack for 1024-byte alignment
+template <int D>
+constexpr int smem_bytes() { return Layout<D>::kOffList + 4 * kMaxKeyTiles + 16 + 1024; }  // + alignment slack
 // Lazy rescaling: a row keeps its reference maximum until a tile's maximum
 // exceeds it by more than this (log2 units), so P <= 2^8 and O is rescaled
 // only on large jumps (O and the row sum always share the reference).
@@ -151,6 +157,7 @@ __device__ __forceinline__ int tile_limit_fast(const PrefillParams& p, int quota
 // registers before a P store can overwrite it.  P = 2^(s * scale * log2(e) - m)
 // against a lazily updated reference maximum m; O and the row sum are rescaled
 // when m moves (rescale_ok: O holds earlier tiles, none of them in flight).
+template <int D>
 __device__ __forceinline__ void softmax_tile(const PrefillParams& p, int lim, uint32_t tmem_s, uint32_t tmem_o,
                                              bool rescale_ok, SoftmaxState& st) {
   const float sl2 = p.scale_log2;  // lim: visible columns of this row are c < lim
@@ -180,7 +187,7 @@ __device__ __forceinline__ void softmax_tile(const PrefillParams& p, int lim, ui
   const float alpha = need ? fast_exp2(st.m_run - m_use) : 1.f;
   if (rescale_ok && __any_sync(0xffffffffu, need)) {
 #pragma unroll 1
-    for (int c4 = 0; c4 < 4; ++c4) {
+    for (int c4 = 0; c4 < D / 32; ++c4) {
       float t[32];
       tmem_ld32(tmem_o + c4 * 32, t);
       tmem_wait_ld();
@@ -230,7 +237,12 @@ __device__ __forceinline__ bool visit_tile(const PrefillParams& p, int hA, int h
   return tile_class(p, hA, qt, kt, pl) != 0 || (hB >= 0 && tile_class(p, hB, qt, kt, pl) != 0);
 }
 
+template <int D>
 __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_constant__ PrefillParams p) {
+  using LY = Layout<D>;
+  constexpr int kQBytes = LY::kQBytes, kKVHalf = LY::kKVHalf, kStageBytes = LY::kStageBytes;
+  constexpr int kOffKV = LY::kOffKV, kOffBar = LY::kOffBar, kOffList = LY::kOffList, kAtoms = LY::kAtoms;
+  constexpr uint32_t kIdescPV = LY::kIdescPV;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kOffBar);
@@ -297,11 +309,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
     // ---------------- TMA producer ----------------
     if (lane == 0) {
       mbar_expect_tx(q_full, (hB >= 0 ? 2 : 1) * kQBytes);
-      tma_load_4d(smem + kOffQ, &p.tm_q, 0, qt * kBM, hA, b, q_full);
-      tma_load_4d(smem + kOffQ + kQBytes / 2, &p.tm_q, 64, qt * kBM, hA, b, q_full);
-      if (hB >= 0) {
-        tma_load_4d(smem + kOffQ + kQBytes, &p.tm_q, 0, qt * kBM, hB, b, q_full);
-        tma_load_4d(smem + kOffQ + kQBytes + kQBytes / 2, &p.tm_q, 64, qt * kBM, hB, b, q_full);
+      for (int a = 0; a < kAtoms; ++a) {
+        tma_load_4d(smem + kOffQ + a * (kQBytes / kAtoms), &p.tm_q, 64 * a, qt * kBM, hA, b, q_full);
+        if (hB >= 0)
+          tma_load_4d(smem + kOffQ + kQBytes + a * (kQBytes / kAtoms), &p.tm_q, 64 * a, qt * kBM, hB, b, q_full);
       }
       for (int j = 0; j < n_tiles; ++j) {
         const int e = s_list[j];
@@ -310,10 +321,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         if (!wait_or_abort(&kv_empty[st], (uint32_t)(((j / kStages) & 1) ^ 1), dead, p.err)) break;
         uint8_t* kbuf = smem + kOffKV + st * kStageBytes;
         mbar_expect_tx(&kv_full[st], kStageBytes);
-        tma_load_4d(kbuf, &p.tm_k, 0, k0, hk, b, &kv_full[st]);
-        tma_load_4d(kbuf + kKVHalf / 2, &p.tm_k, 64, k0, hk, b, &kv_full[st]);
-        tma_load_4d(kbuf + kKVHalf, &p.tm_v, 0, k0, hk, b, &kv_full[st]);
-        tma_load_4d(kbuf + kKVHalf + kKVHalf / 2, &p.tm_v, 64, k0, hk, b, &kv_full[st]);
+        for (int a = 0; a < kAtoms; ++a) {
+          tma_load_4d(kbuf + a * (kKVHalf / kAtoms), &p.tm_k, 64 * a, k0, hk, b, &kv_full[st]);
+          tma_load_4d(kbuf + kKVHalf + a * (kKVHalf / kAtoms), &p.tm_v, 64 * a, k0, hk, b, &kv_full[st]);
+        }
       }
     }
   } else if (warp == 1) {
@@ -326,16 +337,17 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
       auto issue_s = [&](uint32_t qaddr, uint32_t sd, int st) {
         const uint32_t kaddr = smem_u32(smem + kOffKV + st * kStageBytes);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {  // over head_dim in steps of 16
-          umma(sd, desc_kmajor_sw128(qaddr + (kk >> 2) * (kQBytes / 2) + (kk & 3) * 32),
-               desc_kmajor_sw128(kaddr + (kk >> 2) * (kKVHalf / 2) + (kk & 3) * 32), kIdescQK, kk > 0 ? 1u : 0u);
+        for (int kk = 0; kk < D / 16; ++kk) {  // over head_dim in steps of 16 (4 per atom column)
+          umma(sd, desc_kmajor_sw128(qaddr + (kk >> 2) * (kQBytes / kAtoms) + (kk & 3) * 32),
+               desc_kmajor_sw128(kaddr + (kk >> 2) * (kKVHalf / kAtoms) + (kk & 3) * 32), kIdescQK,
+               kk > 0 ? 1u : 0u);
         }
       };
       auto issue_pv = [&](uint32_t ptmem, uint32_t od, int st, bool first) {
         const uint32_t vaddr = smem_u32(smem + kOffKV + st * kStageBytes + kKVHalf);
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk) {  // over the tile's keys in steps of 16 (8 TMEM columns)
-          umma_tmem_a(od, ptmem + kk * 8, desc_mnmajor_sw128(vaddr + kk * 2048, kKVHalf / 2), kIdescPV,
+          umma_tmem_a(od, ptmem + kk * 8, desc_mnmajor_sw128(vaddr + kk * 2048, kKVHalf / kAtoms), kIdescPV,
                       (!first || kk > 0) ? 1u : 0u);
         }
       };
@@ -402,7 +414,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
           break;
         }
         tc_fence_after();
-        softmax_tile(p, lim, tmem_h + lane_base, tmem_o + lane_base, j > 0, st);
+        softmax_tile<D>(p, lim, tmem_h + lane_base, tmem_o + lane_base, j > 0, st);
         tc_fence_before();  // P's tcgen05.st completed (wait::st) before the arrival
         mbar_arrive_one(&p_full[head_slot]);
       }
@@ -414,7 +426,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         const float inv = none ? 0.f : 1.f / st.l_run;
         __nv_bfloat16* orow = p.out + (int64_t)b * p.o_sb + (int64_t)h * p.o_sh + (int64_t)q * p.o_ss;
 #pragma unroll 1
-        for (int c4 = 0; c4 < 4; ++c4) {
+        for (int c4 = 0; c4 < D / 32; ++c4) {
           float t[32];
           tmem_ld32(tmem_o + lane_base + c4 * 32, t);
           tmem_wait_ld();
@@ -448,10 +460,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
 }
 
 // ---------------------------------------------------------------------------
-// [B][heads][S][128] bf16 with element strides (sb, sh, ss) -> 4D tensor map,
+// [B][heads][S][D] bf16 with element strides (sb, sh, ss) -> 4D tensor map,
 // box = 64 dims x box_rows rows, 128B swizzle.
-int make_map(CUtensorMap* m, const void* base, int B, int heads, int S, const int64_t* strides, int box_rows) {
-  const cuuint64_t dims[4] = {(cuuint64_t)kD, (cuuint64_t)S, (cuuint64_t)heads, (cuuint64_t)B};
+int make_map(CUtensorMap* m, const void* base, int B, int heads, int S, int D, const int64_t* strides,
+             int box_rows) {
+  const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)S, (cuuint64_t)heads, (cuuint64_t)B};
   const cuuint64_t gstr[3] = {(cuuint64_t)strides[2] * 2, (cuuint64_t)strides[1] * 2, (cuuint64_t)strides[0] * 2};
   const cuuint32_t box[4] = {64, (cuuint32_t)box_rows, 1, 1};
   return tc::encode_tiled_4d(m, base, dims, gstr, box);
@@ -470,7 +483,7 @@ extern "C" int abkv_prefill_masked(const void* q, const int64_t* q_strides, cons
                                    void* workspace, size_t workspace_bytes, void* stream) {
   if (!q || !k || !v || !out || !q_strides || !k_strides || !v_strides || !out_strides) return ABKV_ERR_INVALID_ARG;
   if (B <= 0 || H <= 0 || Hkv <= 0 || S <= 0 || H % Hkv != 0 || !(scale > 0.f)) return ABKV_ERR_INVALID_ARG;
-  if (head_dim != kD || H > kMaxHeads || B > 65535) return ABKV_ERR_UNSUPPORTED;
+  if ((head_dim != 64 && head_dim != 128) || H > kMaxHeads || B > 65535) return ABKV_ERR_UNSUPPORTED;
   if (C <= 0 || K_layout <= 0 || C % kBM || K_layout % kBM || S % (C + K_layout)) return ABKV_ERR_UNSUPPORTED;
   if (S / kBN > kMaxKeyTiles || C + K_layout > 65535) return ABKV_ERR_UNSUPPORTED;
   if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) |
@@ -481,9 +494,9 @@ extern "C" int abkv_prefill_masked(const void* q, const int64_t* q_strides, cons
     return ABKV_ERR_WORKSPACE;
   PrefillParams prm;
   std::memset(&prm, 0, sizeof(prm));
-  int st = make_map(&prm.tm_q, q, B, H, S, q_strides, kBM);
-  if (st == ABKV_OK) st = make_map(&prm.tm_k, k, B, Hkv, S, k_strides, kBN);
-  if (st == ABKV_OK) st = make_map(&prm.tm_v, v, B, Hkv, S, v_strides, kBN);
+  int st = make_map(&prm.tm_q, q, B, H, S, head_dim, q_strides, kBM);
+  if (st == ABKV_OK) st = make_map(&prm.tm_k, k, B, Hkv, S, head_dim, k_strides, kBN);
+  if (st == ABKV_OK) st = make_map(&prm.tm_v, v, B, Hkv, S, head_dim, v_strides, kBN);
   if (st != ABKV_OK) return st;
   prm.out = static_cast<__nv_bfloat16*>(out);
   prm.o_sb = out_strides[0];
@@ -508,12 +521,14 @@ extern "C" int abkv_prefill_masked(const void* q, const int64_t* q_strides, cons
   prm.per = C + K_layout;
   prm.n_qtiles = S / kBM;
   prm.scale_log2 = scale * 1.4426950408889634f;
-  if (cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) !=
+  auto kernel = head_dim == 64 ? prefill_kernel<64> : prefill_kernel<128>;
+  const int smem = head_dim == 64 ? smem_bytes<64>() : smem_bytes<128>();
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
       cudaSuccess)
     return ABKV_ERR_CUDA;
   if (Hkv * prm.npairs > 65535) return ABKV_ERR_UNSUPPORTED;
   dim3 grid(prm.n_qtiles, Hkv * prm.npairs, B);
-  prefill_kernel<<<grid, kThreads, kSmemBytes, reinterpret_cast<cudaStream_t>(stream)>>>(prm);
+  kernel<<<grid, kThreads, smem, reinterpret_cast<cudaStream_t>(stream)>>>(prm);
   if (cudaGetLastError() != cudaSuccess) return ABKV_ERR_CUDA;
   return ABKV_OK;
 }

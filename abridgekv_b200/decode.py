@@ -26,9 +26,6 @@ import torch
 from . import _lib
 from .workspace import Workspace, default_workspace
 
-HEAD_DIM = 128
-
-
 def _check_cuda(name: str, t: torch.Tensor, dtype: torch.dtype | None = None) -> None:
     if not isinstance(t, torch.Tensor) or not t.is_cuda:
         raise TypeError(f"{name} must be a CUDA tensor (libabkv has no CPU path)")

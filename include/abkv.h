@@ -86,7 +86,7 @@ int abkv_workspace_error(void* workspace, void* stream, int32_t* host_error);
  * device pointers (q, kv, block_tables, seq_lens, out) or host integers
  * (bt_strides, num_blocks).
  *
- * Supported: head_dim 128; num_kv_heads in {1,2,4,8}; group size
+ * Supported: head_dim 64 or 128; num_kv_heads in {1,2,4,8}; group size
  * num_q_heads/num_kv_heads in 1..8; page_size a multiple of 16;
  * max_pages_per_seq >= every ceil(seq_len/page_size) (it bounds the launch
  * grid).  chunk_tokens = tokens per split-KV work item (0 = automatic; else
@@ -326,7 +326,7 @@ int abkv_gather_rows(const void* const* src, void* const* dst, int num_tensors,
  * contiguous [B][H][S] f32, natural log.  Sequence layout: blocks of
  * [C content | K_layout code rows]; quota_per_head: HOST [H] code quota of each
  * query head (NULL = K_layout); prompt_len: DEVICE [B] raw prompt lengths
- * (NULL = none).  Supported: head_dim 128, C and K_layout multiples of 128,
+ * (NULL = none).  Supported: head_dim 64 or 128, C and K_layout multiples of 128,
  * S a multiple of C + K_layout, H <= 128, H % Hkv == 0.
  * ====================================================================== */
 int abkv_prefill_masked(const void* q, const int64_t* q_strides, const void* k,

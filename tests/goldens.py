@@ -34,10 +34,11 @@ def load_prefill(name: str):
     z = dict(np.load(GOLDEN / f"prefill_{name}.npz"))
     B, H, Hkv = int(z["B"]), int(z["H"]), int(z["Hkv"])
     S0 = int(z["N"]) * (int(z["C"]) + int(z["K"]))
-    q, k, v = prefill_inputs(int(z["seed"]), B, H, Hkv, S0)
+    D = int(z["D"]) if "D" in z else 128
+    q, k, v = prefill_inputs(int(z["seed"]), B, H, Hkv, S0, D)
     mask = np.unpackbits(z["mask_bits"])[: B * H * S0 * S0].reshape(B, H, S0, S0).astype(bool)
     pl = z["prompt_len"] if z["prompt_len"].size else None
-    return dict(B=B, H=H, Hkv=Hkv, S0=S0, C=int(z["C"]), K=int(z["K"]), quota=z["quota_per_head"], prompt_len=pl,
+    return dict(B=B, H=H, Hkv=Hkv, S0=S0, D=D, C=int(z["C"]), K=int(z["K"]), quota=z["quota_per_head"], prompt_len=pl,
                 q=q, k=k, v=v, mask=mask, rows=z["rows"], out_rows=z["out_rows"], lse=z["lse"])
 
 

@@ -40,6 +40,7 @@ def test_decode_workspace_size():
     n = lib.abkv_decode_workspace_size(36, 64, 32, 128, 16, 544, 0)
     assert n > 0 and n % 256 == 0
     assert lib.abkv_decode_workspace_size(36, 64, 32, 96, 16, 544, 0) == 0   # head_dim 96 unsupported
+    assert lib.abkv_decode_workspace_size(2, 1, 4, 64, 16, 128, 0) > 0      # head_dim 64 (config 1)
     assert lib.abkv_decode_workspace_size(36, 64, 32, 128, 8, 544, 0) == 0   # page 8 unsupported
     assert lib.abkv_decode_workspace_size(1, 1, 8, 128, 16, 1, 0) == 256     # single chunk: header only
 

@@ -33,7 +33,7 @@ def test_prefill_matches_reference_flex_and_oracle(name):
     assert ws.read_error() == 0
     got = out.float().cpu().numpy()
     assert np.isfinite(got).all()
-    ref64, lse64 = masked_attention(g["q"], g["k"], g["v"], g["mask"], 1.0 / np.sqrt(128))
+    ref64, lse64 = masked_attention(g["q"], g["k"], g["v"], g["mask"], 1.0 / np.sqrt(g["D"]))
     err = np.abs(got - ref64)
     print(f"{name}: max|gpu-f64|={err.max():.3e} mean={err.mean():.3e}")
     assert err.max() <= ATOL and err.mean() <= MEAN

@@ -16,7 +16,7 @@ def test_oracle_mask_matches_reference(name):
 @pytest.mark.parametrize("name", prefill_cases())
 def test_oracle_attention_matches_reference_flex(name):
     g = load_prefill(name)
-    out, lse = masked_attention(g["q"], g["k"], g["v"], g["mask"], 1.0 / np.sqrt(128))
+    out, lse = masked_attention(g["q"], g["k"], g["v"], g["mask"], 1.0 / np.sqrt(g["D"]))
     assert np.abs(out[:, :, g["rows"], :] - g["out_rows"]).max() < 1e-4
     assert np.abs(lse - g["lse"]).max() < 1e-4
 
