@@ -32,6 +32,13 @@ class GatherT(C.Structure):
                 ("rank", C.c_int), ("hq_total", C.c_int), ("epoch", C.c_uint32), ("timeout_us", C.c_uint32)]
 
 
+class SidecarT(C.Structure):
+    """abkv_sidecar_t."""
+    _fields_ = [("pages", C.c_void_p), ("page_table", C.c_void_p), ("page_count", C.c_void_p),
+                ("page_table_stride", C.c_int64), ("num_pages", C.c_int64), ("slots", C.c_int),
+                ("quotas", C.c_int * 8)]
+
+
 # name -> (restype, argtypes); must mirror include/abkv.h exactly.
 SIGNATURES: dict[str, tuple] = {
     "abkv_status_string": (C.c_char_p, [c_int]),
@@ -49,6 +56,12 @@ SIGNATURES: dict[str, tuple] = {
          c_int, c_int, C.c_float, c_int, c_vp, c_vp],
     ),
     "abkv_decode_gather": (
+        c_int,
+        [c_vpp, c_vpp, c_vpp, c_i64p, c_vpp, c_i64p, c_vpp, c_int, c_int, c_int, c_int, c_int,
+         c_int, c_int, C.c_float, c_int, c_vp, c_vp, c_size, c_vp],
+    ),
+    "abkv_decode_packed_workspace_size": (c_size, [c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_i64]),
+    "abkv_decode_packed": (
         c_int,
         [c_vpp, c_vpp, c_vpp, c_i64p, c_vpp, c_i64p, c_vpp, c_int, c_int, c_int, c_int, c_int,
          c_int, c_int, C.c_float, c_int, c_vp, c_vp, c_size, c_vp],

@@ -46,7 +46,7 @@ constexpr int kTile = 16;
 constexpr int kWarps = 8;                  // consumer warps
 constexpr int kThreads = (kWarps + 1) * 32;  // + producer warp
 constexpr int kConsumerThreads = kWarps * 32;
-constexpr int kMaxLayers = 56;       // layers per launch: keeps params < 4 KB
+constexpr int kMaxLayers = 56;       // layers per launch (kernel parameters ~9.7 KB)
 constexpr int kMaxChunkPages = 512;  // page ids staged per work item
 constexpr int kMaxG = 8;             // query heads per KV head
 constexpr int kStages = 3;
@@ -60,6 +60,16 @@ struct LayerArgs {
   __nv_bfloat16* out;
   int64_t bt_stride;
   int64_t num_blocks;
+  // Packed sidecar of per-head code quotas (null side = none): page i of a
+  // request holds, for KV head h, slots [side_off[h], side_off[h] + side_q[h])
+  // of a [2][side_slots][D] page; a head's keys are its slots of every sidecar
+  // page of the request (in page order), then the main rows.
+  const __nv_bfloat16* side;
+  const int32_t* side_bt;     // [B][side_bt_stride] page ids into `side`
+  const int32_t* side_count;  // [B] sidecar pages of each request
+  int64_t side_bt_stride, side_num_pages;
+  int side_slots, side_qmax;
+  int side_off[kWarps], side_q[kWarps];
 };
 
 // Output placement.  Row (b, h) of a layer goes to out + b * out_row + (head0 + h) * D
@@ -95,11 +105,15 @@ struct DecodeParams {
   int num_items;
 };
 
+// A group is either main tiles (16 rows x all KV heads; ok bit per tile) or
+// sidecar tiles (16 slots of one KV head; ok bit per (tile, head) pair, and
+// seq_len holds the request's sidecar page count).
 struct StageMeta {
-  int li, b, chunk, n_chunks, seq_len, t0, ntiles, bits;  // bits: ok mask | kFirst | kLast
+  int li, b, chunk, n_chunks, seq_len, t0, ntiles, bits;  // bits: ok mask | kFirst | kLast | kSide
 };
 constexpr int kFirst = 1 << 8;
 constexpr int kLast = 1 << 9;
+constexpr int kSide = 1 << 10;
 
 // Dynamic shared memory layout.
 constexpr size_t kOffStage = 0;
@@ -121,6 +135,15 @@ __device__ __forceinline__ int clamp_seq_len(const DecodeParams& p, const LayerA
     s = s < 0 ? 0 : (int)cap;
   }
   return s;
+}
+
+__device__ __forceinline__ int clamp_side_count(const DecodeParams& p, const LayerArgs& L, int b, bool report) {
+  int c = __ldg(L.side_count + b);
+  if (c < 0 || (int64_t)c > L.side_bt_stride) {
+    if (report) set_error(p.err, ABKV_DEVERR_SEQ_OOB);
+    c = c < 0 ? 0 : (int)L.side_bt_stride;
+  }
+  return c;
 }
 
 __device__ __forceinline__ uint4 lds128(const void* ptr) {
@@ -208,7 +231,7 @@ __device__ void producer(const DecodeParams& p, uint8_t* smem) {
   bool alive = true;
 
   while (alive) {
-    int li = -1, b = 0, chunk = 0, nch = 0, slen = 0;
+    int li = -1, b = 0, chunk = 0, nch = 0, slen = 0, nside = 0, scount = 0;
     if (lane == 0) {
       for (;;) {
         const int i = atomicAdd(p.work, 1);
@@ -217,9 +240,14 @@ __device__ void producer(const DecodeParams& p, uint8_t* smem) {
         const int rem = i - chunk * lb_items;
         li = rem / p.B;
         b = rem - li * p.B;
-        slen = clamp_seq_len(p, p.layer[li], b, chunk == 0);
+        const LayerArgs& L = p.layer[li];
+        slen = clamp_seq_len(p, L, b, chunk == 0);
+        scount = L.side ? clamp_side_count(p, L, b, chunk == 0) : 0;
+        // chunks [0, nside) cover the sidecar rows, the rest the main rows
         const int ntl = (slen + kTile - 1) / kTile;
-        nch = max(1, (ntl + p.chunk_tiles - 1) / p.chunk_tiles);
+        const int stl = (scount * (L.side ? L.side_qmax : 0) + kTile - 1) / kTile;
+        nside = (stl + p.chunk_tiles - 1) / p.chunk_tiles;
+        nch = max(1, nside + (ntl + p.chunk_tiles - 1) / p.chunk_tiles);
         if (chunk < nch) break;
         li = -1;
       }
@@ -230,9 +258,68 @@ __device__ void producer(const DecodeParams& p, uint8_t* smem) {
     chunk = __shfl_sync(0xffffffffu, chunk, 0);
     nch = __shfl_sync(0xffffffffu, nch, 0);
     slen = __shfl_sync(0xffffffffu, slen, 0);
+    nside = __shfl_sync(0xffffffffu, nside, 0);
+    scount = __shfl_sync(0xffffffffu, scount, 0);
     const LayerArgs& L = p.layer[li];
+    if (chunk < nside) {
+      // ---- sidecar item: lane i < nsub * Hkv owns (tile sub = i / Hkv, head h = i % Hkv) of a
+      // group; a tile is 16 consecutive slots of one head (quotas are multiples of 16, so
+      // they lie in one page); heads whose slots ran out are masked
+      const int stl = (scount * L.side_qmax + kTile - 1) / kTile;
+      const int tile0 = chunk * p.chunk_tiles;
+      const int tile1 = min(tile0 + p.chunk_tiles, stl);
+      const int ntiles = max(0, tile1 - tile0);
+      const int ngroups = max(1, (ntiles + nsub - 1) / nsub);
+      const int head_tile = kTile * D * 2;
+      for (int grp = 0; grp < ngroups; ++grp, ++gq) {
+        const int st = gq % kStages;
+        const int tg0 = tile0 + grp * nsub;
+        const int nt = max(0, min(nsub, tile1 - tg0));
+        int64_t src = -1;
+        const int sub = lane / Hkv, hh = lane % Hkv;
+        if (lane < nsub * Hkv && sub < nt) {
+          const int row0 = (tg0 + sub) * kTile, qh = L.side_q[hh];
+          if (row0 < scount * qh) {
+            const int pi = row0 / qh;
+            const int64_t pid = __ldg(L.side_bt + (int64_t)b * L.side_bt_stride + pi);
+            if (pid >= 0 && pid < L.side_num_pages) {
+              src = (pid * 2 * L.side_slots + L.side_off[hh] + row0 % qh) * D;
+            } else {
+              set_error(p.err, ABKV_DEVERR_PAGE_OOB);
+            }
+          }
+        }
+        const uint32_t okmask = __ballot_sync(0xffffffffu, src >= 0) & ((1u << (nsub * Hkv)) - 1u);
+        if (lane == 0) {
+          const uint32_t k = (uint32_t)(gq / kStages);
+          if (!mbar_wait(&empty[st], (k & 1u) ^ 1u)) {
+            set_error(p.err, ABKV_DEVERR_TIMEOUT);
+            alive = false;
+          }
+        }
+        alive = __shfl_sync(0xffffffffu, alive ? 1 : 0, 0) != 0;
+        if (!alive) break;
+        if (lane == 0) {
+          StageMeta m;
+          m.li = li; m.b = b; m.chunk = chunk; m.n_chunks = nch; m.seq_len = scount;
+          m.t0 = tg0; m.ntiles = nt;
+          m.bits = (int)okmask | kSide | (grp == 0 ? kFirst : 0) | (grp == ngroups - 1 ? kLast : 0);
+          meta[st] = m;
+          mbar_expect_tx(&full[st], (uint32_t)__popc(okmask) * 2u * (uint32_t)head_tile);
+        }
+        __syncwarp();  // the expected byte count is posted before any copy can complete
+        if (src >= 0) {
+          uint8_t* dst = smem + kOffStage + (size_t)st * kStageBytes + (size_t)sub * 2 * tile_half +
+                         (size_t)hh * head_tile;
+          bulk_g2s(dst, L.side + src, (uint32_t)head_tile, &full[st]);
+          bulk_g2s(dst + tile_half, L.side + src + (int64_t)L.side_slots * D, (uint32_t)head_tile, &full[st]);
+        }
+      }
+      continue;
+    }
+    // ---- main item: tiles of 16 rows x all KV heads through the block table
     const int ntl = (slen + kTile - 1) / kTile;
-    const int tile0 = chunk * p.chunk_tiles;
+    const int tile0 = (chunk - nside) * p.chunk_tiles;
     const int tile1 = min(tile0 + p.chunk_tiles, ntl);
     const int ntiles = max(0, tile1 - tile0);
     const int page0 = tile0 * kTile / P;
@@ -352,10 +439,15 @@ __device__ void consumer(const DecodeParams& p, uint8_t* smem) {
       }
     }
     if (sub < M.ntiles) {
-      const bool ok = (M.bits >> sub) & 1;
+      // main tile: row T of KV head h at T * row_bytes + h * D * 2, rows < seq_len;
+      // sidecar tile: this head's 16 slots at h * 16 * D * 2, rows < pages * quota_h
+      const bool side_grp = (M.bits & kSide) != 0;
+      const bool ok = (M.bits >> (side_grp ? sub * Hkv + h : sub)) & 1;
       const int tok0 = (M.t0 + sub) * kTile;
-      const int seq_len = M.seq_len;
-      const uint8_t* kb = smem + kOffStage + (size_t)st * kStageBytes + (size_t)sub * 2 * tile_half + h * D * 2;
+      const int seq_len = side_grp ? M.seq_len * L.side_q[h] : M.seq_len;
+      const int rstride = side_grp ? D * 2 : row_bytes;
+      const uint8_t* kb = smem + kOffStage + (size_t)st * kStageBytes + (size_t)sub * 2 * tile_half +
+                          (side_grp ? h * kTile * D * 2 : h * D * 2);
       const uint8_t* vb = kb + tile_half;
 
       // S = Q.K^T : rows = query heads (g < G real), cols = tokens 8nt + 2c + {0,1}
@@ -368,7 +460,7 @@ __device__ void consumer(const DecodeParams& p, uint8_t* smem) {
 #pragma unroll
         for (int m = 0; m < kQC; ++m) {
           uint4 v = make_uint4(0, 0, 0, 0);
-          if (valid) v = lds128(kb + T * row_bytes + (32 * m + 8 * c) * 2);
+          if (valid) v = lds128(kb + T * rstride + (32 * m + 8 * c) * 2);
           kr[m][0] = v.x; kr[m][1] = v.y; kr[m][2] = v.z; kr[m][3] = v.w;
         }
         s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
@@ -420,7 +512,7 @@ __device__ void consumer(const DecodeParams& p, uint8_t* smem) {
         for (int i = 0; i < 4; ++i) {
           const int T = 2 * c + (i & 1) + 8 * (i >> 1);
           uint4 v = make_uint4(0, 0, 0, 0);
-          if (ok && (tok0 + T < seq_len)) v = lds128(vb + T * row_bytes + (64 * hh + 8 * g) * 2);
+          if (ok && (tok0 + T < seq_len)) v = lds128(vb + T * rstride + (64 * hh + 8 * g) * 2);
           vr[i][0] = v.x; vr[i][1] = v.y; vr[i][2] = v.z; vr[i][3] = v.w;
         }
 #pragma unroll
@@ -559,17 +651,21 @@ struct DecodePlan {
 
 constexpr size_t kWsHeader = 256;
 
+// max_side_rows: an upper bound of the sidecar rows of one (layer, request, head)
+// (sidecar pages x largest quota), 0 without a sidecar.
 int plan_decode(int num_layers, int num_seqs, int num_q_heads, int head_dim, int page_size,
-                int max_pages, int chunk_tokens, DecodePlan* plan) {
+                int max_pages, int chunk_tokens, int64_t max_side_rows, DecodePlan* plan) {
   if (num_layers <= 0 || num_seqs <= 0 || num_q_heads <= 0 || page_size <= 0 || max_pages <= 0)
     return ABKV_ERR_INVALID_ARG;
   if ((head_dim != 64 && head_dim != kD) || page_size % kTile != 0) return ABKV_ERR_UNSUPPORTED;
   const int page_tiles = page_size / kTile;
   const int64_t max_tiles = (int64_t)max_pages * page_tiles;
-  if (max_tiles > (1 << 26)) return ABKV_ERR_UNSUPPORTED;
+  if (max_side_rows < 0) return ABKV_ERR_INVALID_ARG;
+  const int64_t side_tiles = (max_side_rows + kTile - 1) / kTile;
+  if (max_tiles > (1 << 26) || side_tiles > (1 << 26)) return ABKV_ERR_UNSUPPORTED;
   int ct;
   if (chunk_tokens == 0) {
-    ct = auto_chunk_tiles(num_layers, num_seqs, (int)max_tiles, page_tiles);
+    ct = auto_chunk_tiles(num_layers, num_seqs, (int)(max_tiles + side_tiles), page_tiles);
   } else {
     if (chunk_tokens < 0 || chunk_tokens % kTile || chunk_tokens % page_size) return ABKV_ERR_INVALID_ARG;
     ct = chunk_tokens / kTile;
@@ -577,7 +673,7 @@ int plan_decode(int num_layers, int num_seqs, int num_q_heads, int head_dim, int
   if (ct * kTile / page_size > kMaxChunkPages - 1) return ABKV_ERR_UNSUPPORTED;
   plan->chunk_tiles = ct;
   plan->max_tiles = (int)max_tiles;
-  plan->max_chunks = (int)((max_tiles + ct - 1) / ct);
+  plan->max_chunks = (int)((max_tiles + ct - 1) / ct + (side_tiles + ct - 1) / ct);
   if (plan->max_chunks > 1) {
     const size_t rows = (size_t)num_layers * num_seqs * plan->max_chunks * num_q_heads;
     plan->counter_bytes = ((size_t)num_layers * num_seqs * sizeof(int32_t) + 255) / 256 * 256;
@@ -600,7 +696,7 @@ extern "C" size_t abkv_decode_workspace_size(int num_layers, int num_seqs, int n
                                              int chunk_tokens) {
   DecodePlan plan;
   if (plan_decode(num_layers, num_seqs, num_q_heads, head_dim, page_size, max_pages_per_seq,
-                  chunk_tokens, &plan) != ABKV_OK)
+                  chunk_tokens, 0, &plan) != ABKV_OK)
     return 0;
   return plan.total;
 }
@@ -611,7 +707,8 @@ int launch_decode(const void* const* q, const void* const* kv, const int32_t* co
                   const int64_t* bt_strides, const int32_t* const* seq_lens, const int64_t* num_blocks,
                   void* const* out, int num_layers, int num_seqs, int num_q_heads, int num_kv_heads,
                   int head_dim, int page_size, int max_pages_per_seq, float scale, int chunk_tokens,
-                  void* workspace, size_t workspace_bytes, void* stream, const GatherArgs& gather) {
+                  void* workspace, size_t workspace_bytes, void* stream, const GatherArgs& gather,
+                  const abkv_sidecar_t* sidecars = nullptr) {
   if (!q || !kv || !block_tables || !bt_strides || !seq_lens || !num_blocks || !out)
     return ABKV_ERR_INVALID_ARG;
   if (num_kv_heads <= 0 || num_q_heads % num_kv_heads != 0) return ABKV_ERR_INVALID_ARG;
@@ -620,9 +717,31 @@ int launch_decode(const void* const* q, const void* const* kv, const int32_t* co
   if (G > kMaxG) return ABKV_ERR_UNSUPPORTED;
   if (num_seqs > 65535) return ABKV_ERR_UNSUPPORTED;
   if (!(scale > 0.f)) return ABKV_ERR_INVALID_ARG;
+  // sidecars: per layer, pages == NULL means none; quotas multiples of 16 in [16, 2^16)
+  int64_t max_side_rows = 0;
+  if (sidecars) {
+    for (int l = 0; l < num_layers; ++l) {
+      const abkv_sidecar_t& sc = sidecars[l];
+      if (!sc.pages) continue;
+      if (!sc.page_table || !sc.page_count || sc.page_table_stride <= 0 || sc.num_pages <= 0)
+        return ABKV_ERR_INVALID_ARG;
+      if ((reinterpret_cast<uintptr_t>(sc.pages) & 15) || (reinterpret_cast<uintptr_t>(sc.page_table) & 3))
+        return ABKV_ERR_INVALID_ARG;
+      int sum = 0, qmax = 0;
+      for (int h = 0; h < num_kv_heads; ++h) {
+        const int qh = sc.quotas[h];
+        if (qh <= 0 || qh % kTile || qh >= (1 << 16)) return ABKV_ERR_UNSUPPORTED;
+        sum += qh;
+        qmax = qh > qmax ? qh : qmax;
+      }
+      if (sum != sc.slots) return ABKV_ERR_INVALID_ARG;
+      const int64_t rows = sc.page_table_stride * qmax;
+      max_side_rows = rows > max_side_rows ? rows : max_side_rows;
+    }
+  }
   DecodePlan plan;
   int st = plan_decode(num_layers, num_seqs, num_q_heads, head_dim, page_size, max_pages_per_seq,
-                       chunk_tokens, &plan);
+                       chunk_tokens, max_side_rows, &plan);
   if (st != ABKV_OK) return st;
   if (!workspace || workspace_bytes < plan.total) return ABKV_ERR_WORKSPACE;
   if (reinterpret_cast<uintptr_t>(workspace) & 255) return ABKV_ERR_WORKSPACE;
@@ -678,6 +797,23 @@ int launch_decode(const void* const* q, const void* const* kv, const int32_t* co
       a.out = static_cast<__nv_bfloat16*>(out[l0 + i]);
       a.bt_stride = bt_strides[l0 + i];
       a.num_blocks = num_blocks[l0 + i];
+      a.side = nullptr;
+      if (sidecars && sidecars[l0 + i].pages) {
+        const abkv_sidecar_t& sc = sidecars[l0 + i];
+        a.side = static_cast<const __nv_bfloat16*>(sc.pages);
+        a.side_bt = sc.page_table;
+        a.side_count = sc.page_count;
+        a.side_bt_stride = sc.page_table_stride;
+        a.side_num_pages = sc.num_pages;
+        a.side_slots = sc.slots;
+        a.side_qmax = 0;
+        for (int h = 0, off = 0; h < num_kv_heads; ++h) {
+          a.side_off[h] = off;
+          a.side_q[h] = sc.quotas[h];
+          off += sc.quotas[h];
+          a.side_qmax = sc.quotas[h] > a.side_qmax ? sc.quotas[h] : a.side_qmax;
+        }
+      }
     }
     prm.layer_base = l0;
     prm.nl = nl;
@@ -705,6 +841,33 @@ extern "C" int abkv_decode(const void* const* q, const void* const* kv,
   return launch_decode(q, kv, block_tables, bt_strides, seq_lens, num_blocks, out, num_layers, num_seqs,
                        num_q_heads, num_kv_heads, head_dim, page_size, max_pages_per_seq, scale, chunk_tokens,
                        workspace, workspace_bytes, stream, g);
+}
+
+extern "C" size_t abkv_decode_packed_workspace_size(int num_layers, int num_seqs, int num_q_heads, int head_dim,
+                                                    int page_size, int max_pages_per_seq, int chunk_tokens,
+                                                    int64_t max_side_rows) {
+  DecodePlan plan;
+  if (plan_decode(num_layers, num_seqs, num_q_heads, head_dim, page_size, max_pages_per_seq, chunk_tokens,
+                  max_side_rows, &plan) != ABKV_OK)
+    return 0;
+  return plan.total;
+}
+
+extern "C" int abkv_decode_packed(const void* const* q, const void* const* kv,
+                                  const int32_t* const* block_tables, const int64_t* bt_strides,
+                                  const int32_t* const* seq_lens, const int64_t* num_blocks,
+                                  void* const* out, int num_layers, int num_seqs, int num_q_heads,
+                                  int num_kv_heads, int head_dim, int page_size, int max_pages_per_seq,
+                                  float scale, int chunk_tokens, const abkv_sidecar_t* sidecars,
+                                  void* workspace, size_t workspace_bytes, void* stream) {
+  if (!sidecars) return ABKV_ERR_INVALID_ARG;
+  GatherArgs g;
+  memset(&g, 0, sizeof(g));
+  g.out_row = (int64_t)num_q_heads * head_dim;
+  g.world = 1;
+  return launch_decode(q, kv, block_tables, bt_strides, seq_lens, num_blocks, out, num_layers, num_seqs,
+                       num_q_heads, num_kv_heads, head_dim, page_size, max_pages_per_seq, scale, chunk_tokens,
+                       workspace, workspace_bytes, stream, g, sidecars);
 }
 
 extern "C" int abkv_decode_gather(const void* const* q, const void* const* kv,
@@ -792,7 +955,7 @@ extern "C" int abkv_decode_noalloc(const void* const* q, const void* const* kv,
                                    float scale, int chunk_tokens, int32_t* device_error, void* stream) {
   DecodePlan plan;
   const int st = plan_decode(num_layers, num_seqs, num_q_heads, head_dim, page_size, max_pages_per_seq,
-                             chunk_tokens, &plan);
+                             chunk_tokens, 0, &plan);
   if (st != ABKV_OK) return st;
   if (plan.total > kNoAllocScratchBytes) return ABKV_ERR_SCRATCH_LIMIT;
   void* scratch = nullptr;

@@ -134,6 +134,45 @@ int abkv_decode_noalloc(const void* const* q, const void* const* kv,
                         int max_pages_per_seq, float scale, int chunk_tokens,
                         int32_t* device_error, void* stream);
 
+/* Decode with a packed sidecar of per-head code quotas.
+ *
+ * Replaces PackedKVSidecar._attend_decode_batched with sidecar pages
+ * (third_party/vllm_overlay/vllm/v1/worker/compresslm_packed_kv.py:526-616;
+ * page layout PackedKVLayout, :13-155): every compressed block of a request
+ * stores, per layer, one packed page [2][slots][head_dim] bf16 in which KV head
+ * h owns slots [off_h, off_h + quotas[h]) (off_h = sum of the earlier quotas).
+ * For KV head h of request b the keys are, in order, head h's slots of each of
+ * the request's page_count[b] pages (ids page_table[b][0..]), then main rows
+ * [0, seq_lens[b]) of the paged cache as in abkv_decode.  One descriptor per
+ * layer; pages == NULL = no sidecar for that layer.  quotas: multiples of 16.
+ * Workspace: abkv_decode_packed_workspace_size with max_side_rows = the largest
+ * page_table_stride * max(quotas) over the layers. */
+typedef struct abkv_sidecar {
+  const void* pages;           /* DEVICE [num_pages][2][slots][head_dim] bf16 */
+  const int32_t* page_table;   /* DEVICE [B][page_table_stride] page ids     */
+  const int32_t* page_count;   /* DEVICE [B] sidecar pages of each request  */
+  int64_t page_table_stride;
+  int64_t num_pages;
+  int slots;                   /* sum of quotas                              */
+  int quotas[8];               /* per KV head (num_kv_heads entries used)    */
+} abkv_sidecar_t;
+
+size_t abkv_decode_packed_workspace_size(int num_layers, int num_seqs,
+                                         int num_q_heads, int head_dim,
+                                         int page_size, int max_pages_per_seq,
+                                         int chunk_tokens, int64_t max_side_rows);
+
+int abkv_decode_packed(const void* const* q, const void* const* kv,
+                       const int32_t* const* block_tables,
+                       const int64_t* bt_strides,
+                       const int32_t* const* seq_lens,
+                       const int64_t* num_blocks, void* const* out,
+                       int num_layers, int num_seqs, int num_q_heads,
+                       int num_kv_heads, int head_dim, int page_size,
+                       int max_pages_per_seq, float scale, int chunk_tokens,
+                       const abkv_sidecar_t* sidecars, void* workspace,
+                       size_t workspace_bytes, void* stream);
+
 /* KV-head-sharded decode with the all-gather fused into the epilogue.
  *
  * BASELINE config 5's optional mode (one process per GPU, rank r holding KV

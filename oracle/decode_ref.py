@@ -164,3 +164,44 @@ def sidecar_codestep_torch(query, kv_cache, seq_len: int, block_row, quotas_per_
     weights = torch.softmax(scores, dim=-1, dtype=torch.float32).to(q.dtype)
     att = torch.einsum("qhgt,htd->qhgd", weights, value)
     return att.reshape(k_max, num_kv_heads * groups, D)
+
+
+def packed_offsets(quotas):
+    """Slot offset of each KV head inside a packed page (PackedKVLayout.offsets,
+    compresslm_packed_kv.py:76-84): head h owns slots [off[h], off[h] + quotas[h])."""
+    off = [0]
+    for q in quotas:
+        off.append(off[-1] + int(q))
+    return off
+
+
+def packed_decode_exact(q, kv, block_table, seq_lens, side_pages, counts, quotas, scale, page):
+    """Decode over packed sidecar pages + the paged main cache in float64
+    (PackedKVSidecar._attend_decode_batched with pages, compresslm_packed_kv.py:526-616):
+    for KV head h of request r the keys are, in order, slots [off_h, off_h + q_h) of each of
+    the request's sidecar pages (side_pages[first_r + i], [2, slots, D]), then main rows
+    [0, seq_len).  side_pages holds every request's pages, request after request."""
+    B, Hq, D = q.shape
+    Hkv = kv.shape[3]
+    G = Hq // Hkv
+    off = packed_offsets(quotas)
+    out = np.zeros((B, Hq, D))
+    first = 0
+    for b in range(B):
+        cnt = int(counts[b])
+        pages = side_pages[first:first + cnt]
+        first += cnt
+        s_len = int(seq_lens[b])
+        k_main, v_main = _gather(kv, block_table[b], s_len, page)
+        for h in range(Hq):
+            kh = h // G
+            ks = [pages[i, 0, off[kh]:off[kh + 1]] for i in range(cnt)] + [k_main[:, kh]]
+            vs = [pages[i, 1, off[kh]:off[kh + 1]] for i in range(cnt)] + [v_main[:, kh]]
+            keys = np.concatenate(ks).astype(np.float64)
+            vals = np.concatenate(vs).astype(np.float64)
+            if len(keys) == 0:
+                continue
+            s = (keys @ q[b, h].astype(np.float64)) * scale
+            e = np.exp(s - s.max())
+            out[b, h] = (e / e.sum()) @ vals
+    return out

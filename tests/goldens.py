@@ -59,3 +59,19 @@ def load_codestep(name: str):
     qrows = round_bf16(rng.standard_normal((len(z["seq_lens"]) * K, int(z["num_q_heads"]), 128)).astype(np.float32))
     excl = z["excluded"] if "excluded" in z.files and len(z["excluded"]) else None
     return case, qrows, K, z["quotas"], from_bits(z["out_bits"]), excl
+
+
+def packed_cases():
+    return sorted(p.stem[len("packed_"):] for p in GOLDEN.glob("packed_*.npz"))
+
+
+def load_packed(name: str):
+    """-> (main case, side pages [sum(counts), 2, slots, D], counts, quotas per kv head, k_max,
+    reference output [B, Hq, D])."""
+    from tests.golden.make_golden import packed_side_pages
+
+    z = np.load(GOLDEN / f"packed_{name}.npz")
+    case = paged_case(int(z["seed"]), z["seq_lens"], num_q_heads=int(z["num_q_heads"]),
+                      num_kv_heads=int(z["num_kv_heads"]), head_dim=int(z["head_dim"]), page=int(z["page"]))
+    side = packed_side_pages(int(z["seed"]), z["counts"], int(z["quotas"].sum()), int(z["head_dim"]))
+    return case, side, z["counts"], z["quotas"], int(z["k_max"]), from_bits(z["out_bits"])

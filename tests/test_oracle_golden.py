@@ -62,3 +62,17 @@ def test_codestep_torch_port_matches_reference(name):
                                            None if excl is None else excl[r]).float().numpy())
     got = np.concatenate(outs)
     assert np.abs(got - ref).max() <= 1e-2
+
+
+from oracle.decode_ref import packed_decode_exact  # noqa: E402
+from tests.goldens import load_packed, packed_cases  # noqa: E402
+
+
+@pytest.mark.parametrize("name", packed_cases())
+def test_packed_oracle_matches_reference(name):
+    case, side, counts, quotas, k_max, ref = load_packed(name)
+    ex = packed_decode_exact(case.q, case.kv, case.block_table, case.seq_lens, side, counts, quotas, case.scale,
+                             case.page)
+    assert np.isfinite(ref).all()
+    assert np.abs(ex - ref).max() < 3e-2
+    assert np.abs(ex - ref).mean() < 2e-3
