@@ -3,6 +3,7 @@
     python -m abridgekv_b200.benchmarks prefill   [--layers 36] [--steps 3] [--flex]
     python -m abridgekv_b200.benchmarks compaction [--steps 5]
     python -m abridgekv_b200.benchmarks codestep   [--layers 36] [--steps 3]
+    python -m abridgekv_b200.benchmarks packed     [--steps 20]
 
 prefill    BASELINE config 4: B=16 sequences of 16 blocks x (512 content + 256 code rows)
            = 12,288 rows, Qwen3-4B attention (32 q / 8 kv heads, head_dim 128), per-layer
@@ -20,6 +21,11 @@ codestep   the code step at a block boundary on BASELINE config 2's caches: 64 r
            K=256 freshly written code rows; 256 code queries per request (32 q / 8 kv heads,
            head_dim 128).  One step = all layers (one abkv_code_step_attention launch each).
            Algorithmic FLOPs = 4 x head_dim x visible keys per query per head.
+packed     decode with per-head code quotas in packed sidecar pages: config 2's geometry
+           (64 requests, 36 layers, 256-token prompt + tail U[0,511] in the paged main
+           cache, 31 compressed blocks) with per-KV-head quotas 256/128/64/64/192/64/128/128
+           (mean 128, as config 2's per-layer mean): 31 sidecar pages per request and layer.
+           Algorithmic bytes = every key/value row read once + Q/O.
 """
 from __future__ import annotations
 
@@ -283,16 +289,66 @@ def bench_codestep(args) -> dict:
                        "mean_seq_len": float(wl.rows.mean())}}
 
 
+def bench_packed(args) -> dict:
+    from .sidecar import PackedKVLayout, SidecarPool, packed_decode
+    from .workloads import BLOCK_C, build_decode_workload
+
+    B, L, Hq, Hkv, D, blocks = 64, 36, 32, 8, 128, 31
+    quotas = [256, 128, 64, 64, 192, 64, 128, 128]
+    rng = np.random.default_rng(0)
+    main_rows = 256 + rng.integers(0, BLOCK_C, size=B)
+    wl = build_decode_workload("packed-main", (128,) * L, {128: main_rows}, num_q_heads=Hq, num_kv_heads=Hkv,
+                               head_dim=D)
+    layout = PackedKVLayout.from_schedule([quotas] * L, num_layers=L, num_kv_heads=Hkv, k_max=256)
+    dev = torch.device("cuda")
+    gen = torch.Generator(device=dev).manual_seed(2)
+    pools = []
+    for l in range(L):
+        pool = SidecarPool(layout, l, capacity=B * blocks, num_requests=B, max_pages=blocks, head_dim=D)
+        pool.pages.normal_(generator=gen)
+        perm = torch.randperm(B * blocks, generator=torch.Generator().manual_seed(l)).to(torch.int32)
+        pool.page_table.copy_(perm.view(B, blocks).to(dev))
+        pool.page_count.fill_(blocks)
+        pools.append(pool)
+    outs = [torch.empty_like(q) for q in wl.queries]
+
+    def step():
+        packed_decode(wl.queries, wl.kv_caches, wl.block_tables, wl.seq_lens, pools, outputs=outs)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    side_bytes = L * B * blocks * sum(quotas) * D * 2 * 2
+    alg = side_bytes + wl.kv_bytes + wl.qo_bytes
+    gbs = alg / (ms / 1e3) / 1e9
+    pk = _peaks()
+    return {"metric": "packed per-head-quota decode tokens/s (config 2 geometry)", "value": B / (ms / 1e3),
+            "unit": "tokens/s", "ms_per_step": ms, "algorithmic_gb_per_step": alg / 1e9,
+            "sidecar_gb_per_step": side_bytes / 1e9,
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": pk.get("hbm_gbs"), "unit": "GB/s",
+                         "frac": gbs / pk.get("hbm_gbs", 6650.0)},
+            "config": {"requests": B, "layers": L, "kv_head_quotas": quotas, "sidecar_pages_per_request": blocks,
+                       "main_rows": "256 + U[0,511]"}}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("which", choices=["prefill", "compaction", "codestep"])
+    ap.add_argument("which", choices=["prefill", "compaction", "codestep", "packed"])
     ap.add_argument("--layers", type=int, default=36)
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=2)
     ap.add_argument("--flex", action="store_true")
     ap.add_argument("--blocks", type=int, default=6)
     args = ap.parse_args()
-    fn = {"prefill": bench_prefill, "compaction": bench_compaction, "codestep": bench_codestep}[args.which]
+    fn = {"prefill": bench_prefill, "compaction": bench_compaction, "codestep": bench_codestep,
+          "packed": bench_packed}[args.which]
     print(json.dumps(fn(args)), flush=True)
 
 
