@@ -68,7 +68,7 @@ struct LayerArgs {
   const int32_t* side_bt;     // [B][side_bt_stride] page ids into `side`
   const int32_t* side_count;  // [B] sidecar pages of each request
   int64_t side_bt_stride, side_num_pages;
-  int side_slots, side_qmax;
+  int side_slots;
   int side_off[kWarps], side_q[kWarps];
 };
 
@@ -105,15 +105,17 @@ struct DecodeParams {
   int num_items;
 };
 
-// A group is either main tiles (16 rows x all KV heads; ok bit per tile) or
-// sidecar tiles (16 slots of one KV head; ok bit per (tile, head) pair, and
-// seq_len holds the request's sidecar page count).
+// A group is either main tiles (16 rows x all KV heads; ok bit per tile, warp w
+// takes head w % Hkv of tile w / Hkv) or sidecar tiles of ONE KV head (the
+// item's head, bits 11..13): warp w takes tile w (16 slots); seq_len holds the
+// request's sidecar page count.
 struct StageMeta {
   int li, b, chunk, n_chunks, seq_len, t0, ntiles, bits;  // bits: ok mask | kFirst | kLast | kSide
 };
 constexpr int kFirst = 1 << 8;
 constexpr int kLast = 1 << 9;
 constexpr int kSide = 1 << 10;
+constexpr int kSideHeadShift = 11;
 
 // Dynamic shared memory layout.
 constexpr size_t kOffStage = 0;
@@ -243,10 +245,12 @@ __device__ void producer(const DecodeParams& p, uint8_t* smem) {
         const LayerArgs& L = p.layer[li];
         slen = clamp_seq_len(p, L, b, chunk == 0);
         scount = L.side ? clamp_side_count(p, L, b, chunk == 0) : 0;
-        // chunks [0, nside) cover the sidecar rows, the rest the main rows
+        // chunks [0, nside) cover the sidecar rows, head after head; the rest the main rows
         const int ntl = (slen + kTile - 1) / kTile;
-        const int stl = (scount * (L.side ? L.side_qmax : 0) + kTile - 1) / kTile;
-        nside = (stl + p.chunk_tiles - 1) / p.chunk_tiles;
+        nside = 0;
+        if (L.side)
+          for (int hh = 0; hh < Hkv; ++hh)
+            nside += ((scount * L.side_q[hh] + kTile - 1) / kTile + p.chunk_tiles - 1) / p.chunk_tiles;
         nch = max(1, nside + (ntl + p.chunk_tiles - 1) / p.chunk_tiles);
         if (chunk < nch) break;
         li = -1;
@@ -262,34 +266,36 @@ __device__ void producer(const DecodeParams& p, uint8_t* smem) {
     scount = __shfl_sync(0xffffffffu, scount, 0);
     const LayerArgs& L = p.layer[li];
     if (chunk < nside) {
-      // ---- sidecar item: lane i < nsub * Hkv owns (tile sub = i / Hkv, head h = i % Hkv) of a
-      // group; a tile is 16 consecutive slots of one head (quotas are multiples of 16, so
-      // they lie in one page); heads whose slots ran out are masked
-      const int stl = (scount * L.side_qmax + kTile - 1) / kTile;
-      const int tile0 = chunk * p.chunk_tiles;
+      // ---- sidecar item: tiles of one KV head; lane i < kWarps owns tile i of a group (16
+      // consecutive slots of the head; quotas are multiples of 16, so they lie in one page)
+      int hs = 0, c0 = 0, stl = 0;
+      for (;; ++hs) {
+        stl = (scount * L.side_q[hs] + kTile - 1) / kTile;
+        const int nc = (stl + p.chunk_tiles - 1) / p.chunk_tiles;
+        if (chunk < c0 + nc || hs == Hkv - 1) break;
+        c0 += nc;
+      }
+      const int qh = L.side_q[hs];
+      const int tile0 = (chunk - c0) * p.chunk_tiles;
       const int tile1 = min(tile0 + p.chunk_tiles, stl);
       const int ntiles = max(0, tile1 - tile0);
-      const int ngroups = max(1, (ntiles + nsub - 1) / nsub);
+      const int ngroups = max(1, (ntiles + kWarps - 1) / kWarps);
       const int head_tile = kTile * D * 2;
       for (int grp = 0; grp < ngroups; ++grp, ++gq) {
         const int st = gq % kStages;
-        const int tg0 = tile0 + grp * nsub;
-        const int nt = max(0, min(nsub, tile1 - tg0));
+        const int tg0 = tile0 + grp * kWarps;
+        const int nt = max(0, min(kWarps, tile1 - tg0));
         int64_t src = -1;
-        const int sub = lane / Hkv, hh = lane % Hkv;
-        if (lane < nsub * Hkv && sub < nt) {
-          const int row0 = (tg0 + sub) * kTile, qh = L.side_q[hh];
-          if (row0 < scount * qh) {
-            const int pi = row0 / qh;
-            const int64_t pid = __ldg(L.side_bt + (int64_t)b * L.side_bt_stride + pi);
-            if (pid >= 0 && pid < L.side_num_pages) {
-              src = (pid * 2 * L.side_slots + L.side_off[hh] + row0 % qh) * D;
-            } else {
-              set_error(p.err, ABKV_DEVERR_PAGE_OOB);
-            }
+        if (lane < nt) {
+          const int row0 = (tg0 + lane) * kTile;
+          const int64_t pid = __ldg(L.side_bt + (int64_t)b * L.side_bt_stride + row0 / qh);
+          if (pid >= 0 && pid < L.side_num_pages) {
+            src = (pid * 2 * L.side_slots + L.side_off[hs] + row0 % qh) * D;
+          } else {
+            set_error(p.err, ABKV_DEVERR_PAGE_OOB);
           }
         }
-        const uint32_t okmask = __ballot_sync(0xffffffffu, src >= 0) & ((1u << (nsub * Hkv)) - 1u);
+        const uint32_t okmask = __ballot_sync(0xffffffffu, src >= 0) & ((1u << nt) - 1u);
         if (lane == 0) {
           const uint32_t k = (uint32_t)(gq / kStages);
           if (!mbar_wait(&empty[st], (k & 1u) ^ 1u)) {
@@ -303,16 +309,16 @@ __device__ void producer(const DecodeParams& p, uint8_t* smem) {
           StageMeta m;
           m.li = li; m.b = b; m.chunk = chunk; m.n_chunks = nch; m.seq_len = scount;
           m.t0 = tg0; m.ntiles = nt;
-          m.bits = (int)okmask | kSide | (grp == 0 ? kFirst : 0) | (grp == ngroups - 1 ? kLast : 0);
+          m.bits = (int)okmask | kSide | (hs << kSideHeadShift) | (grp == 0 ? kFirst : 0) |
+                   (grp == ngroups - 1 ? kLast : 0);
           meta[st] = m;
           mbar_expect_tx(&full[st], (uint32_t)__popc(okmask) * 2u * (uint32_t)head_tile);
         }
         __syncwarp();  // the expected byte count is posted before any copy can complete
         if (src >= 0) {
-          uint8_t* dst = smem + kOffStage + (size_t)st * kStageBytes + (size_t)sub * 2 * tile_half +
-                         (size_t)hh * head_tile;
+          uint8_t* dst = smem + kOffStage + (size_t)st * kStageBytes + (size_t)lane * 2 * head_tile;
           bulk_g2s(dst, L.side + src, (uint32_t)head_tile, &full[st]);
-          bulk_g2s(dst + tile_half, L.side + src + (int64_t)L.side_slots * D, (uint32_t)head_tile, &full[st]);
+          bulk_g2s(dst + head_tile, L.side + src + (int64_t)L.side_slots * D, (uint32_t)head_tile, &full[st]);
         }
       }
       continue;
@@ -425,12 +431,16 @@ __device__ void consumer(const DecodeParams& p, uint8_t* smem) {
     const StageMeta M = meta[st];
     if (M.li < 0) break;
     const LayerArgs& L = p.layer[M.li];
+    // sidecar items: every warp works for the item's head, warp w on tile w
+    const bool side_grp = (M.bits & kSide) != 0;
+    const int hw = side_grp ? (M.bits >> kSideHeadShift) & 7 : h;  // head of this warp's rows
+    const int my_tile = side_grp ? warp : sub;
     if (M.bits & kFirst) {
 #pragma unroll
       for (int mt = 0; mt < kOT; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
       m_run = -INFINITY;
       l_run = 0.f;
-      const __nv_bfloat16* qrow = L.q + ((int64_t)M.b * p.Hq + h * G + g) * D + 8 * c;
+      const __nv_bfloat16* qrow = L.q + ((int64_t)M.b * p.Hq + hw * G + g) * D + 8 * c;
 #pragma unroll
       for (int m = 0; m < kQC; ++m) {
         uint4 v = make_uint4(0, 0, 0, 0);
@@ -438,17 +448,17 @@ __device__ void consumer(const DecodeParams& p, uint8_t* smem) {
         qr[m][0] = v.x; qr[m][1] = v.y; qr[m][2] = v.z; qr[m][3] = v.w;
       }
     }
-    if (sub < M.ntiles) {
-      // main tile: row T of KV head h at T * row_bytes + h * D * 2, rows < seq_len;
-      // sidecar tile: this head's 16 slots at h * 16 * D * 2, rows < pages * quota_h
-      const bool side_grp = (M.bits & kSide) != 0;
-      const bool ok = (M.bits >> (side_grp ? sub * Hkv + h : sub)) & 1;
-      const int tok0 = (M.t0 + sub) * kTile;
-      const int seq_len = side_grp ? M.seq_len * L.side_q[h] : M.seq_len;
+    if (my_tile < M.ntiles) {
+      // main tile: row T of KV head h at T * row_bytes + h * D * 2 of tile sub, rows < seq_len;
+      // sidecar tile w: 16 slots of the item's head, K then V, rows < pages * quota
+      const bool ok = (M.bits >> my_tile) & 1;
+      const int tok0 = (M.t0 + my_tile) * kTile;
+      const int seq_len = side_grp ? M.seq_len * L.side_q[hw] : M.seq_len;
       const int rstride = side_grp ? D * 2 : row_bytes;
-      const uint8_t* kb = smem + kOffStage + (size_t)st * kStageBytes + (size_t)sub * 2 * tile_half +
-                          (side_grp ? h * kTile * D * 2 : h * D * 2);
-      const uint8_t* vb = kb + tile_half;
+      const int head_tile = kTile * D * 2;
+      const uint8_t* kb = smem + kOffStage + (size_t)st * kStageBytes +
+                          (side_grp ? (size_t)warp * 2 * head_tile : (size_t)sub * 2 * tile_half + h * D * 2);
+      const uint8_t* vb = kb + (side_grp ? head_tile : tile_half);
 
       // S = Q.K^T : rows = query heads (g < G real), cols = tokens 8nt + 2c + {0,1}
       float s[2][4];
@@ -557,12 +567,19 @@ __device__ void consumer(const DecodeParams& p, uint8_t* smem) {
     for (int it = threadIdx.x; it < items; it += kConsumerThreads) {
       const int d = it % D, hr = it / D;
       const int kh = hr / G, r = hr % G;
+      if (side_grp && kh != hw) {
+        // a sidecar item covers one KV head: the other heads' rows of this chunk are empty
+        if (d == 0 && n_chunks > 1) p.part_lse[prow + hr] = -INFINITY;
+        continue;
+      }
+      // warps holding this row: all of them for a sidecar item, else those of head kh
+      const int nw = side_grp ? kWarps : nsub, w0 = side_grp ? 0 : kh, dw = side_grp ? 1 : Hkv;
       float Mx = -INFINITY;
-      for (int s2 = 0; s2 < nsub; ++s2) Mx = fmaxf(Mx, s_m[s2 * Hkv + kh][r]);
+      for (int s2 = 0; s2 < nw; ++s2) Mx = fmaxf(Mx, s_m[w0 + s2 * dw][r]);
       const float Mu = (Mx == -INFINITY) ? 0.f : Mx;
       float Ls = 0.f, Os = 0.f;
-      for (int s2 = 0; s2 < nsub; ++s2) {
-        const int w = s2 * Hkv + kh;
+      for (int s2 = 0; s2 < nw; ++s2) {
+        const int w = w0 + s2 * dw;
         const float f = exp2f(s_m[w][r] - Mu);
         Ls += s_l[w][r] * f;
         Os += s_o[w][r][d] * f;
@@ -596,7 +613,9 @@ __device__ void consumer(const DecodeParams& p, uint8_t* smem) {
           float Ls = 0.f, Os = 0.f;
           for (int ch = 0; ch < n_chunks; ++ch) {
             const int64_t rr = row0 + (int64_t)ch * p.Hq + hr;
-            const float f = exp2f(__ldcg(p.part_lse + rr) - Mu);
+            const float lse = __ldcg(p.part_lse + rr);
+            if (lse == -INFINITY) continue;  // empty chunk for this row (its O was not written)
+            const float f = exp2f(lse - Mu);
             Ls += f;
             Os += f * __ldcg(p.part_o + rr * D + d);
           }
@@ -651,8 +670,9 @@ struct DecodePlan {
 
 constexpr size_t kWsHeader = 256;
 
-// max_side_rows: an upper bound of the sidecar rows of one (layer, request, head)
-// (sidecar pages x largest quota), 0 without a sidecar.
+// max_side_rows: an upper bound of the sidecar rows of one (layer, request) over
+// all its heads (sidecar pages x slots), 0 without a sidecar.  Sidecar chunks are
+// per head, so each head may round up by one chunk (+2 per head of slack).
 int plan_decode(int num_layers, int num_seqs, int num_q_heads, int head_dim, int page_size,
                 int max_pages, int chunk_tokens, int64_t max_side_rows, DecodePlan* plan) {
   if (num_layers <= 0 || num_seqs <= 0 || num_q_heads <= 0 || page_size <= 0 || max_pages <= 0)
@@ -673,7 +693,7 @@ int plan_decode(int num_layers, int num_seqs, int num_q_heads, int head_dim, int
   if (ct * kTile / page_size > kMaxChunkPages - 1) return ABKV_ERR_UNSUPPORTED;
   plan->chunk_tiles = ct;
   plan->max_tiles = (int)max_tiles;
-  plan->max_chunks = (int)((max_tiles + ct - 1) / ct + (side_tiles + ct - 1) / ct);
+  plan->max_chunks = (int)((max_tiles + ct - 1) / ct + (side_tiles ? (side_tiles + ct - 1) / ct + 2 * kWarps : 0));
   if (plan->max_chunks > 1) {
     const size_t rows = (size_t)num_layers * num_seqs * plan->max_chunks * num_q_heads;
     plan->counter_bytes = ((size_t)num_layers * num_seqs * sizeof(int32_t) + 255) / 256 * 256;
@@ -727,15 +747,14 @@ int launch_decode(const void* const* q, const void* const* kv, const int32_t* co
         return ABKV_ERR_INVALID_ARG;
       if ((reinterpret_cast<uintptr_t>(sc.pages) & 15) || (reinterpret_cast<uintptr_t>(sc.page_table) & 3))
         return ABKV_ERR_INVALID_ARG;
-      int sum = 0, qmax = 0;
+      int sum = 0;
       for (int h = 0; h < num_kv_heads; ++h) {
         const int qh = sc.quotas[h];
         if (qh <= 0 || qh % kTile || qh >= (1 << 16)) return ABKV_ERR_UNSUPPORTED;
         sum += qh;
-        qmax = qh > qmax ? qh : qmax;
       }
       if (sum != sc.slots) return ABKV_ERR_INVALID_ARG;
-      const int64_t rows = sc.page_table_stride * qmax;
+      const int64_t rows = sc.page_table_stride * sum;
       max_side_rows = rows > max_side_rows ? rows : max_side_rows;
     }
   }
@@ -806,12 +825,10 @@ int launch_decode(const void* const* q, const void* const* kv, const int32_t* co
         a.side_bt_stride = sc.page_table_stride;
         a.side_num_pages = sc.num_pages;
         a.side_slots = sc.slots;
-        a.side_qmax = 0;
         for (int h = 0, off = 0; h < num_kv_heads; ++h) {
           a.side_off[h] = off;
           a.side_q[h] = sc.quotas[h];
           off += sc.quotas[h];
-          a.side_qmax = sc.quotas[h] > a.side_qmax ? sc.quotas[h] : a.side_qmax;
         }
       }
     }

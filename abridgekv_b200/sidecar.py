@@ -185,7 +185,7 @@ def packed_decode(queries: Sequence[torch.Tensor], kv_caches: Sequence[torch.Ten
         if len(sc.quotas) != Hkv or sc.pages.shape[-1] != D or sc.page_table.shape[0] < B:
             raise ValueError(f"layer {l}: sidecar does not match the cache geometry")
         descs[l] = sc.descriptor()
-        max_side_rows = max(max_side_rows, sc.page_table.stride(0) * max(sc.quotas))
+        max_side_rows = max(max_side_rows, sc.page_table.stride(0) * sc.slots)
     max_pages = max(int(bt.shape[1]) for bt in block_tables)
     scale = 1.0 / math.sqrt(D) if scale is None else float(scale)
     lib = _lib.lib()

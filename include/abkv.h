@@ -146,7 +146,7 @@ int abkv_decode_noalloc(const void* const* q, const void* const* kv,
  * [0, seq_lens[b]) of the paged cache as in abkv_decode.  One descriptor per
  * layer; pages == NULL = no sidecar for that layer.  quotas: multiples of 16.
  * Workspace: abkv_decode_packed_workspace_size with max_side_rows = the largest
- * page_table_stride * max(quotas) over the layers. */
+ * page_table_stride * slots over the layers. */
 typedef struct abkv_sidecar {
   const void* pages;           /* DEVICE [num_pages][2][slots][head_dim] bf16 */
   const int32_t* page_table;   /* DEVICE [B][page_table_stride] page ids     */
