@@ -46,7 +46,7 @@ constexpr int kTile = 16;
 constexpr int kWarps = 8;                  // consumer warps
 constexpr int kThreads = (kWarps + 1) * 32;  // + producer warp
 constexpr int kConsumerThreads = kWarps * 32;
-constexpr int kMaxLayers = 56;       // layers per launch (kernel parameters ~9.7 KB)
+constexpr int kMaxLayers = 56;       // layers per launch (plain parameters < 4 KB, with sidecars ~9.6 KB)
 constexpr int kMaxChunkPages = 512;  // page ids staged per work item
 constexpr int kMaxG = 8;             // query heads per KV head
 constexpr int kStages = 3;
@@ -60,16 +60,19 @@ struct LayerArgs {
   __nv_bfloat16* out;
   int64_t bt_stride;
   int64_t num_blocks;
-  // Packed sidecar of per-head code quotas (null side = none): page i of a
-  // request holds, for KV head h, slots [side_off[h], side_off[h] + side_q[h])
-  // of a [2][side_slots][D] page; a head's keys are its slots of every sidecar
-  // page of the request (in page order), then the main rows.
-  const __nv_bfloat16* side;
-  const int32_t* side_bt;     // [B][side_bt_stride] page ids into `side`
-  const int32_t* side_count;  // [B] sidecar pages of each request
-  int64_t side_bt_stride, side_num_pages;
-  int side_slots;
-  int side_off[kWarps], side_q[kWarps];
+};
+
+// Packed sidecar of per-head code quotas of one layer (null pages = none): page i
+// of a request holds, for KV head h, slots [off[h], off[h] + q[h]) of a
+// [2][slots][D] page; a head's keys are its slots of every sidecar page of the
+// request (in page order), then the main rows.
+struct SideArgs {
+  const __nv_bfloat16* pages;
+  const int32_t* bt;     // [B][bt_stride] page ids into `pages`
+  const int32_t* count;  // [B] sidecar pages of each request
+  int64_t bt_stride, num_pages;
+  int slots;
+  int off[kWarps], q[kWarps];
 };
 
 // Output placement.  Row (b, h) of a layer goes to out + b * out_row + (head0 + h) * D
@@ -103,6 +106,15 @@ struct DecodeParams {
   int chunk_tiles, max_chunks, max_rows;
   int layer_base, nl;
   int num_items;
+  static constexpr bool kHasSide = false;
+};
+
+// Parameters of the packed-sidecar decode.  The plain decode is compiled from
+// the same templates with DecodeParams, so it carries neither the sidecar
+// parameters nor the sidecar branches.
+struct SideDecodeParams : DecodeParams {
+  SideArgs side[kMaxLayers];
+  static constexpr bool kHasSide = true;
 };
 
 // A group is either main tiles (16 rows x all KV heads; ok bit per tile, warp w
@@ -139,11 +151,11 @@ __device__ __forceinline__ int clamp_seq_len(const DecodeParams& p, const LayerA
   return s;
 }
 
-__device__ __forceinline__ int clamp_side_count(const DecodeParams& p, const LayerArgs& L, int b, bool report) {
-  int c = __ldg(L.side_count + b);
-  if (c < 0 || (int64_t)c > L.side_bt_stride) {
+__device__ __forceinline__ int clamp_side_count(const DecodeParams& p, const SideArgs& S, int b, bool report) {
+  int c = __ldg(S.count + b);
+  if (c < 0 || (int64_t)c > S.bt_stride) {
     if (report) set_error(p.err, ABKV_DEVERR_SEQ_OOB);
-    c = c < 0 ? 0 : (int)L.side_bt_stride;
+    c = c < 0 ? 0 : (int)S.bt_stride;
   }
   return c;
 }
@@ -164,13 +176,17 @@ __device__ __forceinline__ void consumer_sync() {
   asm volatile("bar.sync 1, %0;\n" ::"n"(kConsumerThreads) : "memory");
 }
 
-template <int D>
+template <int D, bool kGather>
 __device__ __forceinline__ void store_out(const DecodeParams& p, const LayerArgs& L, int b, int hr, int d,
                                           float val) {
-  const GatherArgs& g = p.gather;
-  __nv_bfloat16* dst = L.out + (int64_t)b * g.out_row + (int64_t)(g.head0 + hr) * D + d;
   const __nv_bfloat16 v = __float2bfloat16(val);
-  for (int r = 0; r < g.world; ++r) dst[g.peer_delta[r]] = v;
+  if constexpr (kGather) {
+    const GatherArgs& g = p.gather;
+    __nv_bfloat16* dst = L.out + (int64_t)b * g.out_row + (int64_t)(g.head0 + hr) * D + d;
+    for (int r = 0; r < g.world; ++r) dst[g.peer_delta[r]] = v;
+  } else {
+    L.out[((int64_t)b * p.Hq + hr) * D + d] = v;
+  }
 }
 
 __device__ __forceinline__ void st_release_sys(uint32_t* ptr, uint32_t v) {
@@ -216,8 +232,8 @@ __device__ void gather_barrier(const DecodeParams& p) {
 }
 
 // ---------------------------------------------------------------------------
-template <int D>
-__device__ void producer(const DecodeParams& p, uint8_t* smem) {
+template <int D, class Prm>
+__device__ void producer(const Prm& p, uint8_t* smem) {
   StageMeta* meta = reinterpret_cast<StageMeta*>(smem + kOffMeta);
   int32_t* s_pages = reinterpret_cast<int32_t*>(smem + kOffPages);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kOffBar);
@@ -242,15 +258,18 @@ __device__ void producer(const DecodeParams& p, uint8_t* smem) {
         const int rem = i - chunk * lb_items;
         li = rem / p.B;
         b = rem - li * p.B;
-        const LayerArgs& L = p.layer[li];
-        slen = clamp_seq_len(p, L, b, chunk == 0);
-        scount = L.side ? clamp_side_count(p, L, b, chunk == 0) : 0;
+        slen = clamp_seq_len(p, p.layer[li], b, chunk == 0);
         // chunks [0, nside) cover the sidecar rows, head after head; the rest the main rows
         const int ntl = (slen + kTile - 1) / kTile;
-        nside = 0;
-        if (L.side)
-          for (int hh = 0; hh < Hkv; ++hh)
-            nside += ((scount * L.side_q[hh] + kTile - 1) / kTile + p.chunk_tiles - 1) / p.chunk_tiles;
+        if constexpr (Prm::kHasSide) {
+          const SideArgs& S = p.side[li];
+          nside = scount = 0;
+          if (S.pages) {
+            scount = clamp_side_count(p, S, b, chunk == 0);
+            for (int hh = 0; hh < Hkv; ++hh)
+              nside += ((scount * S.q[hh] + kTile - 1) / kTile + p.chunk_tiles - 1) / p.chunk_tiles;
+          }
+        }
         nch = max(1, nside + (ntl + p.chunk_tiles - 1) / p.chunk_tiles);
         if (chunk < nch) break;
         li = -1;
@@ -262,66 +281,69 @@ __device__ void producer(const DecodeParams& p, uint8_t* smem) {
     chunk = __shfl_sync(0xffffffffu, chunk, 0);
     nch = __shfl_sync(0xffffffffu, nch, 0);
     slen = __shfl_sync(0xffffffffu, slen, 0);
-    nside = __shfl_sync(0xffffffffu, nside, 0);
-    scount = __shfl_sync(0xffffffffu, scount, 0);
     const LayerArgs& L = p.layer[li];
-    if (chunk < nside) {
-      // ---- sidecar item: tiles of one KV head; lane i < kWarps owns tile i of a group (16
-      // consecutive slots of the head; quotas are multiples of 16, so they lie in one page)
-      int hs = 0, c0 = 0, stl = 0;
-      for (;; ++hs) {
-        stl = (scount * L.side_q[hs] + kTile - 1) / kTile;
-        const int nc = (stl + p.chunk_tiles - 1) / p.chunk_tiles;
-        if (chunk < c0 + nc || hs == Hkv - 1) break;
-        c0 += nc;
-      }
-      const int qh = L.side_q[hs];
-      const int tile0 = (chunk - c0) * p.chunk_tiles;
-      const int tile1 = min(tile0 + p.chunk_tiles, stl);
-      const int ntiles = max(0, tile1 - tile0);
-      const int ngroups = max(1, (ntiles + kWarps - 1) / kWarps);
-      const int head_tile = kTile * D * 2;
-      for (int grp = 0; grp < ngroups; ++grp, ++gq) {
-        const int st = gq % kStages;
-        const int tg0 = tile0 + grp * kWarps;
-        const int nt = max(0, min(kWarps, tile1 - tg0));
-        int64_t src = -1;
-        if (lane < nt) {
-          const int row0 = (tg0 + lane) * kTile;
-          const int64_t pid = __ldg(L.side_bt + (int64_t)b * L.side_bt_stride + row0 / qh);
-          if (pid >= 0 && pid < L.side_num_pages) {
-            src = (pid * 2 * L.side_slots + L.side_off[hs] + row0 % qh) * D;
-          } else {
-            set_error(p.err, ABKV_DEVERR_PAGE_OOB);
+    if constexpr (Prm::kHasSide) {
+      nside = __shfl_sync(0xffffffffu, nside, 0);
+      scount = __shfl_sync(0xffffffffu, scount, 0);
+      if (chunk < nside) {
+        const SideArgs& S = p.side[li];
+        // ---- sidecar item: tiles of one KV head; lane i < kWarps owns tile i of a group (16
+        // consecutive slots of the head; quotas are multiples of 16, so they lie in one page)
+        int hs = 0, c0 = 0, stl = 0;
+        for (;; ++hs) {
+          stl = (scount * S.q[hs] + kTile - 1) / kTile;
+          const int nc = (stl + p.chunk_tiles - 1) / p.chunk_tiles;
+          if (chunk < c0 + nc || hs == Hkv - 1) break;
+          c0 += nc;
+        }
+        const int qh = S.q[hs];
+        const int tile0 = (chunk - c0) * p.chunk_tiles;
+        const int tile1 = min(tile0 + p.chunk_tiles, stl);
+        const int ntiles = max(0, tile1 - tile0);
+        const int ngroups = max(1, (ntiles + kWarps - 1) / kWarps);
+        const int head_tile = kTile * D * 2;
+        for (int grp = 0; grp < ngroups; ++grp, ++gq) {
+          const int st = gq % kStages;
+          const int tg0 = tile0 + grp * kWarps;
+          const int nt = max(0, min(kWarps, tile1 - tg0));
+          int64_t src = -1;
+          if (lane < nt) {
+            const int row0 = (tg0 + lane) * kTile;
+            const int64_t pid = __ldg(S.bt + (int64_t)b * S.bt_stride + row0 / qh);
+            if (pid >= 0 && pid < S.num_pages) {
+              src = (pid * 2 * S.slots + S.off[hs] + row0 % qh) * D;
+            } else {
+              set_error(p.err, ABKV_DEVERR_PAGE_OOB);
+            }
+          }
+          const uint32_t okmask = __ballot_sync(0xffffffffu, src >= 0) & ((1u << nt) - 1u);
+          if (lane == 0) {
+            const uint32_t k = (uint32_t)(gq / kStages);
+            if (!mbar_wait(&empty[st], (k & 1u) ^ 1u)) {
+              set_error(p.err, ABKV_DEVERR_TIMEOUT);
+              alive = false;
+            }
+          }
+          alive = __shfl_sync(0xffffffffu, alive ? 1 : 0, 0) != 0;
+          if (!alive) break;
+          if (lane == 0) {
+            StageMeta m;
+            m.li = li; m.b = b; m.chunk = chunk; m.n_chunks = nch; m.seq_len = scount;
+            m.t0 = tg0; m.ntiles = nt;
+            m.bits = (int)okmask | kSide | (hs << kSideHeadShift) | (grp == 0 ? kFirst : 0) |
+                     (grp == ngroups - 1 ? kLast : 0);
+            meta[st] = m;
+            mbar_expect_tx(&full[st], (uint32_t)__popc(okmask) * 2u * (uint32_t)head_tile);
+          }
+          __syncwarp();  // the expected byte count is posted before any copy can complete
+          if (src >= 0) {
+            uint8_t* dst = smem + kOffStage + (size_t)st * kStageBytes + (size_t)lane * 2 * head_tile;
+            bulk_g2s(dst, S.pages + src, (uint32_t)head_tile, &full[st]);
+            bulk_g2s(dst + head_tile, S.pages + src + (int64_t)S.slots * D, (uint32_t)head_tile, &full[st]);
           }
         }
-        const uint32_t okmask = __ballot_sync(0xffffffffu, src >= 0) & ((1u << nt) - 1u);
-        if (lane == 0) {
-          const uint32_t k = (uint32_t)(gq / kStages);
-          if (!mbar_wait(&empty[st], (k & 1u) ^ 1u)) {
-            set_error(p.err, ABKV_DEVERR_TIMEOUT);
-            alive = false;
-          }
-        }
-        alive = __shfl_sync(0xffffffffu, alive ? 1 : 0, 0) != 0;
-        if (!alive) break;
-        if (lane == 0) {
-          StageMeta m;
-          m.li = li; m.b = b; m.chunk = chunk; m.n_chunks = nch; m.seq_len = scount;
-          m.t0 = tg0; m.ntiles = nt;
-          m.bits = (int)okmask | kSide | (hs << kSideHeadShift) | (grp == 0 ? kFirst : 0) |
-                   (grp == ngroups - 1 ? kLast : 0);
-          meta[st] = m;
-          mbar_expect_tx(&full[st], (uint32_t)__popc(okmask) * 2u * (uint32_t)head_tile);
-        }
-        __syncwarp();  // the expected byte count is posted before any copy can complete
-        if (src >= 0) {
-          uint8_t* dst = smem + kOffStage + (size_t)st * kStageBytes + (size_t)lane * 2 * head_tile;
-          bulk_g2s(dst, L.side + src, (uint32_t)head_tile, &full[st]);
-          bulk_g2s(dst + head_tile, L.side + src + (int64_t)L.side_slots * D, (uint32_t)head_tile, &full[st]);
-        }
+        continue;
       }
-      continue;
     }
     // ---- main item: tiles of 16 rows x all KV heads through the block table
     const int ntl = (slen + kTile - 1) / kTile;
@@ -399,8 +421,8 @@ __device__ void producer(const DecodeParams& p, uint8_t* smem) {
 // ---------------------------------------------------------------------------
 // D = head_dim: the Q.K^T product runs over D / 32 chunks of 32 dims (8 per lane),
 // P.V over D / 64 halves of 64 dims, O^T in D / 16 accumulator tiles.
-template <int D>
-__device__ void consumer(const DecodeParams& p, uint8_t* smem) {
+template <int D, class Prm, bool kGather>
+__device__ void consumer(const Prm& p, uint8_t* smem) {
   const StageMeta* meta = reinterpret_cast<const StageMeta*>(smem + kOffMeta);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint64_t* empty = full + kStages;
@@ -432,7 +454,7 @@ __device__ void consumer(const DecodeParams& p, uint8_t* smem) {
     if (M.li < 0) break;
     const LayerArgs& L = p.layer[M.li];
     // sidecar items: every warp works for the item's head, warp w on tile w
-    const bool side_grp = (M.bits & kSide) != 0;
+    const bool side_grp = Prm::kHasSide && (M.bits & kSide) != 0;
     const int hw = side_grp ? (M.bits >> kSideHeadShift) & 7 : h;  // head of this warp's rows
     const int my_tile = side_grp ? warp : sub;
     if (M.bits & kFirst) {
@@ -453,7 +475,10 @@ __device__ void consumer(const DecodeParams& p, uint8_t* smem) {
       // sidecar tile w: 16 slots of the item's head, K then V, rows < pages * quota
       const bool ok = (M.bits >> my_tile) & 1;
       const int tok0 = (M.t0 + my_tile) * kTile;
-      const int seq_len = side_grp ? M.seq_len * L.side_q[hw] : M.seq_len;
+      int seq_len = M.seq_len;
+      if constexpr (Prm::kHasSide) {
+        if (side_grp) seq_len *= p.side[M.li].q[hw];
+      }
       const int rstride = side_grp ? D * 2 : row_bytes;
       const int head_tile = kTile * D * 2;
       const uint8_t* kb = smem + kOffStage + (size_t)st * kStageBytes +
@@ -586,7 +611,7 @@ __device__ void consumer(const DecodeParams& p, uint8_t* smem) {
       }
       const float val = Ls > 0.f ? Os / Ls : 0.f;
       if (n_chunks == 1) {
-        store_out<D>(p, L, M.b, hr, d, val);
+        store_out<D, kGather>(p, L, M.b, hr, d, val);
       } else {
         p.part_o[(prow + hr) * D + d] = val;
         if (d == 0) p.part_lse[prow + hr] = Ls > 0.f ? Mu + log2f(Ls) : -INFINITY;
@@ -614,12 +639,12 @@ __device__ void consumer(const DecodeParams& p, uint8_t* smem) {
           for (int ch = 0; ch < n_chunks; ++ch) {
             const int64_t rr = row0 + (int64_t)ch * p.Hq + hr;
             const float lse = __ldcg(p.part_lse + rr);
-            if (lse == -INFINITY) continue;  // empty chunk for this row (its O was not written)
+            if (Prm::kHasSide && lse == -INFINITY) continue;  // empty sidecar chunk: its O was not written
             const float f = exp2f(lse - Mu);
             Ls += f;
             Os += f * __ldcg(p.part_o + rr * D + d);
           }
-          store_out<D>(p, L, M.b, hr, d, Ls > 0.f ? Os / Ls : 0.f);
+          store_out<D, kGather>(p, L, M.b, hr, d, Ls > 0.f ? Os / Ls : 0.f);
         }
         if (threadIdx.x == 0) p.counters[lb] = 0;  // ready for the next call on this workspace
       }
@@ -628,8 +653,8 @@ __device__ void consumer(const DecodeParams& p, uint8_t* smem) {
   }
 }
 
-template <int D>
-__global__ void __launch_bounds__(kThreads, 1) decode_split_kernel(const __grid_constant__ DecodeParams p) {
+template <int D, class Prm, bool kGather>
+__global__ void __launch_bounds__(kThreads, 1) decode_split_kernel(const __grid_constant__ Prm p) {
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint64_t* empty = full + kStages;
@@ -643,9 +668,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_split_kernel(const __grid_
   if ((threadIdx.x >> 5) == kWarps) {
     producer<D>(p, smem);
   } else {
-    consumer<D>(p, smem);
+    consumer<D, Prm, kGather>(p, smem);
   }
-  if (p.gather.my_flags) {
+  if constexpr (kGather) {
     __threadfence_system();  // this thread's output stores, to every rank
     __syncthreads();
     if (threadIdx.x == 0) gather_barrier(p);
@@ -723,6 +748,94 @@ extern "C" size_t abkv_decode_workspace_size(int num_layers, int num_seqs, int n
 
 namespace abkv {
 namespace {
+template <class Prm, bool kGather>
+int launch_kernel(const Prm& prm, int head_dim, int grid, cudaStream_t s) {
+  auto kernel = head_dim == 64 ? decode_split_kernel<64, Prm, kGather> : decode_split_kernel<kD, Prm, kGather>;
+  // opt in to > 48 KiB of dynamic shared memory (idempotent, per device)
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes) != cudaSuccess)
+    return ABKV_ERR_CUDA;
+  kernel<<<grid, kThreads, kSmemBytes, s>>>(prm);
+  return ABKV_OK;
+}
+
+template <class Prm>
+int fill_and_launch(Prm& prm, const DecodePlan& plan, const void* const* q, const void* const* kv,
+                    const int32_t* const* block_tables, const int64_t* bt_strides, const int32_t* const* seq_lens,
+                    const int64_t* num_blocks, void* const* out, int num_layers, int num_seqs, int num_q_heads,
+                    int num_kv_heads, int head_dim, int page_size, float scale, char* ws, void* stream,
+                    const GatherArgs& gather, const abkv_sidecar_t* sidecars) {
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  int dev = 0, num_sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || num_sms <= 0)
+    return ABKV_ERR_CUDA;
+  const bool gathering = gather.my_flags != nullptr;
+  prm.err = reinterpret_cast<int32_t*>(ws);
+  prm.work = reinterpret_cast<int32_t*>(ws + 64);  // [next item, CTAs done], inside the header
+  const bool split = plan.max_chunks > 1;
+  prm.counters = split ? reinterpret_cast<int32_t*>(ws + kWsHeader) : nullptr;
+  prm.part_lse = split ? reinterpret_cast<float*>(ws + kWsHeader + plan.counter_bytes) : nullptr;
+  prm.part_o = split ? reinterpret_cast<float*>(ws + kWsHeader + plan.counter_bytes +
+                                                plan.part_lse_bytes)
+                     : nullptr;
+  prm.scale_log2 = scale * 1.4426950408889634f;
+  prm.B = num_seqs;
+  prm.Hq = num_q_heads;
+  prm.Hkv = num_kv_heads;
+  prm.G = num_q_heads / num_kv_heads;
+  prm.P = page_size;
+  prm.chunk_tiles = plan.chunk_tiles;
+  prm.max_chunks = plan.max_chunks;
+  prm.max_rows = plan.max_tiles * kTile;
+  prm.gather = gather;
+
+  for (int l0 = 0; l0 < num_layers; l0 += kMaxLayers) {
+    const int nl = (num_layers - l0) < kMaxLayers ? (num_layers - l0) : kMaxLayers;
+    for (int i = 0; i < nl; ++i) {
+      LayerArgs& a = prm.layer[i];
+      a.q = static_cast<const __nv_bfloat16*>(q[l0 + i]);
+      a.kv = static_cast<const __nv_bfloat16*>(kv[l0 + i]);
+      a.bt = block_tables[l0 + i];
+      a.seq_lens = seq_lens[l0 + i];
+      a.out = static_cast<__nv_bfloat16*>(out[l0 + i]);
+      a.bt_stride = bt_strides[l0 + i];
+      a.num_blocks = num_blocks[l0 + i];
+      if constexpr (Prm::kHasSide) {
+        SideArgs& sa = prm.side[i];
+        sa.pages = nullptr;
+        if (sidecars[l0 + i].pages) {
+          const abkv_sidecar_t& sc = sidecars[l0 + i];
+          sa.pages = static_cast<const __nv_bfloat16*>(sc.pages);
+          sa.bt = sc.page_table;
+          sa.count = sc.page_count;
+          sa.bt_stride = sc.page_table_stride;
+          sa.num_pages = sc.num_pages;
+          sa.slots = sc.slots;
+          for (int h = 0, off = 0; h < num_kv_heads; ++h) {
+            sa.off[h] = off;
+            sa.q[h] = sc.quotas[h];
+            off += sc.quotas[h];
+          }
+        }
+      }
+    }
+    prm.layer_base = l0;
+    prm.nl = nl;
+    prm.num_items = plan.max_chunks * nl * num_seqs;
+    const int grid = prm.num_items < num_sms ? prm.num_items : num_sms;
+    int rc;
+    if constexpr (Prm::kHasSide) {
+      rc = launch_kernel<Prm, false>(prm, head_dim, grid, s);  // the sidecar decode does not gather
+    } else {
+      rc = gathering ? launch_kernel<Prm, true>(prm, head_dim, grid, s)
+                     : launch_kernel<Prm, false>(prm, head_dim, grid, s);
+    }
+    if (rc != ABKV_OK) return rc;
+  }
+  if (cudaGetLastError() != cudaSuccess) return ABKV_ERR_CUDA;
+  return ABKV_OK;
+}
+
 int launch_decode(const void* const* q, const void* const* kv, const int32_t* const* block_tables,
                   const int64_t* bt_strides, const int32_t* const* seq_lens, const int64_t* num_blocks,
                   void* const* out, int num_layers, int num_seqs, int num_q_heads, int num_kv_heads,
@@ -772,75 +885,22 @@ int launch_decode(const void* const* q, const void* const* kv, const int32_t* co
       return ABKV_ERR_INVALID_ARG;
     if (reinterpret_cast<uintptr_t>(block_tables[l]) & 3) return ABKV_ERR_INVALID_ARG;
   }
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   char* ws = static_cast<char*>(workspace);
-  // opt in to > 48 KiB of dynamic shared memory (idempotent, per device)
-  auto kernel = head_dim == 64 ? decode_split_kernel<64> : decode_split_kernel<kD>;
-  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)kSmemBytes) != cudaSuccess)
-    return ABKV_ERR_CUDA;
-  int dev = 0, num_sms = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess ||
-      cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || num_sms <= 0)
-    return ABKV_ERR_CUDA;
-
+  const bool gathering = gather.my_flags != nullptr;
+  if (sidecars) {
+    if (gathering) return ABKV_ERR_UNSUPPORTED;
+    SideDecodeParams prm;
+    memset(&prm, 0, sizeof(prm));
+    return fill_and_launch(prm, plan, q, kv, block_tables, bt_strides, seq_lens, num_blocks, out, num_layers,
+                           num_seqs, num_q_heads, num_kv_heads, head_dim, page_size, scale, ws, stream, gather,
+                           sidecars);
+  }
   DecodeParams prm;
   memset(&prm, 0, sizeof(prm));
-  prm.err = reinterpret_cast<int32_t*>(ws);
-  prm.work = reinterpret_cast<int32_t*>(ws + 64);  // [next item, CTAs done], inside the header
-  const bool split = plan.max_chunks > 1;
-  prm.counters = split ? reinterpret_cast<int32_t*>(ws + kWsHeader) : nullptr;
-  prm.part_lse = split ? reinterpret_cast<float*>(ws + kWsHeader + plan.counter_bytes) : nullptr;
-  prm.part_o = split ? reinterpret_cast<float*>(ws + kWsHeader + plan.counter_bytes +
-                                                plan.part_lse_bytes)
-                     : nullptr;
-  prm.scale_log2 = scale * 1.4426950408889634f;
-  prm.B = num_seqs;
-  prm.Hq = num_q_heads;
-  prm.Hkv = num_kv_heads;
-  prm.G = G;
-  prm.P = page_size;
-  prm.chunk_tiles = plan.chunk_tiles;
-  prm.max_chunks = plan.max_chunks;
-  prm.max_rows = plan.max_tiles * kTile;
-  prm.gather = gather;
-
-  for (int l0 = 0; l0 < num_layers; l0 += kMaxLayers) {
-    const int nl = (num_layers - l0) < kMaxLayers ? (num_layers - l0) : kMaxLayers;
-    for (int i = 0; i < nl; ++i) {
-      LayerArgs& a = prm.layer[i];
-      a.q = static_cast<const __nv_bfloat16*>(q[l0 + i]);
-      a.kv = static_cast<const __nv_bfloat16*>(kv[l0 + i]);
-      a.bt = block_tables[l0 + i];
-      a.seq_lens = seq_lens[l0 + i];
-      a.out = static_cast<__nv_bfloat16*>(out[l0 + i]);
-      a.bt_stride = bt_strides[l0 + i];
-      a.num_blocks = num_blocks[l0 + i];
-      a.side = nullptr;
-      if (sidecars && sidecars[l0 + i].pages) {
-        const abkv_sidecar_t& sc = sidecars[l0 + i];
-        a.side = static_cast<const __nv_bfloat16*>(sc.pages);
-        a.side_bt = sc.page_table;
-        a.side_count = sc.page_count;
-        a.side_bt_stride = sc.page_table_stride;
-        a.side_num_pages = sc.num_pages;
-        a.side_slots = sc.slots;
-        for (int h = 0, off = 0; h < num_kv_heads; ++h) {
-          a.side_off[h] = off;
-          a.side_q[h] = sc.quotas[h];
-          off += sc.quotas[h];
-        }
-      }
-    }
-    prm.layer_base = l0;
-    prm.nl = nl;
-    prm.num_items = plan.max_chunks * nl * num_seqs;
-    const int grid = prm.num_items < num_sms ? prm.num_items : num_sms;
-    kernel<<<grid, kThreads, kSmemBytes, s>>>(prm);
-  }
-  if (cudaGetLastError() != cudaSuccess) return ABKV_ERR_CUDA;
-  return ABKV_OK;
+  return fill_and_launch(prm, plan, q, kv, block_tables, bt_strides, seq_lens, num_blocks, out, num_layers, num_seqs,
+                         num_q_heads, num_kv_heads, head_dim, page_size, scale, ws, stream, gather, nullptr);
 }
+
 }  // namespace
 }  // namespace abkv
 
