@@ -31,8 +31,10 @@
 // otherwise each chunk stores a normalised partial + log-sum-exp and the last
 // chunk to finish for its (layer, sequence) (a counter in the workspace,
 // reset by that chunk) combines them.  The last CTA to run out of work resets
-// the work counters, so a workspace is ready for the next call; concurrent
-// calls must not share a workspace.  Every mbarrier wait is bounded.
+// the work counters; the host clears the chunk counters before each call (a
+// call with another plan may find the previous call's partials there), so a
+// workspace is ready for any later call on the same stream; concurrent calls
+// must not share a workspace.  Every mbarrier wait is bounded.
 #include <cstring>
 #include <mutex>
 
@@ -98,7 +100,8 @@ struct DecodeParams {
   GatherArgs gather;
   float* part_o;      // [layers][B][max_chunks][Hq][D]
   float* part_lse;    // [layers][B][max_chunks][Hq]
-  int32_t* counters;  // [layers][B] chunks finished; zero between calls
+  int32_t* counters;  // [layers][B] (CTA epilogue) or [layers][B][Hkv] (warp epilogue) chunks
+                      // finished; cleared by the host before each call
   int32_t* work;      // [2]: next item, CTAs done; zero between calls
   int32_t* err;
   float scale_log2;
@@ -106,6 +109,7 @@ struct DecodeParams {
   int chunk_tiles, max_chunks, max_rows;
   int layer_base, nl;
   int num_items;
+  int warp_epi;  // 1: per-warp epilogue (one consumer warp per KV head, 16-byte aligned outputs)
   static constexpr bool kHasSide = false;
 };
 
@@ -187,6 +191,33 @@ __device__ __forceinline__ void store_out(const DecodeParams& p, const LayerArgs
   } else {
     L.out[((int64_t)b * p.Hq + hr) * D + d] = v;
   }
+}
+
+// Eight consecutive dims [d0, d0 + 8) of row (b, hr) as one 16-byte store (per rank when gathering).
+template <int D, bool kGather>
+__device__ __forceinline__ void store_out8(const DecodeParams& p, const LayerArgs& L, int b, int hr, int d0,
+                                           const float (&v)[8]) {
+  uint4 u;
+  u.x = pack_bf16x2(v[0], v[1]);
+  u.y = pack_bf16x2(v[2], v[3]);
+  u.z = pack_bf16x2(v[4], v[5]);
+  u.w = pack_bf16x2(v[6], v[7]);
+  if constexpr (kGather) {
+    const GatherArgs& g = p.gather;
+    __nv_bfloat16* dst = L.out + (int64_t)b * g.out_row + (int64_t)(g.head0 + hr) * D + d0;
+    for (int r = 0; r < g.world; ++r) *reinterpret_cast<uint4*>(dst + g.peer_delta[r]) = u;
+  } else {
+    *reinterpret_cast<uint4*>(L.out + ((int64_t)b * p.Hq + hr) * D + d0) = u;
+  }
+}
+
+// Chunk count of a (layer, sequence[, KV head]): the release publishes this
+// warp's partial stores (ordered before it by __syncwarp), the acquire makes the
+// other chunks' partials visible to the warp that sees the final count.
+__device__ __forceinline__ int atom_add_acq_rel_gpu(int32_t* ptr, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;\n" : "=r"(old) : "l"(ptr), "r"(v) : "memory");
+  return old;
 }
 
 __device__ __forceinline__ void st_release_sys(uint32_t* ptr, uint32_t v) {
@@ -419,6 +450,117 @@ __device__ void producer(const Prm& p, uint8_t* smem) {
 }
 
 // ---------------------------------------------------------------------------
+// End of an item when each consumer warp owns one KV head (8 KV heads): the
+// warp's registers hold the item's complete result for its G query heads, so it
+// writes the output rows (single-chunk items) or its partial rows + log-sum-exp
+// itself, counts the chunk for (layer, sequence, KV head) and, if it finished
+// the last one, combines that head's chunk partials -- no shared memory, no CTA
+// barrier, so the other warps keep consuming stages meanwhile.  Lane (g, c)
+// holds dims [8g, 8g + 8) + 64 hh of query heads 2c and 2c + 1 (o[4 hh + i][jh]
+// = dim 8g + 64 hh + 2i, o[4 hh + i][2 + jh] = the next dim); the row statistics
+// of query head r sit in lanes 4r..4r+3.  Arithmetic as the shared-memory merge
+// (one warp: weight exp2(0) = 1) and combine, so both epilogues give the same bits.
+template <int D, bool kGather>
+__device__ __forceinline__ void warp_epilogue(const DecodeParams& p, const LayerArgs& L, const StageMeta& M, int h,
+                                              int lane, const float (&o)[D / 16][4], float m_run, float l_run) {
+  constexpr int kVH = D / 64;
+  const int g = lane >> 2, c = lane & 3, G = p.G;
+  float lq = l_run;
+  lq += __shfl_xor_sync(0xffffffffu, lq, 1);
+  lq += __shfl_xor_sync(0xffffffffu, lq, 2);
+  float mh[2], lh[2];
+  mh[0] = __shfl_sync(0xffffffffu, m_run, 8 * c);
+  mh[1] = __shfl_sync(0xffffffffu, m_run, 8 * c + 4);
+  lh[0] = __shfl_sync(0xffffffffu, lq, 8 * c);
+  lh[1] = __shfl_sync(0xffffffffu, lq, 8 * c + 4);
+  const int n_chunks = M.n_chunks;
+  const int64_t lb = (int64_t)(p.layer_base + M.li) * p.B + M.b;
+  if (n_chunks == 1) {
+#pragma unroll
+    for (int jh = 0; jh < 2; ++jh) {
+      const int head = 2 * c + jh;
+      if (head >= G) continue;
+      const float Ls = lh[jh];
+#pragma unroll
+      for (int hh = 0; hh < kVH; ++hh) {
+        float v[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          v[2 * i] = Ls > 0.f ? o[4 * hh + i][jh] / Ls : 0.f;
+          v[2 * i + 1] = Ls > 0.f ? o[4 * hh + i][2 + jh] / Ls : 0.f;
+        }
+        store_out8<D, kGather>(p, L, M.b, h * G + head, 64 * hh + 8 * g, v);
+      }
+    }
+    return;
+  }
+  const int64_t prow = (lb * p.max_chunks + M.chunk) * p.Hq;
+#pragma unroll
+  for (int jh = 0; jh < 2; ++jh) {
+    const int head = 2 * c + jh;
+    if (head >= G) continue;
+    const int hr = h * G + head;
+    const float Ls = lh[jh];
+#pragma unroll
+    for (int hh = 0; hh < kVH; ++hh) {
+      float v[8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        v[2 * i] = Ls > 0.f ? o[4 * hh + i][jh] / Ls : 0.f;
+        v[2 * i + 1] = Ls > 0.f ? o[4 * hh + i][2 + jh] / Ls : 0.f;
+      }
+      float4* dst = reinterpret_cast<float4*>(p.part_o + (prow + hr) * D + 64 * hh + 8 * g);
+      dst[0] = make_float4(v[0], v[1], v[2], v[3]);
+      dst[1] = make_float4(v[4], v[5], v[6], v[7]);
+    }
+    if (g == 0) p.part_lse[prow + hr] = Ls > 0.f ? mh[jh] + log2f(Ls) : -INFINITY;
+  }
+  __syncwarp();
+  int prev = 0;
+  int32_t* counter = p.counters + lb * p.Hkv + h;
+  if (lane == 0) prev = atom_add_acq_rel_gpu(counter, 1);
+  __syncwarp();
+  prev = __shfl_sync(0xffffffffu, prev, 0);
+  if (prev != n_chunks - 1) return;
+  if (lane == 0) *counter = 0;  // ready for the next call on this workspace
+  const int64_t row0 = lb * p.max_chunks * p.Hq;
+#pragma unroll
+  for (int jh = 0; jh < 2; ++jh) {
+    const int head = 2 * c + jh;
+    if (head >= G) continue;
+    const int hr = h * G + head;
+    float Mx = -INFINITY;
+    for (int ch = 0; ch < n_chunks; ++ch) Mx = fmaxf(Mx, __ldcg(p.part_lse + row0 + (int64_t)ch * p.Hq + hr));
+    const float Mu = (Mx == -INFINITY) ? 0.f : Mx;
+    float Ls = 0.f, acc[kVH][8];
+#pragma unroll
+    for (int hh = 0; hh < kVH; ++hh)
+#pragma unroll
+      for (int k = 0; k < 8; ++k) acc[hh][k] = 0.f;
+#pragma unroll 2
+    for (int ch = 0; ch < n_chunks; ++ch) {
+      const int64_t rr = row0 + (int64_t)ch * p.Hq + hr;
+      const float f = exp2f(__ldcg(p.part_lse + rr) - Mu);
+      Ls += f;
+#pragma unroll
+      for (int hh = 0; hh < kVH; ++hh) {
+        const float4* src = reinterpret_cast<const float4*>(p.part_o + rr * D + 64 * hh + 8 * g);
+        const float4 a = __ldcg(src), bq = __ldcg(src + 1);
+        acc[hh][0] += f * a.x; acc[hh][1] += f * a.y; acc[hh][2] += f * a.z; acc[hh][3] += f * a.w;
+        acc[hh][4] += f * bq.x; acc[hh][5] += f * bq.y; acc[hh][6] += f * bq.z; acc[hh][7] += f * bq.w;
+      }
+    }
+#pragma unroll
+    for (int hh = 0; hh < kVH; ++hh) {
+      float v[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) v[k] = Ls > 0.f ? acc[hh][k] / Ls : 0.f;
+      store_out8<D, kGather>(p, L, M.b, hr, 64 * hh + 8 * g, v);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // D = head_dim: the Q.K^T product runs over D / 32 chunks of 32 dims (8 per lane),
 // P.V over D / 64 halves of 64 dims, O^T in D / 16 accumulator tiles.
 template <int D, class Prm, bool kGather>
@@ -562,6 +704,12 @@ __device__ void consumer(const Prm& p, uint8_t* smem) {
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[st]);  // this warp is done with the stage
     if (!(M.bits & kLast)) continue;
+    if constexpr (!Prm::kHasSide) {
+      if (p.warp_epi) {
+        warp_epilogue<D, kGather>(p, L, M, h, lane, o, m_run, l_run);
+        continue;
+      }
+    }
 
     // ---- end of item: merge warp partials, write output or chunk partial ----
     float lq = l_run;
@@ -721,7 +869,8 @@ int plan_decode(int num_layers, int num_seqs, int num_q_heads, int head_dim, int
   plan->max_chunks = (int)((max_tiles + ct - 1) / ct + (side_tiles ? (side_tiles + ct - 1) / ct + 2 * kWarps : 0));
   if (plan->max_chunks > 1) {
     const size_t rows = (size_t)num_layers * num_seqs * plan->max_chunks * num_q_heads;
-    plan->counter_bytes = ((size_t)num_layers * num_seqs * sizeof(int32_t) + 255) / 256 * 256;
+    // one counter per (layer, sequence, KV head); num_q_heads bounds the KV heads
+    plan->counter_bytes = ((size_t)num_layers * num_seqs * num_q_heads * sizeof(int32_t) + 255) / 256 * 256;
     plan->part_o_bytes = rows * head_dim * sizeof(float);
     plan->part_lse_bytes = ((rows * sizeof(float)) + 255) / 256 * 256;
   } else {
@@ -788,6 +937,19 @@ int fill_and_launch(Prm& prm, const DecodePlan& plan, const void* const* q, cons
   prm.max_chunks = plan.max_chunks;
   prm.max_rows = plan.max_tiles * kTile;
   prm.gather = gather;
+  // Per-warp epilogue: one consumer warp per KV head and 16-byte stores into
+  // every output (and every rank's copy of it).
+  bool warp_epi = !Prm::kHasSide && num_kv_heads == kWarps;
+  for (int l = 0; l < num_layers && warp_epi; ++l)
+    if (reinterpret_cast<uintptr_t>(out[l]) & 15) warp_epi = false;
+  if (gathering)
+    for (int r = 0; r < gather.world && warp_epi; ++r)
+      if ((gather.peer_delta[r] * 2) & 15) warp_epi = false;
+  prm.warp_epi = warp_epi ? 1 : 0;
+  // The chunk counters must start at zero.  Each launch resets the ones it used,
+  // but a call with a larger plan on the same workspace would also find, in its
+  // counter range, the previous plan's partials: clear them on the stream.
+  if (split && cudaMemsetAsync(prm.counters, 0, plan.counter_bytes, s) != cudaSuccess) return ABKV_ERR_CUDA;
 
   for (int l0 = 0; l0 < num_layers; l0 += kMaxLayers) {
     const int nl = (num_layers - l0) < kMaxLayers ? (num_layers - l0) : kMaxLayers;

@@ -158,3 +158,29 @@ def test_config2_full_size_sampled_rows_and_page_permutation():
         o1 = decode.paged_decode([wl.queries[l]], [wl.kv_caches[l]], [wl.block_tables[l]],
                                  [wl.seq_lens[l]], max_pages_per_seq=wl.max_pages, chunk_tokens=1024)[0]
         assert torch.equal(o1, outs[l])
+
+
+def _random_layers(L, B=48, Hq=32, Hkv=8, D=128, page=16, max_pages=64, seed=0):
+    g = torch.Generator("cuda").manual_seed(seed)
+    qs, kvs, bts, sls = [], [], [], []
+    for _ in range(L):
+        nb = B * max_pages
+        kvs.append(torch.randn((nb, 2, page, Hkv, D), generator=g, device="cuda").to(torch.bfloat16))
+        qs.append(torch.randn((B, Hq, D), generator=g, device="cuda").to(torch.bfloat16))
+        bts.append(torch.randperm(nb, generator=g, device="cuda").to(torch.int32).view(B, max_pages).contiguous())
+        sls.append(torch.randint(0, max_pages * page + 1, (B,), generator=g, device="cuda", dtype=torch.int32))
+    return qs, kvs, bts, sls
+
+
+def test_workspace_reuse_across_plans():
+    """A workspace used by a small split launch (its partials land where a larger plan keeps
+    its chunk counters) gives the larger plan the same rows as a fresh workspace."""
+    qs, kvs, bts, sls = _random_layers(4)
+    ws = Workspace()
+    fresh = decode.paged_decode(qs, kvs, bts, sls, chunk_tokens=64, workspace=Workspace())
+    for _ in range(2):
+        decode.paged_decode(qs[:1], kvs[:1], bts[:1], sls[:1], chunk_tokens=64, workspace=ws)
+        again = decode.paged_decode(qs, kvs, bts, sls, chunk_tokens=64, workspace=ws)
+        assert ws.read_error() == 0
+        for a, b in zip(again, fresh):
+            assert torch.equal(a, b)

@@ -109,3 +109,31 @@ def test_packed_decode_without_sidecar_equals_plain_decode():
     both = packed_decode([q, q], [kv, kv], [bt, bt], [sl, sl], [None, pool], scale=case.scale)
     assert torch.equal(both[0], plain)
     assert not torch.equal(both[1], plain)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("chunk_tokens", [0, 32])
+def test_packed_decode_repeat_calls_on_one_workspace_are_identical(chunk_tokens):
+    """Work items past a request's last chunk are claimed and skipped; a skipped item must not
+    change the chunking of the next one, and every call leaves the workspace counters at zero,
+    so repeated launches on one workspace give bit-identical rows with no device error."""
+    from abridgekv_b200.sidecar import packed_decode
+    from abridgekv_b200.workspace import Workspace
+    from tests.goldens import load_packed, packed_cases
+
+    for name in packed_cases():
+        case, side, counts, quotas, k_max, _ = load_packed(name)
+        if chunk_tokens and chunk_tokens % case.page:
+            continue
+        layout = PackedKVLayout.from_schedule([list(quotas)], num_layers=1, num_kv_heads=len(quotas), k_max=k_max)
+        pool = _pool(layout, side, counts, case.q.shape[-1])
+        q = torch.from_numpy(case.q).to(torch.bfloat16).cuda()
+        kv = torch.from_numpy(case.kv).to(torch.bfloat16).cuda()
+        bt, sl = torch.from_numpy(case.block_table).cuda(), torch.from_numpy(case.seq_lens).cuda()
+        ws = Workspace()
+        outs = [packed_decode([q, q], [kv, kv], [bt, bt], [sl, sl], [pool, pool], scale=case.scale,
+                              chunk_tokens=chunk_tokens, workspace=ws) for _ in range(4)]
+        torch.cuda.synchronize()
+        assert ws.read_error() == 0, name
+        for o in outs[1:]:
+            assert torch.equal(o[0], outs[0][0]) and torch.equal(o[1], outs[0][0]), name
