@@ -22,7 +22,7 @@ from . import decode
 from .workspace import Workspace, default_workspace
 
 
-def split_layers(num_layers: int, max_group: int = 12, edge: int = 1) -> list[range]:
+def split_layers(num_layers: int, max_group: int = 16, edge: int = 2) -> list[range]:
     """Launch groups for ``num_layers`` layers: ``edge`` layers first and last (their copies are
     the only ones not hidden behind a decode), the rest in near-equal groups of at most
     ``max_group`` layers (each group is one persistent launch, so fewer groups means fewer
