@@ -329,19 +329,19 @@ __global__ void __launch_bounds__(kThreads, 1) codestep_kernel(const __grid_cons
       const uint32_t qa = smem_u32(smem + kOffQ), qbv = qa + kQBytes;
       const uint32_t sA = tmem, oA = tmem + 128, sB = tmem + 256, oB = tmem + 384;
       auto issue_s = [&](uint32_t qaddr, uint32_t sd, int st) {
-        const uint32_t kaddr = smem_u32(smem + kOffKV + st * kStageBytes);
+        const uint64_t dq = desc_kmajor_sw128(qaddr);
+        const uint64_t dk = desc_kmajor_sw128(smem_u32(smem + kOffKV + st * kStageBytes));
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {  // over head_dim in steps of 16
-          umma(sd, desc_kmajor_sw128(qaddr + (kk >> 2) * (kQBytes / 2) + (kk & 3) * 32),
-               desc_kmajor_sw128(kaddr + (kk >> 2) * (kKVHalf / 2) + (kk & 3) * 32), kIdescQK, kk > 0 ? 1u : 0u);
+          umma(sd, desc_advance(dq, (kk >> 2) * (kQBytes / 2) + (kk & 3) * 32),
+               desc_advance(dk, (kk >> 2) * (kKVHalf / 2) + (kk & 3) * 32), kIdescQK, kk > 0 ? 1u : 0u);
         }
       };
       auto issue_pv = [&](uint32_t ptmem, uint32_t od, int st, bool first) {
-        const uint32_t vaddr = smem_u32(smem + kOffKV + st * kStageBytes + kKVHalf);
+        const uint64_t dv = desc_mnmajor_sw128(smem_u32(smem + kOffKV + st * kStageBytes + kKVHalf), kKVHalf / 2);
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk) {  // over the tile's keys in steps of 16 (8 TMEM columns)
-          umma_tmem_a(od, ptmem + kk * 8, desc_mnmajor_sw128(vaddr + kk * 2048, kKVHalf / 2), kIdescPV,
-                      (!first || kk > 0) ? 1u : 0u);
+          umma_tmem_a(od, ptmem + kk * 8, desc_advance(dv, kk * 2048), kIdescPV, (!first || kk > 0) ? 1u : 0u);
         }
       };
       // tile sequence; S of tile j goes to S buffer j % 2 of each head

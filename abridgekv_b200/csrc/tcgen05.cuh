@@ -51,6 +51,11 @@ static __device__ __forceinline__ uint64_t desc_mnmajor_sw128(uint32_t saddr, ui
   return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
          ((uint64_t)(1024 >> 4) << 32) | ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
+// The descriptor of the same operand `bytes` further on in shared memory (bytes a
+// multiple of 16).  Shared memory addresses stay below 256 KiB, so the 14-bit
+// start-address field (address >> 4) cannot carry into the next field: one add
+// instead of rebuilding the descriptor for every instruction of an unrolled loop.
+static __device__ __forceinline__ uint64_t desc_advance(uint64_t desc, uint32_t bytes) { return desc + (bytes >> 4); }
 // kind::f16 instruction descriptor: D f32 (bit 4), A and B bf16 (bits 7, 10),
 // B MN-major if b_mn_major (bit 16; A is K-major), N >> 3 at bit 17, M >> 4 at
 // bit 24 (M = 128).
