@@ -733,16 +733,18 @@ __device__ void consumer(const Prm& p, uint8_t* smem) {
       s_l[warp][g] = lq;
     }
     consumer_sync();
-    const int items = p.Hq * D;
+    // four consecutive dims per thread and step: 16-byte shared-memory reads and partial stores
+    constexpr int kD4 = D / 4;
+    const int items4 = p.Hq * kD4;
     const int n_chunks = M.n_chunks;
     const int64_t lb = (int64_t)(p.layer_base + M.li) * p.B + M.b;  // (layer, sequence) slot
     const int64_t prow = (lb * p.max_chunks + M.chunk) * p.Hq;
-    for (int it = threadIdx.x; it < items; it += kConsumerThreads) {
-      const int d = it % D, hr = it / D;
+    for (int it = threadIdx.x; it < items4; it += kConsumerThreads) {
+      const int d0 = (it % kD4) * 4, hr = it / kD4;
       const int kh = hr / G, r = hr % G;
       if (side_grp && kh != hw) {
         // a sidecar item covers one KV head: the other heads' rows of this chunk are empty
-        if (d == 0 && n_chunks > 1) p.part_lse[prow + hr] = -INFINITY;
+        if (d0 == 0 && n_chunks > 1) p.part_lse[prow + hr] = -INFINITY;
         continue;
       }
       // warps holding this row: all of them for a sidecar item, else those of head kh
@@ -750,49 +752,64 @@ __device__ void consumer(const Prm& p, uint8_t* smem) {
       float Mx = -INFINITY;
       for (int s2 = 0; s2 < nw; ++s2) Mx = fmaxf(Mx, s_m[w0 + s2 * dw][r]);
       const float Mu = (Mx == -INFINITY) ? 0.f : Mx;
-      float Ls = 0.f, Os = 0.f;
+      float Ls = 0.f, Os[4] = {0.f, 0.f, 0.f, 0.f};
       for (int s2 = 0; s2 < nw; ++s2) {
         const int w = w0 + s2 * dw;
         const float f = exp2f(s_m[w][r] - Mu);
         Ls += s_l[w][r] * f;
-        Os += s_o[w][r][d] * f;
+        const float4 ov = *reinterpret_cast<const float4*>(&s_o[w][r][d0]);
+        Os[0] += ov.x * f;
+        Os[1] += ov.y * f;
+        Os[2] += ov.z * f;
+        Os[3] += ov.w * f;
       }
-      const float val = Ls > 0.f ? Os / Ls : 0.f;
+      float val[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) val[k] = Ls > 0.f ? Os[k] / Ls : 0.f;
       if (n_chunks == 1) {
-        store_out<D, kGather>(p, L, M.b, hr, d, val);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) store_out<D, kGather>(p, L, M.b, hr, d0 + k, val[k]);
       } else {
-        p.part_o[(prow + hr) * D + d] = val;
-        if (d == 0) p.part_lse[prow + hr] = Ls > 0.f ? Mu + log2f(Ls) : -INFINITY;
+        *reinterpret_cast<float4*>(p.part_o + (prow + hr) * D + d0) = make_float4(val[0], val[1], val[2], val[3]);
+        if (d0 == 0) p.part_lse[prow + hr] = Ls > 0.f ? Mu + log2f(Ls) : -INFINITY;
       }
     }
     if (n_chunks > 1) {
-      // the last chunk of this (layer, sequence) combines all chunk partials
-      __threadfence();
+      // The last chunk of this (layer, sequence) combines all chunk partials.  The barrier
+      // orders every thread's partial stores before thread 0's acq_rel count (a cumulative
+      // release at GPU scope); the count's acquire side plus the next barrier order the
+      // combine's loads after the other chunks' releases.
       consumer_sync();
       if (threadIdx.x == 0) {
-        const int prev = atomicAdd(p.counters + lb, 1);
+        const int prev = atom_add_acq_rel_gpu(p.counters + lb, 1);
         *s_flag = (prev == n_chunks - 1);
       }
       consumer_sync();
       if (*s_flag) {
-        __threadfence();
         const int64_t row0 = lb * p.max_chunks * p.Hq;
-        for (int it = threadIdx.x; it < items; it += kConsumerThreads) {
-          const int d = it % D, hr = it / D;
+        for (int it = threadIdx.x; it < items4; it += kConsumerThreads) {
+          const int d0 = (it % kD4) * 4, hr = it / kD4;
           float Mx = -INFINITY;
+#pragma unroll 4
           for (int ch = 0; ch < n_chunks; ++ch)
             Mx = fmaxf(Mx, __ldcg(p.part_lse + row0 + (int64_t)ch * p.Hq + hr));
           const float Mu = (Mx == -INFINITY) ? 0.f : Mx;
-          float Ls = 0.f, Os = 0.f;
+          float Ls = 0.f, Os[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 2
           for (int ch = 0; ch < n_chunks; ++ch) {
             const int64_t rr = row0 + (int64_t)ch * p.Hq + hr;
             const float lse = __ldcg(p.part_lse + rr);
             if (Prm::kHasSide && lse == -INFINITY) continue;  // empty sidecar chunk: its O was not written
             const float f = exp2f(lse - Mu);
             Ls += f;
-            Os += f * __ldcg(p.part_o + rr * D + d);
+            const float4 ov = __ldcg(reinterpret_cast<const float4*>(p.part_o + rr * D + d0));
+            Os[0] += f * ov.x;
+            Os[1] += f * ov.y;
+            Os[2] += f * ov.z;
+            Os[3] += f * ov.w;
           }
-          store_out<D, kGather>(p, L, M.b, hr, d, Ls > 0.f ? Os / Ls : 0.f);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) store_out<D, kGather>(p, L, M.b, hr, d0 + k, Ls > 0.f ? Os[k] / Ls : 0.f);
         }
         if (threadIdx.x == 0) p.counters[lb] = 0;  // ready for the next call on this workspace
       }
