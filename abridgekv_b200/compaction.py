@@ -19,6 +19,7 @@ FlashInfer ``[num_blocks, 2, page, Hkv, D]``.  The copy is byte-exact for any
 from __future__ import annotations
 
 import itertools
+from collections.abc import Sequence as _SequenceABC
 from typing import Hashable, Sequence
 
 import numpy as np
@@ -26,6 +27,50 @@ import torch
 
 from . import _lib
 from .workspace import Workspace, default_workspace
+
+
+class CopyOps(_SequenceABC):
+    """One ordered batch of ``(src_block, src_off, dst_block, dst_off)`` copy operations held as
+    an int32 array ``[n, 4]``.  It behaves like the reference's list of tuples (length, indexing,
+    iteration, equality with a list), so callers of ``take_pending`` see the reference structure,
+    while the executor hands the array to the kernel without a round trip through Python ints."""
+
+    __slots__ = ("array",)
+
+    def __init__(self, array) -> None:
+        self.array = np.ascontiguousarray(np.asarray(array, dtype=np.int32).reshape(-1, 4))
+
+    def __len__(self) -> int:
+        return int(self.array.shape[0])
+
+    def __getitem__(self, i):
+        if isinstance(i, slice):
+            return CopyOps(self.array[i])
+        return tuple(int(v) for v in self.array[i])
+
+    def __iter__(self):
+        return iter(map(tuple, self.array.tolist()))
+
+    def __eq__(self, other) -> bool:
+        if isinstance(other, CopyOps):
+            return bool(np.array_equal(self.array, other.array))
+        try:
+            return list(self) == [tuple(op) for op in other]
+        except TypeError:
+            return NotImplemented
+
+    def __repr__(self) -> str:
+        return f"CopyOps({list(self)!r})"
+
+
+def _flatten(batches) -> tuple[np.ndarray, list[int]]:
+    """Concatenated [4 x ops] int32 and per-batch counts of a list of batches."""
+    counts = [len(b) for b in batches]
+    if batches and all(isinstance(b, CopyOps) for b in batches):
+        return np.concatenate([b.array for b in batches]).reshape(-1), counts
+    flat = np.fromiter(itertools.chain.from_iterable(itertools.chain.from_iterable(batches)), dtype=np.int32,
+                       count=4 * sum(counts))
+    return flat, counts
 
 
 def _layout_of(kv: torch.Tensor) -> tuple[int, int, int, int, int]:
@@ -54,12 +99,10 @@ def _compact(layer_caches: Sequence[torch.Tensor], batches: Sequence[Sequence[Se
     elem = kv0.element_size()
     # the kernel moves rows as bytes: express the row as 2-byte units
     units = hkv * d * elem // 2
-    counts = [len(b) for b in batches]
     n_batches = len(batches)
-    if sum(counts) == 0:
+    if sum(len(b) for b in batches) == 0:
         return
-    flat = np.fromiter(itertools.chain.from_iterable(itertools.chain.from_iterable(batches)), dtype=np.int32,
-                       count=4 * sum(counts))
+    flat, counts = _flatten(batches)
     offsets = np.zeros(n_batches + 1, dtype=np.int64)
     np.cumsum(counts, out=offsets[1:])
     max_ops = max(counts)
@@ -91,11 +134,12 @@ def execute_kv_copy_operations(kv_copy_operations: dict[Hashable, list[list[list
         nb = max((len(b) for b in per_req), default=0)
         batches = []
         for b in range(nb):
-            merged = []
-            for req_batches in per_req:
-                if b < len(req_batches):
-                    merged.extend(req_batches[b])
-            if merged:
+            parts = [req_batches[b] for req_batches in per_req if b < len(req_batches)]
+            if parts and all(isinstance(x, CopyOps) for x in parts):
+                merged = CopyOps(np.concatenate([x.array for x in parts]))
+            else:
+                merged = [tuple(op) for x in parts for op in x]
+            if len(merged):
                 batches.append(merged)
         if batches:
             _compact(layer_caches, batches, workspace, stream)

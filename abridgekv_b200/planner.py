@@ -8,6 +8,8 @@ Mirrors the scheduler-side interfaces of the reference's vLLM overlay:
 * ``take_pending()`` returns the worker-bound structure of
   ``Scheduler.pending_kv_copy_operations``: request -> per KV-cache group ->
   ORDERED list of batches -> list of ``(src_block, src_off, dst_block, dst_off)``
+  (each batch a ``compaction.CopyOps``: it reads like the reference's list of
+  tuples and carries the int32 array the executor passes to the kernel)
   (consumed by ``GPUModelRunner._execute_kv_copy_operations``,
   vllm/v1/worker/gpu_model_runner.py:1147-1176).
 * ``finish_block`` is the physical-quota branch of
@@ -29,6 +31,7 @@ from typing import Hashable, Iterable, Sequence
 import numpy as np
 
 from . import _lib
+from .compaction import CopyOps
 
 
 @dataclass
@@ -209,8 +212,7 @@ class BlockPlanner:
                     _lib.check("abkv_planner_pending_batch",
                                self._lib.abkv_planner_pending_batch(self._h, k, g, b, buf, cnt.value,
                                                                     C.byref(cnt)))
-                    rows = np.frombuffer(buf, dtype=np.int32, count=4 * cnt.value).reshape(-1, 4)
-                    batches.append(list(zip(*rows.T.tolist())))
+                    batches.append(CopyOps(np.frombuffer(buf, dtype=np.int32, count=4 * cnt.value).copy()))
                 per_group.append(batches)
             ops[self._names.get(k, k)] = per_group
         trunc = {}

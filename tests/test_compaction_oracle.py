@@ -144,3 +144,23 @@ def _random_serving(seed, G=3, K=16, C=32, page=4, pool=600, n_req=5):
 @pytest.mark.parametrize("seed", range(6))
 def test_cpp_planner_matches_oracle_random_serving(seed):
     _random_serving(seed)
+
+
+def test_copy_ops_reads_like_reference_lists_and_flattens_identically():
+    """take_pending batches (CopyOps) compare, index and iterate like the reference's lists of
+    (src_block, src_off, dst_block, dst_off) tuples, and the executor flattens them to the same
+    int32 buffer as the plain-list form."""
+    import numpy as np
+    from abridgekv_b200.compaction import CopyOps, _flatten
+
+    rng = np.random.default_rng(0)
+    arrays = [rng.integers(0, 5000, size=(n, 4)).astype(np.int32) for n in (3, 0, 17)]
+    ops = [CopyOps(a) for a in arrays]
+    lists = [[tuple(int(v) for v in row) for row in a] for a in arrays]
+    for o, l in zip(ops, lists):
+        assert o == l and list(o) == l and len(o) == len(l)
+        if l:
+            assert o[0] == l[0] and o[-1] == l[-1] and list(o[1:]) == l[1:]
+    f_fast, c_fast = _flatten(ops)
+    f_list, c_list = _flatten(lists)
+    assert c_fast == c_list and np.array_equal(f_fast, f_list)
