@@ -97,6 +97,11 @@ SIGNATURES: dict[str, tuple] = {
     "abkv_prefill_masked": (c_int, [c_vp, c_i64p, c_vp, c_i64p, c_vp, c_i64p, c_vp, c_i64p, c_vp, c_i32p, c_vp,
                                     c_int, c_int, c_int, c_int, c_int, c_int, c_int, C.c_float, c_vp, c_size,
                                     c_vp]),
+    "abkv_prefill_masked_backward_workspace_size": (c_size, [c_int, c_int, c_int, c_int]),
+    "abkv_prefill_masked_backward": (c_int, [c_vp, c_i64p, c_vp, c_i64p, c_vp, c_i64p, c_vp, c_i64p, c_vp,
+                                             c_i64p, c_vp, c_vp, c_i64p, c_vp, c_i64p, c_vp, c_i64p, c_i32p,
+                                             c_vp, c_int, c_int, c_int, c_int, c_int, c_int, c_int, C.c_float,
+                                             c_vp, c_size, c_vp]),
     "abkv_code_step_attention": (c_int, [c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_vp, c_int, c_i64, c_int,
                                          c_vp, c_i64, c_vp, c_vp, c_i32p, c_int, c_int, c_int, c_int, c_int,
                                          c_int, C.c_float, c_vp, c_size, c_vp]),

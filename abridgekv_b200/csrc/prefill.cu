@@ -46,11 +46,14 @@
 // Every mbarrier wait is bounded and records ABKV_DEVERR_TIMEOUT on expiry.
 #include <cstring>
 
+#include "prefill_mask.cuh"
 #include "tcgen05.cuh"
 
 namespace abkv {
 namespace {
 using namespace tc;
+using mask::tile_class;
+using mask::tile_limit_fast;
 
 constexpr int kBM = 128, kBN = 128;  // head_dim D is 64 or 128 (template parameter)
 constexpr int kThreads = 320;
@@ -100,54 +103,6 @@ struct alignas(64) PrefillParams {
   int B, H, Hkv, G, npairs, S, C, KL, per, n_qtiles;
   float scale_log2;
 };
-
-// 0 = empty, 1 = full, 2 = partial, for query tile qt / key tile kt of head h.
-__device__ __forceinline__ int tile_class(const PrefillParams& p, int h, int qt, int kt, int pl) {
-  const int q0 = qt * kBM, q1 = q0 + kBM - 1;
-  const int k0 = kt * kBN, k1 = k0 + kBN - 1;
-  const int qb = q0 / p.per, kb = k0 / p.per;
-  if (kb > qb) return 0;
-  const int qw0 = q0 - qb * p.per;
-  const int kw0 = k0 - kb * p.per, kw1 = k1 - kb * p.per;
-  const bool q_code = qw0 >= p.C;
-  if (kw0 < p.C) {  // content keys
-    if (kb == qb) {  // own block: causal (the raw-prompt term adds nothing here)
-      if (q_code || k1 <= q0) return 1;
-      if (k0 > q1) return 0;
-      return 2;
-    }
-    // earlier block: visible only as raw prompt (kb*C + kw < prompt_len)
-    const int a0 = kb * p.C + kw0, a1 = kb * p.C + kw1;
-    if (a1 < pl) return 1;
-    if (a0 >= pl) return 0;
-    return 2;
-  }
-  // code keys: quota on the slot; own block only for code queries
-  const int s0 = kw0 - p.C, s1 = kw1 - p.C;
-  const int qq = p.quota[h];
-  const int qc = (s1 < qq) ? 1 : (s0 >= qq ? 0 : 2);
-  if (kb < qb) return qc;
-  return q_code ? qc : 0;
-}
-
-// Inside any tile the visible keys of one query row are a PREFIX of the tile's
-// columns: the causal diagonal of the own block (kv <= q), the raw-prompt
-// boundary of an earlier block (kb*C + kw < prompt_len) or the quota boundary
-// of a code tile (kw - C < quota).  tile_limit_fast returns that prefix length
-// in [0, kBN] from precomputed coordinates: the row's block qb and in-block
-// offset qw, the tile's block kb and in-block offset kw0 (k0 = key tile start).
-__device__ __forceinline__ int tile_limit_fast(const PrefillParams& p, int quota, int q, int qb, int qw, int kb,
-                                               int kw0, int k0, int pl) {
-  int lim;
-  if (kw0 < p.C) {
-    if (kb == qb) lim = (qw >= p.C) ? kBN : q - k0 + 1;
-    else lim = pl - (kb * p.C + kw0);
-  } else {
-    if (kb == qb && qw < p.C) return 0;
-    lim = quota - (kw0 - p.C);
-  }
-  return lim < 0 ? 0 : (lim > kBN ? kBN : lim);
-}
 
 // Softmax of one (head, 128-key tile) for query row `row` (= TMEM lane).
 // tmem_s / tmem_o already carry this warp's lane base.  Pass 1 reads the row of

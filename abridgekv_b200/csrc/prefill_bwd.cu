@@ -1,0 +1,515 @@
+// Backward of the pause-token prefill attention (dQ, dK, dV) on 5th-generation
+// tensor cores (tcgen05 + TMEM) for sm_100a: the gradients of the training
+// path, which the reference runs through torch FlexAttention's backward with
+// the mask of CompressLM._arith_mask_mod (abridgekv/compress_forward.py:248,
+// 695-727, 1229; training: sft_ddp.py:1225).
+//
+// With P = softmax(scale q k^T + mask) recomputed from the forward's log-sum-exp:
+//   dV = sum_h P^T dO            dP = dO V^T          Di = rowsum(dO * O)
+//   dS = P * (dP - Di)           dQ = scale dS K      dK = scale sum_h dS^T Q
+// (sums over the query heads h of a KV head).
+//
+// CTA = one 128-key tile of one KV head; it walks every (query tile, query head
+// of the group) pair whose 128 x 128 tile the mask does not empty, keeping dK and
+// dV in TMEM, and adds each pair's dQ tile into an fp32 buffer with vector
+// reductions.  6 warps:
+//   warp 0      TMA: the CTA's K and V tiles once, then Q and dO of each pair
+//               (cp.async.bulk.tensor, 128B swizzle, no multicast)
+//   warp 1      TMEM owner (512 columns) and MMA issuer, per pair:
+//                 S^T  = K Q^T  -> [0,128)     dP^T = V dO^T -> [128,256)
+//                 (thread phase: P^T, dS^T)
+//                 dV  += P^T dO  (A = P^T, bf16 in [64,128))      -> [256,256+D)
+//                 dK  += dS^T Q  (A = dS^T, bf16 in [192,256))    -> [384,384+D)
+//                 dQ   = dS K    (A = dS from shared memory, MN-major; two
+//                                   N = 64 halves into [0,64) and [128,192))
+//   warps 2..5  thread = one TMEM lane: a key row for the P / dS phase, a query
+//               row when dQ is read back.  Per pair they stage lse, Di and the
+//               row limit of the 128 query rows in shared memory, form P and dS
+//               for their key row from S^T and dP^T (the mask is a per-query
+//               prefix of the key tile), store P^T / dS^T into TMEM and dS into
+//               shared memory (the A operand of dQ), then reduce dQ into the fp32
+//               buffer.  At the end they write dK and dV.
+// The phases of one pair run one after the other (one S^T / dP^T buffer).
+// Every mbarrier wait is bounded and records ABKV_DEVERR_TIMEOUT on expiry.
+#include <cstring>
+
+#include "prefill_mask.cuh"
+#include "tcgen05.cuh"
+
+namespace abkv {
+namespace {
+using namespace tc;
+using mask::tile_class;
+using mask::tile_limit_fast;
+
+constexpr int kT = 128;                // key / query tile rows
+constexpr int kThreads = 192;
+constexpr int kMaxHeads = 128;
+constexpr int kMaxPairs = 2048;        // (query tile, head) pairs per key tile
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kIdescT = idesc_bf16_m128(kT, false);  // S^T, dP^T: N = 128 query rows, both K-major
+
+template <int D>
+struct Layout {
+  static constexpr int kAtoms = D / 64;
+  static constexpr int kTileBytes = kT * D * 2;   // K, V, Q, dO tiles
+  static constexpr int kOffK = 0;
+  static constexpr int kOffV = kOffK + kTileBytes;
+  static constexpr int kOffQ = kOffV + kTileBytes;
+  static constexpr int kOffDO = kOffQ + kTileBytes;
+  static constexpr int kOffDS = kOffDO + kTileBytes;  // dS [128 keys][128 q] bf16, MN-major A of dQ
+  static constexpr int kOffRow = kOffDS + kT * kT * 2;  // lse2[128], di[128], lim[128]
+  static constexpr int kOffBar = kOffRow + 3 * kT * 4;
+  static constexpr int kOffList = kOffBar + 256;
+  static constexpr int kSmem = kOffList + 4 * kMaxPairs + 16 + 1024;
+  static constexpr uint32_t kIdescAcc = idesc_bf16_m128(D, true);  // dV, dK: N = D, B MN-major
+};
+// dQ = dS K: M = 128 query rows, N = 64 dims, A (dS) and B (K) MN-major
+constexpr uint32_t kIdescDQ = idesc_bf16_m128(64, true) | (1u << 15);
+
+// barriers: kv_full, qd_full, qd_empty, s_full, p_full, dq_full, tm_free, acc_full, TMEM address
+constexpr int kBarKV = 0, kBarQD = 1, kBarQDE = 2, kBarS = 3, kBarP = 4, kBarDQ = 5, kBarFree = 6, kBarAcc = 7,
+              kBarTmem = 8;
+
+struct alignas(64) BwdParams {
+  CUtensorMap tm_q, tm_k, tm_v, tm_do;
+  const float* lse;   // [B][H][S], natural log (the forward's)
+  const float* di;    // [B][H][S], rowsum(dO * O)
+  float* dq_acc;      // [B][H][S][D] fp32
+  __nv_bfloat16* dk;  // strided [B][Hkv][S][D]
+  __nv_bfloat16* dv;
+  int64_t dk_sb, dk_sh, dk_ss, dv_sb, dv_sh, dv_ss;
+  const int32_t* prompt_len;
+  int32_t* err;
+  int quota[kMaxHeads];
+  int B, H, Hkv, G, S, C, KL, per, n_tiles;
+  float scale, scale_log2;
+};
+
+__device__ __forceinline__ void red_add_v4(float* dst, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};\n" ::"l"(dst), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
+__device__ __forceinline__ void sts128(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};\n" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+__device__ __forceinline__ void softmax_bar() { asm volatile("bar.sync 1, 128;\n" ::: "memory"); }
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1) prefill_bwd_kernel(const __grid_constant__ BwdParams p) {
+  using LY = Layout<D>;
+  constexpr int kAtoms = LY::kAtoms, kTileBytes = LY::kTileBytes;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + LY::kOffBar);
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bar + kBarTmem);
+  float* s_lse2 = reinterpret_cast<float*>(smem + LY::kOffRow);
+  float* s_di = s_lse2 + kT;
+  int32_t* s_lim = reinterpret_cast<int32_t*>(s_di + kT);
+  int32_t* s_list = reinterpret_cast<int32_t*>(smem + LY::kOffList);
+  int32_t* s_n = s_list + kMaxPairs;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kt = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
+  const int G = p.G;
+  const int pl = p.prompt_len ? __ldg(p.prompt_len + b) : 0;
+  const int kb = kt * kT / p.per, kw0 = kt * kT - kb * p.per;
+  const int qt_first = kb * p.per / kT;  // query tiles of earlier blocks never see this key tile
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kBarTmem; ++i) mbar_init(&bar[i], (i == kBarP || i == kBarFree) ? 128 : 1);
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(s_tmem)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n");
+  }
+  if (warp == 2) {  // the (query tile, head) pairs this key tile contributes to, by ballot
+    int n = 0;
+    const int total = (p.n_tiles - qt_first) * G;
+    for (int base = 0; base < total; base += 32) {
+      const int i = base + lane;
+      const int qt = qt_first + i / G, g = i % G;
+      const bool vis = i < total && tile_class(p, hk * G + g, qt, kt, pl) != 0;
+      const uint32_t m = __ballot_sync(0xffffffffu, vis);
+      if (vis && n + __popc(m & ((1u << lane) - 1u)) < kMaxPairs)
+        s_list[n + __popc(m & ((1u << lane) - 1u))] = (qt << 8) | g;
+      n += __popc(m);
+    }
+    if (lane == 0) {
+      if (n > kMaxPairs) set_error(p.err, ABKV_DEVERR_RANGE);
+      *s_n = n < kMaxPairs ? n : kMaxPairs;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *s_tmem;
+  const int n_pairs = *s_n;
+  bool dead = false;
+
+  if (warp == 0) {
+    // ---------------- TMA ----------------
+    if (lane == 0) {
+      mbar_expect_tx(&bar[kBarKV], 2 * kTileBytes);
+      for (int a = 0; a < kAtoms; ++a) {
+        tma_load_4d(smem + LY::kOffK + a * (kTileBytes / kAtoms), &p.tm_k, 64 * a, kt * kT, hk, b, &bar[kBarKV]);
+        tma_load_4d(smem + LY::kOffV + a * (kTileBytes / kAtoms), &p.tm_v, 64 * a, kt * kT, hk, b, &bar[kBarKV]);
+      }
+      for (int i = 0; i < n_pairs; ++i) {
+        const int e = s_list[i];
+        const int qt = e >> 8, h = hk * G + (e & 0xFF);
+        if (!wait_or_abort(&bar[kBarQDE], (uint32_t)((i & 1) ^ 1), dead, p.err)) break;
+        mbar_expect_tx(&bar[kBarQD], 2 * kTileBytes);
+        for (int a = 0; a < kAtoms; ++a) {
+          tma_load_4d(smem + LY::kOffQ + a * (kTileBytes / kAtoms), &p.tm_q, 64 * a, qt * kT, h, b, &bar[kBarQD]);
+          tma_load_4d(smem + LY::kOffDO + a * (kTileBytes / kAtoms), &p.tm_do, 64 * a, qt * kT, h, b, &bar[kBarQD]);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      const uint64_t dk_k = desc_kmajor_sw128(smem_u32(smem + LY::kOffK));   // K as the A of S^T
+      const uint64_t dv_k = desc_kmajor_sw128(smem_u32(smem + LY::kOffV));   // V as the A of dP^T
+      const uint64_t dq_k = desc_kmajor_sw128(smem_u32(smem + LY::kOffQ));   // Q as the B of S^T
+      const uint64_t ddo_k = desc_kmajor_sw128(smem_u32(smem + LY::kOffDO)); // dO as the B of dP^T
+      const uint64_t dq_mn = desc_mnmajor_sw128(smem_u32(smem + LY::kOffQ), kTileBytes / kAtoms);    // B of dK
+      const uint64_t ddo_mn = desc_mnmajor_sw128(smem_u32(smem + LY::kOffDO), kTileBytes / kAtoms);  // B of dV
+      const uint64_t dds_mn = desc_mnmajor_sw128(smem_u32(smem + LY::kOffDS), kT * 128);             // A of dQ
+      const uint64_t dk_mn = desc_mnmajor_sw128(smem_u32(smem + LY::kOffK), kTileBytes / kAtoms);    // B of dQ
+      constexpr int kAtomBytes = kTileBytes / kAtoms;
+      wait_or_abort(&bar[kBarKV], 0, dead, p.err);
+      for (int i = 0; i < n_pairs && !dead; ++i) {
+        const uint32_t par = (uint32_t)(i & 1);
+        if (!wait_or_abort(&bar[kBarQD], par, dead, p.err)) break;
+        // S^T / dP^T overwrite the columns the threads read dQ(i-1) from
+        if (i > 0 && !wait_or_abort(&bar[kBarFree], par ^ 1u, dead, p.err)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * kAtomBytes + (kk & 3) * 32;
+          umma(tmem + 0, desc_advance(dk_k, off), desc_advance(dq_k, off), kIdescT, kk > 0 ? 1u : 0u);
+        }
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * kAtomBytes + (kk & 3) * 32;
+          umma(tmem + 128, desc_advance(dv_k, off), desc_advance(ddo_k, off), kIdescT, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&bar[kBarS]);
+        if (!wait_or_abort(&bar[kBarP], par, dead, p.err)) break;
+        tc_fence_after();
+        // dV += P^T dO, dK += dS^T Q over the 128 query rows in steps of 16
+#pragma unroll
+        for (int kk = 0; kk < kT / 16; ++kk)
+          umma_tmem_a(tmem + 256, tmem + 64 + kk * 8, desc_advance(ddo_mn, kk * 2048), LY::kIdescAcc,
+                      (i > 0 || kk > 0) ? 1u : 0u);
+#pragma unroll
+        for (int kk = 0; kk < kT / 16; ++kk)
+          umma_tmem_a(tmem + 384, tmem + 192 + kk * 8, desc_advance(dq_mn, kk * 2048), LY::kIdescAcc,
+                      (i > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&bar[kBarQDE]);  // Q and dO may be replaced once these ran
+        // dQ = dS K over the 128 keys in steps of 16, per 64-dim half of K
+#pragma unroll
+        for (int hd = 0; hd < D / 64; ++hd)
+#pragma unroll
+          for (int kk = 0; kk < kT / 16; ++kk)
+            umma(tmem + (hd ? 128 : 0), desc_advance(dds_mn, kk * 2048),
+                 desc_advance(dk_mn, hd * kAtomBytes + kk * 2048), kIdescDQ, kk > 0 ? 1u : 0u);
+        umma_commit(&bar[kBarDQ]);
+      }
+      umma_commit(&bar[kBarAcc]);
+    }
+  } else {
+    // ---------------- threads of TMEM lanes: P / dS, dQ, then dK and dV ----------------
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;  // key row (P / dS phase), query row (dQ read-back)
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    const float sl2 = p.scale_log2, scale = p.scale;
+    const uint32_t ds_row = smem_u32(smem + LY::kOffDS) + row * 128;  // row r of each 16 KiB atom column
+    for (int i = 0; i < n_pairs; ++i) {
+      const uint32_t par = (uint32_t)(i & 1);
+      const int e = s_list[i];
+      const int qt = e >> 8, h = hk * G + (e & 0xFF);
+      {  // the 128 query rows of this pair: log2-domain lse, Di and the visible-key prefix
+        const int q = qt * kT + row;
+        const int64_t rr = ((int64_t)b * p.H + h) * p.S + q;
+        const int qb = q / p.per, qw = q - qb * p.per;
+        const float l = __ldg(p.lse + rr);
+        s_lse2[row] = l * 1.4426950408889634f;
+        s_di[row] = __ldg(p.di + rr);
+        s_lim[row] = tile_limit_fast(p, p.quota[h], q, qb, qw, kb, kw0, kt * kT, pl);
+      }
+      softmax_bar();
+      const bool ok = __all_sync(0xffffffffu, wait_or_abort(&bar[kBarS], par, dead, p.err));
+      if (!ok) dead = true;
+      tc_fence_after();
+      // upper query half first: its P^T / dS^T words land in columns whose scores were read
+#pragma unroll 1
+      for (int half = 1; half >= 0; --half) {
+        float s[64], dp[64];
+        tmem_ld32(tmem + lane_base + 64 * half, *reinterpret_cast<float(*)[32]>(s));
+        tmem_ld32(tmem + lane_base + 64 * half + 32, *reinterpret_cast<float(*)[32]>(s + 32));
+        tmem_ld32(tmem + lane_base + 128 + 64 * half, *reinterpret_cast<float(*)[32]>(dp));
+        tmem_ld32(tmem + lane_base + 128 + 64 * half + 32, *reinterpret_cast<float(*)[32]>(dp + 32));
+        tmem_wait_ld();
+        uint32_t wp[32], wd[32];
+#pragma unroll
+        for (int c8 = 0; c8 < 8; ++c8) {
+          const int q0 = 64 * half + 8 * c8;
+          const float4 la = *reinterpret_cast<const float4*>(s_lse2 + q0);
+          const float4 lb = *reinterpret_cast<const float4*>(s_lse2 + q0 + 4);
+          const float4 da = *reinterpret_cast<const float4*>(s_di + q0);
+          const float4 db = *reinterpret_cast<const float4*>(s_di + q0 + 4);
+          const int4 ma = *reinterpret_cast<const int4*>(s_lim + q0);
+          const int4 mb = *reinterpret_cast<const int4*>(s_lim + q0 + 4);
+          const float lse[8] = {la.x, la.y, la.z, la.w, lb.x, lb.y, lb.z, lb.w};
+          const float di[8] = {da.x, da.y, da.z, da.w, db.x, db.y, db.z, db.w};
+          const int lim[8] = {ma.x, ma.y, ma.z, ma.w, mb.x, mb.y, mb.z, mb.w};
+          float pv[8], dsv[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const int c = 8 * c8 + j;
+            const float pe = row < lim[j] ? fast_exp2(s[c] * sl2 - lse[j]) : 0.f;
+            pv[j] = pe;
+            dsv[j] = pe * (dp[c] - di[j]) * scale;
+          }
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            wp[4 * c8 + j] = pack_bf16x2(pv[2 * j], pv[2 * j + 1]);
+            wd[4 * c8 + j] = pack_bf16x2(dsv[2 * j], dsv[2 * j + 1]);
+          }
+          // dS row `row`, query rows q0..q0+7: chunk c8 of atom column `half`, 128B swizzle
+          sts128(ds_row + half * (kT * 128) + ((c8 ^ (row & 7)) << 4), wd[4 * c8], wd[4 * c8 + 1],
+                 wd[4 * c8 + 2], wd[4 * c8 + 3]);
+        }
+        tmem_st32(tmem + lane_base + 64 + 32 * half, reinterpret_cast<const float(&)[32]>(wp));
+        tmem_st32(tmem + lane_base + 192 + 32 * half, reinterpret_cast<const float(&)[32]>(wd));
+      }
+      tmem_wait_st();
+      asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // dS visible to the tensor core
+      tc_fence_before();
+      mbar_arrive_one(&bar[kBarP]);
+      // dQ of this pair: query row `row`, dims [0,64) in columns [0,64), [64,128) in [128,192)
+      const bool okq = __all_sync(0xffffffffu, wait_or_abort(&bar[kBarDQ], par, dead, p.err));
+      if (!okq) dead = true;
+      tc_fence_after();
+      float* dst = p.dq_acc + ((((int64_t)b * p.H + h) * p.S) + qt * kT + row) * D;
+#pragma unroll 1
+      for (int hd = 0; hd < D / 64; ++hd) {
+#pragma unroll
+        for (int c2 = 0; c2 < 2; ++c2) {
+          float t[32];
+          tmem_ld32(tmem + lane_base + (hd ? 128 : 0) + 32 * c2, t);
+          tmem_wait_ld();
+          if (!dead) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              red_add_v4(dst + 64 * hd + 32 * c2 + 4 * j, t[4 * j], t[4 * j + 1], t[4 * j + 2], t[4 * j + 3]);
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive_one(&bar[kBarFree]);
+      softmax_bar();  // the row arrays are rewritten by the next pair
+    }
+    // dK and dV of this key tile: key row `row`
+    const bool oka = __all_sync(0xffffffffu, wait_or_abort(&bar[kBarAcc], 0, dead, p.err));
+    tc_fence_after();
+    if (oka) {
+      const int key = kt * kT + row;
+      __nv_bfloat16* dkr = p.dk + (int64_t)b * p.dk_sb + (int64_t)hk * p.dk_sh + (int64_t)key * p.dk_ss;
+      __nv_bfloat16* dvr = p.dv + (int64_t)b * p.dv_sb + (int64_t)hk * p.dv_sh + (int64_t)key * p.dv_ss;
+#pragma unroll 1
+      for (int which = 0; which < 2; ++which) {
+        __nv_bfloat16* out = which ? dkr : dvr;
+        const uint32_t col = which ? 384u : 256u;
+#pragma unroll 1
+        for (int c4 = 0; c4 < D / 32; ++c4) {
+          float t[32];
+          tmem_ld32(tmem + lane_base + col + c4 * 32, t);
+          tmem_wait_ld();
+          if (n_pairs == 0) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) t[j] = 0.f;
+          }
+#pragma unroll
+          for (int v8 = 0; v8 < 4; ++v8) {
+            uint4 pk;
+            pk.x = pack_bf16x2(t[v8 * 8 + 0], t[v8 * 8 + 1]);
+            pk.y = pack_bf16x2(t[v8 * 8 + 2], t[v8 * 8 + 3]);
+            pk.z = pack_bf16x2(t[v8 * 8 + 4], t[v8 * 8 + 5]);
+            pk.w = pack_bf16x2(t[v8 * 8 + 6], t[v8 * 8 + 7]);
+            *reinterpret_cast<uint4*>(out + c4 * 32 + v8 * 8) = pk;
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(kTmemCols));
+  }
+}
+
+// Di = rowsum(dO * O) in fp32: one warp per row.
+__global__ void rowdot_kernel(const __nv_bfloat16* __restrict__ o, int64_t o_sb, int64_t o_sh, int64_t o_ss,
+                              const __nv_bfloat16* __restrict__ dout, int64_t d_sb, int64_t d_sh, int64_t d_ss,
+                              float* di, int B, int H, int S, int D) {
+  const int64_t r = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (r >= (int64_t)B * H * S) return;
+  const int q = (int)(r % S);
+  const int h = (int)((r / S) % H);
+  const int b = (int)(r / ((int64_t)S * H));
+  const __nv_bfloat16* orow = o + b * o_sb + h * o_sh + q * o_ss;
+  const __nv_bfloat16* drow = dout + b * d_sb + h * d_sh + q * d_ss;
+  float acc = 0.f;
+  for (int d = lane * 2; d < D; d += 64) {
+    const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(orow + d);
+    const __nv_bfloat162 g = *reinterpret_cast<const __nv_bfloat162*>(drow + d);
+    acc += __bfloat162float(a.x) * __bfloat162float(g.x) + __bfloat162float(a.y) * __bfloat162float(g.y);
+  }
+#pragma unroll
+  for (int o2 = 16; o2; o2 >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o2);
+  if (lane == 0) di[r] = acc;
+}
+
+// dq (strided bf16) = dq_acc (contiguous fp32), 8 dims per thread.
+__global__ void dq_store_kernel(const float* __restrict__ acc, __nv_bfloat16* dq, int64_t sb, int64_t sh, int64_t ss,
+                                int B, int H, int S, int D) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t per_row = D / 8;
+  if (i >= (int64_t)B * H * S * per_row) return;
+  const int64_t r = i / per_row;
+  const int d0 = (int)(i % per_row) * 8;
+  const int q = (int)(r % S);
+  const int h = (int)((r / S) % H);
+  const int b = (int)(r / ((int64_t)S * H));
+  const float4 x = *reinterpret_cast<const float4*>(acc + r * D + d0);
+  const float4 y = *reinterpret_cast<const float4*>(acc + r * D + d0 + 4);
+  uint4 pk;
+  pk.x = pack_bf16x2(x.x, x.y);
+  pk.y = pack_bf16x2(x.z, x.w);
+  pk.z = pack_bf16x2(y.x, y.y);
+  pk.w = pack_bf16x2(y.z, y.w);
+  *reinterpret_cast<uint4*>(dq + b * sb + h * sh + q * ss + d0) = pk;
+}
+
+int make_map(CUtensorMap* m, const void* base, int B, int heads, int S, int D, const int64_t* strides) {
+  const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)S, (cuuint64_t)heads, (cuuint64_t)B};
+  const cuuint64_t gstr[3] = {(cuuint64_t)strides[2] * 2, (cuuint64_t)strides[1] * 2, (cuuint64_t)strides[0] * 2};
+  const cuuint32_t box[4] = {64, (cuuint32_t)kT, 1, 1};
+  return tc::encode_tiled_4d(m, base, dims, gstr, box);
+}
+
+constexpr size_t kWsHeader = 256;
+size_t bwd_workspace(int B, int H, int S, int D) {
+  const size_t rows = (size_t)B * H * S;
+  return kWsHeader + (rows * D * 4 + 255) / 256 * 256 + (rows * 4 + 255) / 256 * 256;
+}
+
+}  // namespace
+}  // namespace abkv
+
+using namespace abkv;
+
+extern "C" size_t abkv_prefill_masked_backward_workspace_size(int B, int H, int S, int head_dim) {
+  if (B <= 0 || H <= 0 || S <= 0 || (head_dim != 64 && head_dim != 128)) return 0;
+  return bwd_workspace(B, H, S, head_dim);
+}
+
+extern "C" int abkv_prefill_masked_backward(
+    const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides, const void* v,
+    const int64_t* v_strides, const void* out, const int64_t* out_strides, const void* dout,
+    const int64_t* dout_strides, const float* lse, void* dq, const int64_t* dq_strides, void* dk,
+    const int64_t* dk_strides, void* dv, const int64_t* dv_strides, const int32_t* quota_per_head,
+    const int32_t* prompt_len, int B, int H, int Hkv, int S, int head_dim, int C, int K_layout, float scale,
+    void* workspace, size_t workspace_bytes, void* stream) {
+  const void* ptrs[9] = {q, k, v, out, dout, dq, dk, dv, lse};
+  for (const void* x : ptrs)
+    if (!x) return ABKV_ERR_INVALID_ARG;
+  const int64_t* strs[8] = {q_strides, k_strides, v_strides, out_strides, dout_strides, dq_strides, dk_strides,
+                            dv_strides};
+  for (const int64_t* x : strs)
+    if (!x) return ABKV_ERR_INVALID_ARG;
+  if (B <= 0 || H <= 0 || Hkv <= 0 || S <= 0 || H % Hkv != 0 || !(scale > 0.f)) return ABKV_ERR_INVALID_ARG;
+  if ((head_dim != 64 && head_dim != 128) || H > kMaxHeads || B > 65535 || Hkv > 65535) return ABKV_ERR_UNSUPPORTED;
+  if (H / Hkv > 255) return ABKV_ERR_UNSUPPORTED;
+  if (C <= 0 || K_layout <= 0 || C % kT || K_layout % kT || S % (C + K_layout)) return ABKV_ERR_UNSUPPORTED;
+  if ((int64_t)(S / kT) * (H / Hkv) > kMaxPairs || S / kT > (1 << 23)) return ABKV_ERR_UNSUPPORTED;
+  for (int i = 0; i < 8; ++i)
+    if (reinterpret_cast<uintptr_t>(ptrs[i]) & 15) return ABKV_ERR_INVALID_ARG;
+  for (int i = 3; i < 8; ++i)  // rows of out, dout, dq, dk, dv are written or read as 16-byte vectors
+    if (strs[i][0] % 8 || strs[i][1] % 8 || strs[i][2] % 8) return ABKV_ERR_INVALID_ARG;
+  const size_t need = bwd_workspace(B, H, S, head_dim);
+  if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255))
+    return ABKV_ERR_WORKSPACE;
+  char* ws = static_cast<char*>(workspace);
+  const size_t rows = (size_t)B * H * S;
+  float* dq_acc = reinterpret_cast<float*>(ws + kWsHeader);
+  float* di = reinterpret_cast<float*>(ws + kWsHeader + (rows * head_dim * 4 + 255) / 256 * 256);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+
+  BwdParams prm;
+  std::memset(&prm, 0, sizeof(prm));
+  int st = make_map(&prm.tm_q, q, B, H, S, head_dim, q_strides);
+  if (st == ABKV_OK) st = make_map(&prm.tm_do, dout, B, H, S, head_dim, dout_strides);
+  if (st == ABKV_OK) st = make_map(&prm.tm_k, k, B, Hkv, S, head_dim, k_strides);
+  if (st == ABKV_OK) st = make_map(&prm.tm_v, v, B, Hkv, S, head_dim, v_strides);
+  if (st != ABKV_OK) return st;
+  for (int h = 0; h < H; ++h) {
+    const int qq = quota_per_head ? quota_per_head[h] : K_layout;
+    if (qq < 0) return ABKV_ERR_INVALID_ARG;
+    prm.quota[h] = qq;
+  }
+  prm.lse = lse;
+  prm.di = di;
+  prm.dq_acc = dq_acc;
+  prm.dk = static_cast<__nv_bfloat16*>(dk);
+  prm.dv = static_cast<__nv_bfloat16*>(dv);
+  prm.dk_sb = dk_strides[0];
+  prm.dk_sh = dk_strides[1];
+  prm.dk_ss = dk_strides[2];
+  prm.dv_sb = dv_strides[0];
+  prm.dv_sh = dv_strides[1];
+  prm.dv_ss = dv_strides[2];
+  prm.prompt_len = prompt_len;
+  prm.err = reinterpret_cast<int32_t*>(ws);
+  prm.B = B;
+  prm.H = H;
+  prm.Hkv = Hkv;
+  prm.G = H / Hkv;
+  prm.S = S;
+  prm.C = C;
+  prm.KL = K_layout;
+  prm.per = C + K_layout;
+  prm.n_tiles = S / kT;
+  prm.scale = scale;
+  prm.scale_log2 = scale * 1.4426950408889634f;
+
+  if (cudaMemsetAsync(dq_acc, 0, rows * head_dim * 4, s) != cudaSuccess) return ABKV_ERR_CUDA;
+  {
+    const int64_t warps_per_block = 8;
+    const int64_t blocks = ((int64_t)rows + warps_per_block - 1) / warps_per_block;
+    rowdot_kernel<<<(unsigned)blocks, 256, 0, s>>>(
+        static_cast<const __nv_bfloat16*>(out), out_strides[0], out_strides[1], out_strides[2],
+        static_cast<const __nv_bfloat16*>(dout), dout_strides[0], dout_strides[1], dout_strides[2], di, B, H, S,
+        head_dim);
+  }
+  auto kernel = head_dim == 64 ? prefill_bwd_kernel<64> : prefill_bwd_kernel<128>;
+  const int smem = head_dim == 64 ? Layout<64>::kSmem : Layout<128>::kSmem;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    return ABKV_ERR_CUDA;
+  kernel<<<dim3(prm.n_tiles, Hkv, B), kThreads, smem, s>>>(prm);
+  {
+    const int64_t n = (int64_t)rows * (head_dim / 8);
+    dq_store_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(dq_acc, static_cast<__nv_bfloat16*>(dq),
+                                                                  dq_strides[0], dq_strides[1], dq_strides[2], B, H,
+                                                                  S, head_dim);
+  }
+  if (cudaGetLastError() != cudaSuccess) return ABKV_ERR_CUDA;
+  return ABKV_OK;
+}

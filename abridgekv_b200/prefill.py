@@ -87,6 +87,75 @@ def prefill_masked(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, C: int,
     return (out, lse) if return_lse else out
 
 
+def prefill_masked_backward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor,
+                            dout: torch.Tensor, lse: torch.Tensor, *, C: int, K_layout: int,
+                            quota_per_head: Sequence[int] | None = None, prompt_len: torch.Tensor | None = None,
+                            scale: float | None = None, workspace: Workspace | None = None,
+                            stream: torch.cuda.Stream | None = None):
+    """Gradients (dq, dk, dv) of ``prefill_masked`` for the upstream gradient ``dout``, from the
+    forward's output and log-sum-exp (abkv_prefill_masked_backward)."""
+    for name, t in (("query", q), ("key", k), ("value", v), ("out", out), ("dout", dout)):
+        _check(name, t)
+    B, H, S, D = q.shape
+    Hkv = k.shape[1]
+    if tuple(out.shape) != (B, H, S, D) or tuple(dout.shape) != (B, H, S, D):
+        raise ValueError("out and dout must be [B, H, S, D] like the query")
+    if lse.dtype != torch.float32 or tuple(lse.shape) != (B, H, S) or not lse.is_contiguous():
+        raise ValueError("lse must be the forward's contiguous float32 [B, H, S] log-sum-exp")
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    pl = None
+    if prompt_len is not None:
+        pl = prompt_len.to(device=q.device, dtype=torch.int32).contiguous()
+    if quota_per_head is not None and len(quota_per_head) != H:
+        raise ValueError("quota_per_head must hold one quota per query head")
+    scale = 1.0 / math.sqrt(D) if scale is None else float(scale)
+    lib = _lib.lib()
+    need = lib.abkv_prefill_masked_backward_workspace_size(B, H, S, D)
+    if need == 0:
+        raise _lib.AbkvError("abkv_prefill_masked_backward_workspace_size", 3, f"unsupported shape D={D}")
+    ws = (workspace or default_workspace(q.device)).ensure(need)
+    s = torch.cuda.current_stream(q.device) if stream is None else stream
+    strides = lambda t: _lib.i64_array([t.stride(0), t.stride(1), t.stride(2)])  # noqa: E731
+    quota = _lib.i32_array(quota_per_head) if quota_per_head is not None else None
+    with torch.cuda.device(q.device):
+        st = lib.abkv_prefill_masked_backward(
+            q.data_ptr(), strides(q), k.data_ptr(), strides(k), v.data_ptr(), strides(v), out.data_ptr(),
+            strides(out), dout.data_ptr(), strides(dout), lse.data_ptr(), dq.data_ptr(), strides(dq), dk.data_ptr(),
+            strides(dk), dv.data_ptr(), strides(dv), quota, pl.data_ptr() if pl is not None else None, B, H, Hkv,
+            S, D, C, K_layout, scale, ws.ptr(), ws.nbytes, s.cuda_stream)
+    _lib.check("abkv_prefill_masked_backward", st)
+    return dq, dk, dv
+
+
+class PrefillMaskedAttention(torch.autograd.Function):
+    """prefill_masked with its backward: the forward keeps its output and log-sum-exp."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, C, K_layout, quota_per_head, prompt_len, scale):
+        out, lse = prefill_masked(q, k, v, C=C, K_layout=K_layout, quota_per_head=quota_per_head,
+                                  prompt_len=prompt_len, scale=scale, return_lse=True)
+        ctx.save_for_backward(q, k, v, out, lse)
+        ctx.args = (C, K_layout, quota_per_head, prompt_len, scale)
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        q, k, v, out, lse = ctx.saved_tensors
+        C, K_layout, quota, pl, scale = ctx.args
+        if dout.stride(-1) != 1:
+            dout = dout.contiguous()
+        dq, dk, dv = prefill_masked_backward(q, k, v, out, dout, lse, C=C, K_layout=K_layout, quota_per_head=quota,
+                                             prompt_len=pl, scale=scale)
+        return dq, dk, dv, None, None, None, None, None
+
+
+def prefill_masked_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, C: int, K_layout: int,
+                             quota_per_head: Sequence[int] | None = None, prompt_len: torch.Tensor | None = None,
+                             scale: float | None = None) -> torch.Tensor:
+    """Differentiable ``prefill_masked`` (forward and backward on the tcgen05 kernels)."""
+    return PrefillMaskedAttention.apply(q, k, v, C, K_layout, quota_per_head, prompt_len, scale)
+
+
 def abkv_attention_forward(module, query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
                            attention_mask, scaling: float | None = None, dropout: float = 0.0,
                            softcap: float | None = None, s_aux=None, **kwargs):
@@ -95,9 +164,12 @@ def abkv_attention_forward(module, query: torch.Tensor, key: torch.Tensor, value
         raise TypeError("abkv_sm100 attention needs a CompressMask descriptor as attention_mask")
     if dropout != 0.0 or softcap is not None or s_aux is not None:
         raise ValueError("abkv_sm100 attention supports no dropout, softcap or attention sinks")
-    out = prefill_masked(query, key, value, C=attention_mask.C, K_layout=attention_mask.K_layout,
-                         quota_per_head=attention_mask.quota_per_head, prompt_len=attention_mask.prompt_len,
-                         scale=scaling)
+    kw = dict(C=attention_mask.C, K_layout=attention_mask.K_layout,
+              quota_per_head=attention_mask.quota_per_head, prompt_len=attention_mask.prompt_len, scale=scaling)
+    if torch.is_grad_enabled() and any(t.requires_grad for t in (query, key, value)):
+        out = prefill_masked_attention(query, key, value, **kw)  # training: gradients through the backward kernel
+    else:
+        out = prefill_masked(query, key, value, **kw)
     return out.transpose(1, 2), None
 
 

@@ -377,6 +377,30 @@ int abkv_prefill_masked(const void* q, const int64_t* q_strides, const void* k,
                         int K_layout, float scale, void* workspace,
                         size_t workspace_bytes, void* stream);
 
+/* Backward of abkv_prefill_masked: dq, dk, dv for the upstream gradient dout,
+ * the gradients torch FlexAttention's backward gives the training path
+ * (abridgekv/compress_forward.py:248,1229 with the same mask; sft_ddp.py:1225).
+ * q, k, v, quota_per_head, prompt_len, C, K_layout, scale as in the forward;
+ * out: the forward's output [B][H][S][head_dim]; dout likewise; lse: the
+ * forward's CONTIGUOUS [B][H][S] f32 log-sum-exp (natural log); dq [B][H][S][D],
+ * dk / dv [B][Hkv][S][D] bf16 outputs (strides multiples of 8 elements).
+ * The workspace holds an fp32 dq accumulator and rowsum(dout * out):
+ * abkv_prefill_masked_backward_workspace_size(B, H, S, head_dim) bytes,
+ * 256-byte aligned.  Same shape limits as the forward, and (S / 128) x (H / Hkv)
+ * <= 2048. */
+size_t abkv_prefill_masked_backward_workspace_size(int B, int H, int S,
+                                                   int head_dim);
+int abkv_prefill_masked_backward(
+    const void* q, const int64_t* q_strides, const void* k,
+    const int64_t* k_strides, const void* v, const int64_t* v_strides,
+    const void* out, const int64_t* out_strides, const void* dout,
+    const int64_t* dout_strides, const float* lse, void* dq,
+    const int64_t* dq_strides, void* dk, const int64_t* dk_strides, void* dv,
+    const int64_t* dv_strides, const int32_t* quota_per_head,
+    const int32_t* prompt_len, int B, int H, int Hkv, int S, int head_dim, int C,
+    int K_layout, float scale, void* workspace, size_t workspace_bytes,
+    void* stream);
+
 /* ========================================================================
  * 5. Code step: K_code code queries per request over the paged cache (tcgen05).
  *

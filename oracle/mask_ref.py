@@ -70,3 +70,34 @@ def masked_attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, mask: np.ndarr
             out[b, h] = (e / np.where(l > 0, l, 1.0)) @ v[b, h // G].astype(np.float64)
             lse[b, h] = np.where(l[:, 0] > 0, m[:, 0] + np.log(np.where(l[:, 0] > 0, l[:, 0], 1.0)), -np.inf)
     return out, lse
+
+
+def masked_attention_grad(q: np.ndarray, k: np.ndarray, v: np.ndarray, mask: np.ndarray, scale: float,
+                          dout: np.ndarray):
+    """Gradients of masked_attention for the upstream gradient dout [B,H,S,D], float64:
+    P = softmax(scale q k^T + mask), O = P v;  dV = sum over the KV head's query heads of P^T dO;
+    dP = dO v^T;  dS = P * (dP - rowsum(dO * O));  dQ = scale dS k;  dK = scale sum dS^T q.
+    -> (dq [B,H,S,D], dk [B,Hkv,S,D], dv [B,Hkv,S,D])."""
+    B, H, S, D = q.shape
+    Hkv = k.shape[1]
+    G = H // Hkv
+    dq = np.zeros((B, H, S, D))
+    dk = np.zeros((B, Hkv, S, D))
+    dv = np.zeros((B, Hkv, S, D))
+    for b in range(B):
+        for h in range(H):
+            kh, vh = k[b, h // G].astype(np.float64), v[b, h // G].astype(np.float64)
+            qh, do = q[b, h].astype(np.float64), dout[b, h].astype(np.float64)
+            s = np.where(mask[b, h], (qh @ kh.T) * scale, -np.inf)
+            m = s.max(axis=1, keepdims=True)
+            m = np.where(np.isfinite(m), m, 0.0)
+            e = np.exp(s - m)
+            l = e.sum(axis=1, keepdims=True)
+            p = e / np.where(l > 0, l, 1.0)
+            o = p @ vh
+            dv[b, h // G] += p.T @ do
+            dp = do @ vh.T
+            ds = p * (dp - (do * o).sum(axis=1, keepdims=True))
+            dq[b, h] = scale * (ds @ kh)
+            dk[b, h // G] += scale * (ds.T @ qh)
+    return dq, dk, dv

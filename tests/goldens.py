@@ -75,3 +75,18 @@ def load_packed(name: str):
                       num_kv_heads=int(z["num_kv_heads"]), head_dim=int(z["head_dim"]), page=int(z["page"]))
     side = packed_side_pages(int(z["seed"]), z["counts"], int(z["quotas"].sum()), int(z["head_dim"]))
     return case, side, z["counts"], z["quotas"], int(z["k_max"]), from_bits(z["out_bits"])
+
+
+def prefill_bwd_cases():
+    return sorted(p.stem[len("prefillbwd_"):] for p in GOLDEN.glob("prefillbwd_*.npz"))
+
+
+def load_prefill_bwd(name: str):
+    """-> (load_prefill(name) dict, dout [B,H,S,D], rows, dq_rows, dk_rows, dv_rows) of the reference goldens."""
+    from tests.golden.make_golden import prefill_dout
+
+    g = load_prefill(name)
+    z = np.load(GOLDEN / f"prefillbwd_{name}.npz")
+    z0 = np.load(GOLDEN / f"prefill_{name}.npz")
+    dout = prefill_dout(int(z0["seed"]), g["B"], g["H"], g["S0"], g["D"])
+    return g, dout, z["rows"], z["dq_rows"], z["dk_rows"], z["dv_rows"]

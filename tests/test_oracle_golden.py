@@ -76,3 +76,16 @@ def test_packed_oracle_matches_reference(name):
     assert np.isfinite(ref).all()
     assert np.abs(ex - ref).max() < 3e-2
     assert np.abs(ex - ref).mean() < 2e-3
+
+
+@pytest.mark.parametrize("name", ["c128k128_quota_prompt", "c256k128_g4"])
+def test_prefill_backward_oracle_matches_reference(name):
+    """The float64 gradient oracle (hand-derived dQ / dK / dV of masked softmax attention with GQA)
+    against torch autograd through the reference's mask (tests/golden/prefillbwd_*)."""
+    from oracle.mask_ref import masked_attention_grad
+    from tests.goldens import load_prefill_bwd
+
+    g, dout, rows, dq_r, dk_r, dv_r = load_prefill_bwd(name)
+    dq, dk, dv = masked_attention_grad(g["q"], g["k"], g["v"], g["mask"], 1.0 / np.sqrt(g["D"]), dout)
+    for got, ref in ((dq[:, :, rows], dq_r), (dk[:, :, rows], dk_r), (dv[:, :, rows], dv_r)):
+        assert np.abs(got - ref).max() <= 1e-5 * max(1.0, np.abs(ref).max())
