@@ -107,6 +107,112 @@ def bench_prefill(args) -> dict:
     return line
 
 
+def bench_prefill_bwd(args) -> dict:
+    """Backward of the config-4 prefill (36 layers at their quotas): abkv_prefill_masked_backward
+    timed alone (the forward's output and log-sum-exp computed beforehand), and forward + backward.
+    Algorithmic work: 10 x D FLOP per visible (query, key) pair per head (S recomputed, dP, dV, dK, dQ)."""
+    from . import prefill
+
+    B, H, Hkv, D, C, K, N = 16, 32, 8, 128, 512, 256, 16
+    S0 = N * (C + K)
+    dev = torch.device("cuda")
+    gen = torch.Generator(device=dev).manual_seed(0)
+    q = torch.randn((B, S0, H, D), device=dev, generator=gen, dtype=torch.bfloat16).transpose(1, 2)
+    k = torch.randn((B, S0, Hkv, D), device=dev, generator=gen, dtype=torch.bfloat16).transpose(1, 2)
+    v = torch.randn((B, S0, Hkv, D), device=dev, generator=gen, dtype=torch.bfloat16).transpose(1, 2)
+    dout = torch.randn((B, S0, H, D), device=dev, generator=gen, dtype=torch.bfloat16).transpose(1, 2)
+    quotas = SCHEDULE_PERLAYER_MEAN128[: args.layers]
+    fwd = {}
+    for qq in sorted(set(quotas)):
+        fwd[qq] = prefill.prefill_masked(q, k, v, C=C, K_layout=K, quota_per_head=[qq] * H, return_lse=True)
+    pairs = sum(visible_pairs(N, C, K, qq) for qq in quotas) * B * H
+    flops_bwd, flops_fwd = 10.0 * D * pairs, 4.0 * D * pairs
+
+    def bwd_step():
+        for qq in quotas:
+            out, lse = fwd[qq]
+            prefill.prefill_masked_backward(q, k, v, out, dout, lse, C=C, K_layout=K, quota_per_head=[qq] * H)
+
+    def train_step():
+        for qq in quotas:
+            out, lse = prefill.prefill_masked(q, k, v, C=C, K_layout=K, quota_per_head=[qq] * H, return_lse=True)
+            prefill.prefill_masked_backward(q, k, v, out, dout, lse, C=C, K_layout=K, quota_per_head=[qq] * H)
+
+    def timed(fn, steps):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / steps
+
+    ms = timed(bwd_step, args.steps)
+    ms_train = timed(train_step, max(1, args.steps // 2))
+    pk = _peaks()
+    tflops = flops_bwd / (ms / 1e3) / 1e12
+    line = {
+        "metric": "pause-token prefill attention backward TFLOP/s (config 4)", "value": tflops, "unit": "TFLOP/s",
+        "ms_per_step": ms, "layers": len(quotas), "algorithmic_tflop_per_step": flops_bwd / 1e12,
+        "forward_plus_backward_ms": ms_train,
+        "forward_plus_backward_tflops": (flops_fwd + flops_bwd) / (ms_train / 1e3) / 1e12,
+        "roofline": {"bound": "tensor", "achieved": tflops, "peak": pk.get("bf16_tflops_sustained"),
+                     "peak_kind": "measured sustained cuBLAS bf16 (MEASURED_PEAKS.json)",
+                     "frac": tflops / pk.get("bf16_tflops_sustained", 1400.0)},
+        "config": {"B": B, "S0": S0, "heads": f"{H}/{Hkv}", "C": C, "K_layout": K, "quotas": "per layer",
+                   "prompt_len": 0},
+    }
+    if args.flex:
+        line["flex"] = bench_flex_train(q, k, v, dout, quotas, C, K, args, flops_fwd + flops_bwd)
+        line["train_speedup_vs_flex"] = line["flex"]["forward_plus_backward_ms"] / ms_train
+    return line
+
+
+def bench_flex_train(q, k, v, dout, quotas, C, K, args, flops) -> dict:
+    """Compiled FlexAttention forward + backward (the reference's training path) on the same inputs."""
+    from torch.nn.attention.flex_attention import create_block_mask, flex_attention
+
+    B, H, S0, D = q.shape
+    per = C + K
+    masks = {}
+    for qq in sorted(set(quotas)):
+        def mm(b, h, qi, kv, qq=qq):
+            qb, qw = qi // per, qi % per
+            kb, kw = kv // per, kv % per
+            kc = kw < C
+            same = kb == qb
+            vis = (kc & same) | (~kc & (kb < qb))
+            vis = (kv <= qi) & vis
+            vis = vis | ((qw >= C) & ~kc & same)
+            return vis & (kc | ((kw - C) < qq))
+        masks[qq] = create_block_mask(mm, B=None, H=None, Q_LEN=S0, KV_LEN=S0, device="cuda", _compile=True)
+    fa = torch.compile(flex_attention, dynamic=False)
+    scale = 1.0 / math.sqrt(D)
+    qg, kg, vg = (t.detach().requires_grad_(True) for t in (q, k, v))
+
+    def step():
+        for qq in quotas:
+            out = fa(qg, kg, vg, block_mask=masks[qq], scale=scale, enable_gqa=True)
+            out.backward(dout)
+            qg.grad = kg.grad = vg.grad = None
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    steps = max(1, args.steps // 2)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    return {"forward_plus_backward_ms": ms, "tflops": flops / (ms / 1e3) / 1e12}
+
+
 def bench_flex(q, k, v, quotas, C, K, N, args, flops) -> dict:
     from torch.nn.attention.flex_attention import create_block_mask, flex_attention
 
@@ -340,15 +446,15 @@ def bench_packed(args) -> dict:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("which", choices=["prefill", "compaction", "codestep", "packed"])
+    ap.add_argument("which", choices=["prefill", "prefill_bwd", "compaction", "codestep", "packed"])
     ap.add_argument("--layers", type=int, default=36)
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=2)
     ap.add_argument("--flex", action="store_true")
     ap.add_argument("--blocks", type=int, default=6)
     args = ap.parse_args()
-    fn = {"prefill": bench_prefill, "compaction": bench_compaction, "codestep": bench_codestep,
-          "packed": bench_packed}[args.which]
+    fn = {"prefill": bench_prefill, "prefill_bwd": bench_prefill_bwd, "compaction": bench_compaction,
+          "codestep": bench_codestep, "packed": bench_packed}[args.which]
     print(json.dumps(fn(args)), flush=True)
 
 

@@ -12,23 +12,25 @@
 // CTA = one 128-key tile of one KV head; it walks every (query tile, query head
 // of the group) pair whose 128 x 128 tile the mask does not empty, keeping dK and
 // dV in TMEM, and adds each pair's dQ tile into an fp32 buffer with vector
-// reductions.  6 warps:
+// reductions.  10 warps:
 //   warp 0      TMA: the CTA's K and V tiles once, then Q and dO of each pair
 //               (cp.async.bulk.tensor, 128B swizzle, no multicast)
 //   warp 1      TMEM owner (512 columns) and MMA issuer, per pair:
 //                 S^T  = K Q^T  -> [0,128)     dP^T = V dO^T -> [128,256)
 //                 (thread phase: P^T, dS^T)
-//                 dV  += P^T dO  (A = P^T, bf16 in [64,128))      -> [256,256+D)
-//                 dK  += dS^T Q  (A = dS^T, bf16 in [192,256))    -> [384,384+D)
+//                 dV  += P^T dO  (A = P^T, bf16 in [32,96))       -> [256,256+D)
+//                 dK  += dS^T Q  (A = dS^T, bf16 in [160,224))    -> [384,384+D)
 //                 dQ   = dS K    (A = dS from shared memory, MN-major; two
 //                                   N = 64 halves into [0,64) and [128,192))
-//   warps 2..5  thread = one TMEM lane: a key row for the P / dS phase, a query
-//               row when dQ is read back.  Per pair they stage lse, Di and the
-//               row limit of the 128 query rows in shared memory, form P and dS
-//               for their key row from S^T and dP^T (the mask is a per-query
-//               prefix of the key tile), store P^T / dS^T into TMEM and dS into
-//               shared memory (the A operand of dQ), then reduce dQ into the fp32
-//               buffer.  At the end they write dK and dV.
+//   warps 2..9  thread = one TMEM lane: a key row for the P / dS phase, a query
+//               row when dQ is read back; the two warps of a lane quarter take
+//               one half of the 128 query columns (and of dQ's dims) each.  Per
+//               pair they stage lse, Di and the row limit of the 128 query rows
+//               in shared memory, form P and dS for their key row from S^T and
+//               dP^T (the mask is a per-query prefix of the key tile), store
+//               P^T / dS^T into TMEM and dS into shared memory (the A operand of
+//               dQ), then reduce dQ into the fp32 buffer.  At the end they write
+//               dV (first half) and dK (second half).
 // The phases of one pair run one after the other (one S^T / dP^T buffer).
 // Every mbarrier wait is bounded and records ABKV_DEVERR_TIMEOUT on expiry.
 #include <cstring>
@@ -43,7 +45,7 @@ using mask::tile_class;
 using mask::tile_limit_fast;
 
 constexpr int kT = 128;                // key / query tile rows
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;
 constexpr int kMaxHeads = 128;
 constexpr int kMaxPairs = 2048;        // (query tile, head) pairs per key tile
 constexpr uint32_t kTmemCols = 512;
@@ -93,7 +95,15 @@ __device__ __forceinline__ void red_add_v4(float* dst, float a, float b, float c
 __device__ __forceinline__ void sts128(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};\n" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }
-__device__ __forceinline__ void softmax_bar() { asm volatile("bar.sync 1, 128;\n" ::: "memory"); }
+__device__ __forceinline__ void softmax_bar() { asm volatile("bar.sync 1, 256;\n" ::: "memory"); }
+// 16 columns of 32-bit words from this warp's TMEM lanes
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};\n"
+      ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
 
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1) prefill_bwd_kernel(const __grid_constant__ BwdParams p) {
@@ -117,7 +127,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_bwd_kernel(const __grid_c
   const int qt_first = kb * p.per / kT;  // query tiles of earlier blocks never see this key tile
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kBarTmem; ++i) mbar_init(&bar[i], (i == kBarP || i == kBarFree) ? 128 : 1);
+    for (int i = 0; i < kBarTmem; ++i) mbar_init(&bar[i], (i == kBarP || i == kBarFree) ? 256 : 1);
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(s_tmem)),
@@ -202,14 +212,15 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_bwd_kernel(const __grid_c
         // dV += P^T dO, dK += dS^T Q over the 128 query rows in steps of 16
 #pragma unroll
         for (int kk = 0; kk < kT / 16; ++kk)
-          umma_tmem_a(tmem + 256, tmem + 64 + kk * 8, desc_advance(ddo_mn, kk * 2048), LY::kIdescAcc,
+          umma_tmem_a(tmem + 256, tmem + 32 + kk * 8, desc_advance(ddo_mn, kk * 2048), LY::kIdescAcc,
                       (i > 0 || kk > 0) ? 1u : 0u);
 #pragma unroll
         for (int kk = 0; kk < kT / 16; ++kk)
-          umma_tmem_a(tmem + 384, tmem + 192 + kk * 8, desc_advance(dq_mn, kk * 2048), LY::kIdescAcc,
+          umma_tmem_a(tmem + 384, tmem + 160 + kk * 8, desc_advance(dq_mn, kk * 2048), LY::kIdescAcc,
                       (i > 0 || kk > 0) ? 1u : 0u);
         umma_commit(&bar[kBarQDE]);  // Q and dO may be replaced once these ran
-        // dQ = dS K over the 128 keys in steps of 16, per 64-dim half of K
+        // dQ = dS K over the 128 keys in steps of 16, per 64-dim half of K (its accumulators overlap
+        // P^T / dS^T, which the dV / dK MMAs above read first: one thread's MMAs run in issue order)
 #pragma unroll
         for (int hd = 0; hd < D / 64; ++hd)
 #pragma unroll
@@ -222,21 +233,22 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_bwd_kernel(const __grid_c
     }
   } else {
     // ---------------- threads of TMEM lanes: P / dS, dQ, then dK and dV ----------------
-    const int quarter = warp & 3;
+    // Warps 2..9: the two warps of a lane quarter share its 32 rows; warp half hf takes query
+    // columns [64 hf, 64 hf + 64) in the P / dS phase and dims [64 hf, 64 hf + 64) of dQ.
+    const int quarter = warp & 3, hf = (warp - 2) >> 2;
     const int row = quarter * 32 + lane;  // key row (P / dS phase), query row (dQ read-back)
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
     const float sl2 = p.scale_log2, scale = p.scale;
-    const uint32_t ds_row = smem_u32(smem + LY::kOffDS) + row * 128;  // row r of each 16 KiB atom column
+    const uint32_t ds_row = smem_u32(smem + LY::kOffDS) + hf * (kT * 128) + row * 128;  // atom column hf
     for (int i = 0; i < n_pairs; ++i) {
       const uint32_t par = (uint32_t)(i & 1);
       const int e = s_list[i];
       const int qt = e >> 8, h = hk * G + (e & 0xFF);
-      {  // the 128 query rows of this pair: log2-domain lse, Di and the visible-key prefix
+      if (hf == 0) {  // the 128 query rows of this pair: log2-domain lse, Di and the visible-key prefix
         const int q = qt * kT + row;
         const int64_t rr = ((int64_t)b * p.H + h) * p.S + q;
         const int qb = q / p.per, qw = q - qb * p.per;
-        const float l = __ldg(p.lse + rr);
-        s_lse2[row] = l * 1.4426950408889634f;
+        s_lse2[row] = __ldg(p.lse + rr) * 1.4426950408889634f;
         s_di[row] = __ldg(p.di + rr);
         s_lim[row] = tile_limit_fast(p, p.quota[h], q, qb, qw, kb, kw0, kt * kT, pl);
       }
@@ -244,19 +256,21 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_bwd_kernel(const __grid_c
       const bool ok = __all_sync(0xffffffffu, wait_or_abort(&bar[kBarS], par, dead, p.err));
       if (!ok) dead = true;
       tc_fence_after();
-      // upper query half first: its P^T / dS^T words land in columns whose scores were read
+      // P^T (bf16 pairs) goes to columns 32 + q/2 and dS^T to 160 + q/2: for this warp's query
+      // range those are score columns of its own range, so each 32-column chunk is read before the
+      // chunk whose words land on it is stored (half 0: chunk 1 first; half 1: chunk 0 first).
 #pragma unroll 1
-      for (int half = 1; half >= 0; --half) {
-        float s[64], dp[64];
-        tmem_ld32(tmem + lane_base + 64 * half, *reinterpret_cast<float(*)[32]>(s));
-        tmem_ld32(tmem + lane_base + 64 * half + 32, *reinterpret_cast<float(*)[32]>(s + 32));
-        tmem_ld32(tmem + lane_base + 128 + 64 * half, *reinterpret_cast<float(*)[32]>(dp));
-        tmem_ld32(tmem + lane_base + 128 + 64 * half + 32, *reinterpret_cast<float(*)[32]>(dp + 32));
+      for (int c = 0; c < 2; ++c) {
+        const int chunk = hf ? c : 1 - c;
+        const int qc = 64 * hf + 32 * chunk;  // first query column of the chunk
+        float sv[32], dpv[32];
+        tmem_ld32(tmem + lane_base + qc, sv);
+        tmem_ld32(tmem + lane_base + 128 + qc, dpv);
         tmem_wait_ld();
-        uint32_t wp[32], wd[32];
+        uint32_t wp[16], wd[16];
 #pragma unroll
-        for (int c8 = 0; c8 < 8; ++c8) {
-          const int q0 = 64 * half + 8 * c8;
+        for (int c8 = 0; c8 < 4; ++c8) {
+          const int q0 = qc + 8 * c8;
           const float4 la = *reinterpret_cast<const float4*>(s_lse2 + q0);
           const float4 lb = *reinterpret_cast<const float4*>(s_lse2 + q0 + 4);
           const float4 da = *reinterpret_cast<const float4*>(s_di + q0);
@@ -269,43 +283,42 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_bwd_kernel(const __grid_c
           float pv[8], dsv[8];
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
-            const int c = 8 * c8 + j;
-            const float pe = row < lim[j] ? fast_exp2(s[c] * sl2 - lse[j]) : 0.f;
+            const int cc = 8 * c8 + j;
+            const float pe = row < lim[j] ? fast_exp2(sv[cc] * sl2 - lse[j]) : 0.f;
             pv[j] = pe;
-            dsv[j] = pe * (dp[c] - di[j]) * scale;
+            dsv[j] = pe * (dpv[cc] - di[j]) * scale;
           }
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             wp[4 * c8 + j] = pack_bf16x2(pv[2 * j], pv[2 * j + 1]);
             wd[4 * c8 + j] = pack_bf16x2(dsv[2 * j], dsv[2 * j + 1]);
           }
-          // dS row `row`, query rows q0..q0+7: chunk c8 of atom column `half`, 128B swizzle
-          sts128(ds_row + half * (kT * 128) + ((c8 ^ (row & 7)) << 4), wd[4 * c8], wd[4 * c8 + 1],
-                 wd[4 * c8 + 2], wd[4 * c8 + 3]);
+          // dS row `row`, query rows q0..q0+7: chunk (q0 % 64) / 8 of atom column hf, 128B swizzle
+          const int c16 = (q0 & 63) >> 3;
+          sts128(ds_row + ((c16 ^ (row & 7)) << 4), wd[4 * c8], wd[4 * c8 + 1], wd[4 * c8 + 2], wd[4 * c8 + 3]);
         }
-        tmem_st32(tmem + lane_base + 64 + 32 * half, reinterpret_cast<const float(&)[32]>(wp));
-        tmem_st32(tmem + lane_base + 192 + 32 * half, reinterpret_cast<const float(&)[32]>(wd));
+        tmem_st16(tmem + lane_base + 32 + qc / 2, wp);
+        tmem_st16(tmem + lane_base + 160 + qc / 2, wd);
       }
       tmem_wait_st();
       asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // dS visible to the tensor core
       tc_fence_before();
       mbar_arrive_one(&bar[kBarP]);
-      // dQ of this pair: query row `row`, dims [0,64) in columns [0,64), [64,128) in [128,192)
+      // dQ of this pair: query row `row`, dims [64 hf, 64 hf + 64) in columns [128 hf, 128 hf + 64)
       const bool okq = __all_sync(0xffffffffu, wait_or_abort(&bar[kBarDQ], par, dead, p.err));
       if (!okq) dead = true;
       tc_fence_after();
-      float* dst = p.dq_acc + ((((int64_t)b * p.H + h) * p.S) + qt * kT + row) * D;
-#pragma unroll 1
-      for (int hd = 0; hd < D / 64; ++hd) {
+      if (hf < D / 64) {
+        float* dst = p.dq_acc + ((((int64_t)b * p.H + h) * p.S) + qt * kT + row) * D + 64 * hf;
 #pragma unroll
         for (int c2 = 0; c2 < 2; ++c2) {
           float t[32];
-          tmem_ld32(tmem + lane_base + (hd ? 128 : 0) + 32 * c2, t);
+          tmem_ld32(tmem + lane_base + 128 * hf + 32 * c2, t);
           tmem_wait_ld();
           if (!dead) {
 #pragma unroll
             for (int j = 0; j < 8; ++j)
-              red_add_v4(dst + 64 * hd + 32 * c2 + 4 * j, t[4 * j], t[4 * j + 1], t[4 * j + 2], t[4 * j + 3]);
+              red_add_v4(dst + 32 * c2 + 4 * j, t[4 * j], t[4 * j + 1], t[4 * j + 2], t[4 * j + 3]);
           }
         }
       }
@@ -313,35 +326,31 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_bwd_kernel(const __grid_c
       mbar_arrive_one(&bar[kBarFree]);
       softmax_bar();  // the row arrays are rewritten by the next pair
     }
-    // dK and dV of this key tile: key row `row`
+    // dV (warp half 0) and dK (half 1) of this key tile: key row `row`
     const bool oka = __all_sync(0xffffffffu, wait_or_abort(&bar[kBarAcc], 0, dead, p.err));
     tc_fence_after();
     if (oka) {
       const int key = kt * kT + row;
-      __nv_bfloat16* dkr = p.dk + (int64_t)b * p.dk_sb + (int64_t)hk * p.dk_sh + (int64_t)key * p.dk_ss;
-      __nv_bfloat16* dvr = p.dv + (int64_t)b * p.dv_sb + (int64_t)hk * p.dv_sh + (int64_t)key * p.dv_ss;
+      __nv_bfloat16* outr = hf ? p.dk + (int64_t)b * p.dk_sb + (int64_t)hk * p.dk_sh + (int64_t)key * p.dk_ss
+                               : p.dv + (int64_t)b * p.dv_sb + (int64_t)hk * p.dv_sh + (int64_t)key * p.dv_ss;
+      const uint32_t col = hf ? 384u : 256u;
 #pragma unroll 1
-      for (int which = 0; which < 2; ++which) {
-        __nv_bfloat16* out = which ? dkr : dvr;
-        const uint32_t col = which ? 384u : 256u;
-#pragma unroll 1
-        for (int c4 = 0; c4 < D / 32; ++c4) {
-          float t[32];
-          tmem_ld32(tmem + lane_base + col + c4 * 32, t);
-          tmem_wait_ld();
-          if (n_pairs == 0) {
+      for (int c4 = 0; c4 < D / 32; ++c4) {
+        float t[32];
+        tmem_ld32(tmem + lane_base + col + c4 * 32, t);
+        tmem_wait_ld();
+        if (n_pairs == 0) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) t[j] = 0.f;
-          }
+          for (int j = 0; j < 32; ++j) t[j] = 0.f;
+        }
 #pragma unroll
-          for (int v8 = 0; v8 < 4; ++v8) {
-            uint4 pk;
-            pk.x = pack_bf16x2(t[v8 * 8 + 0], t[v8 * 8 + 1]);
-            pk.y = pack_bf16x2(t[v8 * 8 + 2], t[v8 * 8 + 3]);
-            pk.z = pack_bf16x2(t[v8 * 8 + 4], t[v8 * 8 + 5]);
-            pk.w = pack_bf16x2(t[v8 * 8 + 6], t[v8 * 8 + 7]);
-            *reinterpret_cast<uint4*>(out + c4 * 32 + v8 * 8) = pk;
-          }
+        for (int v8 = 0; v8 < 4; ++v8) {
+          uint4 pk;
+          pk.x = pack_bf16x2(t[v8 * 8 + 0], t[v8 * 8 + 1]);
+          pk.y = pack_bf16x2(t[v8 * 8 + 2], t[v8 * 8 + 3]);
+          pk.z = pack_bf16x2(t[v8 * 8 + 4], t[v8 * 8 + 5]);
+          pk.w = pack_bf16x2(t[v8 * 8 + 6], t[v8 * 8 + 7]);
+          *reinterpret_cast<uint4*>(outr + c4 * 32 + v8 * 8) = pk;
         }
       }
     }

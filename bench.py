@@ -519,6 +519,39 @@ def cpu_baseline_prefill(budget_s: float) -> dict:
                       f"fp32 dense-mask attention), {t:.1f} s"}
 
 
+def cpu_baseline_prefill_bwd(budget_s: float) -> dict:
+    """torch autograd backward of the eager dense-mask attention in fp32 on the host cores, reduced
+    shape (the forward runs outside the timed part); credited with 10 x D FLOP per visible pair."""
+    from oracle.mask_ref import arith_mask
+
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    C, K, N, D = 512, 256, 4, 128
+    quota = [256, 128, 64, 128]
+    S0 = N * (C + K)
+    g = torch.Generator().manual_seed(0)
+    q = torch.randn((len(quota), S0, D), generator=g, requires_grad=True)
+    k = torch.randn((1, S0, D), generator=g, requires_grad=True)
+    v = torch.randn((1, S0, D), generator=g, requires_grad=True)
+    dout = torch.randn((len(quota), S0, D), generator=g)
+    mask = torch.from_numpy(arith_mask(S0, C, K, quota_per_head=quota)[0])
+    flops = 10.0 * D * float(mask.sum())
+    scale = 1.0 / np.sqrt(D)
+    n, t = 0, 0.0
+    while t < budget_s or n == 0:
+        s_ = (q @ k.transpose(1, 2)) * scale
+        s_ = s_.masked_fill(~mask, float("-inf"))
+        out = torch.softmax(s_, dim=-1) @ v
+        t0 = time.perf_counter()
+        out.backward(dout)
+        t += time.perf_counter() - t0
+        q.grad = k.grad = v.grad = None
+        n += 1
+    return {"value": flops * n / t / 1e12, "unit": "TFLOP/s", "cores": cores, "kind": "port",
+            "sample": f"{n} x backward of (1 sequence of {N} blocks x (512 + 256), 4 query heads with quotas "
+                      f"{quota}, fp32 dense-mask attention), {t:.1f} s"}
+
+
 def cpu_baseline_codestep(budget_s: float) -> dict:
     """The reference's noncausal code step (_attend_request_vectorized, torch CPU port) on one
     config-2 request's caches + 256 code rows, layer after layer."""
@@ -593,6 +626,9 @@ def run_path(args) -> None:
     if args.path == "prefill":
         line = benchmarks.bench_prefill(ns)
         launches = 36 * args.steps
+    elif args.path == "prefill_bwd":
+        line = benchmarks.bench_prefill_bwd(ns)
+        launches = 3 * 36 * args.steps  # per layer: row-dot, backward, dq store
     elif args.path == "codestep":
         line = benchmarks.bench_codestep(ns)
         launches = 36 * args.steps
@@ -601,7 +637,8 @@ def run_path(args) -> None:
         launches = None
     clocks = sampler.stop()
     budget = 0.0 if args.no_cpu_baseline else args.cpu_budget
-    cpu = None if args.no_cpu_baseline else {"prefill": cpu_baseline_prefill, "codestep": cpu_baseline_codestep,
+    cpu = None if args.no_cpu_baseline else {"prefill": cpu_baseline_prefill, "prefill_bwd": cpu_baseline_prefill_bwd,
+                                             "codestep": cpu_baseline_codestep,
                                              "compaction": cpu_baseline_compaction}[args.path](budget)
     line.update({"n_gpus": 1, "steps": args.steps if args.path != "compaction" else ns.blocks,
                  "warmup": args.warmup, "higher_is_better": True, "scaling": None, "vs_baseline": None,
@@ -629,7 +666,7 @@ def main() -> None:
     ap.add_argument("--config", type=int, choices=[2, 3, 5], default=2,
                     help="2 (default, headline): weak scaling; 3 / 5: strong-scaling saturation runs")
     ap.add_argument("--shard", choices=["seq", "kv"], default="seq", help="config 5: sequence or KV-head sharding")
-    ap.add_argument("--path", choices=["decode", "prefill", "codestep", "compaction"], default="decode",
+    ap.add_argument("--path", choices=["decode", "prefill", "prefill_bwd", "codestep", "compaction"], default="decode",
                     help="decode (default, the headline) or a secondary path's line with its CPU baseline")
     ap.add_argument("--flex", action="store_true", help="--path prefill: also time compiled FlexAttention")
     ap.add_argument("--gather", choices=["fused", "nccl"], default="fused",
