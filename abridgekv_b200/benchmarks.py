@@ -113,7 +113,7 @@ def bench_prefill_bwd(args) -> dict:
     Algorithmic work: 10 x D FLOP per visible (query, key) pair per head (S recomputed, dP, dV, dK, dQ)."""
     from . import prefill
 
-    B, H, Hkv, D, C, K, N = 16, 32, 8, 128, 512, 256, 16
+    B, H, Hkv, D, C, K, N = getattr(args, "batch", 16), 32, 8, 128, 512, 256, 16
     S0 = N * (C + K)
     dev = torch.device("cuda")
     gen = torch.Generator(device=dev).manual_seed(0)
@@ -452,6 +452,7 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=2)
     ap.add_argument("--flex", action="store_true")
     ap.add_argument("--blocks", type=int, default=6)
+    ap.add_argument("--batch", type=int, default=16, help="prefill_bwd: sequences (16 = config 4)")
     args = ap.parse_args()
     fn = {"prefill": bench_prefill, "prefill_bwd": bench_prefill_bwd, "compaction": bench_compaction,
           "codestep": bench_codestep, "packed": bench_packed}[args.which]
