@@ -178,6 +178,16 @@ static inline int encode_tiled_4d(CUtensorMap* m, const void* base, const cuuint
   for (int i = 0; i < 3; ++i)
     if (gstr[i] % 16 != 0 || gstr[i] == 0) return ABKV_ERR_INVALID_ARG;
   const cuuint32_t es[4] = {1, 1, 1, 1};
+  // cuTensorMapEncodeTiled is a driver call: it needs the device's context current in the calling
+  // thread, which a thread that made no runtime call yet (autograd's device thread, a worker
+  // pool) does not have.  cudaFree(nullptr) binds the primary context; once per thread and device.
+  static thread_local int bound_device = -1;
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess) return ABKV_ERR_CUDA;
+  if (bound_device != device) {
+    if (cudaFree(nullptr) != cudaSuccess) return ABKV_ERR_CUDA;
+    bound_device = device;
+  }
   void* fn = nullptr;
   cudaDriverEntryPointQueryResult qres;
   if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &qres) != cudaSuccess ||

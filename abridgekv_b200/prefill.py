@@ -103,6 +103,13 @@ def prefill_masked_backward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o
     if lse.dtype != torch.float32 or tuple(lse.shape) != (B, H, S) or not lse.is_contiguous():
         raise ValueError("lse must be the forward's contiguous float32 [B, H, S] log-sum-exp")
     dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    for name, t in (("query", q), ("key", k), ("value", v), ("out", out), ("dout", dout), ("dq", dq), ("dk", dk),
+                    ("dv", dv)):
+        if t.data_ptr() % 16:
+            raise ValueError(f"{name} must start on a 16-byte boundary")
+    for name, t in (("out", out), ("dout", dout), ("dq", dq), ("dk", dk), ("dv", dv)):
+        if any(t.stride(i) % 8 for i in range(3)):
+            raise ValueError(f"{name} strides must be multiples of 8 elements, got {tuple(t.stride())}")
     pl = None
     if prompt_len is not None:
         pl = prompt_len.to(device=q.device, dtype=torch.int32).contiguous()
@@ -123,7 +130,11 @@ def prefill_masked_backward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o
             strides(out), dout.data_ptr(), strides(dout), lse.data_ptr(), dq.data_ptr(), strides(dq), dk.data_ptr(),
             strides(dk), dv.data_ptr(), strides(dv), quota, pl.data_ptr() if pl is not None else None, B, H, Hkv,
             S, D, C, K_layout, scale, ws.ptr(), ws.nbytes, s.cuda_stream)
-    _lib.check("abkv_prefill_masked_backward", st)
+    _lib.check("abkv_prefill_masked_backward", st,
+               f"B={B} H={H} Hkv={Hkv} S={S} D={D} C={C} K_layout={K_layout} scale={scale} "
+               f"quota={None if quota_per_head is None else list(quota_per_head)} "
+               f"strides q{tuple(q.stride())} k{tuple(k.stride())} out{tuple(out.stride())} "
+               f"dout{tuple(dout.stride())} dq{tuple(dq.stride())} dk{tuple(dk.stride())}")
     return dq, dk, dv
 
 

@@ -73,3 +73,30 @@ def test_autograd_function_and_attention_interface():
     o.backward(_dev(dout).transpose(1, 2))
     for t, d in zip((qt, kt, vt), direct):
         assert np.array_equal(t.grad.float().cpu().numpy(), d)
+
+
+def test_forward_and_backward_from_a_fresh_thread():
+    """Tensor-map encoding is a driver call: a thread that made no CUDA runtime call yet (autograd's
+    device thread, a worker pool) must still get results equal to the calling thread's."""
+    import threading
+
+    g, dout, *_ = load_prefill_bwd("c256k128_g4")
+    (q, k, v, pl), direct = _run(g, dout)
+    box = {}
+
+    def work():
+        try:
+            out, lse = prefill.prefill_masked(q, k, v, C=g["C"], K_layout=g["K"], quota_per_head=list(g["quota"]),
+                                              prompt_len=pl, return_lse=True)
+            box["grads"] = prefill.prefill_masked_backward(q, k, v, out, _dev(dout), lse, C=g["C"], K_layout=g["K"],
+                                                           quota_per_head=list(g["quota"]), prompt_len=pl)
+            torch.cuda.current_stream().synchronize()
+        except Exception as e:  # reported below, in the test thread
+            box["error"] = e
+
+    t = threading.Thread(target=work)
+    t.start()
+    t.join()
+    assert "error" not in box, box.get("error")
+    for got, d in zip(box["grads"], direct):
+        np.testing.assert_allclose(got.float().cpu().numpy(), d, atol=2e-3 * float(np.abs(d).max()))
