@@ -110,3 +110,45 @@ def test_gather_struct_layout():
     # abkv_gather_t: 8 pointers, size_t, 3 ints, 2 uint32 (natural alignment, no packing)
     assert C.sizeof(_lib.GatherT) == 8 * 8 + 8 + 4 * 5 + 4
     assert _lib.GatherT.epoch.offset == 84
+
+
+def test_prefill_backward_workspace_size():
+    lib = _lib.lib()
+    n = lib.abkv_prefill_masked_backward_workspace_size(16, 32, 12288, 128)
+    rows = 16 * 32 * 12288
+    assert n >= rows * 128 * 4 + rows * 4 and n % 256 == 0   # fp32 dQ accumulator + rowsum(dO * O)
+    assert lib.abkv_prefill_masked_backward_workspace_size(1, 4, 512, 96) == 0   # head_dim 96 unsupported
+    assert lib.abkv_prefill_masked_backward_workspace_size(0, 4, 512, 128) == 0
+
+
+@pytest.mark.parametrize("bad", ["null_dout", "heads", "scale", "head_dim", "layout", "unaligned", "stride",
+                                 "workspace"])
+def test_prefill_backward_validation_rejects_before_launch(bad):
+    """abkv_prefill_masked_backward checks pointers, shapes, alignment, strides and the workspace before
+    it encodes a tensor map or launches anything."""
+    lib = _lib.lib()
+    fake = 1 << 20  # never dereferenced: validation fails first
+    ptr = {n: fake for n in ("q", "k", "v", "out", "dout", "lse", "dq", "dk", "dv")}
+    if bad == "null_dout":
+        ptr["dout"] = 0
+    if bad == "unaligned":
+        ptr["dq"] = fake + 8
+    B, H, Hkv, S, D, Cc, K = 1, 4, 2, 512, 128, 128, 128
+    if bad == "heads":
+        H, Hkv = 6, 4
+    if bad == "head_dim":
+        D = 96
+    if bad == "layout":
+        S = 500
+    scale = -1.0 if bad == "scale" else 0.088
+    st_q = _lib.i64_array([H * S * D, S * D, D])
+    st_kv = _lib.i64_array([Hkv * S * D, S * D, D])
+    st_dq = _lib.i64_array([H * S * D, S * D, D + 4]) if bad == "stride" else st_q
+    ws, ws_bytes = (0, 0) if bad == "workspace" else (fake, 1 << 30)
+    st = lib.abkv_prefill_masked_backward(
+        ptr["q"], st_q, ptr["k"], st_kv, ptr["v"], st_kv, ptr["out"], st_q, ptr["dout"], st_q, ptr["lse"],
+        ptr["dq"], st_dq, ptr["dk"], st_kv, ptr["dv"], st_kv, None, None, B, H, Hkv, S, D, Cc, K, scale, ws,
+        ws_bytes, None)
+    expect = {"null_dout": 1, "heads": 1, "scale": 1, "head_dim": 3, "layout": 3, "unaligned": 1, "stride": 1,
+              "workspace": 2}[bad]
+    assert st == expect, (bad, st)
