@@ -11,7 +11,7 @@
 //
 // CTA = one 128-key tile of one KV head; it walks every (query tile, query head
 // of the group) pair whose 128 x 128 tile the mask does not empty, keeping dK and
-// dV in TMEM, and adds each pair's dQ tile into an fp32 buffer with vector
+// dV in TMEM, and adds each pair's dQ tile into an fp32 buffer with TMA tensor
 // reductions.  10 warps:
 //   warp 0      TMA: the CTA's K and V tiles once, then Q and dO of each pair
 //               (cp.async.bulk.tensor, 128B swizzle, no multicast)
@@ -29,8 +29,9 @@
 //               in shared memory, form P and dS for their key row from S^T and
 //               dP^T (the mask is a per-query prefix of the key tile), store
 //               P^T / dS^T into TMEM and dS into shared memory (the A operand of
-//               dQ), then reduce dQ into the fp32 buffer.  At the end they write
-//               dV (first half) and dK (second half).
+//               dQ), then add dQ into the fp32 buffer by TMA tensor reductions
+//               from a staging buffer.  At the end they write dV (first half)
+//               and dK (second half).
 // The phases of one pair run one after the other (one S^T / dP^T buffer).
 // Every mbarrier wait is bounded and records ABKV_DEVERR_TIMEOUT on expiry.
 #include <cstring>
@@ -60,7 +61,8 @@ struct Layout {
   static constexpr int kOffQ = kOffV + kTileBytes;
   static constexpr int kOffDO = kOffQ + kTileBytes;
   static constexpr int kOffDS = kOffDO + kTileBytes;  // dS [128 keys][128 q] bf16, MN-major A of dQ
-  static constexpr int kOffRow = kOffDS + kT * kT * 2;  // lse2[128], di[128], lim[128]
+  static constexpr int kOffStage = kOffDS + kT * kT * 2;  // dQ staging: 2 boxes [128 rows][32 f32], 128B swizzle
+  static constexpr int kOffRow = kOffStage + 2 * kT * 128;  // lse2[128], di[128], lim[128]
   static constexpr int kOffBar = kOffRow + 3 * kT * 4;
   static constexpr int kOffList = kOffBar + 256;
   static constexpr int kSmem = kOffList + 4 * kMaxPairs + 16 + 1024;
@@ -75,6 +77,7 @@ constexpr int kBarKV = 0, kBarQD = 1, kBarQDE = 2, kBarS = 3, kBarP = 4, kBarDQ 
 
 struct alignas(64) BwdParams {
   CUtensorMap tm_q, tm_k, tm_v, tm_do;
+  CUtensorMap tm_dq;  // the fp32 dQ accumulator as [B*H*S rows][D], box [128 rows][32], 128B swizzle
   const float* lse;   // [B][H][S], natural log (the forward's)
   const float* di;    // [B][H][S], rowsum(dO * O)
   float* dq_acc;      // [B][H][S][D] fp32
@@ -88,10 +91,16 @@ struct alignas(64) BwdParams {
   float scale, scale_log2;
 };
 
-__device__ __forceinline__ void red_add_v4(float* dst, float a, float b, float c, float d) {
-  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};\n" ::"l"(dst), "f"(a), "f"(b), "f"(c), "f"(d)
+// global[tile at (x, y)] += shared box (f32 add by the TMA engine), tracked by the bulk group.
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, uint32_t src, int x, int y) {
+  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%1, %2}], [%3];\n"
+               ::"l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(src)
                : "memory");
 }
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;\n" ::: "memory"); }
+// this thread's bulk operations have read their shared-memory sources / have completed
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;\n" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory"); }
 __device__ __forceinline__ void sts128(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};\n" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }
@@ -304,28 +313,51 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_bwd_kernel(const __grid_c
       asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // dS visible to the tensor core
       tc_fence_before();
       mbar_arrive_one(&bar[kBarP]);
-      // dQ of this pair: query row `row`, dims [64 hf, 64 hf + 64) in columns [128 hf, 128 hf + 64)
+      // dQ of this pair: query row `row`, dims [64 hf, 64 hf + 64) in columns [128 hf, 128 hf + 64).
+      // Read into registers and release the TMEM columns; then each 64-dim half in turn goes through
+      // the staging buffer (two [128 rows][32 dims] boxes, 128B swizzle) into the fp32 accumulator
+      // with TMA tensor reductions issued by one thread.
       const bool okq = __all_sync(0xffffffffu, wait_or_abort(&bar[kBarDQ], par, dead, p.err));
       if (!okq) dead = true;
       tc_fence_after();
+      float t[64];
       if (hf < D / 64) {
-        float* dst = p.dq_acc + ((((int64_t)b * p.H + h) * p.S) + qt * kT + row) * D + 64 * hf;
-#pragma unroll
-        for (int c2 = 0; c2 < 2; ++c2) {
-          float t[32];
-          tmem_ld32(tmem + lane_base + 128 * hf + 32 * c2, t);
-          tmem_wait_ld();
-          if (!dead) {
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-              red_add_v4(dst + 32 * c2 + 4 * j, t[4 * j], t[4 * j + 1], t[4 * j + 2], t[4 * j + 3]);
-          }
-        }
+        tmem_ld32(tmem + lane_base + 128 * hf, *reinterpret_cast<float(*)[32]>(t));
+        tmem_ld32(tmem + lane_base + 128 * hf + 32, *reinterpret_cast<float(*)[32]>(t + 32));
+        tmem_wait_ld();
       }
       tc_fence_before();
       mbar_arrive_one(&bar[kBarFree]);
+      const bool issuer = threadIdx.x == 64;
+      const uint32_t stage = smem_u32(smem + LY::kOffStage);
+      const int y0 = (int)(((int64_t)b * p.H + h) * p.S + qt * kT);
+      if (issuer) bulk_wait_read();  // the previous pair's reductions have read the staging buffer
+#pragma unroll 1
+      for (int half = 0; half < D / 64; ++half) {
+        softmax_bar();  // staging buffer free
+        if (hf == half) {
+#pragma unroll
+          for (int j = 0; j < 2; ++j)
+#pragma unroll
+            for (int c = 0; c < 8; ++c)
+              sts128(stage + j * (kT * 128) + row * 128 + ((c ^ (row & 7)) << 4), __float_as_uint(t[32 * j + 4 * c]),
+                     __float_as_uint(t[32 * j + 4 * c + 1]), __float_as_uint(t[32 * j + 4 * c + 2]),
+                     __float_as_uint(t[32 * j + 4 * c + 3]));
+          asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+        }
+        softmax_bar();  // every row of this half is staged
+        if (issuer) {
+          if (!dead) {
+            tma_reduce_add_2d(&p.tm_dq, stage, 64 * half, y0);
+            tma_reduce_add_2d(&p.tm_dq, stage + kT * 128, 64 * half + 32, y0);
+            bulk_commit();
+          }
+          if (half + 1 < D / 64) bulk_wait_read();
+        }
+      }
       softmax_bar();  // the row arrays are rewritten by the next pair
     }
+    if (threadIdx.x == 64) bulk_wait_all();  // every dQ reduction of this CTA has landed
     // dV (warp half 0) and dK (half 1) of this key tile: key row `row`
     const bool oka = __all_sync(0xffffffffu, wait_or_abort(&bar[kBarAcc], 0, dead, p.err));
     tc_fence_after();
@@ -468,6 +500,13 @@ extern "C" int abkv_prefill_masked_backward(
   if (st == ABKV_OK) st = make_map(&prm.tm_do, dout, B, H, S, head_dim, dout_strides);
   if (st == ABKV_OK) st = make_map(&prm.tm_k, k, B, Hkv, S, head_dim, k_strides);
   if (st == ABKV_OK) st = make_map(&prm.tm_v, v, B, Hkv, S, head_dim, v_strides);
+  if (st == ABKV_OK) {
+    const cuuint64_t dims[2] = {(cuuint64_t)head_dim, (cuuint64_t)rows};
+    const cuuint64_t gstr[1] = {(cuuint64_t)head_dim * 4};
+    const cuuint32_t box[2] = {32, (cuuint32_t)kT};
+    st = tc::encode_tiled(&prm.tm_dq, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, dq_acc, dims, gstr, box,
+                          CU_TENSOR_MAP_SWIZZLE_128B);
+  }
   if (st != ABKV_OK) return st;
   for (int h = 0; h < H; ++h) {
     const int qq = quota_per_head ? quota_per_head[h] : K_layout;

@@ -170,14 +170,15 @@ using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, 
                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
-// 4D tensor map over bf16 with byte strides gstr (dims 1..3), 128B swizzle.  The
+// Tiled tensor map of rank 1..5 with byte strides gstr (dims 1..rank-1).  The
 // driver entry point is resolved through the runtime, so the library does not
 // link libcuda and still loads on hosts without a GPU driver.
-static inline int encode_tiled_4d(CUtensorMap* m, const void* base, const cuuint64_t (&dims)[4],
-                                  const cuuint64_t (&gstr)[3], const cuuint32_t (&box)[4]) {
-  for (int i = 0; i < 3; ++i)
+static inline int encode_tiled(CUtensorMap* m, CUtensorMapDataType dtype, int rank, const void* base,
+                               const cuuint64_t* dims, const cuuint64_t* gstr, const cuuint32_t* box,
+                               CUtensorMapSwizzle swizzle) {
+  for (int i = 0; i < rank - 1; ++i)
     if (gstr[i] % 16 != 0 || gstr[i] == 0) return ABKV_ERR_INVALID_ARG;
-  const cuuint32_t es[4] = {1, 1, 1, 1};
+  const cuuint32_t es[5] = {1, 1, 1, 1, 1};
   // cuTensorMapEncodeTiled is a driver call: it needs the device's context current in the calling
   // thread, which a thread that made no runtime call yet (autograd's device thread, a worker
   // pool) does not have.  cudaFree(nullptr) binds the primary context; once per thread and device.
@@ -194,10 +195,15 @@ static inline int encode_tiled_4d(CUtensorMap* m, const void* base, const cuuint
       qres != cudaDriverEntryPointSuccess || !fn)
     return ABKV_ERR_CUDA;
   CUresult r = reinterpret_cast<EncodeTiled>(fn)(
-      m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, gstr, box, es,
-      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+      m, dtype, (cuuint32_t)rank, const_cast<void*>(base), dims, gstr, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+      swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? ABKV_OK : ABKV_ERR_INVALID_ARG;
+}
+
+// 4D tensor map over bf16 with byte strides gstr (dims 1..3), 128B swizzle.
+static inline int encode_tiled_4d(CUtensorMap* m, const void* base, const cuuint64_t (&dims)[4],
+                                  const cuuint64_t (&gstr)[3], const cuuint32_t (&box)[4]) {
+  return encode_tiled(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, base, dims, gstr, box, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 }  // namespace tc
