@@ -97,6 +97,21 @@ __device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, uint32
                ::"l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(src)
                : "memory");
 }
+// Packed fp32 pairs: (a0, a1) * (b0, b1) + (c0, c1) and (a0 - b0, a1 - b1) * (c0, c1).
+__device__ __forceinline__ void fma2v(float& d0, float& d1, float a0, float a1, float b0, float b1, float c0,
+                                      float c1) {
+  asm("{\n .reg .b64 x, y, z, r;\n mov.b64 x, {%2, %3};\n mov.b64 y, {%4, %5};\n mov.b64 z, {%6, %7};\n"
+      " fma.rn.f32x2 r, x, y, z;\n mov.b64 {%0, %1}, r;\n}\n"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+__device__ __forceinline__ void submul2(float& d0, float& d1, float a0, float a1, float b0, float b1, float c0,
+                                        float c1) {
+  asm("{\n .reg .b64 x, y, z, r;\n mov.b64 x, {%2, %3};\n mov.b64 y, {%4, %5};\n mov.b64 z, {%6, %7};\n"
+      " sub.rn.f32x2 r, x, y;\n mul.rn.f32x2 r, r, z;\n mov.b64 {%0, %1}, r;\n}\n"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;\n" ::: "memory"); }
 // this thread's bulk operations have read their shared-memory sources / have completed
 __device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;\n" ::: "memory"); }
@@ -291,11 +306,14 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_bwd_kernel(const __grid_c
           const int lim[8] = {ma.x, ma.y, ma.z, ma.w, mb.x, mb.y, mb.z, mb.w};
           float pv[8], dsv[8];
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
+          for (int j = 0; j < 8; j += 2) {
             const int cc = 8 * c8 + j;
-            const float pe = row < lim[j] ? fast_exp2(sv[cc] * sl2 - lse[j]) : 0.f;
-            pv[j] = pe;
-            dsv[j] = pe * (dpv[cc] - di[j]) * scale;
+            float x0, x1;
+            fma2v(x0, x1, sv[cc], sv[cc + 1], sl2, sl2, -lse[j], -lse[j + 1]);
+            pv[j] = row < lim[j] ? fast_exp2(x0) : 0.f;
+            pv[j + 1] = row < lim[j + 1] ? fast_exp2(x1) : 0.f;
+            // dS = (dP - Di) * (P * scale)
+            submul2(dsv[j], dsv[j + 1], dpv[cc], dpv[cc + 1], di[j], di[j + 1], pv[j] * scale, pv[j + 1] * scale);
           }
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
