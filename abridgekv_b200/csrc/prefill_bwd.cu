@@ -499,6 +499,7 @@ extern "C" int abkv_prefill_masked_backward(
   if (H / Hkv > 255) return ABKV_ERR_UNSUPPORTED;
   if (C <= 0 || K_layout <= 0 || C % kT || K_layout % kT || S % (C + K_layout)) return ABKV_ERR_UNSUPPORTED;
   if ((int64_t)(S / kT) * (H / Hkv) > kMaxPairs || S / kT > (1 << 23)) return ABKV_ERR_UNSUPPORTED;
+  if ((int64_t)B * H * S > INT32_MAX) return ABKV_ERR_UNSUPPORTED;  // dQ rows are 32-bit TMA coordinates
   for (int i = 0; i < 8; ++i)
     if (reinterpret_cast<uintptr_t>(ptrs[i]) & 15) return ABKV_ERR_INVALID_ARG;
   for (int i = 3; i < 8; ++i)  // rows of out, dout, dq, dk, dv are written or read as 16-byte vectors

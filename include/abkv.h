@@ -386,8 +386,8 @@ int abkv_prefill_masked(const void* q, const int64_t* q_strides, const void* k,
  * dk / dv [B][Hkv][S][D] bf16 outputs (strides multiples of 8 elements).
  * The workspace holds an fp32 dq accumulator and rowsum(dout * out):
  * abkv_prefill_masked_backward_workspace_size(B, H, S, head_dim) bytes,
- * 256-byte aligned.  Same shape limits as the forward, and (S / 128) x (H / Hkv)
- * <= 2048. */
+ * 256-byte aligned.  Same shape limits as the forward, (S / 128) x (H / Hkv)
+ * <= 2048 and B x H x S < 2^31. */
 size_t abkv_prefill_masked_backward_workspace_size(int B, int H, int S,
                                                    int head_dim);
 int abkv_prefill_masked_backward(
