@@ -4,6 +4,7 @@
     python -m abridgekv_b200.benchmarks compaction [--steps 5]
     python -m abridgekv_b200.benchmarks codestep   [--layers 36] [--steps 3]
     python -m abridgekv_b200.benchmarks packed     [--steps 20]
+    python -m abridgekv_b200.benchmarks kvshard    [--kv-heads 1] [--seqs 256] [--chunk-tokens 0]
 
 prefill    BASELINE config 4: B=16 sequences of 16 blocks x (512 content + 256 code rows)
            = 12,288 rows, Qwen3-4B attention (32 q / 8 kv heads, head_dim 128), per-layer
@@ -26,6 +27,11 @@ packed     decode with per-head code quotas in packed sidecar pages: config 2's 
            cache, 31 compressed blocks) with per-KV-head quotas 256/128/64/64/192/64/128/128
            (mean 128, as config 2's per-layer mean): 31 sidecar pages per request and layer.
            Algorithmic bytes = every key/value row read once + Q/O.
+kvshard    one GPU's share of BASELINE config 5 under KV-head sharding: --kv-heads of the 8
+           KV heads (with their 4 query heads each) of --seqs sequences, 36 layers of 128-row
+           quotas over a 32K-token generation, one decode launch over all layers per step.
+           --chunk-tokens 0 is the automatic split-KV chunk.  Algorithmic bytes = every kept
+           key/value row of the shard read once + Q/O.
 """
 from __future__ import annotations
 
@@ -444,18 +450,57 @@ def bench_packed(args) -> dict:
                        "main_rows": "256 + U[0,511]"}}
 
 
+def bench_kvshard(args) -> dict:
+    from . import decode
+    from .workloads import qwen3_decode_workload
+    from .workspace import Workspace
+
+    wl = qwen3_decode_workload(5, num_seqs=args.seqs, kv_heads=slice(0, args.kv_heads))
+    ws = Workspace()
+    outs = [torch.empty_like(q) for q in wl.queries]
+
+    def step():
+        decode.paged_decode(wl.queries, wl.kv_caches, wl.block_tables, wl.seq_lens, outputs=outs,
+                            max_pages_per_seq=wl.max_pages, chunk_tokens=args.chunk_tokens, workspace=ws)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    if ws.read_error():
+        raise RuntimeError(f"decode device error flag {ws.read_error():#x}")
+    ms = e0.elapsed_time(e1) / args.steps
+    alg = wl.kv_bytes + wl.qo_bytes
+    gbs = alg / (ms / 1e3) / 1e9
+    pk = _peaks()
+    return {"metric": "config-5 KV-head shard decode tokens/s (one GPU's share)", "value": args.seqs / (ms / 1e3),
+            "unit": "tokens/s", "ms_per_step": ms, "algorithmic_gb_per_step": alg / 1e9,
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": pk.get("hbm_gbs"), "unit": "GB/s",
+                         "frac": gbs / pk.get("hbm_gbs", 6650.0)},
+            "config": {"kv_heads": args.kv_heads, "seqs": args.seqs, "layers": wl.num_layers,
+                       "chunk_tokens": args.chunk_tokens or "auto"}}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("which", choices=["prefill", "prefill_bwd", "compaction", "codestep", "packed"])
+    ap.add_argument("which", choices=["prefill", "prefill_bwd", "compaction", "codestep", "packed", "kvshard"])
     ap.add_argument("--layers", type=int, default=36)
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=2)
     ap.add_argument("--flex", action="store_true")
     ap.add_argument("--blocks", type=int, default=6)
     ap.add_argument("--batch", type=int, default=16, help="prefill_bwd: sequences (16 = config 4)")
+    ap.add_argument("--kv-heads", type=int, default=1, help="kvshard: KV heads of the shard (1, 2, 4, 8)")
+    ap.add_argument("--seqs", type=int, default=256, help="kvshard: sequences")
+    ap.add_argument("--chunk-tokens", type=int, default=0, help="kvshard: split-KV chunk rows (0 = auto)")
     args = ap.parse_args()
     fn = {"prefill": bench_prefill, "prefill_bwd": bench_prefill_bwd, "compaction": bench_compaction,
-          "codestep": bench_codestep, "packed": bench_packed}[args.which]
+          "codestep": bench_codestep, "packed": bench_packed, "kvshard": bench_kvshard}[args.which]
     print(json.dumps(fn(args)), flush=True)
 
 

@@ -842,7 +842,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_split_kernel(const __grid_
   }
 }
 
-int auto_chunk_tiles(int num_layers, int num_seqs, int max_tiles, int page_tiles) {
+constexpr int kMaxAutoChunkTiles = 384;  // 6144 cache rows
+
+int auto_chunk_tiles(int num_layers, int num_seqs, int max_tiles, int page_tiles, int num_kv_heads) {
   // Persistent CTAs take items dynamically: aim for >= ~8 items per SM, with
   // chunks of 16..128 tiles (256..2048 cache rows).
   const int64_t total = (int64_t)num_layers * num_seqs * max_tiles;
@@ -850,6 +852,16 @@ int auto_chunk_tiles(int num_layers, int num_seqs, int max_tiles, int page_tiles
   while (ct > 16 && total / ct < 148 * 8) ct >>= 1;
   if (ct < page_tiles) ct = page_tiles;
   ct = (ct / page_tiles) * page_tiles;
+  // A tile of fewer than 8 KV heads carries fewer bytes, so the per-item costs
+  // (page-id staging, the chunk merge) weigh more: with enough items, grow the
+  // chunk by 8 / num_kv_heads up to kMaxAutoChunkTiles.  Never below the chunk
+  // chosen without the head count, so a workspace sized without it still fits.
+  if (ct == 128 && num_kv_heads > 0 && num_kv_heads < 8) {
+    int big = 128 * (8 / num_kv_heads);
+    if (big > kMaxAutoChunkTiles) big = kMaxAutoChunkTiles;
+    big = (big / page_tiles) * page_tiles;
+    if (big > ct && total / big >= 148 * 8) ct = big;
+  }
   return ct;
 }
 
@@ -863,8 +875,11 @@ constexpr size_t kWsHeader = 256;
 // max_side_rows: an upper bound of the sidecar rows of one (layer, request) over
 // all its heads (sidecar pages x slots), 0 without a sidecar.  Sidecar chunks are
 // per head, so each head may round up by one chunk (+2 per head of slack).
+// num_kv_heads: the launch's KV heads, or 0 where it is not known (workspace
+// queries); it only ever enlarges the auto chunk, so 0 gives the larger plan.
 int plan_decode(int num_layers, int num_seqs, int num_q_heads, int head_dim, int page_size,
-                int max_pages, int chunk_tokens, int64_t max_side_rows, DecodePlan* plan) {
+                int max_pages, int chunk_tokens, int64_t max_side_rows, DecodePlan* plan,
+                int num_kv_heads = 0) {
   if (num_layers <= 0 || num_seqs <= 0 || num_q_heads <= 0 || page_size <= 0 || max_pages <= 0)
     return ABKV_ERR_INVALID_ARG;
   if ((head_dim != 64 && head_dim != kD) || page_size % kTile != 0) return ABKV_ERR_UNSUPPORTED;
@@ -875,7 +890,7 @@ int plan_decode(int num_layers, int num_seqs, int num_q_heads, int head_dim, int
   if (max_tiles > (1 << 26) || side_tiles > (1 << 26)) return ABKV_ERR_UNSUPPORTED;
   int ct;
   if (chunk_tokens == 0) {
-    ct = auto_chunk_tiles(num_layers, num_seqs, (int)(max_tiles + side_tiles), page_tiles);
+    ct = auto_chunk_tiles(num_layers, num_seqs, (int)(max_tiles + side_tiles), page_tiles, num_kv_heads);
   } else {
     if (chunk_tokens < 0 || chunk_tokens % kTile || chunk_tokens % page_size) return ABKV_ERR_INVALID_ARG;
     ct = chunk_tokens / kTile;
@@ -1052,7 +1067,7 @@ int launch_decode(const void* const* q, const void* const* kv, const int32_t* co
   }
   DecodePlan plan;
   int st = plan_decode(num_layers, num_seqs, num_q_heads, head_dim, page_size, max_pages_per_seq,
-                       chunk_tokens, max_side_rows, &plan);
+                       chunk_tokens, max_side_rows, &plan, num_kv_heads);
   if (st != ABKV_OK) return st;
   if (!workspace || workspace_bytes < plan.total) return ABKV_ERR_WORKSPACE;
   if (reinterpret_cast<uintptr_t>(workspace) & 255) return ABKV_ERR_WORKSPACE;

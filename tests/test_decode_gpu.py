@@ -158,6 +158,37 @@ def test_config2_full_size_sampled_rows_and_page_permutation():
         o1 = decode.paged_decode([wl.queries[l]], [wl.kv_caches[l]], [wl.block_tables[l]],
                                  [wl.seq_lens[l]], max_pages_per_seq=wl.max_pages, chunk_tokens=1024)[0]
         assert torch.equal(o1, outs[l])
+    # with all 8 KV heads the automatic chunk stays at 2048 rows
+    auto = decode.paged_decode(wl.queries, wl.kv_caches, wl.block_tables, wl.seq_lens,
+                               max_pages_per_seq=wl.max_pages)
+    fixed = decode.paged_decode(wl.queries, wl.kv_caches, wl.block_tables, wl.seq_lens,
+                                max_pages_per_seq=wl.max_pages, chunk_tokens=2048)
+    assert all(torch.equal(a, b) for a, b in zip(auto, fixed))
+
+
+def test_config5_one_kv_head_shard_auto_chunk():
+    """Config 5's KV-head shard at full size (1 KV head, 256 sequences, 36 layers): the
+    automatic chunk grows to 6144 rows for a 1-head launch (bitwise equal to an explicit
+    6144-row chunk), workspace sized without the head count still fits, and sampled rows
+    match a PyTorch fp32 reference."""
+    from abridgekv_b200.workloads import qwen3_decode_workload
+
+    wl = qwen3_decode_workload(5, num_seqs=256, kv_heads=slice(0, 1))
+    ws = Workspace()
+    auto = decode.paged_decode(wl.queries, wl.kv_caches, wl.block_tables, wl.seq_lens,
+                               max_pages_per_seq=wl.max_pages, workspace=ws)
+    assert ws.read_error() == 0
+    fixed = decode.paged_decode(wl.queries, wl.kv_caches, wl.block_tables, wl.seq_lens,
+                                max_pages_per_seq=wl.max_pages, chunk_tokens=6144)
+    assert all(torch.equal(a, b) for a, b in zip(auto, fixed))
+    scale = 1.0 / np.sqrt(wl.head_dim)
+    rng = np.random.default_rng(5)
+    for l in rng.choice(wl.num_layers, 3, replace=False):
+        sel = torch.as_tensor(rng.choice(wl.num_seqs, 3, replace=False), device="cuda")
+        ref = _torch_fp32_decode(wl.queries[l][sel], wl.kv_caches[l], wl.block_tables[l][sel],
+                                 wl.seq_lens[l][sel], wl.page, scale)
+        err = (auto[l][sel].float() - ref).abs()
+        assert err.max().item() <= ATOL_EXACT, (l, err.max().item())
 
 
 def _random_layers(L, B=48, Hq=32, Hkv=8, D=128, page=16, max_pages=64, seed=0):
