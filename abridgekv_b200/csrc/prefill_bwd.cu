@@ -413,6 +413,334 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_bwd_kernel(const __grid_c
   }
 }
 
+// ---------------------------------------------------------------------------
+// head_dim 128: the same CTA work (one 128-key tile of one KV head, every
+// visible (query tile, head) pair) cut into 64-query units -- the two halves of
+// each pair -- so that two units are in flight: the tensor core computes the
+// scores of unit u+1 and the gradients of unit u while the threads form P / dS
+// of one unit and add the dQ of the previous one.  Per unit u (slot s = u % 2):
+//   S^T  = K Q_u^T   -> TMEM [128 s, 128 s + 64)        (N = 64 queries)
+//   dP^T = V dO_u^T  -> TMEM [128 s + 64, 128 s + 128)
+//   (threads: P^T bf16 -> [128 s + 16, 128 s + 48), dS^T -> [128 s + 80, 128 s + 112),
+//    dS -> shared memory, atom column s of the dS buffer)
+//   dV  += P^T dO_u  -> [256, 384)      dK += dS^T Q_u -> [384, 512)
+//   dQ_u^T = K^T dS_u^T (M = 128 dims, N = 64 queries; both operands MN-major in
+//            shared memory) -> [128 s, 128 s + 64), over the consumed S^T / P^T
+// Q / dO of a unit sit in a two-slot ring ([64 rows][128 dims] each); the
+// threads read dQ_u^T back (lane = dim), stage it as [64 query rows][128 dims]
+// fp32 and add it to the accumulator with four TMA tensor reductions.
+// ---------------------------------------------------------------------------
+constexpr int kU = 64;  // queries per unit
+constexpr uint32_t kIdescU = idesc_bf16_m128(kU, false);  // S^T, dP^T of a unit: N = 64, both K-major
+constexpr uint32_t kIdescAccU = idesc_bf16_m128(128, true);  // dV, dK: N = 128 dims, B MN-major
+
+struct LayoutU {
+  static constexpr int kKV = kT * 128 * 2;      // K or V tile: 2 atoms of [128 rows][128 B]
+  static constexpr int kSlot = kU * 128 * 2;    // Q or dO of a unit: 2 atoms of [64 rows][128 B]
+  static constexpr int kOffK = 0;
+  static constexpr int kOffV = kOffK + kKV;
+  static constexpr int kOffQ = kOffV + kKV;          // Q slots 0, 1
+  static constexpr int kOffDO = kOffQ + 2 * kSlot;   // dO slots 0, 1
+  static constexpr int kOffDS = kOffDO + 2 * kSlot;  // dS: atom column s = [128 keys][64 queries] of slot s
+  static constexpr int kOffStage = kOffDS + kT * kT * 2;  // dQ staging: 4 boxes [64 rows][32 f32]
+  static constexpr int kOffRow = kOffStage + kU * 128 * 4;  // lse2, di, lim: [2 slots][64] each
+  static constexpr int kOffBar = kOffRow + 3 * 2 * kU * 4;
+  static constexpr int kOffList = kOffBar + 256;
+  static constexpr int kSmem = kOffList + 4 * kMaxPairs + 16 + 1024;
+};
+static_assert(LayoutU::kSmem <= 227 * 1024, "shared memory of the 64-query-unit backward");
+
+// barriers of the unit kernel: [2] = one per slot
+constexpr int kUBarKV = 0, kUBarQD = 1, kUBarQDE = 3, kUBarS = 5, kUBarP = 7, kUBarDQ = 9, kUBarFree = 11,
+              kUBarAcc = 13, kUBarTmem = 14;
+static_assert((kUBarTmem + 1) * 8 <= 256, "barrier area");
+
+__global__ void __launch_bounds__(kThreads, 1) prefill_bwd_unit_kernel(const __grid_constant__ BwdParams p) {
+  using LY = LayoutU;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + LY::kOffBar);
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bar + kUBarTmem);
+  float* s_lse2 = reinterpret_cast<float*>(smem + LY::kOffRow);  // [2][64]
+  float* s_di = s_lse2 + 2 * kU;                                   // [2][64]
+  int32_t* s_lim = reinterpret_cast<int32_t*>(s_di + 2 * kU);      // [2][64]
+  int32_t* s_list = reinterpret_cast<int32_t*>(smem + LY::kOffList);
+  int32_t* s_n = s_list + kMaxPairs;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kt = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
+  const int G = p.G;
+  const int pl = p.prompt_len ? __ldg(p.prompt_len + b) : 0;
+  const int kb = kt * kT / p.per, kw0 = kt * kT - kb * p.per;
+  const int qt_first = kb * p.per / kT;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kUBarTmem; ++i) {
+      const bool threads = (i >= kUBarP && i < kUBarP + 2) || (i >= kUBarFree && i < kUBarFree + 2);
+      mbar_init(&bar[i], threads ? 256 : 1);
+    }
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(s_tmem)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n");
+  }
+  if (warp == 2) {  // the (query tile, head) pairs this key tile contributes to, by ballot
+    int n = 0;
+    const int total = (p.n_tiles - qt_first) * G;
+    for (int base = 0; base < total; base += 32) {
+      const int i = base + lane;
+      const int qt = qt_first + i / G, g = i % G;
+      const bool vis = i < total && tile_class(p, hk * G + g, qt, kt, pl) != 0;
+      const uint32_t m = __ballot_sync(0xffffffffu, vis);
+      if (vis && n + __popc(m & ((1u << lane) - 1u)) < kMaxPairs)
+        s_list[n + __popc(m & ((1u << lane) - 1u))] = (qt << 8) | g;
+      n += __popc(m);
+    }
+    if (lane == 0) {
+      if (n > kMaxPairs) set_error(p.err, ABKV_DEVERR_RANGE);
+      *s_n = n < kMaxPairs ? n : kMaxPairs;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *s_tmem;
+  const int n_units = 2 * *s_n;
+  bool dead = false;
+
+  if (warp == 0) {
+    // ---------------- TMA ----------------
+    if (lane == 0) {
+      mbar_expect_tx(&bar[kUBarKV], 2 * LY::kKV);
+      for (int a = 0; a < 2; ++a) {
+        tma_load_4d(smem + LY::kOffK + a * (LY::kKV / 2), &p.tm_k, 64 * a, kt * kT, hk, b, &bar[kUBarKV]);
+        tma_load_4d(smem + LY::kOffV + a * (LY::kKV / 2), &p.tm_v, 64 * a, kt * kT, hk, b, &bar[kUBarKV]);
+      }
+      for (int u = 0; u < n_units; ++u) {
+        const int s = u & 1, i = u >> 1;
+        const int e = s_list[i];
+        const int qrow = (e >> 8) * kT + kU * s, h = hk * G + (e & 0xFF);
+        // slot s is free once the dV / dK MMAs of unit u - 2 ran (immediate for the first use)
+        if (!wait_or_abort(&bar[kUBarQDE + s], (uint32_t)((i & 1) ^ 1), dead, p.err)) break;
+        mbar_expect_tx(&bar[kUBarQD + s], 2 * LY::kSlot);
+        for (int a = 0; a < 2; ++a) {
+          tma_load_4d(smem + LY::kOffQ + s * LY::kSlot + a * (LY::kSlot / 2), &p.tm_q, 64 * a, qrow, h, b,
+                      &bar[kUBarQD + s]);
+          tma_load_4d(smem + LY::kOffDO + s * LY::kSlot + a * (LY::kSlot / 2), &p.tm_do, 64 * a, qrow, h, b,
+                      &bar[kUBarQD + s]);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      const uint64_t dk_k = desc_kmajor_sw128(smem_u32(smem + LY::kOffK));                // A of S^T
+      const uint64_t dv_k = desc_kmajor_sw128(smem_u32(smem + LY::kOffV));                // A of dP^T
+      const uint64_t dk_mn = desc_mnmajor_sw128(smem_u32(smem + LY::kOffK), LY::kKV / 2);  // A of dQ^T (K^T)
+      wait_or_abort(&bar[kUBarKV], 0, dead, p.err);
+      // scores of unit u into TMEM buffer u % 2
+      auto issue_s = [&](int u) -> bool {
+        const int s = u & 1, i = u >> 1;
+        if (!wait_or_abort(&bar[kUBarQD + s], (uint32_t)(i & 1), dead, p.err)) return false;
+        // the buffer held dQ^T of unit u - 2: the threads have read it back
+        if (!wait_or_abort(&bar[kUBarFree + s], (uint32_t)((i & 1) ^ 1), dead, p.err)) return false;
+        tc_fence_after();
+        const uint64_t dq_k = desc_kmajor_sw128(smem_u32(smem + LY::kOffQ + s * LY::kSlot));
+        const uint64_t ddo_k = desc_kmajor_sw128(smem_u32(smem + LY::kOffDO + s * LY::kSlot));
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t oa = (kk >> 2) * (LY::kKV / 2) + (kk & 3) * 32, ob = (kk >> 2) * (LY::kSlot / 2) + (kk & 3) * 32;
+          umma(tmem + 128 * s, desc_advance(dk_k, oa), desc_advance(dq_k, ob), kIdescU, kk > 0 ? 1u : 0u);
+        }
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t oa = (kk >> 2) * (LY::kKV / 2) + (kk & 3) * 32, ob = (kk >> 2) * (LY::kSlot / 2) + (kk & 3) * 32;
+          umma(tmem + 128 * s + 64, desc_advance(dv_k, oa), desc_advance(ddo_k, ob), kIdescU, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&bar[kUBarS + s]);
+        return true;
+      };
+      // gradients of unit u once its P^T / dS^T are in TMEM and dS in shared memory
+      auto finish = [&](int u) -> bool {
+        const int s = u & 1, i = u >> 1;
+        if (!wait_or_abort(&bar[kUBarP + s], (uint32_t)(i & 1), dead, p.err)) return false;
+        tc_fence_after();
+        const uint64_t ddo_mn = desc_mnmajor_sw128(smem_u32(smem + LY::kOffDO + s * LY::kSlot), LY::kSlot / 2);
+        const uint64_t dq_mn = desc_mnmajor_sw128(smem_u32(smem + LY::kOffQ + s * LY::kSlot), LY::kSlot / 2);
+        const uint64_t dds_mn = desc_mnmajor_sw128(smem_u32(smem + LY::kOffDS + s * (kT * 128)), kT * 128);
+#pragma unroll
+        for (int kk = 0; kk < kU / 16; ++kk)
+          umma_tmem_a(tmem + 256, tmem + 128 * s + 16 + kk * 8, desc_advance(ddo_mn, kk * 2048),
+                      kIdescAccU, (u > 0 || kk > 0) ? 1u : 0u);
+#pragma unroll
+        for (int kk = 0; kk < kU / 16; ++kk)
+          umma_tmem_a(tmem + 384, tmem + 128 * s + 80 + kk * 8, desc_advance(dq_mn, kk * 2048),
+                      kIdescAccU, (u > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&bar[kUBarQDE + s]);  // Q / dO slot s may be refilled once these ran
+        // dQ^T over the 128 keys in steps of 16 (its columns overlap P^T, which dV read first:
+        // one thread's MMAs run in issue order)
+#pragma unroll
+        for (int kk = 0; kk < kT / 16; ++kk)
+          umma(tmem + 128 * s, desc_advance(dk_mn, kk * 2048), desc_advance(dds_mn, kk * 2048), kIdescDQ,
+               kk > 0 ? 1u : 0u);
+        umma_commit(&bar[kUBarDQ + s]);
+        return true;
+      };
+      if (n_units > 0 && !dead) issue_s(0);
+      for (int u = 0; u < n_units && !dead; ++u) {
+        if (u + 1 < n_units && !issue_s(u + 1)) break;
+        if (!finish(u)) break;
+      }
+      umma_commit(&bar[kUBarAcc]);
+    }
+  } else {
+    // ---------------- threads of TMEM lanes ----------------
+    // P / dS phase: lane = key row, warp half hf = query columns [32 hf, 32 hf + 32) of the unit.
+    // dQ read-back: lane = dim, warp half hf = the same query columns.
+    const int quarter = warp & 3, hf = (warp - 2) >> 2;
+    const int row = quarter * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    const float sl2 = p.scale_log2, scale = p.scale;
+    const bool issuer = threadIdx.x == 64;
+    const uint32_t stage = smem_u32(smem + LY::kOffStage);
+    auto readback_reduce = [&](int v) {
+      const int s = v & 1, i = v >> 1;
+      const int e = s_list[i];
+      const int qt = e >> 8, h = hk * G + (e & 0xFF);
+      const bool okq = __all_sync(0xffffffffu, wait_or_abort(&bar[kUBarDQ + s], (uint32_t)(i & 1), dead, p.err));
+      if (!okq) dead = true;
+      tc_fence_after();
+      float t[32];
+      tmem_ld32(tmem + lane_base + 128 * s + 32 * hf, t);
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive_one(&bar[kUBarFree + s]);
+      if (issuer) bulk_wait_read();  // the previous unit's reductions have read the staging buffer
+      softmax_bar();
+      // dim `row` of query rows 32 hf .. 32 hf + 31: box `quarter` ([64 rows][32 f32], 128B swizzle)
+      const uint32_t box = stage + quarter * (kU * 128) + (lane & 3) * 4;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const int q = 32 * hf + j;
+        asm volatile("st.shared.b32 [%0], %1;\n" ::"r"(box + q * 128 + (((lane >> 2) ^ (q & 7)) << 4)),
+                     "r"(__float_as_uint(t[j]))
+                     : "memory");
+      }
+      asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+      softmax_bar();  // the unit's dQ is staged
+      if (issuer && !dead) {
+        const int y0 = (int)(((int64_t)b * p.H + h) * p.S + qt * kT + kU * s);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tma_reduce_add_2d(&p.tm_dq, stage + c * (kU * 128), 32 * c, y0);
+        bulk_commit();
+      }
+    };
+    for (int u = 0; u < n_units; ++u) {
+      const int s = u & 1, i = u >> 1;
+      const int e = s_list[i];
+      const int qt = e >> 8, h = hk * G + (e & 0xFF);
+      if (hf == 0 && row < kU) {  // lse (log2 domain), Di and the visible-key prefix of the unit's rows
+        const int q = qt * kT + kU * s + row;
+        const int64_t rr = ((int64_t)b * p.H + h) * p.S + q;
+        const int qb = q / p.per, qw = q - qb * p.per;
+        s_lse2[kU * s + row] = __ldg(p.lse + rr) * 1.4426950408889634f;
+        s_di[kU * s + row] = __ldg(p.di + rr);
+        s_lim[kU * s + row] = tile_limit_fast(p, p.quota[h], q, qb, qw, kb, kw0, kt * kT, pl);
+      }
+      softmax_bar();
+      const bool ok = __all_sync(0xffffffffu, wait_or_abort(&bar[kUBarS + s], (uint32_t)(i & 1), dead, p.err));
+      if (!ok) dead = true;
+      tc_fence_after();
+      {
+        const int qc = 32 * hf;
+        float sv[32], dpv[32];
+        tmem_ld32(tmem + lane_base + 128 * s + qc, sv);
+        tmem_ld32(tmem + lane_base + 128 * s + 64 + qc, dpv);
+        tmem_wait_ld();
+        uint32_t wp[16], wd[16];
+        const uint32_t ds_row = smem_u32(smem + LY::kOffDS) + s * (kT * 128) + row * 128;
+#pragma unroll
+        for (int c8 = 0; c8 < 4; ++c8) {
+          const int q0 = qc + 8 * c8;
+          const float4 la = *reinterpret_cast<const float4*>(s_lse2 + kU * s + q0);
+          const float4 lb = *reinterpret_cast<const float4*>(s_lse2 + kU * s + q0 + 4);
+          const float4 da = *reinterpret_cast<const float4*>(s_di + kU * s + q0);
+          const float4 db = *reinterpret_cast<const float4*>(s_di + kU * s + q0 + 4);
+          const int4 ma = *reinterpret_cast<const int4*>(s_lim + kU * s + q0);
+          const int4 mb = *reinterpret_cast<const int4*>(s_lim + kU * s + q0 + 4);
+          const float lse[8] = {la.x, la.y, la.z, la.w, lb.x, lb.y, lb.z, lb.w};
+          const float di[8] = {da.x, da.y, da.z, da.w, db.x, db.y, db.z, db.w};
+          const int lim[8] = {ma.x, ma.y, ma.z, ma.w, mb.x, mb.y, mb.z, mb.w};
+          float pv[8], dsv[8];
+#pragma unroll
+          for (int j = 0; j < 8; j += 2) {
+            const int cc = 8 * c8 + j;
+            float x0, x1;
+            fma2v(x0, x1, sv[cc], sv[cc + 1], sl2, sl2, -lse[j], -lse[j + 1]);
+            pv[j] = row < lim[j] ? fast_exp2(x0) : 0.f;
+            pv[j + 1] = row < lim[j + 1] ? fast_exp2(x1) : 0.f;
+            // dS = (dP - Di) * (P * scale)
+            submul2(dsv[j], dsv[j + 1], dpv[cc], dpv[cc + 1], di[j], di[j + 1], pv[j] * scale, pv[j + 1] * scale);
+          }
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            wp[4 * c8 + j] = pack_bf16x2(pv[2 * j], pv[2 * j + 1]);
+            wd[4 * c8 + j] = pack_bf16x2(dsv[2 * j], dsv[2 * j + 1]);
+          }
+          // dS row `row`, unit query columns q0..q0+7: 16-byte chunk q0 / 8 of the row, 128B swizzle
+          const int c16 = q0 >> 3;
+          sts128(ds_row + ((c16 ^ (row & 7)) << 4), wd[4 * c8], wd[4 * c8 + 1], wd[4 * c8 + 2], wd[4 * c8 + 3]);
+        }
+        // P^T / dS^T (bf16 pairs) land on score columns this warp has already read
+        tmem_st16(tmem + lane_base + 128 * s + 16 + qc / 2, wp);
+        tmem_st16(tmem + lane_base + 128 * s + 80 + qc / 2, wd);
+      }
+      tmem_wait_st();
+      asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // dS visible to the tensor core
+      tc_fence_before();
+      mbar_arrive_one(&bar[kUBarP + s]);
+      if (u >= 1) readback_reduce(u - 1);
+    }
+    if (n_units > 0) readback_reduce(n_units - 1);
+    if (issuer) bulk_wait_all();  // every dQ reduction of this CTA has landed
+    // dV (warp half 0) and dK (half 1) of this key tile: key row `row`
+    const bool oka = __all_sync(0xffffffffu, wait_or_abort(&bar[kUBarAcc], 0, dead, p.err));
+    tc_fence_after();
+    if (oka) {
+      const int key = kt * kT + row;
+      __nv_bfloat16* outr = hf ? p.dk + (int64_t)b * p.dk_sb + (int64_t)hk * p.dk_sh + (int64_t)key * p.dk_ss
+                               : p.dv + (int64_t)b * p.dv_sb + (int64_t)hk * p.dv_sh + (int64_t)key * p.dv_ss;
+      const uint32_t col = hf ? 384u : 256u;
+#pragma unroll 1
+      for (int c4 = 0; c4 < 4; ++c4) {
+        float t[32];
+        tmem_ld32(tmem + lane_base + col + c4 * 32, t);
+        tmem_wait_ld();
+        if (n_units == 0) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) t[j] = 0.f;
+        }
+#pragma unroll
+        for (int v8 = 0; v8 < 4; ++v8) {
+          uint4 pk;
+          pk.x = pack_bf16x2(t[v8 * 8 + 0], t[v8 * 8 + 1]);
+          pk.y = pack_bf16x2(t[v8 * 8 + 2], t[v8 * 8 + 3]);
+          pk.z = pack_bf16x2(t[v8 * 8 + 4], t[v8 * 8 + 5]);
+          pk.w = pack_bf16x2(t[v8 * 8 + 6], t[v8 * 8 + 7]);
+          *reinterpret_cast<uint4*>(outr + c4 * 32 + v8 * 8) = pk;
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(kTmemCols));
+  }
+}
+
 // Di = rowsum(dO * O) in fp32: one warp per row.
 __global__ void rowdot_kernel(const __nv_bfloat16* __restrict__ o, int64_t o_sb, int64_t o_sh, int64_t o_ss,
                               const __nv_bfloat16* __restrict__ dout, int64_t d_sb, int64_t d_sh, int64_t d_ss,
@@ -457,10 +785,11 @@ __global__ void dq_store_kernel(const float* __restrict__ acc, __nv_bfloat16* dq
   *reinterpret_cast<uint4*>(dq + b * sb + h * sh + q * ss + d0) = pk;
 }
 
-int make_map(CUtensorMap* m, const void* base, int B, int heads, int S, int D, const int64_t* strides) {
+int make_map(CUtensorMap* m, const void* base, int B, int heads, int S, int D, const int64_t* strides,
+             int box_rows) {
   const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)S, (cuuint64_t)heads, (cuuint64_t)B};
   const cuuint64_t gstr[3] = {(cuuint64_t)strides[2] * 2, (cuuint64_t)strides[1] * 2, (cuuint64_t)strides[0] * 2};
-  const cuuint32_t box[4] = {64, (cuuint32_t)kT, 1, 1};
+  const cuuint32_t box[4] = {64, (cuuint32_t)box_rows, 1, 1};
   return tc::encode_tiled_4d(m, base, dims, gstr, box);
 }
 
@@ -515,14 +844,16 @@ extern "C" int abkv_prefill_masked_backward(
 
   BwdParams prm;
   std::memset(&prm, 0, sizeof(prm));
-  int st = make_map(&prm.tm_q, q, B, H, S, head_dim, q_strides);
-  if (st == ABKV_OK) st = make_map(&prm.tm_do, dout, B, H, S, head_dim, dout_strides);
-  if (st == ABKV_OK) st = make_map(&prm.tm_k, k, B, Hkv, S, head_dim, k_strides);
-  if (st == ABKV_OK) st = make_map(&prm.tm_v, v, B, Hkv, S, head_dim, v_strides);
+  // head_dim 128 runs the 64-query-unit kernel: Q, dO and dQ move in 64-row boxes
+  const int qrows = head_dim == 128 ? kU : kT;
+  int st = make_map(&prm.tm_q, q, B, H, S, head_dim, q_strides, qrows);
+  if (st == ABKV_OK) st = make_map(&prm.tm_do, dout, B, H, S, head_dim, dout_strides, qrows);
+  if (st == ABKV_OK) st = make_map(&prm.tm_k, k, B, Hkv, S, head_dim, k_strides, kT);
+  if (st == ABKV_OK) st = make_map(&prm.tm_v, v, B, Hkv, S, head_dim, v_strides, kT);
   if (st == ABKV_OK) {
     const cuuint64_t dims[2] = {(cuuint64_t)head_dim, (cuuint64_t)rows};
     const cuuint64_t gstr[1] = {(cuuint64_t)head_dim * 4};
-    const cuuint32_t box[2] = {32, (cuuint32_t)kT};
+    const cuuint32_t box[2] = {32, (cuuint32_t)qrows};
     st = tc::encode_tiled(&prm.tm_dq, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, dq_acc, dims, gstr, box,
                           CU_TENSOR_MAP_SWIZZLE_128B);
   }
@@ -566,8 +897,8 @@ extern "C" int abkv_prefill_masked_backward(
         static_cast<const __nv_bfloat16*>(dout), dout_strides[0], dout_strides[1], dout_strides[2], di, B, H, S,
         head_dim);
   }
-  auto kernel = head_dim == 64 ? prefill_bwd_kernel<64> : prefill_bwd_kernel<128>;
-  const int smem = head_dim == 64 ? Layout<64>::kSmem : Layout<128>::kSmem;
+  auto kernel = head_dim == 64 ? prefill_bwd_kernel<64> : prefill_bwd_unit_kernel;
+  const int smem = head_dim == 64 ? Layout<64>::kSmem : LayoutU::kSmem;
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return ABKV_ERR_CUDA;
   kernel<<<dim3(prm.n_tiles, Hkv, B), kThreads, smem, s>>>(prm);
