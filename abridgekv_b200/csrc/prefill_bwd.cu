@@ -561,14 +561,13 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_bwd_unit_kernel(const __g
         umma_commit(&bar[kUBarS + s]);
         return true;
       };
-      // gradients of unit u once its P^T / dS^T are in TMEM and dS in shared memory
-      auto finish = [&](int u) -> bool {
+      // dV / dK of unit u once its P^T / dS^T are in TMEM: the last reads of Q / dO slot u % 2
+      auto grad_kv = [&](int u) -> bool {
         const int s = u & 1, i = u >> 1;
         if (!wait_or_abort(&bar[kUBarP + s], (uint32_t)(i & 1), dead, p.err)) return false;
         tc_fence_after();
         const uint64_t ddo_mn = desc_mnmajor_sw128(smem_u32(smem + LY::kOffDO + s * LY::kSlot), LY::kSlot / 2);
         const uint64_t dq_mn = desc_mnmajor_sw128(smem_u32(smem + LY::kOffQ + s * LY::kSlot), LY::kSlot / 2);
-        const uint64_t dds_mn = desc_mnmajor_sw128(smem_u32(smem + LY::kOffDS + s * (kT * 128)), kT * 128);
 #pragma unroll
         for (int kk = 0; kk < kU / 16; ++kk)
           umma_tmem_a(tmem + 256, tmem + 128 * s + 16 + kk * 8, desc_advance(ddo_mn, kk * 2048),
@@ -578,19 +577,26 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_bwd_unit_kernel(const __g
           umma_tmem_a(tmem + 384, tmem + 128 * s + 80 + kk * 8, desc_advance(dq_mn, kk * 2048),
                       kIdescAccU, (u > 0 || kk > 0) ? 1u : 0u);
         umma_commit(&bar[kUBarQDE + s]);  // Q / dO slot s may be refilled once these ran
-        // dQ^T over the 128 keys in steps of 16 (its columns overlap P^T, which dV read first:
-        // one thread's MMAs run in issue order)
+        return true;
+      };
+      // dQ^T of unit u over the 128 keys in steps of 16 (its columns overlap P^T, which dV read
+      // first: one thread's MMAs run in issue order)
+      auto grad_q = [&](int u) {
+        const int s = u & 1;
+        const uint64_t dds_mn = desc_mnmajor_sw128(smem_u32(smem + LY::kOffDS + s * (kT * 128)), kT * 128);
 #pragma unroll
         for (int kk = 0; kk < kT / 16; ++kk)
           umma(tmem + 128 * s, desc_advance(dk_mn, kk * 2048), desc_advance(dds_mn, kk * 2048), kIdescDQ,
                kk > 0 ? 1u : 0u);
         umma_commit(&bar[kUBarDQ + s]);
-        return true;
       };
+      // order per unit: dV / dK(u) (frees the Q / dO slot for unit u + 2's loads as early as
+      // possible), the scores of unit u + 1, then dQ^T(u)
       if (n_units > 0 && !dead) issue_s(0);
       for (int u = 0; u < n_units && !dead; ++u) {
+        if (!grad_kv(u)) break;
         if (u + 1 < n_units && !issue_s(u + 1)) break;
-        if (!finish(u)) break;
+        grad_q(u);
       }
       umma_commit(&bar[kUBarAcc]);
     }
@@ -636,19 +642,32 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_bwd_unit_kernel(const __g
         bulk_commit();
       }
     };
+    // lse (log2 domain), Di and the visible-key prefix of a unit's 64 query rows: the threads
+    // of warp half 0 with row < 64 fetch unit u + 1's values while unit u is computed and store
+    // them at the start of unit u + 1, so the global loads' latency stays off the unit's path
+    const bool stager = hf == 0 && row < kU;
+    float n_lse = 0.f, n_di = 0.f;
+    int n_lim = 0;
+    auto fetch_rows = [&](int u) {
+      const int e = s_list[u >> 1];
+      const int qt = e >> 8, h = hk * G + (e & 0xFF);
+      const int q = qt * kT + kU * (u & 1) + row;
+      const int64_t rr = ((int64_t)b * p.H + h) * p.S + q;
+      const int qb = q / p.per, qw = q - qb * p.per;
+      n_lse = __ldg(p.lse + rr);
+      n_di = __ldg(p.di + rr);
+      n_lim = tile_limit_fast(p, p.quota[h], q, qb, qw, kb, kw0, kt * kT, pl);
+    };
+    if (stager && n_units > 0) fetch_rows(0);
     for (int u = 0; u < n_units; ++u) {
       const int s = u & 1, i = u >> 1;
-      const int e = s_list[i];
-      const int qt = e >> 8, h = hk * G + (e & 0xFF);
-      if (hf == 0 && row < kU) {  // lse (log2 domain), Di and the visible-key prefix of the unit's rows
-        const int q = qt * kT + kU * s + row;
-        const int64_t rr = ((int64_t)b * p.H + h) * p.S + q;
-        const int qb = q / p.per, qw = q - qb * p.per;
-        s_lse2[kU * s + row] = __ldg(p.lse + rr) * 1.4426950408889634f;
-        s_di[kU * s + row] = __ldg(p.di + rr);
-        s_lim[kU * s + row] = tile_limit_fast(p, p.quota[h], q, qb, qw, kb, kw0, kt * kT, pl);
+      if (stager) {
+        s_lse2[kU * s + row] = n_lse * 1.4426950408889634f;
+        s_di[kU * s + row] = n_di;
+        s_lim[kU * s + row] = n_lim;
       }
       softmax_bar();
+      if (stager && u + 1 < n_units) fetch_rows(u + 1);
       const bool ok = __all_sync(0xffffffffu, wait_or_abort(&bar[kUBarS + s], (uint32_t)(i & 1), dead, p.err));
       if (!ok) dead = true;
       tc_fence_after();
