@@ -32,7 +32,10 @@
 //               dQ), then add dQ into the fp32 buffer by TMA tensor reductions
 //               from a staging buffer.  At the end they write dV (first half)
 //               and dK (second half).
-// The phases of one pair run one after the other (one S^T / dP^T buffer).
+// The phases of one pair run one after the other (one S^T / dP^T buffer).  This
+// pair kernel serves head_dim 64; head_dim 128 runs prefill_bwd_unit_kernel
+// further down, which cuts each pair into two 64-query units so that two units
+// are in flight in TMEM at once.
 // Every mbarrier wait is bounded and records ABKV_DEVERR_TIMEOUT on expiry.
 #include <cstring>
 
@@ -426,7 +429,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_bwd_kernel(const __grid_c
 //   dV  += P^T dO_u  -> [256, 384)      dK += dS^T Q_u -> [384, 512)
 //   dQ_u^T = K^T dS_u^T (M = 128 dims, N = 64 queries; both operands MN-major in
 //            shared memory) -> [128 s, 128 s + 64), over the consumed S^T / P^T
-// Q / dO of a unit sit in a two-slot ring ([64 rows][128 dims] each); the
+// Q / dO of a unit sit in a two-slot ring ([64 rows][128 dims] each); the MMA
+// thread issues dV / dK(u), the scores of u + 1, then dQ^T(u), so the slot of
+// unit u is released (and unit u + 2's loads start) as early as possible.  The
 // threads read dQ_u^T back (lane = dim), stage it as [64 query rows][128 dims]
 // fp32 and add it to the accumulator with four TMA tensor reductions.
 // ---------------------------------------------------------------------------
