@@ -38,6 +38,7 @@
 // are in flight in TMEM at once.
 // Every mbarrier wait is bounded and records ABKV_DEVERR_TIMEOUT on expiry.
 #include <cstring>
+#include <type_traits>
 
 #include "prefill_mask.cuh"
 #include "tcgen05.cuh"
@@ -449,7 +450,7 @@ struct LayoutU {
   static constexpr int kOffDS = kOffDO + 2 * kSlot;  // dS: atom column s = [128 keys][64 queries] of slot s
   static constexpr int kOffStage = kOffDS + kT * kT * 2;  // dQ staging: 4 boxes [64 rows][32 f32]
   static constexpr int kOffRow = kOffStage + kU * 128 * 4;  // lse2, di, lim: [2 slots][64] each
-  static constexpr int kOffBar = kOffRow + 3 * 2 * kU * 4;
+  static constexpr int kOffBar = kOffRow + 3 * 2 * kU * 4 + 16;  // + [2 slots][2] "all keys visible" flags
   static constexpr int kOffList = kOffBar + 256;
   static constexpr int kSmem = kOffList + 4 * kMaxPairs + 16 + 1024;
 };
@@ -469,6 +470,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_bwd_unit_kernel(const __g
   float* s_lse2 = reinterpret_cast<float*>(smem + LY::kOffRow);  // [2][64]
   float* s_di = s_lse2 + 2 * kU;                                   // [2][64]
   int32_t* s_lim = reinterpret_cast<int32_t*>(s_di + 2 * kU);      // [2][64]
+  int32_t* s_allvis = s_lim + 2 * kU;                               // [2][2]
   int32_t* s_list = reinterpret_cast<int32_t*>(smem + LY::kOffList);
   int32_t* s_n = s_list + kMaxPairs;
 
@@ -670,8 +672,12 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_bwd_unit_kernel(const __g
         s_lse2[kU * s + row] = n_lse * 1.4426950408889634f;
         s_di[kU * s + row] = n_di;
         s_lim[kU * s + row] = n_lim;
+        // the stagers are lane quarters 0 and 1 (rows 0..63), one warp each
+        const bool all = __all_sync(0xffffffffu, n_lim >= kT);
+        if (lane == 0) s_allvis[2 * s + quarter] = all;
       }
       softmax_bar();
+      const bool allvis = s_allvis[2 * s] && s_allvis[2 * s + 1];  // every key of the tile is visible
       if (stager && u + 1 < n_units) fetch_rows(u + 1);
       const bool ok = __all_sync(0xffffffffu, wait_or_abort(&bar[kUBarS + s], (uint32_t)(i & 1), dead, p.err));
       if (!ok) dead = true;
@@ -684,38 +690,54 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_bwd_unit_kernel(const __g
         tmem_wait_ld();
         uint32_t wp[16], wd[16];
         const uint32_t ds_row = smem_u32(smem + LY::kOffDS) + s * (kT * 128) + row * 128;
+        // dS is stored without the softmax scale (dS' = P (dP - Di)); dK's epilogue and the dQ
+        // conversion apply it.  kAll: no query of the unit has a masked key in this tile.
+        auto form = [&](auto all_c) {
+          constexpr bool kAll = decltype(all_c)::value;
 #pragma unroll
-        for (int c8 = 0; c8 < 4; ++c8) {
-          const int q0 = qc + 8 * c8;
-          const float4 la = *reinterpret_cast<const float4*>(s_lse2 + kU * s + q0);
-          const float4 lb = *reinterpret_cast<const float4*>(s_lse2 + kU * s + q0 + 4);
-          const float4 da = *reinterpret_cast<const float4*>(s_di + kU * s + q0);
-          const float4 db = *reinterpret_cast<const float4*>(s_di + kU * s + q0 + 4);
-          const int4 ma = *reinterpret_cast<const int4*>(s_lim + kU * s + q0);
-          const int4 mb = *reinterpret_cast<const int4*>(s_lim + kU * s + q0 + 4);
-          const float lse[8] = {la.x, la.y, la.z, la.w, lb.x, lb.y, lb.z, lb.w};
-          const float di[8] = {da.x, da.y, da.z, da.w, db.x, db.y, db.z, db.w};
-          const int lim[8] = {ma.x, ma.y, ma.z, ma.w, mb.x, mb.y, mb.z, mb.w};
-          float pv[8], dsv[8];
+          for (int c8 = 0; c8 < 4; ++c8) {
+            const int q0 = qc + 8 * c8;
+            const float4 la = *reinterpret_cast<const float4*>(s_lse2 + kU * s + q0);
+            const float4 lb = *reinterpret_cast<const float4*>(s_lse2 + kU * s + q0 + 4);
+            const float4 da = *reinterpret_cast<const float4*>(s_di + kU * s + q0);
+            const float4 db = *reinterpret_cast<const float4*>(s_di + kU * s + q0 + 4);
+            const float lse[8] = {la.x, la.y, la.z, la.w, lb.x, lb.y, lb.z, lb.w};
+            const float di[8] = {da.x, da.y, da.z, da.w, db.x, db.y, db.z, db.w};
+            int lim[8];
+            if constexpr (!kAll) {
+              const int4 ma = *reinterpret_cast<const int4*>(s_lim + kU * s + q0);
+              const int4 mb = *reinterpret_cast<const int4*>(s_lim + kU * s + q0 + 4);
+              lim[0] = ma.x; lim[1] = ma.y; lim[2] = ma.z; lim[3] = ma.w;
+              lim[4] = mb.x; lim[5] = mb.y; lim[6] = mb.z; lim[7] = mb.w;
+            }
+            float pv[8], dsv[8];
 #pragma unroll
-          for (int j = 0; j < 8; j += 2) {
-            const int cc = 8 * c8 + j;
-            float x0, x1;
-            fma2v(x0, x1, sv[cc], sv[cc + 1], sl2, sl2, -lse[j], -lse[j + 1]);
-            pv[j] = row < lim[j] ? fast_exp2(x0) : 0.f;
-            pv[j + 1] = row < lim[j + 1] ? fast_exp2(x1) : 0.f;
-            // dS = (dP - Di) * (P * scale)
-            submul2(dsv[j], dsv[j + 1], dpv[cc], dpv[cc + 1], di[j], di[j + 1], pv[j] * scale, pv[j + 1] * scale);
+            for (int j = 0; j < 8; j += 2) {
+              const int cc = 8 * c8 + j;
+              float x0, x1;
+              fma2v(x0, x1, sv[cc], sv[cc + 1], sl2, sl2, -lse[j], -lse[j + 1]);
+              pv[j] = fast_exp2(x0);
+              pv[j + 1] = fast_exp2(x1);
+              if constexpr (!kAll) {
+                pv[j] = row < lim[j] ? pv[j] : 0.f;
+                pv[j + 1] = row < lim[j + 1] ? pv[j + 1] : 0.f;
+              }
+              submul2(dsv[j], dsv[j + 1], dpv[cc], dpv[cc + 1], di[j], di[j + 1], pv[j], pv[j + 1]);
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              wp[4 * c8 + j] = pack_bf16x2(pv[2 * j], pv[2 * j + 1]);
+              wd[4 * c8 + j] = pack_bf16x2(dsv[2 * j], dsv[2 * j + 1]);
+            }
+            // dS row `row`, unit query columns q0..q0+7: 16-byte chunk q0 / 8 of the row, 128B swizzle
+            const int c16 = q0 >> 3;
+            sts128(ds_row + ((c16 ^ (row & 7)) << 4), wd[4 * c8], wd[4 * c8 + 1], wd[4 * c8 + 2], wd[4 * c8 + 3]);
           }
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            wp[4 * c8 + j] = pack_bf16x2(pv[2 * j], pv[2 * j + 1]);
-            wd[4 * c8 + j] = pack_bf16x2(dsv[2 * j], dsv[2 * j + 1]);
-          }
-          // dS row `row`, unit query columns q0..q0+7: 16-byte chunk q0 / 8 of the row, 128B swizzle
-          const int c16 = q0 >> 3;
-          sts128(ds_row + ((c16 ^ (row & 7)) << 4), wd[4 * c8], wd[4 * c8 + 1], wd[4 * c8 + 2], wd[4 * c8 + 3]);
-        }
+        };
+        if (allvis)
+          form(std::true_type{});
+        else
+          form(std::false_type{});
         // P^T / dS^T (bf16 pairs) land on score columns this warp has already read
         tmem_st16(tmem + lane_base + 128 * s + 16 + qc / 2, wp);
         tmem_st16(tmem + lane_base + 128 * s + 80 + qc / 2, wd);
@@ -736,15 +758,14 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_bwd_unit_kernel(const __g
       __nv_bfloat16* outr = hf ? p.dk + (int64_t)b * p.dk_sb + (int64_t)hk * p.dk_sh + (int64_t)key * p.dk_ss
                                : p.dv + (int64_t)b * p.dv_sb + (int64_t)hk * p.dv_sh + (int64_t)key * p.dv_ss;
       const uint32_t col = hf ? 384u : 256u;
+      const float gs = hf ? p.scale : 1.f;  // dK carries the softmax scale (dS is stored unscaled)
 #pragma unroll 1
       for (int c4 = 0; c4 < 4; ++c4) {
         float t[32];
         tmem_ld32(tmem + lane_base + col + c4 * 32, t);
         tmem_wait_ld();
-        if (n_units == 0) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) t[j] = 0.f;
-        }
+        for (int j = 0; j < 32; ++j) t[j] = n_units == 0 ? 0.f : t[j] * gs;
 #pragma unroll
         for (int v8 = 0; v8 < 4; ++v8) {
           uint4 pk;
@@ -788,9 +809,10 @@ __global__ void rowdot_kernel(const __nv_bfloat16* __restrict__ o, int64_t o_sb,
   if (lane == 0) di[r] = acc;
 }
 
-// dq (strided bf16) = dq_acc (contiguous fp32), 8 dims per thread.
+// dq (strided bf16) = scale x dq_acc (contiguous fp32), 8 dims per thread; scale is the softmax
+// scale when the accumulator holds unscaled dS K (head_dim 128), else 1.
 __global__ void dq_store_kernel(const float* __restrict__ acc, __nv_bfloat16* dq, int64_t sb, int64_t sh, int64_t ss,
-                                int B, int H, int S, int D) {
+                                int B, int H, int S, int D, float scale) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t per_row = D / 8;
   if (i >= (int64_t)B * H * S * per_row) return;
@@ -802,10 +824,10 @@ __global__ void dq_store_kernel(const float* __restrict__ acc, __nv_bfloat16* dq
   const float4 x = *reinterpret_cast<const float4*>(acc + r * D + d0);
   const float4 y = *reinterpret_cast<const float4*>(acc + r * D + d0 + 4);
   uint4 pk;
-  pk.x = pack_bf16x2(x.x, x.y);
-  pk.y = pack_bf16x2(x.z, x.w);
-  pk.z = pack_bf16x2(y.x, y.y);
-  pk.w = pack_bf16x2(y.z, y.w);
+  pk.x = pack_bf16x2(x.x * scale, x.y * scale);
+  pk.y = pack_bf16x2(x.z * scale, x.w * scale);
+  pk.z = pack_bf16x2(y.x * scale, y.y * scale);
+  pk.w = pack_bf16x2(y.z * scale, y.w * scale);
   *reinterpret_cast<uint4*>(dq + b * sb + h * sh + q * ss + d0) = pk;
 }
 
@@ -930,7 +952,8 @@ extern "C" int abkv_prefill_masked_backward(
     const int64_t n = (int64_t)rows * (head_dim / 8);
     dq_store_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(dq_acc, static_cast<__nv_bfloat16*>(dq),
                                                                   dq_strides[0], dq_strides[1], dq_strides[2], B, H,
-                                                                  S, head_dim);
+                                                                  S, head_dim,
+                                                                  head_dim == 128 ? scale : 1.f);
   }
   if (cudaGetLastError() != cudaSuccess) return ABKV_ERR_CUDA;
   return ABKV_OK;
