@@ -436,7 +436,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_bwd_kernel(const __grid_c
 // threads read dQ_u^T back (lane = dim), stage it as [64 query rows][128 dims]
 // fp32 and add it to the accumulator with four TMA tensor reductions.
 // ---------------------------------------------------------------------------
-constexpr int kU = 64;  // queries per unit
+constexpr int kU = 64;      // queries per unit
+constexpr int kQSlots = 3;  // Q / dO ring depth
 constexpr uint32_t kIdescU = idesc_bf16_m128(kU, false);  // S^T, dP^T of a unit: N = 64, both K-major
 constexpr uint32_t kIdescAccU = idesc_bf16_m128(128, true);  // dV, dK: N = 128 dims, B MN-major
 
@@ -445,10 +446,10 @@ struct LayoutU {
   static constexpr int kSlot = kU * 128 * 2;    // Q or dO of a unit: 2 atoms of [64 rows][128 B]
   static constexpr int kOffK = 0;
   static constexpr int kOffV = kOffK + kKV;
-  static constexpr int kOffQ = kOffV + kKV;          // Q slots 0, 1
-  static constexpr int kOffDO = kOffQ + 2 * kSlot;   // dO slots 0, 1
-  static constexpr int kOffDS = kOffDO + 2 * kSlot;  // dS: atom column s = [128 keys][64 queries] of slot s
-  static constexpr int kOffStage = kOffDS + kT * kT * 2;  // dQ staging: 4 boxes [64 rows][32 f32]
+  static constexpr int kOffQ = kOffV + kKV;                // Q slots
+  static constexpr int kOffDO = kOffQ + kQSlots * kSlot;   // dO slots
+  static constexpr int kOffDS = kOffDO + kQSlots * kSlot;  // dS of the current unit: [128 keys][64 queries]
+  static constexpr int kOffStage = kOffDS + kT * kU * 2;   // dQ staging: 4 boxes [64 rows][32 f32]
   static constexpr int kOffRow = kOffStage + kU * 128 * 4;  // lse2, di, lim: [2 slots][64] each
   static constexpr int kOffBar = kOffRow + 3 * 2 * kU * 4 + 16;  // + [2 slots][2] "all keys visible" flags
   static constexpr int kOffList = kOffBar + 256;
@@ -456,9 +457,10 @@ struct LayoutU {
 };
 static_assert(LayoutU::kSmem <= 227 * 1024, "shared memory of the 64-query-unit backward");
 
-// barriers of the unit kernel: [2] = one per slot
-constexpr int kUBarKV = 0, kUBarQD = 1, kUBarQDE = 3, kUBarS = 5, kUBarP = 7, kUBarDQ = 9, kUBarFree = 11,
-              kUBarAcc = 13, kUBarTmem = 14;
+// barriers of the unit kernel: QD / QDE one per Q / dO slot; S / P / DQ / Free one per TMEM buffer
+constexpr int kUBarKV = 0, kUBarQD = 1, kUBarQDE = kUBarQD + kQSlots, kUBarS = kUBarQDE + kQSlots,
+              kUBarP = kUBarS + 2, kUBarDQ = kUBarP + 2, kUBarFree = kUBarDQ + 2, kUBarAcc = kUBarFree + 2,
+              kUBarTmem = kUBarAcc + 1;
 static_assert((kUBarTmem + 1) * 8 <= 256, "barrier area");
 
 __global__ void __launch_bounds__(kThreads, 1) prefill_bwd_unit_kernel(const __grid_constant__ BwdParams p) {
@@ -525,17 +527,17 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_bwd_unit_kernel(const __g
         tma_load_4d(smem + LY::kOffV + a * (LY::kKV / 2), &p.tm_v, 64 * a, kt * kT, hk, b, &bar[kUBarKV]);
       }
       for (int u = 0; u < n_units; ++u) {
-        const int s = u & 1, i = u >> 1;
-        const int e = s_list[i];
-        const int qrow = (e >> 8) * kT + kU * s, h = hk * G + (e & 0xFF);
-        // slot s is free once the dV / dK MMAs of unit u - 2 ran (immediate for the first use)
-        if (!wait_or_abort(&bar[kUBarQDE + s], (uint32_t)((i & 1) ^ 1), dead, p.err)) break;
-        mbar_expect_tx(&bar[kUBarQD + s], 2 * LY::kSlot);
+        const int e = s_list[u >> 1];
+        const int qrow = (e >> 8) * kT + kU * (u & 1), h = hk * G + (e & 0xFF);
+        const int qs = u % kQSlots, use = u / kQSlots;
+        // slot qs is free once the dV / dK MMAs of unit u - 3 ran (immediate for the first use)
+        if (!wait_or_abort(&bar[kUBarQDE + qs], (uint32_t)((use & 1) ^ 1), dead, p.err)) break;
+        mbar_expect_tx(&bar[kUBarQD + qs], 2 * LY::kSlot);
         for (int a = 0; a < 2; ++a) {
-          tma_load_4d(smem + LY::kOffQ + s * LY::kSlot + a * (LY::kSlot / 2), &p.tm_q, 64 * a, qrow, h, b,
-                      &bar[kUBarQD + s]);
-          tma_load_4d(smem + LY::kOffDO + s * LY::kSlot + a * (LY::kSlot / 2), &p.tm_do, 64 * a, qrow, h, b,
-                      &bar[kUBarQD + s]);
+          tma_load_4d(smem + LY::kOffQ + qs * LY::kSlot + a * (LY::kSlot / 2), &p.tm_q, 64 * a, qrow, h, b,
+                      &bar[kUBarQD + qs]);
+          tma_load_4d(smem + LY::kOffDO + qs * LY::kSlot + a * (LY::kSlot / 2), &p.tm_do, 64 * a, qrow, h, b,
+                      &bar[kUBarQD + qs]);
         }
       }
     }
@@ -548,13 +550,13 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_bwd_unit_kernel(const __g
       wait_or_abort(&bar[kUBarKV], 0, dead, p.err);
       // scores of unit u into TMEM buffer u % 2
       auto issue_s = [&](int u) -> bool {
-        const int s = u & 1, i = u >> 1;
-        if (!wait_or_abort(&bar[kUBarQD + s], (uint32_t)(i & 1), dead, p.err)) return false;
+        const int s = u & 1, i = u >> 1, qs = u % kQSlots;
+        if (!wait_or_abort(&bar[kUBarQD + qs], (uint32_t)((u / kQSlots) & 1), dead, p.err)) return false;
         // the buffer held dQ^T of unit u - 2: the threads have read it back
         if (!wait_or_abort(&bar[kUBarFree + s], (uint32_t)((i & 1) ^ 1), dead, p.err)) return false;
         tc_fence_after();
-        const uint64_t dq_k = desc_kmajor_sw128(smem_u32(smem + LY::kOffQ + s * LY::kSlot));
-        const uint64_t ddo_k = desc_kmajor_sw128(smem_u32(smem + LY::kOffDO + s * LY::kSlot));
+        const uint64_t dq_k = desc_kmajor_sw128(smem_u32(smem + LY::kOffQ + qs * LY::kSlot));
+        const uint64_t ddo_k = desc_kmajor_sw128(smem_u32(smem + LY::kOffDO + qs * LY::kSlot));
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t oa = (kk >> 2) * (LY::kKV / 2) + (kk & 3) * 32, ob = (kk >> 2) * (LY::kSlot / 2) + (kk & 3) * 32;
@@ -568,13 +570,13 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_bwd_unit_kernel(const __g
         umma_commit(&bar[kUBarS + s]);
         return true;
       };
-      // dV / dK of unit u once its P^T / dS^T are in TMEM: the last reads of Q / dO slot u % 2
+      // dV / dK of unit u once its P^T / dS^T are in TMEM: the last reads of its Q / dO slot
       auto grad_kv = [&](int u) -> bool {
-        const int s = u & 1, i = u >> 1;
+        const int s = u & 1, i = u >> 1, qs = u % kQSlots;
         if (!wait_or_abort(&bar[kUBarP + s], (uint32_t)(i & 1), dead, p.err)) return false;
         tc_fence_after();
-        const uint64_t ddo_mn = desc_mnmajor_sw128(smem_u32(smem + LY::kOffDO + s * LY::kSlot), LY::kSlot / 2);
-        const uint64_t dq_mn = desc_mnmajor_sw128(smem_u32(smem + LY::kOffQ + s * LY::kSlot), LY::kSlot / 2);
+        const uint64_t ddo_mn = desc_mnmajor_sw128(smem_u32(smem + LY::kOffDO + qs * LY::kSlot), LY::kSlot / 2);
+        const uint64_t dq_mn = desc_mnmajor_sw128(smem_u32(smem + LY::kOffQ + qs * LY::kSlot), LY::kSlot / 2);
 #pragma unroll
         for (int kk = 0; kk < kU / 16; ++kk)
           umma_tmem_a(tmem + 256, tmem + 128 * s + 16 + kk * 8, desc_advance(ddo_mn, kk * 2048),
@@ -583,27 +585,28 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_bwd_unit_kernel(const __g
         for (int kk = 0; kk < kU / 16; ++kk)
           umma_tmem_a(tmem + 384, tmem + 128 * s + 80 + kk * 8, desc_advance(dq_mn, kk * 2048),
                       kIdescAccU, (u > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(&bar[kUBarQDE + s]);  // Q / dO slot s may be refilled once these ran
+        umma_commit(&bar[kUBarQDE + qs]);  // Q / dO slot qs may be refilled once these ran
         return true;
       };
       // dQ^T of unit u over the 128 keys in steps of 16 (its columns overlap P^T, which dV read
       // first: one thread's MMAs run in issue order)
       auto grad_q = [&](int u) {
         const int s = u & 1;
-        const uint64_t dds_mn = desc_mnmajor_sw128(smem_u32(smem + LY::kOffDS + s * (kT * 128)), kT * 128);
+        const uint64_t dds_mn = desc_mnmajor_sw128(smem_u32(smem + LY::kOffDS), kT * 128);
 #pragma unroll
         for (int kk = 0; kk < kT / 16; ++kk)
           umma(tmem + 128 * s, desc_advance(dk_mn, kk * 2048), desc_advance(dds_mn, kk * 2048), kIdescDQ,
                kk > 0 ? 1u : 0u);
         umma_commit(&bar[kUBarDQ + s]);
       };
-      // order per unit: dV / dK(u) (frees the Q / dO slot for unit u + 2's loads as early as
-      // possible), the scores of unit u + 1, then dQ^T(u)
-      if (n_units > 0 && !dead) issue_s(0);
-      for (int u = 0; u < n_units && !dead; ++u) {
-        if (!grad_kv(u)) break;
-        if (u + 1 < n_units && !issue_s(u + 1)) break;
-        grad_q(u);
+      // order: the scores of unit u as soon as the threads have read dQ^T(u - 2) out of its
+      // buffer (they do that before forming P of unit u - 1), then dV / dK and dQ^T of unit u - 1
+      for (int u = 0; u <= n_units && !dead; ++u) {
+        if (u < n_units && !issue_s(u)) break;
+        if (u > 0) {
+          if (!grad_kv(u - 1)) break;
+          grad_q(u - 1);
+        }
       }
       umma_commit(&bar[kUBarAcc]);
     }
@@ -617,18 +620,24 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_bwd_unit_kernel(const __g
     const float sl2 = p.scale_log2, scale = p.scale;
     const bool issuer = threadIdx.x == 64;
     const uint32_t stage = smem_u32(smem + LY::kOffStage);
-    auto readback_reduce = [&](int v) {
+    // dQ^T of unit v: read out of its TMEM buffer (lane = dim, query columns [32 hf, 32 hf + 32))
+    // before the next unit's P / dS, which frees the buffer for the scores of unit v + 2 early;
+    // staged and added to the accumulator after that P / dS.
+    float dqt[32];
+    auto fetch_dq = [&](int v) {
       const int s = v & 1, i = v >> 1;
-      const int e = s_list[i];
-      const int qt = e >> 8, h = hk * G + (e & 0xFF);
       const bool okq = __all_sync(0xffffffffu, wait_or_abort(&bar[kUBarDQ + s], (uint32_t)(i & 1), dead, p.err));
       if (!okq) dead = true;
       tc_fence_after();
-      float t[32];
-      tmem_ld32(tmem + lane_base + 128 * s + 32 * hf, t);
+      tmem_ld32(tmem + lane_base + 128 * s + 32 * hf, dqt);
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive_one(&bar[kUBarFree + s]);
+    };
+    auto reduce_dq = [&](int v) {
+      const int s = v & 1, i = v >> 1;
+      const int e = s_list[i];
+      const int qt = e >> 8, h = hk * G + (e & 0xFF);
       if (issuer) bulk_wait_read();  // the previous unit's reductions have read the staging buffer
       softmax_bar();
       // dim `row` of query rows 32 hf .. 32 hf + 31: box `quarter` ([64 rows][32 f32], 128B swizzle)
@@ -637,7 +646,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_bwd_unit_kernel(const __g
       for (int j = 0; j < 32; ++j) {
         const int q = 32 * hf + j;
         asm volatile("st.shared.b32 [%0], %1;\n" ::"r"(box + q * 128 + (((lane >> 2) ^ (q & 7)) << 4)),
-                     "r"(__float_as_uint(t[j]))
+                     "r"(__float_as_uint(dqt[j]))
                      : "memory");
       }
       asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
@@ -681,6 +690,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_bwd_unit_kernel(const __g
       if (stager && u + 1 < n_units) fetch_rows(u + 1);
       const bool ok = __all_sync(0xffffffffu, wait_or_abort(&bar[kUBarS + s], (uint32_t)(i & 1), dead, p.err));
       if (!ok) dead = true;
+      // dQ^T(u - 1) out of TMEM; its MMA also finished reading the dS buffer this unit rewrites
+      if (u >= 1) fetch_dq(u - 1);
       tc_fence_after();
       {
         const int qc = 32 * hf;
@@ -689,7 +700,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_bwd_unit_kernel(const __g
         tmem_ld32(tmem + lane_base + 128 * s + 64 + qc, dpv);
         tmem_wait_ld();
         uint32_t wp[16], wd[16];
-        const uint32_t ds_row = smem_u32(smem + LY::kOffDS) + s * (kT * 128) + row * 128;
+        const uint32_t ds_row = smem_u32(smem + LY::kOffDS) + row * 128;
         // dS is stored without the softmax scale (dS' = P (dP - Di)); dK's epilogue and the dQ
         // conversion apply it.  kAll: no query of the unit has a masked key in this tile.
         auto form = [&](auto all_c) {
@@ -746,9 +757,12 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_bwd_unit_kernel(const __g
       asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // dS visible to the tensor core
       tc_fence_before();
       mbar_arrive_one(&bar[kUBarP + s]);
-      if (u >= 1) readback_reduce(u - 1);
+      if (u >= 1) reduce_dq(u - 1);
     }
-    if (n_units > 0) readback_reduce(n_units - 1);
+    if (n_units > 0) {
+      fetch_dq(n_units - 1);
+      reduce_dq(n_units - 1);
+    }
     if (issuer) bulk_wait_all();  // every dQ reduction of this CTA has landed
     // dV (warp half 0) and dK (half 1) of this key tile: key row `row`
     const bool oka = __all_sync(0xffffffffu, wait_or_abort(&bar[kUBarAcc], 0, dead, p.err));
