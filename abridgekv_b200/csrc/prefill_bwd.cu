@@ -426,15 +426,19 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_bwd_kernel(const __grid_c
 //   S^T  = K Q_u^T   -> TMEM [128 s, 128 s + 64)        (N = 64 queries)
 //   dP^T = V dO_u^T  -> TMEM [128 s + 64, 128 s + 128)
 //   (threads: P^T bf16 -> [128 s + 16, 128 s + 48), dS^T -> [128 s + 80, 128 s + 112),
-//    dS -> shared memory, atom column s of the dS buffer)
+//    dS -> the shared-memory dS buffer; dS is kept without the softmax scale,
+//    which dK's epilogue and the dQ conversion apply)
 //   dV  += P^T dO_u  -> [256, 384)      dK += dS^T Q_u -> [384, 512)
 //   dQ_u^T = K^T dS_u^T (M = 128 dims, N = 64 queries; both operands MN-major in
 //            shared memory) -> [128 s, 128 s + 64), over the consumed S^T / P^T
-// Q / dO of a unit sit in a two-slot ring ([64 rows][128 dims] each); the MMA
-// thread issues dV / dK(u), the scores of u + 1, then dQ^T(u), so the slot of
-// unit u is released (and unit u + 2's loads start) as early as possible.  The
-// threads read dQ_u^T back (lane = dim), stage it as [64 query rows][128 dims]
-// fp32 and add it to the accumulator with four TMA tensor reductions.
+// Per unit the threads wait for S(u), read dQ^T(u-1) out of TMEM (lane = dim,
+// kept in registers), form P / dS of u, then stage dQ^T(u-1) as [64 query
+// rows][128 dims] fp32 and add it to the accumulator with four TMA tensor
+// reductions.  Reading dQ^T(u-1) first frees its buffer, so the MMA thread
+// issues the scores of u + 1 while P(u) is formed, then dV / dK(u) and
+// dQ^T(u); and dQ^T(u-1) has read dS before P(u) rewrites it (one dS buffer).
+// Q / dO of a unit sit in a three-slot ring ([64 rows][128 dims] each), a slot
+// refilled once the dV / dK MMAs of its unit ran.
 // ---------------------------------------------------------------------------
 constexpr int kU = 64;      // queries per unit
 constexpr int kQSlots = 3;  // Q / dO ring depth
