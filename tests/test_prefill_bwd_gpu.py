@@ -100,3 +100,32 @@ def test_forward_and_backward_from_a_fresh_thread():
     assert "error" not in box, box.get("error")
     for got, d in zip(box["grads"], direct):
         np.testing.assert_allclose(got.float().cpu().numpy(), d, atol=2e-3 * float(np.abs(d).max()))
+
+
+def test_gradients_are_linear_in_dout():
+    """A size-independent property at a larger shape than the goldens (B = 2, 4 blocks of 512 + 256
+    rows, 8 / 2 heads, head_dim 128, mixed quotas, a prompt on one sequence): doubling dO (exact in
+    bf16) doubles every gradient.  dK and dV accumulate in a fixed order, so they double bit for bit;
+    dQ is summed by unordered fp32 reductions, so it doubles to within fp32 rounding."""
+    B, H, Hkv, D, C, K, N = 2, 8, 2, 128, 512, 256, 4
+    S = N * (C + K)
+    g = torch.Generator(device="cuda").manual_seed(7)
+    mk = lambda h: torch.randn((B, S, h, D), device="cuda", generator=g, dtype=torch.bfloat16).transpose(1, 2)
+    q, k, v, dout = mk(H), mk(Hkv), mk(Hkv), mk(H)
+    quotas = [256, 128, 64, 192, 256, 32, 64, 128]
+    pl = torch.tensor([300, 0], dtype=torch.int32, device="cuda")
+    ws = Workspace()
+    out, lse = prefill.prefill_masked(q, k, v, C=C, K_layout=K, quota_per_head=quotas, prompt_len=pl,
+                                      return_lse=True, workspace=ws)
+    g1 = prefill.prefill_masked_backward(q, k, v, out, dout, lse, C=C, K_layout=K, quota_per_head=quotas,
+                                         prompt_len=pl, workspace=ws)
+    g2 = prefill.prefill_masked_backward(q, k, v, out, dout * 2, lse, C=C, K_layout=K, quota_per_head=quotas,
+                                         prompt_len=pl, workspace=ws)
+    torch.cuda.synchronize()
+    assert ws.read_error() == 0
+    dq1, dk1, dv1 = (t.float() for t in g1)
+    dq2, dk2, dv2 = (t.float() for t in g2)
+    assert torch.isfinite(dq1).all() and dk1.abs().max() > 0 and dv1.abs().max() > 0
+    assert torch.equal(dk2, 2 * dk1)
+    assert torch.equal(dv2, 2 * dv1)
+    assert ((dq2 - 2 * dq1).abs().max() <= 1e-2 * dq1.abs().max()).item()
