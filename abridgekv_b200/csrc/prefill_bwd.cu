@@ -81,7 +81,8 @@ constexpr int kBarKV = 0, kBarQD = 1, kBarQDE = 2, kBarS = 3, kBarP = 4, kBarDQ 
 
 struct alignas(64) BwdParams {
   CUtensorMap tm_q, tm_k, tm_v, tm_do;
-  CUtensorMap tm_dq;  // the fp32 dQ accumulator as [B*H*S rows][D], box [128 rows][32], 128B swizzle
+  CUtensorMap tm_dq;  // the fp32 dQ accumulator as [B*H*S rows][D], box [rows][32], 128B swizzle
+                      // (rows = 128 for the pair kernel, 64 for the unit kernel; Q / dO likewise)
   const float* lse;   // [B][H][S], natural log (the forward's)
   const float* di;    // [B][H][S], rowsum(dO * O)
   float* dq_acc;      // [B][H][S][D] fp32
