@@ -5,6 +5,7 @@
     python -m abridgekv_b200.benchmarks codestep   [--layers 36] [--steps 3]
     python -m abridgekv_b200.benchmarks packed     [--steps 20]
     python -m abridgekv_b200.benchmarks kvshard    [--kv-heads 1] [--seqs 256] [--chunk-tokens 0]
+    python -m abridgekv_b200.benchmarks codestep_compact [--steps 20]
 
 prefill    BASELINE config 4: B=16 sequences of 16 blocks x (512 content + 256 code rows)
            = 12,288 rows, Qwen3-4B attention (32 q / 8 kv heads, head_dim 128), per-layer
@@ -32,6 +33,12 @@ kvshard    one GPU's share of BASELINE config 5 under KV-head sharding: --kv-hea
            quotas over a 32K-token generation, one decode launch over all layers per step.
            --chunk-tokens 0 is the automatic split-KV chunk.  Algorithmic bytes = every kept
            key/value row of the shard read once + Q/O.
+codestep_compact
+           one layer of the code step at a block boundary (64 requests, 3-5K cache rows + K=256
+           code rows, 32 q / 8 kv heads, quota 128) followed by each request's finished-block
+           compaction (its first 128 code rows moved over the start of its last content block):
+           code step alone, code step + the separate executor (abkv_compact), and the fused
+           abkv_code_step_attention_compact, each from the host call to completion.
 """
 from __future__ import annotations
 
@@ -486,9 +493,78 @@ def bench_kvshard(args) -> dict:
                        "chunk_tokens": args.chunk_tokens or "auto"}}
 
 
+def bench_codestep_compact(args) -> dict:
+    from . import codestep, compaction
+    from .workspace import Workspace
+
+    g = torch.Generator().manual_seed(5)
+    R, K, C, Hq, Hkv, D, page, qk = 64, 256, 512, 32, 8, 128, 16, 128
+    quotas = [qk] * Hkv
+    lens = torch.randint(3000, 5000, (R,), generator=g) + K
+    pages = (lens + page - 1) // page
+    nb = int(pages.sum()) + 1
+    dev = torch.device("cuda")
+    kv = torch.randn((nb, 2, page, Hkv, D), device=dev, dtype=torch.bfloat16)
+    perm = torch.randperm(nb - 1, generator=g) + 1
+    bt = torch.zeros((R, int(pages.max())), dtype=torch.int32)
+    o = 0
+    for r in range(R):
+        bt[r, :pages[r]] = perm[o:o + pages[r]]
+        o += int(pages[r])
+    ops, off = [], [0]
+    for r in range(R):
+        L = int(lens[r])
+        for j in range(qk):
+            sr, dr = L - K + j, L - K - C + j
+            ops.append((int(bt[r, sr // page]), sr % page, int(bt[r, dr // page]), dr % page))
+        off.append(len(ops))
+    ops_arr = np.asarray(ops, dtype=np.int32)
+    btd, sl = bt.to(dev), lens.to(torch.int32).to(dev)
+    q = torch.randn((R * K, Hq, D), device=dev, dtype=torch.bfloat16)
+    qs = (torch.arange(R + 1) * K).to(torch.int32).to(dev)
+    out = torch.empty_like(q)
+    ws = Workspace()
+    kw = dict(quota_per_kv_head=quotas, k_max=K, workspace=ws, out=out)
+
+    def alone():
+        codestep.code_step_attention(q, kv, btd, sl, qs, **kw)
+
+    def separate():
+        codestep.code_step_attention(q, kv, btd, sl, qs, **kw)
+        compaction.execute_kv_copy_group(compaction.CopyOps(ops_arr), [kv], workspace=ws)
+
+    def fused():
+        codestep.code_step_attention_compact(q, kv, btd, sl, qs, ops=ops_arr, op_offsets=off, **kw)
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / args.steps
+
+    res = {name: [] for name in ("code_step", "code_step_then_executor", "fused")}
+    for _ in range(2):  # the copies are idempotent: every call moves the same rows
+        res["code_step"].append(round(timed(alone), 4))
+        res["code_step_then_executor"].append(round(timed(separate), 4))
+        res["fused"].append(round(timed(fused), 4))
+    if ws.read_error():
+        raise RuntimeError(f"device error flag {ws.read_error():#x}")
+    moved = len(ops) * 2 * Hkv * D * 2
+    return {"metric": "code step + finished-block compaction, one layer (ms per call)", "unit": "ms",
+            "ms": res, "rows_moved": len(ops), "bytes_moved": moved,
+            "config": {"requests": R, "K": K, "C": C, "heads": f"{Hq}/{Hkv}", "quota": qk, "steps": args.steps}}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("which", choices=["prefill", "prefill_bwd", "compaction", "codestep", "packed", "kvshard"])
+    ap.add_argument("which", choices=["prefill", "prefill_bwd", "compaction", "codestep", "packed", "kvshard",
+                                          "codestep_compact"])
     ap.add_argument("--layers", type=int, default=36)
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=2)
@@ -500,7 +576,7 @@ def main() -> None:
     ap.add_argument("--chunk-tokens", type=int, default=0, help="kvshard: split-KV chunk rows (0 = auto)")
     args = ap.parse_args()
     fn = {"prefill": bench_prefill, "prefill_bwd": bench_prefill_bwd, "compaction": bench_compaction,
-          "codestep": bench_codestep, "packed": bench_packed, "kvshard": bench_kvshard}[args.which]
+          "codestep": bench_codestep, "packed": bench_packed, "kvshard": bench_kvshard, "codestep_compact": bench_codestep_compact}[args.which]
     print(json.dumps(fn(args)), flush=True)
 
 

@@ -20,6 +20,7 @@ from __future__ import annotations
 import math
 from typing import Mapping, Sequence
 
+import numpy as np
 import torch
 
 from . import _lib
@@ -37,17 +38,10 @@ def _layout_of(kv: torch.Tensor, num_kv_heads: int) -> tuple[int, int, int]:
     raise ValueError(f"unrecognised paged KV layout {tuple(kv.shape)}")
 
 
-def code_step_attention(query: torch.Tensor, kv_cache: torch.Tensor, block_table: torch.Tensor,
-                        seq_lens: torch.Tensor, query_start_loc: torch.Tensor, *,
-                        quota_per_kv_head: Sequence[int], k_max: int, scale: float | None = None,
-                        excluded: torch.Tensor | None = None, num_requests: int | None = None,
-                        out: torch.Tensor | None = None, workspace: Workspace | None = None,
-                        stream: torch.cuda.Stream | None = None) -> torch.Tensor:
-    """query [T, Hq, D] bf16 (last dim contiguous); kv_cache paged bf16 (either layout);
-    block_table [R, max_pages] int32; seq_lens [R] int32 (each >= k_max); query_start_loc
-    [>= R] int32 (request r's code queries are rows query_start_loc[r] .. + k_max - 1);
-    quota_per_kv_head: this layer's quotas (each in [0, k_max]); excluded: optional [R, 2]
-    int32 hidden row ranges (start == end = none).  Writes and returns out [T, Hq, D]."""
+def _prepare(query, kv_cache, block_table, seq_lens, query_start_loc, quota_per_kv_head, scale, excluded,
+             num_requests, out):
+    """Checks the code-step arguments -> (leading arguments of the C call, out, R, num_blocks, page, T,
+    scale)."""
     for name, t in (("query", query), ("kv_cache", kv_cache)):
         if not isinstance(t, torch.Tensor) or not t.is_cuda or t.dtype != torch.bfloat16:
             raise TypeError(f"{name} must be a bf16 CUDA tensor (libabkv has no CPU path)")
@@ -81,15 +75,64 @@ def code_step_attention(query: torch.Tensor, kv_cache: torch.Tensor, block_table
     if tuple(out.shape) != (T, Hq, D) or out.dtype != torch.bfloat16 or out.stride(2) != 1:
         raise ValueError("out must be a bf16 [T, Hq, D] tensor with a contiguous last dimension")
     scale = 1.0 / math.sqrt(D) if scale is None else float(scale)
+    head = (query.data_ptr(), query.stride(0), query.stride(1), out.data_ptr(), out.stride(0), out.stride(1),
+            qs.data_ptr(), kv_cache.data_ptr(), layout, nb, page, bt.data_ptr(), bt.stride(0), sl.data_ptr(),
+            ex.data_ptr() if ex is not None else None, _lib.i32_array(quota_per_kv_head), R, Hq, Hkv, D)
+    return head, out, R, nb, page, T, scale
+
+
+def code_step_attention(query: torch.Tensor, kv_cache: torch.Tensor, block_table: torch.Tensor,
+                        seq_lens: torch.Tensor, query_start_loc: torch.Tensor, *,
+                        quota_per_kv_head: Sequence[int], k_max: int, scale: float | None = None,
+                        excluded: torch.Tensor | None = None, num_requests: int | None = None,
+                        out: torch.Tensor | None = None, workspace: Workspace | None = None,
+                        stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """query [T, Hq, D] bf16 (last dim contiguous); kv_cache paged bf16 (either layout);
+    block_table [R, max_pages] int32; seq_lens [R] int32 (each >= k_max); query_start_loc
+    [>= R] int32 (request r's code queries are rows query_start_loc[r] .. + k_max - 1);
+    quota_per_kv_head: this layer's quotas (each in [0, k_max]); excluded: optional [R, 2]
+    int32 hidden row ranges (start == end = none).  Writes and returns out [T, Hq, D]."""
+    head, out, R, nb, page, T, scale = _prepare(query, kv_cache, block_table, seq_lens, query_start_loc,
+                                                quota_per_kv_head, scale, excluded, num_requests, out)
+    dev = query.device
     ws = workspace or default_workspace(dev)
     s = torch.cuda.current_stream(dev) if stream is None else stream
     with torch.cuda.device(dev):
-        st = _lib.lib().abkv_code_step_attention(
-            query.data_ptr(), query.stride(0), query.stride(1), out.data_ptr(), out.stride(0), out.stride(1),
-            qs.data_ptr(), kv_cache.data_ptr(), layout, nb, page, bt.data_ptr(), bt.stride(0), sl.data_ptr(),
-            ex.data_ptr() if ex is not None else None, _lib.i32_array(quota_per_kv_head), R, Hq, Hkv, D,
-            int(k_max), T, scale, ws.ptr(), ws.nbytes, s.cuda_stream)
+        st = _lib.lib().abkv_code_step_attention(*head, int(k_max), T, scale, ws.ptr(), ws.nbytes, s.cuda_stream)
     _lib.check("abkv_code_step_attention", st)
+    return out
+
+
+def code_step_attention_compact(query: torch.Tensor, kv_cache: torch.Tensor, block_table: torch.Tensor,
+                                seq_lens: torch.Tensor, query_start_loc: torch.Tensor, *, ops,
+                                op_offsets: Sequence[int], quota_per_kv_head: Sequence[int], k_max: int,
+                                scale: float | None = None, excluded: torch.Tensor | None = None,
+                                num_requests: int | None = None, out: torch.Tensor | None = None,
+                                workspace: Workspace | None = None,
+                                stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """``code_step_attention`` followed, in the same launch, by the compaction of this layer's cache:
+    request r's (src_block, src_off, dst_block, dst_off) row copies ``ops[op_offsets[r] ..
+    op_offsets[r + 1])`` are applied once every CTA of request r has read the cache.  Same result as
+    ``code_step_attention`` then ``compaction.execute_kv_copy_group(ops, [kv_cache])``; a batch whose
+    destinations repeat or overlap its sources is rejected (use the separate executor for it)."""
+    head, out, R, nb, page, T, scale = _prepare(query, kv_cache, block_table, seq_lens, query_start_loc,
+                                                quota_per_kv_head, scale, excluded, num_requests, out)
+    arr = np.ascontiguousarray(getattr(ops, "array", ops), dtype=np.int32).reshape(-1, 4)
+    off = np.ascontiguousarray(op_offsets, dtype=np.int64)
+    if off.shape != (R + 1,):
+        raise ValueError(f"op_offsets must hold R + 1 = {R + 1} entries")
+    dev = query.device
+    lib = _lib.lib()
+    need = lib.abkv_code_step_compact_workspace_size(R, len(arr))
+    if need == 0:
+        raise ValueError("too many copy ops")
+    ws = (workspace or default_workspace(dev)).ensure(need)
+    s = torch.cuda.current_stream(dev) if stream is None else stream
+    with torch.cuda.device(dev):
+        st = lib.abkv_code_step_attention_compact(*head, int(k_max), T, scale, arr.ctypes.data_as(_lib.c_i32p),
+                                                  off.ctypes.data_as(_lib.c_i64p), len(arr), ws.ptr(), ws.nbytes,
+                                                  s.cuda_stream)
+    _lib.check("abkv_code_step_attention_compact", st)
     return out
 
 

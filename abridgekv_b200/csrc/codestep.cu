@@ -31,7 +31,9 @@
 // With all tiles full (no causal diagonal), the double-buffered S keeps the
 // tensor core busier here than the 128-key single-buffer tiling of prefill.cu.
 // Every mbarrier wait is bounded and records ABKV_DEVERR_TIMEOUT on expiry.
+#include <algorithm>
 #include <cstring>
+#include <vector>
 
 #include "tcgen05.cuh"
 
@@ -86,7 +88,54 @@ struct alignas(64) CodeStepParams {
   const int32_t* excl;  // optional [R][2]: rows [start, end) hidden from the code queries
   int64_t bt_stride, num_blocks;
   int page, Kc, T, fa_layout;
+  // optional compaction that follows the code step (abkv_code_step_attention_compact): request r's
+  // row copies cops[coff[r] .. coff[r + 1]) ([n][4] = src block, src offset, dst block, dst offset),
+  // applied to this layer's cache by the last CTA of the request to finish its reads
+  const int32_t* cops;
+  const int32_t* coff;
+  int32_t* ccount;  // [R] finished CTAs per request (zeroed by the host before the launch)
+  char* kv;
+  int64_t row_bytes;
+  int ctas_per_req;
 };
+
+// The last CTA of request blockIdx.z applies that request's copy ops.  Every CTA of the request
+// counts itself once all its reads of the cache are done: its TMA loads were consumed (waited on)
+// before its MMAs, and the barrier before this call orders every thread.  A CTA that gave up on a
+// wait does not count, so the request's ops are not applied and the error word says why.  The host
+// checked that no op writes a row any op reads and that destinations are unique, so the copies may
+// run in any order.
+__device__ __noinline__ void commit_request_ops(const CodeStepParams& p, bool dead) {
+  __shared__ int s_last;
+  const int any_dead = __syncthreads_or(dead ? 1 : 0);
+  if (threadIdx.x == 0) {
+    int last = 0;
+    if (!any_dead) {
+      __threadfence();
+      last = atomicAdd(p.ccount + blockIdx.z, 1) == p.ctas_per_req - 1;
+      if (last) __threadfence();
+    }
+    s_last = last;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  const int o0 = __ldcg(p.coff + blockIdx.z), o1 = __ldcg(p.coff + blockIdx.z + 1);
+  const int64_t vecs = p.row_bytes >> 4;  // 16-byte vectors per K or V row
+  const int64_t total = (int64_t)(o1 - o0) * 2 * vecs;
+  for (int64_t idx = threadIdx.x; idx < total; idx += blockDim.x) {
+    const int op = o0 + (int)(idx / (2 * vecs));
+    const int64_t rem = idx - (int64_t)(op - o0) * 2 * vecs;
+    const int half = (int)(rem / vecs);
+    const int64_t v = rem - half * vecs;
+    const int sb = __ldcg(p.cops + 4 * op), so = __ldcg(p.cops + 4 * op + 1);
+    const int db = __ldcg(p.cops + 4 * op + 2), dof = __ldcg(p.cops + 4 * op + 3);
+    const int64_t ps = p.fa_layout ? (half ? p.num_blocks + sb : sb) : 2 * (int64_t)sb + half;
+    const int64_t pd = p.fa_layout ? (half ? p.num_blocks + db : db) : 2 * (int64_t)db + half;
+    const uint4* src = reinterpret_cast<const uint4*>(p.kv + (ps * p.page + so) * p.row_bytes) + v;
+    uint4* dst = reinterpret_cast<uint4*>(p.kv + (pd * p.page + dof) * p.row_bytes) + v;
+    __stcg(dst, __ldcg(src));
+  }
+}
 
 // Softmax of one (head, key tile) for query row `row` (= TMEM lane):
 // reads S, updates the reference maximum / row sum, waits until the previous
@@ -467,12 +516,35 @@ __global__ void __launch_bounds__(kThreads, 1) codestep_kernel(const __grid_cons
   if (warp == 1) {
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(kTmemCols));
   }
+  if (p.cops) commit_request_ops(p, dead);
 }
 
 }  // namespace
 }  // namespace abkv
 
 using namespace abkv;
+
+namespace {
+// Copy ops of the compaction that follows the code step, already validated and uploaded.
+struct CommitArgs {
+  const int32_t* ops;  // device [n][4]
+  const int32_t* off;  // device [R + 1]
+  int32_t* count;      // device [R], zeroed
+};
+
+int code_step_launch(const void* q, int64_t q_row_stride, int64_t q_head_stride, void* out,
+                     int64_t out_row_stride, int64_t out_head_stride, const int32_t* q_start,
+                     const void* kv_cache, int kv_layout, int64_t num_blocks, int page_size,
+                     const int32_t* block_table, int64_t bt_stride, const int32_t* seq_lens,
+                     const int32_t* excluded, const int32_t* quota_per_kv_head, int R, int Hq,
+                     int Hkv, int head_dim, int K_code, int T, float scale, void* workspace,
+                     size_t workspace_bytes, void* stream, const CommitArgs* commit);
+
+constexpr size_t align256(size_t x) { return (x + 255) / 256 * 256; }
+size_t commit_workspace(int R, int64_t n_ops) {
+  return 256 + align256((size_t)R * 4) + align256((size_t)(R + 1) * 4) + align256((size_t)n_ops * 16);
+}
+}  // namespace
 
 extern "C" int abkv_code_step_attention(const void* q, int64_t q_row_stride, int64_t q_head_stride, void* out,
                                         int64_t out_row_stride, int64_t out_head_stride, const int32_t* q_start,
@@ -481,6 +553,80 @@ extern "C" int abkv_code_step_attention(const void* q, int64_t q_row_stride, int
                                         const int32_t* excluded, const int32_t* quota_per_kv_head, int R, int Hq,
                                         int Hkv, int head_dim, int K_code, int T, float scale, void* workspace,
                                         size_t workspace_bytes, void* stream) {
+  return code_step_launch(q, q_row_stride, q_head_stride, out, out_row_stride, out_head_stride, q_start, kv_cache,
+                          kv_layout, num_blocks, page_size, block_table, bt_stride, seq_lens, excluded,
+                          quota_per_kv_head, R, Hq, Hkv, head_dim, K_code, T, scale, workspace, workspace_bytes,
+                          stream, nullptr);
+}
+
+extern "C" size_t abkv_code_step_compact_workspace_size(int num_requests, int64_t n_ops) {
+  if (num_requests <= 0 || n_ops < 0 || n_ops > INT32_MAX / 4) return 0;
+  return commit_workspace(num_requests, n_ops);
+}
+
+extern "C" int abkv_code_step_attention_compact(
+    const void* q, int64_t q_row_stride, int64_t q_head_stride, void* out, int64_t out_row_stride,
+    int64_t out_head_stride, const int32_t* q_start, void* kv_cache, int kv_layout, int64_t num_blocks,
+    int page_size, const int32_t* block_table, int64_t bt_stride, const int32_t* seq_lens, const int32_t* excluded,
+    const int32_t* quota_per_kv_head, int R, int Hq, int Hkv, int head_dim, int K_code, int T, float scale,
+    const int32_t* ops, const int64_t* op_offsets, int64_t n_ops, void* workspace, size_t workspace_bytes,
+    void* stream) {
+  if (R <= 0 || !op_offsets || n_ops < 0 || n_ops > INT32_MAX / 4 || (n_ops > 0 && !ops) || num_blocks <= 0 ||
+      page_size <= 0)
+    return ABKV_ERR_INVALID_ARG;
+  if (op_offsets[0] != 0 || op_offsets[R] != n_ops) return ABKV_ERR_INVALID_ARG;
+  for (int r = 0; r < R; ++r)
+    if (op_offsets[r + 1] < op_offsets[r]) return ABKV_ERR_INVALID_ARG;
+  // every op in range; destinations unique and never a source, so the copies may run in any order
+  // (the same result as the executor's gather-all-then-scatter batch)
+  std::vector<int64_t> src((size_t)n_ops), dst((size_t)n_ops);
+  for (int64_t i = 0; i < n_ops; ++i) {
+    const int32_t sb = ops[4 * i], so = ops[4 * i + 1], db = ops[4 * i + 2], dof = ops[4 * i + 3];
+    if (sb < 0 || sb >= num_blocks || db < 0 || db >= num_blocks || so < 0 || so >= page_size || dof < 0 ||
+        dof >= page_size)
+      return ABKV_ERR_INVALID_ARG;
+    src[i] = (int64_t)sb * page_size + so;
+    dst[i] = (int64_t)db * page_size + dof;
+  }
+  std::sort(src.begin(), src.end());
+  std::sort(dst.begin(), dst.end());
+  if (std::adjacent_find(dst.begin(), dst.end()) != dst.end()) return ABKV_ERR_UNSUPPORTED;
+  for (size_t i = 0, j = 0; i < dst.size() && j < src.size();) {
+    if (dst[i] == src[j]) return ABKV_ERR_UNSUPPORTED;
+    if (dst[i] < src[j]) ++i; else ++j;
+  }
+  const size_t need = commit_workspace(R, n_ops);
+  if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255))
+    return ABKV_ERR_WORKSPACE;
+  char* ws = static_cast<char*>(workspace);
+  CommitArgs c;
+  c.count = reinterpret_cast<int32_t*>(ws + 256);
+  int32_t* d_off = reinterpret_cast<int32_t*>(ws + 256 + align256((size_t)R * 4));
+  int32_t* d_ops = reinterpret_cast<int32_t*>(ws + 256 + align256((size_t)R * 4) + align256((size_t)(R + 1) * 4));
+  c.off = d_off;
+  c.ops = d_ops;
+  std::vector<int32_t> off32((size_t)R + 1);
+  for (int r = 0; r <= R; ++r) off32[r] = (int32_t)op_offsets[r];
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  // pageable host sources: each copy is staged before the call returns
+  if (cudaMemcpyAsync(d_off, off32.data(), off32.size() * 4, cudaMemcpyHostToDevice, s) != cudaSuccess ||
+      (n_ops > 0 && cudaMemcpyAsync(d_ops, ops, (size_t)n_ops * 16, cudaMemcpyHostToDevice, s) != cudaSuccess) ||
+      cudaMemsetAsync(c.count, 0, (size_t)R * 4, s) != cudaSuccess)
+    return ABKV_ERR_CUDA;
+  return code_step_launch(q, q_row_stride, q_head_stride, out, out_row_stride, out_head_stride, q_start, kv_cache,
+                          kv_layout, num_blocks, page_size, block_table, bt_stride, seq_lens, excluded,
+                          quota_per_kv_head, R, Hq, Hkv, head_dim, K_code, T, scale, workspace, workspace_bytes,
+                          stream, &c);
+}
+
+namespace {
+int code_step_launch(const void* q, int64_t q_row_stride, int64_t q_head_stride, void* out,
+                     int64_t out_row_stride, int64_t out_head_stride, const int32_t* q_start,
+                     const void* kv_cache, int kv_layout, int64_t num_blocks, int page_size,
+                     const int32_t* block_table, int64_t bt_stride, const int32_t* seq_lens,
+                     const int32_t* excluded, const int32_t* quota_per_kv_head, int R, int Hq,
+                     int Hkv, int head_dim, int K_code, int T, float scale, void* workspace,
+                     size_t workspace_bytes, void* stream, const CommitArgs* commit) {
   if (!q || !out || !q_start || !kv_cache || !block_table || !seq_lens || !quota_per_kv_head)
     return ABKV_ERR_INVALID_ARG;
   if (R <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv != 0 || T <= 0 || num_blocks <= 0 || bt_stride <= 0 ||
@@ -547,8 +693,17 @@ extern "C" int abkv_code_step_attention(const void* q, int64_t q_row_stride, int
   if (cudaFuncSetAttribute(codestep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) !=
       cudaSuccess)
     return ABKV_ERR_CUDA;
+  if (commit) {
+    prm.cops = commit->ops;
+    prm.coff = commit->off;
+    prm.ccount = commit->count;
+    prm.kv = static_cast<char*>(const_cast<void*>(kv_cache));
+    prm.row_bytes = (int64_t)Hkv * kD * 2;
+    prm.ctas_per_req = (K_code / kBM) * Hkv * prm.npairs;
+  }
   dim3 grid(K_code / kBM, Hkv * prm.npairs, R);
   codestep_kernel<<<grid, kThreads, kSmemBytes, reinterpret_cast<cudaStream_t>(stream)>>>(prm);
   if (cudaGetLastError() != cudaSuccess) return ABKV_ERR_CUDA;
   return ABKV_OK;
 }
+}  // namespace

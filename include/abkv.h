@@ -438,6 +438,45 @@ int abkv_code_step_attention(const void* q, int64_t q_row_stride,
                              float scale, void* workspace,
                              size_t workspace_bytes, void* stream);
 
+/* The code step fused with the compaction that follows it in the block
+ * boundary flow (CompressLMProcessor._compact_response_content,
+ * third_party/vllm_overlay/vllm/v1/core/compresslm/processor.py:467-557,
+ * whose copy ops GPUModelRunner._execute_kv_copy_group applies,
+ * .../v1/worker/gpu_model_runner.py:1194-1220): the same attention as
+ * abkv_code_step_attention, then request r's row copies
+ * ops[op_offsets[r] .. op_offsets[r+1]) (HOST [n][4] int32 = src_block,
+ * src_off, dst_block, dst_off; op_offsets HOST [R+1] int64, from 0 to n) are
+ * applied to this layer's kv_cache by the last CTA of the request, once every
+ * CTA of the request has finished reading the cache, so the copies overlap
+ * the other requests' attention instead of needing a separate launch.
+ * Result: out and kv_cache equal abkv_code_step_attention followed by
+ * abkv_compact of the same ops as one batch.  The host rejects ops out of
+ * range (ABKV_ERR_INVALID_ARG), and a batch in which a destination repeats or
+ * is also a source (ABKV_ERR_UNSUPPORTED: use abkv_compact for ordered
+ * batches).  Contract: request r's ops touch only pages no other request of
+ * the launch reads (true of the compaction of a request's own finished block).
+ * If any CTA of a request gives up on a wait, or the request's query rows
+ * are out of range, that request's ops are not applied and the error word
+ * records why.  Workspace:
+ * abkv_code_step_compact_workspace_size(R, n) bytes, 256-byte aligned. */
+size_t abkv_code_step_compact_workspace_size(int num_requests, int64_t n_ops);
+
+int abkv_code_step_attention_compact(const void* q, int64_t q_row_stride,
+                                     int64_t q_head_stride, void* out,
+                                     int64_t out_row_stride,
+                                     int64_t out_head_stride,
+                                     const int32_t* q_start, void* kv_cache,
+                                     int kv_layout, int64_t num_blocks,
+                                     int page_size, const int32_t* block_table,
+                                     int64_t bt_stride, const int32_t* seq_lens,
+                                     const int32_t* excluded,
+                                     const int32_t* quota_per_kv_head, int R,
+                                     int Hq, int Hkv, int head_dim, int K_code,
+                                     int T, float scale, const int32_t* ops,
+                                     const int64_t* op_offsets, int64_t n_ops,
+                                     void* workspace, size_t workspace_bytes,
+                                     void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -181,3 +181,72 @@ def test_codestep_rows_with_no_visible_key_are_zero():
     assert torch.all(out[:, :2] == 0)
     ref = kv[bt[0].long()[64 // page], 1, 0, 1].float()   # heads 2, 3: only code slot 0 (row 64) visible
     assert torch.allclose(out[:, 2:].float(), ref.expand(K, 2, D), atol=1e-2)
+
+
+def _finished_block_ops(bt, lens, K, C, q):
+    """Each request's compaction of its last finished block: code rows [L - K, L - K + q) move over
+    the start of the block's content rows [L - K - C, L - K - C + q) (its own pages)."""
+    ops, off = [], [0]
+    page = 16
+    for r in range(len(lens)):
+        L = int(lens[r])
+        for j in range(q):
+            s_row, d_row = L - K + j, L - K - C + j
+            ops.append((int(bt[r, s_row // page]), s_row % page, int(bt[r, d_row // page]), d_row % page))
+        off.append(len(ops))
+    return ops, off
+
+
+def test_codestep_fused_compaction_equals_code_step_then_executor():
+    """abkv_code_step_attention_compact equals abkv_code_step_attention followed by abkv_compact of
+    the same ops, bit for bit: the outputs and the whole cache.  Also the host checks of the ops."""
+    from abridgekv_b200 import compaction
+
+    torch.manual_seed(5)
+    R, K, C, Hq, Hkv, D, page = 16, 256, 512, 32, 8, 128, 16
+    quotas = [128] * Hkv
+    lens = torch.randint(1500, 3000, (R,)) + K
+    pages = (lens + page - 1) // page
+    nb = int(pages.sum()) + 1
+    kv = torch.randn((nb, 2, page, Hkv, D), device="cuda", dtype=torch.bfloat16)
+    perm = torch.randperm(nb - 1) + 1
+    bt = torch.zeros((R, int(pages.max())), dtype=torch.int32)
+    o = 0
+    for r in range(R):
+        bt[r, :pages[r]] = perm[o:o + pages[r]]
+        o += int(pages[r])
+    ops, off = _finished_block_ops(bt, lens, K, C, 128)
+    btd, sl = bt.cuda(), lens.to(torch.int32).cuda()
+    q = torch.randn((R * K, Hq, D), device="cuda", dtype=torch.bfloat16)
+    qs = (torch.arange(R + 1) * K).to(torch.int32).cuda()
+    kv_a, kv_b = kv.clone(), kv.clone()
+    ws = Workspace()
+    out_a = codestep.code_step_attention(q, kv_a, btd, sl, qs, quota_per_kv_head=quotas, k_max=K, workspace=ws)
+    compaction.execute_kv_copy_group(ops, [kv_a], workspace=ws)
+    out_b = codestep.code_step_attention_compact(q, kv_b, btd, sl, qs, ops=ops, op_offsets=off,
+                                                 quota_per_kv_head=quotas, k_max=K, workspace=ws)
+    torch.cuda.synchronize()
+    assert ws.read_error() == 0
+    assert torch.equal(out_a, out_b)
+    assert torch.equal(kv_a, kv_b)
+    assert not torch.equal(kv_a, kv)
+    # a second call on the same workspace (counters cleared per call) keeps the same result
+    kv_c = kv.clone()
+    out_c = codestep.code_step_attention_compact(q, kv_c, btd, sl, qs, ops=ops, op_offsets=off,
+                                                 quota_per_kv_head=quotas, k_max=K, workspace=ws)
+    torch.cuda.synchronize()
+    assert torch.equal(out_c, out_a) and torch.equal(kv_c, kv_a)
+    # host checks: a destination that is also a source, a block out of range, bad offsets
+    bad = list(ops)
+    bad[0] = (ops[1][2], ops[1][3], ops[0][2], ops[0][3])
+    with pytest.raises(AbkvError):
+        codestep.code_step_attention_compact(q, kv.clone(), btd, sl, qs, ops=bad, op_offsets=off,
+                                             quota_per_kv_head=quotas, k_max=K, workspace=ws)
+    bad = list(ops)
+    bad[3] = (nb, 0, ops[3][2], ops[3][3])
+    with pytest.raises(AbkvError):
+        codestep.code_step_attention_compact(q, kv.clone(), btd, sl, qs, ops=bad, op_offsets=off,
+                                             quota_per_kv_head=quotas, k_max=K, workspace=ws)
+    with pytest.raises(AbkvError):
+        codestep.code_step_attention_compact(q, kv.clone(), btd, sl, qs, ops=ops, op_offsets=off[:-1] + [0],
+                                             quota_per_kv_head=quotas, k_max=K, workspace=ws)
