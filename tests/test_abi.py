@@ -152,3 +152,46 @@ def test_prefill_backward_validation_rejects_before_launch(bad):
     expect = {"null_dout": 1, "heads": 1, "scale": 1, "head_dim": 3, "layout": 3, "unaligned": 1, "stride": 1,
               "workspace": 2}[bad]
     assert st == expect, (bad, st)
+
+
+def test_code_step_compact_workspace_size():
+    lib = _lib.lib()
+    n = lib.abkv_code_step_compact_workspace_size(64, 8192)
+    assert n >= 256 + 64 * 4 + 65 * 4 + 8192 * 16 and n % 256 == 0
+    assert lib.abkv_code_step_compact_workspace_size(0, 10) == 0
+    assert lib.abkv_code_step_compact_workspace_size(4, -1) == 0
+
+
+@pytest.mark.parametrize("bad", ["offsets_start", "offsets_end", "offsets_order", "block_oob", "offset_oob",
+                                 "dst_repeats", "dst_is_src", "workspace"])
+def test_code_step_compact_rejects_ops_before_launch(bad):
+    """abkv_code_step_attention_compact checks the copy ops (offsets, bounds, a destination that repeats
+    or is also a source) and the workspace before any upload or launch."""
+    lib = _lib.lib()
+    fake = 1 << 20  # never dereferenced: validation fails first
+    R, nb, page = 2, 10, 16
+    ops = [[1, 0, 2, 0], [1, 1, 2, 1], [3, 0, 4, 0], [3, 1, 4, 1]]
+    off = [0, 2, 4]
+    if bad == "offsets_start":
+        off = [1, 2, 4]
+    if bad == "offsets_end":
+        off = [0, 2, 3]
+    if bad == "offsets_order":
+        off = [0, 3, 2]
+    if bad == "block_oob":
+        ops[2][0] = nb
+    if bad == "offset_oob":
+        ops[3][3] = page
+    if bad == "dst_repeats":
+        ops[3][2:] = ops[2][2:]
+    if bad == "dst_is_src":
+        ops[3][2:] = ops[0][:2]
+    flat = (C.c_int32 * 16)(*[x for op in ops for x in op])
+    offs = _lib.i64_array(off)
+    ws, ws_bytes = (fake, 64) if bad == "workspace" else (fake, 1 << 30)
+    st = lib.abkv_code_step_attention_compact(
+        fake, 32 * 128, 128, fake, 32 * 128, 128, fake, fake, 0, nb, page, fake, 8, fake, None,
+        _lib.i32_array([128] * 8), R, 32, 8, 128, 256, 512, 0.088, flat, offs, len(ops), ws, ws_bytes, None)
+    expect = {"offsets_start": 1, "offsets_end": 1, "offsets_order": 1, "block_oob": 1, "offset_oob": 1,
+              "dst_repeats": 3, "dst_is_src": 3, "workspace": 2}[bad]
+    assert st == expect, (bad, st)
