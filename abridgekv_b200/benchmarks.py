@@ -534,7 +534,8 @@ def bench_codestep_compact(args) -> dict:
         compaction.execute_kv_copy_group(compaction.CopyOps(ops_arr), [kv], workspace=ws)
 
     def fused():
-        codestep.code_step_attention_compact(q, kv, btd, sl, qs, ops=ops_arr, op_offsets=off, **kw)
+        codestep.code_step_attention_compact(q, kv, btd, sl, qs, ops=ops_arr, op_offsets=off, replay_tail=0,
+                                             **kw)
 
     def timed(fn):
         for _ in range(args.warmup):

@@ -103,9 +103,40 @@ def code_step_attention(query: torch.Tensor, kv_cache: torch.Tensor, block_table
     return out
 
 
+def check_op_ownership(ops: np.ndarray, op_offsets: np.ndarray, block_table_host, seq_lens_host,
+                       page: int) -> None:
+    """Raise ValueError unless request r's copy ops read and write only pages of its own live
+    block-table row (the first ceil(seq_len / page) entries) and no other request's live row holds
+    a page that r writes.  Shared (prefix-cached) pages fail the check: their copies would race
+    with the other request's loads inside the fused launch."""
+    bt = np.asarray(block_table_host)
+    sl = np.asarray(seq_lens_host).astype(np.int64)
+    R = len(op_offsets) - 1
+    if bt.ndim != 2 or bt.shape[0] < R or sl.shape[0] < R:
+        raise ValueError("block_table_host / seq_lens_host must cover every request of the launch")
+    live = [bt[r, :(int(sl[r]) + page - 1) // page].astype(np.int64) for r in range(R)]
+    owners: dict[int, set[int]] = {}
+    for r, row in enumerate(live):
+        for pg in np.unique(row).tolist():
+            owners.setdefault(pg, set()).add(r)
+    for r in range(R):
+        mine = ops[op_offsets[r]:op_offsets[r + 1]]
+        if not len(mine):
+            continue
+        own = set(live[r].tolist())
+        for pg in np.unique(np.concatenate([mine[:, 0], mine[:, 2]])).tolist():
+            if pg not in own:
+                raise ValueError(f"request {r}: copy op touches page {pg} outside its own block-table row")
+        for pg in np.unique(mine[:, 2]).tolist():
+            if owners.get(pg, {r}) != {r}:
+                raise ValueError(f"request {r}: copy op writes page {pg}, which other requests of the launch "
+                                 "also read (shared pages): use code_step_attention + the executor")
+
+
 def code_step_attention_compact(query: torch.Tensor, kv_cache: torch.Tensor, block_table: torch.Tensor,
                                 seq_lens: torch.Tensor, query_start_loc: torch.Tensor, *, ops,
                                 op_offsets: Sequence[int], quota_per_kv_head: Sequence[int], k_max: int,
+                                replay_tail: int, block_table_host=None, seq_lens_host=None,
                                 scale: float | None = None, excluded: torch.Tensor | None = None,
                                 num_requests: int | None = None, out: torch.Tensor | None = None,
                                 workspace: Workspace | None = None,
@@ -114,13 +145,31 @@ def code_step_attention_compact(query: torch.Tensor, kv_cache: torch.Tensor, blo
     request r's (src_block, src_off, dst_block, dst_off) row copies ``ops[op_offsets[r] ..
     op_offsets[r + 1])`` are applied once every CTA of request r has read the cache.  Same result as
     ``code_step_attention`` then ``compaction.execute_kv_copy_group(ops, [kv_cache])``; a batch whose
-    destinations repeat or overlap its sources is rejected (use the separate executor for it)."""
+    destinations repeat or overlap its sources is rejected (use the separate executor for it).
+
+    Ordering: the reference finishes a block (and plans its compaction) right after the code step
+    only when the configuration has no replay tail -- ``CompressLMProcessor.update_after_step``
+    calls ``_finish_block`` at the end of the code role only when the block has no replay positions
+    (third_party/vllm_overlay/vllm/v1/core/compresslm/processor.py:250-262); with a replay tail the
+    block finishes after the replay step, whose queries still read the uncompacted rows.  So the
+    caller states ``replay_tail`` (``CompressLMConfig.replay_tail``) and any value but 0 is refused;
+    the ops are those the planner's ``finish_block`` produced for the block, planned before this
+    launch.  Ownership: each request's ops must stay in its own pages; pass ``block_table_host`` and
+    ``seq_lens_host`` (host copies of the launch's tables) to have that checked."""
+    if int(replay_tail) != 0:
+        raise ValueError(f"code_step_attention_compact needs replay_tail == 0 (got {replay_tail}): with a replay "
+                         "tail the block finishes after its replay step, so its compaction cannot ride in the "
+                         "code step; use code_step_attention and apply the ops after the replay step")
     head, out, R, nb, page, T, scale = _prepare(query, kv_cache, block_table, seq_lens, query_start_loc,
                                                 quota_per_kv_head, scale, excluded, num_requests, out)
     arr = np.ascontiguousarray(getattr(ops, "array", ops), dtype=np.int32).reshape(-1, 4)
     off = np.ascontiguousarray(op_offsets, dtype=np.int64)
     if off.shape != (R + 1,):
         raise ValueError(f"op_offsets must hold R + 1 = {R + 1} entries")
+    if block_table_host is not None or seq_lens_host is not None:
+        if block_table_host is None or seq_lens_host is None:
+            raise ValueError("the ownership check needs both block_table_host and seq_lens_host")
+        check_op_ownership(arr, off, block_table_host, seq_lens_host, page)
     dev = query.device
     lib = _lib.lib()
     need = lib.abkv_code_step_compact_workspace_size(R, len(arr))

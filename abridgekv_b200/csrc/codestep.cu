@@ -102,7 +102,8 @@ struct alignas(64) CodeStepParams {
 // The last CTA of request blockIdx.z applies that request's copy ops.  Every CTA of the request
 // counts itself once all its reads of the cache are done: its TMA loads were consumed (waited on)
 // before its MMAs, and the barrier before this call orders every thread.  A CTA that gave up on a
-// wait does not count, so the request's ops are not applied and the error word says why.  The host
+// wait, or that met an out-of-range page id in the request's block-table row, does not count, so
+// the request's ops are not applied and the error word says why.  The host
 // checked that no op writes a row any op reads and that destinations are unique, so the copies may
 // run in any order.
 __device__ __noinline__ void commit_request_ops(const CodeStepParams& p, bool dead) {
@@ -307,6 +308,10 @@ __global__ void __launch_bounds__(kThreads, 1) codestep_kernel(const __grid_cons
   const uint32_t tmem = *s_tmem;
   const int n_tiles = *s_nlist;
   bool dead = false;
+  // set by the producer lane that met an out-of-range page id: the attention
+  // still completes (that slice is not loaded), but the request's copy ops
+  // are not applied after attention over a bad block table
+  bool bad_page = false;
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
@@ -334,6 +339,7 @@ __global__ void __launch_bounds__(kThreads, 1) codestep_kernel(const __grid_cons
         const int v = __ldg(p.bt + (int64_t)b * p.bt_stride + row0 / p.page);
         if (v < 0 || (int64_t)v >= p.num_blocks) {
           set_error(p.err, ABKV_DEVERR_PAGE_OOB);
+          bad_page = true;
           return -1;
         }
         return v;
@@ -516,7 +522,7 @@ __global__ void __launch_bounds__(kThreads, 1) codestep_kernel(const __grid_cons
   if (warp == 1) {
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(kTmemCols));
   }
-  if (p.cops) commit_request_ops(p, dead);
+  if (p.cops) commit_request_ops(p, dead || bad_page);
 }
 
 }  // namespace

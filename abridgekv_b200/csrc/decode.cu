@@ -1224,9 +1224,12 @@ extern "C" int abkv_decode_noalloc(const void* const* q, const void* const* kv,
                                    void* const* out, int num_layers, int num_seqs, int num_q_heads,
                                    int num_kv_heads, int head_dim, int page_size, int max_pages_per_seq,
                                    float scale, int chunk_tokens, int32_t* device_error, void* stream) {
+  if (num_kv_heads <= 0 || num_q_heads % num_kv_heads != 0) return ABKV_ERR_INVALID_ARG;
+  // The plan of the launch itself (with its KV-head count), so the limit check
+  // refuses exactly the requests whose launch would not fit.
   DecodePlan plan;
   const int st = plan_decode(num_layers, num_seqs, num_q_heads, head_dim, page_size, max_pages_per_seq,
-                             chunk_tokens, 0, &plan);
+                             chunk_tokens, 0, &plan, num_kv_heads);
   if (st != ABKV_OK) return st;
   if (plan.total > kNoAllocScratchBytes) return ABKV_ERR_SCRATCH_LIMIT;
   void* scratch = nullptr;

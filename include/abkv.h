@@ -114,7 +114,10 @@ int abkv_decode(const void* const* q, const void* const* kv,
  * keeps until the process exits.
  *   - The first call on a device looks up that array's device address (with
  *     the device current) and caches it; make that first call before any
- *     stream capture.
+ *     stream capture.  The cached address belongs to the device's primary
+ *     context: after that context is reset or destroyed
+ *     (cudaDeviceReset) it is stale, and the library must be unloaded and
+ *     loaded again before the next call.
  *   - A request whose scratch would exceed 32 MiB is rejected with
  *     ABKV_ERR_SCRATCH_LIMIT before anything runs (the scratch grows with
  *     num_layers x num_seqs x split-KV chunks x num_q_heads x head_dim x 4 B;
@@ -453,11 +456,24 @@ int abkv_code_step_attention(const void* q, int64_t q_row_stride,
  * abkv_compact of the same ops as one batch.  The host rejects ops out of
  * range (ABKV_ERR_INVALID_ARG), and a batch in which a destination repeats or
  * is also a source (ABKV_ERR_UNSUPPORTED: use abkv_compact for ordered
- * batches).  Contract: request r's ops touch only pages no other request of
- * the launch reads (true of the compaction of a request's own finished block).
- * If any CTA of a request gives up on a wait, or the request's query rows
- * are out of range, that request's ops are not applied and the error word
- * records why.  Workspace:
+ * batches).  Preconditions the caller guarantees (nothing here can check
+ * them against device-side tables):
+ *   - ordering: the block finishes directly after its code step, i.e. the
+ *     configuration has no replay tail (replay_tail == 0; the reference calls
+ *     _finish_block at the end of the code role only when the block has no
+ *     replay positions, processor.py:250-262), and the ops are the ones the
+ *     planner's finish_block produced for that block before this launch;
+ *   - ownership: request r's ops read and write only pages of request r's
+ *     own block-table row, and no other request of the launch reads those
+ *     pages (true without prefix sharing, which CompressLM disables); with
+ *     shared pages the copies would race with the other request's loads, so
+ *     use abkv_code_step_attention + abkv_compact instead.
+ * The Python wrapper (codestep.code_step_attention_compact) requires the
+ * replay tail to be stated and checks ownership against a host copy of the
+ * block table when one is given.  If any CTA of a request gives up on a
+ * wait, meets an out-of-range page id in the request's block-table row, or
+ * the request's query rows are out of range, that request's ops are not
+ * applied and the error word records why.  Workspace:
  * abkv_code_step_compact_workspace_size(R, n) bytes, 256-byte aligned. */
 size_t abkv_code_step_compact_workspace_size(int num_requests, int64_t n_ops);
 

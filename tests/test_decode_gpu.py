@@ -4,7 +4,9 @@ Tolerances (bf16 outputs): the kernel computes scores in fp32 while the
 reference rounds them to bf16, so its results sit closer to the float64 truth
 than the reference's; both must stay within
   |gpu - reference| <= 3e-2 and |gpu - float64| <= 1.5e-2 (max abs),
-with mean abs error vs float64 below 2e-3.
+with mean abs error vs float64 below 2e-3; relative error (max |gpu - float64|
+/ max |float64| and the per-element median, tests/errstats.py) is reported and
+bounded as well.
 """
 import numpy as np
 import pytest
@@ -13,6 +15,7 @@ import torch
 from abridgekv_b200 import decode
 from abridgekv_b200.workspace import Workspace
 from oracle.decode_ref import decode_exact
+from tests.errstats import assert_relative, report
 from tests.goldens import decode_cases, load_decode
 
 pytestmark = pytest.mark.gpu
@@ -44,13 +47,11 @@ def test_decode_matches_reference_golden(name, chunk_tokens):
     assert ws.read_error() == 0
     assert np.isfinite(got).all(), "kernel read a poisoned row or page"
     exact = decode_exact(case.q, case.kv, case.block_table, case.seq_lens, case.scale, case.page)
-    err_ref = np.abs(got - ref).max()
-    err_ex = np.abs(got - exact)
-    print(f"{name} chunk={chunk_tokens}: max|gpu-ref|={err_ref:.3e} max|gpu-f64|={err_ex.max():.3e} "
-          f"mean|gpu-f64|={err_ex.mean():.3e}")
-    assert err_ref <= ATOL_REF
-    assert err_ex.max() <= ATOL_EXACT
-    assert err_ex.mean() <= MEAN_EXACT
+    se, sr = report(f"{name} chunk={chunk_tokens}", got, exact, ref)
+    assert sr["max_abs"] <= ATOL_REF
+    assert se["max_abs"] <= ATOL_EXACT
+    assert se["mean_abs"] <= MEAN_EXACT
+    assert_relative(se, name)
 
 
 def test_multi_layer_launch_equals_single_layer_calls():
@@ -215,3 +216,37 @@ def test_workspace_reuse_across_plans():
         assert ws.read_error() == 0
         for a, b in zip(again, fresh):
             assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("name", ["g4_ragged", "qwen3_heads", "config1_d64"])
+def test_dropin_attend_decode_batched_and_forward_decode(name):
+    """The two functions a maintainer binds (decode.attend_decode_batched in place of
+    PackedKVSidecar._attend_decode_batched, decode.forward_decode in AttentionImpl.forward's
+    shape) on the golden inputs: host seq_lens (vLLM's _seq_lens_cpu), a [T, Hq*D] output that
+    is written in place for the first n rows only, and a block table with extra rows."""
+    case, ref = load_decode(name)
+    q, kv, bt, _ = _dev(case)
+    n, Hq, D = q.shape
+    Hkv = kv.shape[3]
+    exact = decode_exact(case.q, case.kv, case.block_table, case.seq_lens, case.scale, case.page)
+    sl_host = torch.from_numpy(case.seq_lens.astype(np.int32))
+    # vLLM pads the batch: two extra query rows and block-table rows that must stay untouched
+    q_pad = torch.cat([q, torch.randn((2, Hq, D), device="cuda").to(torch.bfloat16)])
+    bt_pad = torch.cat([bt, torch.zeros((2, bt.shape[1]), dtype=torch.int32, device="cuda")])
+    output = torch.full((n + 2, Hq * D), 7.0, dtype=torch.bfloat16, device="cuda")
+    decode.attend_decode_batched(query=q_pad, kv_cache=kv, output=output, seq_lens=sl_host, block_table=bt_pad,
+                                 num_kv_heads=Hkv, groups=Hq // Hkv, scale=case.scale, num_requests=n)
+    got = output[:n].view(n, Hq, D).float().cpu().numpy()
+    assert torch.all(output[n:] == 7.0), "rows past the active requests were written"
+    se, sr = report(f"attend_decode_batched {name}", got, exact, ref)
+    assert se["max_abs"] <= ATOL_EXACT and se["mean_abs"] <= MEAN_EXACT and sr["max_abs"] <= ATOL_REF
+    assert_relative(se, name)
+    # the same rows through the direct launch
+    direct = decode.paged_decode([q], [kv], [bt], [torch.from_numpy(case.seq_lens).cuda()], scale=case.scale)[0]
+    assert torch.equal(output[:n].view(n, Hq, D), direct)
+    # AttentionImpl.forward shape: [T, Hq, D] query, [T, Hq*D] output (allocated or given)
+    out2 = decode.forward_decode(q, kv, bt, sl_host, case.scale)
+    assert out2.shape == (n, Hq * D) and torch.equal(out2.view(n, Hq, D), direct)
+    given = torch.empty((n, Hq * D), dtype=torch.bfloat16, device="cuda")
+    assert decode.forward_decode(q, kv, bt, sl_host, case.scale, output=given) is given
+    assert torch.equal(given, out2)

@@ -21,6 +21,29 @@ def test_decode_oracle_matches_reference(name):
 
 
 @pytest.mark.parametrize("name", decode_cases())
+def test_decode_torch_port_matches_reference(name):
+    """The torch CPU port that bench.py times as the decode CPU baseline and as the reference arm
+    (oracle/decode_ref.sidecar_decode_torch) reproduces the reference's own
+    _attend_decode_batched outputs on every golden case: within two bf16 ulps, as the numpy
+    restatement above."""
+    import torch
+
+    from oracle.decode_ref import sidecar_decode_torch
+
+    case, ref = load_decode(name)
+    Hq, Hkv = case.q.shape[1], case.kv.shape[3]
+    got = sidecar_decode_torch(torch.from_numpy(case.q).to(torch.bfloat16),
+                               torch.from_numpy(case.kv).to(torch.bfloat16),
+                               torch.from_numpy(case.seq_lens), torch.from_numpy(case.block_table),
+                               Hkv, Hq // Hkv, case.scale, case.page).float().numpy()
+    live = case.seq_lens > 0  # the reference leaves rows of empty requests untouched
+    diff = np.abs(got[live] - ref[live])
+    ulp = np.maximum(np.abs(ref[live]), np.abs(got[live])) * 2.0 ** -6 + 1e-5
+    assert (diff <= ulp).all(), float(diff.max())
+    assert (diff == 0).mean() > 0.97
+
+
+@pytest.mark.parametrize("name", decode_cases())
 def test_reference_rounding_error_is_small(name):
     """Bound on the reference's own bf16-score error vs float64 (the budget our
     kernel's tolerance is set against)."""

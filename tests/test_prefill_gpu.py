@@ -2,7 +2,8 @@
 
 Tolerances (bf16 output; P rounded to bf16 before P.V as FlexAttention's
 kernels do): max |gpu - float64 oracle| <= 2.5e-2, mean <= 2e-3; the same
-bounds against the reference's FlexAttention rows; lse within 1e-2.
+bounds against the reference's FlexAttention rows; lse within 1e-2; relative
+error (tests/errstats.py) reported and bounded.
 """
 import numpy as np
 import pytest
@@ -11,6 +12,7 @@ import torch
 from abridgekv_b200 import prefill
 from abridgekv_b200.workspace import Workspace
 from oracle.mask_ref import arith_mask, masked_attention
+from tests.errstats import assert_relative, report
 from tests.goldens import load_prefill, prefill_cases
 
 pytestmark = pytest.mark.gpu
@@ -34,11 +36,12 @@ def test_prefill_matches_reference_flex_and_oracle(name):
     got = out.float().cpu().numpy()
     assert np.isfinite(got).all()
     ref64, lse64 = masked_attention(g["q"], g["k"], g["v"], g["mask"], 1.0 / np.sqrt(g["D"]))
-    err = np.abs(got - ref64)
-    print(f"{name}: max|gpu-f64|={err.max():.3e} mean={err.mean():.3e}")
-    assert err.max() <= ATOL and err.mean() <= MEAN
-    errf = np.abs(got[:, :, g["rows"], :] - g["out_rows"])
-    assert errf.max() <= ATOL
+    se, _ = report(name, got, ref64)
+    assert se["max_abs"] <= ATOL and se["mean_abs"] <= MEAN
+    assert_relative(se, name)
+    _, sr = report(f"{name} (reference FlexAttention rows)", got[:, :, g["rows"], :],
+                   ref64[:, :, g["rows"], :], g["out_rows"])
+    assert sr["max_abs"] <= ATOL
     assert np.abs(lse.cpu().numpy() - g["lse"]).max() <= 1e-2
 
 

@@ -1,7 +1,7 @@
 """Packed per-head-quota sidecar: PackedKVLayout on CPU; decode over sidecar pages + the paged
 main cache through abkv_decode_packed on a B200 against the reference goldens and the float64
 oracle (tolerances as the plain decode: |gpu - reference| <= 3e-2, |gpu - float64| <= 1.5e-2 max
-and <= 2e-3 mean)."""
+and <= 2e-3 mean; relative error reported and bounded as in tests/errstats.py)."""
 import numpy as np
 import pytest
 import torch
@@ -56,6 +56,7 @@ def test_packed_decode_matches_reference_golden(chunk_tokens):
     from abridgekv_b200.sidecar import attend_decode_batched_packed
     from abridgekv_b200.workspace import Workspace
     from oracle.decode_ref import packed_decode_exact
+    from tests.errstats import assert_relative, report
     from tests.goldens import load_packed, packed_cases
 
     for name in packed_cases():
@@ -77,11 +78,10 @@ def test_packed_decode_matches_reference_golden(chunk_tokens):
         got = out.float().cpu().numpy()
         ex = packed_decode_exact(case.q, case.kv, case.block_table, case.seq_lens, side, counts, quotas,
                                  case.scale, case.page)
-        e = np.abs(got - ex)
-        print(f"{name} chunk={chunk_tokens}: max|gpu-ref|={np.abs(got - ref).max():.3e} "
-              f"max|gpu-f64|={e.max():.3e} mean={e.mean():.3e}")
-        assert np.abs(got - ref).max() <= ATOL_REF, name
-        assert e.max() <= ATOL_EXACT and e.mean() <= MEAN_EXACT, name
+        se, sr = report(f"{name} chunk={chunk_tokens}", got, ex, ref)
+        assert sr["max_abs"] <= ATOL_REF, name
+        assert se["max_abs"] <= ATOL_EXACT and se["mean_abs"] <= MEAN_EXACT, name
+        assert_relative(se, name)
         # the drop-in form writes the same rows
         out2 = torch.zeros((q.shape[0], q.shape[1] * q.shape[2]), dtype=torch.bfloat16, device="cuda")
         attend_decode_batched_packed(query=q, kv_cache=kv, output=out2,
