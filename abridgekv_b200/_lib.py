@@ -94,6 +94,8 @@ SIGNATURES: dict[str, tuple] = {
                              c_vp, c_size, c_vp]),
     "abkv_gather_rows": (c_int, [c_vpp, c_vpp, c_int, C.c_int64, C.c_int64, C.c_int64, C.c_int64, c_vp,
                                  c_vp, c_size, c_vp]),
+    "abkv_store_kv": (c_int, [c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_int, c_i64, c_int, c_int, c_int,
+                              c_vp, c_int, c_vp, c_size, c_vp]),
     "abkv_prefill_masked": (c_int, [c_vp, c_i64p, c_vp, c_i64p, c_vp, c_i64p, c_vp, c_i64p, c_vp, c_i32p, c_vp,
                                     c_int, c_int, c_int, c_int, c_int, c_int, c_int, C.c_float, c_vp, c_size,
                                     c_vp]),
@@ -105,6 +107,9 @@ SIGNATURES: dict[str, tuple] = {
     "abkv_code_step_attention": (c_int, [c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_vp, c_int, c_i64, c_int,
                                          c_vp, c_i64, c_vp, c_vp, c_i32p, c_int, c_int, c_int, c_int, c_int,
                                          c_int, C.c_float, c_vp, c_size, c_vp]),
+    "abkv_paged_prefill": (c_int, [c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_vp, c_int, c_i64, c_int, c_vp,
+                                   c_i64, c_vp, c_int, c_int, c_int, c_int, c_int, c_int, C.c_float, c_vp, c_size,
+                                   c_vp]),
     "abkv_code_step_compact_workspace_size": (c_size, [c_int, c_i64]),
     "abkv_code_step_attention_compact": (c_int, [c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_vp, c_int, c_i64,
                                                  c_int, c_vp, c_i64, c_vp, c_vp, c_i32p, c_int, c_int, c_int, c_int,

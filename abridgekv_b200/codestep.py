@@ -39,18 +39,18 @@ def _layout_of(kv: torch.Tensor, num_kv_heads: int) -> tuple[int, int, int]:
 
 
 def _prepare(query, kv_cache, block_table, seq_lens, query_start_loc, quota_per_kv_head, scale, excluded,
-             num_requests, out):
-    """Checks the code-step arguments -> (leading arguments of the C call, out, R, num_blocks, page, T,
-    scale)."""
+             num_requests, out, num_kv_heads=None):
+    """Checks the code-step (or, with quota_per_kv_head None, the causal prefill) arguments ->
+    (leading arguments of the C call, out, R, num_blocks, page, T, scale)."""
     for name, t in (("query", query), ("kv_cache", kv_cache)):
         if not isinstance(t, torch.Tensor) or not t.is_cuda or t.dtype != torch.bfloat16:
             raise TypeError(f"{name} must be a bf16 CUDA tensor (libabkv has no CPU path)")
     if query.dim() != 3 or query.stride(2) != 1:
         raise ValueError("query must be [T, Hq, D] with a contiguous last dimension")
     T, Hq, D = query.shape
-    Hkv = len(quota_per_kv_head)
-    if Hkv == 0 or Hq % Hkv:
-        raise ValueError("quota_per_kv_head must hold one quota per KV head dividing the query heads")
+    Hkv = len(quota_per_kv_head) if quota_per_kv_head is not None else int(num_kv_heads)
+    if Hkv <= 0 or Hq % Hkv:
+        raise ValueError("the KV heads (one quota per KV head) must divide the query heads")
     layout, nb, page = _layout_of(kv_cache, Hkv)
     R = block_table.shape[0] if num_requests is None else int(num_requests)
     dev = query.device
@@ -66,7 +66,8 @@ def _prepare(query, kv_cache, block_table, seq_lens, query_start_loc, quota_per_
     if bt.stride(1) != 1:
         raise ValueError("block_table rows must be contiguous")
     sl = i32("seq_lens", seq_lens, lambda t: t.dim() == 1 and t.shape[0] >= R)
-    qs = i32("query_start_loc", query_start_loc, lambda t: t.dim() == 1 and t.shape[0] >= R)
+    need_qs = R if quota_per_kv_head is not None else R + 1  # the causal mode reads query_start_loc[r + 1]
+    qs = i32("query_start_loc", query_start_loc, lambda t: t.dim() == 1 and t.shape[0] >= need_qs)
     ex = None
     if excluded is not None:
         ex = i32("excluded", excluded, lambda t: t.dim() == 2 and t.shape[0] >= R and t.shape[1] == 2)
@@ -75,6 +76,11 @@ def _prepare(query, kv_cache, block_table, seq_lens, query_start_loc, quota_per_
     if tuple(out.shape) != (T, Hq, D) or out.dtype != torch.bfloat16 or out.stride(2) != 1:
         raise ValueError("out must be a bf16 [T, Hq, D] tensor with a contiguous last dimension")
     scale = 1.0 / math.sqrt(D) if scale is None else float(scale)
+    if quota_per_kv_head is None:  # abkv_paged_prefill's leading arguments
+        head = (query.data_ptr(), query.stride(0), query.stride(1), out.data_ptr(), out.stride(0), out.stride(1),
+                qs.data_ptr(), kv_cache.data_ptr(), layout, nb, page, bt.data_ptr(), bt.stride(0), sl.data_ptr(),
+                R, Hq, Hkv, D)
+        return head, out, R, nb, page, T, scale
     head = (query.data_ptr(), query.stride(0), query.stride(1), out.data_ptr(), out.stride(0), out.stride(1),
             qs.data_ptr(), kv_cache.data_ptr(), layout, nb, page, bt.data_ptr(), bt.stride(0), sl.data_ptr(),
             ex.data_ptr() if ex is not None else None, _lib.i32_array(quota_per_kv_head), R, Hq, Hkv, D)
@@ -100,6 +106,34 @@ def code_step_attention(query: torch.Tensor, kv_cache: torch.Tensor, block_table
     with torch.cuda.device(dev):
         st = _lib.lib().abkv_code_step_attention(*head, int(k_max), T, scale, ws.ptr(), ws.nbytes, s.cuda_stream)
     _lib.check("abkv_code_step_attention", st)
+    return out
+
+
+def paged_prefill(query: torch.Tensor, kv_cache: torch.Tensor, block_table: torch.Tensor, seq_lens: torch.Tensor,
+                  query_start_loc: torch.Tensor, *, max_query_len: int, num_kv_heads: int,
+                  scale: float | None = None, num_requests: int | None = None, out: torch.Tensor | None = None,
+                  workspace: Workspace | None = None, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """Causal attention of ragged query rows over the paged cache (prompt prefill, chunked prefill and
+    mixed prefill/decode batches): request r's rows are ``query_start_loc[r] .. query_start_loc[r + 1] - 1``
+    (qlen rows, their keys already written at cache rows [seq_len - qlen, seq_len)), and row i attends
+    to cache rows ``[0, seq_len - qlen + i + 1)``.  This is the causal branch of
+    PackedKVSidecar._attend_request_vectorized (compresslm_packed_kv.py:700-707) without sidecar
+    pages, and the paged causal prefill the stock backend runs for a CompressLM KV-cache group.
+
+    query [T, Hq, D] bf16 (last dim contiguous), D = 128; kv_cache paged bf16 (either layout);
+    block_table [R, max_pages] int32; seq_lens [R] int32 (each >= its qlen); query_start_loc
+    [>= R + 1] int32; max_query_len >= every qlen (vLLM's ``max_query_len``).  Writes and returns
+    out [T, Hq, D] (rows of no request are left untouched)."""
+    head, out, R, nb, page, T, scale = _prepare(query, kv_cache, block_table, seq_lens, query_start_loc, None,
+                                                scale, None, num_requests, out, num_kv_heads=num_kv_heads)
+    if int(max_query_len) <= 0 or int(max_query_len) > T:
+        raise ValueError(f"max_query_len must be in [1, T={T}]")
+    dev = query.device
+    ws = workspace or default_workspace(dev)
+    s = torch.cuda.current_stream(dev) if stream is None else stream
+    with torch.cuda.device(dev):
+        st = _lib.lib().abkv_paged_prefill(*head, int(max_query_len), T, scale, ws.ptr(), ws.nbytes, s.cuda_stream)
+    _lib.check("abkv_paged_prefill", st)
     return out
 
 

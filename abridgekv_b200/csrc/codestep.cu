@@ -97,6 +97,9 @@ struct alignas(64) CodeStepParams {
   char* kv;
   int64_t row_bytes;
   int ctas_per_req;
+  // causal mode (abkv_paged_prefill): request r's query rows are q_start[r] .. q_start[r + 1] - 1
+  // (qlen rows, any count); row i sees cache rows [0, seq_len - qlen + i + 1), every head alike
+  int causal;
 };
 
 // The last CTA of request blockIdx.z applies that request's copy ops.  Every CTA of the request
@@ -238,11 +241,22 @@ __global__ void __launch_bounds__(kThreads, 1) codestep_kernel(const __grid_cons
   const int hB = (2 * hp + 1 < p.G) ? hA + 1 : -1;  // odd group size: the last pair has one head
   const int b = blockIdx.z;  // request
   int kt_end = 0, seq_len = 0, leffA = 0, leffB = 0, hole_s = 0, hole_e = 0;
+  int qlen = p.Kc;  // the request's query rows (all Kc code rows in the code step)
   {
     // every thread reads the same values, so an early return is CTA-uniform and
     // happens before any barrier, TMEM allocation or copy
     const int q0 = __ldg(p.q_start + b);
-    if (q0 < 0 || (int64_t)q0 + p.Kc > p.T) {
+    if (p.causal) {
+      const int q1 = __ldg(p.q_start + b + 1);
+      qlen = q1 - q0;
+      if (q0 < 0 || qlen < 0 || q1 > p.T) {
+        if (threadIdx.x == 0) set_error(p.err, ABKV_DEVERR_RANGE);
+        return;
+      }
+      // rows past the grid's tiles (max_query_len understated) are not computed
+      if (qlen > (int)gridDim.x * kBM && qt == 0 && threadIdx.x == 0) set_error(p.err, ABKV_DEVERR_RANGE);
+      if (qt * kBM >= qlen) return;  // no row of this request in this tile
+    } else if (q0 < 0 || (int64_t)q0 + p.Kc > p.T) {
       if (threadIdx.x == 0) set_error(p.err, ABKV_DEVERR_RANGE);
       return;
     }
@@ -250,9 +264,11 @@ __global__ void __launch_bounds__(kThreads, 1) codestep_kernel(const __grid_cons
     // its own code slots >= q are the last Kc - q rows of the request
     int sl = __ldg(p.seq_lens + b);
     const int64_t cap = min(p.bt_stride * (int64_t)p.page, (int64_t)kMaxKeyTiles * kBN);
-    if (sl < p.Kc || (int64_t)sl > cap) {
+    if (sl < qlen || (int64_t)sl > cap) {
       if (threadIdx.x == 0) set_error(p.err, ABKV_DEVERR_SEQ_OOB);
-      sl = sl < p.Kc ? p.Kc : (int)cap;
+      sl = sl < qlen ? qlen : (int)cap;
+      // more query rows than the key-tile list holds: nothing of the request is computed
+      if ((int64_t)sl > cap) return;
     }
     seq_len = sl;
     if (p.excl) {
@@ -265,8 +281,14 @@ __global__ void __launch_bounds__(kThreads, 1) codestep_kernel(const __grid_cons
         hole_s = hole_e = 0;
       }
     }
-    leffA = min(max(seq_len - (p.Kc - p.quota[hA]), 0), seq_len);
-    leffB = hB >= 0 ? min(max(seq_len - (p.Kc - p.quota[hB]), 0), seq_len) : 0;
+    if (p.causal) {
+      // the tile's last row (qt * 128 + 127, or the request's last) sees the most keys
+      const int last = min(qt * kBM + kBM, qlen);
+      leffA = leffB = seq_len - qlen + last;
+    } else {
+      leffA = min(max(seq_len - (p.Kc - p.quota[hA]), 0), seq_len);
+      leffB = hB >= 0 ? min(max(seq_len - (p.Kc - p.quota[hB]), 0), seq_len) : 0;
+    }
     kt_end = (max(leffA, leffB) + kBN - 1) / kBN;
   }
 
@@ -452,7 +474,9 @@ __global__ void __launch_bounds__(kThreads, 1) codestep_kernel(const __grid_cons
     const uint32_t tmem_h = tmem + (head_slot ? 256 : 0), tmem_o = tmem_h + 128;
     if (h >= 0) {
       SoftmaxState st{-INFINITY, 0.f};
-      const int leff = head_slot ? leffB : leffA;
+      // causal: row q sees seq_len - qlen + q + 1 keys (rows past the request's
+      // last row, which are never written, take the last row's limit)
+      const int leff = p.causal ? seq_len - qlen + min(q, qlen - 1) + 1 : (head_slot ? leffB : leffA);
       for (int j = 0; j < n_tiles; ++j) {
         const int e = s_list[j];
         const int lim = min(max(leff - e * kBN, 0), kBN);
@@ -503,14 +527,18 @@ __global__ void __launch_bounds__(kThreads, 1) codestep_kernel(const __grid_cons
 #pragma unroll
             for (int i = 0; i < 32; ++i) t[i] = 0.f;
           }
+          // tcgen05.ld above is warp-collective; only the stores skip rows past
+          // the request's last query row (causal mode)
+          if (q < qlen) {
 #pragma unroll
-          for (int v8 = 0; v8 < 4; ++v8) {
-            uint4 pk;
-            pk.x = pack_bf16x2(t[v8 * 8 + 0] * inv, t[v8 * 8 + 1] * inv);
-            pk.y = pack_bf16x2(t[v8 * 8 + 2] * inv, t[v8 * 8 + 3] * inv);
-            pk.z = pack_bf16x2(t[v8 * 8 + 4] * inv, t[v8 * 8 + 5] * inv);
-            pk.w = pack_bf16x2(t[v8 * 8 + 6] * inv, t[v8 * 8 + 7] * inv);
-            *reinterpret_cast<uint4*>(orow + c4 * 32 + v8 * 8) = pk;
+            for (int v8 = 0; v8 < 4; ++v8) {
+              uint4 pk;
+              pk.x = pack_bf16x2(t[v8 * 8 + 0] * inv, t[v8 * 8 + 1] * inv);
+              pk.y = pack_bf16x2(t[v8 * 8 + 2] * inv, t[v8 * 8 + 3] * inv);
+              pk.z = pack_bf16x2(t[v8 * 8 + 4] * inv, t[v8 * 8 + 5] * inv);
+              pk.w = pack_bf16x2(t[v8 * 8 + 6] * inv, t[v8 * 8 + 7] * inv);
+              *reinterpret_cast<uint4*>(orow + c4 * 32 + v8 * 8) = pk;
+            }
           }
         }
       }
@@ -544,7 +572,7 @@ int code_step_launch(const void* q, int64_t q_row_stride, int64_t q_head_stride,
                      const int32_t* block_table, int64_t bt_stride, const int32_t* seq_lens,
                      const int32_t* excluded, const int32_t* quota_per_kv_head, int R, int Hq,
                      int Hkv, int head_dim, int K_code, int T, float scale, void* workspace,
-                     size_t workspace_bytes, void* stream, const CommitArgs* commit);
+                     size_t workspace_bytes, void* stream, const CommitArgs* commit, int causal_max_qlen = 0);
 
 constexpr size_t align256(size_t x) { return (x + 255) / 256 * 256; }
 size_t commit_workspace(int R, int64_t n_ops) {
@@ -563,6 +591,19 @@ extern "C" int abkv_code_step_attention(const void* q, int64_t q_row_stride, int
                           kv_layout, num_blocks, page_size, block_table, bt_stride, seq_lens, excluded,
                           quota_per_kv_head, R, Hq, Hkv, head_dim, K_code, T, scale, workspace, workspace_bytes,
                           stream, nullptr);
+}
+
+extern "C" int abkv_paged_prefill(const void* q, int64_t q_row_stride, int64_t q_head_stride, void* out,
+                                  int64_t out_row_stride, int64_t out_head_stride, const int32_t* query_start_loc,
+                                  const void* kv_cache, int kv_layout, int64_t num_blocks, int page_size,
+                                  const int32_t* block_table, int64_t bt_stride, const int32_t* seq_lens, int R,
+                                  int Hq, int Hkv, int head_dim, int max_query_len, int T, float scale,
+                                  void* workspace, size_t workspace_bytes, void* stream) {
+  if (max_query_len <= 0) return ABKV_ERR_INVALID_ARG;
+  return code_step_launch(q, q_row_stride, q_head_stride, out, out_row_stride, out_head_stride, query_start_loc,
+                          kv_cache, kv_layout, num_blocks, page_size, block_table, bt_stride, seq_lens, nullptr,
+                          nullptr, R, Hq, Hkv, head_dim, 0, T, scale, workspace, workspace_bytes, stream, nullptr,
+                          max_query_len);
 }
 
 extern "C" size_t abkv_code_step_compact_workspace_size(int num_requests, int64_t n_ops) {
@@ -632,15 +673,18 @@ int code_step_launch(const void* q, int64_t q_row_stride, int64_t q_head_stride,
                      const int32_t* block_table, int64_t bt_stride, const int32_t* seq_lens,
                      const int32_t* excluded, const int32_t* quota_per_kv_head, int R, int Hq,
                      int Hkv, int head_dim, int K_code, int T, float scale, void* workspace,
-                     size_t workspace_bytes, void* stream, const CommitArgs* commit) {
-  if (!q || !out || !q_start || !kv_cache || !block_table || !seq_lens || !quota_per_kv_head)
+                     size_t workspace_bytes, void* stream, const CommitArgs* commit, int causal_max_qlen) {
+  const bool causal = causal_max_qlen > 0;  // abkv_paged_prefill: no quotas, no exclusion, no copies
+  if (!q || !out || !q_start || !kv_cache || !block_table || !seq_lens || (!causal && !quota_per_kv_head))
     return ABKV_ERR_INVALID_ARG;
   if (R <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv != 0 || T <= 0 || num_blocks <= 0 || bt_stride <= 0 ||
       !(scale > 0.f) || (kv_layout != 0 && kv_layout != 1))
     return ABKV_ERR_INVALID_ARG;
-  if (head_dim != kD || Hq > kMaxHeads || R > 65535 || K_code <= 0 || K_code % kBM || page_size <= 0 ||
-      page_size % 16 || 2 * num_blocks > INT32_MAX || K_code > T)
+  if (causal && (excluded || commit || causal_max_qlen > T)) return ABKV_ERR_INVALID_ARG;
+  if (head_dim != kD || Hq > kMaxHeads || R > 65535 || page_size <= 0 || page_size % 16 ||
+      2 * num_blocks > INT32_MAX)
     return ABKV_ERR_UNSUPPORTED;
+  if (!causal && (K_code <= 0 || K_code % kBM || K_code > T)) return ABKV_ERR_UNSUPPORTED;
   if (q_row_stride <= 0 || q_head_stride <= 0 || out_row_stride % 8 || out_head_stride % 8 ||
       out_row_stride <= 0 || out_head_stride <= 0)
     return ABKV_ERR_INVALID_ARG;
@@ -675,11 +719,12 @@ int code_step_launch(const void* q, int64_t q_row_stride, int64_t q_head_stride,
   prm.o_ss = out_row_stride;
   prm.err = static_cast<int32_t*>(workspace);
   const int G = Hq / Hkv;
-  for (int h = 0; h < Hq; ++h) {
+  for (int h = 0; h < Hq && !causal; ++h) {
     const int qq = quota_per_kv_head[h / G];
     if (qq < 0 || qq > K_code) return ABKV_ERR_INVALID_ARG;
     prm.quota[h] = qq;
   }
+  prm.causal = causal ? 1 : 0;
   prm.H = Hq;
   prm.Hkv = Hkv;
   prm.G = G;
@@ -707,7 +752,7 @@ int code_step_launch(const void* q, int64_t q_row_stride, int64_t q_head_stride,
     prm.row_bytes = (int64_t)Hkv * kD * 2;
     prm.ctas_per_req = (K_code / kBM) * Hkv * prm.npairs;
   }
-  dim3 grid(K_code / kBM, Hkv * prm.npairs, R);
+  dim3 grid(causal ? (causal_max_qlen + kBM - 1) / kBM : K_code / kBM, Hkv * prm.npairs, R);
   codestep_kernel<<<grid, kThreads, kSmemBytes, reinterpret_cast<cudaStream_t>(stream)>>>(prm);
   if (cudaGetLastError() != cudaSuccess) return ABKV_ERR_CUDA;
   return ABKV_OK;

@@ -393,8 +393,86 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const __grid_constant_
   const char* src = p.src[t] + (o * p.src_rows + r) * p.row_bytes;
   for (int64_t v = lane; v < vecs; v += 32) st_cg(dst + 16 * v, ld_cg(src + 16 * v));
 }
+// New rows into the paged cache (vLLM's reshape_and_cache_flash, which the backend's
+// AttentionImpl.forward runs before attention): token t's K and V rows ([Hkv][D], each head's D
+// contiguous, free token / head strides) go to slot slot_mapping[t] = block * page + offset of
+// the cache; a negative slot (padding) is skipped.  One warp per (token, K|V), 16-byte vectors.
+struct StoreParams {
+  const char* src[2];   // key, value
+  int64_t src_row[2];   // bytes between tokens
+  int64_t src_head[2];  // bytes between heads
+  const int64_t* slots;
+  char* kv;
+  int32_t* err;
+  int64_t blk_stride, half_stride, row_bytes, num_slots;
+  int T, page, head_vecs;  // head_vecs: 16-byte vectors per head row (D * 2 / 16)
+};
+
+__global__ void __launch_bounds__(256) store_kv_kernel(const __grid_constant__ StoreParams p) {
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= 2 * (int64_t)p.T) return;
+  const int t = (int)(warp >> 1), half = (int)(warp & 1);
+  const int64_t slot = __ldg(p.slots + t);
+  if (slot < 0) return;
+  if (slot >= p.num_slots) {
+    if (lane == 0) set_error(p.err, ABKV_DEVERR_ROW_OOB);
+    return;
+  }
+  char* dst = p.kv + (slot / p.page) * p.blk_stride + half * p.half_stride + (slot % p.page) * p.row_bytes;
+  const char* src = p.src[half] + t * p.src_row[half];
+  const int64_t vecs = p.row_bytes >> 4;
+  for (int64_t v = lane; v < vecs; v += 32) {
+    const int64_t h = v / p.head_vecs, w = v - h * p.head_vecs;
+    st_cg(dst + 16 * v, ld_cg(src + h * p.src_head[half] + 16 * w));
+  }
+}
 }  // namespace
 }  // namespace abkv
+
+extern "C" int abkv_store_kv(const void* key, int64_t key_row_stride, int64_t key_head_stride, const void* value,
+                             int64_t value_row_stride, int64_t value_head_stride, void* kv_cache, int kv_layout,
+                             int64_t num_blocks, int page_size, int num_kv_heads, int head_dim,
+                             const int64_t* slot_mapping, int T, void* workspace, size_t workspace_bytes,
+                             void* stream) {
+  if (T < 0 || !kv_cache || num_blocks <= 0 || page_size <= 0 || num_kv_heads <= 0 || head_dim <= 0 ||
+      (kv_layout != 0 && kv_layout != 1))
+    return ABKV_ERR_INVALID_ARG;
+  if (!workspace || workspace_bytes < kWsHeader || (reinterpret_cast<uintptr_t>(workspace) & 255))
+    return ABKV_ERR_WORKSPACE;
+  if (T == 0) return ABKV_OK;
+  if (!key || !value || !slot_mapping || key_row_stride <= 0 || value_row_stride <= 0 || key_head_stride <= 0 ||
+      value_head_stride <= 0)
+    return ABKV_ERR_INVALID_ARG;
+  // 16-byte vectors: every head row starts on a 16-byte boundary
+  if ((head_dim * 2) % 16 || ((key_row_stride | key_head_stride | value_row_stride | value_head_stride) * 2) % 16 ||
+      ((reinterpret_cast<uintptr_t>(key) | reinterpret_cast<uintptr_t>(value) |
+        reinterpret_cast<uintptr_t>(kv_cache)) & 15))
+    return ABKV_ERR_UNSUPPORTED;
+  StoreParams prm;
+  std::memset(&prm, 0, sizeof(prm));
+  prm.src[0] = static_cast<const char*>(key);
+  prm.src[1] = static_cast<const char*>(value);
+  prm.src_row[0] = key_row_stride * 2;
+  prm.src_row[1] = value_row_stride * 2;
+  prm.src_head[0] = key_head_stride * 2;
+  prm.src_head[1] = value_head_stride * 2;
+  prm.slots = slot_mapping;
+  prm.kv = static_cast<char*>(kv_cache);
+  prm.err = static_cast<int32_t*>(workspace);
+  prm.row_bytes = (int64_t)num_kv_heads * head_dim * 2;
+  const int64_t page_bytes = prm.row_bytes * page_size;
+  prm.blk_stride = kv_layout ? page_bytes : 2 * page_bytes;  // [nb][2][page] or [2][nb][page]
+  prm.half_stride = kv_layout ? num_blocks * page_bytes : page_bytes;
+  prm.num_slots = num_blocks * page_size;
+  prm.T = T;
+  prm.page = page_size;
+  prm.head_vecs = head_dim * 2 / 16;
+  const int64_t threads = 2 * (int64_t)T * 32;
+  store_kv_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(prm);
+  if (cudaGetLastError() != cudaSuccess) return ABKV_ERR_CUDA;
+  return ABKV_OK;
+}
 
 extern "C" int abkv_gather_rows(const void* const* src, void* const* dst, int num_tensors, int64_t outer,
                                 int64_t src_rows, int64_t dst_rows, int64_t row_bytes, const int64_t* keep,

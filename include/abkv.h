@@ -355,6 +355,26 @@ int abkv_gather_rows(const void* const* src, void* const* dst, int num_tensors,
                      int64_t row_bytes, const int64_t* keep, void* workspace,
                      size_t workspace_bytes, void* stream);
 
+/* The step's new K / V rows into the paged cache, before attention: the
+ * slot write vLLM's attention backend makes at the start of
+ * AttentionImpl.forward (reshape_and_cache_flash in vLLM 0.13.0, the
+ * third-party version the overlay pins, requirements.txt:10-12; the
+ * overlay's forward then reads the rows back through the block table,
+ * compresslm_packed_kv.py:744-761).  Token t's rows key[t] / value[t]
+ * ([num_kv_heads][head_dim] bf16, element strides row / head, each head's
+ * head_dim contiguous) go to slot s = slot_mapping[t] (DEVICE int64):
+ * block s / page_size, offset s % page_size, in either paged layout.  A
+ * negative slot (padding) is skipped; a slot past the cache sets
+ * ABKV_DEVERR_ROW_OOB and is skipped.  Needs 16-byte aligned bases and
+ * strides (ABKV_ERR_UNSUPPORTED otherwise). */
+int abkv_store_kv(const void* key, int64_t key_row_stride,
+                  int64_t key_head_stride, const void* value,
+                  int64_t value_row_stride, int64_t value_head_stride,
+                  void* kv_cache, int kv_layout, int64_t num_blocks,
+                  int page_size, int num_kv_heads, int head_dim,
+                  const int64_t* slot_mapping, int T, void* workspace,
+                  size_t workspace_bytes, void* stream);
+
 /* ========================================================================
  * 4. Pause-token prefill attention with the compressed-cache mask (tcgen05).
  *
@@ -440,6 +460,37 @@ int abkv_code_step_attention(const void* q, int64_t q_row_stride,
                              int Hkv, int head_dim, int K_code, int T,
                              float scale, void* workspace,
                              size_t workspace_bytes, void* stream);
+
+/* Causal attention of ragged query rows over the paged cache: the prompt
+ * prefill, chunked prefill and mixed prefill/decode steps of a CompressLM
+ * KV-cache group.  Replaces the causal branch of
+ * PackedKVSidecar._attend_request_vectorized with no sidecar pages
+ * (third_party/vllm_overlay/vllm/v1/worker/compresslm_packed_kv.py:700-707,
+ * reached from override_attention :371-399 when query_len > 1) and the
+ * stock backend's causal paged prefill of a KV-cache group
+ * (gpu_model_runner.py:1872-1886 metadata, causal=True).
+ * Request r's query rows are query_start_loc[r] .. query_start_loc[r+1]-1
+ * (qlen rows; their keys are already at cache rows [seq_len - qlen,
+ * seq_len)); row i attends to cache rows [0, seq_len - qlen + i + 1) of its
+ * block-table row, every query head alike (GQA: head h reads KV head
+ * h / (Hq / Hkv)).  Same kernel as abkv_code_step_attention in its causal
+ * mode (tcgen05, 128 query rows x 2 heads per CTA, 64-key tiles).
+ * query_start_loc: DEVICE [R+1] int32; max_query_len: >= every qlen (the
+ * grid has ceil(max_query_len / 128) query tiles per request; a longer
+ * request sets ABKV_DEVERR_RANGE and its rows past the grid stay
+ * unwritten).  Other arguments as abkv_code_step_attention; seq_lens[r] in
+ * [qlen, min(bt_stride * page, 131072)].  Rows of out that belong to no
+ * request are not written. */
+int abkv_paged_prefill(const void* q, int64_t q_row_stride,
+                       int64_t q_head_stride, void* out,
+                       int64_t out_row_stride, int64_t out_head_stride,
+                       const int32_t* query_start_loc, const void* kv_cache,
+                       int kv_layout, int64_t num_blocks, int page_size,
+                       const int32_t* block_table, int64_t bt_stride,
+                       const int32_t* seq_lens, int R, int Hq, int Hkv,
+                       int head_dim, int max_query_len, int T, float scale,
+                       void* workspace, size_t workspace_bytes,
+                       void* stream);
 
 /* The code step fused with the compaction that follows it in the block
  * boundary flow (CompressLMProcessor._compact_response_content,

@@ -17,7 +17,8 @@ Two numpy forms: ``decode_reference`` reproduces those roundings,
 ``sidecar_decode_torch`` is the same computation as torch CPU ops (used to
 time the reference's CPU path in bench.py).  ``codestep_exact`` (float64) and
 ``sidecar_codestep_torch`` (torch CPU, the reference's op sequence) restate the
-noncausal code step of _attend_request_vectorized (:648-741).
+noncausal code step of _attend_request_vectorized (:648-741); ``paged_causal_exact``
+(float64) its causal branch for ragged query rows (:700-707).
 """
 from __future__ import annotations
 
@@ -133,6 +134,36 @@ def codestep_exact(qrows, kv, block_table, seq_lens, K, quota_per_kv_head, scale
             s = (qrows[r * K:(r + 1) * K, h].astype(np.float64) @ kh.T) * scale
             e = np.exp(s - s.max(axis=1, keepdims=True))
             out[r * K:(r + 1) * K, h] = (e / e.sum(axis=1, keepdims=True)) @ vh
+    return out
+
+
+def paged_causal_exact(qrows, kv, block_table, seq_lens, query_start, scale, page) -> np.ndarray:
+    """Causal attention of ragged query rows over the paged cache in float64: the causal branch of
+    PackedKVSidecar._attend_request_vectorized without sidecar pages (compresslm_packed_kv.py:
+    700-707, per request from override_attention :371-399).  Request r's queries are rows
+    query_start[r] .. query_start[r + 1] - 1 of qrows ([T, Hq, D]); with qlen of them and
+    prefix = seq_len - qlen, query i sees cache rows [0, prefix + i + 1).  Rows of qrows outside
+    every request stay zero.  Returns [T, Hq, D]."""
+    T, Hq, D = qrows.shape
+    Hkv = kv.shape[3]
+    G = Hq // Hkv
+    out = np.zeros((T, Hq, D))
+    for r, s_len in enumerate(seq_lens):
+        s_len = int(s_len)
+        q0, q1 = int(query_start[r]), int(query_start[r + 1])
+        qlen = q1 - q0
+        if qlen <= 0:
+            continue
+        k, v = _gather(kv, block_table[r], s_len, page)
+        prefix = s_len - qlen
+        hidden = np.arange(s_len)[None, :] >= (prefix + np.arange(1, qlen + 1))[:, None]   # [qlen, S]
+        for h in range(Hq):
+            kh = k[:, h // G, :].astype(np.float64)
+            vh = v[:, h // G, :].astype(np.float64)
+            sc = (qrows[q0:q1, h].astype(np.float64) @ kh.T) * scale
+            sc[hidden] = -np.inf
+            e = np.exp(sc - sc.max(axis=1, keepdims=True))
+            out[q0:q1, h] = (e / e.sum(axis=1, keepdims=True)) @ vh
     return out
 
 

@@ -90,3 +90,38 @@ def load_prefill_bwd(name: str):
     z0 = np.load(GOLDEN / f"prefill_{name}.npz")
     dout = prefill_dout(int(z0["seed"]), g["B"], g["H"], g["S0"], g["D"])
     return g, dout, z["rows"], z["dq_rows"], z["dk_rows"], z["dv_rows"]
+
+
+def causal_cases():
+    return sorted(p.stem[len("causal_"):] for p in GOLDEN.glob("causal_*.npz"))
+
+
+def load_causal(name: str):
+    """-> (case, qrows [T,Hq,D], query_start [R+1], rows kept, reference output at those rows)."""
+    from tests.golden.make_golden import causal_query_rows
+
+    z = np.load(GOLDEN / f"causal_{name}.npz")
+    case = paged_case(int(z["seed"]), z["seq_lens"], num_q_heads=int(z["num_q_heads"]),
+                      num_kv_heads=int(z["num_kv_heads"]), head_dim=128, page=int(z["page"]))
+    qlens = z["query_lens"].astype(np.int64)
+    qstart = np.concatenate([[0], np.cumsum(qlens)]).astype(np.int32)
+    qrows = causal_query_rows(int(z["seed"]), int(qlens.sum()), int(z["num_q_heads"]))
+    return case, qrows, qstart, z["rows"], from_bits(z["out_bits"])
+
+
+def qmask_cases():
+    return sorted(p.stem[len("qmask_"):] for p in GOLDEN.glob("qmask_*.npz"))
+
+
+def load_qmask(name: str):
+    """-> (K, quotas, requests [(query_len, seq_len, spans, excluded)], {quota: reference ragged mask})
+    of the reference's build_layer_quota_masks (tests/golden/qmask_*.npz)."""
+    z = np.load(GOLDEN / f"qmask_{name}.npz")
+    K = int(z["K"])
+    reqs = []
+    for q, s_, own, ex in zip(z["query_lens"], z["seq_lens"], z["own_span"], z["excluded"]):
+        q, s_ = int(q), int(s_)
+        reqs.append((q, s_, [(s_ - K, s_)] if own else [], (int(ex[0]), int(ex[1])) if ex[1] > ex[0] else None))
+    masks = {int(q): np.unpackbits(z[f"mask_{int(q)}"])[: int(z[f"size_{int(q)}"])].astype(bool)
+             for q in z["quotas"]}
+    return K, [int(q) for q in z["quotas"]], reqs, masks

@@ -252,3 +252,62 @@ def test_codestep_fused_compaction_equals_code_step_then_executor():
     with pytest.raises(AbkvError):
         codestep.code_step_attention_compact(q, kv.clone(), btd, sl, qs, ops=ops, op_offsets=off[:-1] + [0],
                                              quota_per_kv_head=quotas, k_max=K, replay_tail=0, workspace=ws)
+
+
+from oracle.decode_ref import paged_causal_exact  # noqa: E402
+from tests.goldens import causal_cases, load_causal  # noqa: E402
+
+
+@pytest.mark.parametrize("name", causal_cases())
+def test_paged_prefill_matches_reference_golden(name):
+    """abkv_paged_prefill (the code-step kernel's causal mode) on ragged requests -- fresh prompts,
+    chunks after a prefix, a single decode row -- against the reference's causal
+    _attend_request_vectorized rows and the float64 oracle; both paged layouts give the same bits;
+    padding rows of no request stay untouched."""
+    case, qrows, qstart, rows, ref = load_causal(name)
+    Hkv = case.kv.shape[3]
+    T = qrows.shape[0]
+    q = torch.zeros((T + 5, qrows.shape[1], 128), dtype=torch.bfloat16, device="cuda")
+    q[:T] = torch.from_numpy(qrows).to(torch.bfloat16).cuda()
+    kv = torch.from_numpy(case.kv).to(torch.bfloat16).cuda()
+    bt = torch.from_numpy(case.block_table).cuda()
+    sl = torch.from_numpy(case.seq_lens).cuda()
+    qs = torch.from_numpy(qstart).cuda()
+    max_q = int(np.diff(qstart).max())
+    ws = Workspace()
+    out = torch.full_like(q, float("nan"))
+    codestep.paged_prefill(q, kv, bt, sl, qs, max_query_len=max_q, num_kv_heads=Hkv, scale=case.scale, out=out,
+                           workspace=ws)
+    torch.cuda.synchronize()
+    assert ws.read_error() == 0
+    assert torch.isnan(out[T:].float()).all(), "rows of no request were written"
+    got = out[:T].float().cpu().numpy()
+    assert np.isfinite(got).all()
+    exact = paged_causal_exact(qrows, case.kv, case.block_table, case.seq_lens, qstart, case.scale, case.page)
+    se, _ = report(name, got, exact)
+    assert se["max_abs"] <= ATOL_EXACT and se["mean_abs"] <= MEAN_EXACT
+    assert_relative(se, name)
+    _, sr = report(f"{name} (reference rows)", got[rows], exact[rows], ref)
+    assert sr["max_abs"] <= ATOL_REF
+    out_fa = codestep.paged_prefill(q, kv.transpose(0, 1).contiguous(), bt, sl, qs, max_query_len=max_q,
+                                    num_kv_heads=Hkv, scale=case.scale)
+    assert torch.equal(out_fa[:T], out[:T])
+
+
+def test_paged_prefill_understated_max_query_len_is_flagged():
+    """A request longer than max_query_len sets ABKV_DEVERR_RANGE; the rows the grid covers are still
+    right and the rows past it are left unwritten."""
+    case, qrows, qstart, rows, ref = load_causal("g3_page32")
+    q = torch.from_numpy(qrows).to(torch.bfloat16).cuda()
+    kv = torch.from_numpy(case.kv).to(torch.bfloat16).cuda()
+    args = (kv, torch.from_numpy(case.block_table).cuda(), torch.from_numpy(case.seq_lens).cuda(),
+            torch.from_numpy(qstart).cuda())
+    ws = Workspace()
+    full = codestep.paged_prefill(q, *args, max_query_len=250, num_kv_heads=2, scale=case.scale, workspace=ws)
+    assert ws.read_error() == 0
+    short = torch.full_like(q, float("nan"))
+    codestep.paged_prefill(q, *args, max_query_len=128, num_kv_heads=2, scale=case.scale, out=short, workspace=ws)
+    assert ws.read_error() & 0x10  # ABKV_DEVERR_RANGE
+    last = int(qstart[2])  # request 2 has 250 rows: its first 128 are computed, the rest are not
+    assert torch.equal(short[:last + 128], full[:last + 128])
+    assert torch.isnan(short[last + 128:].float()).all()

@@ -112,3 +112,18 @@ def test_prefill_backward_oracle_matches_reference(name):
     dq, dk, dv = masked_attention_grad(g["q"], g["k"], g["v"], g["mask"], 1.0 / np.sqrt(g["D"]), dout)
     for got, ref in ((dq[:, :, rows], dq_r), (dk[:, :, rows], dk_r), (dv[:, :, rows], dv_r)):
         assert np.abs(got - ref).max() <= 1e-5 * max(1.0, np.abs(ref).max())
+
+
+from oracle.decode_ref import paged_causal_exact  # noqa: E402
+from tests.goldens import causal_cases, load_causal  # noqa: E402
+
+
+@pytest.mark.parametrize("name", causal_cases())
+def test_paged_causal_oracle_matches_reference(name):
+    """The float64 restatement of the causal branch of _attend_request_vectorized against the
+    reference's own outputs (bf16 scores and weights there): within its rounding budget."""
+    case, qrows, qstart, rows, ref = load_causal(name)
+    ex = paged_causal_exact(qrows, case.kv, case.block_table, case.seq_lens, qstart, case.scale, case.page)
+    assert np.isfinite(ref).all()
+    assert np.abs(ex[rows] - ref).max() < 3e-2
+    assert np.abs(ex[rows] - ref).mean() < 2e-3
