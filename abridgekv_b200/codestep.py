@@ -184,7 +184,7 @@ def code_step_attention_compact(query: torch.Tensor, kv_cache: torch.Tensor, blo
     Ordering: the reference finishes a block (and plans its compaction) right after the code step
     only when the configuration has no replay tail -- ``CompressLMProcessor.update_after_step``
     calls ``_finish_block`` at the end of the code role only when the block has no replay positions
-    (third_party/vllm_overlay/vllm/v1/core/compresslm/processor.py:250-262); with a replay tail the
+    (third_party/vllm_overlay/vllm/v1/core/compresslm/processor.py:236-255); with a replay tail the
     block finishes after the replay step, whose queries still read the uncompacted rows.  So the
     caller states ``replay_tail`` (``CompressLMConfig.replay_tail``) and any value but 0 is refused;
     the ops are those the planner's ``finish_block`` produced for the block, planned before this

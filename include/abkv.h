@@ -17,7 +17,9 @@
  *     workspace whose minimum size is reported by the matching *_workspace_size
  *     function.  Byte 0..3 of every workspace is a device error word that the
  *     kernels OR error bits into (read it with abkv_workspace_error).
- *   - Entry points are reentrant: no global mutable state.
+ *   - Entry points are reentrant: no global mutable state, except the fixed
+ *     scratch array of abkv_decode_noalloc (whose calls must be serialised;
+ *     see there).
  */
 #ifndef ABKV_H_
 #define ABKV_H_
@@ -512,7 +514,7 @@ int abkv_paged_prefill(const void* q, int64_t q_row_stride,
  *   - ordering: the block finishes directly after its code step, i.e. the
  *     configuration has no replay tail (replay_tail == 0; the reference calls
  *     _finish_block at the end of the code role only when the block has no
- *     replay positions, processor.py:250-262), and the ops are the ones the
+ *     replay positions, processor.py:236-255), and the ops are the ones the
  *     planner's finish_block produced for that block before this launch;
  *   - ownership: request r's ops read and write only pages of request r's
  *     own block-table row, and no other request of the launch reads those

@@ -3,7 +3,7 @@
 * The reference plans a block's compaction right after its code step only without a replay tail
   (CompressLMProcessor.update_after_step calls _finish_block at the end of the code role only when
   the block has no replay positions, third_party/vllm_overlay/vllm/v1/core/compresslm/
-  processor.py:250-262), so code_step_attention_compact refuses any other replay_tail before it
+  processor.py:236-255), so code_step_attention_compact refuses any other replay_tail before it
   touches a device.
 * Ownership: the copy ops the planner's finish_block produces for a request stay inside that
   request's own pages; ops that reach another request's pages, or write pages another request
