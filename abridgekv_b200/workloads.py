@@ -164,11 +164,12 @@ def config5_rows(num_seqs: int = 256, seed: int = 0, prompt: int = 256, blocks: 
 
 
 def qwen3_decode_workload(config: int = 2, *, num_seqs: int | None = None, device="cuda", seed: int = 0,
-                          seq_slice: slice | None = None, kv_heads: slice | None = None) -> DecodeWorkload:
+                          seq_slice: slice | np.ndarray | None = None, kv_heads: slice | None = None
+                          ) -> DecodeWorkload:
     """Config 2 / 3 / 5 decode workloads at Qwen3-4B shape.
 
-    seq_slice picks this rank's sequences (sequence sharding); kv_heads picks this
-    rank's KV heads (KV-head sharding)."""
+    seq_slice picks this rank's sequences (sequence sharding: a slice or an index array);
+    kv_heads picks this rank's KV heads (KV-head sharding)."""
     geo = dict(QWEN3_4B)
     if config == 2:
         rows = config2_rows(num_seqs or 64, seed)
@@ -192,5 +193,6 @@ def qwen3_decode_workload(config: int = 2, *, num_seqs: int | None = None, devic
     return build_decode_workload(
         f"config{config}", quotas, rows, num_q_heads=hq, num_kv_heads=hkv,
         head_dim=geo["head_dim"], device=device, seed=seed,
-        meta={"config": config, "seq_slice": str(seq_slice), "kv_heads": str(kv_heads)},
+        meta={"config": config, "kv_heads": str(kv_heads),
+              "seqs": str(seq_slice) if not isinstance(seq_slice, np.ndarray) else f"{len(seq_slice)} indexed"},
     )

@@ -205,14 +205,14 @@ def run_reference(args, rank: int, world: int) -> None:
     dt = time.perf_counter() - t0
     value = args.steps / dt  # one sequence per step
     line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s (sum over GPUs)", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic", "config": config_block(world),
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
                          "sample": "1 config-2 sequence x 36 layers per step (torch CPU port of "
                                    "compresslm_packed_kv.py:564-616)"},
-        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "e2e": {"value": value, "unit": "tokens/s (sum over GPUs)", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
@@ -316,18 +316,32 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
                                   max_pages_per_seq=wl.max_pages, chunk_tokens=args.chunk_tokens, workspace=ws)
         assert all(torch.equal(out_host[l], r.cpu()) for l, r in zip(g, ref))
     assert ws.read_error() == 0
+    alg_bytes = wl.kv_bytes + wl.qo_bytes
+    headline_launches = args.steps * ((L + 55) // 56)
+    del wl, outs, host_decode, ref
+    torch.cuda.empty_cache()
+
+    # ---- config 3 at this N: the fixed 512-sequence batch, sharded by bytes (strong scaling) ----
+    strong = None
+    if not args.no_strong:
+        strong = strong_decode(3, rank=rank, world=world, local=local, steps=args.strong_steps, warmup=3,
+                               mem_budget_gb=args.mem_budget_gb)
+    # ---- the other kernels of the path, one GPU ----
+    secondary = None
+    if world == 1 and not args.no_secondary:
+        secondary = run_secondary(args)
 
     if rank != 0:
         return
     peak, peak_kind = measured_hbm_peak()
-    alg_bytes = wl.kv_bytes + wl.qo_bytes
     achieved = alg_bytes / (mean_launch_ms / 1e3) / 1e9
     traffic = profiled_traffic("decode_split_kernel")
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline_decode(_config2_rows_for_cpu(), budget_s=args.cpu_budget)
     line = {
-        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "metric": METRIC, "value": value, "unit": "tokens/s (sum over GPUs)", "value_per_gpu": value / world,
+        "unit_per_gpu": "tokens/s/GPU", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": total_ms_max / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": config_block(world, args.chunk_tokens, args.num_seqs),
@@ -337,49 +351,54 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
                      "traffic": traffic, "algorithmic_bytes_per_launch": alg_bytes,
                      "mean_launch_ms": mean_launch_ms},
         "cpu_baseline": cpu,
-        "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "steps": e2e_steps},
-        "gpu_launches": args.steps * ((L + 55) // 56),
+        "e2e": {"value": e2e_value, "unit": "tokens/s (sum over GPUs)", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "steps": e2e_steps},
+        "gpu_launches": headline_launches,
         "clocks": clocks,
+        "strong_scaling": strong,
+        "secondary": secondary,
     }
     print(json.dumps(line), flush=True)
 
 
-def run_scaling(args, rank: int, world: int, local: int) -> None:
-    """BASELINE configs 3 and 5 (strong scaling: the global batch is fixed).
+def strong_decode(cfg: int, *, rank: int, world: int, local: int, steps: int, warmup: int, chunk_tokens: int = 0,
+                  mem_budget_gb: float = 130.0, shard: str = "seq", gather: str = "fused",
+                  num_seqs: int | None = None) -> dict:
+    """One strong-scaling decode measurement (the global batch is fixed); every rank calls it.
 
-    config 3: 512 sequences with generated lengths log-uniform in [2K, 32K]
-      (247.8 GB of K/V), sequence-sharded; a rank whose share exceeds
-      --mem-budget-gb decodes it in waves (each wave's caches are built, timed
-      and freed in turn) and one step = one decode step of every wave.
-    config 5: 256 sequences, quota 128 in every layer, 63 compressed blocks +
-      tail (323.7 GB).  --shard seq: whole sequences per rank, one 36-layer
-      launch per step.  --shard kv: every rank holds KV heads
-      [r*8/W, (r+1)*8/W) of all sequences; per layer one decode launch of its
-      heads whose epilogue all-gathers the [B, 32, 128] outputs into every
-      rank's buffer over NVLink (--gather fused, abkv_decode_gather), or the
-      plain decode followed by an NCCL all-gather (--gather nccl)."""
+    config 3: 512 sequences with generated lengths log-uniform in [2K, 32K] (247.8 GB of K/V),
+      sequence-sharded by bytes (parallel.shard_by_bytes: every rank reads about the same bytes per
+      step); a rank whose share exceeds mem_budget_gb decodes it in waves (each wave's caches are
+      built, timed and freed in turn) and one step = one decode step of every wave.
+    config 5: 256 sequences, quota 128 in every layer, 63 compressed blocks + tail (323.7 GB).
+      shard "seq": whole sequences per rank (by bytes), one 36-layer launch per step.  shard "kv":
+      every rank holds KV heads [r*8/W, (r+1)*8/W) of all sequences; per layer one decode launch of
+      its heads whose epilogue all-gathers the [B, 32, 128] outputs into every rank's buffer over
+      NVLink (gather "fused", abkv_decode_gather), or the plain decode followed by an NCCL
+      all-gather (gather "nccl").
+    Returns (meaningful on rank 0) value = sequences / max-over-ranks ms per step, the roofline of
+    the per-GPU mean bytes, the waves of rank 0 and the byte imbalance of the shards."""
     from abridgekv_b200 import decode, parallel
-    from abridgekv_b200.workloads import QWEN3_4B, config3_rows, config5_rows, qwen3_decode_workload
+    from abridgekv_b200.workloads import (QWEN3_4B, SCHEDULE_PERLAYER_MEAN128, config3_rows, config5_rows,
+                                          qwen3_decode_workload)
     from abridgekv_b200.workspace import Workspace
 
     dev = torch.device("cuda", local)
-    cfg = args.config
-    n_global = args.num_seqs if args.num_seqs != 64 else (512 if cfg == 3 else 256)
+    n_global = num_seqs or (512 if cfg == 3 else 256)
     rows_all = (config3_rows if cfg == 3 else config5_rows)(n_global, 0)
     hkv, hd = QWEN3_4B["num_kv_heads"], QWEN3_4B["head_dim"]
-    kv_mode = cfg == 5 and args.shard == "kv"
+    kv_mode = cfg == 5 and shard == "kv"
     heads = parallel.kv_head_shard(hkv, world, rank) if kv_mode else None
-    seqs = slice(0, n_global) if kv_mode else parallel.shard_sequences(n_global, world, rank)
-    sched = (128,) * 36 if cfg == 5 else None
-    from abridgekv_b200.workloads import SCHEDULE_PERLAYER_MEAN128
-    quotas = sched or SCHEDULE_PERLAYER_MEAN128
+    quotas = (128,) * 36 if cfg == 5 else SCHEDULE_PERLAYER_MEAN128
     h_local = hkv // world if kv_mode else hkv
     per_seq = np.zeros(n_global)
     for q in quotas:
         per_seq += rows_all[q] * h_local * hd * 4
-    mine = np.arange(n_global)[seqs]
-    budget = args.mem_budget_gb * 1e9
+    shards = [np.arange(n_global)] * world if kv_mode else \
+        [parallel.shard_by_bytes(per_seq, world, r) for r in range(world)]
+    loads = np.array([per_seq[s].sum() for s in shards])
+    mine = shards[rank]
+    budget = mem_budget_gb * 1e9
     waves, cur, acc = [], [], 0.0
     for i in mine:
         if cur and acc + per_seq[i] > budget:
@@ -391,19 +410,18 @@ def run_scaling(args, rank: int, world: int, local: int) -> None:
         waves.append(cur)
     if kv_mode and len(waves) > 1:
         raise SystemExit(f"config 5 KV-head sharding needs {per_seq.sum() / 1e9:.1f} GB per rank "
-                         f"(> --mem-budget-gb {args.mem_budget_gb}); use more GPUs")
+                         f"(> --mem-budget-gb {mem_budget_gb}); use more GPUs")
     ws = Workspace(dev)
     stream = torch.cuda.current_stream(dev)
     wave_ms, alg_bytes, launches, waves_info = [], 0, 0, []
     head_gather = None
-    for wi, idx in enumerate(waves):
-        sl = slice(idx[0], idx[-1] + 1)
-        assert idx == list(range(sl.start, sl.stop))
-        wl = qwen3_decode_workload(cfg, num_seqs=n_global, device=dev, seed=0, seq_slice=sl, kv_heads=heads)
+    for idx in waves:
+        wl = qwen3_decode_workload(cfg, num_seqs=n_global, device=dev, seed=0,
+                                   seq_slice=None if kv_mode else np.asarray(idx), kv_heads=heads)
         outs = [torch.empty_like(q) for q in wl.queries]
         gathered = [None] * wl.num_layers
 
-        if kv_mode and args.gather == "fused":
+        if kv_mode and gather == "fused":
             from abridgekv_b200.gather import HeadGather
             head_gather = HeadGather(wl.num_layers, wl.num_seqs, wl.num_q_heads * world, device=dev)
 
@@ -411,37 +429,36 @@ def run_scaling(args, rank: int, world: int, local: int) -> None:
                 for l in range(wl.num_layers):
                     head_gather.decode([l], [wl.queries[l]], [wl.kv_caches[l]], [wl.block_tables[l]],
                                        [wl.seq_lens[l]], max_pages_per_seq=wl.max_pages,
-                                       chunk_tokens=args.chunk_tokens, workspace=ws)
+                                       chunk_tokens=chunk_tokens, workspace=ws)
             per_step = wl.num_layers
         elif kv_mode:
             def step():
                 for l in range(wl.num_layers):
                     decode.paged_decode([wl.queries[l]], [wl.kv_caches[l]], [wl.block_tables[l]],
                                         [wl.seq_lens[l]], outputs=[outs[l]], max_pages_per_seq=wl.max_pages,
-                                        chunk_tokens=args.chunk_tokens, workspace=ws)
+                                        chunk_tokens=chunk_tokens, workspace=ws)
                     gathered[l] = parallel.gather_head_outputs(outs[l])
             per_step = wl.num_layers
         else:
             def step():
                 decode.paged_decode(wl.queries, wl.kv_caches, wl.block_tables, wl.seq_lens, outputs=outs,
-                                    max_pages_per_seq=wl.max_pages, chunk_tokens=args.chunk_tokens,
-                                    workspace=ws)
+                                    max_pages_per_seq=wl.max_pages, chunk_tokens=chunk_tokens, workspace=ws)
             per_step = (wl.num_layers + 55) // 56
-        for _ in range(max(args.warmup, 3)):
+        for _ in range(max(warmup, 3)):
             step()
         torch.cuda.synchronize()
         assert ws.read_error() == 0, "device error word set during warm-up"
         barrier(world)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        for _ in range(args.steps):
+        for _ in range(steps):
             step()
         e1.record(stream)
         torch.cuda.synchronize()
         barrier(world)
-        wave_ms.append(e0.elapsed_time(e1) / args.steps)
+        wave_ms.append(e0.elapsed_time(e1) / steps)
         alg_bytes += wl.kv_bytes + wl.qo_bytes
-        launches += per_step * args.steps
+        launches += per_step * steps
         waves_info.append({"seqs": len(idx), "kv_gb": wl.kv_bytes / 1e9, "ms_per_step": wave_ms[-1]})
         if head_gather is not None:
             assert ws.read_error() == 0, "device error word set during the timed region"
@@ -457,36 +474,50 @@ def run_scaling(args, rank: int, world: int, local: int) -> None:
         t = torch.tensor([float(alg_bytes)], dtype=torch.float64, device=dev)
         dist.all_reduce(t)
         bytes_total = float(t.item())
+    peak, peak_kind = measured_hbm_peak()
+    achieved = bytes_total / world / (ms_max / 1e3) / 1e9
+    return {
+        "config": cfg, "global_batch": n_global, "n_gpus": world, "value": n_global / (ms_max / 1e3),
+        "unit": "tokens/s (sum over GPUs)", "ms_per_step": ms_max, "steps": steps,
+        "parallelism": ((f"KV-head-sharded x{world}, all-gather fused into the decode epilogue (peer stores "
+                         "over NVLink)" if gather == "fused" else f"KV-head-sharded x{world} + NCCL all-gather "
+                         "per layer") if kv_mode else f"sequence-sharded x{world} by bytes (greedy longest-first), "
+                                                      "no collective"),
+        "shard_bytes_max_over_mean": float(loads.max() / loads.mean()),
+        "waves_rank0": waves_info, "mem_budget_gb": mem_budget_gb, "gpu_launches_rank0": launches,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "note": "per-GPU mean: all ranks' algorithmic bytes / W / max time",
+                     "peak_source": peak_kind},
+    }
+
+
+def run_scaling(args, rank: int, world: int, local: int) -> None:
+    """--config 3 / 5: a strong-scaling decode line of its own (see strong_decode)."""
+    res = strong_decode(args.config, rank=rank, world=world, local=local, steps=args.steps, warmup=args.warmup,
+                        chunk_tokens=args.chunk_tokens, mem_budget_gb=args.mem_budget_gb, shard=args.shard,
+                        gather=args.gather, num_seqs=args.num_seqs if args.num_seqs != 64 else None)
     if rank != 0:
         return
-    peak, peak_kind = measured_hbm_peak()
-    value = n_global / (ms_max / 1e3)
-    achieved = bytes_total / world / (ms_max / 1e3) / 1e9
+    cfg = args.config
     line = {
-        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True, "scaling": "strong",
+        "metric": METRIC, "value": res["value"], "unit": res["unit"], "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": res["ms_per_step"], "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": f"config{cfg}: Qwen3-4B decode attention, {n_global} sequences, "
+        "config": {"workload": f"config{cfg}: Qwen3-4B decode attention, {res['global_batch']} sequences, "
                                + ("per-layer quotas 6x256/18x128/12x64, generated length log-uniform [2K,32K]"
                                   if cfg == 3 else "quota 128 in all 36 layers, 63 compressed blocks + tail"),
-                   "global_batch": n_global,
-                   "parallelism": ((f"KV-head-sharded x{world}, all-gather fused into the decode epilogue "
-                                    "(peer stores over NVLink)" if args.gather == "fused"
-                                    else f"KV-head-sharded x{world} + NCCL all-gather per layer") if kv_mode
-                                   else f"sequence-sharded x{world}, no collective"),
-                   "waves_rank0": waves_info, "mem_budget_gb": args.mem_budget_gb,
+                   "global_batch": res["global_batch"], "parallelism": res["parallelism"],
+                   "waves_rank0": res["waves_rank0"], "mem_budget_gb": res["mem_budget_gb"],
+                   "shard_bytes_max_over_mean": res["shard_bytes_max_over_mean"],
                    "l2": "inputs larger than L2; no flush"},
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "note": "per-GPU mean: all ranks' algorithmic bytes / W / max time",
-                     "peak_source": peak_kind},
-        "gpu_launches": launches,
+        "roofline": res["roofline"], "gpu_launches": res["gpu_launches_rank0"],
     }
     print(json.dumps(line), flush=True)
 
 
 # ---------------------------------------------------------------------------
 # Secondary paths (--path prefill | codestep | compaction): one GPU, one JSON line
-# with the GPU measurement of abridgekv_b200.benchmarks and the reference's CPU
+# with the GPU measurement of benchmarks.py and the reference's CPU
 # path timed on this box's host cores over a bounded sample.
 def cpu_baseline_prefill(budget_s: float) -> dict:
     """Eager dense-mask attention (the reference's _dense_mask + matmul/softmax path) in fp32
@@ -616,7 +647,7 @@ def cpu_baseline_compaction(budget_s: float) -> dict:
 
 
 def run_path(args) -> None:
-    from abridgekv_b200 import benchmarks
+    import benchmarks
 
     torch.cuda.set_device(0)
     ns = argparse.Namespace(layers=36, steps=args.steps, warmup=args.warmup, flex=args.flex, blocks=6)
@@ -648,6 +679,37 @@ def run_path(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_secondary(args) -> dict:
+    """The path's other kernels, one short measurement each on this GPU (CUDA events after 3 warm-up
+    steps) with its roofline and the reference's CPU path timed on the host cores over a bounded
+    sample: config-4 prefill (36 layers), its backward, the code step on config-2 caches + 256 code
+    rows (36 layers), and config 4's block compaction (planner + executor, 16 sequences x 36 layers)."""
+    import benchmarks
+
+    ns = argparse.Namespace(layers=36, steps=2, warmup=3, flex=False, blocks=4, batch=16)
+    budget = args.secondary_cpu_budget
+    runs = (("prefill", benchmarks.bench_prefill, cpu_baseline_prefill, 36 * ns.steps),
+            ("prefill_bwd", benchmarks.bench_prefill_bwd, cpu_baseline_prefill_bwd, 3 * 36 * ns.steps),
+            ("codestep", benchmarks.bench_codestep, cpu_baseline_codestep, 36 * ns.steps),
+            ("compaction", benchmarks.bench_compaction, cpu_baseline_compaction, None))
+    out = {}
+    for name, fn, cpu_fn, launches in runs:
+        line = fn(ns)
+        roof = dict(line["roofline"])
+        roof.setdefault("unit", line["unit"])
+        roof["peak_source"] = roof.pop("peak_kind", None) or (
+            "measured sustained cuBLAS bf16 (MEASURED_PEAKS.json)" if roof["bound"] == "tensor"
+            else "measured copy bandwidth (MEASURED_PEAKS.json hbm_gbs)")
+        keep = {k: line[k] for k in ("metric", "value", "unit", "ms_per_step", "algorithmic_tflop_per_step",
+                                     "device_ms_per_block_finish", "host_ms_executor_call", "host_ms_planner",
+                                     "bytes_per_block_finish", "forward_plus_backward_ms") if k in line}
+        keep.update({"roofline": roof, "gpu_launches": launches, "config": line.get("config"),
+                     "cpu_baseline": None if args.no_cpu_baseline else cpu_fn(budget)})
+        out[name] = keep
+        torch.cuda.empty_cache()
+    return out
+
+
 def _config2_rows_for_cpu():
     from abridgekv_b200.workloads import config2_rows
     return config2_rows(64, seed=0)
@@ -673,6 +735,12 @@ def main() -> None:
                     help="config 5 --shard kv: all-gather fused into the decode kernel, or NCCL after it")
     ap.add_argument("--mem-budget-gb", type=float, default=130.0,
                     help="configs 3/5: K/V bytes one wave may hold per GPU")
+    ap.add_argument("--strong-steps", type=int, default=10,
+                    help="timed steps of the config-3 strong-scaling block of the headline line")
+    ap.add_argument("--no-strong", action="store_true", help="omit the config-3 strong-scaling block")
+    ap.add_argument("--no-secondary", action="store_true", help="omit the secondary kernels' block (N=1)")
+    ap.add_argument("--secondary-cpu-budget", type=float, default=6.0,
+                    help="seconds of CPU baseline per secondary kernel")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -1,11 +1,12 @@
 """Secondary benchmarks (one JSON line each); the headline decode line is bench.py.
 
-    python -m abridgekv_b200.benchmarks prefill   [--layers 36] [--steps 3] [--flex]
-    python -m abridgekv_b200.benchmarks compaction [--steps 5]
-    python -m abridgekv_b200.benchmarks codestep   [--layers 36] [--steps 3]
-    python -m abridgekv_b200.benchmarks packed     [--steps 20]
-    python -m abridgekv_b200.benchmarks kvshard    [--kv-heads 1] [--seqs 256] [--chunk-tokens 0]
-    python -m abridgekv_b200.benchmarks codestep_compact [--steps 20]
+    python benchmarks.py prefill   [--layers 36] [--steps 3] [--flex]
+    python benchmarks.py compaction [--steps 5]
+    python benchmarks.py codestep   [--layers 36] [--steps 3]
+    python benchmarks.py packed     [--steps 20]
+    python benchmarks.py kvshard    [--kv-heads 1] [--seqs 256] [--chunk-tokens 0]
+    python benchmarks.py codestep_compact [--steps 20]
+    python benchmarks.py flashinfer [--steps 10]
 
 prefill    BASELINE config 4: B=16 sequences of 16 blocks x (512 content + 256 code rows)
            = 12,288 rows, Qwen3-4B attention (32 q / 8 kv heads, head_dim 128), per-layer
@@ -39,6 +40,8 @@ codestep_compact
            compaction (its first 128 code rows moved over the start of its last content block):
            code step alone, code step + the separate executor (abkv_compact), and the fused
            abkv_code_step_attention_compact, each from the host call to completion.
+flashinfer BASELINE config 2's decode step through FlashInfer's paged decode (the reference's
+           production decode library) on the same caches, against abkv_decode.
 """
 from __future__ import annotations
 
@@ -50,7 +53,7 @@ import time
 import numpy as np
 import torch
 
-from .workloads import SCHEDULE_PERLAYER_MEAN128
+from abridgekv_b200.workloads import SCHEDULE_PERLAYER_MEAN128
 
 
 def visible_pairs(N: int, C: int, K: int, quota: int, prompt_len: int = 0) -> int:
@@ -66,7 +69,7 @@ def visible_pairs(N: int, C: int, K: int, quota: int, prompt_len: int = 0) -> in
 def _peaks() -> dict:
     from pathlib import Path
 
-    p = Path(__file__).resolve().parents[1] / "MEASURED_PEAKS.json"
+    p = Path(__file__).resolve().parent / "MEASURED_PEAKS.json"
     try:
         return json.loads(p.read_text())
     except Exception:
@@ -74,7 +77,7 @@ def _peaks() -> dict:
 
 
 def bench_prefill(args) -> dict:
-    from . import prefill
+    from abridgekv_b200 import prefill
 
     B, H, Hkv, D, C, K, N = 16, 32, 8, 128, 512, 256, 16
     S0 = N * (C + K)
@@ -124,7 +127,7 @@ def bench_prefill_bwd(args) -> dict:
     """Backward of the config-4 prefill (36 layers at their quotas): abkv_prefill_masked_backward
     timed alone (the forward's output and log-sum-exp computed beforehand), and forward + backward.
     Algorithmic work: 10 x D FLOP per visible (query, key) pair per head (S recomputed, dP, dV, dK, dQ)."""
-    from . import prefill
+    from abridgekv_b200 import prefill
 
     B, H, Hkv, D, C, K, N = getattr(args, "batch", 16), 32, 8, 128, 512, 256, 16
     S0 = N * (C + K)
@@ -229,7 +232,7 @@ def bench_flex_train(q, k, v, dout, quotas, C, K, args, flops) -> dict:
 def bench_flex(q, k, v, quotas, C, K, N, args, flops) -> dict:
     from torch.nn.attention.flex_attention import create_block_mask, flex_attention
 
-    from . import prefill
+    from abridgekv_b200 import prefill
 
     B, H, S0, D = q.shape
     per = C + K
@@ -295,9 +298,9 @@ def bench_compaction(args) -> dict:
     the host has enqueued everything before the GPU reaches the first event; the reference's torch
     executor (index gather + index scatter per layer tensor, ops uploaded per batch) is timed on the
     same ops and caches."""
-    from . import compaction
-    from .planner import BlockPlanner
-    from .workspace import Workspace
+    from abridgekv_b200 import compaction
+    from abridgekv_b200.planner import BlockPlanner
+    from abridgekv_b200.workspace import Workspace
 
     C, K, page = 512, 256, 16
     quotas = (256, 128, 64)
@@ -364,8 +367,8 @@ def bench_compaction(args) -> dict:
 
 
 def bench_codestep(args) -> dict:
-    from . import codestep
-    from .workloads import QWEN3_4B, build_decode_workload, config2_rows
+    from abridgekv_b200 import codestep
+    from abridgekv_b200.workloads import QWEN3_4B, build_decode_workload, config2_rows
 
     K = 256
     rows = {q: r + K for q, r in config2_rows(64, 0).items()}
@@ -409,8 +412,8 @@ def bench_codestep(args) -> dict:
 
 
 def bench_packed(args) -> dict:
-    from .sidecar import PackedKVLayout, SidecarPool, packed_decode
-    from .workloads import BLOCK_C, build_decode_workload
+    from abridgekv_b200.sidecar import PackedKVLayout, SidecarPool, packed_decode
+    from abridgekv_b200.workloads import BLOCK_C, build_decode_workload
 
     B, L, Hq, Hkv, D, blocks = 64, 36, 32, 8, 128, 31
     quotas = [256, 128, 64, 64, 192, 64, 128, 128]
@@ -458,9 +461,9 @@ def bench_packed(args) -> dict:
 
 
 def bench_kvshard(args) -> dict:
-    from . import decode
-    from .workloads import qwen3_decode_workload
-    from .workspace import Workspace
+    from abridgekv_b200 import decode
+    from abridgekv_b200.workloads import qwen3_decode_workload
+    from abridgekv_b200.workspace import Workspace
 
     wl = qwen3_decode_workload(5, num_seqs=args.seqs, kv_heads=slice(0, args.kv_heads))
     ws = Workspace()
@@ -494,8 +497,8 @@ def bench_kvshard(args) -> dict:
 
 
 def bench_codestep_compact(args) -> dict:
-    from . import codestep, compaction
-    from .workspace import Workspace
+    from abridgekv_b200 import codestep, compaction
+    from abridgekv_b200.workspace import Workspace
 
     g = torch.Generator().manual_seed(5)
     R, K, C, Hq, Hkv, D, page, qk = 64, 256, 512, 32, 8, 128, 16, 128
@@ -562,10 +565,116 @@ def bench_codestep_compact(args) -> dict:
             "config": {"requests": R, "K": K, "C": C, "heads": f"{Hq}/{Hkv}", "quota": qk, "steps": args.steps}}
 
 
+def bench_flashinfer(args) -> dict:
+    """BASELINE config 2 decode on the same caches through FlashInfer, the library the reference's
+    vLLM backend runs decode with (patch_stock_flashinfer.py; FlashInfer 0.5.3 pinned by vLLM 0.13.0,
+    the installed one is reported), against abkv_decode:
+
+    * ``wrapper``: BatchDecodeWithPagedKVCacheWrapper over the NHD cache, planned once per quota
+      group (indptr / indices / last_page_len from the group's block table), one run per layer;
+      with ``use_tensor_cores`` False and True (its two decode paths for grouped heads);
+    * ``trtllm``: trtllm_batch_decode_with_kv_cache on the NHD cache with the block tables and
+      seq_lens directly (the decode kernel vLLM's FlashInfer backend selects on Blackwell).
+
+    Each variant: ms per 36-layer step (CUDA events), GB/s of the algorithmic bytes, and the max abs
+    difference of its outputs from abkv_decode's on every layer.  A variant that fails (import, JIT,
+    unsupported shape) records its error instead."""
+    import flashinfer
+
+    from abridgekv_b200 import decode
+    from abridgekv_b200.workloads import qwen3_decode_workload
+
+    wl = qwen3_decode_workload(2, num_seqs=64)
+    L, Hq, Hkv, D, page = wl.num_layers, wl.num_q_heads, wl.num_kv_heads, wl.head_dim, wl.page
+    scale = 1.0 / math.sqrt(D)
+    alg = wl.kv_bytes + wl.qo_bytes
+    pk = _peaks()
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / args.steps
+
+    ours = [torch.empty_like(q) for q in wl.queries]
+
+    def run_ours():
+        decode.paged_decode(wl.queries, wl.kv_caches, wl.block_tables, wl.seq_lens, outputs=ours,
+                            max_pages_per_seq=wl.max_pages)
+
+    ms = timed(run_ours)
+    res = {"abkv_decode": {"ms_per_step": ms, "gbs": alg / (ms / 1e3) / 1e9,
+                           "frac_of_hbm_peak": alg / (ms / 1e3) / 1e9 / pk["hbm_gbs"]}}
+
+    def record(name, fn, outs):
+        try:
+            t = timed(fn)
+            diff = max(float((o.float() - r.float()).abs().max()) for o, r in zip(outs, ours))
+            res[name] = {"ms_per_step": t, "gbs": alg / (t / 1e3) / 1e9,
+                         "frac_of_hbm_peak": alg / (t / 1e3) / 1e9 / pk["hbm_gbs"],
+                         "abkv_speedup": t / ms, "max_abs_diff_vs_abkv": diff}
+        except Exception as e:  # noqa: BLE001 -- a library path that does not run here is reported
+            res[name] = {"error": f"{type(e).__name__}: {e}"[:400]}
+
+    # one plan per quota group: layers of a group share the block-table tensor
+    groups: dict[int, dict] = {}
+    for l, bt in enumerate(wl.block_tables):
+        g = groups.setdefault(id(bt), {"layers": [], "bt": bt, "sl": wl.seq_lens[l]})
+        g["layers"].append(l)
+    for tc in (False, True):
+        name = f"wrapper_tensor_cores={tc}"
+        try:
+            wrappers = {}
+            for key, g in groups.items():
+                sl = g["sl"].cpu().to(torch.int64)
+                pages = (sl + page - 1) // page
+                bt = g["bt"].cpu()
+                indptr = torch.cat([torch.zeros(1, dtype=torch.int64), pages.cumsum(0)]).to(torch.int32)
+                indices = torch.cat([bt[b, :int(pages[b])] for b in range(bt.shape[0])]).to(torch.int32)
+                last = ((sl - 1) % page + 1).to(torch.int32)
+                w = flashinfer.BatchDecodeWithPagedKVCacheWrapper(
+                    torch.zeros(128 << 20, dtype=torch.uint8, device="cuda"), "NHD", use_tensor_cores=tc)
+                w.plan(indptr.cuda(), indices.cuda(), last.cuda(), Hq, Hkv, D, page, q_data_type=torch.bfloat16,
+                       kv_data_type=torch.bfloat16, sm_scale=scale)
+                wrappers[key] = w
+            fo = [torch.empty_like(q) for q in wl.queries]
+            per_layer = [wrappers[id(bt)] for bt in wl.block_tables]
+
+            def run_wrapper(per_layer=per_layer, fo=fo):
+                for l in range(L):
+                    per_layer[l].run(wl.queries[l], wl.kv_caches[l], out=fo[l])
+        except Exception as e:  # noqa: BLE001
+            res[name] = {"error": f"{type(e).__name__}: {e}"[:400]}
+            continue
+        record(name, run_wrapper, fo)
+    tr_ws = torch.zeros(256 << 20, dtype=torch.uint8, device="cuda")
+    to = [torch.empty_like(q) for q in wl.queries]
+    max_seq = int(max(int(s.max()) for s in wl.seq_lens))
+
+    def run_trtllm():
+        for l in range(L):
+            flashinfer.decode.trtllm_batch_decode_with_kv_cache(
+                wl.queries[l], wl.kv_caches[l], tr_ws, wl.block_tables[l], wl.seq_lens[l], max_seq,
+                bmm1_scale=scale, bmm2_scale=1.0, out=to[l], kv_layout="NHD")
+
+    record("trtllm_nhd", run_trtllm, to)
+    return {"metric": "config-2 decode: abkv_decode vs FlashInfer on the same caches (ms per 36-layer step)",
+            "unit": "ms", "flashinfer_version": getattr(flashinfer, "__version__", "?"),
+            "algorithmic_bytes_per_step": alg, "hbm_peak_gbs": pk["hbm_gbs"], "results": res,
+            "config": {"B": wl.num_seqs, "layers": L, "heads": f"{Hq}/{Hkv}", "page": page,
+                       "steps": args.steps, "warmup": args.warmup}}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("which", choices=["prefill", "prefill_bwd", "compaction", "codestep", "packed", "kvshard",
-                                          "codestep_compact"])
+                                          "codestep_compact", "flashinfer"])
     ap.add_argument("--layers", type=int, default=36)
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=2)
@@ -577,7 +686,8 @@ def main() -> None:
     ap.add_argument("--chunk-tokens", type=int, default=0, help="kvshard: split-KV chunk rows (0 = auto)")
     args = ap.parse_args()
     fn = {"prefill": bench_prefill, "prefill_bwd": bench_prefill_bwd, "compaction": bench_compaction,
-          "codestep": bench_codestep, "packed": bench_packed, "kvshard": bench_kvshard, "codestep_compact": bench_codestep_compact}[args.which]
+          "codestep": bench_codestep, "packed": bench_packed, "kvshard": bench_kvshard,
+          "codestep_compact": bench_codestep_compact, "flashinfer": bench_flashinfer}[args.which]
     print(json.dumps(fn(args)), flush=True)
 
 

@@ -9,7 +9,9 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from abridgekv_b200.parallel import gather_head_outputs, kv_head_shard, shard_sequences
+import numpy as np
+
+from abridgekv_b200.parallel import gather_head_outputs, kv_head_shard, shard_by_bytes, shard_sequences
 
 
 def _free_port() -> int:
@@ -34,11 +36,27 @@ def _worker(rank, world, port, q):
         ok_gather = torch.equal(gathered, full)
         t = torch.tensor([float(rank + 1)], dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        q.put((rank, ok_gather, float(t.item()), shard_sequences(7, world, rank)))
+        # byte-balanced shards: each rank computes its own from the same byte counts; the union
+        # (all-gathered) partitions the batch
+        mine = torch.tensor(shard_by_bytes(_config3_bytes(), world, rank), dtype=torch.int64)
+        sizes = [torch.zeros(1, dtype=torch.int64) for _ in range(world)]
+        dist.all_gather(sizes, torch.tensor([mine.numel()]))
+        parts = [torch.zeros(int(n), dtype=torch.int64) for n in sizes]
+        dist.all_gather(parts, mine)
+        ok_bytes = sorted(torch.cat(parts).tolist()) == list(range(512))
+        q.put((rank, ok_gather and ok_bytes, float(t.item()), shard_sequences(7, world, rank)))
     except Exception as e:  # report instead of leaving the parent waiting
         q.put((rank, False, -1.0, slice(0, 0), repr(e)))
     finally:
         dist.destroy_process_group()
+
+
+def _config3_bytes():
+    """K/V bytes per decode step of each of config 3's 512 sequences (36 layers, 8 KV heads x 128 dims)."""
+    from abridgekv_b200.workloads import SCHEDULE_PERLAYER_MEAN128, config3_rows
+
+    rows = config3_rows(512, 0)
+    return sum(rows[q] for q in SCHEDULE_PERLAYER_MEAN128) * 8 * 128 * 4
 
 
 def test_two_rank_sharding_and_gather():
@@ -67,3 +85,17 @@ def test_shard_sequences_partition(n, w):
         s = shard_sequences(n, w, r)
         seen += list(range(s.start, s.stop))
     assert seen == list(range(n))
+
+
+@pytest.mark.parametrize("w", [1, 2, 4, 8])
+def test_shard_by_bytes_partitions_and_balances_config3(w):
+    """The 512 config-3 sequences (generated length log-uniform in [2K, 32K], 0.07-1.3 GB each) spread
+    by bytes: every sequence exactly once, and every rank within 0.5 % of the mean bytes (contiguous
+    equal-count shares are off by up to ~10 %)."""
+    b = _config3_bytes()
+    shards = [shard_by_bytes(b, w, r) for r in range(w)]
+    assert sorted(np.concatenate(shards).tolist()) == list(range(512))
+    loads = np.array([b[s].sum() for s in shards])
+    assert loads.max() / loads.mean() < 1.005, loads / loads.mean()
+    counts = np.array([b[shard_sequences(512, w, r)].sum() for r in range(w)])
+    assert loads.max() <= counts.max()
