@@ -26,6 +26,7 @@ for the packed sidecar, a ``CompressMask`` for the prefill.
 from __future__ import annotations
 
 import json
+import re
 from dataclasses import dataclass, field, fields
 from pathlib import Path
 from typing import Any, Sequence
@@ -59,17 +60,89 @@ def load_layer_quotas(path: str | Path) -> tuple[int, ...]:
     return tuple(out)
 
 
+_LAYER_TOKEN = re.compile(r"\.layers\.([^.]*)")
+
+
 def layer_index(layer_name: str) -> int | None:
-    """n of an attention layer named '....layers.n....' (None when the name has no index)."""
-    _, sep, rest = layer_name.partition(".layers.")
-    if not sep:
-        return None
-    head = rest.split(".", 1)[0]
-    return int(head) if head.isdigit() else None
+    """n of an attention layer named '....layers.n....' (the token after the first '.layers.'; None
+    when there is none or it is not a number)."""
+    m = _LAYER_TOKEN.search(layer_name)
+    return int(m.group(1)) if m and m.group(1).isdecimal() else None
+
+
+def _pow2_or_zero(n: int) -> bool:
+    # the power-of-two test the geometry uses: n & (n - 1) clears the lowest set bit
+    return (n & (n - 1)) == 0
+
+
+def _first_violation(items, bad, message) -> str | None:
+    """message(index, item) of the first item for which bad(item) holds, else None."""
+    for i, item in enumerate(items):
+        if bad(item):
+            return message(i, item)
+    return None
+
+
+def _packed_rows_violation(c: "CompressLMConfig") -> str | None:
+    for layer, row in enumerate(c.packed_kv_quotas):
+        if not row:
+            return f"packed_kv_quotas[{layer}] must not be empty"
+        msg = _first_violation(row, lambda q: not 0 < q <= c.packed_kv_k_max,
+                               lambda h, q: f"packed_kv_quotas[{layer}][{h}]={q} must be in [1, {c.packed_kv_k_max}]")
+        if msg:
+            return msg
+    return None
+
+
+# Validation of an enabled configuration, in the order the overlay's CompressLMConfig reports the
+# first problem (vllm/config/compresslm.py:76-190): each rule returns its message when violated.
+# The geometry comes first, then what vLLM serving supports, then per-layer and packed quotas.
+_ENABLED_RULES: tuple = (
+    lambda c: None if (_pow2_or_zero(c.block_size) and _pow2_or_zero(c.num_code_tokens) and not c.replay_tail
+                       and not c.raw_tail and c.num_passes == 1) or c.code_positions != "bitrev" else
+    "code_positions=bitrev needs power-of-two block_size and num_code_tokens, no replay/raw tail and num_passes=1",
+    lambda c: None if c.block_size > 0 else "block_size must be positive",
+    lambda c: None if c.num_code_tokens > 0 else "num_code_tokens must be positive",
+    lambda c: None if 0 <= c.replay_tail <= c.block_size else "replay_tail must be in [0, block_size]",
+    lambda c: None if 0 <= c.retain_tail_kv < c.block_size else "retain_tail_kv must be in [0, block_size)",
+    lambda c: None if c.retain_tail_policy != "sticky" or c.retain_tail_kv else
+    "retain_tail_policy='sticky' requires retain_tail_kv > 0",
+    lambda c: None if np.count_nonzero([c.raw_tail, c.replay_tail, c.retain_tail_kv]) <= 1 else
+    "raw_tail, replay_tail, and retain_tail_kv are mutually exclusive",
+    lambda c: None if not c.code_exclude_replay_tail or 0 < c.replay_tail < c.block_size else
+    "code_exclude_replay_tail requires replay_tail in [1, block_size)",
+    lambda c: None if c.num_passes == 1 else "vLLM CompressLM decoding currently supports L=1 only",
+    lambda c: None if c.pause_xattn == "full" else "vLLM CompressLM decoding currently requires pause_xattn='full'",
+    lambda c: None if not c.raw_tail else "vLLM CompressLM decoding currently supports raw_tail=0 only",
+    lambda c: None if c.raw_prompt else "vLLM CompressLM decoding currently requires raw_prompt=True",
+    lambda c: _first_violation(c.layer_code_quotas, lambda q: not 0 < q <= c.num_code_tokens,
+                               lambda i, q: f"layer_code_quotas[{i}]={q} must be in [1, {c.num_code_tokens}]"),
+    lambda c: None if not c.uses_layer_quotas or c.code_positions == "bitrev" else
+    "layer_code_quotas below num_code_tokens need code_positions=bitrev (nested-prefix code layout)",
+    lambda c: None if not (c.uses_layer_quotas and c.packed_kv) else
+    "layer_code_quotas and packed KV are mutually exclusive",
+    lambda c: None if not c.physical_layer_quotas or c.layer_code_quotas else
+    "physical_layer_quotas needs layer_code_quotas",
+    lambda c: None if not c.packed_kv or not (c.raw_tail or (c.retain_tail_kv and c.retain_tail_policy != "static"))
+    else "packed KV supports code/replay checkpoints and the static retained tail, not window (rolling/sticky) or "
+         "raw tails",
+    lambda c: None if not (c.packed_kv and c.code_exclude_replay_tail) else
+    "packed KV does not yet support code_exclude_replay_tail",
+    lambda c: None if not c.packed_kv or c.packed_kv_k_max == c.num_code_tokens else
+    "packed_kv_k_max must equal num_code_tokens so the dense code pass computes every schedulable slot",
+    lambda c: None if not c.packed_kv or c.packed_kv_k_max > 0 else "packed_kv_k_max must be positive",
+    lambda c: _packed_rows_violation(c) if c.packed_kv else None,
+)
 
 
 @dataclass
 class CompressLMConfig:
+    """The geometry of a CompressLM deployment (field names and defaults of the overlay's class).
+
+    Construction normalises the quota fields to int tuples, checks the two enumerations always and,
+    when ``enable`` is set, runs ``_ENABLED_RULES`` in order: the first violated rule raises
+    ``ValueError`` with its message."""
+
     enable: bool = False
     block_size: int = 512
     num_code_tokens: int = 128
@@ -90,83 +163,32 @@ class CompressLMConfig:
     extra: dict[str, Any] = field(default_factory=dict, repr=False)  # export keys this class does not model
 
     def __post_init__(self) -> None:
-        self.packed_kv_quotas = tuple(tuple(int(v) for v in row) for row in self.packed_kv_quotas)
-        self.layer_code_quotas = tuple(int(q) for q in self.layer_code_quotas)
+        self.packed_kv_quotas = tuple(map(lambda row: tuple(map(int, row)), self.packed_kv_quotas))
+        self.layer_code_quotas = tuple(map(int, self.layer_code_quotas))
         if self.retain_tail_policy not in _POLICIES:
             raise ValueError("retain_tail_policy must be one of: rolling, sticky, static")
         if self.code_positions not in ("appended", "bitrev"):
             raise ValueError("code_positions must be appended or bitrev")
-        if not self.enable:
-            return
-        C, K = self.block_size, self.num_code_tokens
-        if self.code_positions == "bitrev":
-            pow2 = C > 0 and K > 0 and not (C & (C - 1)) and not (K & (K - 1))
-            if not pow2 or self.replay_tail or self.raw_tail or self.num_passes != 1:
-                raise ValueError("code_positions=bitrev needs power-of-two block_size and num_code_tokens, "
-                                 "no replay/raw tail and num_passes=1")
-        if C <= 0:
-            raise ValueError("block_size must be positive")
-        if K <= 0:
-            raise ValueError("num_code_tokens must be positive")
-        if not 0 <= self.replay_tail <= C:
-            raise ValueError("replay_tail must be in [0, block_size]")
-        if not 0 <= self.retain_tail_kv < C:
-            raise ValueError("retain_tail_kv must be in [0, block_size)")
-        if self.retain_tail_policy == "sticky" and not self.retain_tail_kv:
-            raise ValueError("retain_tail_policy='sticky' requires retain_tail_kv > 0")
-        if sum(1 for v in (self.raw_tail, self.replay_tail, self.retain_tail_kv) if v) > 1:
-            raise ValueError("raw_tail, replay_tail, and retain_tail_kv are mutually exclusive")
-        if self.code_exclude_replay_tail and not 0 < self.replay_tail < C:
-            raise ValueError("code_exclude_replay_tail requires replay_tail in [1, block_size)")
-        if self.num_passes != 1:
-            raise ValueError("vLLM CompressLM decoding currently supports L=1 only")
-        if self.pause_xattn != "full":
-            raise ValueError("vLLM CompressLM decoding currently requires pause_xattn='full'")
-        if self.raw_tail:
-            raise ValueError("vLLM CompressLM decoding currently supports raw_tail=0 only")
-        if not self.raw_prompt:
-            raise ValueError("vLLM CompressLM decoding currently requires raw_prompt=True")
-        for layer, quota in enumerate(self.layer_code_quotas):
-            if not 0 < quota <= K:
-                raise ValueError(f"layer_code_quotas[{layer}]={quota} must be in [1, {K}]")
-        if self.uses_layer_quotas:
-            if self.code_positions != "bitrev":
-                raise ValueError("layer_code_quotas below num_code_tokens need code_positions=bitrev "
-                                 "(nested-prefix code layout)")
-            if self.packed_kv:
-                raise ValueError("layer_code_quotas and packed KV are mutually exclusive")
-        if self.physical_layer_quotas and not self.layer_code_quotas:
-            raise ValueError("physical_layer_quotas needs layer_code_quotas")
-        if self.packed_kv:
-            if self.raw_tail or (self.retain_tail_kv and self.retain_tail_policy != "static"):
-                raise ValueError("packed KV supports code/replay checkpoints and the static retained tail, "
-                                 "not window (rolling/sticky) or raw tails")
-            if self.code_exclude_replay_tail:
-                raise ValueError("packed KV does not yet support code_exclude_replay_tail")
-            if self.packed_kv_k_max != K:
-                raise ValueError("packed_kv_k_max must equal num_code_tokens so the dense code pass computes "
-                                 "every schedulable slot")
-            for layer, row in enumerate(self.packed_kv_quotas):
-                if not row:
-                    raise ValueError(f"packed_kv_quotas[{layer}] must not be empty")
-                for head, quota in enumerate(row):
-                    if not 0 < quota <= self.packed_kv_k_max:
-                        raise ValueError(f"packed_kv_quotas[{layer}][{head}]={quota} must be in "
-                                         f"[1, {self.packed_kv_k_max}]")
+        if self.enable:
+            for rule in _ENABLED_RULES:
+                msg = rule(self)
+                if msg:
+                    raise ValueError(msg)
 
-    # ---- the overlay's helpers -------------------------------------------------
+    # ---- quota views -------------------------------------------------------------------
     @property
     def code_excluded_tail(self) -> int:
+        """Content rows at the end of a block the codes do not summarise (and a code step hides)."""
         return self.replay_tail if self.code_exclude_replay_tail else self.retain_tail_kv
 
     @property
     def uses_layer_quotas(self) -> bool:
         """Some layer sees fewer code slots than the cache holds."""
-        return any(q < self.num_code_tokens for q in self.layer_code_quotas)
+        return min(self.layer_code_quotas, default=self.num_code_tokens) < self.num_code_tokens
 
     @property
     def uses_physical_layer_quotas(self) -> bool:
-        return bool(self.physical_layer_quotas) and self.uses_layer_quotas
+        return self.uses_layer_quotas and bool(self.physical_layer_quotas)
 
     @property
     def uses_packed_kv(self) -> bool:
@@ -174,42 +196,39 @@ class CompressLMConfig:
 
     def layer_quota(self, layer: int) -> int:
         """Code slots visible at `layer` (all K past the end of the schedule)."""
-        if 0 <= layer < len(self.layer_code_quotas):
-            return self.layer_code_quotas[layer]
-        return self.num_code_tokens
+        table = self.layer_code_quotas
+        return table[layer] if 0 <= layer < len(table) else self.num_code_tokens
 
     @property
     def distinct_layer_quotas(self) -> tuple[int, ...]:
-        return tuple(sorted(set(self.layer_code_quotas)))
+        return tuple(np.unique(np.asarray(self.layer_code_quotas, dtype=np.int64)).tolist())
 
     def kv_group_quotas(self, group_layer_names: Sequence[Sequence[str]]) -> tuple[int, ...]:
-        """The code quota of every KV-cache group; a group must hold layers of one quota."""
-        out = []
+        """The code quota of every KV-cache group; each group must hold layers of a single quota."""
+        quotas = []
         for names in group_layer_names:
-            seen = set()
-            for name in names:
-                idx = layer_index(name)
-                if idx is None:
-                    raise ValueError(f"physical per-layer quotas need indexed attention layers; got {name!r}")
-                seen.add(self.layer_quota(idx))
-            if len(seen) != 1:
-                raise ValueError(f"KV cache group mixes code quotas {sorted(seen)}: {list(names)}")
-            out.append(next(iter(seen)))
-        return tuple(out)
+            indices = [layer_index(n) for n in names]
+            missing = [n for n, i in zip(names, indices) if i is None]
+            if missing:
+                raise ValueError(f"physical per-layer quotas need indexed attention layers; got {missing[0]!r}")
+            found = sorted({self.layer_quota(i) for i in indices})
+            if len(found) != 1:
+                raise ValueError(f"KV cache group mixes code quotas {found}: {list(names)}")
+            quotas.append(found[0])
+        return tuple(quotas)
 
+    # ---- code RoPE layout --------------------------------------------------------------
     def bitrev_code_offsets(self) -> np.ndarray:
-        """In-block RoPE offset of each code row k: floor(bitreverse_{log2 K}(k) * span / K), span = C minus
-        the tail the codes do not summarise."""
+        """In-block RoPE offset of each code row k: (k with its log2 K bits reversed) x span // K, where
+        span = C minus the tail the codes do not summarise."""
         K = self.num_code_tokens
         span = self.block_size - self.code_excluded_tail
         if span < K:
             raise ValueError(f"bitrev code span {span} < num_code_tokens {K}")
-        bits = K.bit_length() - 1
-        k = np.arange(K, dtype=np.int64)
-        rev = np.zeros_like(k)
-        for b in range(bits):
-            rev |= ((k >> b) & 1) << (bits - 1 - b)
-        return rev * span // K
+        width = K.bit_length() - 1
+        reversed_index = np.array([int(np.binary_repr(k, width=width)[::-1] or "0", 2) for k in range(K)],
+                                  dtype=np.int64)
+        return reversed_index * span // K
 
     def bitrev_rope_positions(self, logical) -> np.ndarray:
         """RoPE positions of logical sequence positions (period C + K per block) under the bitrev layout:
@@ -217,8 +236,8 @@ class CompressLMConfig:
         C, K = self.block_size, self.num_code_tokens
         logical = np.asarray(logical, dtype=np.int64)
         blk, within = np.divmod(logical, C + K)
-        offs = self.bitrev_code_offsets()[np.clip(within - C, 0, K - 1)]
-        return blk * C + np.where(within >= C, offs, within)
+        code_offset = self.bitrev_code_offsets()[np.clip(within - C, 0, K - 1)]
+        return blk * C + np.where(within < C, within, code_offset)
 
     # ---- adapters to this package ---------------------------------------------------
     def decode_groups(self, num_layers: int) -> dict[int, list[int]]:

@@ -25,6 +25,7 @@ import math
 from dataclasses import dataclass
 from typing import Sequence
 
+import numpy as np
 import torch
 
 from . import _lib
@@ -34,8 +35,9 @@ from .workspace import Workspace, default_workspace
 
 @dataclass(frozen=True)
 class PackedKVLayout:
-    """Static ``K[layer, kv_head]`` layout for one compressed block (same fields and checks as
-    the reference's dataclass)."""
+    """Static ``K[layer, kv_head]`` quotas of one compressed block (the reference dataclass's fields and
+    error messages): KV head h of layer l owns ``quotas[l][h]`` slots of each packed page, at slot
+    offset ``offsets[l][h]``.  Checked on construction; the geometry is read from one int array."""
 
     quotas: tuple[tuple[int, ...], ...]
     k_max: int
@@ -43,32 +45,35 @@ class PackedKVLayout:
     def __post_init__(self) -> None:
         if self.k_max <= 0:
             raise ValueError("packed KV k_max must be positive")
-        if not self.quotas or not self.quotas[0]:
+        widths = [len(row) for row in self.quotas]
+        if not widths or widths[0] == 0:
             raise ValueError("packed KV quotas must be a non-empty 2D schedule")
-        num_heads = len(self.quotas[0])
-        for layer, row in enumerate(self.quotas):
-            if len(row) != num_heads:
-                raise ValueError("packed KV quota rows must have equal length; "
-                                 f"layer 0 has {num_heads}, layer {layer} has {len(row)}")
-            for head, quota in enumerate(row):
-                if not 0 < quota <= self.k_max:
-                    raise ValueError(f"packed KV quota[{layer}][{head}]={quota} must be in [1, {self.k_max}]")
+        uneven = next((l for l, w in enumerate(widths) if w != widths[0]), None)
+        if uneven is not None:
+            raise ValueError("packed KV quota rows must have equal length; "
+                             f"layer 0 has {widths[0]}, layer {uneven} has {widths[uneven]}")
+        q = self._array()
+        bad = np.argwhere((q <= 0) | (q > self.k_max))  # row-major: the first layer, then its first head
+        if len(bad):
+            layer, head = (int(x) for x in bad[0])
+            raise ValueError(f"packed KV quota[{layer}][{head}]={int(q[layer, head])} must be in [1, {self.k_max}]")
+
+    def _array(self) -> np.ndarray:
+        return np.asarray(self.quotas, dtype=np.int64).reshape(len(self.quotas), -1)
 
     @classmethod
     def from_schedule(cls, schedule: Sequence[Sequence[int]] | None, *, num_layers: int, num_kv_heads: int,
                       k_max: int) -> "PackedKVLayout":
+        """Layout of a quota schedule ([layer][KV head]); without one, every head keeps all k_max slots."""
         if num_layers <= 0 or num_kv_heads <= 0:
             raise ValueError("packed KV model dimensions must be positive")
-        if schedule:
-            quotas = tuple(tuple(int(v) for v in row) for row in schedule)
-        else:
-            quotas = tuple((int(k_max),) * num_kv_heads for _ in range(num_layers))
-        if len(quotas) != num_layers:
-            raise ValueError(f"packed KV schedule has {len(quotas)} layers; model has {num_layers}")
-        if any(len(row) != num_kv_heads for row in quotas):
-            widths = sorted(set(len(row) for row in quotas))
+        rows = [tuple(map(int, r)) for r in schedule] if schedule else [(int(k_max),) * num_kv_heads] * num_layers
+        if len(rows) != num_layers:
+            raise ValueError(f"packed KV schedule has {len(rows)} layers; model has {num_layers}")
+        widths = sorted({len(r) for r in rows})
+        if widths != [num_kv_heads]:
             raise ValueError(f"packed KV schedule row widths {widths} do not match model num_kv_heads={num_kv_heads}")
-        return cls(quotas=quotas, k_max=int(k_max))
+        return cls(quotas=tuple(rows), k_max=int(k_max))
 
     @property
     def num_layers(self) -> int:
@@ -80,17 +85,14 @@ class PackedKVLayout:
 
     @property
     def offsets(self) -> tuple[tuple[int, ...], ...]:
-        rows = []
-        for quotas in self.quotas:
-            off = [0]
-            for q in quotas:
-                off.append(off[-1] + q)
-            rows.append(tuple(off))
-        return tuple(rows)
+        """Per layer, the first slot of every head and the end: [0, q_0, q_0 + q_1, ..., sum q]."""
+        q = self._array()
+        edges = np.concatenate([np.zeros((q.shape[0], 1), dtype=np.int64), np.cumsum(q, axis=1)], axis=1)
+        return tuple(tuple(row) for row in edges.tolist())
 
     @property
     def packed_slots_per_layer(self) -> tuple[int, ...]:
-        return tuple(sum(row) for row in self.quotas)
+        return tuple(self._array().sum(axis=1).tolist())
 
     def _index(self, layer: int, device) -> torch.Tensor:
         """Dense (slot, head) pairs of the packed slots, head-major: [slots, 2]."""

@@ -137,3 +137,29 @@ def test_packed_decode_repeat_calls_on_one_workspace_are_identical(chunk_tokens)
         assert ws.read_error() == 0, name
         for o in outs[1:]:
             assert torch.equal(o[0], outs[0][0]) and torch.equal(o[1], outs[0][0]), name
+
+
+def test_layout_matches_the_reference_class():
+    """PackedKVLayout against the reference's own class on the same inputs
+    (tests/golden/packed_layout_reference.json, made by make_golden.py --only layout): the same
+    validation messages, offsets and packed slot counts."""
+    import json
+    from pathlib import Path
+
+    gold = json.loads((Path(__file__).resolve().parent / "golden" / "packed_layout_reference.json").read_text())
+
+    def describe(fn):
+        try:
+            x = fn()
+            return {"quotas": [list(r) for r in x.quotas], "offsets": [list(r) for r in x.offsets],
+                    "slots": list(x.packed_slots_per_layer), "k_max": x.k_max}
+        except ValueError as e:
+            return {"error": str(e)}
+
+    for case in gold["layouts"]:
+        quotas = tuple(tuple(r) for r in case["quotas"])
+        assert describe(lambda: PackedKVLayout(quotas=quotas, k_max=case["k_max"])) == case["result"], case
+    for case in gold["schedules"]:
+        got = describe(lambda: PackedKVLayout.from_schedule(case["schedule"], num_layers=case["num_layers"],
+                                                            num_kv_heads=case["num_kv_heads"], k_max=case["k_max"]))
+        assert got == case["result"], case
