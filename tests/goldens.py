@@ -125,3 +125,48 @@ def load_qmask(name: str):
     masks = {int(q): np.unpackbits(z[f"mask_{int(q)}"])[: int(z[f"size_{int(q)}"])].astype(bool)
              for q in z["quotas"]}
     return K, [int(q) for q in z["quotas"]], reqs, masks
+
+
+def load_config1():
+    """BASELINE config 1 through the reference's own CompressLM.forward and CompressGen
+    (tests/golden/config1_reference.npz, make_golden.py --only config1) -> dict with
+    prefill[l] = (q_rows [H, n, D], k [Hkv, S0, D], v [Hkv, S0, D], out_rows [n, H, D] fp32) and the row
+    indices; decode[l] = (k_store [Hkv, T, D], v_store, {step: (q [H, D], cols [m], out [H, D] fp32)})."""
+    z = np.load(GOLDEN / "config1_reference.npz")
+    prefill = {l: (from_bits(z[f"prefill{l}_q_bits"]), from_bits(z[f"prefill{l}_k_bits"]),
+                   from_bits(z[f"prefill{l}_v_bits"]), z[f"prefill{l}_out"]) for l in range(2)}
+    decode = {}
+    for l in range(2):
+        steps = {int(s): (from_bits(z[f"decode{l}_s{int(s)}_q_bits"]), z[f"decode{l}_s{int(s)}_cols"],
+                          z[f"decode{l}_s{int(s)}_out"]) for s in z["decode_steps"]}
+        decode[l] = (from_bits(z[f"decode{l}_k_bits"]), from_bits(z[f"decode{l}_v_bits"]), steps)
+    return {"C": 512, "K": 128, "N": 4, "quotas": (128, 64), "rows": z["prefill_rows"], "prefill": prefill,
+            "decode": decode, "tokens": z["tokens"]}
+
+
+def config1_paged(decode_layer, page=16, seed=0):
+    """The decode steps of one config-1 layer as a paged batch: sequence i = step i's visible store
+    columns (in order) laid into pages of a shuffled pool.  -> (q [B, H, D], kv [pages, 2, page, Hkv, D],
+    block_table [B, max_pages] int32, seq_lens [B] int32, reference out [B, H, D], steps)."""
+    k_store, v_store, steps = decode_layer
+    keys = sorted(steps)
+    rng = np.random.default_rng(seed)
+    lens = [len(steps[s][1]) for s in keys]
+    pages = [(n + page - 1) // page for n in lens]
+    total = sum(pages) + 1
+    perm = 1 + rng.permutation(total - 1)
+    Hkv, _, D = k_store.shape
+    kv = np.zeros((total, 2, page, Hkv, D), dtype=np.float32)
+    bt = np.zeros((len(keys), max(pages)), dtype=np.int32)
+    at = 0
+    for i, s in enumerate(keys):
+        cols = steps[s][1]
+        ids = perm[at:at + pages[i]]
+        at += pages[i]
+        bt[i, :pages[i]] = ids
+        for r, c in enumerate(cols):
+            kv[ids[r // page], 0, r % page] = k_store[:, c]
+            kv[ids[r // page], 1, r % page] = v_store[:, c]
+    q = np.stack([steps[s][0] for s in keys])
+    out = np.stack([steps[s][2] for s in keys])
+    return q, kv, bt, np.asarray(lens, np.int32), out, keys
