@@ -176,8 +176,22 @@ using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, 
 static inline int encode_tiled(CUtensorMap* m, CUtensorMapDataType dtype, int rank, const void* base,
                                const cuuint64_t* dims, const cuuint64_t* gstr, const cuuint32_t* box,
                                CUtensorMapSwizzle swizzle) {
-  for (int i = 0; i < rank - 1; ++i)
-    if (gstr[i] % 16 != 0 || gstr[i] == 0) return ABKV_ERR_INVALID_ARG;
+  if (rank < 2 || rank > 5) return ABKV_ERR_INVALID_ARG;
+  // gstr[i] is the byte stride of dimension i + 1.  A dimension of extent 1 is never stepped
+  // through, so its stride addresses nothing (torch and numpy give such dimensions stride 0 after
+  // unsqueeze / expand, which the encoder rejects): replace it with the packed extent of the
+  // dimensions inside it, a legal value.
+  const size_t esize = dtype == CU_TENSOR_MAP_DATA_TYPE_FLOAT32 ? 4 : 2;
+  cuuint64_t g[4];
+  for (int i = 0; i < rank - 1; ++i) {
+    g[i] = gstr[i];
+    if (dims[i + 1] == 1) {
+      const cuuint64_t packed = i == 0 ? dims[0] * esize : g[i - 1] * dims[i];
+      g[i] = (packed + 15) / 16 * 16;
+    }
+    if (g[i] % 16 != 0 || g[i] == 0) return ABKV_ERR_INVALID_ARG;
+  }
+  gstr = g;
   const cuuint32_t es[5] = {1, 1, 1, 1, 1};
   // cuTensorMapEncodeTiled is a driver call: it needs the device's context current in the calling
   // thread, which a thread that made no runtime call yet (autograd's device thread, a worker

@@ -107,3 +107,14 @@ def test_config4_full_size_sampled_rows():
             ref = torch.softmax(s, dim=-1) @ v[b, h // 4].float()
             err = (out[b, h, rows].float() - ref).abs()
             assert err.max().item() <= ATOL, (b, h, err.max().item())
+
+
+def test_prefill_accepts_any_stride_on_an_extent_one_batch():
+    """A batch of one may carry any stride on that dimension (numpy / torch give 0 after unsqueeze or
+    expand); the stride addresses nothing and the result equals the contiguous call's."""
+    g = load_prefill("config1_d64")
+    q, k, v = _dev(g["q"]), _dev(g["k"]), _dev(g["v"])
+    assert q.shape[0] == 1
+    zero = [torch.as_strided(t, t.shape, (0,) + t.stride()[1:]) for t in (q, k, v)]
+    kw = dict(C=g["C"], K_layout=g["K"], quota_per_head=list(g["quota"]))
+    assert torch.equal(prefill.prefill_masked(*zero, **kw), prefill.prefill_masked(q, k, v, **kw))
