@@ -326,6 +326,18 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     if not args.no_strong:
         strong = strong_decode(3, rank=rank, world=world, local=local, steps=args.strong_steps, warmup=3,
                                mem_budget_gb=args.mem_budget_gb)
+    # ---- config 5 at N >= 4 (323.7 GB: two GPUs cannot hold it): KV-head sharding with the all-gather
+    # fused into the decode epilogue (peer stores over NVLink), and sequence sharding of the same batch
+    kv_heads = None
+    if world >= 4 and not args.no_kvshard:
+        kv = strong_decode(5, rank=rank, world=world, local=local, steps=args.strong_steps, warmup=3,
+                           mem_budget_gb=args.mem_budget_gb, shard="kv", gather="fused")
+        seq = strong_decode(5, rank=rank, world=world, local=local, steps=args.strong_steps, warmup=3,
+                            mem_budget_gb=args.mem_budget_gb, shard="seq")
+        kv_heads = {"config": 5, "global_batch": kv["global_batch"], "unit": kv["unit"],
+                    "kv_head_sharded": {k: kv[k] for k in ("value", "ms_per_step", "parallelism", "roofline")},
+                    "sequence_sharded": {k: seq[k] for k in ("value", "ms_per_step", "parallelism", "roofline")},
+                    "kv_over_sequence": kv["value"] / seq["value"]}
     # ---- the other kernels of the path, one GPU ----
     secondary = None
     if world == 1 and not args.no_secondary:
@@ -356,6 +368,7 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
         "gpu_launches": headline_launches,
         "clocks": clocks,
         "strong_scaling": strong,
+        "config5_kv_heads": kv_heads,
         "secondary": secondary,
     }
     print(json.dumps(line), flush=True)
@@ -739,6 +752,7 @@ def main() -> None:
                     help="timed steps of the config-3 strong-scaling block of the headline line")
     ap.add_argument("--no-strong", action="store_true", help="omit the config-3 strong-scaling block")
     ap.add_argument("--no-secondary", action="store_true", help="omit the secondary kernels' block (N=1)")
+    ap.add_argument("--no-kvshard", action="store_true", help="omit the config-5 KV-head block (N >= 4)")
     ap.add_argument("--secondary-cpu-budget", type=float, default=6.0,
                     help="seconds of CPU baseline per secondary kernel")
     args = ap.parse_args()
