@@ -110,6 +110,12 @@ SIGNATURES: dict[str, tuple] = {
     "abkv_paged_prefill": (c_int, [c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_vp, c_int, c_i64, c_int, c_vp,
                                    c_i64, c_vp, c_int, c_int, c_int, c_int, c_int, c_int, C.c_float, c_vp, c_size,
                                    c_vp]),
+    "abkv_code_step_attention_packed": (c_int, [c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_vp, c_int, c_i64,
+                                                c_int, c_vp, c_i64, c_vp, c_vp, c_i32p, c_int, c_int, c_int, c_int,
+                                                c_int, c_int, C.c_float, c_vp, c_vp, c_size, c_vp]),
+    "abkv_paged_prefill_packed": (c_int, [c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_vp, c_int, c_i64, c_int,
+                                          c_vp, c_i64, c_vp, c_int, c_int, c_int, c_int, c_int, c_int, C.c_float,
+                                          c_vp, c_vp, c_size, c_vp]),
     "abkv_code_step_compact_workspace_size": (c_size, [c_int, c_i64]),
     "abkv_code_step_attention_compact": (c_int, [c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_vp, c_int, c_i64,
                                                  c_int, c_vp, c_i64, c_vp, c_vp, c_i32p, c_int, c_int, c_int, c_int,

@@ -31,11 +31,9 @@ attention meets the cache at two places, both reproduced here over libabkv:
   with the layer's per-KV-head quotas.
 
 Every attention call runs a libabkv kernel (abkv_decode, abkv_decode_packed,
-abkv_paged_prefill, abkv_code_step_attention, abkv_store_kv).  There is no CPU
-path and no fallback.  A combination the kernels do not serve raises
-``NotImplementedError`` naming it: the packed code step or causal prefill of a
-request that already holds sidecar pages, and masked (non-physical) per-layer
-quotas.
+abkv_paged_prefill[_packed], abkv_code_step_attention[_packed], abkv_store_kv).
+There is no CPU path and no fallback.  Masked (non-physical) per-layer quotas,
+which the kernels do not serve, raise ``NotImplementedError``.
 """
 from __future__ import annotations
 
@@ -250,14 +248,15 @@ class AbkvAttentionImpl:
 def attend(q: torch.Tensor, kv_cache: torch.Tensor, md: AbkvAttentionMetadata, out: torch.Tensor, *,
            num_kv_heads: int, scale: float, workspace: Workspace | None = None,
            k_max: int | None = None, quota_per_kv_head: Sequence[int] | None = None,
-           excluded: torch.Tensor | None = None) -> None:
+           excluded: torch.Tensor | None = None, sidecar: SidecarPool | None = None) -> None:
     """Attention of one layer's step over its KV-cache group (the dispatch of AbkvAttentionImpl and of
-    the sidecar hook): decode, causal paged prefill, or the code step.  q / out ``[T, Hq, D]``."""
+    the sidecar hook): decode, causal paged prefill, or the code step; with a sidecar pool, the causal
+    prefill and the code step read the requests' packed pages first.  q / out ``[T, Hq, D]``."""
     R = md.num_reqs
     if R == 0 or md.num_actual_tokens == 0:
         return
     if md.causal:
-        if md.decode_only:
+        if md.decode_only and sidecar is None:
             qc = q if q.is_contiguous() else q.contiguous()
             direct = out.is_contiguous()
             o = out if direct else torch.empty_like(qc)
@@ -268,7 +267,7 @@ def attend(q: torch.Tensor, kv_cache: torch.Tensor, md: AbkvAttentionMetadata, o
             return
         codestep.paged_prefill(q, kv_cache, md.block_table, md.seq_lens, md.query_start_loc,
                                max_query_len=md.max_query_len, num_kv_heads=num_kv_heads, scale=scale,
-                               num_requests=R, out=out, workspace=workspace)
+                               num_requests=R, out=out, workspace=workspace, sidecar=sidecar)
         return
     # noncausal: the code step (every request's query rows are its code queries)
     qlens = (md.query_start_loc_cpu[1:] - md.query_start_loc_cpu[:-1]).tolist()
@@ -284,7 +283,7 @@ def attend(q: torch.Tensor, kv_cache: torch.Tensor, md: AbkvAttentionMetadata, o
         excluded = mask.excluded_device(q.device)
     codestep.code_step_attention(q, kv_cache, md.block_table, md.seq_lens, md.query_start_loc,
                                  quota_per_kv_head=list(quota_per_kv_head), k_max=k_max, scale=scale,
-                                 excluded=excluded, num_requests=R, out=out, workspace=workspace)
+                                 excluded=excluded, num_requests=R, out=out, workspace=workspace, sidecar=sidecar)
 
 
 class AbkvAttentionBackend:
@@ -447,14 +446,12 @@ class CompressedKVSidecar:
                           workspace=ws)
             out[:n].copy_(o)
             return
-        if has_pages:
-            raise NotImplementedError("packed KV: the code step / causal prefill of requests that already hold "
-                                      "sidecar pages is not served by libabkv (decode is)")
         excluded = None
         if not md.causal:
             excluded = codestep.excluded_tensor(self.active_request_ids, self.code_excluded_ranges, query.device)
         attend(q, kv_cache, md, out, num_kv_heads=Hkv, scale=scale, workspace=ws, k_max=self.layout.k_max,
-               quota_per_kv_head=self.layout.quotas[layer_index], excluded=excluded)
+               quota_per_kv_head=self.layout.quotas[layer_index], excluded=excluded,
+               sidecar=self.pools[layer_index] if has_pages else None)
 
 
 class _SidecarView:

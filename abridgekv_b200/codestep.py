@@ -17,6 +17,7 @@ CPU path: a missing library or a non-CUDA tensor raises.
 """
 from __future__ import annotations
 
+import ctypes as C
 import math
 from typing import Mapping, Sequence
 
@@ -87,32 +88,48 @@ def _prepare(query, kv_cache, block_table, seq_lens, query_start_loc, quota_per_
     return head, out, R, nb, page, T, scale
 
 
+def _sidecar(sidecar, Hkv: int, D: int, R: int):
+    """abkv_sidecar_t of a SidecarPool (its request slot i = request i of the launch)."""
+    if len(sidecar.quotas) != Hkv or sidecar.pages.shape[-1] != D or sidecar.page_table.shape[0] < R:
+        raise ValueError("the sidecar pool does not match the cache geometry or the number of requests")
+    return sidecar.descriptor()
+
+
 def code_step_attention(query: torch.Tensor, kv_cache: torch.Tensor, block_table: torch.Tensor,
                         seq_lens: torch.Tensor, query_start_loc: torch.Tensor, *,
                         quota_per_kv_head: Sequence[int], k_max: int, scale: float | None = None,
                         excluded: torch.Tensor | None = None, num_requests: int | None = None,
                         out: torch.Tensor | None = None, workspace: Workspace | None = None,
-                        stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+                        stream: torch.cuda.Stream | None = None, sidecar=None) -> torch.Tensor:
     """query [T, Hq, D] bf16 (last dim contiguous); kv_cache paged bf16 (either layout);
     block_table [R, max_pages] int32; seq_lens [R] int32 (each >= k_max); query_start_loc
     [>= R] int32 (request r's code queries are rows query_start_loc[r] .. + k_max - 1);
     quota_per_kv_head: this layer's quotas (each in [0, k_max]); excluded: optional [R, 2]
-    int32 hidden row ranges (start == end = none).  Writes and returns out [T, Hq, D]."""
+    int32 hidden row ranges (start == end = none); sidecar: an optional ``sidecar.SidecarPool`` of this
+    layer whose request slot i holds request i's packed pages -- KV head h then first attends to its
+    slots of those pages (``abkv_code_step_attention_packed``).  Writes and returns out [T, Hq, D]."""
     head, out, R, nb, page, T, scale = _prepare(query, kv_cache, block_table, seq_lens, query_start_loc,
                                                 quota_per_kv_head, scale, excluded, num_requests, out)
     dev = query.device
     ws = workspace or default_workspace(dev)
     s = torch.cuda.current_stream(dev) if stream is None else stream
+    lib = _lib.lib()
     with torch.cuda.device(dev):
-        st = _lib.lib().abkv_code_step_attention(*head, int(k_max), T, scale, ws.ptr(), ws.nbytes, s.cuda_stream)
-    _lib.check("abkv_code_step_attention", st)
+        if sidecar is None:
+            st = lib.abkv_code_step_attention(*head, int(k_max), T, scale, ws.ptr(), ws.nbytes, s.cuda_stream)
+        else:
+            desc = _sidecar(sidecar, len(quota_per_kv_head), query.shape[2], R)
+            st = lib.abkv_code_step_attention_packed(*head, int(k_max), T, scale, C.addressof(desc), ws.ptr(),
+                                                     ws.nbytes, s.cuda_stream)
+    _lib.check("abkv_code_step_attention" + ("_packed" if sidecar is not None else ""), st)
     return out
 
 
 def paged_prefill(query: torch.Tensor, kv_cache: torch.Tensor, block_table: torch.Tensor, seq_lens: torch.Tensor,
                   query_start_loc: torch.Tensor, *, max_query_len: int, num_kv_heads: int,
                   scale: float | None = None, num_requests: int | None = None, out: torch.Tensor | None = None,
-                  workspace: Workspace | None = None, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+                  workspace: Workspace | None = None, stream: torch.cuda.Stream | None = None,
+                  sidecar=None) -> torch.Tensor:
     """Causal attention of ragged query rows over the paged cache (prompt prefill, chunked prefill and
     mixed prefill/decode batches): request r's rows are ``query_start_loc[r] .. query_start_loc[r + 1] - 1``
     (qlen rows, their keys already written at cache rows [seq_len - qlen, seq_len)), and row i attends
@@ -122,7 +139,9 @@ def paged_prefill(query: torch.Tensor, kv_cache: torch.Tensor, block_table: torc
 
     query [T, Hq, D] bf16 (last dim contiguous), D = 128; kv_cache paged bf16 (either layout);
     block_table [R, max_pages] int32; seq_lens [R] int32 (each >= its qlen); query_start_loc
-    [>= R + 1] int32; max_query_len >= every qlen (vLLM's ``max_query_len``).  Writes and returns
+    [>= R + 1] int32; max_query_len >= every qlen (vLLM's ``max_query_len``); sidecar: an optional
+    ``sidecar.SidecarPool`` (request slot i = request i): KV head h first attends to its slots of the
+    request's packed pages, from every query row (``abkv_paged_prefill_packed``).  Writes and returns
     out [T, Hq, D] (rows of no request are left untouched)."""
     head, out, R, nb, page, T, scale = _prepare(query, kv_cache, block_table, seq_lens, query_start_loc, None,
                                                 scale, None, num_requests, out, num_kv_heads=num_kv_heads)
@@ -131,9 +150,15 @@ def paged_prefill(query: torch.Tensor, kv_cache: torch.Tensor, block_table: torc
     dev = query.device
     ws = workspace or default_workspace(dev)
     s = torch.cuda.current_stream(dev) if stream is None else stream
+    lib = _lib.lib()
     with torch.cuda.device(dev):
-        st = _lib.lib().abkv_paged_prefill(*head, int(max_query_len), T, scale, ws.ptr(), ws.nbytes, s.cuda_stream)
-    _lib.check("abkv_paged_prefill", st)
+        if sidecar is None:
+            st = lib.abkv_paged_prefill(*head, int(max_query_len), T, scale, ws.ptr(), ws.nbytes, s.cuda_stream)
+        else:
+            desc = _sidecar(sidecar, int(num_kv_heads), query.shape[2], R)
+            st = lib.abkv_paged_prefill_packed(*head, int(max_query_len), T, scale, C.addressof(desc), ws.ptr(),
+                                               ws.nbytes, s.cuda_stream)
+    _lib.check("abkv_paged_prefill" + ("_packed" if sidecar is not None else ""), st)
     return out
 
 

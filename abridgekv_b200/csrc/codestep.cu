@@ -100,6 +100,15 @@ struct alignas(64) CodeStepParams {
   // causal mode (abkv_paged_prefill): request r's query rows are q_start[r] .. q_start[r + 1] - 1
   // (qlen rows, any count); row i sees cache rows [0, seq_len - qlen + i + 1), every head alike
   int causal;
+  // optional packed sidecar (the *_packed entries): before its paged rows, KV head h of request r
+  // attends to head h's slots [side_off[h], side_off[h] + side_q[h]) of each of the request's
+  // side_count[r] packed pages (ids side_bt[r * side_bt_stride + i]); every query row sees them all
+  CUtensorMap tm_side;  // (dim, 1, slot, plane = 2 * page + {0: K, 1: V}) over [pages][2][slots][D]
+  const int32_t* side_bt;
+  const int32_t* side_count;
+  int64_t side_bt_stride, side_pages;
+  int side_off[8], side_q[8];
+  int has_side;
 };
 
 // The last CTA of request blockIdx.z applies that request's copy ops.  Every CTA of the request
@@ -242,6 +251,7 @@ __global__ void __launch_bounds__(kThreads, 1) codestep_kernel(const __grid_cons
   const int b = blockIdx.z;  // request
   int kt_end = 0, seq_len = 0, leffA = 0, leffB = 0, hole_s = 0, hole_e = 0;
   int qlen = p.Kc;  // the request's query rows (all Kc code rows in the code step)
+  int n_side = 0, side_tiles = 0;  // sidecar rows of this CTA's KV head, in 64-row tiles
   {
     // every thread reads the same values, so an early return is CTA-uniform and
     // happens before any barrier, TMEM allocation or copy
@@ -290,6 +300,19 @@ __global__ void __launch_bounds__(kThreads, 1) codestep_kernel(const __grid_cons
       leffB = hB >= 0 ? min(max(seq_len - (p.Kc - p.quota[hB]), 0), seq_len) : 0;
     }
     kt_end = (max(leffA, leffB) + kBN - 1) / kBN;
+    if (p.has_side) {
+      int cnt = __ldg(p.side_count + b);
+      if (cnt < 0 || (int64_t)cnt > p.side_bt_stride) {
+        if (threadIdx.x == 0) set_error(p.err, ABKV_DEVERR_SEQ_OOB);
+        cnt = cnt < 0 ? 0 : (int)p.side_bt_stride;
+      }
+      n_side = cnt * p.side_q[hk];
+    }
+    side_tiles = (n_side + kBN - 1) / kBN;
+    if (side_tiles + kt_end > kMaxKeyTiles) {  // the tile list would not hold them: skip the request
+      if (threadIdx.x == 0) set_error(p.err, ABKV_DEVERR_SEQ_OOB);
+      return;
+    }
   }
 
   if (threadIdx.x == 0) {
@@ -314,6 +337,13 @@ __global__ void __launch_bounds__(kThreads, 1) codestep_kernel(const __grid_cons
   int32_t* s_nlist = s_list + kMaxKeyTiles;
   if (warp == 2) {
     int n = 0;
+    // sidecar tiles first (entry -(t + 1) = sidecar tile t), all visible
+    for (int base = 0; base < side_tiles; base += 32) {
+      const int t = base + lane;
+      const uint32_t m = __ballot_sync(0xffffffffu, t < side_tiles);
+      if (t < side_tiles) s_list[n + __popc(m & ((1u << lane) - 1u))] = -(t + 1);
+      n += __popc(m);
+    }
     for (int base = 0; base < kt_end; base += 32) {
       const int kt = base + lane;
       // tiles entirely inside the exclusion range are skipped for both heads
@@ -356,6 +386,17 @@ __global__ void __launch_bounds__(kThreads, 1) codestep_kernel(const __grid_cons
       auto slice_page = [&](int j0) -> int {
         const int j = j0 + (lane >> 2);
         if (j >= n_tiles) return -1;
+        if (s_list[j] < 0) {  // sidecar tile: the page holding this 16-slot slice
+          const int row0 = (-s_list[j] - 1) * kBN + 16 * (lane & 3);
+          if (row0 >= n_side) return -1;
+          const int v = __ldg(p.side_bt + (int64_t)b * p.side_bt_stride + row0 / p.side_q[hk]);
+          if (v < 0 || (int64_t)v >= p.side_pages) {
+            set_error(p.err, ABKV_DEVERR_PAGE_OOB);
+            bad_page = true;
+            return -1;
+          }
+          return v;
+        }
         const int row0 = s_list[j] * kBN + 16 * (lane & 3);
         if (row0 >= seq_len) return -1;
         const int v = __ldg(p.bt + (int64_t)b * p.bt_stride + row0 / p.page);
@@ -384,7 +425,16 @@ __global__ void __launch_bounds__(kThreads, 1) codestep_kernel(const __grid_cons
             stop = true;
             break;
           }
-          if (lane < 4 && pg >= 0) {
+          if (lane < 4 && pg >= 0 && kt < 0) {
+            // sidecar slice: 16 slots of head hk's segment of packed page pg (K plane, V plane)
+            uint8_t* kbuf = smem + kOffKV + st * kStageBytes + lane * 2048;
+            const int row0 = (-kt - 1) * kBN + 16 * lane;
+            const int slot = p.side_off[hk] + row0 % p.side_q[hk];
+            tma_load_4d(kbuf, &p.tm_side, 0, 0, slot, 2 * pg, &kv_full[st]);
+            tma_load_4d(kbuf + kKVHalf / 2, &p.tm_side, 64, 0, slot, 2 * pg, &kv_full[st]);
+            tma_load_4d(kbuf + kKVHalf, &p.tm_side, 0, 0, slot, 2 * pg + 1, &kv_full[st]);
+            tma_load_4d(kbuf + kKVHalf + kKVHalf / 2, &p.tm_side, 64, 0, slot, 2 * pg + 1, &kv_full[st]);
+          } else if (lane < 4 && pg >= 0) {
             uint8_t* kbuf = smem + kOffKV + st * kStageBytes + lane * 2048;
             const int off = (kt * kBN + 16 * lane) % p.page;
             const int pk = p.fa_layout ? pg : 2 * pg;
@@ -479,7 +529,10 @@ __global__ void __launch_bounds__(kThreads, 1) codestep_kernel(const __grid_cons
       const int leff = p.causal ? seq_len - qlen + min(q, qlen - 1) + 1 : (head_slot ? leffB : leffA);
       for (int j = 0; j < n_tiles; ++j) {
         const int e = s_list[j];
-        const int lim = min(max(leff - e * kBN, 0), kBN);
+        const bool side = e < 0;  // sidecar tile -(e + 1): every query row sees its rows
+        const int lim = side ? min(max(n_side - (-e - 1) * kBN, 0), kBN) : min(max(leff - e * kBN, 0), kBN);
+        // valid rows of the tile: the rest was not loaded (V zeroed below)
+        const int valid = side ? n_side - (-e - 1) * kBN : seq_len - e * kBN;
         // warp-uniform decision: tcgen05.ld is a warp-collective
         const bool ok = __all_sync(
             0xffffffffu, wait_or_abort(&s_full[2 * head_slot + (j & 1)], (uint32_t)((j >> 1) & 1), dead, p.err));
@@ -488,11 +541,11 @@ __global__ void __launch_bounds__(kThreads, 1) codestep_kernel(const __grid_cons
           break;
         }
         tc_fence_after();
-        if (head_slot == 0 && e * kBN + kBN > seq_len) {
-          // V rows at or past seq_len (stale page slots or unloaded slices) become
-          // zeros before either head's P.V reads them (P is 0 there, but 0 * NaN
-          // would not be)
-          const int first = max(seq_len - e * kBN, 0);
+        if (head_slot == 0 && valid < kBN) {
+          // V rows at or past seq_len (or the sidecar segment's end): stale page
+          // slots or unloaded slices become zeros before either head's P.V reads
+          // them (P is 0 there, but 0 * NaN would not be)
+          const int first = max(valid, 0);
           uint8_t* vb = smem + kOffKV + (j % kStages) * kStageBytes + kKVHalf;
           const int wt = (warp - 2) * 32 + lane;
           for (int idx = wt; idx < 2 * (kBN - first) * 8; idx += 128) {
@@ -504,8 +557,8 @@ __global__ void __launch_bounds__(kThreads, 1) codestep_kernel(const __grid_cons
           // p_full arrival, and both heads' P.V wait for head A's p_full
           asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
         }
-        softmax_tile<true>(p, lim, hole_s - e * kBN, hole_e - e * kBN, row, tmem_h + 64 * (j & 1), tmem_o,
-                           lane_base, j, &o_done[head_slot], dead, st);
+        softmax_tile<true>(p, lim, side ? 0 : hole_s - e * kBN, side ? 0 : hole_e - e * kBN, row,
+                           tmem_h + 64 * (j & 1), tmem_o, lane_base, j, &o_done[head_slot], dead, st);
         tc_fence_before();  // P's tcgen05.st completed (wait::st) before the arrival
         mbar_arrive_one(&p_full[2 * head_slot + (j & 1)]);
       }
@@ -572,7 +625,8 @@ int code_step_launch(const void* q, int64_t q_row_stride, int64_t q_head_stride,
                      const int32_t* block_table, int64_t bt_stride, const int32_t* seq_lens,
                      const int32_t* excluded, const int32_t* quota_per_kv_head, int R, int Hq,
                      int Hkv, int head_dim, int K_code, int T, float scale, void* workspace,
-                     size_t workspace_bytes, void* stream, const CommitArgs* commit, int causal_max_qlen = 0);
+                     size_t workspace_bytes, void* stream, const CommitArgs* commit, int causal_max_qlen = 0,
+                     const abkv_sidecar_t* side = nullptr);
 
 constexpr size_t align256(size_t x) { return (x + 255) / 256 * 256; }
 size_t commit_workspace(int R, int64_t n_ops) {
@@ -604,6 +658,34 @@ extern "C" int abkv_paged_prefill(const void* q, int64_t q_row_stride, int64_t q
                           kv_cache, kv_layout, num_blocks, page_size, block_table, bt_stride, seq_lens, nullptr,
                           nullptr, R, Hq, Hkv, head_dim, 0, T, scale, workspace, workspace_bytes, stream, nullptr,
                           max_query_len);
+}
+
+extern "C" int abkv_code_step_attention_packed(
+    const void* q, int64_t q_row_stride, int64_t q_head_stride, void* out, int64_t out_row_stride,
+    int64_t out_head_stride, const int32_t* q_start, const void* kv_cache, int kv_layout, int64_t num_blocks,
+    int page_size, const int32_t* block_table, int64_t bt_stride, const int32_t* seq_lens, const int32_t* excluded,
+    const int32_t* quota_per_kv_head, int R, int Hq, int Hkv, int head_dim, int K_code, int T, float scale,
+    const abkv_sidecar_t* sidecar, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!sidecar) return ABKV_ERR_INVALID_ARG;
+  return code_step_launch(q, q_row_stride, q_head_stride, out, out_row_stride, out_head_stride, q_start, kv_cache,
+                          kv_layout, num_blocks, page_size, block_table, bt_stride, seq_lens, excluded,
+                          quota_per_kv_head, R, Hq, Hkv, head_dim, K_code, T, scale, workspace, workspace_bytes,
+                          stream, nullptr, 0, sidecar);
+}
+
+extern "C" int abkv_paged_prefill_packed(const void* q, int64_t q_row_stride, int64_t q_head_stride, void* out,
+                                         int64_t out_row_stride, int64_t out_head_stride,
+                                         const int32_t* query_start_loc, const void* kv_cache, int kv_layout,
+                                         int64_t num_blocks, int page_size, const int32_t* block_table,
+                                         int64_t bt_stride, const int32_t* seq_lens, int R, int Hq, int Hkv,
+                                         int head_dim, int max_query_len, int T, float scale,
+                                         const abkv_sidecar_t* sidecar, void* workspace, size_t workspace_bytes,
+                                         void* stream) {
+  if (max_query_len <= 0 || !sidecar) return ABKV_ERR_INVALID_ARG;
+  return code_step_launch(q, q_row_stride, q_head_stride, out, out_row_stride, out_head_stride, query_start_loc,
+                          kv_cache, kv_layout, num_blocks, page_size, block_table, bt_stride, seq_lens, nullptr,
+                          nullptr, R, Hq, Hkv, head_dim, 0, T, scale, workspace, workspace_bytes, stream, nullptr,
+                          max_query_len, sidecar);
 }
 
 extern "C" size_t abkv_code_step_compact_workspace_size(int num_requests, int64_t n_ops) {
@@ -673,7 +755,8 @@ int code_step_launch(const void* q, int64_t q_row_stride, int64_t q_head_stride,
                      const int32_t* block_table, int64_t bt_stride, const int32_t* seq_lens,
                      const int32_t* excluded, const int32_t* quota_per_kv_head, int R, int Hq,
                      int Hkv, int head_dim, int K_code, int T, float scale, void* workspace,
-                     size_t workspace_bytes, void* stream, const CommitArgs* commit, int causal_max_qlen) {
+                     size_t workspace_bytes, void* stream, const CommitArgs* commit, int causal_max_qlen,
+                     const abkv_sidecar_t* side) {
   const bool causal = causal_max_qlen > 0;  // abkv_paged_prefill: no quotas, no exclusion, no copies
   if (!q || !out || !q_start || !kv_cache || !block_table || !seq_lens || (!causal && !quota_per_kv_head))
     return ABKV_ERR_INVALID_ARG;
@@ -741,6 +824,35 @@ int code_step_launch(const void* q, int64_t q_row_stride, int64_t q_head_stride,
   prm.T = T;
   prm.fa_layout = kv_layout;
   if (Hkv * prm.npairs > 65535) return ABKV_ERR_UNSUPPORTED;
+  if (side) {
+    // pages [num_pages][2][slots][D]; quotas multiples of 16 (a 16-slot slice never leaves its head's
+    // segment) summing to slots
+    if (!side->pages || !side->page_table || !side->page_count || side->page_table_stride <= 0 ||
+        side->num_pages <= 0 || side->num_pages > (INT32_MAX / 2) || commit)
+      return ABKV_ERR_INVALID_ARG;
+    if ((reinterpret_cast<uintptr_t>(side->pages) & 15) || (reinterpret_cast<uintptr_t>(side->page_table) & 3))
+      return ABKV_ERR_INVALID_ARG;
+    if (Hkv > 8) return ABKV_ERR_UNSUPPORTED;
+    int sum = 0;
+    for (int h = 0; h < Hkv; ++h) {
+      const int qh = side->quotas[h];
+      if (qh <= 0 || qh % 16 || qh >= (1 << 16)) return ABKV_ERR_UNSUPPORTED;
+      prm.side_off[h] = sum;
+      prm.side_q[h] = qh;
+      sum += qh;
+    }
+    if (sum != side->slots) return ABKV_ERR_INVALID_ARG;
+    const cuuint64_t dims[4] = {(cuuint64_t)kD, 1, (cuuint64_t)side->slots, (cuuint64_t)(2 * side->num_pages)};
+    const cuuint64_t gstr[3] = {(cuuint64_t)kD * 2, (cuuint64_t)kD * 2, (cuuint64_t)side->slots * kD * 2};
+    const cuuint32_t box[4] = {64, 1, 16, 1};
+    const int st = tc::encode_tiled_4d(&prm.tm_side, side->pages, dims, gstr, box);
+    if (st != ABKV_OK) return st;
+    prm.side_bt = side->page_table;
+    prm.side_count = side->page_count;
+    prm.side_bt_stride = side->page_table_stride;
+    prm.side_pages = side->num_pages;
+    prm.has_side = 1;
+  }
   if (cudaFuncSetAttribute(codestep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) !=
       cudaSuccess)
     return ABKV_ERR_CUDA;

@@ -494,6 +494,45 @@ int abkv_paged_prefill(const void* q, int64_t q_row_stride,
                        void* workspace, size_t workspace_bytes,
                        void* stream);
 
+/* The code step and the causal paged attention of requests that hold packed
+ * sidecar pages (per-head quotas): PackedKVSidecar._attend_request_vectorized
+ * with layer_pages (third_party/vllm_overlay/vllm/v1/worker/
+ * compresslm_packed_kv.py:648-741, noncausal :708-733 and causal :700-707).
+ * For KV head h of request r the keys are, first, head h's slots of each of
+ * the request's sidecar->page_count[r] packed pages (the layout of
+ * abkv_decode_packed), visible to every query row, then the paged rows with
+ * the masks of abkv_code_step_attention / abkv_paged_prefill.  Arguments as
+ * those two entries plus one sidecar descriptor (quotas: multiples of 16,
+ * at most 8 KV heads). */
+int abkv_code_step_attention_packed(const void* q, int64_t q_row_stride,
+                                    int64_t q_head_stride, void* out,
+                                    int64_t out_row_stride,
+                                    int64_t out_head_stride,
+                                    const int32_t* q_start, const void* kv_cache,
+                                    int kv_layout, int64_t num_blocks,
+                                    int page_size, const int32_t* block_table,
+                                    int64_t bt_stride, const int32_t* seq_lens,
+                                    const int32_t* excluded,
+                                    const int32_t* quota_per_kv_head, int R,
+                                    int Hq, int Hkv, int head_dim, int K_code,
+                                    int T, float scale,
+                                    const abkv_sidecar_t* sidecar,
+                                    void* workspace, size_t workspace_bytes,
+                                    void* stream);
+
+int abkv_paged_prefill_packed(const void* q, int64_t q_row_stride,
+                              int64_t q_head_stride, void* out,
+                              int64_t out_row_stride, int64_t out_head_stride,
+                              const int32_t* query_start_loc,
+                              const void* kv_cache, int kv_layout,
+                              int64_t num_blocks, int page_size,
+                              const int32_t* block_table, int64_t bt_stride,
+                              const int32_t* seq_lens, int R, int Hq, int Hkv,
+                              int head_dim, int max_query_len, int T,
+                              float scale, const abkv_sidecar_t* sidecar,
+                              void* workspace, size_t workspace_bytes,
+                              void* stream);
+
 /* The code step fused with the compaction that follows it in the block
  * boundary flow (CompressLMProcessor._compact_response_content,
  * third_party/vllm_overlay/vllm/v1/core/compresslm/processor.py:467-557,

@@ -236,3 +236,48 @@ def packed_decode_exact(q, kv, block_table, seq_lens, side_pages, counts, quotas
             e = np.exp(s - s.max())
             out[b, h] = (e / e.sum()) @ vals
     return out
+
+
+def packed_step_exact(qrows, kv, block_table, seq_lens, query_start, side_pages, counts, quotas, causal, scale,
+                      page, excluded=None) -> np.ndarray:
+    """The code step (causal=False) or causal rows of requests holding packed sidecar pages, in float64:
+    PackedKVSidecar._attend_request_vectorized with layer_pages (compresslm_packed_kv.py:648-741).
+    For KV head h of request r the keys are head h's slots [off_h, off_h + quotas[h]) of each of its
+    counts[r] pages (side_pages[first_r + i], [2, slots, D]; every query row sees them), then its main
+    rows [0, seq_len): noncausal, rows < prefix + quotas[h] minus the optional excluded[r] range
+    (:711-726); causal, rows < prefix + i + 1 for query i (:700-707), prefix = seq_len - query_len.
+    Returns [T, Hq, D]."""
+    T, Hq, D = qrows.shape
+    Hkv = kv.shape[3]
+    G = Hq // Hkv
+    off = packed_offsets(quotas)
+    out = np.zeros((T, Hq, D))
+    first = 0
+    for r, s_len in enumerate(seq_lens):
+        s_len = int(s_len)
+        q0, q1 = int(query_start[r]), int(query_start[r + 1])
+        qlen = q1 - q0
+        pages = side_pages[first:first + int(counts[r])]
+        first += int(counts[r])
+        if qlen <= 0:
+            continue
+        k_main, v_main = _gather(kv, block_table[r], s_len, page)
+        prefix = s_len - qlen
+        pos = np.arange(s_len)
+        for h in range(Hq):
+            kh = h // G
+            ks = np.concatenate([pg[0, off[kh]:off[kh + 1]] for pg in pages] + [k_main[:, kh]]).astype(np.float64)
+            vs = np.concatenate([pg[1, off[kh]:off[kh + 1]] for pg in pages] + [v_main[:, kh]]).astype(np.float64)
+            n_side = ks.shape[0] - s_len
+            if causal:
+                hidden_main = pos[None, :] >= (prefix + np.arange(1, qlen + 1))[:, None]
+            else:
+                hidden_main = np.broadcast_to(pos >= prefix + int(quotas[kh]), (qlen, s_len)).copy()
+                if excluded is not None and excluded[r][1] > excluded[r][0]:
+                    hidden_main[:, int(excluded[r][0]):int(excluded[r][1])] = True
+            hidden = np.concatenate([np.zeros((qlen, n_side), bool), hidden_main], axis=1)
+            sc = (qrows[q0:q1, h].astype(np.float64) @ ks.T) * scale
+            sc[hidden] = -np.inf
+            e = np.exp(sc - sc.max(axis=1, keepdims=True))
+            out[q0:q1, h] = (e / e.sum(axis=1, keepdims=True)) @ vs
+    return out

@@ -170,3 +170,25 @@ def config1_paged(decode_layer, page=16, seed=0):
     q = np.stack([steps[s][0] for s in keys])
     out = np.stack([steps[s][2] for s in keys])
     return q, kv, bt, np.asarray(lens, np.int32), out, keys
+
+
+def packedstep_cases():
+    return sorted(p.stem[len("packedstep_"):] for p in GOLDEN.glob("packedstep_*.npz"))
+
+
+def load_packedstep(name: str):
+    """-> dict(case, qrows [T,Hq,D], qstart [R+1], side pages, counts, quotas, k_max, causal, excluded or
+    None, rows kept, reference output at those rows) of tests/golden/packedstep_<name>.npz."""
+    from tests.golden.make_golden import causal_query_rows, packed_side_pages
+
+    z = np.load(GOLDEN / f"packedstep_{name}.npz")
+    case = paged_case(int(z["seed"]), z["seq_lens"], num_q_heads=int(z["num_q_heads"]),
+                      num_kv_heads=int(z["num_kv_heads"]), head_dim=128, page=int(z["page"]))
+    qlens = z["query_lens"].astype(np.int64)
+    qstart = np.concatenate([[0], np.cumsum(qlens)]).astype(np.int32)
+    qrows = causal_query_rows(int(z["seed"]), int(qlens.sum()), int(z["num_q_heads"]))
+    side = packed_side_pages(int(z["seed"]), z["counts"], int(z["quotas"].sum()), 128)
+    excl = z["excluded"] if len(z["excluded"]) else None
+    return dict(case=case, qrows=qrows, qstart=qstart, side=side, counts=z["counts"], quotas=z["quotas"],
+                k_max=int(z["k_max"]), causal=bool(z["causal"]), excluded=excl, rows=z["rows"],
+                ref=from_bits(z["out_bits"]))

@@ -259,3 +259,42 @@ def test_store_kv_skips_padding_and_takes_both_layouts():
     bad[0] = nb * page  # past the cache: flagged, skipped
     store_kv(key, value, kv, bad, workspace=ws)
     assert ws.read_error() & 0x8  # ABKV_DEVERR_ROW_OOB
+
+
+@pytest.mark.parametrize("name", ["code_qwen", "causal_g4"])
+def test_override_attention_steps_with_sidecar_pages(name):
+    """maybe_override_attention on a code step and on causal chunks of requests that already hold
+    packed pages (captured through CompressedKVSidecar's page store): the reference sidecar's outputs."""
+    from oracle.decode_ref import packed_step_exact
+    from tests.goldens import load_packedstep
+
+    g = load_packedstep(name)
+    c = g["case"]
+    quotas = [int(x) for x in g["quotas"]]
+    Hq, Hkv, D = g["qrows"].shape[1], len(quotas), 128
+    R = len(c.seq_lens)
+    layout = PackedKVLayout.from_schedule([quotas], num_layers=1, num_kv_heads=Hkv, k_max=g["k_max"])
+    layers = _layers(1, Hq, Hkv, c.scale)
+    sc = attention.CompressedKVSidecar(layout, layers, block_size=c.page, max_requests=R, head_dim=D,
+                                       max_pages_per_request=int(max(g["counts"])) + 1)
+    attention.install_sidecar(layers, sc)
+    rids = [f"r{r}" for r in range(R)]
+    first = 0
+    for r, cnt in enumerate(g["counts"]):
+        if cnt:
+            sc.pages[rids[r]] = [[_bf(g["side"][first + i]) for i in range(int(cnt))]]
+        first += int(cnt)
+    sc.set_active_request_ids(rids)
+    qlens = np.diff(g["qstart"]).tolist()
+    sc.set_common_attn_metadata(_common(qlens, c, causal=g["causal"]))
+    T = g["qrows"].shape[0]
+    out = torch.zeros((T, Hq * D), dtype=torch.bfloat16, device="cuda")
+    attention.maybe_override_attention(layers[0], _bf(g["qrows"]).view(T, Hq * D), _bf(c.kv), object(), out)
+    got = out.view(T, Hq, D).float().cpu().numpy()
+    exact = packed_step_exact(g["qrows"], c.kv, c.block_table, c.seq_lens, g["qstart"], g["side"], g["counts"],
+                              g["quotas"], g["causal"], c.scale, c.page, g["excluded"])
+    se, _ = report(f"override packed step {name}", got, exact)
+    assert se["max_abs"] <= ATOL_EXACT and se["mean_abs"] <= MEAN_EXACT
+    assert_relative(se)
+    _, sr = report(f"override packed step {name} (reference rows)", got[g["rows"]], exact[g["rows"]], g["ref"])
+    assert sr["max_abs"] <= ATOL_REF

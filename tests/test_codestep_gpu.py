@@ -311,3 +311,60 @@ def test_paged_prefill_understated_max_query_len_is_flagged():
     last = int(qstart[2])  # request 2 has 250 rows: its first 128 are computed, the rest are not
     assert torch.equal(short[:last + 128], full[:last + 128])
     assert torch.isnan(short[last + 128:].float()).all()
+
+
+from oracle.decode_ref import packed_step_exact  # noqa: E402
+from tests.goldens import load_packedstep, packedstep_cases  # noqa: E402
+
+
+def _packed_pool(g, spare=3):
+    """SidecarPool of the golden's packed pages (request slot r = request r), spare pages poisoned."""
+    from abridgekv_b200.sidecar import PackedKVLayout, SidecarPool
+
+    quotas = [int(x) for x in g["quotas"]]
+    layout = PackedKVLayout.from_schedule([quotas], num_layers=1, num_kv_heads=len(quotas), k_max=g["k_max"])
+    counts = [int(c) for c in g["counts"]]
+    pool = SidecarPool(layout, 0, capacity=sum(counts) + spare, num_requests=len(counts),
+                       max_pages=max(1, max(counts)) + 1, head_dim=128)
+    pool.pages.fill_(float("nan"))
+    first = 0
+    for r, cnt in enumerate(counts):
+        for i in range(cnt):
+            pool.append(r, torch.from_numpy(g["side"][first + i]).to(torch.bfloat16).cuda())
+        first += cnt
+    return layout, pool
+
+
+@pytest.mark.parametrize("name", packedstep_cases())
+def test_packed_step_matches_reference_golden(name):
+    """Code steps and causal chunks of requests holding packed sidecar pages
+    (abkv_code_step_attention_packed / abkv_paged_prefill_packed) against the reference's
+    _attend_request_vectorized with layer_pages and the float64 oracle; the pool's spare pages are
+    poisoned, so a read outside the requests' pages shows up as NaN."""
+    g = load_packedstep(name)
+    c = g["case"]
+    layout, pool = _packed_pool(g)
+    quotas = [int(x) for x in g["quotas"]]
+    q = torch.from_numpy(g["qrows"]).to(torch.bfloat16).cuda()
+    kv = torch.from_numpy(c.kv).to(torch.bfloat16).cuda()
+    bt, sl = torch.from_numpy(c.block_table).cuda(), torch.from_numpy(c.seq_lens).cuda()
+    qs = torch.from_numpy(g["qstart"]).cuda()
+    ws = Workspace()
+    if g["causal"]:
+        out = codestep.paged_prefill(q, kv, bt, sl, qs, max_query_len=int(np.diff(g["qstart"]).max()),
+                                     num_kv_heads=len(quotas), scale=c.scale, workspace=ws, sidecar=pool)
+    else:
+        ex = torch.from_numpy(g["excluded"]).cuda() if g["excluded"] is not None else None
+        out = codestep.code_step_attention(q, kv, bt, sl, qs, quota_per_kv_head=quotas, k_max=g["k_max"],
+                                           scale=c.scale, excluded=ex, workspace=ws, sidecar=pool)
+    torch.cuda.synchronize()
+    assert ws.read_error() == 0
+    got = out.float().cpu().numpy()
+    assert np.isfinite(got).all()
+    exact = packed_step_exact(g["qrows"], c.kv, c.block_table, c.seq_lens, g["qstart"], g["side"], g["counts"],
+                              g["quotas"], g["causal"], c.scale, c.page, g["excluded"])
+    se, _ = report(f"packed step {name}", got, exact)
+    assert se["max_abs"] <= ATOL_EXACT and se["mean_abs"] <= MEAN_EXACT
+    assert_relative(se, name)
+    _, sr = report(f"packed step {name} (reference rows)", got[g["rows"]], exact[g["rows"]], g["ref"])
+    assert sr["max_abs"] <= ATOL_REF

@@ -127,3 +127,21 @@ def test_paged_causal_oracle_matches_reference(name):
     assert np.isfinite(ref).all()
     assert np.abs(ex[rows] - ref).max() < 3e-2
     assert np.abs(ex[rows] - ref).mean() < 2e-3
+
+
+
+from oracle.decode_ref import packed_step_exact  # noqa: E402
+from tests.goldens import load_packedstep, packedstep_cases  # noqa: E402
+
+
+@pytest.mark.parametrize("name", packedstep_cases())
+def test_packed_step_oracle_matches_reference(name):
+    """The float64 restatement of _attend_request_vectorized with packed sidecar pages (code steps and
+    causal chunks) against the reference's own outputs, within its bf16 rounding budget."""
+    g = load_packedstep(name)
+    c = g["case"]
+    ex = packed_step_exact(g["qrows"], c.kv, c.block_table, c.seq_lens, g["qstart"], g["side"], g["counts"],
+                           g["quotas"], g["causal"], c.scale, c.page, g["excluded"])
+    assert np.isfinite(g["ref"]).all()
+    assert np.abs(ex[g["rows"]] - g["ref"]).max() < 3e-2
+    assert np.abs(ex[g["rows"]] - g["ref"]).mean() < 2e-3
