@@ -10,22 +10,28 @@
 // out = softmax(q.k^T * scale + mask) v with an fp32 online softmax.
 //
 // CTA = one 128-row query tile of TWO query heads of the same KV head (both
-// heads share every K/V tile); 64-key tiles; 10 warps:
+// heads share every K/V tile); 64-key tiles; 19 warps:
 //   warp 0      TMA producer: Q of both heads, then the tile's four 16-row page
 //               slices of K and V into a 4-stage ring (cp.async.bulk.tensor,
 //               128B swizzle, no multicast); the block table is read 32 entries
 //               at a time, one lane per slice, the next read in flight
 //   warp 1      TMEM owner (512 columns: per head two S buffers + O); lane 0
-//               issues tcgen05.mma in the order
-//               S_A(0) S_B(0) S_A(1) S_B(1) | PV_A(j) S_A(j+2) PV_B(j) S_B(j+2) | ...
+//               issues head A's tcgen05.mma: S_A(0) S_A(1) | PV_A(j) S_A(j+2) | ...
+//   warp 18     lane 0 issues head B's the same way
 //                 S  = Q K^T   (A = Q, B = K, both K-major, fp32 in TMEM)
 //                 O += P V     (A = P from TMEM, B = V, MN-major)
-//   warps 2..5  softmax of head A, warps 6..9 softmax of head B: thread = one
-//               TMEM lane = one query row; masked online softmax in fp32, P
-//               (bf16 pairs) stored into the upper half of its own S buffer with
-//               tcgen05.st -- P is double-buffered with S, so a head's softmax of
-//               tile j+1 waits for its P.V of tile j only to rescale O; epilogue
-//               divides by the row sum.  The S MMA of tile j+2 overwrites P(j)
+//               One issuer per head: an issuing thread's own mbarrier waits stall
+//               behind the MMA operand reads it has queued (a few MMAs deep), so a
+//               single issuer for both heads left the tensor core idle at every wait.
+//   warps 2..9  softmax of head A, warps 10..17 softmax of head B: thread = one
+//               TMEM lane = one query row, two warps per row quarter, each with
+//               32 of the tile's 64 columns (they exchange partial row maxima at
+//               a named barrier: one warp per row's 64 columns is bound by its own
+//               instruction latencies, not by MUFU or the tensor core); masked
+//               online softmax in fp32, P (bf16 pairs) stored into the upper half
+//               of its own S buffer with tcgen05.st -- P is double-buffered with
+//               S, so a head's softmax of tile j+1 waits for its P.V of tile j
+//               only to rescale O; epilogue divides by the row sum.  The S MMA of tile j+2 overwrites P(j)
 //               after P.V(j) read it: tcgen05.mma operations of one thread run
 //               in issue order.
 // With all tiles full (no causal diagonal), the double-buffered S keeps the
@@ -42,7 +48,10 @@ namespace {
 using namespace tc;
 
 constexpr int kBM = 128, kBN = 64, kD = 128;
-constexpr int kThreads = 320;
+// warp 0 producer, warp 1 head A's MMA issuer (and TMEM owner), warps 2..17 softmax: 8 per head,
+// two per TMEM lane quarter (each owns 32 of a tile's 64 columns), warp 18 head B's MMA issuer
+constexpr int kThreads = 608;
+constexpr int kWarpIssuerB = 18;
 constexpr int kMaxHeads = 128;
 constexpr int kStages = 4;
 constexpr uint32_t kTmemCols = 512;  // per head (A at 0, B at 256): S buffers [0,64) [64,128), O [128,256)
@@ -57,18 +66,25 @@ constexpr int kStageBytes = 2 * kKVHalf;       // K then V
 constexpr int kOffQ = 0;                        // Q_A, Q_B
 constexpr int kOffKV = 2 * kQBytes;
 constexpr int kOffBar = kOffKV + kStages * kStageBytes;
-// mbarriers (u64 slots from kOffBar): q_full, kv_full[kStages], kv_empty[kStages],
-// s_full[head][S buffer], p_full[head][S buffer], o_done[head], o_full, then the TMEM
-// address.  p_full is double-buffered like S: a head's softmax may finish tile j+1
+// mbarriers (u64 slots from kOffBar): q_full, kv_full[kStages], kv_empty[kStages] (one
+// arrival per head's P.V), s_full[head][S buffer], p_full[head][S buffer], o_done[head],
+// o_full[head], v_zero[2] (head A's softmax warps have zeroed the V rows past the valid rows
+// of the last sidecar tile / the last cache tile: head B's P.V of that tile waits for it),
+// then the TMEM address.  p_full is double-buffered like S: a head's softmax may finish tile j+1
 // before the MMA thread has taken tile j's P, and one barrier per buffer keeps the
 // two arrivals in different barriers (a parity wait cannot tell phases 2 apart).
 constexpr int kBarKvFull = 1, kBarKvEmpty = kBarKvFull + kStages, kBarSFull = kBarKvEmpty + kStages,
               kBarPFull = kBarSFull + 4, kBarODone = kBarPFull + 4, kBarOFull = kBarODone + 2,
-              kBarTmem = kBarOFull + 1;
+              kBarVZero = kBarOFull + 2, kBarTmem = kBarVZero + 2;
 static_assert((kBarTmem + 1) * 8 <= 256, "barrier area");
 constexpr int kOffList = kOffBar + 256;         // visited key tiles (tile indices)
 constexpr int kMaxKeyTiles = 2048;              // keys up to 2048 x 64 = 128K rows
-constexpr int kSmemBytes = kOffList + 4 * kMaxKeyTiles + 16 + 1024;  // + slack for 1024-byte alignment
+// exchange between the two warps of a row quarter: partial row maxima [2 parity][2 heads][2 halves][128]
+// and, at the end, partial row sums [2 heads][2 halves][128]
+constexpr int kOffXchg = kOffList + 4 * kMaxKeyTiles + 16;
+constexpr int kXchgMax = 2 * 2 * 2 * 128 * 4, kXchgSum = 2 * 2 * 128 * 4;
+constexpr int kSmemBytes = kOffXchg + kXchgMax + kXchgSum + 1024;  // + slack for 1024-byte alignment
+static_assert(kSmemBytes <= 227 * 1024, "shared memory");
 // Lazy rescaling: a row keeps its reference maximum until a tile's maximum
 // exceeds it by more than this (log2 units), so P <= 2^8 and O is rescaled
 // only on large jumps (O and the row sum always share the reference).
@@ -150,80 +166,86 @@ __device__ __noinline__ void commit_request_ops(const CodeStepParams& p, bool de
   }
 }
 
-// Softmax of one (head, key tile) for query row `row` (= TMEM lane):
-// reads S, updates the reference maximum / row sum, waits until the previous
-// P.V of this head has completed (o_done), rescales O when needed and writes
-// P (bf16, 128B-swizzled K-major: 16-byte chunk index ^= row % 8).
+// Softmax of one (head, key tile) for query row `row` (= TMEM lane), columns
+// [32 half, 32 half + 32) of the tile; the partner warp (same rows, other half)
+// does the rest.  The two exchange their partial row maxima through shared
+// memory (xm_mine / xm_other, one float per row) at the pair's named barrier,
+// so both take the same lazy-rescale decision and reference maximum; each keeps
+// the row sum of its own columns and rescales its own half of O.  P (bf16,
+// 16 words) goes into this half's columns of the upper half of the S buffer.
 // kHole: columns [hs, he) are hidden as well (the code step's tail exclusion).
 template <bool kHole>
-__device__ __forceinline__ void softmax_tile(const CodeStepParams& p, int lim, int hs, int he, int row,
+__device__ __forceinline__ void softmax_half(const CodeStepParams& p, int lim, int hs, int he, int half, int row,
                                              uint32_t tmem_s, uint32_t tmem_o, uint32_t lane_base, int j,
-                                             uint64_t* o_done, bool& dead, SoftmaxState& st) {
+                                             uint64_t* o_done, bool& dead, SoftmaxState& st, float* xm_mine,
+                                             const float* xm_other, int pair_bar) {
   const float sl2 = p.scale_log2;  // lim: visible columns of this row are c < lim
-  float t0[32], t1[32];
-  tmem_ld32(tmem_s + lane_base, t0);
-  tmem_ld32(tmem_s + lane_base + 32, t1);
+  const int c0 = 32 * half;
+  float t[32];
+  tmem_ld32(tmem_s + lane_base + c0, t);
   tmem_wait_ld();
   auto vis = [&](int c) { return c < lim && (!kHole || c < hs || c >= he); };
   const bool full = lim == kBN && (!kHole || he <= 0 || hs >= kBN);
   float mxa[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // independent chains
   if (full) {
 #pragma unroll
-    for (int i = 0; i < 32; ++i) mxa[i & 3] = fmax3(mxa[i & 3], t0[i], t1[i]);
+    for (int i = 0; i < 16; ++i) mxa[i & 3] = fmax3(mxa[i & 3], t[2 * i], t[2 * i + 1]);
   } else {
 #pragma unroll
-    for (int i = 0; i < 32; ++i)
-      mxa[i & 3] = fmax3(mxa[i & 3], vis(i) ? t0[i] : -INFINITY, vis(i + 32) ? t1[i] : -INFINITY);
+    for (int i = 0; i < 16; ++i)
+      mxa[i & 3] = fmax3(mxa[i & 3], vis(c0 + 2 * i) ? t[2 * i] : -INFINITY,
+                         vis(c0 + 2 * i + 1) ? t[2 * i + 1] : -INFINITY);
   }
-  const float mx = fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3])) * sl2;
+  const float mpart = fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3]));
+  xm_mine[row] = mpart;
+  // both warps' S loads are complete (wait::ld) before either stores P over columns [32, 64)
+  tc_fence_before();
+  named_bar_sync(pair_bar, 64);
+  tc_fence_after();
+  const float mx = fmaxf(mpart, xm_other[row]) * sl2;  // the row's maximum over both halves
   const bool need = mx > st.m_run + kRescaleThreshold || (st.m_run == -INFINITY && mx > -INFINITY);
   const float m_new = need ? mx : st.m_run;
   const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
   const float alpha = need ? fast_exp2(st.m_run - m_use) : 1.f;
   float rsa[4][2] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};  // packed pair accumulators
-  uint32_t w[8][4];
+  uint32_t w[16];
 #pragma unroll
-  for (int half = 0; half < 2; ++half) {
-    const float* t = half ? t1 : t0;
-#pragma unroll
-    for (int e8 = 0; e8 < 4; ++e8) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int c = half * 32 + e8 * 8 + 2 * e;
-        float x0, x1;
-        ffma2(x0, x1, t[e8 * 8 + 2 * e], t[e8 * 8 + 2 * e + 1], sl2, -m_use);
-        float p0 = fast_exp2(x0);
-        float p1 = fast_exp2(x1);
-        if (!full) {
-          p0 = vis(c) ? p0 : 0.f;
-          p1 = vis(c + 1) ? p1 : 0.f;
-        }
-        fadd2(rsa[e][0], rsa[e][1], p0, p1);
-        w[half * 4 + e8][e] = pack_bf16x2(p0, p1);
-      }
+  for (int i = 0; i < 16; ++i) {
+    const int c = c0 + 2 * i;
+    float x0, x1;
+    ffma2(x0, x1, t[2 * i], t[2 * i + 1], sl2, -m_use);
+    float p0 = fast_exp2(x0);
+    float p1 = fast_exp2(x1);
+    if (!full) {
+      p0 = vis(c) ? p0 : 0.f;
+      p1 = vis(c + 1) ? p1 : 0.f;
     }
+    fadd2(rsa[i & 3][0], rsa[i & 3][1], p0, p1);
+    w[i] = pack_bf16x2(p0, p1);
   }
   fadd2(rsa[0][0], rsa[0][1], rsa[1][0], rsa[1][1]);
   fadd2(rsa[2][0], rsa[2][1], rsa[3][0], rsa[3][1]);
   st.l_run = st.l_run * alpha + ((rsa[0][0] + rsa[0][1]) + (rsa[2][0] + rsa[2][1]));
   st.m_run = m_new;
-  // P(j) into the upper half of this tile's S buffer (already read into registers);
-  // the buffer's previous P was consumed by P.V(j-2), which completed before S(j)
+  // P(j) into this half's columns of the upper half of the tile's S buffer (already read into
+  // registers); the buffer's previous P was consumed by P.V(j-2), which completed before S(j)
   // was signalled
-  tmem_st32(tmem_s + lane_base + kPCol, reinterpret_cast<const float(&)[32]>(w));
+  tmem_st16(tmem_s + lane_base + kPCol + 16 * half, w);
   if (j > 0 && __any_sync(0xffffffffu, need)) {
-    // O is touched only after the previous P.V of this head completed
+    // O is touched only after the previous P.V of this head completed; the partner warp takes
+    // the same branch (same rows, same maxima) and rescales the other half of O's columns
     const bool ok = __all_sync(0xffffffffu, wait_or_abort(o_done, (uint32_t)((j - 1) & 1), dead, p.err));
     tc_fence_after();
     if (ok) {
 #pragma unroll 1
-      for (int c4 = 0; c4 < 4; ++c4) {
-        float t[32];
-        tmem_ld32(tmem_o + lane_base + c4 * 32, t);
+      for (int c4 = 0; c4 < 2; ++c4) {
+        float o[32];
+        const uint32_t col = tmem_o + lane_base + 64 * half + 32 * c4;
+        tmem_ld32(col, o);
         tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) t[i] *= alpha;
-        tmem_st32(tmem_o + lane_base + c4 * 32, t);
+        for (int i = 0; i < 32; ++i) o[i] *= alpha;
+        tmem_st32(col, o);
       }
     }
   }
@@ -240,7 +262,8 @@ __global__ void __launch_bounds__(kThreads, 1) codestep_kernel(const __grid_cons
   uint64_t* s_full = bar + kBarSFull;      // [head][S buffer]
   uint64_t* p_full = bar + kBarPFull;      // [head][S buffer]
   uint64_t* o_done = bar + kBarODone;      // [head]: one phase per P.V
-  uint64_t* o_full = bar + kBarOFull;
+  uint64_t* o_full = bar + kBarOFull;      // [head]
+  uint64_t* v_zero = bar + kBarVZero;      // [sidecar, cache]: used at most once each
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bar + kBarTmem);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -319,13 +342,15 @@ __global__ void __launch_bounds__(kThreads, 1) codestep_kernel(const __grid_cons
     mbar_init(q_full, 1);
     for (int i = 0; i < kStages; ++i) {
       mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
+      mbar_init(&kv_empty[i], hB >= 0 ? 2 : 1);
     }
     for (int i = 0; i < 4; ++i) mbar_init(&s_full[i], 1);
-    for (int i = 0; i < 4; ++i) mbar_init(&p_full[i], 128);
-    mbar_init(&o_done[0], 1);
-    mbar_init(&o_done[1], 1);
-    mbar_init(o_full, 1);
+    for (int i = 0; i < 4; ++i) mbar_init(&p_full[i], 256);  // the 8 softmax warps of a head
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&o_done[i], 1);
+      mbar_init(&o_full[i], 1);
+      mbar_init(&v_zero[i], 256);
+    }
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(s_tmem)),
@@ -448,14 +473,25 @@ __global__ void __launch_bounds__(kThreads, 1) codestep_kernel(const __grid_cons
         cur = nxt;
       }
     }
-  } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
-    if (lane == 0) {
-      const bool two = hB >= 0;
+  } else if (warp == 1 || warp == kWarpIssuerB) {
+    // ---------------- MMA issuers: warp 1 head A, warp 18 head B ----------------
+    // One issuing thread per head: a thread's shared-memory accesses (its mbarrier waits)
+    // wait behind the tcgen05.mma operand reads it has queued, so while one issuer waits
+    // the other's queued MMAs keep the tensor core busy.
+    const int hs = warp == 1 ? 0 : 1;
+    if (lane == 0 && (hs == 0 || hB >= 0)) {
+      // head B's P.V of a partial tile (the last sidecar tile, the last cache tile) waits
+      // until head A's softmax warps have zeroed its V rows past the valid rows; the two
+      // tile indices, read before any MMA is issued
+      int jz0 = -1, jz1 = -1;
+      if (hs == 1) {
+        if (n_side % kBN) jz0 = side_tiles - 1;
+        if (n_tiles > side_tiles && (seq_len % kBN) && s_list[n_tiles - 1] == (seq_len - 1) / kBN) jz1 = n_tiles - 1;
+      }
       wait_or_abort(q_full, 0, dead, p.err);
-      const uint32_t qa = smem_u32(smem + kOffQ), qbv = qa + kQBytes;
-      const uint32_t sA = tmem, oA = tmem + 128, sB = tmem + 256, oB = tmem + 384;
-      auto issue_s = [&](uint32_t qaddr, uint32_t sd, int st) {
+      const uint32_t qaddr = smem_u32(smem + kOffQ) + hs * kQBytes;
+      const uint32_t sbase = tmem + 256 * hs, obase = sbase + 128;
+      auto issue_s = [&](uint32_t sd, int st) {
         const uint64_t dq = desc_kmajor_sw128(qaddr);
         const uint64_t dk = desc_kmajor_sw128(smem_u32(smem + kOffKV + st * kStageBytes));
 #pragma unroll
@@ -464,66 +500,61 @@ __global__ void __launch_bounds__(kThreads, 1) codestep_kernel(const __grid_cons
                desc_advance(dk, (kk >> 2) * (kKVHalf / 2) + (kk & 3) * 32), kIdescQK, kk > 0 ? 1u : 0u);
         }
       };
-      auto issue_pv = [&](uint32_t ptmem, uint32_t od, int st, bool first) {
+      auto issue_pv = [&](uint32_t ptmem, int st, bool first) {
         const uint64_t dv = desc_mnmajor_sw128(smem_u32(smem + kOffKV + st * kStageBytes + kKVHalf), kKVHalf / 2);
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk) {  // over the tile's keys in steps of 16 (8 TMEM columns)
-          umma_tmem_a(od, ptmem + kk * 8, desc_advance(dv, kk * 2048), kIdescPV, (!first || kk > 0) ? 1u : 0u);
+          umma_tmem_a(obase, ptmem + kk * 8, desc_advance(dv, kk * 2048), kIdescPV, (!first || kk > 0) ? 1u : 0u);
         }
       };
-      // tile sequence; S of tile j goes to S buffer j % 2 of each head
+      // tile sequence; S of tile j goes to S buffer j % 2
       const int n = n_tiles;
       for (int t = 0; t < 2 && t < n && !dead; ++t) {
         if (!wait_or_abort(&kv_full[t], 0, dead, p.err)) break;
         tc_fence_after();
-        issue_s(qa, sA + 64 * t, t);
-        umma_commit(&s_full[t]);
-        if (two) {
-          issue_s(qbv, sB + 64 * t, t);
-          umma_commit(&s_full[2 + t]);
-        }
+        issue_s(sbase + 64 * t, t);
+        umma_commit(&s_full[2 * hs + t]);
       }
       for (int j = 0; j < n && !dead; ++j) {
         const int st = j % kStages, st2 = (j + 2) % kStages;
         const bool more = j + 2 < n;
-        // head A: P_A(j) V_j; S_A(j+2) into the S buffer softmax A(j) has released
-        if (!wait_or_abort(&p_full[j & 1], (uint32_t)((j >> 1) & 1), dead, p.err)) break;
+        // all waits of the step first (after the first one the queue has drained, so the
+        // next cost no further stall), then P(j) V_j and S(j+2) into the S buffer that
+        // softmax(j) has released
+        if (more && !wait_or_abort(&kv_full[st2], (uint32_t)(((j + 2) / kStages) & 1), dead, p.err)) break;
+        if (!wait_or_abort(&p_full[2 * hs + (j & 1)], (uint32_t)((j >> 1) & 1), dead, p.err)) break;
+        if (j == jz0 && !wait_or_abort(&v_zero[0], 0, dead, p.err)) break;
+        if (j == jz1 && !wait_or_abort(&v_zero[1], 0, dead, p.err)) break;
         tc_fence_after();
-        issue_pv(sA + 64 * (j & 1) + kPCol, oA, st, j == 0);
-        umma_commit(&o_done[0]);
-        if (!two) umma_commit(&kv_empty[st]);
+        issue_pv(sbase + 64 * (j & 1) + kPCol, st, j == 0);
+        umma_commit(&o_done[hs]);
+        umma_commit(&kv_empty[st]);  // this head's last use of the K/V stage
         if (more) {
-          if (!wait_or_abort(&kv_full[st2], (uint32_t)(((j + 2) / kStages) & 1), dead, p.err)) break;
-          tc_fence_after();
-          issue_s(qa, sA + 64 * (j & 1), st2);
-          umma_commit(&s_full[j & 1]);
-        }
-        if (two) {
-          // head B: P_B(j) V_j (last use of this K/V stage), then S_B(j+2)
-          if (!wait_or_abort(&p_full[2 + (j & 1)], (uint32_t)((j >> 1) & 1), dead, p.err)) break;
-          tc_fence_after();
-          issue_pv(sB + 64 * (j & 1) + kPCol, oB, st, j == 0);
-          umma_commit(&o_done[1]);
-          umma_commit(&kv_empty[st]);
-          if (more) {
-            issue_s(qbv, sB + 64 * (j & 1), st2);
-            umma_commit(&s_full[2 + (j & 1)]);
-          }
+          issue_s(sbase + 64 * (j & 1), st2);
+          umma_commit(&s_full[2 * hs + (j & 1)]);
         }
       }
-      umma_commit(o_full);
+      umma_commit(&o_full[hs]);
     }
   } else {
     // ---------------- softmax / correction / epilogue ----------------
-    const int head_slot = (warp - 2) >> 2;          // 0: head A (warps 2..5), 1: head B (warps 6..9)
+    const int sw = warp - 2;                         // 0..15
+    const int head_slot = sw >> 3;                   // 0: head A (warps 2..9), 1: head B (warps 10..17)
+    const int half = (sw >> 2) & 1;                  // columns [32 half, 32 half + 32) of every tile
     const int h = head_slot ? hB : hA;
     const int quarter = warp & 3;                    // TMEM lane quarter this warp may access
     const int row = quarter * 32 + lane;             // query row within the tile
     const int q = qt * kBM + row;
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
     const uint32_t tmem_h = tmem + (head_slot ? 256 : 0), tmem_o = tmem_h + 128;
+    // the two warps of these rows (warps w and w + 4) meet at named barrier 1 + head x 4 + quarter;
+    // every exit from the tile loop is decided jointly (named_bar_and), so both always execute
+    // the same barriers
+    const int pair_bar = 1 + head_slot * 4 + quarter;
+    float* xmax = reinterpret_cast<float*>(smem + kOffXchg);            // [parity][head][half][128]
+    float* xsum = reinterpret_cast<float*>(smem + kOffXchg + kXchgMax) + head_slot * 256;  // [half][128]
     if (h >= 0) {
-      SoftmaxState st{-INFINITY, 0.f};
+      SoftmaxState st{-INFINITY, 0.f};  // l_run: the row sum of this warp's columns
       // causal: row q sees seq_len - qlen + q + 1 keys (rows past the request's
       // last row, which are never written, take the last row's limit)
       const int leff = p.causal ? seq_len - qlen + min(q, qlen - 1) + 1 : (head_slot ? leffB : leffA);
@@ -533,9 +564,11 @@ __global__ void __launch_bounds__(kThreads, 1) codestep_kernel(const __grid_cons
         const int lim = side ? min(max(n_side - (-e - 1) * kBN, 0), kBN) : min(max(leff - e * kBN, 0), kBN);
         // valid rows of the tile: the rest was not loaded (V zeroed below)
         const int valid = side ? n_side - (-e - 1) * kBN : seq_len - e * kBN;
-        // warp-uniform decision: tcgen05.ld is a warp-collective
-        const bool ok = __all_sync(
-            0xffffffffu, wait_or_abort(&s_full[2 * head_slot + (j & 1)], (uint32_t)((j >> 1) & 1), dead, p.err));
+        // warp-uniform (tcgen05.ld is a warp-collective) and pair-uniform decision
+        const bool ok = named_bar_and(
+            pair_bar, 64,
+            __all_sync(0xffffffffu,
+                       wait_or_abort(&s_full[2 * head_slot + (j & 1)], (uint32_t)((j >> 1) & 1), dead, p.err)));
         if (!ok) {
           dead = true;
           break;
@@ -547,34 +580,42 @@ __global__ void __launch_bounds__(kThreads, 1) codestep_kernel(const __grid_cons
           // them (P is 0 there, but 0 * NaN would not be)
           const int first = max(valid, 0);
           uint8_t* vb = smem + kOffKV + (j % kStages) * kStageBytes + kKVHalf;
-          const int wt = (warp - 2) * 32 + lane;
-          for (int idx = wt; idx < 2 * (kBN - first) * 8; idx += 128) {
+          const int wt = sw * 32 + lane;  // head A's 256 threads
+          for (int idx = wt; idx < 2 * (kBN - first) * 8; idx += 256) {
             const int dh = idx / ((kBN - first) * 8), rem = idx - dh * (kBN - first) * 8;
             *reinterpret_cast<uint4*>(vb + dh * (kKVHalf / 2) + (first + rem / 8) * 128 + (rem & 7) * 16) =
                 make_uint4(0, 0, 0, 0);
           }
           // each thread's zeros are made visible to the tensor core before its
-          // p_full arrival, and both heads' P.V wait for head A's p_full
+          // p_full and v_zero arrivals (head B's P.V waits for v_zero)
           asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+          mbar_arrive_one(&v_zero[side ? 0 : 1]);
         }
-        softmax_tile<true>(p, lim, side ? 0 : hole_s - e * kBN, side ? 0 : hole_e - e * kBN, row,
-                           tmem_h + 64 * (j & 1), tmem_o, lane_base, j, &o_done[head_slot], dead, st);
+        float* xm = xmax + ((j & 1) * 2 + head_slot) * 256;  // parity j: tile j + 2 reuses it after both
+        softmax_half<true>(p, lim, side ? 0 : hole_s - e * kBN, side ? 0 : hole_e - e * kBN, half, row,
+                           tmem_h + 64 * (j & 1), tmem_o, lane_base, j, &o_done[head_slot], dead, st,
+                           xm + half * 128, xm + (1 - half) * 128, pair_bar);
         tc_fence_before();  // P's tcgen05.st completed (wait::st) before the arrival
         mbar_arrive_one(&p_full[2 * head_slot + (j & 1)]);
       }
-      // epilogue
-      const bool o_ok = __all_sync(0xffffffffu, wait_or_abort(o_full, 0, dead, p.err));
+      // epilogue: this warp writes dims [64 half, 64 half + 64) of its rows
+      const bool o_ok =
+          named_bar_and(pair_bar, 64, __all_sync(0xffffffffu, wait_or_abort(&o_full[head_slot], 0, dead, p.err)));
       tc_fence_after();
+      xsum[half * 128 + row] = st.l_run;
+      named_bar_sync(pair_bar, 64);
+      const float l = st.l_run + xsum[(1 - half) * 128 + row];  // the row sum over both halves
       if (o_ok) {
         // a row that saw no visible key (possible in the code step when the
         // quota and the exclusion hide everything) is written as zeros
-        const bool none = !(st.l_run > 0.f);
-        const float inv = none ? 0.f : 1.f / st.l_run;
-        __nv_bfloat16* orow = p.out + (int64_t)(__ldg(p.q_start + b) + q) * p.o_ss + (int64_t)h * p.o_sh;
+        const bool none = !(l > 0.f);
+        const float inv = none ? 0.f : 1.f / l;
+        __nv_bfloat16* orow =
+            p.out + (int64_t)(__ldg(p.q_start + b) + q) * p.o_ss + (int64_t)h * p.o_sh + 64 * half;
 #pragma unroll 1
-        for (int c4 = 0; c4 < 4; ++c4) {
+        for (int c4 = 0; c4 < 2; ++c4) {
           float t[32];
-          tmem_ld32(tmem_o + lane_base + c4 * 32, t);
+          tmem_ld32(tmem_o + lane_base + 64 * half + c4 * 32, t);
           tmem_wait_ld();
           if (none) {
 #pragma unroll

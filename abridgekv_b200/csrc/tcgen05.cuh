@@ -106,6 +106,30 @@ static __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32])
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
+static __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};\n"
+      ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+
+// Named barrier of `count` threads (whole warps) other than the CTA-wide barrier 0.
+static __device__ __forceinline__ void named_bar_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(count) : "memory");
+}
+// Named barrier that also ANDs a per-thread flag over its `count` threads: every participant gets
+// the same answer, so warps that must stay in step take an early exit together.
+static __device__ __forceinline__ bool named_bar_and(int id, int count, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred q, o;\n setp.ne.u32 q, %1, 0;\n bar.red.and.pred o, %2, %3, q;\n selp.u32 %0, 1, 0, o;\n}\n"
+      : "=r"(r)
+      : "r"((uint32_t)v), "r"(id), "r"(count)
+      : "memory");
+  return r != 0;
+}
+
 static __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
