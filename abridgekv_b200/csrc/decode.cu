@@ -845,11 +845,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_split_kernel(const __grid_
 constexpr int kMaxAutoChunkTiles = 384;  // 6144 cache rows
 
 int auto_chunk_tiles(int num_layers, int num_seqs, int max_tiles, int page_tiles, int num_kv_heads) {
-  // Persistent CTAs take items dynamically: aim for >= ~8 items per SM, with
-  // chunks of 16..128 tiles (256..2048 cache rows).
+  // Persistent CTAs take items dynamically: aim for >= ~4 items per SM, with
+  // chunks of 16..128 tiles (256..2048 cache rows).  (A launch of one layer of
+  // a KV-head shard, 256 sequences x 1 KV head: 2048-row chunks take 203 us per
+  // layer, 1024-row chunks -- the choice at >= 8 items per SM -- 221 us; launches
+  // of many layers have items to spare and keep 128 tiles either way.)
   const int64_t total = (int64_t)num_layers * num_seqs * max_tiles;
   int ct = 128;
-  while (ct > 16 && total / ct < 148 * 8) ct >>= 1;
+  while (ct > 16 && total / ct < 148 * 4) ct >>= 1;
   if (ct < page_tiles) ct = page_tiles;
   ct = (ct / page_tiles) * page_tiles;
   // A tile of fewer than 8 KV heads carries fewer bytes, so the per-item costs

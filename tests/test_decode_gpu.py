@@ -182,6 +182,13 @@ def test_config5_one_kv_head_shard_auto_chunk():
     fixed = decode.paged_decode(wl.queries, wl.kv_caches, wl.block_tables, wl.seq_lens,
                                 max_pages_per_seq=wl.max_pages, chunk_tokens=6144)
     assert all(torch.equal(a, b) for a, b in zip(auto, fixed))
+    # one layer per launch (the KV-head-sharded mode): >= 4 items per SM gives 2048-row chunks
+    one = decode.paged_decode(wl.queries[:1], wl.kv_caches[:1], wl.block_tables[:1], wl.seq_lens[:1],
+                              max_pages_per_seq=wl.max_pages, workspace=ws)[0]
+    assert ws.read_error() == 0
+    one_fixed = decode.paged_decode(wl.queries[:1], wl.kv_caches[:1], wl.block_tables[:1], wl.seq_lens[:1],
+                                    max_pages_per_seq=wl.max_pages, chunk_tokens=2048)[0]
+    assert torch.equal(one, one_fixed)
     scale = 1.0 / np.sqrt(wl.head_dim)
     rng = np.random.default_rng(5)
     for l in rng.choice(wl.num_layers, 3, replace=False):
