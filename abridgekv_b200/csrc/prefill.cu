@@ -14,35 +14,36 @@
 // that of torch FlexAttention, which the reference runs for this mask
 // (compress_forward.py:248,1229).
 //
-// Tiling: 128 query rows x 128 keys.  C and K are multiples of 128, so no tile
+// Tiling: 128 query rows x 64 keys.  C and K are multiples of 128, so no tile
 // straddles a block or the content/code boundary, and every tile is FULL,
-// PARTIAL or EMPTY by the analytic classification below (the block structure
-// of _fast_layer_blockmasks, :760-789).  EMPTY tiles are never loaded; inside
-// a PARTIAL tile the visible keys of a row are a prefix of the tile.
+// PARTIAL or EMPTY by the analytic classification of prefill_mask.cuh (the
+// block structure of _fast_layer_blockmasks, :760-789).  EMPTY tiles are never
+// loaded; inside a PARTIAL tile the visible keys of a row are a prefix of the tile.
 //
 // CTA = one 128-row query tile of TWO query heads of the same KV head.  Their
 // masks are the same block structure, so both heads share every K/V tile
-// (loaded once); 10 warps:
-//   warp 0      TMA producer: Q of both heads, then K/V tiles into a 2-stage
-//               ring (cp.async.bulk.tensor, 128B swizzle, no multicast)
-//   warp 1      TMEM owner (512 columns: per head one S/P buffer + O); lane 0
-//               issues tcgen05.mma in the order
-//               S_A(0) S_B(0) | PV_A(j) S_A(j+1) PV_B(j) S_B(j+1) | ...
+// (loaded once into a 4-stage ring); 19 warps:
+//   warp 0      TMA producer: Q of both heads, then the K/V tiles of the visited
+//               list (cp.async.bulk.tensor, 128B swizzle, no multicast)
+//   warp 1      TMEM owner (512 columns: per head two S/P buffers + O); lane 0
+//               issues head A's tcgen05.mma: S_A(0) S_A(1) | PV_A(j) S_A(j+2) | ...
+//   warp 18     lane 0 issues head B's the same way
 //                 S  = Q K^T   (A = Q, B = K, both K-major, fp32 in TMEM)
 //                 O += P V     (A = P from TMEM, B = V, MN-major)
-//               so one head's softmax overlaps the other head's MMAs; 128-key
-//               tiles give every MMA instruction N = 128 (64-key tiles left the
-//               tensor pipe waiting on instruction issue)
-//   warps 2..5  softmax of head A, warps 6..9 softmax of head B: thread = one
-//               TMEM lane = one query row; S read with tcgen05.ld (row maximum
-//               first, then the exponentials), masked online softmax in fp32,
-//               P (bf16 pairs) stored back into the upper half of the S buffer
-//               with tcgen05.st, O rescaled in TMEM when the row maximum grows
-//               (no wait: the S MMA of this tile was issued after the previous
-//               P.V of the head, and its commit covers that P.V); epilogue
-//               divides by the row sum.  The S MMA of tile j+1 overwrites P(j)
-//               after P.V(j) read it: tcgen05.mma operations of one thread run
-//               in issue order.
+//               One issuer per head: an issuing thread's own mbarrier waits stall
+//               behind the MMA operand reads it has queued, so one issuer for both
+//               heads left the tensor core idle at every wait.
+//   warps 2..9  softmax of head A, warps 10..17 softmax of head B: thread = one
+//               TMEM lane = one query row, two warps per row quarter, each with 32
+//               of the tile's 64 columns (partial row maxima exchanged through
+//               shared memory at a named barrier per pair); masked online softmax
+//               in fp32 with a lazily updated reference maximum, P (bf16 pairs)
+//               stored into the upper half of its S buffer with tcgen05.st -- P is
+//               double-buffered with S, so a head's softmax of tile j+1 waits for
+//               its P.V of tile j only to rescale O; each warp keeps the row sum of
+//               its columns and rescales and writes its half of O.  The S MMA of
+//               tile j+2 overwrites P(j) after P.V(j) read it: tcgen05.mma
+//               operations of one thread run in issue order.
 // Every mbarrier wait is bounded and records ABKV_DEVERR_TIMEOUT on expiry.
 #include <cstring>
 
@@ -52,17 +53,24 @@
 namespace abkv {
 namespace {
 using namespace tc;
-using mask::tile_class;
-using mask::tile_limit_fast;
+using mask::tile_class_t;
+using mask::tile_limit_t;
 
-constexpr int kBM = 128, kBN = 128;  // head_dim D is 64 or 128 (template parameter)
-constexpr int kThreads = 320;
+constexpr int kBM = 128, kBN = 64;  // head_dim D is 64 or 128 (template parameter)
+// warp 0 producer, warp 1 head A's MMA issuer (and TMEM owner), warps 2..17 softmax, warp 18 head B's
+// MMA issuer
+constexpr int kThreads = 608;
+constexpr int kWarpIssuerB = 18;
 constexpr int kMaxHeads = 128;
-constexpr int kStages = 2;
-constexpr uint32_t kTmemCols = 512;  // per head (A at 0, B at 256): S/P [0,128), O [128,128+D)
-constexpr uint32_t kPCol = 64;       // P (128 bf16 = 64 columns) lives in columns [64, 128) of the S buffer
+constexpr int kStages = 4;
+constexpr uint32_t kTmemCols = 512;  // per head (A at 0, B at 256): S/P buffers [0,64) [64,128), O [128,128+D)
+constexpr uint32_t kPCol = 32;       // P (64 bf16 = 32 columns) lives in columns [32, 64) of its S buffer
 constexpr uint32_t kIdescQK = idesc_bf16_m128(kBN, false);  // S = Q K^T: N = keys, A and B K-major
 constexpr int kOffQ = 0;                        // Q_A, Q_B
+constexpr int kMaxKeyTiles = 2048;              // keys up to 2048 x 64 = 128K rows
+// exchange between the two warps of a row quarter: partial row maxima [2 parity][2 heads][2 halves][128],
+// then partial row sums [2 heads][2 halves][128]
+constexpr int kXchgMax = 2 * 2 * 2 * 128 * 4, kXchgSum = 2 * 2 * 128 * 4;
 
 // Dynamic shared memory layout for head_dim D (1024-byte aligned pieces for
 // 128B swizzle): a [rows][D] bf16 tile is D / 64 atom columns of [rows][128 B].
@@ -75,18 +83,19 @@ struct Layout {
   static constexpr int kOffKV = 2 * kQBytes;
   static constexpr int kOffBar = kOffKV + kStages * kStageBytes;
   static constexpr int kOffList = kOffBar + 256;     // visited key tiles: (kb << 16) | kw0, per key tile
+  static constexpr int kOffXchg = kOffList + 4 * kMaxKeyTiles + 16;
+  static constexpr int kSmem = kOffXchg + kXchgMax + kXchgSum + 1024;  // + alignment slack
   static constexpr uint32_t kIdescPV = idesc_bf16_m128(D, true);  // O += P V: N = D, B (V) MN-major
 };
-// mbarriers (u64 slots from kOffBar): q_full, kv_full[kStages], kv_empty[kStages],
-// s_full[head], p_full[head], o_full, then the TMEM address.  A head's softmax of
-// tile j+1 needs S(j+1), which is issued only after the MMA thread took P(j), so
-// no barrier can run two phases ahead of its waiter.
+static_assert(Layout<128>::kSmem <= 227 * 1024, "shared memory");
+// mbarriers (u64 slots from kOffBar): q_full, kv_full[kStages], kv_empty[kStages] (one arrival per
+// head's P.V), s_full[head][S buffer], p_full[head][S buffer], o_done[head], o_full[head], then the TMEM
+// address.  p_full is double-buffered like S: a head's softmax may finish tile j+1 before its issuer
+// has taken tile j's P, and one barrier per buffer keeps the two arrivals apart.
 constexpr int kBarKvFull = 1, kBarKvEmpty = kBarKvFull + kStages, kBarSFull = kBarKvEmpty + kStages,
-              kBarPFull = kBarSFull + 2, kBarOFull = kBarPFull + 2, kBarTmem = kBarOFull + 1;
+              kBarPFull = kBarSFull + 4, kBarODone = kBarPFull + 4, kBarOFull = kBarODone + 2,
+              kBarTmem = kBarOFull + 2;
 static_assert((kBarTmem + 1) * 8 <= 256, "barrier area");
-constexpr int kMaxKeyTiles = 1024;              // keys up to 1024 x 128 = 128K rows
-template <int D>
-constexpr int smem_bytes() { return Layout<D>::kOffList + 4 * kMaxKeyTiles + 16 + 1024; }  // + alignment slack
 // Lazy rescaling: a row keeps its reference maximum until a tile's maximum
 // exceeds it by more than this (log2 units), so P <= 2^8 and O is rescaled
 // only on large jumps (O and the row sum always share the reference).
@@ -104,92 +113,93 @@ struct alignas(64) PrefillParams {
   float scale_log2;
 };
 
-// Softmax of one (head, 128-key tile) for query row `row` (= TMEM lane).
-// tmem_s / tmem_o already carry this warp's lane base.  Pass 1 reads the row of
-// S in two 64-column halves for the maximum (the upper half stays in registers);
-// pass 2 exponentiates the upper half, stores its P into S columns [96, 128),
-// re-reads the lower half and stores its P into [64, 96) -- every S column is in
-// registers before a P store can overwrite it.  P = 2^(s * scale * log2(e) - m)
-// against a lazily updated reference maximum m; O and the row sum are rescaled
-// when m moves (rescale_ok: O holds earlier tiles, none of them in flight).
+// Softmax of one (head, 64-key tile) for query row `row` (= TMEM lane), columns
+// [32 half, 32 half + 32) of the tile; the partner warp (same rows, other half)
+// does the rest.  The two exchange their partial row maxima through shared
+// memory (xm_mine / xm_other, one float per row) at the pair's named barrier,
+// so both take the same lazy-rescale decision and reference maximum; each keeps
+// the row sum of its own columns and rescales its own half of O (D / 2 columns).
+// P (bf16, 16 words) goes into this half's columns of the upper half of the S buffer.
 template <int D>
-__device__ __forceinline__ void softmax_tile(const PrefillParams& p, int lim, uint32_t tmem_s, uint32_t tmem_o,
-                                             bool rescale_ok, SoftmaxState& st) {
+__device__ __forceinline__ void softmax_half(const PrefillParams& p, int lim, int half, int row, uint32_t tmem_s,
+                                             uint32_t tmem_o, uint32_t lane_base, int j, uint64_t* o_done,
+                                             bool& dead, SoftmaxState& st, float* xm_mine, const float* xm_other,
+                                             int pair_bar) {
   const float sl2 = p.scale_log2;  // lim: visible columns of this row are c < lim
+  const int c0 = 32 * half;
+  float t[32];
+  tmem_ld32(tmem_s + lane_base + c0, t);
+  tmem_wait_ld();
   auto vis = [&](int c) { return c < lim; };
   const bool full = lim == kBN;
-  float t0[32], t1[32];
   float mxa[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // independent chains
+  if (full) {
 #pragma unroll
-  for (int h2 = 0; h2 < 2; ++h2) {
-    tmem_ld32(tmem_s + 64 * h2, t0);
-    tmem_ld32(tmem_s + 64 * h2 + 32, t1);
-    tmem_wait_ld();
-    if (full) {
+    for (int i = 0; i < 16; ++i) mxa[i & 3] = fmax3(mxa[i & 3], t[2 * i], t[2 * i + 1]);
+  } else {
 #pragma unroll
-      for (int i = 0; i < 32; ++i) mxa[i & 3] = fmax3(mxa[i & 3], t0[i], t1[i]);
-    } else {
-#pragma unroll
-      for (int i = 0; i < 32; ++i)
-        mxa[i & 3] = fmax3(mxa[i & 3], vis(64 * h2 + i) ? t0[i] : -INFINITY,
-                           vis(64 * h2 + 32 + i) ? t1[i] : -INFINITY);
-    }
+    for (int i = 0; i < 16; ++i)
+      mxa[i & 3] = fmax3(mxa[i & 3], vis(c0 + 2 * i) ? t[2 * i] : -INFINITY,
+                         vis(c0 + 2 * i + 1) ? t[2 * i + 1] : -INFINITY);
   }
-  const float mx = fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3])) * sl2;
+  const float mpart = fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3]));
+  xm_mine[row] = mpart;
+  // both warps' S loads are complete (wait::ld) before either stores P over columns [32, 64)
+  tc_fence_before();
+  named_bar_sync(pair_bar, 64);
+  tc_fence_after();
+  const float mx = fmaxf(mpart, xm_other[row]) * sl2;  // the row's maximum over both halves
   const bool need = mx > st.m_run + kRescaleThreshold || (st.m_run == -INFINITY && mx > -INFINITY);
   const float m_new = need ? mx : st.m_run;
   const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
   const float alpha = need ? fast_exp2(st.m_run - m_use) : 1.f;
-  if (rescale_ok && __any_sync(0xffffffffu, need)) {
-#pragma unroll 1
-    for (int c4 = 0; c4 < D / 32; ++c4) {
-      float t[32];
-      tmem_ld32(tmem_o + c4 * 32, t);
-      tmem_wait_ld();
-#pragma unroll
-      for (int i = 0; i < 32; ++i) t[i] *= alpha;
-      tmem_st32(tmem_o + c4 * 32, t);
-    }
-  }
   float rsa[4][2] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};  // packed pair accumulators
-  // columns [c0, c0 + 64) held in t0 (first 32) and t1 (next 32) -> P pairs in w
-  auto exp_half = [&](int c0, uint32_t (&w)[32]) {
+  uint32_t w[16];
 #pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      const float* t = half ? t1 : t0;
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const int c = c0 + half * 32 + 2 * i;
-        float x0, x1;
-        ffma2(x0, x1, t[2 * i], t[2 * i + 1], sl2, -m_use);
-        float p0 = fast_exp2(x0);
-        float p1 = fast_exp2(x1);
-        if (!full) {
-          p0 = vis(c) ? p0 : 0.f;
-          p1 = vis(c + 1) ? p1 : 0.f;
-        }
-        fadd2(rsa[i & 3][0], rsa[i & 3][1], p0, p1);
-        w[half * 16 + i] = pack_bf16x2(p0, p1);
-      }
+  for (int i = 0; i < 16; ++i) {
+    const int c = c0 + 2 * i;
+    float x0, x1;
+    ffma2(x0, x1, t[2 * i], t[2 * i + 1], sl2, -m_use);
+    float p0 = fast_exp2(x0);
+    float p1 = fast_exp2(x1);
+    if (!full) {
+      p0 = vis(c) ? p0 : 0.f;
+      p1 = vis(c + 1) ? p1 : 0.f;
     }
-  };
-  uint32_t w[32];
-  exp_half(64, w);  // t0/t1 still hold columns [64, 128)
-  tmem_st32(tmem_s + kPCol + 32, reinterpret_cast<const float(&)[32]>(w));
-  tmem_ld32(tmem_s, t0);
-  tmem_ld32(tmem_s + 32, t1);
-  tmem_wait_ld();
-  exp_half(0, w);
-  tmem_st32(tmem_s + kPCol, reinterpret_cast<const float(&)[32]>(w));
+    fadd2(rsa[i & 3][0], rsa[i & 3][1], p0, p1);
+    w[i] = pack_bf16x2(p0, p1);
+  }
   fadd2(rsa[0][0], rsa[0][1], rsa[1][0], rsa[1][1]);
   fadd2(rsa[2][0], rsa[2][1], rsa[3][0], rsa[3][1]);
   st.l_run = st.l_run * alpha + ((rsa[0][0] + rsa[0][1]) + (rsa[2][0] + rsa[2][1]));
   st.m_run = m_new;
+  // P(j) into this half's columns of the upper half of the tile's S buffer (already read into
+  // registers); the buffer's previous P was consumed by P.V(j-2), which completed before S(j)
+  // was signalled
+  tmem_st16(tmem_s + lane_base + kPCol + 16 * half, w);
+  if (j > 0 && __any_sync(0xffffffffu, need)) {
+    // O is touched only after the previous P.V of this head completed; the partner warp takes
+    // the same branch (same rows, same maxima) and rescales the other half of O's columns
+    const bool ok = __all_sync(0xffffffffu, wait_or_abort(o_done, (uint32_t)((j - 1) & 1), dead, p.err));
+    tc_fence_after();
+    if (ok) {
+#pragma unroll 1
+      for (int c4 = 0; c4 < D / 64; ++c4) {
+        float o[32];
+        const uint32_t col = tmem_o + lane_base + (D / 2) * half + 32 * c4;
+        tmem_ld32(col, o);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[i] *= alpha;
+        tmem_st32(col, o);
+      }
+    }
+  }
   tmem_wait_st();
 }
 
 __device__ __forceinline__ bool visit_tile(const PrefillParams& p, int hA, int hB, int qt, int kt, int pl) {
-  return tile_class(p, hA, qt, kt, pl) != 0 || (hB >= 0 && tile_class(p, hB, qt, kt, pl) != 0);
+  return tile_class_t<kBM, kBN>(p, hA, qt, kt, pl) != 0 || (hB >= 0 && tile_class_t<kBM, kBN>(p, hB, qt, kt, pl) != 0);
 }
 
 template <int D>
@@ -204,9 +214,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
   uint64_t* q_full = bar + 0;
   uint64_t* kv_full = bar + kBarKvFull;    // [kStages]
   uint64_t* kv_empty = bar + kBarKvEmpty;  // [kStages]
-  uint64_t* s_full = bar + kBarSFull;      // [head]
-  uint64_t* p_full = bar + kBarPFull;      // [head]
-  uint64_t* o_full = bar + kBarOFull;
+  uint64_t* s_full = bar + kBarSFull;      // [head][S buffer]
+  uint64_t* p_full = bar + kBarPFull;      // [head][S buffer]
+  uint64_t* o_done = bar + kBarODone;      // [head]: one phase per P.V
+  uint64_t* o_full = bar + kBarOFull;      // [head]
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bar + kBarTmem);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -223,13 +234,16 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
     mbar_init(q_full, 1);
     for (int i = 0; i < kStages; ++i) {
       mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
+      mbar_init(&kv_empty[i], hB >= 0 ? 2 : 1);
+    }
+    for (int i = 0; i < 4; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 256);  // the 8 softmax warps of a head
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 128);
+      mbar_init(&o_done[i], 1);
+      mbar_init(&o_full[i], 1);
     }
-    mbar_init(o_full, 1);
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(s_tmem)),
@@ -282,14 +296,14 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         }
       }
     }
-  } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
-    if (lane == 0) {
-      const bool two = hB >= 0;
+  } else if (warp == 1 || warp == kWarpIssuerB) {
+    // ---------------- MMA issuers: warp 1 head A, warp 18 head B ----------------
+    const int hs = warp == 1 ? 0 : 1;
+    if (lane == 0 && (hs == 0 || hB >= 0)) {
       wait_or_abort(q_full, 0, dead, p.err);
-      const uint32_t qa = smem_u32(smem + kOffQ), qbv = qa + kQBytes;
-      const uint32_t sA = tmem, oA = tmem + 128, sB = tmem + 256, oB = tmem + 384;
-      auto issue_s = [&](uint32_t qaddr, uint32_t sd, int st) {
+      const uint32_t qaddr = smem_u32(smem + kOffQ) + hs * kQBytes;
+      const uint32_t sbase = tmem + 256 * hs, obase = sbase + 128;
+      auto issue_s = [&](uint32_t sd, int st) {
         const uint64_t dq = desc_kmajor_sw128(qaddr);
         const uint64_t dk = desc_kmajor_sw128(smem_u32(smem + kOffKV + st * kStageBytes));
 #pragma unroll
@@ -298,91 +312,95 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                desc_advance(dk, (kk >> 2) * (kKVHalf / kAtoms) + (kk & 3) * 32), kIdescQK, kk > 0 ? 1u : 0u);
         }
       };
-      auto issue_pv = [&](uint32_t ptmem, uint32_t od, int st, bool first) {
-        const uint64_t dv = desc_mnmajor_sw128(smem_u32(smem + kOffKV + st * kStageBytes + kKVHalf), kKVHalf / kAtoms);
+      auto issue_pv = [&](uint32_t ptmem, int st, bool first) {
+        const uint64_t dv =
+            desc_mnmajor_sw128(smem_u32(smem + kOffKV + st * kStageBytes + kKVHalf), kKVHalf / kAtoms);
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk) {  // over the tile's keys in steps of 16 (8 TMEM columns)
-          umma_tmem_a(od, ptmem + kk * 8, desc_advance(dv, kk * 2048), kIdescPV, (!first || kk > 0) ? 1u : 0u);
+          umma_tmem_a(obase, ptmem + kk * 8, desc_advance(dv, kk * 2048), kIdescPV, (!first || kk > 0) ? 1u : 0u);
         }
       };
-      // tile sequence: S_A(0) S_B(0) | PV_A(j) S_A(j+1) PV_B(j) S_B(j+1) | ...
+      // tile sequence; S of tile j goes to S buffer j % 2
       const int n = n_tiles;
-      if (n > 0 && wait_or_abort(&kv_full[0], 0, dead, p.err)) {
+      for (int t = 0; t < 2 && t < n && !dead; ++t) {
+        if (!wait_or_abort(&kv_full[t], 0, dead, p.err)) break;
         tc_fence_after();
-        issue_s(qa, sA, 0);
-        umma_commit(&s_full[0]);
-        if (two) {
-          issue_s(qbv, sB, 0);
-          umma_commit(&s_full[1]);
-        }
+        issue_s(sbase + 64 * t, t);
+        umma_commit(&s_full[2 * hs + t]);
       }
       for (int j = 0; j < n && !dead; ++j) {
-        const int st = j % kStages, st1 = (j + 1) % kStages;
-        const bool more = j + 1 < n;
-        // head A: P_A(j) V_j, then S_A(j+1) into the same TMEM buffer (runs after
-        // P.V(j) has read P(j): one issuing thread, in-order execution)
-        if (!wait_or_abort(&p_full[0], (uint32_t)(j & 1), dead, p.err)) break;
+        const int st = j % kStages, st2 = (j + 2) % kStages;
+        const bool more = j + 2 < n;
+        // the step's waits first (after the first the queue has drained, so the next cost no
+        // further stall), then P(j) V_j and S(j+2) into the S buffer softmax(j) has released
+        if (more && !wait_or_abort(&kv_full[st2], (uint32_t)(((j + 2) / kStages) & 1), dead, p.err)) break;
+        if (!wait_or_abort(&p_full[2 * hs + (j & 1)], (uint32_t)((j >> 1) & 1), dead, p.err)) break;
         tc_fence_after();
-        issue_pv(sA + kPCol, oA, st, j == 0);
-        if (!two) umma_commit(&kv_empty[st]);
+        issue_pv(sbase + 64 * (j & 1) + kPCol, st, j == 0);
+        umma_commit(&o_done[hs]);
+        umma_commit(&kv_empty[st]);  // this head's last use of the K/V stage
         if (more) {
-          if (!wait_or_abort(&kv_full[st1], (uint32_t)(((j + 1) / kStages) & 1), dead, p.err)) break;
-          tc_fence_after();
-          issue_s(qa, sA, st1);
-          umma_commit(&s_full[0]);
-        }
-        if (two) {
-          // head B: P_B(j) V_j (last use of this K/V stage), then S_B(j+1)
-          if (!wait_or_abort(&p_full[1], (uint32_t)(j & 1), dead, p.err)) break;
-          tc_fence_after();
-          issue_pv(sB + kPCol, oB, st, j == 0);
-          umma_commit(&kv_empty[st]);
-          if (more) {
-            issue_s(qbv, sB, st1);
-            umma_commit(&s_full[1]);
-          }
+          issue_s(sbase + 64 * (j & 1), st2);
+          umma_commit(&s_full[2 * hs + (j & 1)]);
         }
       }
-      umma_commit(o_full);
+      umma_commit(&o_full[hs]);
     }
   } else {
-    // ---------------- softmax / epilogue ----------------
-    const int head_slot = (warp - 2) >> 2;          // 0: head A (warps 2..5), 1: head B (warps 6..9)
+    // ---------------- softmax / correction / epilogue ----------------
+    const int sw = warp - 2;                         // 0..15
+    const int head_slot = sw >> 3;                   // 0: head A (warps 2..9), 1: head B (warps 10..17)
+    const int half = (sw >> 2) & 1;                  // columns [32 half, 32 half + 32) of every tile
     const int h = head_slot ? hB : hA;
     const int quarter = warp & 3;                    // TMEM lane quarter this warp may access
     const int row = quarter * 32 + lane;             // query row within the tile
     const int q = qt * kBM + row;
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
     const uint32_t tmem_h = tmem + (head_slot ? 256 : 0), tmem_o = tmem_h + 128;
+    // the two warps of these rows meet at named barrier 1 + head x 4 + quarter; every exit from
+    // the tile loop is decided jointly (named_bar_and), so both execute the same barriers
+    const int pair_bar = 1 + head_slot * 4 + quarter;
+    float* xmax = reinterpret_cast<float*>(smem + LY::kOffXchg);                          // [parity][head][half][128]
+    float* xsum = reinterpret_cast<float*>(smem + LY::kOffXchg + kXchgMax) + head_slot * 256;  // [half][128]
     if (h >= 0) {
-      SoftmaxState st{-INFINITY, 0.f};
+      SoftmaxState st{-INFINITY, 0.f};  // l_run: the row sum of this warp's columns
       const int qbr = q / p.per, qwr = q - qbr * p.per, quota = p.quota[h];
       for (int j = 0; j < n_tiles; ++j) {
         const int e = s_list[j];
         const int kb = e >> 16, kw0 = e & 0xFFFF;
-        const int lim = tile_limit_fast(p, quota, q, qbr, qwr, kb, kw0, kb * p.per + kw0, pl);
-        // warp-uniform decision: tcgen05.ld is a warp-collective
-        const bool ok = __all_sync(0xffffffffu, wait_or_abort(&s_full[head_slot], (uint32_t)(j & 1), dead, p.err));
+        const int lim = tile_limit_t<kBN>(p, quota, q, qbr, qwr, kb, kw0, kb * p.per + kw0, pl);
+        // warp-uniform (tcgen05.ld is a warp-collective) and pair-uniform decision
+        const bool ok = named_bar_and(
+            pair_bar, 64,
+            __all_sync(0xffffffffu,
+                       wait_or_abort(&s_full[2 * head_slot + (j & 1)], (uint32_t)((j >> 1) & 1), dead, p.err)));
         if (!ok) {
           dead = true;
           break;
         }
         tc_fence_after();
-        softmax_tile<D>(p, lim, tmem_h + lane_base, tmem_o + lane_base, j > 0, st);
+        float* xm = xmax + ((j & 1) * 2 + head_slot) * 256;  // parity j: tile j + 2 reuses it after both
+        softmax_half<D>(p, lim, half, row, tmem_h + 64 * (j & 1), tmem_o, lane_base, j, &o_done[head_slot], dead,
+                        st, xm + half * 128, xm + (1 - half) * 128, pair_bar);
         tc_fence_before();  // P's tcgen05.st completed (wait::st) before the arrival
-        mbar_arrive_one(&p_full[head_slot]);
+        mbar_arrive_one(&p_full[2 * head_slot + (j & 1)]);
       }
-      // epilogue
-      const bool o_ok = __all_sync(0xffffffffu, wait_or_abort(o_full, 0, dead, p.err));
+      // epilogue: this warp writes dims [D/2 half, D/2 half + D/2) of its row
+      const bool o_ok =
+          named_bar_and(pair_bar, 64, __all_sync(0xffffffffu, wait_or_abort(&o_full[head_slot], 0, dead, p.err)));
       tc_fence_after();
+      xsum[half * 128 + row] = st.l_run;
+      named_bar_sync(pair_bar, 64);
+      const float l = st.l_run + xsum[(1 - half) * 128 + row];  // the row sum over both halves
       if (o_ok) {
-        const bool none = !(st.l_run > 0.f);  // no visible key: zeros
-        const float inv = none ? 0.f : 1.f / st.l_run;
-        __nv_bfloat16* orow = p.out + (int64_t)b * p.o_sb + (int64_t)h * p.o_sh + (int64_t)q * p.o_ss;
+        const bool none = !(l > 0.f);  // no visible key: zeros
+        const float inv = none ? 0.f : 1.f / l;
+        __nv_bfloat16* orow =
+            p.out + (int64_t)b * p.o_sb + (int64_t)h * p.o_sh + (int64_t)q * p.o_ss + (D / 2) * half;
 #pragma unroll 1
-        for (int c4 = 0; c4 < D / 32; ++c4) {
+        for (int c4 = 0; c4 < D / 64; ++c4) {
           float t[32];
-          tmem_ld32(tmem_o + lane_base + c4 * 32, t);
+          tmem_ld32(tmem_o + lane_base + (D / 2) * half + c4 * 32, t);
           tmem_wait_ld();
           if (none) {
 #pragma unroll
@@ -398,8 +416,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
             *reinterpret_cast<uint4*>(orow + c4 * 32 + v8 * 8) = pk;
           }
         }
-        if (p.lse) {
-          const float lse2 = st.l_run > 0.f ? st.m_run + log2f(st.l_run) : -INFINITY;
+        if (p.lse && half == 0) {
+          const float lse2 = l > 0.f ? st.m_run + log2f(l) : -INFINITY;
           p.lse[((int64_t)b * p.H + h) * p.S + q] = lse2 * 0.6931471805599453f;  // natural log
         }
       }
@@ -476,7 +494,7 @@ extern "C" int abkv_prefill_masked(const void* q, const int64_t* q_strides, cons
   prm.n_qtiles = S / kBM;
   prm.scale_log2 = scale * 1.4426950408889634f;
   auto kernel = head_dim == 64 ? prefill_kernel<64> : prefill_kernel<128>;
-  const int smem = head_dim == 64 ? smem_bytes<64>() : smem_bytes<128>();
+  const int smem = head_dim == 64 ? Layout<64>::kSmem : Layout<128>::kSmem;
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
       cudaSuccess)
     return ABKV_ERR_CUDA;

@@ -1,5 +1,5 @@
 // The pause-token mask of CompressLM._arith_mask_mod
-// (abridgekv/compress_forward.py:695-727) at 128 x 128 tile granularity, shared
+// (abridgekv/compress_forward.py:695-727) at tile granularity (128 x 128 by default), shared
 // by the forward (prefill.cu) and backward (prefill_bwd.cu) kernels.  With
 // per = C + K, qb = q / per, kb = kv / per, qw = q % per, kw = kv % per:
 //   vis = (kw < C & kb == qb) | (kw >= C & kb < qb)
@@ -14,11 +14,12 @@ namespace mask {
 
 constexpr int kTile = 128;
 
-// 0 = empty, 1 = full, 2 = partial, for query tile qt / key tile kt of head h.
-template <class P>
-__device__ __forceinline__ int tile_class(const P& p, int h, int qt, int kt, int pl) {
-  const int q0 = qt * kTile, q1 = q0 + kTile - 1;
-  const int k0 = kt * kTile, k1 = k0 + kTile - 1;
+// 0 = empty, 1 = full, 2 = partial, for query tile qt (kQT rows) / key tile kt
+// (kKT keys) of head h; kQT and kKT divide 128.
+template <int kQT, int kKT, class P>
+__device__ __forceinline__ int tile_class_t(const P& p, int h, int qt, int kt, int pl) {
+  const int q0 = qt * kQT, q1 = q0 + kQT - 1;
+  const int k0 = kt * kKT, k1 = k0 + kKT - 1;
   const int qb = q0 / p.per, kb = k0 / p.per;
   if (kb > qb) return 0;
   const int qw0 = q0 - qb * p.per;
@@ -43,25 +44,34 @@ __device__ __forceinline__ int tile_class(const P& p, int h, int qt, int kt, int
   if (kb < qb) return qc;
   return q_code ? qc : 0;
 }
+template <class P>
+__device__ __forceinline__ int tile_class(const P& p, int h, int qt, int kt, int pl) {
+  return tile_class_t<kTile, kTile>(p, h, qt, kt, pl);
+}
 
 // Inside any tile the visible keys of one query row are a PREFIX of the tile's
 // columns: the causal diagonal of the own block (kv <= q), the raw-prompt
 // boundary of an earlier block (kb*C + kw < prompt_len) or the quota boundary
-// of a code tile (kw - C < quota).  tile_limit_fast returns that prefix length
-// in [0, kTile] from precomputed coordinates: the row's block qb and in-block
-// offset qw, the tile's block kb and in-block offset kw0 (k0 = key tile start).
-template <class P>
-__device__ __forceinline__ int tile_limit_fast(const P& p, int quota, int q, int qb, int qw, int kb,
-                                               int kw0, int k0, int pl) {
+// of a code tile (kw - C < quota).  tile_limit_t returns that prefix length in
+// [0, kKT] from precomputed coordinates: the row's block qb and in-block offset
+// qw, the tile's block kb and in-block offset kw0 (k0 = key tile start).
+template <int kKT, class P>
+__device__ __forceinline__ int tile_limit_t(const P& p, int quota, int q, int qb, int qw, int kb, int kw0, int k0,
+                                            int pl) {
   int lim;
   if (kw0 < p.C) {
-    if (kb == qb) lim = (qw >= p.C) ? kTile : q - k0 + 1;
+    if (kb == qb) lim = (qw >= p.C) ? kKT : q - k0 + 1;
     else lim = pl - (kb * p.C + kw0);
   } else {
     if (kb == qb && qw < p.C) return 0;
     lim = quota - (kw0 - p.C);
   }
-  return lim < 0 ? 0 : (lim > kTile ? kTile : lim);
+  return lim < 0 ? 0 : (lim > kKT ? kKT : lim);
+}
+template <class P>
+__device__ __forceinline__ int tile_limit_fast(const P& p, int quota, int q, int qb, int qw, int kb, int kw0,
+                                               int k0, int pl) {
+  return tile_limit_t<kTile>(p, quota, q, qb, qw, kb, kw0, k0, pl);
 }
 
 }  // namespace mask
