@@ -178,7 +178,11 @@ template <bool kHole>
 __device__ __forceinline__ void softmax_half(const CodeStepParams& p, int lim, int hs, int he, int half, int row,
                                              uint32_t tmem_s, uint32_t tmem_o, uint32_t lane_base, int j,
                                              uint64_t* o_done, bool& dead, SoftmaxState& st, float* xm_mine,
-                                             const float* xm_other, int pair_bar) {
+                                             const float* xm_other, int pair_bar, bool live) {
+  if (!live) {  // this warp gave up waiting for S: it only meets its partner at the pair's barrier
+    named_bar_sync(pair_bar, 64);
+    return;
+  }
   const float sl2 = p.scale_log2;  // lim: visible columns of this row are c < lim
   const int c0 = 32 * half;
   float t[32];
@@ -547,9 +551,9 @@ __global__ void __launch_bounds__(kThreads, 1) codestep_kernel(const __grid_cons
     const int q = qt * kBM + row;
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
     const uint32_t tmem_h = tmem + (head_slot ? 256 : 0), tmem_o = tmem_h + 128;
-    // the two warps of these rows (warps w and w + 4) meet at named barrier 1 + head x 4 + quarter;
-    // every exit from the tile loop is decided jointly (named_bar_and), so both always execute
-    // the same barriers
+    // the two warps of these rows (warps w and w + 4) meet at named barrier 1 + head x 4 + quarter,
+    // once per tile and twice at the end: neither leaves the tile loop early (a warp that gave up
+    // waiting skips the work but not the barriers), so both always execute the same barriers
     const int pair_bar = 1 + head_slot * 4 + quarter;
     float* xmax = reinterpret_cast<float*>(smem + kOffXchg);            // [parity][head][half][128]
     float* xsum = reinterpret_cast<float*>(smem + kOffXchg + kXchgMax) + head_slot * 256;  // [half][128]
@@ -564,17 +568,14 @@ __global__ void __launch_bounds__(kThreads, 1) codestep_kernel(const __grid_cons
         const int lim = side ? min(max(n_side - (-e - 1) * kBN, 0), kBN) : min(max(leff - e * kBN, 0), kBN);
         // valid rows of the tile: the rest was not loaded (V zeroed below)
         const int valid = side ? n_side - (-e - 1) * kBN : seq_len - e * kBN;
-        // warp-uniform (tcgen05.ld is a warp-collective) and pair-uniform decision
-        const bool ok = named_bar_and(
-            pair_bar, 64,
-            __all_sync(0xffffffffu,
-                       wait_or_abort(&s_full[2 * head_slot + (j & 1)], (uint32_t)((j >> 1) & 1), dead, p.err)));
-        if (!ok) {
-          dead = true;
-          break;
-        }
+        // warp-uniform (tcgen05.ld is a warp-collective); a warp that gave up waiting keeps
+        // going through the tiles without their work, so both warps of the pair meet at the
+        // same named barriers
+        const bool ok = __all_sync(0xffffffffu,
+                                   wait_or_abort(&s_full[2 * head_slot + (j & 1)], (uint32_t)((j >> 1) & 1), dead, p.err));
+        if (!ok) dead = true;
         tc_fence_after();
-        if (head_slot == 0 && valid < kBN) {
+        if (ok && head_slot == 0 && valid < kBN) {
           // V rows at or past seq_len (or the sidecar segment's end): stale page
           // slots or unloaded slices become zeros before either head's P.V reads
           // them (P is 0 there, but 0 * NaN would not be)
@@ -594,7 +595,7 @@ __global__ void __launch_bounds__(kThreads, 1) codestep_kernel(const __grid_cons
         float* xm = xmax + ((j & 1) * 2 + head_slot) * 256;  // parity j: tile j + 2 reuses it after both
         softmax_half<true>(p, lim, side ? 0 : hole_s - e * kBN, side ? 0 : hole_e - e * kBN, half, row,
                            tmem_h + 64 * (j & 1), tmem_o, lane_base, j, &o_done[head_slot], dead, st,
-                           xm + half * 128, xm + (1 - half) * 128, pair_bar);
+                           xm + half * 128, xm + (1 - half) * 128, pair_bar, ok);
         tc_fence_before();  // P's tcgen05.st completed (wait::st) before the arrival
         mbar_arrive_one(&p_full[2 * head_slot + (j & 1)]);
       }

@@ -124,7 +124,11 @@ template <int D>
 __device__ __forceinline__ void softmax_half(const PrefillParams& p, int lim, int half, int row, uint32_t tmem_s,
                                              uint32_t tmem_o, uint32_t lane_base, int j, uint64_t* o_done,
                                              bool& dead, SoftmaxState& st, float* xm_mine, const float* xm_other,
-                                             int pair_bar) {
+                                             int pair_bar, bool live) {
+  if (!live) {  // this warp gave up waiting for S: it only meets its partner at the pair's barrier
+    named_bar_sync(pair_bar, 64);
+    return;
+  }
   const float sl2 = p.scale_log2;  // lim: visible columns of this row are c < lim
   const int c0 = 32 * half;
   float t[32];
@@ -357,8 +361,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
     const int q = qt * kBM + row;
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
     const uint32_t tmem_h = tmem + (head_slot ? 256 : 0), tmem_o = tmem_h + 128;
-    // the two warps of these rows meet at named barrier 1 + head x 4 + quarter; every exit from
-    // the tile loop is decided jointly (named_bar_and), so both execute the same barriers
+    // the two warps of these rows meet at named barrier 1 + head x 4 + quarter, once per tile and
+    // twice at the end: neither leaves the tile loop early (a warp that gave up waiting skips the
+    // work but not the barriers), so both execute the same barriers
     const int pair_bar = 1 + head_slot * 4 + quarter;
     float* xmax = reinterpret_cast<float*>(smem + LY::kOffXchg);                          // [parity][head][half][128]
     float* xsum = reinterpret_cast<float*>(smem + LY::kOffXchg + kXchgMax) + head_slot * 256;  // [half][128]
@@ -369,19 +374,16 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         const int e = s_list[j];
         const int kb = e >> 16, kw0 = e & 0xFFFF;
         const int lim = tile_limit_t<kBN>(p, quota, q, qbr, qwr, kb, kw0, kb * p.per + kw0, pl);
-        // warp-uniform (tcgen05.ld is a warp-collective) and pair-uniform decision
-        const bool ok = named_bar_and(
-            pair_bar, 64,
-            __all_sync(0xffffffffu,
-                       wait_or_abort(&s_full[2 * head_slot + (j & 1)], (uint32_t)((j >> 1) & 1), dead, p.err)));
-        if (!ok) {
-          dead = true;
-          break;
-        }
+        // warp-uniform (tcgen05.ld is a warp-collective); a warp that gave up waiting keeps
+        // going through the tiles without their work, so both warps of the pair meet at the
+        // same named barriers
+        const bool ok = __all_sync(0xffffffffu,
+                                   wait_or_abort(&s_full[2 * head_slot + (j & 1)], (uint32_t)((j >> 1) & 1), dead, p.err));
+        if (!ok) dead = true;
         tc_fence_after();
         float* xm = xmax + ((j & 1) * 2 + head_slot) * 256;  // parity j: tile j + 2 reuses it after both
         softmax_half<D>(p, lim, half, row, tmem_h + 64 * (j & 1), tmem_o, lane_base, j, &o_done[head_slot], dead,
-                        st, xm + half * 128, xm + (1 - half) * 128, pair_bar);
+                        st, xm + half * 128, xm + (1 - half) * 128, pair_bar, ok);
         tc_fence_before();  // P's tcgen05.st completed (wait::st) before the arrival
         mbar_arrive_one(&p_full[2 * head_slot + (j & 1)]);
       }
