@@ -129,15 +129,6 @@ static __device__ __forceinline__ bool named_bar_and(int id, int count, bool v) 
       : "memory");
   return r != 0;
 }
-static __device__ __forceinline__ bool named_bar_or(int id, int count, bool v) {
-  uint32_t r;
-  asm volatile(
-      "{\n .reg .pred q, o;\n setp.ne.u32 q, %1, 0;\n bar.red.or.pred o, %2, %3, q;\n selp.u32 %0, 1, 0, o;\n}\n"
-      : "=r"(r)
-      : "r"((uint32_t)v), "r"(id), "r"(count)
-      : "memory");
-  return r != 0;
-}
 
 static __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
   asm volatile(
