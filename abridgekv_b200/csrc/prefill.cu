@@ -248,6 +248,14 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
       mbar_init(&o_done[i], 1);
       mbar_init(&o_full[i], 1);
     }
+    // Q of both heads right away: its latency overlaps the tile-list build below
+    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+    mbar_expect_tx(q_full, (hB >= 0 ? 2 : 1) * kQBytes);
+    for (int a = 0; a < kAtoms; ++a) {
+      tma_load_4d(smem + kOffQ + a * (kQBytes / kAtoms), &p.tm_q, 64 * a, qt * kBM, hA, b, q_full);
+      if (hB >= 0)
+        tma_load_4d(smem + kOffQ + kQBytes + a * (kQBytes / kAtoms), &p.tm_q, 64 * a, qt * kBM, hB, b, q_full);
+    }
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(s_tmem)),
@@ -281,12 +289,6 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
-      mbar_expect_tx(q_full, (hB >= 0 ? 2 : 1) * kQBytes);
-      for (int a = 0; a < kAtoms; ++a) {
-        tma_load_4d(smem + kOffQ + a * (kQBytes / kAtoms), &p.tm_q, 64 * a, qt * kBM, hA, b, q_full);
-        if (hB >= 0)
-          tma_load_4d(smem + kOffQ + kQBytes + a * (kQBytes / kAtoms), &p.tm_q, 64 * a, qt * kBM, hB, b, q_full);
-      }
       for (int j = 0; j < n_tiles; ++j) {
         const int e = s_list[j];
         const int k0 = (e >> 16) * p.per + (e & 0xFFFF);
