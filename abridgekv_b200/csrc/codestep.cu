@@ -92,6 +92,8 @@ constexpr float kRescaleThreshold = 8.f;
 
 struct alignas(64) CodeStepParams {
   CUtensorMap tm_q, tm_k;  // q [T][H][D]; K/V planes of the paged cache
+  CUtensorMap tm_out;      // out [T][H][D] (used when out_tma: full query tiles are stored by TMA)
+  int out_tma;
   __nv_bfloat16* out;
   int64_t o_sh, o_ss;
   int32_t* err;
@@ -606,6 +608,11 @@ __global__ void __launch_bounds__(kThreads, 1) codestep_kernel(const __grid_cons
       xsum[half * 128 + row] = st.l_run;
       named_bar_sync(pair_bar, 64);
       const float l = st.l_run + xsum[(1 - half) * 128 + row];  // the row sum over both halves
+      // a full query tile goes through the head's half of the Q buffer (no S MMA reads it any more:
+      // o_full followed the head's last MMAs), 128B-swizzled like the output map's boxes, and one
+      // thread stores it; a partial tile (causal mode) is stored row by row
+      const bool tile_store = p.out_tma && qt * kBM + kBM <= qlen;  // CTA-uniform
+      uint8_t* stage = smem + kOffQ + head_slot * kQBytes;
       if (o_ok) {
         // a row that saw no visible key (possible in the code step when the
         // quota and the exclusion hide everything) is written as zeros
@@ -622,9 +629,17 @@ __global__ void __launch_bounds__(kThreads, 1) codestep_kernel(const __grid_cons
 #pragma unroll
             for (int i = 0; i < 32; ++i) t[i] = 0.f;
           }
-          // tcgen05.ld above is warp-collective; only the stores skip rows past
-          // the request's last query row (causal mode)
-          if (q < qlen) {
+          if (tile_store) {
+            uint8_t* atom = stage + half * (kQBytes / 2);
+#pragma unroll
+            for (int v8 = 0; v8 < 4; ++v8)
+              st_swizzled16(atom, row, 4 * c4 + v8, pack_bf16x2(t[v8 * 8 + 0] * inv, t[v8 * 8 + 1] * inv),
+                            pack_bf16x2(t[v8 * 8 + 2] * inv, t[v8 * 8 + 3] * inv),
+                            pack_bf16x2(t[v8 * 8 + 4] * inv, t[v8 * 8 + 5] * inv),
+                            pack_bf16x2(t[v8 * 8 + 6] * inv, t[v8 * 8 + 7] * inv));
+          } else if (q < qlen) {
+            // tcgen05.ld above is warp-collective; only the stores skip rows past
+            // the request's last query row (causal mode)
 #pragma unroll
             for (int v8 = 0; v8 < 4; ++v8) {
               uint4 pk;
@@ -635,6 +650,19 @@ __global__ void __launch_bounds__(kThreads, 1) codestep_kernel(const __grid_cons
               *reinterpret_cast<uint4*>(orow + c4 * 32 + v8 * 8) = pk;
             }
           }
+        }
+      }
+      if (tile_store) {
+        asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // staged rows visible to the TMA
+        named_bar_sync(9 + head_slot, 256);                            // the head's 8 warps have staged
+        if ((sw & 7) == 0 && lane == 0) {
+          if (o_ok) {
+            const int row0 = __ldg(p.q_start + b) + qt * kBM;
+            tma_store_4d(&p.tm_out, stage, 0, h, row0, 0);
+            tma_store_4d(&p.tm_out, stage + kQBytes / 2, 64, h, row0, 0);
+            tma_store_commit();
+          }
+          tma_store_wait_read();  // the shared memory stays valid until the store has read it
         }
       }
     }
@@ -827,6 +855,18 @@ int code_step_launch(const void* q, int64_t q_row_stride, int64_t q_head_stride,
     const cuuint32_t box[4] = {64, 1, (cuuint32_t)kBM, 1};
     const int st = tc::encode_tiled_4d(&prm.tm_q, q, dims, gstr, box);
     if (st != ABKV_OK) return st;
+  }
+  {
+    // the output map (same shape as q's); without one (strides not multiples of 16 bytes) every
+    // tile is stored row by row
+    const cuuint64_t dims[4] = {(cuuint64_t)kD, (cuuint64_t)Hq, (cuuint64_t)T, 1};
+    const cuuint64_t gstr[3] = {(cuuint64_t)out_head_stride * 2, (cuuint64_t)out_row_stride * 2,
+                                (cuuint64_t)out_row_stride * 2 * (cuuint64_t)T};
+    const cuuint32_t box[4] = {64, 1, (cuuint32_t)kBM, 1};
+    prm.out_tma = ((out_head_stride | out_row_stride) % 8 == 0 && out_head_stride > 0 && out_row_stride > 0 &&
+                   tc::encode_tiled_4d(&prm.tm_out, out, dims, gstr, box) == ABKV_OK)
+                      ? 1
+                      : 0;
   }
   {
     // K and V planes of the paged cache as one 4D tensor: (dim, kv head, page

@@ -102,7 +102,7 @@ static_assert((kBarTmem + 1) * 8 <= 256, "barrier area");
 constexpr float kRescaleThreshold = 8.f;
 
 struct alignas(64) PrefillParams {
-  CUtensorMap tm_q, tm_k, tm_v;
+  CUtensorMap tm_q, tm_k, tm_v, tm_out;
   __nv_bfloat16* out;
   int64_t o_sb, o_sh, o_ss;
   float* lse;  // [B][H][S] or null
@@ -396,11 +396,12 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
       xsum[half * 128 + row] = st.l_run;
       named_bar_sync(pair_bar, 64);
       const float l = st.l_run + xsum[(1 - half) * 128 + row];  // the row sum over both halves
+      // O -> the head's half of the Q buffer (no S MMA reads it any more: o_full followed the head's
+      // last MMAs), 128B-swizzled like the output map's boxes; then one thread stores the head's tile
+      uint8_t* stage = smem + kOffQ + head_slot * kQBytes;
       if (o_ok) {
         const bool none = !(l > 0.f);  // no visible key: zeros
         const float inv = none ? 0.f : 1.f / l;
-        __nv_bfloat16* orow =
-            p.out + (int64_t)b * p.o_sb + (int64_t)h * p.o_sh + (int64_t)q * p.o_ss + (D / 2) * half;
 #pragma unroll 1
         for (int c4 = 0; c4 < D / 64; ++c4) {
           float t[32];
@@ -410,20 +411,29 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
 #pragma unroll
             for (int i = 0; i < 32; ++i) t[i] = 0.f;
           }
+          const int d0 = (D / 2) * half + 32 * c4;  // first dim of these 32
+          uint8_t* atom = stage + (d0 / 64) * (kQBytes / kAtoms);
 #pragma unroll
-          for (int v8 = 0; v8 < 4; ++v8) {
-            uint4 pk;
-            pk.x = pack_bf16x2(t[v8 * 8 + 0] * inv, t[v8 * 8 + 1] * inv);
-            pk.y = pack_bf16x2(t[v8 * 8 + 2] * inv, t[v8 * 8 + 3] * inv);
-            pk.z = pack_bf16x2(t[v8 * 8 + 4] * inv, t[v8 * 8 + 5] * inv);
-            pk.w = pack_bf16x2(t[v8 * 8 + 6] * inv, t[v8 * 8 + 7] * inv);
-            *reinterpret_cast<uint4*>(orow + c4 * 32 + v8 * 8) = pk;
-          }
+          for (int v8 = 0; v8 < 4; ++v8)
+            st_swizzled16(atom, row, (d0 % 64) / 8 + v8, pack_bf16x2(t[v8 * 8 + 0] * inv, t[v8 * 8 + 1] * inv),
+                          pack_bf16x2(t[v8 * 8 + 2] * inv, t[v8 * 8 + 3] * inv),
+                          pack_bf16x2(t[v8 * 8 + 4] * inv, t[v8 * 8 + 5] * inv),
+                          pack_bf16x2(t[v8 * 8 + 6] * inv, t[v8 * 8 + 7] * inv));
         }
         if (p.lse && half == 0) {
           const float lse2 = l > 0.f ? st.m_run + log2f(l) : -INFINITY;
           p.lse[((int64_t)b * p.H + h) * p.S + q] = lse2 * 0.6931471805599453f;  // natural log
         }
+      }
+      asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // staged rows visible to the TMA
+      named_bar_sync(9 + head_slot, 256);                            // the head's 8 warps have staged
+      if ((sw & 7) == 0 && lane == 0) {
+        if (o_ok) {
+          for (int a = 0; a < kAtoms; ++a)
+            tma_store_4d(&p.tm_out, stage + a * (kQBytes / kAtoms), 64 * a, qt * kBM, h, b);
+          tma_store_commit();
+        }
+        tma_store_wait_read();  // the shared memory stays valid until the store has read it
       }
     }
   }
@@ -473,6 +483,7 @@ extern "C" int abkv_prefill_masked(const void* q, const int64_t* q_strides, cons
   int st = make_map(&prm.tm_q, q, B, H, S, head_dim, q_strides, kBM);
   if (st == ABKV_OK) st = make_map(&prm.tm_k, k, B, Hkv, S, head_dim, k_strides, kBN);
   if (st == ABKV_OK) st = make_map(&prm.tm_v, v, B, Hkv, S, head_dim, v_strides, kBN);
+  if (st == ABKV_OK) st = make_map(&prm.tm_out, out, B, H, S, head_dim, out_strides, kBM);
   if (st != ABKV_OK) return st;
   prm.out = static_cast<__nv_bfloat16*>(out);
   prm.o_sb = out_strides[0];

@@ -158,6 +158,28 @@ static __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap*
       "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
       : "memory");
 }
+// Shared -> global tensor store of one box (no multicast), tracked by the issuing thread's bulk
+// async-group: commit it, then wait for its reads before the shared memory is reused or the CTA exits.
+static __device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void* src, int c0, int c1, int c2,
+                                             int c3) {
+  asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];\n" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+               : "memory");
+}
+static __device__ __forceinline__ void tma_store_commit() { asm volatile("cp.async.bulk.commit_group;\n" ::: "memory"); }
+static __device__ __forceinline__ void tma_store_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read 0;\n" ::: "memory");
+}
+// Eight bf16 (four words) into row `row` of a [rows][128 B] 128B-swizzled shared-memory atom at
+// 16-byte chunk `chunk` (0..7): the layout a SWIZZLE_128B tensor map reads.
+static __device__ __forceinline__ void st_swizzled16(uint8_t* atom, int row, int chunk, uint32_t a, uint32_t b,
+                                              uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};\n" ::"r"(smem_u32(atom + row * 128 + ((chunk ^ (row & 7)) << 4))),
+               "r"(a), "r"(b), "r"(c), "r"(d)
+               : "memory");
+}
+
 // Bounded wait; after the first expiry a thread stops waiting altogether (its
 // remaining work is skipped and the error word says why), so a fault in one
 // role cannot stall the CTA for long.
