@@ -31,7 +31,9 @@
 //               online softmax in fp32, P (bf16 pairs) stored into the upper half
 //               of its own S buffer with tcgen05.st -- P is double-buffered with
 //               S, so a head's softmax of tile j+1 waits for its P.V of tile j
-//               only to rescale O; epilogue divides by the row sum.  The S MMA of tile j+2 overwrites P(j)
+//               only to rescale O; the epilogue divides by the row sum and stages a full
+//               query tile's output in the head's (then idle) Q buffer for one TMA tensor
+//               store per 64-dim box (partial causal tiles: row stores).  The S MMA of tile j+2 overwrites P(j)
 //               after P.V(j) read it: tcgen05.mma operations of one thread run
 //               in issue order.
 // With all tiles full (no causal diagonal), the double-buffered S keeps the

@@ -41,7 +41,9 @@
 //               stored into the upper half of its S buffer with tcgen05.st -- P is
 //               double-buffered with S, so a head's softmax of tile j+1 waits for
 //               its P.V of tile j only to rescale O; each warp keeps the row sum of
-//               its columns and rescales and writes its half of O.  The S MMA of
+//               its columns and rescales its half of O; at the end both stage the
+//               output tile in the head's (then idle) Q buffer, 128B-swizzled, and one
+//               thread stores it with a TMA tensor store per 64-dim box.  The S MMA of
 //               tile j+2 overwrites P(j) after P.V(j) read it: tcgen05.mma
 //               operations of one thread run in issue order.
 // Every mbarrier wait is bounded and records ABKV_DEVERR_TIMEOUT on expiry.
