@@ -192,7 +192,18 @@ __device__ __forceinline__ void softmax_half(const CodeStepParams& p, int lim, i
   float t[32];
   tmem_ld32(tmem_s + lane_base + c0, t);
   tmem_wait_ld();
-  auto vis = [&](int c) { return c < lim && (!kHole || c < hs || c >= he); };
+  // visible columns of this half as a bit mask (bit i: column c0 + i): c < lim, outside [hs, he)
+  auto span = [](int a, int e) -> uint32_t {  // bits [a, e) of 32, a and e clamped to [0, 32]
+    a = a < 0 ? 0 : (a > 32 ? 32 : a);
+    e = e < 0 ? 0 : (e > 32 ? 32 : e);
+    if (e <= a) return 0u;
+    const uint32_t hi = e >= 32 ? 0xFFFFFFFFu : ((1u << e) - 1u);
+    const uint32_t lo = (1u << a) - 1u;  // a < 32 here
+    return hi & ~lo;
+  };
+  uint32_t vm = span(0, lim - c0);
+  if (kHole) vm &= ~span(hs - c0, he - c0);
+  auto vis = [&](int c) { return ((vm >> (c - c0)) & 1u) != 0u; };
   const bool full = lim == kBN && (!kHole || he <= 0 || hs >= kBN);
   float mxa[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // independent chains
   if (full) {

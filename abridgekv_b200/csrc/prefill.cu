@@ -136,7 +136,10 @@ __device__ __forceinline__ void softmax_half(const PrefillParams& p, int lim, in
   float t[32];
   tmem_ld32(tmem_s + lane_base + c0, t);
   tmem_wait_ld();
-  auto vis = [&](int c) { return c < lim; };
+  // visible columns of this half as a bit mask (bit i: column c0 + i visible, i.e. c0 + i < lim)
+  const int nv = lim - c0;
+  const uint32_t vm = nv >= 32 ? 0xFFFFFFFFu : (nv <= 0 ? 0u : ((1u << nv) - 1u));
+  auto vis = [&](int c) { return ((vm >> (c - c0)) & 1u) != 0u; };
   const bool full = lim == kBN;
   float mxa[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // independent chains
   if (full) {
