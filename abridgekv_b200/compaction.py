@@ -125,24 +125,65 @@ def execute_kv_copy_group(all_ops: Sequence[Sequence[int]], layer_caches: Sequen
     _compact(layer_caches, [list(all_ops)], workspace, stream)
 
 
+def _group_batches(kv_copy_operations, g: int) -> list:
+    """Group g's ordered batches: batch b of every request concatenated (the reference's order)."""
+    per_req = [ops[g] for ops in kv_copy_operations.values() if g < len(ops)]
+    nb = max((len(b) for b in per_req), default=0)
+    batches = []
+    for b in range(nb):
+        parts = [req_batches[b] for req_batches in per_req if b < len(req_batches)]
+        if parts and all(isinstance(x, CopyOps) for x in parts):
+            merged = CopyOps(np.concatenate([x.array for x in parts]))
+        else:
+            merged = [tuple(op) for x in parts for op in x]
+        if len(merged):
+            batches.append(merged)
+    return batches
+
+
+def _blocks_of(batches) -> np.ndarray:
+    """Every block id (source or destination) the batches touch."""
+    if not batches:
+        return np.zeros(0, dtype=np.int64)
+    flat, _ = _flatten(batches)
+    ops = flat.reshape(-1, 4)
+    return np.unique(np.concatenate([ops[:, 0], ops[:, 2]]))
+
+
 def execute_kv_copy_operations(kv_copy_operations: dict[Hashable, list[list[list[tuple[int, int, int, int]]]]],
                                kv_caches_by_group: Sequence[Sequence[torch.Tensor]],
                                workspace: Workspace | None = None, stream=None) -> None:
-    """request -> per group -> ordered batches, applied group by group."""
+    """request -> per group -> ordered batches, applied group by group.
+
+    When every group names the same layer tensors (the hybrid layout, where the groups share
+    physical tensors and own disjoint blocks of one pool) and no block is touched by two groups,
+    batch b of every group goes into one call: the groups then move disjoint rows, so applying them
+    together equals applying them one after another, with one launch per batch instead of one per
+    group and batch."""
+    per_group = [_group_batches(kv_copy_operations, g) for g in range(len(kv_caches_by_group))]
+    busy = [g for g, batches in enumerate(per_group) if batches]
+    if len(busy) > 1:
+        first = kv_caches_by_group[busy[0]]
+        same = all(len(kv_caches_by_group[g]) == len(first) and
+                   all(a is b or (a.data_ptr() == b.data_ptr() and a.shape == b.shape and a.dtype == b.dtype)
+                       for a, b in zip(kv_caches_by_group[g], first)) for g in busy)
+        if same:
+            blocks = [_blocks_of(per_group[g]) for g in busy]
+            allb = np.concatenate(blocks)
+            if np.unique(allb).size == allb.size:  # pairwise disjoint
+                n = max(len(per_group[g]) for g in busy)
+                merged = []
+                for b in range(n):
+                    parts = [per_group[g][b] for g in busy if b < len(per_group[g])]
+                    if all(isinstance(x, CopyOps) for x in parts):
+                        merged.append(CopyOps(np.concatenate([x.array for x in parts])))
+                    else:
+                        merged.append([tuple(op) for x in parts for op in x])
+                _compact(first, merged, workspace, stream)
+                return
     for g, layer_caches in enumerate(kv_caches_by_group):
-        per_req = [ops[g] for ops in kv_copy_operations.values() if g < len(ops)]
-        nb = max((len(b) for b in per_req), default=0)
-        batches = []
-        for b in range(nb):
-            parts = [req_batches[b] for req_batches in per_req if b < len(req_batches)]
-            if parts and all(isinstance(x, CopyOps) for x in parts):
-                merged = CopyOps(np.concatenate([x.array for x in parts]))
-            else:
-                merged = [tuple(op) for x in parts for op in x]
-            if len(merged):
-                batches.append(merged)
-        if batches:
-            _compact(layer_caches, batches, workspace, stream)
+        if per_group[g]:
+            _compact(layer_caches, per_group[g], workspace, stream)
 
 
 def evict_columns(K: Sequence[torch.Tensor], V: Sequence[torch.Tensor], keep_cols: torch.Tensor,
