@@ -37,7 +37,8 @@
 //               after P.V(j) read it: tcgen05.mma operations of one thread run
 //               in issue order.
 // With all tiles full (no causal diagonal), the double-buffered S keeps the
-// tensor core busier here than the 128-key single-buffer tiling of prefill.cu.
+// tensor core busier here than a 128-key tiling with one S buffer per head (which TMEM
+// would impose: 2 heads x (128 S + 128 O) = 512 columns).
 // Every mbarrier wait is bounded and records ABKV_DEVERR_TIMEOUT on expiry.
 #include <algorithm>
 #include <cstring>
