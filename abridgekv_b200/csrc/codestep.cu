@@ -202,10 +202,13 @@ __device__ __forceinline__ void softmax_half(const CodeStepParams& p, int lim, i
     const uint32_t lo = (1u << a) - 1u;  // a < 32 here
     return hi & ~lo;
   };
-  uint32_t vm = span(0, lim - c0);
-  if (kHole) vm &= ~span(hs - c0, he - c0);
-  auto vis = [&](int c) { return ((vm >> (c - c0)) & 1u) != 0u; };
   const bool full = lim == kBN && (!kHole || he <= 0 || hs >= kBN);
+  uint32_t vm = 0xFFFFFFFFu;  // only a partial tile needs the mask
+  if (!full) {
+    vm = span(0, lim - c0);
+    if (kHole) vm &= ~span(hs - c0, he - c0);
+  }
+  auto vis = [&](int c) { return ((vm >> (c - c0)) & 1u) != 0u; };
   float mxa[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // independent chains
   if (full) {
 #pragma unroll
