@@ -88,6 +88,9 @@ SIGNATURES: dict[str, tuple] = {
     "abkv_planner_pending_num_batches": (c_int, [c_vp, C.c_int64, c_int]),
     "abkv_planner_pending_batch": (c_int, [c_vp, C.c_int64, c_int, c_int, c_i32p, c_int, C.POINTER(c_int)]),
     "abkv_planner_pending_truncation": (c_int, [c_vp, C.c_int64, c_i32p, c_int, C.POINTER(c_int)]),
+    "abkv_planner_pending_export": (c_int, [c_vp, c_i64p, c_i32p, c_i32p, c_i32p, c_int, c_int, c_int,
+                                            C.POINTER(c_int), C.POINTER(c_int), C.POINTER(c_int)]),
+    "abkv_planner_pending_trunc_export": (c_int, [c_vp, c_i64p, c_i32p, c_int, C.POINTER(c_int)]),
     "abkv_planner_clear_pending": (c_int, [c_vp]),
     "abkv_compact_workspace_size": (c_size, [c_int, c_int, c_int, c_int, C.c_int64]),
     "abkv_compact": (c_int, [c_vpp, c_int, c_int, C.c_int64, c_int, c_int, c_int, c_i32p, c_i64p, c_int,

@@ -553,6 +553,64 @@ int abkv_planner_pending_truncation(const abkv_planner_t* p, int64_t req, int32_
   return ABKV_OK;
 }
 
+int abkv_planner_pending_export(const abkv_planner_t* p, int64_t* req_ids, int32_t* group_batches,
+                                int32_t* batch_ops, int32_t* ops, int cap_reqs, int cap_batches, int cap_ops,
+                                int* n_reqs, int* n_batches, int* n_ops) {
+  if (!p || !n_reqs || !n_batches || !n_ops) return ABKV_ERR_INVALID_ARG;
+  const int G = p->num_groups;
+  int64_t nr = 0, nbt = 0, no = 0;
+  for (const auto& kv : p->pending_ops) {
+    ++nr;
+    for (const auto& batches : kv.second) {
+      nbt += (int64_t)batches.size();
+      for (const auto& b : batches) no += (int64_t)b.size();
+    }
+  }
+  if (nr > INT32_MAX || nbt > INT32_MAX || no > INT32_MAX / 4) return ABKV_ERR_INVALID_ARG;
+  *n_reqs = (int)nr;
+  *n_batches = (int)nbt;
+  *n_ops = (int)no;
+  const bool query = !req_ids && !group_batches && !batch_ops && !ops && !cap_reqs && !cap_batches && !cap_ops;
+  if (query) return ABKV_OK;
+  if (nr > cap_reqs || nbt > cap_batches || no > cap_ops || (nr && (!req_ids || !group_batches)) ||
+      (nbt && !batch_ops) || (no && !ops))
+    return ABKV_ERR_INVALID_ARG;
+  int64_t r = 0, bi = 0, oi = 0;
+  for (const auto& kv : p->pending_ops) {
+    req_ids[r] = kv.first;
+    for (int g = 0; g < G; ++g) {
+      const bool has = g < (int)kv.second.size();
+      group_batches[r * G + g] = has ? (int32_t)kv.second[g].size() : 0;
+      if (!has) continue;
+      for (const auto& b : kv.second[g]) {
+        batch_ops[bi++] = (int32_t)b.size();
+        for (const auto& op : b) {
+          for (int k = 0; k < 4; ++k) ops[4 * oi + k] = op[k];
+          ++oi;
+        }
+      }
+    }
+    ++r;
+  }
+  return ABKV_OK;
+}
+
+int abkv_planner_pending_trunc_export(const abkv_planner_t* p, int64_t* req_ids, int32_t* counts, int cap,
+                                      int* n) {
+  if (!p || !n) return ABKV_ERR_INVALID_ARG;
+  const int G = p->num_groups;
+  *n = (int)p->pending_trunc.size();
+  if (!req_ids && !counts && !cap) return ABKV_OK;
+  if (*n > cap || (*n && (!req_ids || !counts))) return ABKV_ERR_INVALID_ARG;
+  int r = 0;
+  for (const auto& kv : p->pending_trunc) {
+    req_ids[r] = kv.first;
+    for (int g = 0; g < G; ++g) counts[r * G + g] = g < (int)kv.second.size() ? kv.second[g] : -1;
+    ++r;
+  }
+  return ABKV_OK;
+}
+
 int abkv_planner_clear_pending(abkv_planner_t* p) {
   if (!p) return ABKV_ERR_INVALID_ARG;
   p->pending_ops.clear();

@@ -194,34 +194,46 @@ class BlockPlanner:
         src_off, dst_block, dst_off)] (Scheduler.pending_kv_copy_operations);
         truncations: request -> per-group block count after compaction
         (Scheduler.pending_block_table_truncations)."""
-        n = C.c_int(0)
-        self._lib.abkv_planner_pending_requests(self._h, None, 0, C.byref(n))
-        keys = (C.c_int64 * max(n.value, 1))()
-        _lib.check("abkv_planner_pending_requests",
-                   self._lib.abkv_planner_pending_requests(self._h, keys, n.value, C.byref(n)))
+        G = self.num_groups
+        nr, nb, no = C.c_int(0), C.c_int(0), C.c_int(0)
+        _lib.check("abkv_planner_pending_export",
+                   self._lib.abkv_planner_pending_export(self._h, None, None, None, None, 0, 0, 0, C.byref(nr),
+                                                         C.byref(nb), C.byref(no)))
+        req_ids = np.zeros(max(nr.value, 1), dtype=np.int64)
+        group_batches = np.zeros(max(nr.value * G, 1), dtype=np.int32)
+        batch_ops = np.zeros(max(nb.value, 1), dtype=np.int32)
+        flat = np.zeros(max(4 * no.value, 4), dtype=np.int32)
+        _lib.check("abkv_planner_pending_export",
+                   self._lib.abkv_planner_pending_export(
+                       self._h, req_ids.ctypes.data_as(_lib.c_i64p), group_batches.ctypes.data_as(_lib.c_i32p),
+                       batch_ops.ctypes.data_as(_lib.c_i32p), flat.ctypes.data_as(_lib.c_i32p), nr.value, nb.value,
+                       no.value, C.byref(nr), C.byref(nb), C.byref(no)))
+        ops_arr = flat[:4 * no.value].reshape(-1, 4)
         ops: dict = {}
-        for k in keys[:n.value]:
+        bi = oi = 0
+        for r in range(nr.value):
             per_group = []
-            for g in range(self.num_groups):
-                nb = self._lib.abkv_planner_pending_num_batches(self._h, k, g)
+            for g in range(G):
                 batches = []
-                for b in range(nb):
-                    cnt = C.c_int(0)
-                    self._lib.abkv_planner_pending_batch(self._h, k, g, b, None, 0, C.byref(cnt))
-                    buf = (C.c_int32 * max(4 * cnt.value, 4))()
-                    _lib.check("abkv_planner_pending_batch",
-                               self._lib.abkv_planner_pending_batch(self._h, k, g, b, buf, cnt.value,
-                                                                    C.byref(cnt)))
-                    batches.append(CopyOps(np.frombuffer(buf, dtype=np.int32, count=4 * cnt.value).copy()))
+                for _ in range(int(group_batches[r * G + g])):
+                    cnt = int(batch_ops[bi])
+                    batches.append(CopyOps(ops_arr[oi:oi + cnt].copy()))
+                    bi += 1
+                    oi += cnt
                 per_group.append(batches)
+            k = int(req_ids[r])
             ops[self._names.get(k, k)] = per_group
-        trunc = {}
-        for rid, k in self._ids.items():
-            buf = (C.c_int32 * self.num_groups)()
-            _lib.check("abkv_planner_pending_truncation",
-                       self._lib.abkv_planner_pending_truncation(self._h, k, buf, self.num_groups, C.byref(n)))
-            if n.value:
-                trunc[rid] = tuple(buf[:n.value])
+        nt = C.c_int(0)
+        _lib.check("abkv_planner_pending_trunc_export",
+                   self._lib.abkv_planner_pending_trunc_export(self._h, None, None, 0, C.byref(nt)))
+        t_ids = np.zeros(max(nt.value, 1), dtype=np.int64)
+        t_counts = np.zeros(max(nt.value * G, 1), dtype=np.int32)
+        _lib.check("abkv_planner_pending_trunc_export",
+                   self._lib.abkv_planner_pending_trunc_export(
+                       self._h, t_ids.ctypes.data_as(_lib.c_i64p), t_counts.ctypes.data_as(_lib.c_i32p), nt.value,
+                       C.byref(nt)))
+        by_id = {int(t_ids[r]): tuple(int(v) for v in t_counts[r * G:(r + 1) * G]) for r in range(nt.value)}
+        trunc = {rid: by_id[k] for rid, k in self._ids.items() if k in by_id}
         self.clear_pending()
         return ops, trunc
 

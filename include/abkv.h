@@ -316,6 +316,23 @@ int abkv_planner_pending_batch(const abkv_planner_t* planner, int64_t request,
 int abkv_planner_pending_truncation(const abkv_planner_t* planner,
                                     int64_t request, int32_t* out, int cap,
                                     int* n);
+/* Every pending copy op in one call (the same content as the per-request /
+ * per-group / per-batch functions above, for hosts that read it all at once):
+ * req_ids[n_reqs] in request-id order; group_batches[n_reqs * num_groups] =
+ * batches of (request, group); batch_ops[n_batches] = ops per batch, batches
+ * in (request, group, order) order; ops[4 * n_ops] the ops themselves.  With
+ * every pointer NULL and every cap 0 it only reports the three counts. */
+int abkv_planner_pending_export(const abkv_planner_t* planner, int64_t* req_ids,
+                                int32_t* group_batches, int32_t* batch_ops,
+                                int32_t* ops, int cap_reqs, int cap_batches,
+                                int cap_ops, int* n_reqs, int* n_batches,
+                                int* n_ops);
+/* Every pending truncation in one call: req_ids[n], counts[n * num_groups]
+ * (the per-group block counts of abkv_planner_pending_truncation).  With both
+ * pointers NULL and cap 0 it only reports n. */
+int abkv_planner_pending_trunc_export(const abkv_planner_t* planner,
+                                      int64_t* req_ids, int32_t* counts,
+                                      int cap, int* n);
 int abkv_planner_clear_pending(abkv_planner_t* planner);
 
 /* ========================================================================
