@@ -21,8 +21,9 @@
 // path instead: gather every source row into the workspace, then scatter
 // (for duplicate destinations the op listed last wins).
 //
-// Kernel work item = (chain, layer, K|V half); one warp per item, 16-byte
-// loads/stores, 64 bytes per lane per 2 KiB row half (Hkv*D*2 bytes).
+// Kernel work item = (chain, layer); one warp per item moves the K and V row
+// halves of each op together, 16-byte loads/stores, 64 bytes per lane per
+// 2 KiB row half (Hkv*D*2 bytes), both halves' loads in flight before the stores.
 #include <algorithm>
 #include <cstring>
 #include <vector>
@@ -69,18 +70,18 @@ __device__ __forceinline__ void st_cg(void* ptr, uint4 v) {
                : "memory");
 }
 
-// One warp walks one chain for one (layer, half).  Rows are processed in
-// 512-byte slabs (32 lanes x 16 B); each lane keeps up to kVec vectors.
+// One warp walks one chain for one layer, moving each op's K and V row halves
+// together: rows are processed in 512-byte slabs (32 lanes x 16 B), and each
+// lane keeps up to kVec vectors of each half in flight before its stores.
 constexpr int kVec = 4;
 
 __global__ void __launch_bounds__(256) compact_chain_kernel(const __grid_constant__ CompactParams p) {
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  const int64_t items = (int64_t)p.n_chains * p.num_layers * 2;
+  const int64_t items = (int64_t)p.n_chains * p.num_layers;
   if (warp >= items) return;
-  const int half = (int)(warp & 1);
-  const int layer = (int)((warp >> 1) % p.num_layers);
-  const int c = (int)((warp >> 1) / p.num_layers);
+  const int layer = (int)(warp % p.num_layers);
+  const int c = (int)(warp / p.num_layers);
   const int o0 = p.chain[c], o1 = p.chain[c + 1];
   const int64_t vecs = p.row_bytes >> 4;  // 16-byte vectors per row half
   for (int i = o0; i < o1; ++i) {
@@ -89,20 +90,24 @@ __global__ void __launch_bounds__(256) compact_chain_kernel(const __grid_constan
       if (lane == 0) set_error(p.err, ABKV_DEVERR_ROW_OOB);
       continue;
     }
-    const char* src = row_ptr(p, layer, half, sb, so);
-    char* dst = row_ptr(p, layer, half, db, dof);
+    const char* src = row_ptr(p, layer, 0, sb, so);
+    char* dst = row_ptr(p, layer, 0, db, dof);
     for (int64_t v0 = 0; v0 < vecs; v0 += 32 * kVec) {
-      uint4 buf[kVec];
+      uint4 buf[2][kVec];
 #pragma unroll
-      for (int k = 0; k < kVec; ++k) {
-        const int64_t v = v0 + k * 32 + lane;
-        if (v < vecs) buf[k] = ld_cg(src + 16 * v);
-      }
+      for (int h = 0; h < 2; ++h)
 #pragma unroll
-      for (int k = 0; k < kVec; ++k) {
-        const int64_t v = v0 + k * 32 + lane;
-        if (v < vecs) st_cg(dst + 16 * v, buf[k]);
-      }
+        for (int k = 0; k < kVec; ++k) {
+          const int64_t v = v0 + k * 32 + lane;
+          if (v < vecs) buf[h][k] = ld_cg(src + h * p.half_stride + 16 * v);
+        }
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int k = 0; k < kVec; ++k) {
+          const int64_t v = v0 + k * 32 + lane;
+          if (v < vecs) st_cg(dst + h * p.half_stride + 16 * v, buf[h][k]);
+        }
     }
   }
 }
@@ -342,7 +347,7 @@ extern "C" int abkv_compact(void* const* layer_caches, int num_layers, int layou
     prm.n_ops = (int)n;
     if (!pl.two_phase) {
       prm.n_chains = pl.n_chains;
-      const int64_t warps = (int64_t)pl.n_chains * num_layers * 2;
+      const int64_t warps = (int64_t)pl.n_chains * num_layers;
       const int64_t blocks = (warps * 32 + 255) / 256;
       compact_chain_kernel<<<(unsigned)blocks, 256, 0, s>>>(prm);
     } else {
