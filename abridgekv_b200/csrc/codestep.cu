@@ -154,20 +154,39 @@ __device__ __noinline__ void commit_request_ops(const CodeStepParams& p, bool de
   __syncthreads();
   if (!s_last) return;
   const int o0 = __ldcg(p.coff + blockIdx.z), o1 = __ldcg(p.coff + blockIdx.z + 1);
+  // one warp per op moves its K and V rows, each lane with up to 2 x 4 vectors in flight
+  constexpr int kCV = 4;
+  const int lane = threadIdx.x & 31, nw = blockDim.x >> 5;
   const int64_t vecs = p.row_bytes >> 4;  // 16-byte vectors per K or V row
-  const int64_t total = (int64_t)(o1 - o0) * 2 * vecs;
-  for (int64_t idx = threadIdx.x; idx < total; idx += blockDim.x) {
-    const int op = o0 + (int)(idx / (2 * vecs));
-    const int64_t rem = idx - (int64_t)(op - o0) * 2 * vecs;
-    const int half = (int)(rem / vecs);
-    const int64_t v = rem - half * vecs;
+  for (int op = o0 + (int)(threadIdx.x >> 5); op < o1; op += nw) {
     const int sb = __ldcg(p.cops + 4 * op), so = __ldcg(p.cops + 4 * op + 1);
     const int db = __ldcg(p.cops + 4 * op + 2), dof = __ldcg(p.cops + 4 * op + 3);
-    const int64_t ps = p.fa_layout ? (half ? p.num_blocks + sb : sb) : 2 * (int64_t)sb + half;
-    const int64_t pd = p.fa_layout ? (half ? p.num_blocks + db : db) : 2 * (int64_t)db + half;
-    const uint4* src = reinterpret_cast<const uint4*>(p.kv + (ps * p.page + so) * p.row_bytes) + v;
-    uint4* dst = reinterpret_cast<uint4*>(p.kv + (pd * p.page + dof) * p.row_bytes) + v;
-    __stcg(dst, __ldcg(src));
+    const uint4* src[2];
+    uint4* dst[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int64_t ps = p.fa_layout ? (h ? p.num_blocks + sb : sb) : 2 * (int64_t)sb + h;
+      const int64_t pd = p.fa_layout ? (h ? p.num_blocks + db : db) : 2 * (int64_t)db + h;
+      src[h] = reinterpret_cast<const uint4*>(p.kv + (ps * p.page + so) * p.row_bytes);
+      dst[h] = reinterpret_cast<uint4*>(p.kv + (pd * p.page + dof) * p.row_bytes);
+    }
+    for (int64_t v0 = 0; v0 < vecs; v0 += 32 * kCV) {
+      uint4 buf[2][kCV];
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int k = 0; k < kCV; ++k) {
+          const int64_t v = v0 + k * 32 + lane;
+          if (v < vecs) buf[h][k] = __ldcg(src[h] + v);
+        }
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int k = 0; k < kCV; ++k) {
+          const int64_t v = v0 + k * 32 + lane;
+          if (v < vecs) __stcg(dst[h] + v, buf[h][k]);
+        }
+    }
   }
 }
 
