@@ -142,12 +142,25 @@ def _group_batches(kv_copy_operations, g: int) -> list:
 
 
 def _blocks_of(batches) -> np.ndarray:
-    """Every block id (source or destination) the batches touch."""
+    """Every block id (source or destination) the batches touch, with repeats."""
     if not batches:
         return np.zeros(0, dtype=np.int64)
     flat, _ = _flatten(batches)
     ops = flat.reshape(-1, 4)
-    return np.unique(np.concatenate([ops[:, 0], ops[:, 2]]))
+    return np.concatenate([ops[:, 0], ops[:, 2]])
+
+
+def _disjoint(block_sets: Sequence[np.ndarray], num_blocks: int) -> bool:
+    """No block id in two of the sets: an owner per block, marked set after set (ids outside
+    [0, num_blocks) share one slot, so two sets holding such ids count as overlapping)."""
+    owner = np.full(num_blocks + 1, -1, dtype=np.int32)
+    for i, ids in enumerate(block_sets):
+        ids = np.where((ids >= 0) & (ids < num_blocks), ids, num_blocks)
+        seen = owner[ids]
+        if np.any((seen >= 0) & (seen != i)):
+            return False
+        owner[ids] = i
+    return True
 
 
 def execute_kv_copy_operations(kv_copy_operations: dict[Hashable, list[list[list[tuple[int, int, int, int]]]]],
@@ -168,9 +181,7 @@ def execute_kv_copy_operations(kv_copy_operations: dict[Hashable, list[list[list
                    all(a is b or (a.data_ptr() == b.data_ptr() and a.shape == b.shape and a.dtype == b.dtype)
                        for a, b in zip(kv_caches_by_group[g], first)) for g in busy)
         if same:
-            blocks = [_blocks_of(per_group[g]) for g in busy]
-            allb = np.concatenate(blocks)
-            if np.unique(allb).size == allb.size:  # pairwise disjoint
+            if _disjoint([_blocks_of(per_group[g]) for g in busy], _layout_of(first[0])[1]):
                 n = max(len(per_group[g]) for g in busy)
                 merged = []
                 for b in range(n):

@@ -57,3 +57,24 @@ def test_single_group_and_empty_groups(calls):
     calls.clear()
     compaction.execute_kv_copy_operations({}, [tensors, tensors])
     assert calls == []
+
+
+def test_block_ids_outside_the_pool_keep_groups_separate(calls):
+    """Ids outside [0, num_blocks) are not compared one by one: two groups holding such ids take the
+    per-group path (in group order), so the kernel reports them exactly as the unmerged executor would."""
+    tensors = [torch.zeros(4, 2, 16, 1, 8)]  # 4 blocks
+    ops = {"r0": [[_ops((1, 0, 9, 5))], [_ops((2, 7, 11, 3))]]}
+    compaction.execute_kv_copy_operations(ops, [tensors, tensors])
+    assert [b for _, b in calls] == [[[(1, 0, 9, 5)]], [[(2, 7, 11, 3)]]]
+
+
+def test_disjoint_check_matches_set_intersection():
+    rng = np.random.default_rng(3)
+    for _ in range(200):
+        n = int(rng.integers(1, 5))
+        sets = [rng.integers(-2, 40, size=int(rng.integers(0, 12))) for _ in range(n)]
+        inside = [set(int(x) for x in s if 0 <= x < 32) for s in sets]
+        outside = [any(not (0 <= x < 32) for x in s) for s in sets]
+        expect = all(not (inside[i] & inside[j]) and not (outside[i] and outside[j])
+                     for i in range(n) for j in range(i + 1, n))
+        assert compaction._disjoint(sets, 32) == expect
