@@ -192,28 +192,63 @@ class SlotMap {
   size_t mask_ = 0;
 };
 
+// Row (block * page + offset, >= 0) -> the op that reads it and the op that writes it, in one
+// 16-byte entry: open addressing with linear probing at load <= 1/2, Fibonacci hashing.  One probe
+// per source and per destination row; the source's entry index is kept, so finding the op that
+// overwrites a source row needs no second lookup.
+class RowMap {
+ public:
+  struct Entry {
+    int64_t key;
+    int32_t reader, writer;
+  };
+  explicit RowMap(int64_t rows) {
+    size_t cap = 16;
+    while (cap < (size_t)rows * 2) cap <<= 1;
+    e_.assign(cap, Entry{-1, -1, -1});
+    mask_ = cap - 1;
+  }
+  // The index of `key`'s entry, inserted (reader and writer unset) when absent.
+  size_t locate(int64_t key) {
+    const uint64_t x = (uint64_t)key * 0x9E3779B97F4A7C15ull;
+    for (size_t i = (size_t)(x ^ (x >> 29)) & mask_;; i = (i + 1) & mask_) {
+      if (e_[i].key == key) return i;
+      if (e_[i].key < 0) {
+        e_[i].key = key;
+        return i;
+      }
+    }
+  }
+  Entry& operator[](size_t i) { return e_[i]; }
+
+ private:
+  std::vector<Entry> e_;
+  size_t mask_ = 0;
+};
+
 // Split one batch into chains (see file comment); returns false when the
 // batch needs the two-phase path.
 bool plan_chains(const int32_t* ops, int64_t n, int page, BatchPlan* out) {
   auto key = [page](int32_t blk, int32_t off) -> int64_t { return (int64_t)blk * page + off; };
-  SlotMap reader(n), writer(n);
+  RowMap rows(2 * n);
+  std::vector<size_t> src_at(n);
   for (int64_t i = 0; i < n; ++i) {
-    bool fresh;
-    int64_t& rv = reader.slot(key(ops[4 * i], ops[4 * i + 1]), &fresh);
-    if (!fresh) return false;  // a row read twice
-    rv = i;
-    int64_t& wv = writer.slot(key(ops[4 * i + 2], ops[4 * i + 3]), &fresh);
-    if (!fresh) return false;  // duplicate destination
-    wv = i;
+    const size_t a = rows.locate(key(ops[4 * i], ops[4 * i + 1]));
+    if (rows[a].reader >= 0) return false;  // a row read twice
+    rows[a].reader = (int32_t)i;
+    src_at[i] = a;
+    const size_t w = rows.locate(key(ops[4 * i + 2], ops[4 * i + 3]));
+    if (rows[w].writer >= 0) return false;  // duplicate destination
+    rows[w].writer = (int32_t)i;
   }
   // next(j) = the op that overwrites j's source row (other than j itself)
   std::vector<int64_t> next(n, -1);
   std::vector<char> has_prev(n, 0);
   for (int64_t j = 0; j < n; ++j) {
-    const int64_t* w = writer.find(key(ops[4 * j], ops[4 * j + 1]));
-    if (w && *w != j) {
-      next[j] = *w;
-      has_prev[*w] = 1;
+    const int64_t w = rows[src_at[j]].writer;
+    if (w >= 0 && w != j) {
+      next[j] = w;
+      has_prev[w] = 1;
     }
   }
   std::vector<char> seen(n, 0);
