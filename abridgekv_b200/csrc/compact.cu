@@ -16,7 +16,8 @@
 // order by ONE thread group, with each lane always handling the same bytes of
 // every row, reproduces gather-then-scatter exactly with no grid barrier (no
 // op outside a chain reads or writes that chain's rows).  Batches without any
-// hazard are chains of length one and run fully parallel.  A batch with a
+// hazard are chains of length one and run fully parallel (found with a bit per
+// pool row for "read" and "written", without hashing, when the pool is small).  A batch with a
 // cycle, a row read twice, or a duplicate destination takes the two-phase
 // path instead: gather every source row into the workspace, then scatter
 // (for duplicate destinations the op listed last wins).
@@ -82,7 +83,7 @@ __global__ void __launch_bounds__(256) compact_chain_kernel(const __grid_constan
   if (warp >= items) return;
   const int layer = (int)(warp % p.num_layers);
   const int c = (int)(warp / p.num_layers);
-  const int o0 = p.chain[c], o1 = p.chain[c + 1];
+  const int o0 = p.chain ? p.chain[c] : c, o1 = p.chain ? p.chain[c + 1] : c + 1;  // null: one op per chain
   const int64_t vecs = p.row_bytes >> 4;  // 16-byte vectors per row half
   for (int i = o0; i < o1; ++i) {
     const int sb = p.ops[4 * i], so = p.ops[4 * i + 1], db = p.ops[4 * i + 2], dof = p.ops[4 * i + 3];
@@ -148,7 +149,36 @@ struct BatchPlan {
   std::vector<int32_t> chain;  // chain offsets (chain path) or superseded flags (two-phase)
   bool two_phase = false;
   int n_chains = 0;
+  const int32_t* singles = nullptr;  // hazard-free batch: the caller's ops, one op per chain
 };
+
+// Hazard-free batches (no row read twice, no destination twice, no source row that an op of the
+// batch writes) are every op its own chain, in input order: one bit per cache row for "read" and
+// one for "written" decide it without hashing, when the pool's rows fit a small bitmap.
+bool plan_singles(const int32_t* ops, int64_t n, int page, int64_t num_blocks, BatchPlan* out) {
+  const int64_t rows = num_blocks * page;
+  if (rows > ((int64_t)1 << 23) || rows > 256 * n + 65536) return false;
+  const size_t words = (size_t)((rows + 63) >> 6);
+  std::vector<uint64_t> rd(words, 0), wr(words, 0);
+  for (int64_t i = 0; i < n; ++i) {
+    const int64_t r = (int64_t)ops[4 * i] * page + ops[4 * i + 1];
+    const int64_t w = (int64_t)ops[4 * i + 2] * page + ops[4 * i + 3];
+    const uint64_t rb = 1ull << (r & 63), wb = 1ull << (w & 63);
+    if ((rd[r >> 6] & rb) || (wr[w >> 6] & wb)) return false;  // a row read twice, or written twice
+    rd[r >> 6] |= rb;
+    wr[w >> 6] |= wb;
+  }
+  for (int64_t i = 0; i < n; ++i) {
+    const int64_t r = (int64_t)ops[4 * i] * page + ops[4 * i + 1];
+    if (wr[r >> 6] & (1ull << (r & 63))) return false;  // a source row is overwritten in the batch
+  }
+  out->ops.clear();
+  out->chain.clear();
+  out->singles = ops;
+  out->n_chains = (int)n;
+  out->two_phase = false;
+  return true;
+}
 
 // Slot (block * page + offset, >= 0) -> op index, open addressing with linear
 // probing at load <= 1/4 and Fibonacci (Knuth multiplicative) hashing: the host
@@ -361,24 +391,26 @@ extern "C" int abkv_compact(void* const* layer_caches, int num_layers, int layou
   for (int b = 0; b < num_batches; ++b) {
     const int64_t n = batch_offsets[b + 1] - batch_offsets[b];
     const int32_t* bo = ops + 4 * batch_offsets[b];
-    if (!plan_chains(bo, n, page_size, &plans[b])) plan_two_phase(bo, n, page_size, &plans[b]);
+    if (!plan_singles(bo, n, page_size, num_blocks, &plans[b]) && !plan_chains(bo, n, page_size, &plans[b]))
+      plan_two_phase(bo, n, page_size, &plans[b]);
     if (plans[b].two_phase &&
         workspace_bytes < base_need + (size_t)n * num_layers * 2 * (size_t)row_bytes)
       return ABKV_ERR_WORKSPACE;
   }
   for (int b = 0; b < num_batches; ++b) {
     BatchPlan& pl = plans[b];
-    const int64_t n = (int64_t)pl.ops.size() / 4;
+    const int64_t n = pl.singles ? pl.n_chains : (int64_t)pl.ops.size() / 4;
     if (n == 0) continue;
     // Pageable-host copies are staged before cudaMemcpyAsync returns, so the
-    // plan vectors may be released afterwards; stream order protects the
-    // device buffer from the next batch's upload until this batch's kernels ran.
-    if (cudaMemcpyAsync(d_ops, pl.ops.data(), pl.ops.size() * sizeof(int32_t), cudaMemcpyHostToDevice,
-                        s) != cudaSuccess)
+    // plan vectors (and the caller's ops) may be released afterwards; stream order
+    // protects the device buffer from the next batch's upload until this batch's kernels ran.
+    const int32_t* host_ops = pl.singles ? pl.singles : pl.ops.data();
+    if (cudaMemcpyAsync(d_ops, host_ops, (size_t)n * 4 * sizeof(int32_t), cudaMemcpyHostToDevice, s) != cudaSuccess)
       return ABKV_ERR_CUDA;
-    if (cudaMemcpyAsync(d_chain, pl.chain.data(), pl.chain.size() * sizeof(int32_t),
-                        cudaMemcpyHostToDevice, s) != cudaSuccess)
+    if (!pl.singles && cudaMemcpyAsync(d_chain, pl.chain.data(), pl.chain.size() * sizeof(int32_t),
+                                       cudaMemcpyHostToDevice, s) != cudaSuccess)
       return ABKV_ERR_CUDA;
+    prm.chain = pl.singles ? nullptr : d_chain;
     prm.n_ops = (int)n;
     if (!pl.two_phase) {
       prm.n_chains = pl.n_chains;

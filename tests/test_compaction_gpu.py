@@ -3,7 +3,8 @@
 * the reference's own executor results (tests/golden/executor_*.json) in both
   paged layouts;
 * adversarial batches (overlapping left shifts = long chains, swap cycles,
-  duplicate destinations, rows read twice) against the numpy oracle;
+  duplicate destinations, rows read twice, rows copied onto themselves,
+  hazard-free moves) against the numpy oracle;
 * BASELINE config 4 at full size: 16 sequences x 16 blocks (C=512, K=256),
   quotas 256/128/64, all 36 layers; after every block's compaction, each
   surviving logical row's checksum equals its pre-compaction checksum
@@ -62,6 +63,10 @@ def _random_batch(rng, nb, page, kind):
         s = rng.randrange(slots)
         ops = [(s, rng.randrange(slots)) for _ in range(5)]
         ops = list({d: (x, d) for x, d in ops}.values())
+    elif kind == "self":  # rows copied onto themselves among disjoint moves
+        pool = rng.sample(range(slots), 300)
+        ops = [(pool[i], pool[100 + i]) for i in range(100)] + [(pool[200 + i], pool[200 + i]) for i in range(100)]
+        rng.shuffle(ops)
     else:  # disjoint
         pool = rng.sample(range(slots), 400)
         ops = [(pool[i], pool[200 + i]) for i in range(200)]
@@ -71,7 +76,7 @@ def _random_batch(rng, nb, page, kind):
 
 
 @pytest.mark.parametrize("layout", [0, 1])
-@pytest.mark.parametrize("kind", ["shift", "swap", "dup", "read_twice", "disjoint"])
+@pytest.mark.parametrize("kind", ["shift", "swap", "dup", "read_twice", "self", "disjoint"])
 def test_executor_hazards_match_oracle(layout, kind):
     rng = random.Random(hash((layout, kind)) & 0xFFFF)
     nb, page, hkv, d, L = 48, 16, 8, 128, 5
