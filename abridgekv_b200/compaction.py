@@ -40,6 +40,13 @@ class CopyOps(_SequenceABC):
     def __init__(self, array) -> None:
         self.array = np.ascontiguousarray(np.asarray(array, dtype=np.int32).reshape(-1, 4))
 
+    @classmethod
+    def wrap(cls, array: np.ndarray) -> "CopyOps":
+        """A batch over ``array`` as it is: a C-contiguous int32 ``[n, 4]`` array (no conversion)."""
+        obj = object.__new__(cls)
+        obj.array = array
+        return obj
+
     def __len__(self) -> int:
         return int(self.array.shape[0])
 

@@ -208,20 +208,22 @@ class BlockPlanner:
                        self._h, req_ids.ctypes.data_as(_lib.c_i64p), group_batches.ctypes.data_as(_lib.c_i32p),
                        batch_ops.ctypes.data_as(_lib.c_i32p), flat.ctypes.data_as(_lib.c_i32p), nr.value, nb.value,
                        no.value, C.byref(nr), C.byref(nb), C.byref(no)))
+        # each batch is a row slice of this call's own array (C-contiguous, never reused)
         ops_arr = flat[:4 * no.value].reshape(-1, 4)
+        n_batches = group_batches[:nr.value * G].tolist()
+        counts = batch_ops[:nb.value].tolist()
         ops: dict = {}
         bi = oi = 0
-        for r in range(nr.value):
+        for r, k in enumerate(req_ids[:nr.value].tolist()):
             per_group = []
             for g in range(G):
                 batches = []
-                for _ in range(int(group_batches[r * G + g])):
-                    cnt = int(batch_ops[bi])
-                    batches.append(CopyOps(ops_arr[oi:oi + cnt].copy()))
+                for _ in range(n_batches[r * G + g]):
+                    cnt = counts[bi]
+                    batches.append(CopyOps.wrap(ops_arr[oi:oi + cnt]))
                     bi += 1
                     oi += cnt
                 per_group.append(batches)
-            k = int(req_ids[r])
             ops[self._names.get(k, k)] = per_group
         nt = C.c_int(0)
         _lib.check("abkv_planner_pending_trunc_export",
@@ -232,7 +234,7 @@ class BlockPlanner:
                    self._lib.abkv_planner_pending_trunc_export(
                        self._h, t_ids.ctypes.data_as(_lib.c_i64p), t_counts.ctypes.data_as(_lib.c_i32p), nt.value,
                        C.byref(nt)))
-        by_id = {int(t_ids[r]): tuple(int(v) for v in t_counts[r * G:(r + 1) * G]) for r in range(nt.value)}
+        by_id = dict(zip(t_ids[:nt.value].tolist(), map(tuple, t_counts[:nt.value * G].reshape(-1, G).tolist())))
         trunc = {rid: by_id[k] for rid, k in self._ids.items() if k in by_id}
         self.clear_pending()
         return ops, trunc
