@@ -231,10 +231,20 @@ struct abkv_planner {
     const int64_t removed = end - start;
     if ((n_active + block_size - 1) / block_size > (int64_t)blocks.size()) return ABKV_ERR_SPAN;
     ops->reserve(ops->size() + (size_t)(n_active - end));
+    // slot s moves to s - removed, for s in [end, n_active): block and offset of both advance by one
+    // slot per op (no division per op)
+    int64_t sb = end / block_size, d0 = end - removed, db = d0 / block_size;
+    int32_t so = (int32_t)(end % block_size), dof = (int32_t)(d0 % block_size);
     for (int64_t s = end; s < n_active; ++s) {
-      const int64_t d = s - removed;
-      ops->push_back({blocks[s / block_size], (int32_t)(s % block_size), blocks[d / block_size],
-                      (int32_t)(d % block_size)});
+      ops->push_back({blocks[sb], so, blocks[db], dof});
+      if (++so == block_size) {
+        so = 0;
+        ++sb;
+      }
+      if (++dof == block_size) {
+        dof = 0;
+        ++db;
+      }
     }
     *freed = truncate(blocks, n_active - removed);
     return ABKV_OK;
