@@ -158,16 +158,15 @@ def _blocks_of(batches) -> np.ndarray:
 
 
 def _disjoint(block_sets: Sequence[np.ndarray], num_blocks: int) -> bool:
-    """No block id in two of the sets: an owner per block, marked set after set (ids outside
-    [0, num_blocks) share one slot, so two sets holding such ids count as overlapping)."""
-    owner = np.full(num_blocks + 1, -1, dtype=np.int32)
-    for i, ids in enumerate(block_sets):
-        ids = np.where((ids >= 0) & (ids < num_blocks), ids, num_blocks)
-        seen = owner[ids]
-        if np.any((seen >= 0) & (seen != i)):
-            return False
-        owner[ids] = i
-    return True
+    """No block id in two of the sets: each set marks its blocks once in a flag array and the
+    counts add up (ids outside [0, num_blocks) all land in one extra slot, so two sets holding such
+    ids count as overlapping)."""
+    count = np.zeros(num_blocks + 1, dtype=np.uint16)
+    for ids in block_sets:
+        seen = np.zeros(num_blocks + 1, dtype=bool)
+        seen[np.clip(ids, -1, num_blocks)] = True  # -1 indexes the extra slot, as num_blocks does
+        count += seen
+    return len(block_sets) < 2 or int(count.max()) <= 1
 
 
 def execute_kv_copy_operations(kv_copy_operations: dict[Hashable, list[list[list[tuple[int, int, int, int]]]]],
