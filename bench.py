@@ -678,7 +678,7 @@ def run_path(args) -> None:
         launches = 36 * args.steps
     else:
         line = benchmarks.bench_compaction(ns)
-        launches = None
+        launches = line.get("gpu_launches")  # counted by the benchmark over its steady block finishes
     clocks = sampler.stop()
     budget = 0.0 if args.no_cpu_baseline else args.cpu_budget
     cpu = None if args.no_cpu_baseline else {"prefill": cpu_baseline_prefill, "prefill_bwd": cpu_baseline_prefill_bwd,
@@ -716,7 +716,8 @@ def run_secondary(args) -> dict:
         keep = {k: line[k] for k in ("metric", "value", "unit", "ms_per_step", "algorithmic_tflop_per_step",
                                      "device_ms_per_block_finish", "host_ms_executor_call", "host_ms_planner",
                                      "bytes_per_block_finish", "forward_plus_backward_ms") if k in line}
-        keep.update({"roofline": roof, "gpu_launches": launches, "config": line.get("config"),
+        keep.update({"roofline": roof, "gpu_launches": line.get("gpu_launches") if launches is None else launches,
+                     "config": line.get("config"),
                      "cpu_baseline": None if args.no_cpu_baseline else cpu_fn(budget)})
         out[name] = keep
         torch.cuda.empty_cache()

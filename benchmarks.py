@@ -318,6 +318,14 @@ def bench_compaction(args) -> dict:
     ws = Workspace(dev)
     rec = []
     sleep_cycles = int(2e8)  # ~0.1 s at 1.9 GHz
+    launched = []
+    real_compact = compaction._compact
+
+    def counting_compact(layer_caches, batches, workspace, stream):
+        launched.append(list(batches))
+        real_compact(layer_caches, batches, workspace, stream)
+
+    compaction._compact = counting_compact
     for blk in range(blocks):
         t_plan = time.perf_counter()
         for b in range(B):
@@ -336,6 +344,10 @@ def bench_compaction(args) -> dict:
         t0 = time.perf_counter()
         compaction.execute_kv_copy_operations(ops, [caches] * G, workspace=ws)
         host_ms = (time.perf_counter() - t0) * 1e3
+        # kernel launches of that call: one chain kernel per non-empty batch of each abkv_compact call
+        # (a batch with a cycle or a duplicate would take two; config 4's batches have neither)
+        launches = sum(1 for batches in launched for b in batches if len(b))
+        launched.clear()
         ev[2].record()
         torch.cuda._sleep(sleep_cycles)
         ev[3].record()
@@ -346,8 +358,9 @@ def bench_compaction(args) -> dict:
         # block 0 includes one-time set-up and is not reported
         assert blk == 0 or host_ms < sleep_ms, "the sleep kernel must outlast the host enqueue"
         rec.append({"rows": rows, "plan_ms": plan_ms, "host_ms": host_ms, "device_ms": ev[1].elapsed_time(ev[2]),
-                     "torch_ms": ev[3].elapsed_time(ev[4]),
+                     "torch_ms": ev[3].elapsed_time(ev[4]), "launches": launches,
                      "bytes": rows * n_tensors * 2 * 2 * 8 * 128 * 2})  # rows x tensors x (K,V) x R+W x bytes
+    compaction._compact = real_compact
     assert ws.read_error() == 0
     steady = rec[1:] or rec
     mean = lambda k: float(np.mean([r[k] for r in steady]))  # noqa: E731
@@ -362,6 +375,7 @@ def bench_compaction(args) -> dict:
             "speedup_vs_reference_torch_executor": mean("torch_ms") / dev_ms,
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": pk.get("hbm_gbs"), "unit": "GB/s",
                          "frac": gbs / pk.get("hbm_gbs", 6650.0)},
+            "gpu_launches": int(sum(r["launches"] for r in steady)),
             "config": {"sequences": B, "layers": L, "quota_groups": list(quotas), "physical_tensors": n_tensors,
                        "blocks_finished": blocks, "note": "mean over block finishes 2.."}}
 
