@@ -622,7 +622,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_bwd_unit_kernel(const __g
     const int quarter = warp & 3, hf = (warp - 2) >> 2;
     const int row = quarter * 32 + lane;
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
-    const float sl2 = p.scale_log2, scale = p.scale;
+    const float sl2 = p.scale_log2;
     const bool issuer = threadIdx.x == 64;
     const uint32_t stage = smem_u32(smem + LY::kOffStage);
     // dQ^T of unit v: read out of its TMEM buffer (lane = dim, query columns [32 hf, 32 hf + 32))
