@@ -474,6 +474,48 @@ def bench_packed(args) -> dict:
                        "main_rows": "256 + U[0,511]"}}
 
 
+def bench_hostdecode(args) -> dict:
+    """Config-2 decode end to end through HostDecode (pinned host queries, tables and outputs) for
+    several launch groupings of the 36 layers, in alternating rounds on one GPU (tokens/s)."""
+    from abridgekv_b200.hostdecode import HostDecode, split_layers
+    from abridgekv_b200.workloads import qwen3_decode_workload
+    from abridgekv_b200.workspace import Workspace
+
+    dev = torch.device("cuda", 0)
+    wl = qwen3_decode_workload(2, num_seqs=64, device=dev, seed=0)
+    ws = Workspace(dev)
+    q_host = [q.cpu().pin_memory() for q in wl.queries]
+    bt_host = {id(t): t.cpu().pin_memory() for t in wl.block_tables}
+    sl_host = {id(t): t.cpu().pin_memory() for t in wl.seq_lens}
+    out_host = [torch.empty(q.shape, dtype=q.dtype).pin_memory() for q in wl.queries]
+    bts = [bt_host[id(t)] for t in wl.block_tables]
+    sls = [sl_host[id(t)] for t in wl.seq_lens]
+    L = wl.num_layers
+    groupings = {"default": split_layers(L), "edge1": split_layers(L, edge=1),
+                 "max32": split_layers(L, max_group=32), "max32_edge3": split_layers(L, max_group=32, edge=3)}
+    runners = {k: HostDecode(wl.kv_caches, groups=g, max_pages_per_seq=wl.max_pages, workspace=ws)
+               for k, g in groupings.items()}
+    stream = torch.cuda.current_stream(dev)
+    res = {k: [] for k in groupings}
+    for _ in range(3):
+        for k, hd in runners.items():
+            for _ in range(args.warmup):
+                hd.run(q_host, bts, sls, out_host)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(args.steps):
+                hd.run(q_host, bts, sls, out_host)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            res[k].append(round(wl.num_seqs * args.steps / (e0.elapsed_time(e1) / 1e3)))
+    if ws.read_error():
+        raise RuntimeError(f"device error flag {ws.read_error():#x}")
+    return {"metric": "config-2 decode end to end through HostDecode, per launch grouping", "unit": "tokens/s",
+            "rounds": res, "groups": {k: [len(g) for g in v] for k, v in groupings.items()},
+            "config": {"sequences": wl.num_seqs, "layers": L, "steps": args.steps, "warmup": args.warmup}}
+
+
 def bench_kvshard(args) -> dict:
     from abridgekv_b200 import decode
     from abridgekv_b200.workloads import qwen3_decode_workload
@@ -688,7 +730,7 @@ def bench_flashinfer(args) -> dict:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("which", choices=["prefill", "prefill_bwd", "compaction", "codestep", "packed", "kvshard",
-                                          "codestep_compact", "flashinfer"])
+                                          "codestep_compact", "flashinfer", "hostdecode"])
     ap.add_argument("--layers", type=int, default=36)
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=2)
@@ -701,7 +743,8 @@ def main() -> None:
     args = ap.parse_args()
     fn = {"prefill": bench_prefill, "prefill_bwd": bench_prefill_bwd, "compaction": bench_compaction,
           "codestep": bench_codestep, "packed": bench_packed, "kvshard": bench_kvshard,
-          "codestep_compact": bench_codestep_compact, "flashinfer": bench_flashinfer}[args.which]
+          "codestep_compact": bench_codestep_compact, "flashinfer": bench_flashinfer,
+          "hostdecode": bench_hostdecode}[args.which]
     print(json.dumps(fn(args)), flush=True)
 
 
